@@ -1,0 +1,194 @@
+/*
+ * luna_b200.h -- C ABI of the B200 LiRPA bound-propagation engine.
+ *
+ * The engine computes IBP, CROWN and alpha-CROWN bounds for a batch of input
+ * boxes on one GPU.  Every entry point returns an int status (0 = ok); the
+ * message of the last failure on the calling thread is read with
+ * lb200_last_error().  No C++ exception crosses this boundary.
+ *
+ * Ownership: the caller owns every host buffer it passes; the engine copies
+ * weights to device memory at lb200_model_create() and owns all device
+ * buffers it allocates.  A model handle is thread-compatible, not
+ * thread-safe: one thread at a time may use a given handle.
+ *
+ * Reference interface replaced (Luna, paths within its project):
+ *   - NLR::TorchModel(nodes, inputIndices, outputIndex, dependencies)
+ *       src/engine/TorchModel.h:47-50           -> lb200_model_create
+ *   - LunaConfiguration static result-affecting flags
+ *       src/configuration/LunaConfiguration.cpp:22-66 -> lb200_options
+ *   - TorchModel::compute_bounds(input_bounds, C, method, lower, upper)
+ *       src/engine/TorchModel.h:97-103, TorchModel.cpp:653-698
+ *                                                -> lb200_compute_bounds
+ *   - Luna has one box per call (A is [spec, batch=1, features],
+ *       src/engine/CROWNAnalysis.cpp:1106-1127); here one call bounds
+ *       n_boxes independent boxes, each exactly as a fresh TorchModel
+ *       would.
+ */
+#ifndef LUNA_B200_H
+#define LUNA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Node kinds.  The numbering is NLR::NodeType
+ * (src/engine/nodes/BoundedTorchNode.h:37) so a front end that walks a Luna
+ * graph can pass getNodeType() through unchanged. */
+typedef enum {
+    LB200_NODE_INPUT = 0,
+    LB200_NODE_CONSTANT = 1,
+    LB200_NODE_LINEAR = 2,
+    LB200_NODE_RELU = 3,
+    LB200_NODE_RESHAPE = 4,
+    LB200_NODE_IDENTITY = 5,
+    LB200_NODE_SUB = 6,
+    LB200_NODE_FLATTEN = 7,
+    LB200_NODE_ADD = 8,
+    LB200_NODE_CONV = 9,
+    LB200_NODE_BATCHNORM = 10,
+    LB200_NODE_SIGMOID = 11,
+    LB200_NODE_CONVTRANSPOSE = 12,
+    LB200_NODE_CONCAT = 13,
+    LB200_NODE_SLICE = 14
+} lb200_node_type;
+
+/* Analysis methods.  CROWN and ALPHA_CROWN are
+ * LunaConfiguration::AnalysisMethod (src/configuration/LunaConfiguration.h:21-24);
+ * IBP returns the interval bounds of the output node that Luna keeps in
+ * CROWNAnalysis::getOutputIBPBounds (src/engine/CROWNAnalysis.cpp:1582-1589),
+ * projected through the specification matrix C. */
+enum {
+    LB200_METHOD_IBP = 0,
+    LB200_METHOD_CROWN = 1,
+    LB200_METHOD_ALPHA_CROWN = 2
+};
+
+/* One node of the computation graph (one Bounded*Node).  Fields a node kind
+ * does not use are ignored.  All pointers are host memory, fp32, row-major,
+ * and only read during lb200_model_create(). */
+typedef struct {
+    int32_t type;          /* lb200_node_type */
+    int32_t num_inputs;    /* number of producers (TorchModel dependencies) */
+    int32_t inputs[4];     /* producer node indices, in dependency order */
+    /* LINEAR: weight [out_features, in_features], bias [out_features] or NULL,
+     * scale = ONNX Gemm alpha folded into the weight
+     * (BoundedLinearNode.cpp:91-93). */
+    int64_t in_features;
+    int64_t out_features;
+    float scale;
+    const float* weight;
+    const float* bias;
+    /* Shape of this node's output as (C, H, W); a flat vector of n features
+     * is (n, 1, 1).  Filled for every node. */
+    int32_t out_shape[3];
+    /* CONV / CONVTRANSPOSE geometry (square or rectangular kernels). */
+    int32_t kernel[2];
+    int32_t stride[2];
+    int32_t padding[2];
+    int32_t output_padding[2];
+    /* BATCHNORM (eval mode): weight = gamma, bias = beta, plus running stats. */
+    const float* running_mean;
+    const float* running_var;
+    float eps;
+} lb200_node_desc;
+
+typedef struct {
+    int32_t num_nodes;
+    const lb200_node_desc* nodes;   /* indexed by node id */
+    int32_t input_index;            /* TorchModel inputIndices[0] */
+    int32_t output_index;           /* TorchModel outputIndex */
+} lb200_graph_desc;
+
+/* Result-affecting options, one field per LunaConfiguration flag
+ * (src/configuration/LunaConfiguration.cpp:28-50).  lb200_options_default()
+ * fills Luna's defaults. */
+typedef struct {
+    uint32_t alpha_iterations;        /* ALPHA_ITERATIONS = 20 */
+    float alpha_lr;                   /* ALPHA_LR = 0.5 */
+    float alpha_lr_decay;             /* ALPHA_LR_DECAY = 0.98 */
+    uint32_t early_stop_patience;     /* EARLY_STOP_PATIENCE = 10 */
+    float start_save_best;            /* START_SAVE_BEST = 0.5 */
+    int32_t stabilize_intermediate_bounds;  /* STABILIZE_INTERMEDIATE_BOUNDS = 1 */
+    int32_t recompute_intermediate_bounds;  /* RECOMPUTE_INTERMEDIATE_BOUNDS = 1 */
+    int32_t optimize_lower;           /* OPTIMIZE_LOWER = 1 */
+    int32_t optimize_upper;           /* OPTIMIZE_UPPER = 0 */
+    int32_t stop_crown_on_verified;   /* STOP_CROWN_ON_VERIFIED = 1 */
+    int32_t stop_alpha_on_verified;   /* STOP_ALPHA_ON_VERIFIED = 1 */
+    int32_t enable_first_linear_ibp;  /* ENABLE_FIRST_LINEAR_IBP = 1 */
+    int32_t use_patches_mode;         /* USE_PATCHES_MODE = 1 */
+} lb200_options;
+
+/* Per-call statistics. */
+typedef struct {
+    double ms_total;          /* wall time of the call on the host */
+    double ms_device;         /* CUDA-event time of the device work */
+    int64_t kernel_launches;  /* kernels this call launched */
+    int64_t backward_rows;    /* A-matrix rows (both sides) propagated */
+    double algorithmic_flops; /* 2*M*N*K summed over real rows, contractions */
+    int32_t alpha_iterations_run; /* max over boxes */
+} lb200_stats;
+
+typedef struct lb200_model lb200_model;
+
+/* Fill *opt with Luna's defaults (LunaConfiguration.cpp:28-50). */
+int lb200_options_default(lb200_options* opt);
+
+/* Build a model on CUDA device `device`.  Replaces
+ * TorchModel(nodes, inputIndices, outputIndex, dependencies)
+ * (src/engine/TorchModel.h:47-50, TorchModel.cpp:23-64). */
+int lb200_model_create(const lb200_graph_desc* graph, int device, lb200_model** out);
+
+/* Set the result-affecting options (the LunaConfiguration globals that
+ * TorchModel::compute_bounds reads, TorchModel.cpp:668-670,683-684). */
+int lb200_set_options(lb200_model* model, const lb200_options* opt);
+
+/* Bound n_boxes input boxes.  Replaces TorchModel::compute_bounds
+ * (src/engine/TorchModel.cpp:653-698) called once per box on a fresh model.
+ *   x_lower, x_upper : [n_boxes, n_in] host, the flat input box per box
+ *   C                : [c_boxes, nspec, n_out] host; c_boxes is 1 (shared)
+ *                      or n_boxes (one specification per box)
+ *   thresholds       : [nspec] host or NULL.  With thresholds, a box whose
+ *                      lower bounds exceed any threshold counts as verified
+ *                      (TorchModel::isSpecVerified, TorchModel.cpp:616-651)
+ *                      and the STOP_*_ON_VERIFIED options apply; without
+ *                      them nothing is ever verified, as in Luna after
+ *                      setSpecificationMatrix.
+ *   out_lb, out_ub   : [n_boxes, nspec] host
+ *   stats            : may be NULL. */
+int lb200_compute_bounds(lb200_model* model, int method,
+                         const float* x_lower, const float* x_upper, int64_t n_boxes,
+                         const float* C, int64_t c_boxes, int64_t nspec,
+                         const float* thresholds, int bound_lower, int bound_upper,
+                         float* out_lb, float* out_ub, lb200_stats* stats);
+
+/* As lb200_compute_bounds, with every array already in device memory of the
+ * model's GPU; the work is ordered on `stream` (a cudaStream_t, or NULL for
+ * the legacy default stream) and the call returns once it has completed. */
+int lb200_compute_bounds_device(lb200_model* model, int method,
+                                const float* d_x_lower, const float* d_x_upper, int64_t n_boxes,
+                                const float* d_C, int64_t c_boxes, int64_t nspec,
+                                const float* d_thresholds, int bound_lower, int bound_upper,
+                                float* d_out_lb, float* d_out_ub, void* stream,
+                                lb200_stats* stats);
+
+/* Copy the intermediate (pre-activation) bounds of the last call into host
+ * buffers: for every node that feeds a ReLU, in node-id order, [n_boxes,
+ * size] lower then upper.  Mirrors TorchModel::getState().allBounds
+ * (src/engine/TorchModel.cpp:975-1014).  *count receives the total floats
+ * per side; pass NULL buffers to query it. */
+int lb200_get_intermediate_bounds(lb200_model* model, float* lower, float* upper, int64_t* count);
+
+/* Copy the last error message of this thread into buf (always terminated). */
+int lb200_last_error(char* buf, size_t len);
+
+/* Release the model and every device buffer it owns. */
+void lb200_model_destroy(lb200_model* model);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LUNA_B200_H */

@@ -1,0 +1,537 @@
+"""CPU restatement of Luna's IBP / CROWN / alpha-CROWN -- test infrastructure.
+
+This module is the oracle: a plain PyTorch (fp32, CPU, autograd) restatement
+of the algorithm Luna runs for one input box, written from the reference's
+behaviour and checked against Luna itself (oracle/_ref, built by
+oracle/Makefile) in tests/test_oracle_vs_ref.py.  Only tests, smoke() and the
+bench's CPU-baseline leg import it; the product never does.
+
+Each function cites the Luna source (path within the Luna project) whose
+behaviour it restates.  Per-box state follows Luna's: IBP bounds, "node
+bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
+parameters keyed by (activation node, start node), and STE reference bounds.
+
+Supported node kinds: Input, Linear, ReLU, Flatten, Identity.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_FLATTEN,
+                           NODE_IDENTITY, NODE_INPUT, NODE_LINEAR, NODE_RELU, Options,
+                           default_options)
+
+
+def topo_order(graph):
+    """Kahn order seeded with in-degree-0 nodes by id (TorchModel::topologicalSort,
+    src/engine/TorchModel.cpp:146-184)."""
+    n = len(graph.nodes)
+    deg = [len(graph.nodes[i].inputs) for i in range(n)]
+    dependents = [[] for _ in range(n)]
+    for i, nd in enumerate(graph.nodes):
+        for p in nd.inputs:
+            dependents[p].append(i)
+    q = [i for i in range(n) if deg[i] == 0]
+    out = []
+    while q:
+        c = q.pop(0)
+        out.append(c)
+        for d in dependents[c]:
+            deg[d] -= 1
+            if deg[d] == 0:
+                q.append(d)
+    return out, dependents
+
+
+@dataclass
+class _Alpha:
+    alpha: torch.Tensor          # [2, spec, nU] leaf, requires grad
+    idx: torch.Tensor            # [nU] int64 neuron ids unstable at creation
+
+
+@dataclass
+class _BoxState:
+    node_bounds: dict = field(default_factory=dict)   # id -> (l, u): BoundedTorchNode::setBounds
+    ibp: dict = field(default_factory=dict)           # CROWNAnalysis::_ibpBounds
+    concrete: dict = field(default_factory=dict)      # CROWNAnalysis::_concreteBounds
+    alphas: dict = field(default_factory=dict)        # (relu id, start id) -> _Alpha
+    reference: dict = field(default_factory=dict)     # STE reference bounds id -> (l, u)
+    alpha_mode: bool = False                          # ReLU stage "opt"
+    method_alpha: bool = False                        # ANALYSIS_METHOD == AlphaCROWN
+    first_linear_ibp: bool = True                     # ENABLE_FIRST_LINEAR_IBP
+
+
+class _Adam:
+    """torch::optim::Adam (betas 0.9/0.999, eps 1e-8, no weight decay) as
+    AlphaCROWNAnalysis configures it (src/engine/AlphaCROWNAnalysis.cpp:366-368):
+    m = m*b1 + (1-b1)*g;  v = v*b2 + (1-b2)*g*g;
+    p += (-lr/bc1) * m / (sqrt(v)/sqrt(bc2) + eps), bias corrections in double."""
+
+    def __init__(self, params):
+        self.params = params
+        self.m = [torch.zeros_like(p) for p in params]
+        self.v = [torch.zeros_like(p) for p in params]
+        self.t = 0
+
+    @torch.no_grad()
+    def step(self, lr):
+        self.t += 1
+        bc1 = 1.0 - 0.9 ** self.t
+        bc2 = 1.0 - 0.999 ** self.t
+        for p, m, v in zip(self.params, self.m, self.v):
+            g = p.grad if p.grad is not None else torch.zeros_like(p)
+            m.mul_(0.9).add_(g, alpha=1.0 - 0.9)
+            v.mul_(0.999).addcmul_(g, g, value=1.0 - 0.999)
+            denom = (v.sqrt() / np.sqrt(bc2)).add_(1e-8)
+            p.addcdiv_(m, denom, value=-(lr / bc1))
+
+
+class LirpaOracle:
+    def __init__(self, graph, options: Options | None = None):
+        self.g = graph
+        self.opt = options if options is not None else default_options()
+        self.order, self.dependents = topo_order(graph)
+        self.W = {}
+        self.b = {}
+        for i, nd in enumerate(graph.nodes):
+            if nd.type == NODE_LINEAR:
+                # BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
+                self.W[i] = torch.from_numpy(np.asarray(nd.weight, np.float32)) * nd.scale
+                self.b[i] = (torch.from_numpy(np.asarray(nd.bias, np.float32))
+                             if nd.bias is not None else torch.zeros(nd.weight.shape[0]))
+            elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_FLATTEN, NODE_IDENTITY):
+                raise NotImplementedError(f"oracle: node type {nd.type}")
+        self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type == NODE_RELU]
+        self.preact_ids = sorted({graph.nodes[i].inputs[0] for i in self.act_ids})
+
+    # ------------------------------------------------------------------ IBP
+    def _ibp_node(self, i, ins):
+        """Interval forward of one node: Linear W+/W- matmuls
+        (BoundedLinearNode.cpp:197-228,266-292), ReLU clamp (BoundedReLUNode.cpp:399-422)."""
+        nd = self.g.nodes[i]
+        if nd.type == NODE_LINEAR:
+            l, u = ins[0]
+            W = self.W[i]
+            Wp, Wn = torch.clamp(W, min=0), torch.clamp(W, max=0)
+            lo = torch.matmul(l, Wp.t()) + torch.matmul(u, Wn.t())
+            hi = torch.matmul(u, Wp.t()) + torch.matmul(l, Wn.t())
+            return lo + self.b[i], hi + self.b[i]
+        if nd.type == NODE_RELU:
+            l, u = ins[0]
+            return torch.clamp_min(l, 0), torch.clamp_min(u, 0)
+        if nd.type in (NODE_FLATTEN, NODE_IDENTITY):
+            return ins[0]
+        raise NotImplementedError
+
+    def _input_bounds_of(self, st, i, x):
+        """CROWNAnalysis::getInputBoundsForNode (src/engine/CROWNAnalysis.cpp:1043-1101):
+        input box for the Input node, else node bounds > concrete > IBP."""
+        out = []
+        for p in self.g.nodes[i].inputs:
+            if self.g.nodes[p].type == NODE_INPUT:
+                out.append(x)
+            elif p in st.node_bounds:
+                out.append(st.node_bounds[p])
+            elif p in st.concrete:
+                out.append(st.concrete[p])
+            else:
+                out.append(st.ibp[p])
+        return out
+
+    def _compute_ibp(self, st, x):
+        """CROWNAnalysis::computeIBPBounds (src/engine/CROWNAnalysis.cpp:180-214)."""
+        st.ibp = {}
+        for i in self.order:
+            if self.g.nodes[i].type == NODE_INPUT:
+                st.ibp[i] = x
+                continue
+            lo, hi = self._ibp_node(i, self._input_bounds_of(st, i, x))
+            st.ibp[i] = (lo.detach(), hi.detach())
+
+    # ------------------------------------------------------------ ReLU relax
+    @staticmethod
+    def _upper(l, u):
+        """BoundedReLUNode::_reluUpperBound (BoundedReLUNode.cpp:469-479)."""
+        lb_r = torch.clamp_max(l, 0)
+        ub_r = torch.clamp_min(u, 0)
+        ub_r = torch.max(ub_r, lb_r + 1e-8)
+        d = ub_r / (ub_r - lb_r)
+        return d, -lb_r * d
+
+    @staticmethod
+    def _crown_lower(l, u):
+        """BoundedReLUNode::_computeStandardCROWNLowerBound (BoundedReLUNode.cpp:481-504)."""
+        s = torch.zeros_like(l)
+        s = torch.where(l >= 0, torch.ones_like(s), s)
+        unc = (l < 0) & (u > 0)
+        lb_r = torch.clamp_max(l, 0)
+        ub_r = torch.clamp_min(u, 0)
+        ub_r = torch.max(ub_r, lb_r + 1e-8)
+        up = ub_r / (ub_r - lb_r)
+        ad = torch.where(up > 0.5, torch.ones_like(l), torch.zeros_like(l))
+        return torch.where(unc, ad, s)
+
+    def _relu_backward(self, st, relu_id, start_id, lA, uA, l, u):
+        """BoundedReLUNode::boundBackward (BoundedReLUNode.cpp:54-362) for dense A
+        [spec, n], with _backwardRelaxation (:446-467) and, in the
+        optimisation stage, _maskAlpha (:507-612).  Returns new A and bias
+        terms (bias [spec])."""
+        d_up, b_up = self._upper(l, u)
+        d_lo = self._crown_lower(l, u)
+        spec = lA.shape[0]
+        if st.alpha_mode:
+            key = (relu_id, start_id)
+            ap = st.alphas.get(key)
+            if ap is None or ap.alpha.shape[1] != spec:
+                ap = self._ensure_alpha(st, key, spec, l, u, d_lo)
+            active = l >= 0
+            inactive = u <= 0
+            if ap.idx.numel() > 0:
+                n = l.numel()
+                idx = ap.idx.unsqueeze(0).expand(spec, ap.idx.numel())
+                a_lo = torch.zeros(spec, n).scatter(1, idx, ap.alpha[0])
+                a_up = torch.zeros(spec, n).scatter(1, idx, ap.alpha[1])
+                one = torch.ones(spec, n)
+                a_lo = torch.where(active.unsqueeze(0).expand(spec, n), one, a_lo)
+                a_up = torch.where(active.unsqueeze(0).expand(spec, n), one, a_up)
+                k_up = torch.where(active, torch.ones_like(d_up), d_up)
+                k_up = torch.where(inactive, torch.zeros_like(k_up), k_up)
+                bu = -l * d_up
+                bu = torch.where(active | inactive, torch.zeros_like(bu), bu)
+                Lpos, Lneg = torch.clamp_min(lA, 0), torch.clamp_max(lA, 0)
+                Upos, Uneg = torch.clamp_min(uA, 0), torch.clamp_max(uA, 0)
+                k = k_up.unsqueeze(0)
+                new_l = Lpos * a_lo + Lneg * k
+                new_u = Upos * k + Uneg * a_up
+                bl = (Lpos * torch.zeros_like(bu) + Lneg * bu).sum(-1)
+                bu_ = (Upos * bu + Uneg * torch.zeros_like(bu)).sum(-1)
+                return new_l, new_u, bl, bu_
+        # Standard CROWN relaxation.
+        Lpos, Lneg = torch.clamp_min(lA, 0), torch.clamp_max(lA, 0)
+        Upos, Uneg = torch.clamp_min(uA, 0), torch.clamp_max(uA, 0)
+        zero = torch.zeros_like(l)
+        new_l = Lpos * d_lo + Lneg * d_up
+        new_u = Upos * d_up + Uneg * d_lo
+        bl = (Lpos * zero + Lneg * b_up).sum(-1)
+        bu_ = (Upos * b_up + Uneg * zero).sum(-1)
+        return new_l, new_u, bl, bu_
+
+    def _ensure_alpha(self, st, key, spec, l, u, d_lo):
+        """AlphaCROWNAnalysis::ensureAlphaFor (src/engine/AlphaCROWNAnalysis.cpp:132-304):
+        alpha [2, spec, nU] at the neurons unstable now, initialised with the
+        CROWN lower slope, clamped to [0, 1]."""
+        mask = (l.detach() < 0) & (u.detach() > 0)
+        idx = torch.nonzero(mask).flatten()
+        init = d_lo.detach().flatten().index_select(0, idx)
+        a = init.view(1, 1, -1).expand(2, spec, idx.numel()).contiguous().clone()
+        a = torch.clamp(a, 0.0, 1.0).detach().requires_grad_(True)
+        ap = _Alpha(a, idx)
+        st.alphas[key] = ap
+        return ap
+
+    # -------------------------------------------------------- backward pass
+    def _backward_from(self, st, start, x, rows=None, C=None):
+        """CROWNAnalysis::backwardFrom (src/engine/CROWNAnalysis.cpp:231-706) for
+        dense A: start A is the spec C (output) or one-hot rows at `rows`;
+        Kahn-style reverse schedule; bias attached to the first dependency.
+        Returns (lA, uA, lbias, ubias) at the input node."""
+        n = self.g.nodes[start].size
+        if C is not None:
+            A0 = C
+        else:
+            A0 = torch.zeros(len(rows), n)
+            A0[torch.arange(len(rows)), torch.as_tensor(rows, dtype=torch.long)] = 1.0
+        spec = A0.shape[0]
+        lA = {start: A0}
+        uA = {start: A0}
+        lb = {start: torch.zeros(spec)}
+        ub = {start: torch.zeros(spec)}
+        reach = {start}
+        work = [start]
+        while work:
+            c = work.pop(0)
+            for p in self.g.nodes[c].inputs:
+                if p not in reach:
+                    reach.add(p)
+                    work.append(p)
+        pending = {v: sum(1 for d in self.dependents[v] if d in reach) for v in reach}
+        queue = [start]
+        done = set()
+        inp = self.g.input_index
+        while queue:
+            c = queue.pop(0)
+            if c in done:
+                continue
+            done.add(c)
+            nd = self.g.nodes[c]
+            if c in lA:
+                a_l, a_u = lA[c], uA[c]
+                if nd.type == NODE_LINEAR:
+                    W, bb = self.W[c], self.b[c]
+                    out = [(torch.matmul(a_l, W), torch.matmul(a_u, W))]
+                    nb_l = (a_l * bb).sum(-1)
+                    nb_u = (a_u * bb).sum(-1)
+                elif nd.type == NODE_RELU:
+                    l, u = self._input_bounds_of(st, c, x)[0]
+                    nl, nu, nb_l, nb_u = self._relu_backward(st, c, start, a_l, a_u, l, u)
+                    out = [(nl, nu)]
+                elif nd.type in (NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT):
+                    out = [(a_l, a_u)]
+                    nb_l = nb_u = None
+                else:
+                    raise NotImplementedError
+                for k, p in enumerate(nd.inputs):
+                    if k >= len(out):
+                        break
+                    pl, pu = out[k]
+                    lA[p] = lA[p] + pl if p in lA else pl
+                    uA[p] = uA[p] + pu if p in uA else pu
+                    if k == 0:
+                        # propagated = node bias + accumulated bias (:629-657)
+                        tl = lb[c] if nb_l is None else nb_l + lb[c]
+                        tu = ub[c] if nb_u is None else nb_u + ub[c]
+                        lb[p] = lb[p] + tl if p in lb else tl
+                        ub[p] = ub[p] + tu if p in ub else tu
+                if c != inp:
+                    del lA[c], uA[c], lb[c], ub[c]
+            for p in nd.inputs:
+                if p in pending and pending[p] > 0:
+                    pending[p] -= 1
+                    if pending[p] == 0:
+                        queue.append(p)
+        return lA[inp], uA[inp], lb[inp], ub[inp]
+
+    @staticmethod
+    def _concretize(lA, uA, lb, ub, x):
+        """computeConcreteLowerBound/UpperBound (src/engine/CROWNAnalysis.cpp:1164-1224):
+        lb = A+ xL + A- xU + bias, ub = A+ xU + A- xL + bias."""
+        xl, xu = x
+        lo = (torch.matmul(torch.clamp_min(lA, 0), xl) + torch.matmul(torch.clamp_max(lA, 0), xu)) + lb
+        hi = (torch.matmul(torch.clamp_min(uA, 0), xu) + torch.matmul(torch.clamp_max(uA, 0), xl)) + ub
+        return lo, hi
+
+    def _is_first_linear(self, i):
+        """CROWNAnalysis::isFirstLinearLayer (:1672-1701)."""
+        nd = self.g.nodes[i]
+        return (nd.type == NODE_LINEAR and len(nd.inputs) == 1
+                and self.g.nodes[nd.inputs[0]].type == NODE_INPUT)
+
+    def _lazy_intermediate(self, st, i, x):
+        """CROWNAnalysis::computeIntermediateBoundsLazy (:1744-1795) and
+        concretizeNode's scatter + STE clamp (:877-938)."""
+        if i in st.node_bounds or i in st.concrete:
+            return
+        if st.first_linear_ibp and self._is_first_linear(i):
+            lo, hi = self._ibp_node(i, self._input_bounds_of(st, i, x))
+            st.node_bounds[i] = (lo, hi)
+            st.ibp[i] = (lo, hi)
+            st.concrete[i] = (lo, hi)
+            return
+        il, iu = st.ibp[i]
+        rows = torch.nonzero((il < 0) & (iu > 0)).flatten().tolist()
+        if not rows:
+            st.concrete[i] = st.ibp[i]
+            st.node_bounds[i] = st.ibp[i]
+            return
+        lA, uA, lb, ub = self._backward_from(st, i, x, rows=rows)
+        lo, hi = self._concretize(lA, uA, lb, ub, x)
+        idx = torch.as_tensor(rows, dtype=torch.long)
+        if not st.method_alpha:
+            lo, hi = lo.detach(), hi.detach()
+        full_l = il.detach().clone().index_put((idx,), lo)
+        full_u = iu.detach().clone().index_put((idx,), hi)
+        if st.method_alpha and i in st.reference:
+            rl, ru = st.reference[i]
+            full_l = torch.max(rl, full_l).detach() - full_l.detach() + full_l
+            full_u = full_u - (full_u.detach() - torch.min(ru, full_u).detach())
+        st.concrete[i] = (full_l, full_u)
+        st.node_bounds[i] = (full_l, full_u)
+
+    def _check_prior(self, st, i, x):
+        """CROWNAnalysis::checkPriorBounds (:1797-1818)."""
+        nd = self.g.nodes[i]
+        for p in nd.inputs:
+            self._check_prior(st, p, x)
+        if nd.type == NODE_RELU:
+            self._lazy_intermediate(st, nd.inputs[0], x)
+
+    def _run(self, st, x, C):
+        """CROWNAnalysis::run with USE_STANDARD_CROWN (:93-142).  Returns the
+        output (lb, ub) [nspec]."""
+        self._compute_ibp(st, x)
+        out = self.g.output_index
+        self._check_prior(st, out, x)
+        lA, uA, lb, ub = self._backward_from(st, out, x, C=C)
+        lo, hi = self._concretize(lA, uA, lb, ub, x)
+        st.node_bounds[out] = (lo, hi)
+        st.concrete[out] = (lo, hi)
+        return lo, hi
+
+    # ---------------------------------------------------------- public API
+    def ibp(self, xl, xu, C):
+        st = _BoxState()
+        x = (torch.as_tensor(xl), torch.as_tensor(xu))
+        self._compute_ibp(st, x)
+        lo, hi = st.ibp[self.g.output_index]
+        Cp, Cn = torch.clamp_min(C, 0), torch.clamp_max(C, 0)
+        return Cp @ lo + Cn @ hi, Cp @ hi + Cn @ lo
+
+    def crown(self, xl, xu, C, st=None):
+        """TorchModel::runCROWN (src/engine/TorchModel.cpp:710-740) on a fresh model."""
+        st = st or _BoxState(first_linear_ibp=bool(self.opt.enable_first_linear_ibp))
+        x = (torch.as_tensor(xl), torch.as_tensor(xu))
+        with torch.no_grad():
+            lo, hi = self._run(st, x, C)
+        return lo, hi, st
+
+    def alpha_crown(self, xl, xu, C, trace=None):
+        """TorchModel::runAlphaCROWN (src/engine/TorchModel.cpp:798-893) with
+        AlphaCROWNAnalysis::computeOptimizedBounds(Lower)
+        (src/engine/AlphaCROWNAnalysis.cpp:306-511) for the lower side and
+        runCROWN on the same nodes for the upper side."""
+        o = self.opt
+        x = (torch.as_tensor(xl), torch.as_tensor(xu))
+        st = _BoxState(method_alpha=True, first_linear_ibp=False)
+        out = self.g.output_index
+        # The CROWN initialisation pass (AlphaCROWNAnalysis.cpp:118-129) only
+        # matters with thresholds; its state is cleared before optimisation.
+        # --- computeOptimizedBounds(Lower)
+        st.alpha_mode = True
+        st.node_bounds, st.concrete = {}, {}
+        lo, hi = self._run(st, x, C)
+        best_int = {i: (st.node_bounds[i][0].detach().clone(), st.node_bounds[i][1].detach().clone())
+                    for i in self.preact_ids if i in st.node_bounds}
+        if o.stabilize_intermediate_bounds:
+            st.reference = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
+        params = [ap.alpha for ap in st.alphas.values()]
+        adam = _Adam(params)
+        iters = int(o.alpha_iterations)
+        best = None
+        lr = float(o.alpha_lr)
+        patience = 0
+        best_loss = None
+        best_alpha = {}
+        for it in range(iters):
+            last = it == iters - 1
+            st.node_bounds, st.concrete = {}, {}
+            with torch.set_grad_enabled(not last):
+                cur_l, cur_u = self._run(st, x, C)
+            cur = cur_l.detach()
+            if trace is not None:
+                trace.append(cur.clone())
+            loss = None if last else -cur_l.sum()
+            if best is None:
+                best = cur.clone()
+                improved_idx = list(range(cur.numel()))
+            else:
+                improved_idx = torch.nonzero(cur > best).flatten().tolist()
+                if improved_idx:
+                    best = torch.max(best, cur)
+            improved = len(improved_idx) > 0
+            save = it < 1 or it > int(iters * o.start_save_best) or patience >= o.early_stop_patience
+            if improved and save:
+                self._update_best_alphas(st, best_alpha, improved_idx)
+                for i in self.preact_ids:
+                    if i in st.node_bounds:
+                        cl, cu = st.node_bounds[i]
+                        if i in best_int:
+                            best_int[i] = (torch.max(best_int[i][0], cl.detach()).clone(),
+                                           torch.min(best_int[i][1], cu.detach()).clone())
+                        else:
+                            best_int[i] = (cl.detach().clone(), cu.detach().clone())
+                if o.stabilize_intermediate_bounds:
+                    st.reference = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
+            if improved:
+                if loss is not None:
+                    best_loss = loss.detach().abs()
+                patience = 0
+            elif loss is not None:
+                cl = loss.detach().abs()
+                if best_loss is None or bool(cl < best_loss):
+                    best_loss = cl
+                    patience = 0
+                else:
+                    patience += 1
+            if patience >= o.early_stop_patience:
+                break
+            if not last and loss is not None:
+                for p in params:
+                    p.grad = None
+                loss.backward()
+                adam.step(lr)
+                with torch.no_grad():
+                    for p in params:
+                        p.clamp_(0.0, 1.0)
+                lr = float(np.float32(lr) * np.float32(o.alpha_lr_decay))
+        # restoreBestAlphas / restoreBestIntermediateBounds / final run(false)
+        with torch.no_grad():
+            for key, ap in st.alphas.items():
+                if key in best_alpha and best_alpha[key].shape == ap.alpha.shape:
+                    ap.alpha.copy_(best_alpha[key])
+            st.reference = {}
+            st.concrete = {}
+            st.node_bounds = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
+            fin_l, _ = self._run(st, x, C)
+            lb_final = torch.max(fin_l, best) if best is not None else fin_l
+            # runCROWN for the non-optimised side: a new analysis over the same
+            # nodes, whose pre-activation bounds are still the best ones and
+            # whose ReLUs still read the optimised alphas (stage "opt").
+            st2 = _BoxState(node_bounds={k: v for k, v in st.node_bounds.items()
+                                         if k in best_int},
+                            alphas=st.alphas, alpha_mode=True, method_alpha=True,
+                            first_linear_ibp=False)
+            _, ub_final = self._run(st2, x, C)
+        inter = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
+        return lb_final.detach(), ub_final.detach(), inter
+
+    @staticmethod
+    def _update_best_alphas(st, best_alpha, improved_idx):
+        """AlphaCROWNAnalysis::updateBestAlphas (src/engine/AlphaCROWNAnalysis.cpp:567-622):
+        first call copies every alpha; later calls copy the rows whose index
+        along the spec dimension is an improved output spec index (also for
+        intermediate starts, where that dimension counts unstable neurons)."""
+        with torch.no_grad():
+            for key, ap in st.alphas.items():
+                if ap.alpha.numel() == 0:
+                    continue
+                cur = ap.alpha.detach()
+                if key not in best_alpha or best_alpha[key].shape != cur.shape:
+                    best_alpha[key] = cur.clone()
+                    continue
+                idx = torch.as_tensor([i for i in improved_idx if i < cur.shape[1]], dtype=torch.long)
+                if idx.numel():
+                    best_alpha[key][:, idx] = cur[:, idx]
+
+    def compute_bounds(self, boxes, method, intermediate=False):
+        """Bound every box with a fresh state.  Returns lb, ub [B, nspec] (and
+        the pre-activation bounds concatenated in node-id order)."""
+        B = boxes.n
+        nspec = boxes.C.shape[1]
+        lb = np.zeros((B, nspec), np.float32)
+        ub = np.zeros((B, nspec), np.float32)
+        inter_l, inter_u = [], []
+        for b in range(B):
+            C = torch.from_numpy(boxes.C[0 if boxes.C.shape[0] == 1 else b].copy())
+            xl = torch.from_numpy(boxes.lower[b].copy())
+            xu = torch.from_numpy(boxes.upper[b].copy())
+            if method == METHOD_IBP:
+                lo, hi = self.ibp(xl, xu, C)
+                inter = {}
+            elif method == METHOD_CROWN:
+                lo, hi, st = self.crown(xl, xu, C)
+                inter = {i: st.node_bounds[i] for i in self.preact_ids if i in st.node_bounds}
+            elif method == METHOD_ALPHA_CROWN:
+                lo, hi, inter = self.alpha_crown(xl, xu, C)
+            else:
+                raise ValueError(method)
+            lb[b] = lo.numpy()
+            ub[b] = hi.numpy()
+            if intermediate:
+                inter_l.append(np.concatenate([inter[i][0].numpy() for i in self.preact_ids]))
+                inter_u.append(np.concatenate([inter[i][1].numpy() for i in self.preact_ids]))
+        if intermediate:
+            return lb, ub, np.stack(inter_l), np.stack(inter_u)
+        return lb, ub

@@ -1,0 +1,215 @@
+// luna_ref_driver.cpp -- test infrastructure, not product code.
+//
+// A C-ABI driver around Luna's own CPU implementation, compiled from the
+// reference sources by oracle/Makefile into oracle/_ref/libluna_ref.so.  It
+// is the ground truth that the CPU restatement in oracle/lirpa_oracle.py and
+// the CUDA engine are checked against, and the CPU baseline that bench.py
+// times.  Nothing in the product links it.
+//
+// Protocol (fresh state per box, as a Luna user bounding independent boxes
+// would do): for every box a new TorchModel is built through the node API,
+// mirroring what OnnxToTorchParser builds for Gemm/Relu/Flatten
+// (src/input_parsers/OnnxToTorch.cpp:1672-1696,1995,2423), then
+// TorchModel::compute_bounds (src/engine/TorchModel.cpp:653-698) is called
+// with flat [n] input bounds and C of shape [1, nspec, n_out].
+#include "../include/luna_b200.h"
+
+#include "TorchModel.h"
+#include "CROWNAnalysis.h"
+#include "configuration/LunaConfiguration.h"
+#include "nodes/BoundedInputNode.h"
+#include "nodes/BoundedLinearNode.h"
+#include "nodes/BoundedReLUNode.h"
+#include "nodes/BoundedFlattenNode.h"
+#include "nodes/BoundedIdentityNode.h"
+#include "input_parsers/Operations.h"
+
+#include <torch/torch.h>
+
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+namespace {
+
+void set_error(char* err, size_t len, const std::string& msg) {
+    if (!err || len == 0) return;
+    std::strncpy(err, msg.c_str(), len - 1);
+    err[len - 1] = '\0';
+}
+
+torch::Tensor from_host(const float* p, std::vector<int64_t> shape) {
+    auto t = torch::from_blob(const_cast<float*>(p), shape, torch::kFloat32);
+    return t.clone();
+}
+
+void apply_options(const lb200_options* o) {
+    LunaConfiguration::ALPHA_ITERATIONS = o->alpha_iterations;
+    LunaConfiguration::ALPHA_LR = o->alpha_lr;
+    LunaConfiguration::ALPHA_LR_DECAY = o->alpha_lr_decay;
+    LunaConfiguration::EARLY_STOP_PATIENCE = o->early_stop_patience;
+    LunaConfiguration::START_SAVE_BEST = o->start_save_best;
+    LunaConfiguration::STABILIZE_INTERMEDIATE_BOUNDS = o->stabilize_intermediate_bounds != 0;
+    LunaConfiguration::RECOMPUTE_INTERMEDIATE_BOUNDS = o->recompute_intermediate_bounds != 0;
+    LunaConfiguration::OPTIMIZE_LOWER = o->optimize_lower != 0;
+    LunaConfiguration::OPTIMIZE_UPPER = o->optimize_upper != 0;
+    LunaConfiguration::STOP_CROWN_ON_VERIFIED = o->stop_crown_on_verified != 0;
+    LunaConfiguration::STOP_ALPHA_ON_VERIFIED = o->stop_alpha_on_verified != 0;
+    LunaConfiguration::ENABLE_FIRST_LINEAR_IBP = o->enable_first_linear_ibp != 0;
+    LunaConfiguration::USE_STANDARD_CROWN = true;
+    LunaConfiguration::USE_PATCHES_MODE = o->use_patches_mode != 0;
+    LunaConfiguration::USE_CUDA = false;
+    LunaConfiguration::DEVICE = torch::Device(torch::kCPU);
+}
+
+std::shared_ptr<NLR::TorchModel> build_model(const lb200_graph_desc* g) {
+    Vector<std::shared_ptr<NLR::BoundedTorchNode>> nodes;
+    Map<unsigned, Vector<unsigned>> deps;
+    for (int i = 0; i < g->num_nodes; ++i) {
+        const lb200_node_desc& d = g->nodes[i];
+        std::shared_ptr<NLR::BoundedTorchNode> node;
+        const int64_t out_numel = (int64_t)d.out_shape[0] * d.out_shape[1] * d.out_shape[2];
+        switch (d.type) {
+        case LB200_NODE_INPUT:
+            node = std::make_shared<NLR::BoundedInputNode>(0, (unsigned)out_numel, "input");
+            break;
+        case LB200_NODE_LINEAR: {
+            torch::nn::Linear lin(torch::nn::LinearOptions(d.in_features, d.out_features));
+            lin->weight = from_host(d.weight, {d.out_features, d.in_features});
+            lin->bias = d.bias ? from_host(d.bias, {d.out_features})
+                               : torch::zeros({d.out_features});
+            node = std::make_shared<NLR::BoundedLinearNode>(lin, d.scale, String("linear"));
+            node->setInputSize((unsigned)d.in_features);
+            node->setOutputSize((unsigned)d.out_features);
+            break;
+        }
+        case LB200_NODE_RELU:
+            node = std::make_shared<NLR::BoundedReLUNode>(torch::nn::ReLU(), String("relu"));
+            node->setInputSize((unsigned)out_numel);
+            node->setOutputSize((unsigned)out_numel);
+            break;
+        case LB200_NODE_FLATTEN:
+            node = std::make_shared<NLR::BoundedFlattenNode>(Operations::FlattenWrapper(1));
+            node->setInputSize((unsigned)out_numel);
+            node->setOutputSize((unsigned)out_numel);
+            break;
+        case LB200_NODE_IDENTITY:
+            node = std::make_shared<NLR::BoundedIdentityNode>(torch::nn::Identity());
+            node->setInputSize((unsigned)out_numel);
+            node->setOutputSize((unsigned)out_numel);
+            break;
+        default:
+            throw std::runtime_error("luna_ref_driver: node type " + std::to_string(d.type) +
+                                     " is not wired into the reference driver");
+        }
+        node->setNodeIndex((unsigned)i);
+        nodes.append(node);
+        Vector<unsigned> dv;
+        for (int k = 0; k < d.num_inputs; ++k) dv.append((unsigned)d.inputs[k]);
+        deps[(unsigned)i] = dv;
+    }
+    Vector<unsigned> inputs;
+    inputs.append((unsigned)g->input_index);
+    return std::make_shared<NLR::TorchModel>(nodes, inputs, (unsigned)g->output_index, deps);
+}
+
+bool feeds_relu(const lb200_graph_desc* g, int node) {
+    for (int i = 0; i < g->num_nodes; ++i) {
+        const lb200_node_desc& d = g->nodes[i];
+        if (d.type != LB200_NODE_RELU && d.type != LB200_NODE_SIGMOID) continue;
+        if (d.num_inputs > 0 && d.inputs[0] == node) return true;
+    }
+    return false;
+}
+
+}  // namespace
+
+extern "C" {
+
+// Number of floats per box in the intermediate-bound dump: every node that
+// feeds an activation, in node-id order.
+int64_t luna_ref_intermediate_size(const lb200_graph_desc* g) {
+    int64_t n = 0;
+    for (int i = 0; i < g->num_nodes; ++i)
+        if (feeds_relu(g, i))
+            n += (int64_t)g->nodes[i].out_shape[0] * g->nodes[i].out_shape[1] * g->nodes[i].out_shape[2];
+    return n;
+}
+
+// Bound boxes [box_begin, box_end) with Luna.  inter_lb / inter_ub may be
+// NULL; otherwise they receive [n_boxes, luna_ref_intermediate_size] floats.
+int luna_ref_compute_bounds(const lb200_graph_desc* g, const lb200_options* opt, int method,
+                            const float* x_lower, const float* x_upper, int64_t n_boxes,
+                            int64_t n_in, const float* C, int64_t c_boxes, int64_t nspec,
+                            int64_t n_out, float* out_lb, float* out_ub, float* inter_lb,
+                            float* inter_ub, int num_threads, char* err, size_t errlen) {
+    try {
+        at::set_num_threads(num_threads > 0 ? num_threads : 1);
+        apply_options(opt);
+        const int64_t inter_n = luna_ref_intermediate_size(g);
+        for (int64_t b = 0; b < n_boxes; ++b) {
+            auto model = build_model(g);
+            torch::Tensor lb = from_host(x_lower + b * n_in, {n_in});
+            torch::Tensor ub = from_host(x_upper + b * n_in, {n_in});
+            const float* cb = C + (c_boxes == 1 ? 0 : b) * nspec * n_out;
+            torch::Tensor Cm = from_host(cb, {1, nspec, n_out});
+            BoundedTensor<torch::Tensor> box(lb, ub);
+            torch::Tensor rl, ru;
+            if (method == LB200_METHOD_IBP) {
+                model->setInputBounds(box);
+                NLR::CROWNAnalysis an(model.get());
+                an.setInputBounds(box);
+                an.computeIBPBounds();
+                auto ob = an.getOutputIBPBounds();
+                torch::Tensor C2 = Cm.squeeze(0);
+                torch::Tensor Cp = torch::clamp_min(C2, 0), Cn = torch::clamp_max(C2, 0);
+                rl = Cp.matmul(ob.lower().flatten()) + Cn.matmul(ob.upper().flatten());
+                ru = Cp.matmul(ob.upper().flatten()) + Cn.matmul(ob.lower().flatten());
+            } else {
+                auto m = method == LB200_METHOD_ALPHA_CROWN
+                             ? LunaConfiguration::AnalysisMethod::AlphaCROWN
+                             : LunaConfiguration::AnalysisMethod::CROWN;
+                // compute_bounds mutates these two globals; reset them per box.
+                LunaConfiguration::ENABLE_FIRST_LINEAR_IBP = opt->enable_first_linear_ibp != 0;
+                auto res = model->compute_bounds(box, &Cm, m, true, true);
+                rl = res.lower().flatten();
+                ru = res.upper().flatten();
+            }
+            if (rl.numel() != nspec || ru.numel() != nspec)
+                throw std::runtime_error("luna_ref_driver: unexpected bound shape");
+            std::memcpy(out_lb + b * nspec, rl.contiguous().data_ptr<float>(), nspec * sizeof(float));
+            std::memcpy(out_ub + b * nspec, ru.contiguous().data_ptr<float>(), nspec * sizeof(float));
+            if (inter_lb && inter_ub && method != LB200_METHOD_IBP) {
+                auto state = model->getState();
+                int64_t off = 0;
+                for (int i = 0; i < g->num_nodes; ++i) {
+                    if (!feeds_relu(g, i)) continue;
+                    const int64_t sz = (int64_t)g->nodes[i].out_shape[0] * g->nodes[i].out_shape[1] *
+                                       g->nodes[i].out_shape[2];
+                    auto it = state.allBounds.find((unsigned)i);
+                    float* dl = inter_lb + b * inter_n + off;
+                    float* du = inter_ub + b * inter_n + off;
+                    if (it != state.allBounds.end()) {
+                        auto l = it->second.first.flatten().contiguous();
+                        auto u = it->second.second.flatten().contiguous();
+                        std::memcpy(dl, l.data_ptr<float>(), sz * sizeof(float));
+                        std::memcpy(du, u.data_ptr<float>(), sz * sizeof(float));
+                    } else {
+                        for (int64_t k = 0; k < sz; ++k) { dl[k] = NAN; du[k] = NAN; }
+                    }
+                    off += sz;
+                }
+            }
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 1;
+    } catch (...) {
+        set_error(err, errlen, "luna_ref_driver: unknown exception");
+        return 1;
+    }
+}
+
+}  // extern "C"
