@@ -30,6 +30,12 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#if defined(__GNUC__)
+#define LB200_API __attribute__((visibility("default")))
+#else
+#define LB200_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -134,16 +140,16 @@ typedef struct {
 typedef struct lb200_model lb200_model;
 
 /* Fill *opt with Luna's defaults (LunaConfiguration.cpp:28-50). */
-int lb200_options_default(lb200_options* opt);
+LB200_API int lb200_options_default(lb200_options* opt);
 
 /* Build a model on CUDA device `device`.  Replaces
  * TorchModel(nodes, inputIndices, outputIndex, dependencies)
  * (src/engine/TorchModel.h:47-50, TorchModel.cpp:23-64). */
-int lb200_model_create(const lb200_graph_desc* graph, int device, lb200_model** out);
+LB200_API int lb200_model_create(const lb200_graph_desc* graph, int device, lb200_model** out);
 
 /* Set the result-affecting options (the LunaConfiguration globals that
  * TorchModel::compute_bounds reads, TorchModel.cpp:668-670,683-684). */
-int lb200_set_options(lb200_model* model, const lb200_options* opt);
+LB200_API int lb200_set_options(lb200_model* model, const lb200_options* opt);
 
 /* Bound n_boxes input boxes.  Replaces TorchModel::compute_bounds
  * (src/engine/TorchModel.cpp:653-698) called once per box on a fresh model.
@@ -158,7 +164,7 @@ int lb200_set_options(lb200_model* model, const lb200_options* opt);
  *                      setSpecificationMatrix.
  *   out_lb, out_ub   : [n_boxes, nspec] host
  *   stats            : may be NULL. */
-int lb200_compute_bounds(lb200_model* model, int method,
+LB200_API int lb200_compute_bounds(lb200_model* model, int method,
                          const float* x_lower, const float* x_upper, int64_t n_boxes,
                          const float* C, int64_t c_boxes, int64_t nspec,
                          const float* thresholds, int bound_lower, int bound_upper,
@@ -167,7 +173,7 @@ int lb200_compute_bounds(lb200_model* model, int method,
 /* As lb200_compute_bounds, with every array already in device memory of the
  * model's GPU; the work is ordered on `stream` (a cudaStream_t, or NULL for
  * the legacy default stream) and the call returns once it has completed. */
-int lb200_compute_bounds_device(lb200_model* model, int method,
+LB200_API int lb200_compute_bounds_device(lb200_model* model, int method,
                                 const float* d_x_lower, const float* d_x_upper, int64_t n_boxes,
                                 const float* d_C, int64_t c_boxes, int64_t nspec,
                                 const float* d_thresholds, int bound_lower, int bound_upper,
@@ -179,13 +185,13 @@ int lb200_compute_bounds_device(lb200_model* model, int method,
  * size] lower then upper.  Mirrors TorchModel::getState().allBounds
  * (src/engine/TorchModel.cpp:975-1014).  *count receives the total floats
  * per side; pass NULL buffers to query it. */
-int lb200_get_intermediate_bounds(lb200_model* model, float* lower, float* upper, int64_t* count);
+LB200_API int lb200_get_intermediate_bounds(lb200_model* model, float* lower, float* upper, int64_t* count);
 
 /* Copy the last error message of this thread into buf (always terminated). */
-int lb200_last_error(char* buf, size_t len);
+LB200_API int lb200_last_error(char* buf, size_t len);
 
 /* Release the model and every device buffer it owns. */
-void lb200_model_destroy(lb200_model* model);
+LB200_API void lb200_model_destroy(lb200_model* model);
 
 #ifdef __cplusplus
 }

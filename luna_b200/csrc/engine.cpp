@@ -1,0 +1,596 @@
+// engine.cpp -- host orchestration of IBP, CROWN and alpha-CROWN on a batch
+// of boxes (one GPU).
+//
+// Luna bounds one box per call and keeps per-box state on the nodes.  Here a
+// chunk of B boxes shares the network weights and every backward start
+// stacks the rows of all boxes: the A matrix of start s is [2 R_s, n] with
+// R_s = sum over boxes of the IBP-unstable neurons of pre-activation s
+// (CROWNAnalysis::computeIntermediateBoundsLazy, CROWNAnalysis.cpp:1744-1795),
+// so each Linear step is a single GEMM whose epilogue applies the ReLU
+// relaxation of the box that owns the row.
+#include "engine.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+namespace lb200 {
+
+// ------------------------------------------------------------ DevCache
+DevCache::~DevCache() { release(); }
+
+void* DevCache::get(const std::string& name, size_t bytes) {
+    if (bytes == 0) bytes = 16;
+    Buf& b = bufs_[name];
+    if (b.bytes < bytes) {
+        if (b.p) LB_CUDA(cudaFree(b.p));
+        b.p = nullptr;
+        const size_t want = (bytes + 255) & ~size_t(255);
+        LB_CUDA(cudaMalloc(&b.p, want));
+        b.bytes = want;
+    }
+    return b.p;
+}
+
+size_t DevCache::total_bytes() const {
+    size_t t = 0;
+    for (auto& kv : bufs_) t += kv.second.bytes;
+    return t;
+}
+
+void DevCache::release() {
+    for (auto& kv : bufs_)
+        if (kv.second.p) cudaFree(kv.second.p);
+    bufs_.clear();
+}
+
+// ------------------------------------------------------------ Model
+static bool pass_through(int t) { return t == LB200_NODE_FLATTEN || t == LB200_NODE_IDENTITY; }
+
+Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
+    if (!g || g->num_nodes <= 0 || !g->nodes) throw std::invalid_argument("empty graph");
+    LB_CUDA(cudaSetDevice(device_));
+    const int n = g->num_nodes;
+    std::vector<std::vector<int>> dependents(n);
+    for (int i = 0; i < n; ++i) {
+        const auto& d = g->nodes[i];
+        if (d.num_inputs < 0 || d.num_inputs > 4) throw std::invalid_argument("bad num_inputs");
+        for (int k = 0; k < d.num_inputs; ++k) {
+            if (d.inputs[k] < 0 || d.inputs[k] >= n) throw std::invalid_argument("bad input index");
+            dependents[d.inputs[k]].push_back(i);
+        }
+    }
+    if (g->input_index < 0 || g->input_index >= n || g->nodes[g->input_index].type != LB200_NODE_INPUT)
+        throw std::invalid_argument("input_index must name an INPUT node");
+    // Walk the chain Input -> [Linear -> ReLU]* -> Linear (Flatten/Identity
+    // pass through).  Graphs with joins or other node kinds are rejected.
+    int cur = g->input_index;
+    bool expect_linear = true;
+    std::vector<const lb200_node_desc*> lins;
+    while (true) {
+        if (cur == g->output_index) break;
+        if (dependents[cur].size() != 1)
+            throw std::invalid_argument("graph is not a chain (node " + std::to_string(cur) +
+                                        " has " + std::to_string(dependents[cur].size()) +
+                                        " consumers); supported: Input/Linear/ReLU/Flatten/Identity chains");
+        const int nx = dependents[cur][0];
+        const auto& d = g->nodes[nx];
+        if (d.num_inputs != 1) throw std::invalid_argument("multi-input node in chain");
+        if (d.type == LB200_NODE_LINEAR) {
+            if (!expect_linear) throw std::invalid_argument("two Linear nodes without a ReLU between");
+            if (!d.weight || d.in_features <= 0 || d.out_features <= 0)
+                throw std::invalid_argument("Linear node without weight");
+            lins.push_back(&d);
+            expect_linear = false;
+            preact_node_ids_.push_back(nx);
+        } else if (d.type == LB200_NODE_RELU) {
+            if (expect_linear) throw std::invalid_argument("ReLU must follow a Linear node");
+            expect_linear = true;
+        } else if (!pass_through(d.type)) {
+            throw std::invalid_argument("node type " + std::to_string(d.type) +
+                                        " is not supported by this engine build");
+        }
+        cur = nx;
+    }
+    if (g->nodes[g->output_index].type != LB200_NODE_LINEAR || expect_linear)
+        throw std::invalid_argument("the output node must be the last Linear of the chain");
+    if (lins.size() < 2) throw std::invalid_argument("need at least two Linear layers");
+    preact_node_ids_.pop_back();  // the output Linear feeds no ReLU
+    K_ = (int)lins.size();
+    layers_.resize(K_);
+    for (int k = 0; k < K_; ++k) {
+        const auto& d = *lins[k];
+        LinearLayer& L = layers_[k];
+        L.n_in = (int)d.in_features;
+        L.n_out = (int)d.out_features;
+        if (k > 0 && L.n_in != layers_[k - 1].n_out) throw std::invalid_argument("width mismatch");
+        std::vector<float> W((size_t)L.n_out * L.n_in), Wt((size_t)L.n_in * L.n_out), b(L.n_out, 0.f);
+        for (int o = 0; o < L.n_out; ++o)
+            for (int i = 0; i < L.n_in; ++i) {
+                // BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
+                const float w = d.scale * d.weight[(size_t)o * L.n_in + i];
+                W[(size_t)o * L.n_in + i] = w;
+                Wt[(size_t)i * L.n_out + o] = w;
+            }
+        if (d.bias)
+            for (int o = 0; o < L.n_out; ++o) b[o] = d.bias[o];
+        L.W = weights_.as<float>(key("W", k), W.size());
+        L.Wt = weights_.as<float>(key("Wt", k), Wt.size());
+        L.b = weights_.as<float>(key("b", k), b.size());
+        LB_CUDA(cudaMemcpy(L.W, W.data(), W.size() * 4, cudaMemcpyHostToDevice));
+        LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
+        LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+    }
+    lb200_options_default(&opt_);
+}
+
+Model::~Model() {
+    cudaSetDevice(device_);
+    cache_.release();
+    weights_.release();
+}
+
+std::string Model::key(const char* what, int a, int b) const {
+    std::string k(what);
+    k += "/" + std::to_string(a);
+    if (b >= 0) k += "/" + std::to_string(b);
+    return k;
+}
+
+size_t Model::bytes_per_box(bool alpha, int nspec) const {
+    size_t total = 0;
+    const int n0 = width(0);
+    int maxw = 0;
+    for (int m = 0; m <= K_; ++m) maxw = std::max(maxw, width(m));
+    for (int s = 2; s <= K_; ++s) {
+        const size_t rows = 2 * (size_t)(s == K_ ? nspec : width(s));
+        size_t per_row = n0 + 4 * (size_t)maxw * 4 + 64;
+        for (int m = 1; m < s; ++m) per_row += (size_t)width(m) * 4 * (alpha ? 6 : 1);
+        total += rows * per_row;
+    }
+    for (int m = 1; m <= K_; ++m) total += (size_t)width(m) * 4 * 16;
+    return total + (size_t)n0 * 8 + (size_t)nspec * 64;
+}
+
+// ------------------------------------------------------------ row maps
+void Model::build_rows(int B, int nspec, cudaStream_t s) {
+    starts_.assign(K_ + 1, StartPlan{});
+    std::vector<int> totals(K_ + 1, 0);
+    for (int st = 2; st < K_; ++st) {
+        StartPlan& sp = starts_[st];
+        sp.s = st;
+        int* counts = cache_.as<int>(key("counts", st), B);
+        sp.box_off = cache_.as<int>(key("boxoff", st), B + 1);
+        launch_count_unstable(cache_.as<float>(key("ibp_l", st), (size_t)B * width(st)),
+                              cache_.as<float>(key("ibp_u", st), (size_t)B * width(st)), B, width(st),
+                              counts, s);
+        launch_scan_counts(counts, B, sp.box_off, s);
+    }
+    // One synchronisation for all row totals.
+    std::vector<int> host(K_ + 1, 0);
+    for (int st = 2; st < K_; ++st)
+        LB_CUDA(cudaMemcpyAsync(&host[st], starts_[st].box_off + B, sizeof(int), cudaMemcpyDeviceToHost, s));
+    LB_CUDA(cudaStreamSynchronize(s));
+    for (int st = 2; st < K_; ++st) {
+        StartPlan& sp = starts_[st];
+        const int R = host[st];
+        sp.row_box = cache_.as<int>(key("rowbox", st), std::max(R, 1));
+        sp.row_id = cache_.as<int>(key("rowid", st), std::max(R, 1));
+        launch_fill_rows(cache_.as<float>(key("ibp_l", st), (size_t)B * width(st)),
+                         cache_.as<float>(key("ibp_u", st), (size_t)B * width(st)), B, width(st),
+                         sp.box_off, sp.row_box, sp.row_id, s);
+        sp.rows = RowMap{sp.row_box, sp.row_id, sp.box_off, R};
+    }
+    StartPlan& out = starts_[K_];
+    out.s = K_;
+    const int R = B * nspec;
+    out.row_box = cache_.as<int>(key("rowbox", K_), std::max(R, 1));
+    out.row_id = cache_.as<int>(key("rowid", K_), std::max(R, 1));
+    out.box_off = cache_.as<int>(key("boxoff", K_), B + 1);
+    launch_fill_spec_rows(B, nspec, out.row_box, out.row_id, out.box_off, s);
+    out.rows = RowMap{out.row_box, out.row_id, out.box_off, R};
+}
+
+// ------------------------------------------------------------ relaxation
+void Model::relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s) {
+    const int n = width(m);
+    const size_t bn = (size_t)B * n;
+    launch_relu_params(cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B,
+                       n, alpha_mode, create, cache_.as<uint8_t>(key("aset", m), bn),
+                       cache_.as<float>(key("init", m), bn), cache_.as<int>(key("hasaset", m), B),
+                       cache_.as<float>(key("rp_s", m), bn), cache_.as<float>(key("rp_k", m), bn),
+                       cache_.as<float>(key("rp_b", m), bn), cache_.as<uint8_t>(key("rp_f", m), bn), s);
+}
+
+static ReluParams relu_view(DevCache& c, const std::string& sfx, int B, int n) {
+    ReluParams rp;
+    const size_t bn = (size_t)B * n;
+    rp.slope_lo = c.as<float>("rp_s/" + sfx, bn);
+    rp.k_up = c.as<float>("rp_k/" + sfx, bn);
+    rp.b_up = c.as<float>("rp_b/" + sfx, bn);
+    rp.flags = c.as<uint8_t>("rp_f/" + sfx, bn);
+    rp.n = n;
+    return rp;
+}
+
+// ------------------------------------------------------------ forward start
+// Backward substitution from start sp.s (CROWNAnalysis::backwardFrom) down to
+// the input, both sides stacked, ending in the concretisation
+// (computeConcreteLowerBound/UpperBound).  Row totals land in "val/s".
+void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s) {
+    const int st = sp.s;
+    const int R = sp.rows.R;
+    if (R == 0) return;
+    const int M = 2 * R;
+    int maxw = 0;
+    for (int m = 0; m < st; ++m) maxw = std::max(maxw, width(m));
+    float* Q[2] = {cache_.as<float>(key("Q", 0), (size_t)M * maxw), cache_.as<float>(key("Q", 1), (size_t)M * maxw)};
+    float* bias = cache_.as<float>(key("bias", st), M);
+    int slots_total = 0;
+    for (int m = st - 1; m >= 1; --m) slots_total += gemm_tiles_n(width(m - 1));
+    float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
+
+    const LinearLayer& Ls = layers_[st - 1];
+    StartStep ss;
+    ss.rows = sp.rows;
+    ss.M = M;
+    ss.W = Ls.W;
+    ss.bW = Ls.b;
+    ss.spec_dim = Ls.n_out;
+    ss.n = Ls.n_in;
+    if (st == K_) {
+        ss.C = C_;
+        ss.c_per_box = c_per_box_;
+        ss.nspec = nspec;
+        flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
+    }
+    const int mb = st - 1;  // ReLU directly below the start
+    ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+    if (alpha) ss.alpha = cache_.as<float>(key("alpha", mb, st), (size_t)M * width(mb));
+    ss.b_next = layers_[mb - 1].b;
+    if (save) ss.P_save = cache_.as<float>(key("Psave", st, mb), (size_t)M * width(mb));
+    ss.Q = Q[0];
+    ss.bias_acc = bias;
+    launch_start_step(ss, s);
+
+    int cur = 0, slot = 0;
+    for (int m = mb; m >= 1; --m) {
+        const LinearLayer& L = layers_[m - 1];
+        const int N = L.n_in, Kd = L.n_out;
+        flops_ += 2.0 * M * (double)N * Kd;
+        if (m - 1 >= 1) {
+            EpiRelaxFwd e;
+            e.rows = sp.rows;
+            e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
+            if (alpha) e.alpha = cache_.as<float>(key("alpha", m - 1, st), (size_t)M * N);
+            e.b_next = layers_[m - 2].b;
+            if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
+            e.Q = Q[1 - cur];
+            launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            cur = 1 - cur;
+        } else {
+            EpiConcretize e;
+            e.rows = sp.rows;
+            e.xl = xl_;
+            e.xu = xu_;
+            if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * N);
+            launch_gemm_concretize(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+        }
+        slot += gemm_tiles_n(N);
+    }
+    launch_sum_partials(bias, part, slot, M, cache_.as<float>(key("val", st), M), s);
+    rows_ += M;
+}
+
+// ------------------------------------------------------------ adjoint start
+// Reverse sweep of forward_start for M stacked rows with seeds g (d loss /
+// d bound of each row).  Produces d loss / d alpha(m, s) for every ReLU m
+// below the start and accumulates d loss / d (k_up, b_up) of those ReLUs.
+void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s) {
+    const int st = sp.s;
+    const int R = sp.rows.R;
+    if (R == 0 || M == 0) return;
+    int maxw = 0;
+    for (int m = 0; m < st; ++m) maxw = std::max(maxw, width(m));
+    float* Pb[2] = {cache_.as<float>(key("Pbar", 0), (size_t)M * maxw),
+                    cache_.as<float>(key("Pbar", 1), (size_t)M * maxw)};
+    const int n0 = width(0);
+    launch_adj_input_seed(sp.rows, M, cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * n0), g, xl_,
+                          xu_, n0, Pb[0], s);
+    int cur = 0;
+    for (int m = 1; m <= st - 1; ++m) {
+        const LinearLayer& L = layers_[m - 1];
+        const int N = L.n_out, Kd = L.n_in;
+        flops_ += 2.0 * M * (double)N * Kd;
+        EpiRelaxAdj e;
+        e.rows = sp.rows;
+        e.rp = relu_view(cache_, std::to_string(m), B, N);
+        e.gseed = g;
+        e.b_lin = L.b;
+        e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * N);
+        e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * N);
+        e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
+        e.alpha_grad = cache_.as<float>(key("agrad", m, st), (size_t)2 * R * N);
+        const size_t nslot = (size_t)relax_grad_slots(M, B) * N;
+        e.kslot = cache_.as<float>("kslot", nslot);
+        e.bslot = cache_.as<float>("bslot", nslot);
+        e.B = B;
+        launch_gemm_relax_adj(Pb[cur], L.Wt, M, N, Kd, e, nullptr, s);
+        launch_reduce_relax_grad(sp.rows, M, B, N, e.kslot, e.bslot,
+                                 cache_.as<float>(key("kbar", m), (size_t)B * N),
+                                 cache_.as<float>(key("bbar", m), (size_t)B * N), s);
+        cur = 1 - cur;
+    }
+    rows_ += M;
+}
+
+// ------------------------------------------------------------ one pass
+void Model::run_pass(Pass pass, int B, int nspec, cudaStream_t s) {
+    const bool alpha = pass != Pass::CROWN;
+    const bool create = pass == Pass::ALPHA_FIRST;
+    const bool save = pass == Pass::ALPHA_FIRST || pass == Pass::ALPHA_ITER;
+    if (pass == Pass::ALPHA_FINAL) {
+        // Intermediate bounds are the best ones (restoreBestIntermediateBounds)
+        // and are not recomputed (computeIntermediateBoundsLazy sees node bounds).
+        for (int m = 1; m < K_; ++m) {
+            const size_t bn = (size_t)B * width(m) * 4;
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("cur_l", m), bn / 4), cache_.as<float>(key("best_l", m), bn / 4),
+                                    bn, cudaMemcpyDeviceToDevice, s));
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("cur_u", m), bn / 4), cache_.as<float>(key("best_u", m), bn / 4),
+                                    bn, cudaMemcpyDeviceToDevice, s));
+            relu_params(m, B, true, false, s);
+        }
+    } else {
+        for (int m = 1; m < K_; ++m) {
+            const size_t bn = (size_t)B * width(m);
+            float* cl = cache_.as<float>(key("cur_l", m), bn);
+            float* cu = cache_.as<float>(key("cur_u", m), bn);
+            LB_CUDA(cudaMemcpyAsync(cl, cache_.as<float>(key("ibp_l", m), bn), bn * 4, cudaMemcpyDeviceToDevice, s));
+            LB_CUDA(cudaMemcpyAsync(cu, cache_.as<float>(key("ibp_u", m), bn), bn * 4, cudaMemcpyDeviceToDevice, s));
+            if (m >= 2) {
+                StartPlan& sp = starts_[m];
+                if (create)
+                    for (int mm = 1; mm < m; ++mm)
+                        launch_alpha_init(sp.rows, cache_.as<float>(key("init", mm), (size_t)B * width(mm)),
+                                          width(mm), cache_.as<float>(key("alpha", mm, m), (size_t)2 * sp.rows.R * width(mm)), s);
+                forward_start(sp, B, nspec, save, alpha, s);
+                const bool ste = pass == Pass::ALPHA_ITER && opt_.stabilize_intermediate_bounds;
+                launch_scatter_start(sp.rows, cache_.as<float>(key("val", m), (size_t)2 * sp.rows.R),
+                                     ste ? cache_.as<float>(key("best_l", m), bn) : nullptr,
+                                     ste ? cache_.as<float>(key("best_u", m), bn) : nullptr, width(m), cl, cu, s);
+            }
+            relu_params(m, B, alpha, create, s);
+        }
+    }
+    StartPlan& out = starts_[K_];
+    if (create)
+        for (int mm = 1; mm < K_; ++mm)
+            launch_alpha_init(out.rows, cache_.as<float>(key("init", mm), (size_t)B * width(mm)), width(mm),
+                              cache_.as<float>(key("alpha", mm, K_), (size_t)2 * out.rows.R * width(mm)), s);
+    forward_start(out, B, nspec, save, alpha, s);
+}
+
+// ------------------------------------------------------------ one chunk
+void Model::run_chunk(int method, const float* xl, const float* xu, int B, const float* C,
+                      int c_per_box, int nspec, bool upper, float* lb, float* ub, cudaStream_t s) {
+    xl_ = xl;
+    xu_ = xu;
+    C_ = C;
+    c_per_box_ = c_per_box;
+    const int nout = width(K_);
+    // IBP (CROWNAnalysis::computeIBPBounds): pure interval bounds of every Linear.
+    for (int k = 1; k <= K_; ++k) {
+        const size_t bn = (size_t)B * width(k);
+        const float* il = k == 1 ? xl : cache_.as<float>(key("ibp_l", k - 1), (size_t)B * width(k - 1));
+        const float* iu = k == 1 ? xu : cache_.as<float>(key("ibp_u", k - 1), (size_t)B * width(k - 1));
+        launch_ibp_linear(layers_[k - 1].W, layers_[k - 1].b, il, iu, cache_.as<float>(key("ibp_l", k), bn),
+                          cache_.as<float>(key("ibp_u", k), bn), B, width(k - 1), width(k), k > 1, s);
+    }
+    if (method == LB200_METHOD_IBP) {
+        launch_ibp_spec(C, c_per_box, cache_.as<float>(key("ibp_l", K_), (size_t)B * nout),
+                        cache_.as<float>(key("ibp_u", K_), (size_t)B * nout), B, nspec, nout, lb, ub, s);
+        return;
+    }
+    build_rows(B, nspec, s);
+    StartPlan& out = starts_[K_];
+    float* val_out = nullptr;
+    if (method == LB200_METHOD_CROWN) {
+        alpha_ = false;
+        run_pass(Pass::CROWN, B, nspec, s);
+        val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
+        launch_scatter_output(out.rows, val_out, nspec, true, lb, ub, s);
+        return;
+    }
+    if (opt_.optimize_upper) throw std::invalid_argument("optimize_upper is not supported by this engine build");
+    alpha_ = true;
+    // --- AlphaCROWNAnalysis::computeOptimizedBounds(Lower) ------------------
+    run_pass(Pass::ALPHA_FIRST, B, nspec, s);
+    for (int m = 1; m < K_; ++m) {
+        const size_t bn = (size_t)B * width(m) * 4;
+        LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_l", m), bn / 4), cache_.as<float>(key("cur_l", m), bn / 4), bn,
+                                cudaMemcpyDeviceToDevice, s));
+        LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_u", m), bn / 4), cache_.as<float>(key("cur_u", m), bn / 4), bn,
+                                cudaMemcpyDeviceToDevice, s));
+    }
+    BoxControl bc;
+    bc.best = cache_.as<float>("ctl_best", (size_t)B * nspec);
+    bc.best_loss = cache_.as<float>("ctl_bestloss", B);
+    bc.patience = cache_.as<int>("ctl_pat", B);
+    bc.active = cache_.as<int>("ctl_active", B);
+    bc.has_best = cache_.as<int>("ctl_hasbest", B);
+    bc.save = cache_.as<int>("ctl_save", B);
+    bc.improved = cache_.as<uint8_t>("ctl_improved", (size_t)B * nspec);
+    bc.first_save = cache_.as<int>("ctl_first", B);
+    launch_fill_f32(bc.best_loss, INFINITY, B, s);
+    LB_CUDA(cudaMemsetAsync(bc.patience, 0, B * 4, s));
+    LB_CUDA(cudaMemsetAsync(bc.has_best, 0, B * 4, s));
+    LB_CUDA(cudaMemsetAsync(bc.save, 0, B * 4, s));
+    std::vector<int> ones(B, 1);
+    LB_CUDA(cudaMemcpyAsync(bc.active, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
+    LB_CUDA(cudaMemcpyAsync(bc.first_save, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
+    for (int st = 2; st <= K_; ++st)
+        for (int m = 1; m < st; ++m) {
+            const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
+            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("am", m, st), cnt), 0, cnt * 4, s));
+            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("av", m, st), cnt), 0, cnt * 4, s));
+        }
+
+    const int iters = (int)opt_.alpha_iterations;
+    const int save_after = (int)((float)iters * opt_.start_save_best);
+    float lr = opt_.alpha_lr;
+    float* cur_lb = cache_.as<float>("cur_lb", (size_t)B * nspec);
+    float* cur_ub = cache_.as<float>("cur_ub", (size_t)B * nspec);
+    float* gout = cache_.as<float>(key("g", K_), std::max(out.rows.R, 1));
+    int steps = 0;
+    for (int it = 0; it < iters; ++it) {
+        const bool last = it == iters - 1;
+        run_pass(Pass::ALPHA_ITER, B, nspec, s);
+        val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
+        launch_scatter_output(out.rows, val_out, nspec, false, cur_lb, cur_ub, s);
+        launch_alpha_control(bc, cur_lb, B, nspec, it, save_after, (int)opt_.early_stop_patience, !last, s);
+        for (int m = 1; m < K_; ++m) {
+            const size_t bn = (size_t)B * width(m);
+            launch_snapshot(bc.save, cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B,
+                            width(m), cache_.as<float>(key("best_l", m), bn), cache_.as<float>(key("best_u", m), bn), s);
+        }
+        for (int st = 2; st <= K_; ++st)
+            for (int m = 1; m < st; ++m) {
+                const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
+                launch_best_alpha(starts_[st].rows, bc.save, bc.first_save, bc.improved, nspec, width(m),
+                                  cache_.as<float>(key("alpha", m, st), cnt), cache_.as<float>(key("abest", m, st), cnt), s);
+            }
+        launch_clear_first_save(bc.save, bc.first_save, B, s);
+        if (last) break;
+        // --- hand-written adjoint of the whole pass (replaces loss.backward()) ---
+        for (int m = 1; m < K_; ++m) {
+            const size_t bn = (size_t)B * width(m);
+            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("kbar", m), bn), 0, bn * 4, s));
+            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("bbar", m), bn), 0, bn * 4, s));
+        }
+        for (int m = 1; m < K_; ++m) {
+            const size_t cnt = (size_t)2 * out.rows.R * width(m);
+            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("agrad", m, K_), cnt), 0, cnt * 4, s));
+        }
+        launch_output_seed(out.rows, bc.active, gout, s);
+        adjoint_start(out, B, gout, out.rows.R, s);
+        for (int st = K_ - 1; st >= 2; --st) {
+            StartPlan& sp = starts_[st];
+            if (sp.rows.R == 0) continue;
+            const size_t bn = (size_t)B * width(st);
+            float* g = cache_.as<float>(key("g", st), (size_t)2 * sp.rows.R);
+            launch_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn), cache_.as<float>(key("cur_u", st), bn),
+                              cache_.as<uint8_t>(key("rp_f", st), bn), cache_.as<float>(key("kbar", st), bn),
+                              cache_.as<float>(key("bbar", st), bn), width(st), g, s);
+            adjoint_start(sp, B, g, 2 * sp.rows.R, s);
+        }
+        // --- torch::optim::Adam step + clip to [0, 1] ---------------------------
+        ++steps;
+        const double bc1 = 1.0 - std::pow(0.9, steps);
+        const double bc2 = 1.0 - std::pow(0.999, steps);
+        const float step_size = (float)((double)lr / bc1);
+        const float bc2_sqrt = (float)std::sqrt(bc2);
+        for (int st = 2; st <= K_; ++st)
+            for (int m = 1; m < st; ++m) {
+                const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
+                launch_adam(starts_[st].rows, bc.active, width(m), cache_.as<float>(key("alpha", m, st), cnt),
+                            cache_.as<float>(key("am", m, st), cnt), cache_.as<float>(key("av", m, st), cnt),
+                            cache_.as<float>(key("agrad", m, st), cnt), step_size, bc2_sqrt, s);
+            }
+        lr = lr * opt_.alpha_lr_decay;
+    }
+    // --- restoreBestAlphas, restoreBestIntermediateBounds, final run(false) ---
+    for (int st = 2; st <= K_; ++st)
+        for (int m = 1; m < st; ++m) {
+            const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
+            launch_restore_alpha(starts_[st].rows, bc.first_save, width(m), cache_.as<float>(key("abest", m, st), cnt),
+                                 cache_.as<float>(key("alpha", m, st), cnt), s);
+        }
+    run_pass(Pass::ALPHA_FINAL, B, nspec, s);
+    val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
+    // Lower: max(final, best).  Upper: runCROWN over the same nodes, i.e. the
+    // upper side of this pass (same best intermediate bounds and alphas).
+    launch_scatter_output(out.rows, val_out, nspec, upper, lb, ub, s);
+    launch_max_best(bc.best, bc.has_best, B * nspec, nspec, lb, s);
+    (void)nout;
+}
+
+// ------------------------------------------------------------ entry
+void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes, const float* d_C,
+                    int64_t c_boxes, int64_t nspec, const float* d_thr, bool lower, bool upper,
+                    float* d_lb, float* d_ub, cudaStream_t stream, lb200_stats* stats) {
+    (void)lower;
+    if (method < LB200_METHOD_IBP || method > LB200_METHOD_ALPHA_CROWN) throw std::invalid_argument("unknown method");
+    if (n_boxes < 0 || nspec <= 0) throw std::invalid_argument("bad sizes");
+    if (c_boxes != 1 && c_boxes != n_boxes) throw std::invalid_argument("c_boxes must be 1 or n_boxes");
+    if (d_thr) throw std::invalid_argument("thresholds are not supported by this engine build");
+    LB_CUDA(cudaSetDevice(device_));
+    const auto t0 = std::chrono::steady_clock::now();
+    launch_counter() = 0;
+    flops_ = 0.0;
+    rows_ = 0;
+    cudaEvent_t e0, e1;
+    LB_CUDA(cudaEventCreate(&e0));
+    LB_CUDA(cudaEventCreate(&e1));
+    LB_CUDA(cudaEventRecord(e0, stream));
+    const bool alpha = method == LB200_METHOD_ALPHA_CROWN;
+    size_t free_b = 0, total_b = 0;
+    LB_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const size_t budget = (size_t)((double)(free_b + cache_.total_bytes()) * 0.7);
+    const int64_t per_box = std::max<int64_t>(1, (int64_t)bytes_per_box(alpha, (int)nspec));
+    int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(n_boxes, (int64_t)(budget / per_box)));
+    chunk = std::min<int64_t>(chunk, 65536);
+    const int n0 = n_in(), nout = n_out();
+    for (int64_t b0 = 0; b0 < n_boxes; b0 += chunk) {
+        const int B = (int)std::min<int64_t>(chunk, n_boxes - b0);
+        const float* C = d_C + (c_boxes == 1 ? 0 : b0 * nspec * nout);
+        run_chunk(method, d_xl + b0 * n0, d_xu + b0 * n0, B, C, c_boxes == 1 ? 0 : 1, (int)nspec, upper,
+                  d_lb + b0 * nspec, d_ub + b0 * nspec, stream);
+        last_B_ = B;
+    }
+    last_alpha_ = alpha;
+    LB_CUDA(cudaEventRecord(e1, stream));
+    LB_CUDA(cudaEventSynchronize(e1));
+    float ms = 0.f;
+    LB_CUDA(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (stats) {
+        stats->ms_device = ms;
+        stats->ms_total = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        stats->kernel_launches = launch_counter();
+        stats->backward_rows = rows_;
+        stats->algorithmic_flops = flops_;
+        stats->alpha_iterations_run = alpha ? (int)opt_.alpha_iterations : 0;
+    }
+}
+
+int64_t Model::intermediate_count() const {
+    int64_t t = 0;
+    for (int m = 1; m < K_; ++m) t += width(m);
+    return t * last_B_;
+}
+
+void Model::copy_intermediate(float* lower, float* upper) const {
+    // Per box, pre-activations in node-id order (the chain order).
+    const int B = last_B_;
+    int64_t per = 0;
+    for (int m = 1; m < K_; ++m) per += width(m);
+    std::vector<float> tmp;
+    int64_t off = 0;
+    for (int m = 1; m < K_; ++m) {
+        const int n = width(m);
+        tmp.resize((size_t)B * n);
+        for (int side = 0; side < 2; ++side) {
+            const char* nm = last_alpha_ ? (side ? "best_u" : "best_l") : (side ? "cur_u" : "cur_l");
+            const void* src = const_cast<DevCache&>(cache_).get(key(nm, m), (size_t)B * n * 4);
+            LB_CUDA(cudaMemcpy(tmp.data(), src, (size_t)B * n * 4, cudaMemcpyDeviceToHost));
+            float* dst = side ? upper : lower;
+            for (int b = 0; b < B; ++b) std::memcpy(dst + b * per + off, tmp.data() + (size_t)b * n, n * 4);
+        }
+        off += n;
+    }
+}
+
+}  // namespace lb200

@@ -1,0 +1,111 @@
+// engine.h -- host side of the luna_b200 engine.
+//
+// A Model holds one network on one GPU and bounds batches of input boxes
+// with IBP, CROWN or alpha-CROWN, each box exactly as Luna bounds it on a
+// fresh TorchModel (src/engine/TorchModel.cpp:653-698).
+#pragma once
+
+#include "../../include/luna_b200.h"
+#include "kernels.cuh"
+
+#include <map>
+#include <string>
+#include <vector>
+
+namespace lb200 {
+
+// Grow-only cache of named device buffers owned by a model.
+class DevCache {
+public:
+    ~DevCache();
+    void* get(const std::string& name, size_t bytes);
+    template <class T>
+    T* as(const std::string& name, size_t count) {
+        return static_cast<T*>(get(name, count * sizeof(T)));
+    }
+    size_t total_bytes() const;
+    void release();
+
+private:
+    struct Buf {
+        void* p = nullptr;
+        size_t bytes = 0;
+    };
+    std::map<std::string, Buf> bufs_;
+};
+
+struct LinearLayer {
+    int n_in = 0, n_out = 0;
+    float* W = nullptr;   // [n_out, n_in]
+    float* Wt = nullptr;  // [n_in, n_out]
+    float* b = nullptr;   // [n_out]
+};
+
+struct StartPlan {
+    int s = 0;          // pre-activation index (1..K-1), or K for the output start
+    RowMap rows;        // device row map (R rows per side)
+    int* row_box = nullptr;
+    int* row_id = nullptr;
+    int* box_off = nullptr;
+};
+
+class Model {
+public:
+    Model(const lb200_graph_desc* g, int device);
+    ~Model();
+
+    void set_options(const lb200_options& o) { opt_ = o; }
+    const lb200_options& options() const { return opt_; }
+
+    void compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes,
+                 const float* d_C, int64_t c_boxes, int64_t nspec, const float* d_thr,
+                 bool lower, bool upper, float* d_lb, float* d_ub, cudaStream_t stream,
+                 lb200_stats* stats);
+
+    // Host-side upload helpers for the host-buffer entry point.
+    float* staging(const std::string& name, size_t count) { return cache_.as<float>(name, count); }
+    int device() const { return device_; }
+    int n_in() const { return layers_.front().n_in; }
+    int n_out() const { return layers_.back().n_out; }
+    int64_t intermediate_count() const;
+    void copy_intermediate(float* lower, float* upper) const;
+
+private:
+    // One bounded chunk of boxes.
+    void run_chunk(int method, const float* xl, const float* xu, int B, const float* C, int c_per_box,
+                   int nspec, bool upper, float* lb, float* ub, cudaStream_t s);
+
+    enum class Pass { CROWN, ALPHA_FIRST, ALPHA_ITER, ALPHA_FINAL };
+    void run_pass(Pass pass, int B, int nspec, cudaStream_t s);
+    void forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s);
+    void adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s);
+    void relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s);
+    void build_rows(int B, int nspec, cudaStream_t s);
+    void alloc_alpha(int B, cudaStream_t s);
+    size_t bytes_per_box(bool alpha, int nspec) const;
+
+    int width(int m) const { return m == 0 ? layers_[0].n_in : layers_[m - 1].n_out; }
+    std::string key(const char* what, int a, int b = -1) const;
+
+    int device_ = 0;
+    lb200_options opt_{};
+    std::vector<LinearLayer> layers_;  // chain Linear 1..K
+    std::vector<int> preact_node_ids_; // node ids of Linear 1..K-1 outputs
+    DevCache weights_;
+    DevCache cache_;
+
+    // Per-chunk state.
+    int K_ = 0;
+    std::vector<StartPlan> starts_;    // index s in 2..K-1 and K (output)
+    const float* xl_ = nullptr;
+    const float* xu_ = nullptr;
+    const float* C_ = nullptr;
+    int c_per_box_ = 0;
+    bool alpha_ = false;
+    double flops_ = 0.0;
+    int64_t rows_ = 0;
+    int last_B_ = 0;
+    bool last_alpha_ = false;
+};
+
+}  // namespace lb200

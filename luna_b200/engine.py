@@ -1,0 +1,141 @@
+"""Python binding of the engine's C ABI (include/luna_b200.h) via ctypes.
+
+This mirrors Luna's TorchModel entry point for the bound-propagation path:
+`Model(graph)` replaces `TorchModel(nodes, inputIndices, outputIndex,
+dependencies)` (src/engine/TorchModel.h:47-50) and `Model.compute_bounds`
+replaces `TorchModel::compute_bounds` (src/engine/TorchModel.cpp:653-698),
+bounding a whole batch of boxes per call.  Errors raise `EngineError` with the
+engine's message, as Luna raises exceptions.  There is no CPU fallback: the
+CUDA library must be present and a GPU visible.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+from .abi import GraphDesc, Options, Stats, default_options, fptr
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libluna_b200.so")
+
+EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
+           "lb200_compute_bounds", "lb200_compute_bounds_device",
+           "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy")
+
+
+class EngineError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def load_library():
+    """Load libluna_b200.so; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise EngineError(f"{LIB_PATH} not built (python -m luna_b200.build)")
+    lib = C.CDLL(LIB_PATH)
+    fp = C.POINTER(C.c_float)
+    vp = C.c_void_p
+    lib.lb200_options_default.argtypes = [C.POINTER(Options)]
+    lib.lb200_model_create.argtypes = [C.POINTER(GraphDesc), C.c_int, C.POINTER(vp)]
+    lib.lb200_set_options.argtypes = [vp, C.POINTER(Options)]
+    lib.lb200_compute_bounds.argtypes = [vp, C.c_int, fp, fp, C.c_int64, fp, C.c_int64, C.c_int64,
+                                         fp, C.c_int, C.c_int, fp, fp, C.POINTER(Stats)]
+    lib.lb200_compute_bounds_device.argtypes = [vp, C.c_int, vp, vp, C.c_int64, vp, C.c_int64,
+                                                C.c_int64, vp, C.c_int, C.c_int, vp, vp, vp,
+                                                C.POINTER(Stats)]
+    lib.lb200_get_intermediate_bounds.argtypes = [vp, fp, fp, C.POINTER(C.c_int64)]
+    lib.lb200_last_error.argtypes = [C.c_char_p, C.c_size_t]
+    lib.lb200_model_destroy.argtypes = [vp]
+    lib.lb200_model_destroy.restype = None
+    _lib = lib
+    return lib
+
+
+def _check(rc: int, what: str):
+    if rc != 0:
+        buf = C.create_string_buffer(4096)
+        _lib.lb200_last_error(buf, len(buf))
+        raise EngineError(f"{what}: {buf.value.decode(errors='replace')}")
+
+
+class Model:
+    """One network on one GPU."""
+
+    def __init__(self, graph, device: int = 0, options: Options | None = None):
+        lib = load_library()
+        self.graph = graph
+        self._desc = graph.desc()
+        h = C.c_void_p()
+        _check(lib.lb200_model_create(C.byref(self._desc), device, C.byref(h)), "lb200_model_create")
+        self._h = h
+        self.options = options if options is not None else default_options()
+        self.set_options(self.options)
+        self.last_stats = Stats()
+
+    def set_options(self, options: Options):
+        self.options = options
+        _check(_lib.lb200_set_options(self._h, C.byref(options)), "lb200_set_options")
+
+    def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,
+                       out_lb: np.ndarray | None = None, out_ub: np.ndarray | None = None):
+        """Bound every box from host arrays; returns (lb, ub) as [B, nspec] fp32."""
+        xl = np.ascontiguousarray(boxes.lower, np.float32)
+        xu = np.ascontiguousarray(boxes.upper, np.float32)
+        Cm = np.ascontiguousarray(boxes.C, np.float32)
+        B, nspec = xl.shape[0], Cm.shape[1]
+        lb = out_lb if out_lb is not None else np.empty((B, nspec), np.float32)
+        ub = out_ub if out_ub is not None else np.empty((B, nspec), np.float32)
+        st = Stats()
+        _check(_lib.lb200_compute_bounds(self._h, method, fptr(xl), fptr(xu), B, fptr(Cm), Cm.shape[0],
+                                         nspec, fptr(None), int(bound_lower), int(bound_upper),
+                                         fptr(lb), fptr(ub), C.byref(st)), "lb200_compute_bounds")
+        self.last_stats = st
+        return lb, ub
+
+    def compute_bounds_ptr(self, method: int, xl: int, xu: int, n_boxes: int, Cp: int, c_boxes: int,
+                           nspec: int, lb: int, ub: int, stream: int = 0):
+        """Device-pointer variant (pointers as ints, e.g. torch data_ptr())."""
+        st = Stats()
+        _check(_lib.lb200_compute_bounds_device(self._h, method, xl, xu, n_boxes, Cp, c_boxes, nspec,
+                                                None, 1, 1, lb, ub, stream or None, C.byref(st)),
+               "lb200_compute_bounds_device")
+        self.last_stats = st
+        return st
+
+    def compute_bounds_host_ptr(self, method: int, xl: int, xu: int, n_boxes: int, Cp: int,
+                                c_boxes: int, nspec: int, lb: int, ub: int):
+        """Host-pointer variant (pointers as ints, e.g. pinned torch tensors)."""
+        st = Stats()
+        f = C.POINTER(C.c_float)
+        _check(_lib.lb200_compute_bounds(self._h, method, C.cast(xl, f), C.cast(xu, f), n_boxes,
+                                         C.cast(Cp, f), c_boxes, nspec, f(), 1, 1, C.cast(lb, f),
+                                         C.cast(ub, f), C.byref(st)), "lb200_compute_bounds")
+        self.last_stats = st
+        return st
+
+    def intermediate_bounds(self):
+        """Pre-activation bounds of the last call, [B, sum of widths] lower and upper."""
+        cnt = C.c_int64()
+        _check(_lib.lb200_get_intermediate_bounds(self._h, None, None, C.byref(cnt)), "intermediate")
+        lo = np.empty(cnt.value, np.float32)
+        hi = np.empty(cnt.value, np.float32)
+        _check(_lib.lb200_get_intermediate_bounds(self._h, fptr(lo), fptr(hi), C.byref(cnt)), "intermediate")
+        return lo, hi
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.lb200_model_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

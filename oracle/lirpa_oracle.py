@@ -227,7 +227,9 @@ class LirpaOracle:
         idx = torch.nonzero(mask).flatten()
         init = d_lo.detach().flatten().index_select(0, idx)
         a = init.view(1, 1, -1).expand(2, spec, idx.numel()).contiguous().clone()
-        a = torch.clamp(a, 0.0, 1.0).detach().requires_grad_(True)
+        # With no unstable neuron Luna stores an empty alpha that does not
+        # require grad (AlphaCROWNAnalysis.cpp:179-188).
+        a = torch.clamp(a, 0.0, 1.0).detach().requires_grad_(idx.numel() > 0)
         ap = _Alpha(a, idx)
         st.alphas[key] = ap
         return ap
@@ -406,7 +408,17 @@ class LirpaOracle:
                     for i in self.preact_ids if i in st.node_bounds}
         if o.stabilize_intermediate_bounds:
             st.reference = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
-        params = [ap.alpha for ap in st.alphas.values()]
+        params = [ap.alpha for ap in st.alphas.values() if ap.alpha.requires_grad]
+        if not params:
+            # collectAlphaParameters() found nothing to optimise: one more
+            # run(false) over the bounds still on the nodes (:360-364).
+            with torch.no_grad():
+                lo, _ = self._run(st, x, C)
+                st2 = _BoxState(node_bounds={k: v for k, v in st.node_bounds.items() if k in best_int},
+                                alphas=st.alphas, alpha_mode=True, method_alpha=True,
+                                first_linear_ibp=False)
+                _, hi = self._run(st2, x, C)
+            return lo.detach(), hi.detach(), best_int
         adam = _Adam(params)
         iters = int(o.alpha_iterations)
         best = None

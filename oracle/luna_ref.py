@@ -26,6 +26,11 @@ def available() -> bool:
 def _load():
     global _lib
     if _lib is None:
+        # libluna_ref.so links the venv's libtorch; loading it through torch's
+        # own import initialises libtorch the way the reference expects (a
+        # bare dlopen crashed inside exception handling of the reference's
+        # best-effort centre forward pass).
+        import torch  # noqa: F401
         if not available():
             raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C oracle`")
         lib = C.CDLL(LIB_PATH)

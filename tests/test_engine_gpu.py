@@ -1,0 +1,119 @@
+"""Parity of the CUDA engine with Luna (golden fixtures) and with the CPU
+oracle, plus soundness by sampling.  Every call goes through the C ABI."""
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as G
+from luna_b200 import abi, workloads as W
+from luna_b200.engine import Model
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from luna_b200.build import build
+    build()
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+
+
+@pytest.mark.parametrize("name", G.names())
+def test_engine_matches_luna(name):
+    c = G.load(name)
+    m = Model(c["graph"], options=c["options"])
+    lb, ub = m.compute_bounds(c["boxes"], c["method"])
+    assert m.last_stats.kernel_launches > 0
+    print(f"{name}: lb excess {G.excess(lb, c['lb']):.3f} ub excess {G.excess(ub, c['ub']):.3f}")
+    assert G.excess(lb, c["lb"]) <= 1.0, G.excess(lb, c["lb"])
+    assert G.excess(ub, c["ub"]) <= 1.0, G.excess(ub, c["ub"])
+    if "inter_lb" in c:
+        lo, hi = m.intermediate_bounds()
+        B = c["boxes"].n
+        e, states = G.check_intermediate(lo.reshape(B, -1), hi.reshape(B, -1), c["inter_lb"], c["inter_ub"])
+        assert e <= 1.0 and states, e
+
+
+@pytest.mark.parametrize("seed", range(4))
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_engine_matches_oracle_random(seed, method):
+    from oracle.lirpa_oracle import LirpaOracle
+    g, bx = W.random_mlp_case(500 + seed, n_boxes=6, depth=2 + seed % 3, width=16)
+    opt = abi.default_options(alpha_lr=0.3, alpha_iterations=6)
+    lb, ub = Model(g, options=opt).compute_bounds(bx, method)
+    olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
+    assert G.excess(lb, olb) <= 1.0
+    assert G.excess(ub, oub) <= 1.0
+
+
+def _sample_outputs(graph, boxes, n_pts, seed=0):
+    """C . f(x) at n_pts uniform points (and the corners' mix) per box, on the GPU."""
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    lo = torch.from_numpy(boxes.lower).cuda()
+    hi = torch.from_numpy(boxes.upper).cuda()
+    Cm = torch.from_numpy(boxes.C).cuda()
+    B = lo.shape[0]
+    out = []
+    for b in range(B):
+        t = torch.rand((n_pts, lo.shape[1]), generator=gen, device="cuda")
+        t[: n_pts // 10] = (t[: n_pts // 10] > 0.5).float()  # vertices
+        x = lo[b] + t * (hi[b] - lo[b])
+        for n in graph.nodes:
+            if n.type == abi.NODE_LINEAR:
+                x = x @ torch.from_numpy(n.weight).cuda().T + torch.from_numpy(n.bias).cuda()
+            elif n.type == abi.NODE_RELU:
+                x = torch.relu(x)
+        c = Cm[0 if Cm.shape[0] == 1 else b]
+        out.append((x @ c.T))
+    return out
+
+
+@pytest.mark.parametrize("method", [abi.METHOD_IBP, abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_sound_by_sampling(method):
+    g, bx = W.mlp_784_256x4_10(8)
+    opt = abi.default_options(alpha_lr=0.1)
+    lb, ub = Model(g, options=opt).compute_bounds(bx, method)
+    ys = _sample_outputs(g, bx, 100_000)
+    for b, y in enumerate(ys):
+        tol = 1e-4 * (1 + np.abs(lb[b]).max())
+        assert (y.min(0).values.cpu().numpy() >= lb[b] - tol).all()
+        assert (y.max(0).values.cpu().numpy() <= ub[b] + tol).all()
+
+
+def test_full_size_properties():
+    """512 boxes of the 784-256x4-10 MLP: alpha-CROWN is sound, at least as
+    tight as CROWN, and CROWN is at least as tight as IBP."""
+    g, bx = W.mlp_784_256x4_10(512)
+    opt = abi.default_options(alpha_lr=0.1)
+    m = Model(g, options=opt)
+    ilb, iub = m.compute_bounds(bx, abi.METHOD_IBP)
+    clb, cub = m.compute_bounds(bx, abi.METHOD_CROWN)
+    alb, aub = m.compute_bounds(bx, abi.METHOD_ALPHA_CROWN)
+    assert np.isfinite(alb).all() and np.isfinite(aub).all()
+    tol = 1e-4 * (1 + np.abs(clb))
+    assert (clb >= ilb - tol).all() and (cub <= iub + tol).all()
+    assert (alb >= clb - tol).all()
+    assert (alb <= aub).all()
+    sub = bx.slice(0, 16)
+    for b, y in enumerate(_sample_outputs(g, sub, 20_000, seed=1)):
+        assert (y.min(0).values.cpu().numpy() >= alb[b] - tol[b]).all()
+        assert (y.max(0).values.cpu().numpy() <= aub[b] + tol[b]).all()
+    # Per-box independence: a box bounded alone gets the same result.
+    one = Model(g, options=opt).compute_bounds(bx.slice(5, 6), abi.METHOD_ALPHA_CROWN)
+    assert G.excess(one[0], alb[5:6]) <= 1.0 and G.excess(one[1], aub[5:6]) <= 1.0
+
+
+def test_device_pointer_entry_point_matches_host_entry_point():
+    g, bx = W.mlp_5_50x6_5(64)
+    m = Model(g, options=abi.default_options(alpha_lr=0.1))
+    lb, ub = m.compute_bounds(bx, abi.METHOD_ALPHA_CROWN)
+    xl = torch.from_numpy(bx.lower).cuda()
+    xu = torch.from_numpy(bx.upper).cuda()
+    Cm = torch.from_numpy(bx.C).cuda()
+    dl = torch.empty((64, 4), device="cuda")
+    du = torch.empty((64, 4), device="cuda")
+    s = torch.cuda.current_stream()
+    m.compute_bounds_ptr(abi.METHOD_ALPHA_CROWN, xl.data_ptr(), xu.data_ptr(), 64, Cm.data_ptr(), 1, 4,
+                         dl.data_ptr(), du.data_ptr(), s.cuda_stream)
+    # Same computation through both entry points: bit-identical results.
+    assert np.array_equal(dl.cpu().numpy(), lb) and np.array_equal(du.cpu().numpy(), ub)

@@ -1,0 +1,45 @@
+"""The CPU oracle (oracle/lirpa_oracle.py) against Luna's own outputs.
+
+The golden fixtures were produced by Luna's CPU implementation compiled from
+the reference sources (tests/golden/make_golden.py); the oracle is trusted as
+the parity checker only because it reproduces them.
+"""
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as G
+from oracle.lirpa_oracle import LirpaOracle
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _one_thread():
+    n = torch.get_num_threads()
+    torch.set_num_threads(1)
+    yield
+    torch.set_num_threads(n)
+
+
+@pytest.mark.parametrize("name", G.names())
+def test_oracle_matches_luna(name):
+    c = G.load(name)
+    res = LirpaOracle(c["graph"], c["options"]).compute_bounds(c["boxes"], c["method"],
+                                                               intermediate="inter_lb" in c)
+    assert G.excess(res[0], c["lb"]) <= 1.0
+    assert G.excess(res[1], c["ub"]) <= 1.0
+    if "inter_lb" in c:
+        e, states = G.check_intermediate(res[2], res[3], c["inter_lb"], c["inter_ub"])
+        assert e <= 1.0 and states
+
+
+def test_planted_error_is_caught():
+    """A wrong relaxation planted in the oracle must break parity."""
+    c = G.load("mlp5_crown")
+    orc = LirpaOracle(c["graph"], c["options"])
+    orig = LirpaOracle._upper
+    try:
+        LirpaOracle._upper = staticmethod(lambda l, u: tuple(v * 1.001 for v in orig(l, u)))
+        lb, ub = orc.compute_bounds(c["boxes"], c["method"])
+    finally:
+        LirpaOracle._upper = staticmethod(orig)
+    assert G.excess(lb, c["lb"]) > 1.0 or G.excess(ub, c["ub"]) > 1.0
