@@ -1,0 +1,380 @@
+"""Throughput of alpha-CROWN bounding on B200: input boxes per second.
+
+Workload (per GPU): the MLP 784->256->256->256->256->10 with ReLU (He-normal
+weights, seed 1), 512 L-inf boxes (centres U[0,1]^784, eps 0.02 clipped to
+[0,1]), 9 margin rows y_t - y_j per box, alpha-CROWN with 20 Adam iterations
+at lr 0.1, lower bounds optimised and upper bounds by CROWN, all as Luna's
+TorchModel::compute_bounds(..., AlphaCROWN) does for each box.
+
+A step bounds one batch of 512 boxes per GPU.  With N GPUs (torchrun) each
+rank bounds its own 512 boxes (weak scaling) and the final bounds are
+all-gathered over NCCL inside the step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+`--impl reference` times Luna's own CPU implementation (oracle/_ref) on the
+host cores for the same workload and metric.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import multiprocessing as mp
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+from luna_b200 import abi, workloads as W  # noqa: E402
+
+BOXES_PER_GPU = 512
+ITERS = 20
+LR = 0.1
+METRIC = "alpha_crown_boxes_per_sec"
+UNIT = "boxes/s"
+WORKLOAD = "mlp_784_256x4_10 alpha-CROWN (20 Adam iterations, lr 0.1), 512 boxes per GPU, eps 0.02, 9 margin specs"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def options():
+    return abi.default_options(alpha_lr=LR, alpha_iterations=ITERS)
+
+
+def config(n_gpus):
+    return {"workload": WORKLOAD, "boxes_per_gpu": BOXES_PER_GPU, "global_boxes": BOXES_PER_GPU * n_gpus,
+            "input_dim": 784, "nspec": 9, "alpha_iterations": ITERS, "alpha_lr": LR,
+            "parallelism": f"box-sharded x{n_gpus}", "l2": "flushed between timed steps (256 MiB write)"}
+
+
+def rank_boxes(rank, n_gpus):
+    """This rank's slice of one seeded global box set (same weights on every rank)."""
+    g, bx = W.mlp_784_256x4_10(BOXES_PER_GPU * n_gpus)
+    return g, bx.slice(rank * BOXES_PER_GPU, (rank + 1) * BOXES_PER_GPU)
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- peaks
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p, "measured"
+    except OSError:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per launch of the contraction kernel from the committed ncu summary."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "contraction_traffic.json")) as f:
+            return json.load(f)
+    except OSError:
+        return None
+
+
+# ---------------------------------------------------------------- engine arm
+def run_engine(args):
+    import torch
+    import torch.distributed as dist
+
+    from luna_b200.build import build
+    from luna_b200.engine import Model
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    if rank == 0:
+        build()
+    if world > 1:
+        dist.barrier()
+    g, bx = rank_boxes(rank, world)
+    model = Model(g, device=local, options=options())
+    dev = torch.device("cuda", local)
+    xl = torch.from_numpy(bx.lower).to(dev)
+    xu = torch.from_numpy(bx.upper).to(dev)
+    Cm = torch.from_numpy(bx.C).to(dev)
+    B, nspec = bx.n, bx.C.shape[1]
+    lb = torch.empty((B, nspec), device=dev)
+    ub = torch.empty((B, nspec), device=dev)
+    gathered = torch.empty((world, 2, B, nspec), device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        model.compute_bounds_ptr(abi.METHOD_ALPHA_CROWN, xl.data_ptr(), xu.data_ptr(), B, Cm.data_ptr(),
+                                 Cm.shape[0], nspec, lb.data_ptr(), ub.data_ptr(), stream.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, torch.stack([lb, ub]).unsqueeze(0).contiguous())
+        return model.last_stats
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+
+    # ---- device-resident timing: per-step CUDA events, L2 flushed between steps
+    model.set_profiling(True)
+    sampler = ClockSampler(local)
+    sampler.start()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    total_ms, launches, contr_ms, contr_flops, contr_launches, flops = 0.0, 0, 0.0, 0.0, 0, 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        st = step()
+        e1.record(stream)
+        e1.synchronize()
+        total_ms += e0.elapsed_time(e1)
+        launches += st.kernel_launches
+        contr_ms += st.ms_contractions
+        contr_flops += st.contraction_flops
+        contr_launches += st.contraction_launches
+        flops += st.algorithmic_flops
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop()
+    model.set_profiling(False)
+    t = torch.tensor([total_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = float(t.item()) / args.steps
+
+    # ---- end to end through the host-buffer C ABI (pinned host memory)
+    hxl = torch.from_numpy(bx.lower).pin_memory()
+    hxu = torch.from_numpy(bx.upper).pin_memory()
+    hC = torch.from_numpy(bx.C).pin_memory()
+    hlb = torch.empty((B, nspec)).pin_memory()
+    hub = torch.empty((B, nspec)).pin_memory()
+    model.compute_bounds_host_ptr(abi.METHOD_ALPHA_CROWN, hxl.data_ptr(), hxu.data_ptr(), B, hC.data_ptr(),
+                                  hC.shape[0], nspec, hlb.data_ptr(), hub.data_ptr())
+    if world > 1:
+        dist.barrier()
+    e2e_steps = max(1, min(args.steps, 3))
+    t0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        model.compute_bounds_host_ptr(abi.METHOD_ALPHA_CROWN, hxl.data_ptr(), hxu.data_ptr(), B,
+                                      hC.data_ptr(), hC.shape[0], nspec, hlb.data_ptr(), hub.data_ptr())
+    e2e_s = (time.perf_counter() - t0) / e2e_steps
+    te = torch.tensor([e2e_s], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+
+    if rank == 0:
+        pk, pk_src = peaks()
+        # 3xTF32 split fp32 contractions: TF32 dense is half the bf16 rate and
+        # the split issues three MMAs per product.
+        peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
+        achieved = (contr_flops / contr_launches) / (contr_ms / contr_launches) / 1e9 if contr_launches else 0.0
+        tr = traffic_per_launch()
+        line = {
+            "metric": METRIC, "value": world * B / (ms_per_step / 1e3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded He-normal weights, uniform box centres)",
+            "config": config(world),
+            "e2e": {"value": world * B / e2e_s, "unit": UNIT,
+                    "h2d_bytes_per_step": int(hxl.numel() * 4 + hxu.numel() * 4 + hC.numel() * 4),
+                    "d2h_bytes_per_step": int(hlb.numel() * 4 + hub.numel() * 4)},
+            "gpu_launches": int(launches),
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak if peak else None,
+                         "traffic": tr.get("bytes_per_launch") if tr else None,
+                         "kernel": "A.W contraction (GEMM + fused relaxation / concretisation / adjoint epilogue)",
+                         "peak_source": f"{pk_src}: bf16_tflops_sustained / 2 (TF32) / 3 (3-pass split)",
+                         "contraction_share_of_step": contr_ms / total_ms if total_ms else None,
+                         "algorithmic_tflops_step": flops / (total_ms / 1e3) / 1e12 if total_ms else None},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_boxes)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- reference arm
+_REF = {}
+
+
+def _ref_worker(span):
+    """One host process: bound boxes [a, b) of the workload with Luna's CPU
+    path on one thread.  The reference library and the workload are loaded
+    once per process."""
+    if not _REF:
+        os.environ["CUDA_VISIBLE_DEVICES"] = ""
+        for var in ("OMP_NUM_THREADS", "MKL_NUM_THREADS", "OPENBLAS_NUM_THREADS"):
+            os.environ[var] = "1"
+        from oracle import luna_ref
+        _REF["lib"] = luna_ref
+        _REF["work"] = W.mlp_784_256x4_10(BOXES_PER_GPU)
+    a, b = span
+    if b <= a:
+        return 0.0
+    g, bx = _REF["work"]
+    t0 = time.perf_counter()
+    _REF["lib"].compute_bounds(g, bx.slice(a, b), abi.METHOD_ALPHA_CROWN, options(), num_threads=1)
+    return time.perf_counter() - t0
+
+
+class CpuBaseline:
+    """Luna's CPU implementation (oracle/_ref) on the host cores: one process
+    per core, one thread each; a sample bounds `boxes_per_proc` boxes per
+    process."""
+
+    def __init__(self, procs=None):
+        self.procs = procs or min(os.cpu_count() or 1, BOXES_PER_GPU)
+        self.pool = mp.get_context("spawn").Pool(self.procs)
+        self.pool.map(_ref_worker, [(0, 0)] * self.procs)  # load the library in every worker
+
+    def sample(self, boxes_per_proc=1):
+        work = [((i * boxes_per_proc) % BOXES_PER_GPU, (i * boxes_per_proc) % BOXES_PER_GPU + boxes_per_proc)
+                for i in range(self.procs)]
+        t0 = time.perf_counter()
+        self.pool.map(_ref_worker, work, chunksize=1)
+        wall = time.perf_counter() - t0
+        n = self.procs * boxes_per_proc
+        return {"value": n / wall, "unit": UNIT, "cores": self.procs, "kind": "reference",
+                "sample": f"{n} of the 512 boxes ({boxes_per_proc} per process, {self.procs} processes x 1 "
+                          f"thread), wall {wall:.2f} s", "wall_s": wall, "boxes": n}
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def cpu_baseline(boxes_per_proc=1):
+    cb = CpuBaseline()
+    try:
+        return cb.sample(boxes_per_proc)
+    finally:
+        cb.close()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import luna_ref
+    if not luna_ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libluna_ref.so not built"}))
+        return
+    cb = CpuBaseline()
+    try:
+        for _ in range(args.warmup):
+            cb.sample(1)
+        vals = [cb.sample(args.cpu_boxes) for _ in range(args.steps)]
+    finally:
+        cb.close()
+    boxes = sum(x["boxes"] for x in vals)
+    wall = sum(x["wall_s"] for x in vals)
+    v = boxes / wall
+    base = dict(vals[0])
+    base["value"] = v
+    base["sample"] = f"{args.steps} samples of {vals[0]['boxes']} boxes ({args.cpu_boxes} per process, " \
+                     f"{cb.procs} processes x 1 thread)"
+    line = {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * wall / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded He-normal weights, uniform box centres)", "config": config(args.gpus),
+            "impl": "reference", "cpu_baseline": base,
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
+    ap.add_argument("--cpu-boxes", type=int, default=1, help="boxes per host process in the CPU baseline")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--boxes", type=int, default=BOXES_PER_GPU,
+                    help="boxes per GPU (smaller cases are for profiling only)")
+    args = ap.parse_args()
+    if args.boxes != BOXES_PER_GPU:
+        globals()["BOXES_PER_GPU"] = args.boxes
+        globals()["WORKLOAD"] = WORKLOAD.replace("512 boxes", f"{args.boxes} boxes")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_engine(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -135,6 +135,11 @@ typedef struct {
     int64_t backward_rows;    /* A-matrix rows (both sides) propagated */
     double algorithmic_flops; /* 2*M*N*K summed over real rows, contractions */
     int32_t alpha_iterations_run; /* max over boxes */
+    /* Filled when profiling is on (lb200_set_profiling): CUDA-event time of
+     * the A.W contraction kernels, their launches and their 2*M*N*K. */
+    double ms_contractions;
+    int64_t contraction_launches;
+    double contraction_flops;
 } lb200_stats;
 
 typedef struct lb200_model lb200_model;
@@ -179,6 +184,11 @@ LB200_API int lb200_compute_bounds_device(lb200_model* model, int method,
                                 const float* d_thresholds, int bound_lower, int bound_upper,
                                 float* d_out_lb, float* d_out_ub, void* stream,
                                 lb200_stats* stats);
+
+/* Time every A.W contraction kernel with CUDA events on the launching stream
+ * (on != 0) so lb200_stats reports ms_contractions.  Off by default.  Luna
+ * has no counterpart: it exists for roofline measurement. */
+LB200_API int lb200_set_profiling(lb200_model* model, int on);
 
 /* Copy the intermediate (pre-activation) bounds of the last call into host
  * buffers: for every node that feeds a ReLU, in node-id order, [n_boxes,

@@ -90,6 +90,9 @@ class Stats(C.Structure):
         ("backward_rows", C.c_int64),
         ("algorithmic_flops", C.c_double),
         ("alpha_iterations_run", C.c_int32),
+        ("ms_contractions", C.c_double),
+        ("contraction_launches", C.c_int64),
+        ("contraction_flops", C.c_double),
     ]
 
 

@@ -78,6 +78,12 @@ int lb200_set_options(lb200_model* model, const lb200_options* opt) {
     return 0;
 }
 
+int lb200_set_profiling(lb200_model* model, int on) {
+    if (!model) return fail("lb200_set_profiling: null model");
+    model->m->set_profiling(on != 0);
+    return 0;
+}
+
 int lb200_compute_bounds_device(lb200_model* model, int method, const float* d_x_lower,
                                 const float* d_x_upper, int64_t n_boxes, const float* d_C,
                                 int64_t c_boxes, int64_t nspec, const float* d_thresholds,

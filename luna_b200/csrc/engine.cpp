@@ -128,6 +128,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
 
 Model::~Model() {
     cudaSetDevice(device_);
+    for (auto e : ev_pool_) cudaEventDestroy(e);
     cache_.release();
     weights_.release();
 }
@@ -268,7 +269,9 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.b_next = layers_[m - 2].b;
             if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
             e.Q = Q[1 - cur];
+            prof_begin(s);
             launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            prof_end(s, 2.0 * M * (double)N * Kd);
             cur = 1 - cur;
         } else {
             EpiConcretize e;
@@ -276,7 +279,9 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.xl = xl_;
             e.xu = xu_;
             if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * N);
+            prof_begin(s);
             launch_gemm_concretize(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            prof_end(s, 2.0 * M * (double)N * Kd);
         }
         slot += gemm_tiles_n(N);
     }
@@ -317,7 +322,9 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         e.kslot = cache_.as<float>("kslot", nslot);
         e.bslot = cache_.as<float>("bslot", nslot);
         e.B = B;
+        prof_begin(s);
         launch_gemm_relax_adj(Pb[cur], L.Wt, M, N, Kd, e, nullptr, s);
+        prof_end(s, 2.0 * M * (double)N * Kd);
         launch_reduce_relax_grad(sp.rows, M, B, N, e.kslot, e.bslot,
                                  cache_.as<float>(key("kbar", m), (size_t)B * N),
                                  cache_.as<float>(key("bbar", m), (size_t)B * N), s);
@@ -516,6 +523,37 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     (void)nout;
 }
 
+// ------------------------------------------------------------ profiling
+void Model::prof_begin(cudaStream_t s) {
+    if (!profile_) return;
+    while (ev_pool_.size() < ev_used_ + 2) {
+        cudaEvent_t e;
+        LB_CUDA(cudaEventCreate(&e));
+        ev_pool_.push_back(e);
+    }
+    LB_CUDA(cudaEventRecord(ev_pool_[ev_used_], s));
+}
+
+void Model::prof_end(cudaStream_t s, double flops) {
+    if (!profile_) return;
+    LB_CUDA(cudaEventRecord(ev_pool_[ev_used_ + 1], s));
+    ev_used_ += 2;
+    contraction_flops_ += flops;
+    ++contraction_launches_;
+}
+
+// Sum of the recorded contraction intervals (the stream has been synchronised).
+double Model::prof_collect() {
+    double ms = 0.0;
+    for (size_t i = 0; i + 1 < ev_used_; i += 2) {
+        float t = 0.f;
+        LB_CUDA(cudaEventElapsedTime(&t, ev_pool_[i], ev_pool_[i + 1]));
+        ms += t;
+    }
+    ev_used_ = 0;
+    return ms;
+}
+
 // ------------------------------------------------------------ entry
 void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes, const float* d_C,
                     int64_t c_boxes, int64_t nspec, const float* d_thr, bool lower, bool upper,
@@ -528,6 +566,9 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
     LB_CUDA(cudaSetDevice(device_));
     const auto t0 = std::chrono::steady_clock::now();
     launch_counter() = 0;
+    ev_used_ = 0;
+    contraction_flops_ = 0.0;
+    contraction_launches_ = 0;
     flops_ = 0.0;
     rows_ = 0;
     cudaEvent_t e0, e1;
@@ -563,6 +604,9 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
         stats->backward_rows = rows_;
         stats->algorithmic_flops = flops_;
         stats->alpha_iterations_run = alpha ? (int)opt_.alpha_iterations : 0;
+        stats->ms_contractions = prof_collect();
+        stats->contraction_launches = contraction_launches_;
+        stats->contraction_flops = contraction_flops_;
     }
 }
 

@@ -55,6 +55,7 @@ public:
     ~Model();
 
     void set_options(const lb200_options& o) { opt_ = o; }
+    void set_profiling(bool on) { profile_ = on; }
     const lb200_options& options() const { return opt_; }
 
     void compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes,
@@ -106,6 +107,16 @@ private:
     int64_t rows_ = 0;
     int last_B_ = 0;
     bool last_alpha_ = false;
+
+    // Contraction-kernel timing (lb200_set_profiling).
+    bool profile_ = false;
+    std::vector<cudaEvent_t> ev_pool_;
+    size_t ev_used_ = 0;
+    double contraction_flops_ = 0.0;
+    int64_t contraction_launches_ = 0;
+    void prof_begin(cudaStream_t s);
+    void prof_end(cudaStream_t s, double flops);
+    double prof_collect();
 };
 
 }  // namespace lb200

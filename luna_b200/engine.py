@@ -22,7 +22,8 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libluna_b200.so")
 
 EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_compute_bounds", "lb200_compute_bounds_device",
-           "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy")
+           "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy",
+           "lb200_set_profiling")
 
 
 class EngineError(RuntimeError):
@@ -52,6 +53,7 @@ def load_library():
                                                 C.POINTER(Stats)]
     lib.lb200_get_intermediate_bounds.argtypes = [vp, fp, fp, C.POINTER(C.c_int64)]
     lib.lb200_last_error.argtypes = [C.c_char_p, C.c_size_t]
+    lib.lb200_set_profiling.argtypes = [vp, C.c_int]
     lib.lb200_model_destroy.argtypes = [vp]
     lib.lb200_model_destroy.restype = None
     _lib = lib
@@ -82,6 +84,10 @@ class Model:
     def set_options(self, options: Options):
         self.options = options
         _check(_lib.lb200_set_options(self._h, C.byref(options)), "lb200_set_options")
+
+    def set_profiling(self, on: bool):
+        """Time the A.W contraction kernels with CUDA events (stats.ms_contractions)."""
+        _check(_lib.lb200_set_profiling(self._h, int(on)), "lb200_set_profiling")
 
     def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,
                        out_lb: np.ndarray | None = None, out_ub: np.ndarray | None = None):
