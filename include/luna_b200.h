@@ -190,6 +190,12 @@ LB200_API int lb200_compute_bounds_device(lb200_model* model, int method,
  * has no counterpart: it exists for roofline measurement. */
 LB200_API int lb200_set_profiling(lb200_model* model, int on);
 
+/* Contraction path: 0 (default) uses the tcgen05 tensor cores with 3xTF32
+ * split precision wherever the shape allows (N a multiple of 16, K of 4),
+ * the SIMT fp32 kernel elsewhere; 1 uses the SIMT fp32 kernel everywhere
+ * (for cross-checking).  Luna has no counterpart. */
+LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
+
 /* Copy the intermediate (pre-activation) bounds of the last call into host
  * buffers: for every node that feeds a ReLU, in node-id order, [n_boxes,
  * size] lower then upper.  Mirrors TorchModel::getState().allBounds

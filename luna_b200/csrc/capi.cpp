@@ -84,6 +84,13 @@ int lb200_set_profiling(lb200_model* model, int on) {
     return 0;
 }
 
+int lb200_set_contraction_path(lb200_model* model, int path) {
+    if (!model) return fail("lb200_set_contraction_path: null model");
+    if (path != 0 && path != 1) return fail("lb200_set_contraction_path: path must be 0 or 1");
+    model->m->set_force_simt(path == 1);
+    return 0;
+}
+
 int lb200_compute_bounds_device(lb200_model* model, int method, const float* d_x_lower,
                                 const float* d_x_upper, int64_t n_boxes, const float* d_C,
                                 int64_t c_boxes, int64_t nspec, const float* d_thresholds,

@@ -9,6 +9,7 @@
 // so each Linear step is a single GEMM whose epilogue applies the ReLU
 // relaxation of the box that owns the row.
 #include "engine.h"
+#include "tc_gemm.cuh"
 
 #include <algorithm>
 #include <chrono>
@@ -122,6 +123,13 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         LB_CUDA(cudaMemcpy(L.W, W.data(), W.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+        L.W_hi = weights_.as<float>(key("Whi", k), W.size());
+        L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
+        L.Wt_hi = weights_.as<float>(key("Wthi", k), Wt.size());
+        L.Wt_lo = weights_.as<float>(key("Wtlo", k), Wt.size());
+        launch_split_tf32(L.W, L.W_hi, L.W_lo, (int64_t)W.size(), 0);
+        launch_split_tf32(L.Wt, L.Wt_hi, L.Wt_lo, (int64_t)Wt.size(), 0);
+        LB_CUDA(cudaDeviceSynchronize());
     }
     lb200_options_default(&opt_);
 }
@@ -230,7 +238,8 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     float* Q[2] = {cache_.as<float>(key("Q", 0), (size_t)M * maxw), cache_.as<float>(key("Q", 1), (size_t)M * maxw)};
     float* bias = cache_.as<float>(key("bias", st), M);
     int slots_total = 0;
-    for (int m = st - 1; m >= 1; --m) slots_total += gemm_tiles_n(width(m - 1));
+    for (int m = st - 1; m >= 1; --m)
+        slots_total += std::max(gemm_tiles_n(width(m - 1)), tc_tiles_n(width(m - 1)));
     float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
 
     const LinearLayer& Ls = layers_[st - 1];
@@ -270,7 +279,10 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
             e.Q = Q[1 - cur];
             prof_begin(s);
-            launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            if (use_tc(M, N, Kd))
+                launch_tc_relax_fwd(Q[cur], L.Wt_hi, L.Wt_lo, M, N, Kd, e, part + (size_t)slot * M, s);
+            else
+                launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
             cur = 1 - cur;
         } else {
@@ -280,10 +292,13 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.xu = xu_;
             if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * N);
             prof_begin(s);
-            launch_gemm_concretize(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            if (use_tc(M, N, Kd))
+                launch_tc_concretize(Q[cur], L.Wt_hi, L.Wt_lo, M, N, Kd, e, part + (size_t)slot * M, s);
+            else
+                launch_gemm_concretize(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
         }
-        slot += gemm_tiles_n(N);
+        slot += use_tc(M, N, Kd) ? tc_tiles_n(N) : gemm_tiles_n(N);
     }
     launch_sum_partials(bias, part, slot, M, cache_.as<float>(key("val", st), M), s);
     rows_ += M;
@@ -318,14 +333,19 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * N);
         e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
         e.alpha_grad = cache_.as<float>(key("agrad", m, st), (size_t)2 * R * N);
-        const size_t nslot = (size_t)relax_grad_slots(M, B) * N;
+        const bool tc = use_tc(M, N, Kd);
+        const int group = tc ? 32 : 8;
+        const size_t nslot = (size_t)relax_grad_slots(M, B, group) * N;
         e.kslot = cache_.as<float>("kslot", nslot);
         e.bslot = cache_.as<float>("bslot", nslot);
         e.B = B;
         prof_begin(s);
-        launch_gemm_relax_adj(Pb[cur], L.Wt, M, N, Kd, e, nullptr, s);
+        if (tc)
+            launch_tc_relax_adj(Pb[cur], L.W_hi, L.W_lo, M, N, Kd, e, s);
+        else
+            launch_gemm_relax_adj(Pb[cur], L.Wt, M, N, Kd, e, nullptr, s);
         prof_end(s, 2.0 * M * (double)N * Kd);
-        launch_reduce_relax_grad(sp.rows, M, B, N, e.kslot, e.bslot,
+        launch_reduce_relax_grad(sp.rows, M, B, N, group, e.kslot, e.bslot,
                                  cache_.as<float>(key("kbar", m), (size_t)B * N),
                                  cache_.as<float>(key("bbar", m), (size_t)B * N), s);
         cur = 1 - cur;
@@ -523,6 +543,8 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     (void)nout;
 }
 
+bool Model::use_tc(int M, int N, int K) const { return !force_simt_ && tc_supported(M, N, K); }
+
 // ------------------------------------------------------------ profiling
 void Model::prof_begin(cudaStream_t s) {
     if (!profile_) return;
@@ -593,6 +615,12 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
     last_alpha_ = alpha;
     LB_CUDA(cudaEventRecord(e1, stream));
     LB_CUDA(cudaEventSynchronize(e1));
+    int tc_err = 0;
+    LB_CUDA(cudaMemcpy(&tc_err, tc_error_flag(), sizeof(int), cudaMemcpyDeviceToHost));
+    if (tc_err) {
+        LB_CUDA(cudaMemset(tc_error_flag(), 0, sizeof(int)));
+        throw std::runtime_error("tensor-core contraction: a bounded wait expired; results are invalid");
+    }
     float ms = 0.f;
     LB_CUDA(cudaEventElapsedTime(&ms, e0, e1));
     cudaEventDestroy(e0);

@@ -39,6 +39,9 @@ struct LinearLayer {
     float* W = nullptr;   // [n_out, n_in]
     float* Wt = nullptr;  // [n_in, n_out]
     float* b = nullptr;   // [n_out]
+    // tf32 (hi, lo) splits for the tensor-core path: W is the K-major B
+    // operand of the adjoint contraction, Wt of the forward one.
+    float *W_hi = nullptr, *W_lo = nullptr, *Wt_hi = nullptr, *Wt_lo = nullptr;
 };
 
 struct StartPlan {
@@ -56,6 +59,9 @@ public:
 
     void set_options(const lb200_options& o) { opt_ = o; }
     void set_profiling(bool on) { profile_ = on; }
+    // Contraction path: tensor cores (3xTF32) where the shape allows, else
+    // the SIMT fp32 kernel.  Forcing SIMT is for cross-checking only.
+    void set_force_simt(bool on) { force_simt_ = on; }
     const lb200_options& options() const { return opt_; }
 
     void compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes,
@@ -107,6 +113,9 @@ private:
     int64_t rows_ = 0;
     int last_B_ = 0;
     bool last_alpha_ = false;
+
+    bool force_simt_ = false;
+    bool use_tc(int M, int N, int K) const;
 
     // Contraction-kernel timing (lb200_set_profiling).
     bool profile_ = false;

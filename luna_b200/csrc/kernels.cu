@@ -562,13 +562,14 @@ void launch_gemm_relax_adj(const float* A, const float* Bm, int M, int N, int K,
     run_gemm(A, Bm, M, N, K, EpiAdjOp{e, M, N}, partial, s);
 }
 
-int relax_grad_slots(int M, int B) { return ceil_div(M, 8) + 2 * B; }
+int relax_grad_slots(int M, int B, int group) { return ceil_div(M, group) + 2 * B; }
 
-// One thread per (box, column): the slots of virtual box vb cover the 8-row
-// groups from first_row/8 to last_row/8, each at slot index group + vb.
-__global__ void reduce_relax_grad_kernel(RowMap rows, int M, int B, int N, const float* __restrict__ kslot,
-                                         const float* __restrict__ bslot, float* __restrict__ kbar,
-                                         float* __restrict__ bbar) {
+// One thread per (box, column): the slots of virtual box vb cover the
+// `group`-row groups from first_row/group to last_row/group, each at slot
+// index (row group + vb).
+__global__ void reduce_relax_grad_kernel(RowMap rows, int M, int B, int N, int group,
+                                         const float* __restrict__ kslot, const float* __restrict__ bslot,
+                                         float* __restrict__ kbar, float* __restrict__ bbar) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= (int64_t)B * N) return;
     const int bx = (int)(idx / N), c = (int)(idx % N);
@@ -578,7 +579,7 @@ __global__ void reduce_relax_grad_kernel(RowMap rows, int M, int B, int N, const
         const int last = min(p * rows.R + rows.box_off[bx + 1], M);  // exclusive
         if (first >= last) continue;
         const int vb = bx + p * B;
-        for (int g = first >> 3; g <= (last - 1) >> 3; ++g) {
+        for (int g = first / group; g <= (last - 1) / group; ++g) {
             const size_t at = (size_t)(g + vb) * N + c;
             ks += kslot[at];
             bs += bslot[at];
@@ -588,10 +589,10 @@ __global__ void reduce_relax_grad_kernel(RowMap rows, int M, int B, int N, const
     bbar[idx] += bs;
 }
 
-void launch_reduce_relax_grad(const RowMap& rows, int M, int B, int N, const float* kslot,
+void launch_reduce_relax_grad(const RowMap& rows, int M, int B, int N, int group, const float* kslot,
                               const float* bslot, float* kbar, float* bbar, cudaStream_t s) {
     if ((int64_t)B * N == 0 || M == 0) return;
-    reduce_relax_grad_kernel<<<ceil_div((int64_t)B * N, 256), 256, 0, s>>>(rows, M, B, N, kslot, bslot,
+    reduce_relax_grad_kernel<<<ceil_div((int64_t)B * N, 256), 256, 0, s>>>(rows, M, B, N, group, kslot, bslot,
                                                                            kbar, bbar);
     LB_LAUNCH();
 }

@@ -127,10 +127,11 @@ void launch_gemm_relax_adj(const float* A, const float* Bm, int M, int N, int K,
 int gemm_tiles_n(int N);
 
 // kbar[b, c] += sum of the slots of virtual boxes b and B + b (rows < M), in
-// row order, for the slot layout of EpiRelaxAdj.
-void launch_reduce_relax_grad(const RowMap& rows, int M, int B, int N, const float* kslot,
+// row order, for the slot layout of EpiRelaxAdj with `group`-row groups
+// (8 for the SIMT kernel, 32 for the tensor-core kernel).
+void launch_reduce_relax_grad(const RowMap& rows, int M, int B, int N, int group, const float* kslot,
                               const float* bslot, float* kbar, float* bbar, cudaStream_t s);
-int relax_grad_slots(int M, int B);
+int relax_grad_slots(int M, int B, int group);
 
 // out[r] = base[r] + sum_t partial[t * M + r] for t in [0, ntiles).
 void launch_sum_partials(const float* base, const float* partial, int ntiles, int M, float* out,

@@ -1,0 +1,632 @@
+// tc_gemm.cu -- tcgen05 / TMEM / TMA contraction kernels for sm_100a.
+//
+// One persistent CTA per SM walks the (128-row, BN-column) output tiles.
+// Warp roles (12 warps):
+//   warp 0      TMA producer (and TMEM allocation)
+//   warp 1      MMA issuer: per K=8 step three tcgen05.mma kind::tf32
+//               (A_lo.B_hi, A_hi.B_lo, A_hi.B_hi) into a TMEM accumulator
+//   warps 4-7   epilogue: tcgen05.ld rows of the accumulator, fused
+//               relaxation / concretisation / relaxation-adjoint, stores
+//   warps 8-11  split: raw fp32 A stage -> (hi, lo) tf32 pair in place
+// Shared memory holds S stages of {A hi, A lo, B hi, B lo}, each a
+// 128-byte-swizzled K-major tile of 32 fp32 columns; the accumulator is
+// double-buffered in TMEM so the epilogue of tile j overlaps the MMAs of
+// tile j+1.  Every wait is bounded (about 2 s); on expiry the CTA raises an
+// error flag, drains what it issued and returns.
+#include "tc_gemm.cuh"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <stdexcept>
+#include <string>
+
+namespace lb200 {
+
+namespace {
+
+constexpr int TC_BM = 128;
+constexpr int TC_BK = 32;  // fp32 columns per 128-byte swizzle row
+constexpr int NUM_THREADS = 384;
+constexpr int WARP_TMA = 0, WARP_MMA = 1, EPI_WARP0 = 4, XF_WARP0 = 8;
+constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
+constexpr int A_TILE_BYTES = TC_BM * TC_BK * 4;  // 16 KB
+
+enum { KIND_FWD = 0, KIND_CONC = 1, KIND_ADJ = 2 };
+
+__device__ int g_tc_error;
+
+struct TcEpi {
+    EpiRelaxFwd f;
+    EpiConcretize c;
+    EpiRelaxAdj a;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t cnt) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(cnt) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Wait for the phase of parity `parity` to complete.  Gives up when another
+// role raised `abort` (unless ignore_abort) or after WAIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
+                                          bool ignore_abort = false) {
+    if (mbar_try(b, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+        if (mbar_try(b, parity)) return true;
+        if (!ignore_abort && *abort) return false;
+        if (clock64() - t0 > WAIT_CYCLES) {
+            *abort = 1;
+            atomicExch(&g_tc_error, 1);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            smem_u32(dst)),
+        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+
+// K-major operand in shared memory, 128-byte swizzle: rows of 128 bytes,
+// 8-row atoms 1024 bytes apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1 << 16;
+    d |= (uint64_t)(1024 >> 4) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    const uint32_t z = 0;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float rna_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+__device__ __forceinline__ void split_row2(int r, int R, int& p, int& rr) {
+    p = r >= R ? 1 : 0;
+    rr = r - p * R;
+}
+
+template <int N16>
+__device__ __forceinline__ void ld16f(const float* p, float (&v)[N16]) {
+#pragma unroll
+    for (int q = 0; q < N16 / 4; ++q) {
+        const float4 t = reinterpret_cast<const float4*>(p)[q];
+        v[4 * q] = t.x;
+        v[4 * q + 1] = t.y;
+        v[4 * q + 2] = t.z;
+        v[4 * q + 3] = t.w;
+    }
+}
+__device__ __forceinline__ void st16f(float* p, const float (&v)[16]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+        reinterpret_cast<float4*>(p)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+
+// ------------------------------------------------------------- epilogues
+// Each epilogue thread owns one output row r of the tile; `v` holds its 16
+// accumulator values for columns [c, c + 16).  N is a multiple of 16, so a
+// 16-column chunk is either fully inside [0, N) or fully outside.
+
+__device__ __forceinline__ void epi_fwd(const EpiRelaxFwd& e, int r, int c, int N, const float (&v)[16],
+                                        float& part) {
+    int p, rr;
+    split_row2(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    const size_t rb = (size_t)r * N + c;
+    const size_t bj = (size_t)bx * e.rp.n + c;
+    if (e.P_save) st16f(e.P_save + rb, v);
+    float sl[16], ku[16], bu[16], al[16];
+    ld16f(e.rp.slope_lo + bj, sl);
+    ld16f(e.rp.k_up + bj, ku);
+    ld16f(e.rp.b_up + bj, bu);
+    const uint4 fl4 = *reinterpret_cast<const uint4*>(e.rp.flags + bj);
+    const uint8_t* fl = reinterpret_cast<const uint8_t*>(&fl4);
+    if (e.alpha) ld16f(e.alpha + rb, al);
+    float bn[16];
+    if (e.b_next) ld16f(e.b_next + c, bn);
+    float q[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float s = (e.alpha && (fl[i] & RF_USE_ALPHA)) ? al[i] : sl[i];
+        const float P = v[i];
+        const float pos = fmaxf(P, 0.f), neg = fminf(P, 0.f);
+        float Q;
+        if (p == 0) {
+            part += neg * bu[i];
+            Q = pos * s + neg * ku[i];
+        } else {
+            part += pos * bu[i];
+            Q = pos * ku[i] + neg * s;
+        }
+        q[i] = Q;
+        if (e.b_next) part = fmaf(Q, bn[i], part);
+    }
+    st16f(e.Q + rb, q);
+}
+
+__device__ __forceinline__ void epi_conc(const EpiConcretize& e, int r, int c, int N, const float (&v)[16],
+                                         float& part) {
+    int p, rr;
+    split_row2(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    float xa[16], xb[16];
+    ld16f((p == 0 ? e.xl : e.xu) + (size_t)bx * N + c, xa);
+    ld16f((p == 0 ? e.xu : e.xl) + (size_t)bx * N + c, xb);
+    uint8_t sg[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float P = v[i];
+        part += fmaxf(P, 0.f) * xa[i] + fminf(P, 0.f) * xb[i];
+        sg[i] = (uint8_t)((P >= 0.f ? 1 : 0) | (P <= 0.f ? 2 : 0));
+    }
+    if (e.sign) *reinterpret_cast<uint4*>(e.sign + (size_t)r * N + c) = *reinterpret_cast<const uint4*>(sg);
+}
+
+// Relaxation adjoint; kv / bv receive this row's contributions to
+// d loss / d k_up and d loss / d b_up for the 16 columns.
+__device__ __forceinline__ void epi_adj(const EpiRelaxAdj& e, int r, int c, int N, const float (&v)[16], float g,
+                                        float (&kv)[16], float (&bv)[16]) {
+    int p, rr;
+    split_row2(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    const size_t rb = (size_t)r * N + c;
+    const size_t bj = (size_t)bx * e.rp.n + c;
+    float P[16], bl[16], sl[16], ku[16], bu[16], al[16];
+    ld16f(e.P_saved + rb, P);
+    ld16f(e.b_lin + c, bl);
+    ld16f(e.rp.slope_lo + bj, sl);
+    ld16f(e.rp.k_up + bj, ku);
+    ld16f(e.rp.b_up + bj, bu);
+    if (e.alpha) ld16f(e.alpha + rb, al);
+    const uint4 fl4 = *reinterpret_cast<const uint4*>(e.rp.flags + bj);
+    const uint8_t* fl = reinterpret_cast<const uint8_t*>(&fl4);
+    float pb[16], ag[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float Qbar = v[i] + g * bl[i];
+        const float s = (e.alpha && (fl[i] & RF_USE_ALPHA)) ? al[i] : sl[i];
+        const float k = ku[i], b = bu[i];
+        const bool pos = P[i] >= 0.f, neg = P[i] <= 0.f;
+        const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
+        const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
+        const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
+        const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
+        pb[i] = Qbar * dq + g * db;
+        const float Pp = fmaxf(P[i], 0.f), Pn = fminf(P[i], 0.f);
+        ag[i] = (fl[i] & RF_USE_ALPHA) ? Qbar * (p == 0 ? Pp : Pn) : 0.f;
+        const bool un = (fl[i] & RF_UNSTABLE) != 0;
+        kv[i] = un ? Qbar * (p == 0 ? Pn : Pp) : 0.f;
+        bv[i] = un ? g * (p == 0 ? Pn : Pp) : 0.f;
+    }
+    if (e.Pbar) st16f(e.Pbar + rb, pb);
+    if (e.alpha_grad) st16f(e.alpha_grad + rb, ag);
+}
+
+// ------------------------------------------------------------- kernel
+template <int BN, int S, int KIND>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tbh,
+                   const __grid_constant__ CUtensorMap tbl, int M, int N, int K, TcEpi ep, float* partial) {
+    constexpr int B_TILE_BYTES = BN * TC_BK * 4;
+    constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
+    constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
+                                                     : (2 * BN <= 256) ? 256 : 512;
+    constexpr uint32_t IDESC = idesc_tf32(BN);
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(base + (size_t)S * STAGE_BYTES);
+    uint64_t* full = bars;            // TMA landed
+    uint64_t* split = bars + S;       // A split into hi/lo
+    uint64_t* empty = bars + 2 * S;   // MMAs done with the stage
+    uint64_t* tfull = bars + 3 * S;   // accumulator ready (2)
+    uint64_t* tempty = bars + 3 * S + 2;  // accumulator drained (2)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&split[s], 128);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull[a], 1);
+            mbar_init(&tempty[a], 128);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == WARP_TMA) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int tiles_n = (N + BN - 1) / BN;
+    const int tiles_m = (M + TC_BM - 1) / TC_BM;
+    const int ntiles = tiles_n * tiles_m;
+    const int nk = (K + TC_BK - 1) / TC_BK;
+
+    auto a_hi = [&](int s) { return base + (size_t)s * STAGE_BYTES; };
+    auto a_lo = [&](int s) { return base + (size_t)s * STAGE_BYTES + A_TILE_BYTES; };
+    auto b_hi = [&](int s) { return base + (size_t)s * STAGE_BYTES + 2 * A_TILE_BYTES; };
+    auto b_lo = [&](int s) { return base + (size_t)s * STAGE_BYTES + 2 * A_TILE_BYTES + B_TILE_BYTES; };
+
+    if (warp == WARP_TMA) {
+        if (lane == 0) {
+            uint32_t g = 0;
+            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+                const int mb = t / tiles_n, nb = t % tiles_n;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % S;
+                    const uint32_t ph = (g / S) & 1;
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+                    mbar_arrive_tx(&full[s], A_TILE_BYTES + 2 * B_TILE_BYTES);
+                    tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
+                    tma_load_2d(&tbh, &full[s], b_hi(s), kb * TC_BK, nb * BN);
+                    tma_load_2d(&tbl, &full[s], b_lo(s), kb * TC_BK, nb * BN);
+                }
+            }
+            if (*abort) {
+                // Drain: wait (bounded) for the last loads issued to land.
+                for (uint32_t q = (g > (uint32_t)S ? g - S : 0); q < g; ++q)
+                    mbar_wait(&full[q % S], (q / S) & 1, abort, true);
+            }
+        }
+    } else if (warp == WARP_MMA) {
+        if (lane == 0) {
+            uint32_t g = 0, j = 0;
+            bool issued = false;
+            uint64_t* last_commit = nullptr;
+            uint32_t last_phase = 0;
+            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++j) {
+                const int acc = j & 1;
+                const uint32_t aph = (j >> 1) & 1;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
+                tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                bool ok = true;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const int s = g % S;
+                    const uint32_t ph = (g / S) & 1;
+                    if (!mbar_wait(&split[s], ph, abort)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t dah = desc_sw128(smem_u32(a_hi(s)));
+                    const uint64_t dal = desc_sw128(smem_u32(a_lo(s)));
+                    const uint64_t dbh = desc_sw128(smem_u32(b_hi(s)));
+                    const uint64_t dbl = desc_sw128(smem_u32(b_lo(s)));
+#pragma unroll
+                    for (int k8 = 0; k8 < TC_BK / 8; ++k8) {
+                        const uint64_t off = (uint64_t)(k8 * 32) >> 4;  // 8 tf32 = 32 bytes along K
+                        umma_tf32(d, dal + off, dbh + off, IDESC, (kb | k8) != 0);
+                        umma_tf32(d, dah + off, dbl + off, IDESC, 1);
+                        umma_tf32(d, dah + off, dbh + off, IDESC, 1);
+                    }
+                    umma_commit(&empty[s]);
+                    issued = true;
+                    last_commit = &empty[s];
+                    last_phase = ph;
+                }
+                if (!ok) break;
+                umma_commit(&tfull[acc]);
+            }
+            if (*abort && issued) mbar_wait(last_commit, last_phase, abort, true);
+        }
+    } else if (warp >= XF_WARP0) {
+        const int xt = threadIdx.x - XF_WARP0 * 32;
+        uint32_t g = 0;
+        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+            bool ok = true;
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % S;
+                const uint32_t ph = (g / S) & 1;
+                if (!mbar_wait(&full[s], ph, abort)) { ok = false; break; }
+                float4* hi = reinterpret_cast<float4*>(a_hi(s));
+                float4* lo = reinterpret_cast<float4*>(a_lo(s));
+#pragma unroll 4
+                for (int i = xt; i < A_TILE_BYTES / 16; i += 128) {
+                    const float4 x = hi[i];
+                    float4 h, l;
+                    h.x = rna_tf32(x.x); l.x = rna_tf32(x.x - h.x);
+                    h.y = rna_tf32(x.y); l.y = rna_tf32(x.y - h.y);
+                    h.z = rna_tf32(x.z); l.z = rna_tf32(x.z - h.z);
+                    h.w = rna_tf32(x.w); l.w = rna_tf32(x.w - h.w);
+                    hi[i] = h;
+                    lo[i] = l;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&split[s]);
+            }
+            if (!ok) break;
+        }
+    } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
+        const int q = warp - EPI_WARP0;
+        uint32_t j = 0;
+        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++j) {
+            const int mb = t / tiles_n, nb = t % tiles_n;
+            const int acc = j & 1;
+            const uint32_t aph = (j >> 1) & 1;
+            if (!mbar_wait(&tfull[acc], aph, abort)) break;
+            tc_fence_after();
+            const int r = mb * TC_BM + q * 32 + lane;
+            const bool row_ok = r < M;
+            const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            float part = 0.f;
+            if constexpr (KIND == KIND_ADJ) {
+                const EpiRelaxAdj& e = ep.a;
+                int vb = -1 - lane;  // rows past M never join a segment
+                float g = 0.f;
+                if (row_ok) {
+                    int p, rr;
+                    split_row2(r, e.rows.R, p, rr);
+                    vb = e.rows.row_box[rr] + p * e.B;
+                    g = e.gseed[r];
+                }
+                bool same[5];
+#pragma unroll
+                for (int o = 0; o < 5; ++o) {
+                    const int off = 1 << o;
+                    const int ovb = __shfl_down_sync(0xffffffffu, vb, off);
+                    same[o] = (lane + off < 32) && (ovb == vb);
+                }
+                const int up = __shfl_up_sync(0xffffffffu, vb, 1);
+                const bool head = row_ok && (lane == 0 || up != vb);
+                const size_t slot = (size_t)((r >> 5) + vb) * N;
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + (uint32_t)c0, v);
+                    const int c = nb * BN + c0;
+                    if (c >= N) continue;
+                    float kv[16], bv[16];
+                    if (row_ok) {
+                        epi_adj(e, r, c, N, v, g, kv, bv);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) kv[i] = bv[i] = 0.f;
+                    }
+#pragma unroll
+                    for (int o = 0; o < 5; ++o) {
+                        const int off = 1 << o;
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float uk = __shfl_down_sync(0xffffffffu, kv[i], off);
+                            const float ub = __shfl_down_sync(0xffffffffu, bv[i], off);
+                            if (same[o]) {
+                                kv[i] += uk;
+                                bv[i] += ub;
+                            }
+                        }
+                    }
+                    if (head) {
+                        st16f(e.kslot + slot + c, kv);
+                        st16f(e.bslot + slot + c, bv);
+                    }
+                }
+            } else {
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + (uint32_t)c0, v);
+                    const int c = nb * BN + c0;
+                    if (c >= N || !row_ok) continue;
+                    if constexpr (KIND == KIND_FWD) epi_fwd(ep.f, r, c, N, v, part);
+                    else epi_conc(ep.c, r, c, N, v, part);
+                }
+                if (row_ok && partial) partial[(size_t)nb * M + r] = part;
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty[acc]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == WARP_TMA) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+    }
+}
+
+// ------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable");
+    return fn;
+}
+
+// 2D map of a row-major [rows, K] fp32 matrix, box = 32 columns x box_rows.
+CUtensorMap make_map(const float* p, int rows, int K, int box_rows) {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)K * 4};
+    cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(p), dims, strides,
+                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return m;
+}
+
+int num_sms() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        LB_CUDA(cudaGetDevice(&dev));
+        LB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+    }
+    return n;
+}
+
+template <int BN, int S, int KIND>
+void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
+            float* partial, cudaStream_t s) {
+    constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * BN * TC_BK * 4;
+    constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
+    static bool configured = false;
+    if (!configured) {
+        LB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN, S, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        configured = true;
+    }
+    const CUtensorMap ta = make_map(A, M, K, TC_BM);
+    const CUtensorMap tbh = make_map(Bhi, N, K, BN);
+    const CUtensorMap tbl = make_map(Blo, N, K, BN);
+    const int ntiles = ((N + BN - 1) / BN) * ((M + TC_BM - 1) / TC_BM);
+    const int grid = std::min(ntiles, num_sms());
+    tc_gemm_kernel<BN, S, KIND><<<grid, NUM_THREADS, SMEM, s>>>(ta, tbh, tbl, M, N, K, ep, partial);
+    LB_LAUNCH();
+}
+
+template <int KIND>
+void dispatch(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
+              float* partial, cudaStream_t s) {
+    switch (tc_block_n(N)) {
+    case 256: run_tc<256, 2, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    case 128: run_tc<128, 3, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    case 112: run_tc<112, 3, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    default: run_tc<64, 4, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    }
+}
+
+__global__ void split_tf32_kernel(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo,
+                                  int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float x = src[i];
+    const float h = rna_tf32(x);
+    hi[i] = h;
+    lo[i] = rna_tf32(x - h);
+}
+
+}  // namespace
+
+bool tc_supported(int M, int N, int K) { return M > 0 && N >= 16 && N % 16 == 0 && K % 4 == 0 && K >= 4; }
+
+int tc_block_n(int N) {
+    const int cands[4] = {256, 128, 112, 64};
+    int best = 64, best_pad = 1 << 30;
+    for (int bn : cands) {
+        const int pad = ((N + bn - 1) / bn) * bn;
+        if (pad < best_pad) {
+            best_pad = pad;
+            best = bn;
+        }
+    }
+    return best;
+}
+
+int tc_tiles_n(int N) { return (N + tc_block_n(N) - 1) / tc_block_n(N); }
+
+int* tc_error_flag() {
+    void* p = nullptr;
+    LB_CUDA(cudaGetSymbolAddress(&p, g_tc_error));
+    return static_cast<int*>(p);
+}
+
+void launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, cudaStream_t s) {
+    if (n == 0) return;
+    split_tf32_kernel<<<ceil_div(n, 256), 256, 0, s>>>(src, hi, lo, n);
+    LB_LAUNCH();
+}
+
+void launch_tc_relax_fwd(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
+                         const EpiRelaxFwd& e, float* partial, cudaStream_t s) {
+    if (M == 0) return;
+    TcEpi ep{};
+    ep.f = e;
+    dispatch<KIND_FWD>(A, Bhi, Blo, M, N, K, ep, partial, s);
+}
+
+void launch_tc_concretize(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
+                          const EpiConcretize& e, float* partial, cudaStream_t s) {
+    if (M == 0) return;
+    TcEpi ep{};
+    ep.c = e;
+    dispatch<KIND_CONC>(A, Bhi, Blo, M, N, K, ep, partial, s);
+}
+
+void launch_tc_relax_adj(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
+                         const EpiRelaxAdj& e, cudaStream_t s) {
+    if (M == 0) return;
+    TcEpi ep{};
+    ep.a = e;
+    dispatch<KIND_ADJ>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
+}
+
+}  // namespace lb200

@@ -23,7 +23,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libluna_b200.so")
 EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_compute_bounds", "lb200_compute_bounds_device",
            "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy",
-           "lb200_set_profiling")
+           "lb200_set_profiling", "lb200_set_contraction_path")
 
 
 class EngineError(RuntimeError):
@@ -54,6 +54,7 @@ def load_library():
     lib.lb200_get_intermediate_bounds.argtypes = [vp, fp, fp, C.POINTER(C.c_int64)]
     lib.lb200_last_error.argtypes = [C.c_char_p, C.c_size_t]
     lib.lb200_set_profiling.argtypes = [vp, C.c_int]
+    lib.lb200_set_contraction_path.argtypes = [vp, C.c_int]
     lib.lb200_model_destroy.argtypes = [vp]
     lib.lb200_model_destroy.restype = None
     _lib = lib
@@ -88,6 +89,10 @@ class Model:
     def set_profiling(self, on: bool):
         """Time the A.W contraction kernels with CUDA events (stats.ms_contractions)."""
         _check(_lib.lb200_set_profiling(self._h, int(on)), "lb200_set_profiling")
+
+    def set_contraction_path(self, path: int):
+        """0: tensor cores (3xTF32) where the shape allows; 1: SIMT fp32 only."""
+        _check(_lib.lb200_set_contraction_path(self._h, int(path)), "lb200_set_contraction_path")
 
     def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,
                        out_lb: np.ndarray | None = None, out_ub: np.ndarray | None = None):

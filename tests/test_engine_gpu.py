@@ -103,6 +103,20 @@ def test_full_size_properties():
     assert G.excess(one[0], alb[5:6]) <= 1.0 and G.excess(one[1], aub[5:6]) <= 1.0
 
 
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_tensor_core_path_matches_simt_path(method):
+    """The tcgen05 3xTF32 contractions agree with the SIMT fp32 ones within
+    the parity bar (both are fp32-accurate; summation orders differ)."""
+    g, bx = W.mlp_784_256x4_10(24)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=8)
+    m = Model(g, options=opt)
+    tlb, tub = m.compute_bounds(bx, method)
+    m.set_contraction_path(1)
+    slb, sub = m.compute_bounds(bx, method)
+    print(f"tc vs simt: lb {G.excess(tlb, slb):.3f} ub {G.excess(tub, sub):.3f}")
+    assert G.excess(tlb, slb) <= 1.0 and G.excess(tub, sub) <= 1.0
+
+
 def test_device_pointer_entry_point_matches_host_entry_point():
     g, bx = W.mlp_5_50x6_5(64)
     m = Model(g, options=abi.default_options(alpha_lr=0.1))
