@@ -196,6 +196,23 @@ LB200_API int lb200_set_profiling(lb200_model* model, int on);
  * (for cross-checking).  Luna has no counterpart. */
 LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 
+/* IBP bounds of n_boxes boxes without allocating any device memory: the
+ * same result as lb200_compute_bounds_device(..., LB200_METHOD_IBP, ...),
+ * for callers that cannot call cudaMalloc where they need bounds (inside a
+ * stream capture, or under a memory manager that owns every allocation).
+ * The per-layer interval bounds live in a fixed 16 MiB __device__ array
+ * held by every GPU that loads this library until the process exits;
+ * batches needing more (n_boxes * 2 * sum of Linear output widths floats
+ * above 4 Mi) are rejected with an error.  Work is enqueued on `stream` and
+ * the call returns without waiting.  The first call on a device resolves the
+ * array's address on that device: make it before any stream capture.  All
+ * calls share the array, so calls that overlap on the GPU race and must be
+ * serialised by the caller.  No counterpart in the reference. */
+LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const float* d_x_lower,
+                                       const float* d_x_upper, int64_t n_boxes, const float* d_C,
+                                       int64_t c_boxes, int64_t nspec, float* d_out_lb,
+                                       float* d_out_ub, void* stream);
+
 /* Copy the intermediate (pre-activation) bounds of the last call into host
  * buffers: for every node that feeds a ReLU, in node-id order, [n_boxes,
  * size] lower then upper.  Mirrors TorchModel::getState().allBounds

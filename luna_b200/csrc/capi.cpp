@@ -1,16 +1,11 @@
 // capi.cpp -- extern "C" entry points declared in include/luna_b200.h.
 // Every entry point catches all exceptions and reports them through
 // lb200_last_error(); nothing is thrown across the boundary.
-#include "engine.h"
+#include "handle.h"
 
 #include <cstring>
 #include <exception>
 #include <string>
-
-struct lb200_model {
-    lb200::Model* m = nullptr;
-    cudaStream_t stream = nullptr;
-};
 
 namespace {
 thread_local std::string g_last_error;
@@ -32,6 +27,8 @@ int guarded(F&& f) {
     }
 }
 }  // namespace
+
+int lb200::set_last_error(const std::string& msg) { return fail(msg); }
 
 extern "C" {
 

@@ -74,6 +74,7 @@ public:
     int device() const { return device_; }
     int n_in() const { return layers_.front().n_in; }
     int n_out() const { return layers_.back().n_out; }
+    const std::vector<LinearLayer>& layers() const { return layers_; }
     int64_t intermediate_count() const;
     void copy_intermediate(float* lower, float* upper) const;
 

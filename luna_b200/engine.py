@@ -23,7 +23,7 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libluna_b200.so")
 EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_compute_bounds", "lb200_compute_bounds_device",
            "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy",
-           "lb200_set_profiling", "lb200_set_contraction_path")
+           "lb200_set_profiling", "lb200_set_contraction_path", "lb200_ibp_bounds_noalloc")
 
 
 class EngineError(RuntimeError):
@@ -55,6 +55,7 @@ def load_library():
     lib.lb200_last_error.argtypes = [C.c_char_p, C.c_size_t]
     lib.lb200_set_profiling.argtypes = [vp, C.c_int]
     lib.lb200_set_contraction_path.argtypes = [vp, C.c_int]
+    lib.lb200_ibp_bounds_noalloc.argtypes = [vp, vp, vp, C.c_int64, vp, C.c_int64, C.c_int64, vp, vp, vp]
     lib.lb200_model_destroy.argtypes = [vp]
     lib.lb200_model_destroy.restype = None
     _lib = lib
@@ -130,6 +131,13 @@ class Model:
                                          C.cast(ub, f), C.byref(st)), "lb200_compute_bounds")
         self.last_stats = st
         return st
+
+    def ibp_bounds_noalloc_ptr(self, xl: int, xu: int, n_boxes: int, Cp: int, c_boxes: int, nspec: int,
+                               lb: int, ub: int, stream: int = 0):
+        """IBP bounds through the allocation-free entry point (device pointers
+        as ints).  Enqueues on `stream` and returns without waiting."""
+        _check(_lib.lb200_ibp_bounds_noalloc(self._h, xl, xu, n_boxes, Cp, c_boxes, nspec, lb, ub,
+                                             stream or None), "lb200_ibp_bounds_noalloc")
 
     def intermediate_bounds(self):
         """Pre-activation bounds of the last call, [B, sum of widths] lower and upper."""
