@@ -35,6 +35,19 @@ inline void count_launch(const char* file, int line) {
 
 inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 
+// One torch::optim::Adam step (betas 0.9 / 0.999, eps 1e-8, no weight decay)
+// followed by AlphaCROWNAnalysis::clipAlphaParameters' clamp to [0, 1]:
+//   m = m*b1 + (1-b1) g;  v = v*b2 + (1-b2) g g;
+//   a += -step * m / (sqrt(v) / sqrt(bc2) + eps),  step = lr / bc1.
+__device__ __forceinline__ float adam_clip_update(float a, float g, float& m, float& v, float step,
+                                                  float bc2_sqrt) {
+    m = m * 0.9f + 0.1f * g;
+    v = v * 0.999f + 0.001f * g * g;
+    const float denom = sqrtf(v) / bc2_sqrt + 1e-8f;
+    a = a + (-step) * m / denom;
+    return fminf(fmaxf(a, 0.f), 1.f);
+}
+
 // Per-(box, neuron) relaxation flags of one ReLU.
 enum : uint8_t {
     RF_USE_ALPHA = 1,   // lower slope comes from the alpha tensor

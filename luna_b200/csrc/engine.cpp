@@ -317,8 +317,11 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     float* Pb[2] = {cache_.as<float>(key("Pbar", 0), (size_t)M * maxw),
                     cache_.as<float>(key("Pbar", 1), (size_t)M * maxw)};
     const int n0 = width(0);
-    launch_adj_input_seed(sp.rows, M, cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * n0), g, xl_,
-                          xu_, n0, Pb[0], s);
+    const uint8_t* sign = cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * n0);
+    // On the tensor-core path the first contraction generates d loss / d A at
+    // the input from the signs itself; the SIMT path materialises it.
+    const bool seed_in_kernel = use_tc(M, width(1), n0);
+    if (!seed_in_kernel) launch_adj_input_seed(sp.rows, M, sign, g, xl_, xu_, n0, Pb[0], s);
     int cur = 0;
     for (int m = 1; m <= st - 1; ++m) {
         const LinearLayer& L = layers_[m - 1];
@@ -332,22 +335,42 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * N);
         e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * N);
         e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
-        e.alpha_grad = cache_.as<float>(key("agrad", m, st), (size_t)2 * R * N);
+        // Projected Adam fused into the epilogue (torch::optim::Adam + clip).
+        e.adam_m = cache_.as<float>(key("am", m, st), (size_t)2 * R * N);
+        e.adam_v = cache_.as<float>(key("av", m, st), (size_t)2 * R * N);
+        e.active = adam_active_;
+        e.adam_step = adam_step_;
+        e.adam_bc2_sqrt = adam_bc2_sqrt_;
         const bool tc = use_tc(M, N, Kd);
-        const int group = tc ? 32 : 8;
-        const size_t nslot = (size_t)relax_grad_slots(M, B, group) * N;
-        e.kslot = cache_.as<float>("kslot", nslot);
-        e.bslot = cache_.as<float>("bslot", nslot);
         e.B = B;
-        prof_begin(s);
-        if (tc)
-            launch_tc_relax_adj(Pb[cur], L.W_hi, L.W_lo, M, N, Kd, e, s);
-        else
+        e.kbar = cache_.as<float>(key("kbar", m), (size_t)B * N);
+        e.bbar = cache_.as<float>(key("bbar", m), (size_t)B * N);
+        if (tc) {
+            // Tensor cores: the contraction stores Qbar only (compute-bound);
+            // the relaxation adjoint + Adam stream through a separate kernel.
+            EpiStoreQbar q;
+            q.gseed = g;
+            q.b_lin = L.b;
+            q.Qbar = cache_.as<float>("Qbar", (size_t)M * N);
+            q.rows = sp.rows;
+            if (m == 1 && seed_in_kernel) {
+                q.seed_sign = sign;
+                q.seed_xl = xl_;
+                q.seed_xu = xu_;
+            }
+            prof_begin(s);
+            launch_tc_store_qbar(Pb[cur], L.W_hi, L.W_lo, M, N, Kd, q, s);
+            prof_end(s, 2.0 * M * (double)N * Kd);
+            launch_relax_adjoint(e, q.Qbar, M, N, s);
+        } else {
+            const size_t nslot = (size_t)relax_grad_slots(M, B, 8) * N;
+            e.kslot = cache_.as<float>("kslot", nslot);
+            e.bslot = cache_.as<float>("bslot", nslot);
+            prof_begin(s);
             launch_gemm_relax_adj(Pb[cur], L.Wt, M, N, Kd, e, nullptr, s);
-        prof_end(s, 2.0 * M * (double)N * Kd);
-        launch_reduce_relax_grad(sp.rows, M, B, N, group, e.kslot, e.bslot,
-                                 cache_.as<float>(key("kbar", m), (size_t)B * N),
-                                 cache_.as<float>(key("bbar", m), (size_t)B * N), s);
+            prof_end(s, 2.0 * M * (double)N * Kd);
+            launch_reduce_relax_grad(sp.rows, M, B, N, 8, e.kslot, e.bslot, e.kbar, e.bbar, s);
+        }
         cur = 1 - cur;
     }
     rows_ += M;
@@ -482,24 +505,33 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
             launch_snapshot(bc.save, cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B,
                             width(m), cache_.as<float>(key("best_l", m), bn), cache_.as<float>(key("best_u", m), bn), s);
         }
+        // updateBestAlphas: every active box saves at iteration 0 (nothing is
+        // best yet, so every spec improves), which is each box's first save
+        // and copies every row; later saves copy only rows whose index inside
+        // the box is an improved spec index.
         for (int st = 2; st <= K_; ++st)
             for (int m = 1; m < st; ++m) {
                 const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
-                launch_best_alpha(starts_[st].rows, bc.save, bc.first_save, bc.improved, nspec, width(m),
-                                  cache_.as<float>(key("alpha", m, st), cnt), cache_.as<float>(key("abest", m, st), cnt), s);
+                float* a = cache_.as<float>(key("alpha", m, st), cnt);
+                float* best_a = cache_.as<float>(key("abest", m, st), cnt);
+                if (it == 0)
+                    LB_CUDA(cudaMemcpyAsync(best_a, a, cnt * 4, cudaMemcpyDeviceToDevice, s));
+                else
+                    launch_best_alpha_rows(starts_[st].rows, B, bc.save, bc.improved, nspec, width(m), a, best_a, s);
             }
         launch_clear_first_save(bc.save, bc.first_save, B, s);
         if (last) break;
-        // --- hand-written adjoint of the whole pass (replaces loss.backward()) ---
+        // --- hand-written adjoint of the whole pass (replaces loss.backward())
+        // with the torch::optim::Adam step + [0, 1] clip fused into it ---------
         for (int m = 1; m < K_; ++m) {
             const size_t bn = (size_t)B * width(m);
             LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("kbar", m), bn), 0, bn * 4, s));
             LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("bbar", m), bn), 0, bn * 4, s));
         }
-        for (int m = 1; m < K_; ++m) {
-            const size_t cnt = (size_t)2 * out.rows.R * width(m);
-            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("agrad", m, K_), cnt), 0, cnt * 4, s));
-        }
+        ++steps;
+        adam_active_ = bc.active;
+        adam_step_ = (float)((double)lr / (1.0 - std::pow(0.9, steps)));
+        adam_bc2_sqrt_ = (float)std::sqrt(1.0 - std::pow(0.999, steps));
         launch_output_seed(out.rows, bc.active, gout, s);
         adjoint_start(out, B, gout, out.rows.R, s);
         for (int st = K_ - 1; st >= 2; --st) {
@@ -512,19 +544,6 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
                               cache_.as<float>(key("bbar", st), bn), width(st), g, s);
             adjoint_start(sp, B, g, 2 * sp.rows.R, s);
         }
-        // --- torch::optim::Adam step + clip to [0, 1] ---------------------------
-        ++steps;
-        const double bc1 = 1.0 - std::pow(0.9, steps);
-        const double bc2 = 1.0 - std::pow(0.999, steps);
-        const float step_size = (float)((double)lr / bc1);
-        const float bc2_sqrt = (float)std::sqrt(bc2);
-        for (int st = 2; st <= K_; ++st)
-            for (int m = 1; m < st; ++m) {
-                const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
-                launch_adam(starts_[st].rows, bc.active, width(m), cache_.as<float>(key("alpha", m, st), cnt),
-                            cache_.as<float>(key("am", m, st), cnt), cache_.as<float>(key("av", m, st), cnt),
-                            cache_.as<float>(key("agrad", m, st), cnt), step_size, bc2_sqrt, s);
-            }
         lr = lr * opt_.alpha_lr_decay;
     }
     // --- restoreBestAlphas, restoreBestIntermediateBounds, final run(false) ---

@@ -118,6 +118,11 @@ private:
     bool force_simt_ = false;
     bool use_tc(int M, int N, int K) const;
 
+    // Adam step of the current alpha iteration (fused into the adjoint).
+    const int* adam_active_ = nullptr;
+    float adam_step_ = 0.f;
+    float adam_bc2_sqrt_ = 1.f;
+
     // Contraction-kernel timing (lb200_set_profiling).
     bool profile_ = false;
     std::vector<cudaEvent_t> ev_pool_;

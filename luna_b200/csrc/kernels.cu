@@ -440,9 +440,18 @@ struct EpiAdjOp {
                     e.Pbar[(size_t)r * N + c] = Qbar * dq + g * db;
                 }
                 const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
-                if (e.alpha_grad)
-                    e.alpha_grad[(size_t)r * N + c] =
-                        (f & RF_USE_ALPHA) ? Qbar * (p == 0 ? Pp : Pn) : 0.f;
+                const float ag = (f & RF_USE_ALPHA) ? Qbar * (p == 0 ? Pp : Pn) : 0.f;
+                if (e.adam_m) {
+                    if (e.active[bx]) {
+                        const size_t at = (size_t)r * N + c;
+                        float mm = e.adam_m[at], vv = e.adam_v[at];
+                        e.alpha[at] = adam_clip_update(e.alpha[at], ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
+                        e.adam_m[at] = mm;
+                        e.adam_v[at] = vv;
+                    }
+                } else if (e.alpha_grad) {
+                    e.alpha_grad[(size_t)r * N + c] = ag;
+                }
                 if (f & RF_UNSTABLE) {
                     kacc[j] += Qbar * (p == 0 ? Pn : Pp);
                     bacc[j] += g * (p == 0 ? Pn : Pp);
@@ -560,6 +569,76 @@ void launch_gemm_concretize(const float* A, const float* Bm, int M, int N, int K
 void launch_gemm_relax_adj(const float* A, const float* Bm, int M, int N, int K,
                            const EpiRelaxAdj& e, float* partial, cudaStream_t s) {
     run_gemm(A, Bm, M, N, K, EpiAdjOp{e, M, N}, partial, s);
+}
+
+// One CTA per (box, 32-column chunk); 256 threads = 32 columns x 8 row lanes.
+// Walks the box's rows of both sides; column sums of the k_up / b_up
+// adjoints go through shared memory in a fixed order.
+__global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const float* __restrict__ Qbar,
+                                                            int M, int n) {
+    const int bx = blockIdx.x;
+    const int c = blockIdx.y * 32 + (threadIdx.x & 31);
+    const int ty = threadIdx.x >> 5;
+    __shared__ float sk[8][32], sb[8][32];
+    float ks = 0.f, bs = 0.f;
+    if (c < n) {
+        const size_t bj = (size_t)bx * e.rp.n + c;
+        const uint8_t f = e.rp.flags[bj];
+        const float sl = e.rp.slope_lo[bj], k = e.rp.k_up[bj], b = e.rp.b_up[bj];
+        const bool use_alpha = (f & RF_USE_ALPHA) != 0, un = (f & RF_UNSTABLE) != 0;
+        const bool act = e.active ? e.active[bx] != 0 : false;
+        for (int p = 0; p < 2; ++p) {
+            const int first = p * e.rows.R + e.rows.box_off[bx];
+            const int last = min(p * e.rows.R + e.rows.box_off[bx + 1], M);
+            for (int r = first + ty; r < last; r += 8) {
+                const size_t at = (size_t)r * n + c;
+                const float Qb = Qbar[at];
+                const float P = e.P_saved[at];
+                const float g = e.gseed[r];
+                const float a = e.alpha ? e.alpha[at] : 0.f;
+                const float s = (e.alpha && use_alpha) ? a : sl;
+                const bool pos = P >= 0.f, neg = P <= 0.f;
+                const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
+                const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
+                if (e.Pbar) {
+                    const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
+                    const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
+                    e.Pbar[at] = Qb * dq + g * db;
+                }
+                const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
+                if (un) {
+                    ks += Qb * (p == 0 ? Pn : Pp);
+                    bs += g * (p == 0 ? Pn : Pp);
+                }
+                if (e.adam_m && act) {
+                    const float ag = use_alpha ? Qb * (p == 0 ? Pp : Pn) : 0.f;
+                    float mm = e.adam_m[at], vv = e.adam_v[at];
+                    e.alpha[at] = adam_clip_update(a, ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
+                    e.adam_m[at] = mm;
+                    e.adam_v[at] = vv;
+                }
+            }
+        }
+    }
+    sk[ty][threadIdx.x & 31] = ks;
+    sb[ty][threadIdx.x & 31] = bs;
+    __syncthreads();
+    if (ty == 0 && c < n) {
+        float kt = 0.f, bt = 0.f;
+        for (int q = 0; q < 8; ++q) {
+            kt += sk[q][threadIdx.x];
+            bt += sb[q][threadIdx.x];
+        }
+        e.kbar[(size_t)bx * n + c] += kt;
+        e.bbar[(size_t)bx * n + c] += bt;
+    }
+}
+
+void launch_relax_adjoint(const EpiRelaxAdj& e, const float* Qbar, int M, int n, cudaStream_t s) {
+    if (M == 0 || e.B == 0) return;
+    dim3 grid(e.B, ceil_div(n, 32));
+    relax_adjoint_kernel<<<grid, 256, 0, s>>>(e, Qbar, M, n);
+    LB_LAUNCH();
 }
 
 int relax_grad_slots(int M, int B, int group) { return ceil_div(M, group) + 2 * B; }
@@ -753,6 +832,34 @@ void launch_best_alpha(const RowMap& rows, const int* save, const int* first_sav
     LB_LAUNCH();
 }
 
+// Thread per (side, box, local row < nspec, column).
+__global__ void best_alpha_rows_kernel(RowMap rows, int B, const int* __restrict__ save,
+                                       const uint8_t* __restrict__ improved, int nspec, int n,
+                                       const float* __restrict__ alpha, float* __restrict__ best) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t per_side = (int64_t)B * nspec * n;
+    if (idx >= 2 * per_side) return;
+    const int p = (int)(idx / per_side);
+    const int64_t rem = idx % per_side;
+    const int bx = (int)(rem / ((int64_t)nspec * n));
+    const int local = (int)((rem / n) % nspec);
+    const int c = (int)(rem % n);
+    if (!save[bx] || !improved[(size_t)bx * nspec + local]) return;
+    const int first = rows.box_off[bx];
+    if (first + local >= rows.box_off[bx + 1]) return;
+    const size_t at = ((size_t)p * rows.R + first + local) * n + c;
+    best[at] = alpha[at];
+}
+
+void launch_best_alpha_rows(const RowMap& rows, int B, const int* save, const uint8_t* improved, int nspec,
+                            int n, const float* alpha, float* best_alpha, cudaStream_t s) {
+    const int64_t total = (int64_t)2 * B * nspec * n;
+    if (total == 0 || rows.R == 0) return;
+    best_alpha_rows_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows, B, save, improved, nspec, n, alpha,
+                                                                best_alpha);
+    LB_LAUNCH();
+}
+
 __global__ void clear_first_save_kernel(const int* save, int* first_save, int B) {
     const int bx = blockIdx.x * blockDim.x + threadIdx.x;
     if (bx < B && save[bx]) first_save[bx] = 0;
@@ -774,14 +881,10 @@ __global__ void adam_kernel(RowMap rows, const int* __restrict__ active, int n,
     const int r2 = (int)(idx / n);
     const int rr = r2 >= rows.R ? r2 - rows.R : r2;
     if (!active[rows.row_box[rr]]) return;
-    const float g = grad[idx];
-    const float mm = m[idx] * 0.9f + 0.1f * g;
-    const float vv = v[idx] * 0.999f + 0.001f * g * g;
+    float mm = m[idx], vv = v[idx];
+    alpha[idx] = adam_clip_update(alpha[idx], grad[idx], mm, vv, step_size, bc2_sqrt);
     m[idx] = mm;
     v[idx] = vv;
-    const float denom = sqrtf(vv) / bc2_sqrt + 1e-8f;
-    float a = alpha[idx] + (-step_size) * mm / denom;
-    alpha[idx] = fminf(fmaxf(a, 0.f), 1.f);
 }
 
 void launch_adam(const RowMap& rows, const int* active, int n, float* alpha, float* m, float* v,

@@ -107,16 +107,34 @@ struct EpiRelaxAdj {
     const float* gseed = nullptr;   // [M] bias adjoint of each row
     const float* b_lin = nullptr;   // [N] bias of the Linear whose W^T is the B operand
     const float* P_saved = nullptr; // [M, N] pre-relaxation A saved by the forward pass
-    const float* alpha = nullptr;   // [2R, N] or null
+    float* alpha = nullptr;         // [2R, N] or null
     float* Pbar = nullptr;          // [M, N] or null
-    float* alpha_grad = nullptr;    // [2R, N] or null
-    // Per-(8-row group, virtual box) partial sums of d loss / d k_up and
+    float* alpha_grad = nullptr;    // [2R, N] or null (gradient output when Adam is not fused)
+    // Fused projected Adam: when adam_m != null, each alpha entry of the rows
+    // of an active box takes its Adam step in place right after its gradient
+    // is formed (each alpha of a start gets its gradient from exactly one
+    // element of this epilogue), and no gradient buffer is written.
+    float* adam_m = nullptr;        // [2R, N]
+    float* adam_v = nullptr;
+    const int* active = nullptr;    // [B]
+    float adam_step = 0.f;          // lr / bias_correction1
+    float adam_bc2_sqrt = 1.f;      // sqrt(bias_correction2)
+    // Per-(row group, virtual box) partial sums of d loss / d k_up and
     // d loss / d b_up, reduced in a fixed order by launch_reduce_relax_grad.
-    // The virtual box of row r is box + side * B; slot = r / 8 + virtual box
-    // is unique because rows are sorted by virtual box.
-    float* kslot = nullptr;         // [(ceil(M/8) + 2B), N]
+    // The virtual box of row r is box + side * B; slot = r / group + virtual
+    // box is unique because rows are sorted by virtual box.
+    float* kslot = nullptr;         // [(ceil(M/group) + 2B), N]
     float* bslot = nullptr;
     int B = 0;
+    // Direct accumulators [B, N] (launch_relax_adjoint).
+    float* kbar = nullptr;
+    float* bbar = nullptr;
+    // First adjoint step on the tensor-core path: the A operand (d loss / d A
+    // at the input) is generated in the kernel from the concretisation signs
+    // instead of being read from memory (see launch_adj_input_seed).
+    const uint8_t* seed_sign = nullptr;  // [M, K]
+    const float* seed_xl = nullptr;      // [B, K]
+    const float* seed_xu = nullptr;
 };
 void launch_gemm_relax_fwd(const float* A, const float* Bm, int M, int N, int K,
                            const EpiRelaxFwd& e, float* partial, cudaStream_t s);
@@ -125,6 +143,26 @@ void launch_gemm_concretize(const float* A, const float* Bm, int M, int N, int K
 void launch_gemm_relax_adj(const float* A, const float* Bm, int M, int N, int K,
                            const EpiRelaxAdj& e, float* partial, cudaStream_t s);
 int gemm_tiles_n(int N);
+
+// Adjoint contraction whose epilogue only adds g[r] b_lin[c] and stores
+// Qbar = A . B + g b_lin (tensor-core path; the relaxation adjoint then runs
+// in launch_relax_adjoint).  Uses the seed_* fields of `e` for the first step.
+struct EpiStoreQbar {
+    const float* gseed = nullptr;   // [M]
+    const float* b_lin = nullptr;   // [N]
+    float* Qbar = nullptr;          // [M, N]
+    RowMap rows;                    // seed generation only
+    const uint8_t* seed_sign = nullptr;
+    const float* seed_xl = nullptr;
+    const float* seed_xu = nullptr;
+};
+
+// Relaxation adjoint of ReLU m for the rows of one start, from Qbar: writes
+// Pbar (may be null), takes the fused projected-Adam step of alpha (rows of
+// active boxes), and adds this start's d loss / d k_up and d loss / d b_up
+// into kbar / bbar [B, n] in a fixed order (one CTA per box and 32 columns,
+// both sides).  M = 2R, or R for the lower side only.
+void launch_relax_adjoint(const EpiRelaxAdj& e, const float* Qbar, int M, int n, cudaStream_t s);
 
 // kbar[b, c] += sum of the slots of virtual boxes b and B + b (rows < M), in
 // row order, for the slot layout of EpiRelaxAdj with `group`-row groups
@@ -171,6 +209,10 @@ void launch_snapshot(const int* save, const float* cur_l, const float* cur_u, in
 void launch_best_alpha(const RowMap& rows, const int* save, const int* first_save,
                        const uint8_t* improved, int nspec, int n, const float* alpha,
                        float* best_alpha, cudaStream_t s);
+// After the first save: only rows with index < nspec inside their box can be
+// copied, so launch over B x nspec rows per side instead of all rows.
+void launch_best_alpha_rows(const RowMap& rows, int B, const int* save, const uint8_t* improved,
+                            int nspec, int n, const float* alpha, float* best_alpha, cudaStream_t s);
 void launch_clear_first_save(const int* save, int* first_save, int B, cudaStream_t s);
 // Projected Adam (torch::optim::Adam + clamp to [0,1]) on the rows of active boxes.
 void launch_adam(const RowMap& rows, const int* active, int n, float* alpha, float* m, float* v,

@@ -33,7 +33,10 @@ constexpr int WARP_TMA = 0, WARP_MMA = 1, EPI_WARP0 = 4, XF_WARP0 = 8;
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 constexpr int A_TILE_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 
-enum { KIND_FWD = 0, KIND_CONC = 1, KIND_ADJ = 2 };
+enum { KIND_FWD = 0, KIND_CONC = 1, KIND_ADJ = 2, KIND_QBAR = 3 };
+// A operand source: raw fp32 tile by TMA, or generated in the kernel from
+// the concretisation signs (first adjoint contraction).
+enum { AMODE_TMA = 0, AMODE_SEED = 1 };
 
 __device__ int g_tc_error;
 
@@ -41,6 +44,7 @@ struct TcEpi {
     EpiRelaxFwd f;
     EpiConcretize c;
     EpiRelaxAdj a;
+    EpiStoreQbar q;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -263,11 +267,63 @@ __device__ __forceinline__ void epi_adj(const EpiRelaxAdj& e, int r, int c, int 
         bv[i] = un ? g * (p == 0 ? Pn : Pp) : 0.f;
     }
     if (e.Pbar) st16f(e.Pbar + rb, pb);
-    if (e.alpha_grad) st16f(e.alpha_grad + rb, ag);
+    if (e.adam_m) {
+        if (e.active[bx]) {
+            float mm[16], vv[16];
+            ld16f(e.adam_m + rb, mm);
+            ld16f(e.adam_v + rb, vv);
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                al[i] = adam_clip_update(al[i], ag[i], mm[i], vv[i], e.adam_step, e.adam_bc2_sqrt);
+            st16f(e.alpha + rb, al);
+            st16f(e.adam_m + rb, mm);
+            st16f(e.adam_v + rb, vv);
+        }
+    } else if (e.alpha_grad) {
+        st16f(e.alpha_grad + rb, ag);
+    }
+}
+
+// d loss / d A at the input for one row and 32 columns [k0, k0 + 32) of the
+// first adjoint contraction, from the concretisation signs (the value
+// launch_adj_input_seed writes): g x_a where A >= 0, g x_b where A <= 0.
+__device__ __forceinline__ void seed_row(const EpiStoreQbar& e, int r, int M, int K, int k0, float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    if (r >= M) return;
+    int p, rr;
+    split_row2(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    const float g = e.gseed[r];
+    const float* xa = (p == 0 ? e.seed_xl : e.seed_xu) + (size_t)bx * K;
+    const float* xb = (p == 0 ? e.seed_xu : e.seed_xl) + (size_t)bx * K;
+    const uint8_t* sg = e.seed_sign + (size_t)r * K;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const int c = k0 + 4 * j;
+        if (c + 3 < K) {
+            const uchar4 s4 = *reinterpret_cast<const uchar4*>(sg + c);
+            const float4 a4 = *reinterpret_cast<const float4*>(xa + c);
+            const float4 b4 = *reinterpret_cast<const float4*>(xb + c);
+            const uint8_t s[4] = {s4.x, s4.y, s4.z, s4.w};
+            const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                v[4 * j + q] = ((s[q] & 1) ? g * a[q] : 0.f) + ((s[q] & 2) ? g * b[q] : 0.f);
+        } else {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                if (c + q < K) {
+                    const uint8_t s = sg[c + q];
+                    v[4 * j + q] = ((s & 1) ? g * xa[c + q] : 0.f) + ((s & 2) ? g * xb[c + q] : 0.f);
+                }
+            }
+        }
+    }
 }
 
 // ------------------------------------------------------------- kernel
-template <int BN, int S, int KIND>
+template <int BN, int S, int KIND, int AMODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tbh,
                    const __grid_constant__ CUtensorMap tbl, int M, int N, int K, TcEpi ep, float* partial) {
@@ -331,8 +387,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const int s = g % S;
                     const uint32_t ph = (g / S) & 1;
                     if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
-                    mbar_arrive_tx(&full[s], A_TILE_BYTES + 2 * B_TILE_BYTES);
-                    tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
+                    mbar_arrive_tx(&full[s], (AMODE == AMODE_TMA ? A_TILE_BYTES : 0) + 2 * B_TILE_BYTES);
+                    if (AMODE == AMODE_TMA) tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
                     tma_load_2d(&tbh, &full[s], b_hi(s), kb * TC_BK, nb * BN);
                     tma_load_2d(&tbl, &full[s], b_lo(s), kb * TC_BK, nb * BN);
                 }
@@ -393,16 +449,36 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (!mbar_wait(&full[s], ph, abort)) { ok = false; break; }
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
+                if constexpr (AMODE == AMODE_TMA) {
 #pragma unroll 4
-                for (int i = xt; i < A_TILE_BYTES / 16; i += 128) {
-                    const float4 x = hi[i];
-                    float4 h, l;
-                    h.x = rna_tf32(x.x); l.x = rna_tf32(x.x - h.x);
-                    h.y = rna_tf32(x.y); l.y = rna_tf32(x.y - h.y);
-                    h.z = rna_tf32(x.z); l.z = rna_tf32(x.z - h.z);
-                    h.w = rna_tf32(x.w); l.w = rna_tf32(x.w - h.w);
-                    hi[i] = h;
-                    lo[i] = l;
+                    for (int i = xt; i < A_TILE_BYTES / 16; i += 128) {
+                        const float4 x = hi[i];
+                        float4 h, l;
+                        h.x = rna_tf32(x.x); l.x = rna_tf32(x.x - h.x);
+                        h.y = rna_tf32(x.y); l.y = rna_tf32(x.y - h.y);
+                        h.z = rna_tf32(x.z); l.z = rna_tf32(x.z - h.z);
+                        h.w = rna_tf32(x.w); l.w = rna_tf32(x.w - h.w);
+                        hi[i] = h;
+                        lo[i] = l;
+                    }
+                } else {
+                    // Generate row xt of the tile and store it in the
+                    // 128-byte swizzled layout TMA would have produced:
+                    // 16-byte chunk j of row r sits at chunk j ^ (r % 8).
+                    float v[32];
+                    const int mb = t / tiles_n;
+                    seed_row(ep.q, mb * TC_BM + xt, M, K, kb * TC_BK, v);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        float4 h, l;
+                        h.x = rna_tf32(v[4 * j]);     l.x = rna_tf32(v[4 * j] - h.x);
+                        h.y = rna_tf32(v[4 * j + 1]); l.y = rna_tf32(v[4 * j + 1] - h.y);
+                        h.z = rna_tf32(v[4 * j + 2]); l.z = rna_tf32(v[4 * j + 2] - h.z);
+                        h.w = rna_tf32(v[4 * j + 3]); l.w = rna_tf32(v[4 * j + 3] - h.w);
+                        const int at = xt * 8 + (j ^ (xt & 7));
+                        hi[at] = h;
+                        lo[at] = l;
+                    }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mbar_arrive(&split[s]);
@@ -472,6 +548,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         st16f(e.bslot + slot + c, bv);
                     }
                 }
+            } else if constexpr (KIND == KIND_QBAR) {
+                const float g = row_ok ? ep.q.gseed[r] : 0.f;
+                for (int c0 = 0; c0 < BN; c0 += 16) {
+                    float v[16];
+                    tmem_ld16(taddr + (uint32_t)c0, v);
+                    const int c = nb * BN + c0;
+                    if (c >= N || !row_ok) continue;
+                    float bl[16];
+                    ld16f(ep.q.b_lin + c, bl);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] = v[i] + g * bl[i];
+                    st16f(ep.q.Qbar + (size_t)r * N + c, v);
+                }
             } else {
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float v[16];
@@ -534,33 +623,36 @@ int num_sms() {
     return n;
 }
 
-template <int BN, int S, int KIND>
+template <int BN, int S, int KIND, int AMODE>
 void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
             float* partial, cudaStream_t s) {
     constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * BN * TC_BK * 4;
     constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
     static bool configured = false;
     if (!configured) {
-        LB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN, S, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        LB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN, S, KIND, AMODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     SMEM));
         configured = true;
     }
-    const CUtensorMap ta = make_map(A, M, K, TC_BM);
+    // In AMODE_SEED the A map is never read; it is encoded over B so that the
+    // descriptor stays valid.
+    const CUtensorMap ta = AMODE == AMODE_TMA ? make_map(A, M, K, TC_BM) : make_map(Bhi, N, K, TC_BM);
     const CUtensorMap tbh = make_map(Bhi, N, K, BN);
     const CUtensorMap tbl = make_map(Blo, N, K, BN);
     const int ntiles = ((N + BN - 1) / BN) * ((M + TC_BM - 1) / TC_BM);
     const int grid = std::min(ntiles, num_sms());
-    tc_gemm_kernel<BN, S, KIND><<<grid, NUM_THREADS, SMEM, s>>>(ta, tbh, tbl, M, N, K, ep, partial);
+    tc_gemm_kernel<BN, S, KIND, AMODE><<<grid, NUM_THREADS, SMEM, s>>>(ta, tbh, tbl, M, N, K, ep, partial);
     LB_LAUNCH();
 }
 
-template <int KIND>
+template <int KIND, int AMODE = AMODE_TMA>
 void dispatch(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
               float* partial, cudaStream_t s) {
     switch (tc_block_n(N)) {
-    case 256: run_tc<256, 2, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
-    case 128: run_tc<128, 3, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
-    case 112: run_tc<112, 3, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
-    default: run_tc<64, 4, KIND>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    case 256: run_tc<256, 2, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    case 128: run_tc<128, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    case 112: run_tc<112, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    default: run_tc<64, 4, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
     }
 }
 
@@ -626,7 +718,18 @@ void launch_tc_relax_adj(const float* A, const float* Bhi, const float* Blo, int
     if (M == 0) return;
     TcEpi ep{};
     ep.a = e;
-    dispatch<KIND_ADJ>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
+    dispatch<KIND_ADJ, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
+}
+
+void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
+                          const EpiStoreQbar& e, cudaStream_t s) {
+    if (M == 0) return;
+    TcEpi ep{};
+    ep.q = e;
+    if (e.seed_sign)
+        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
+    else
+        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
 }
 
 }  // namespace lb200

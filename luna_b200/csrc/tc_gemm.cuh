@@ -34,5 +34,9 @@ void launch_tc_concretize(const float* A, const float* Bhi, const float* Blo, in
 // Adjoint: the k_up / b_up slots are per (32-row group, virtual box).
 void launch_tc_relax_adj(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
                          const EpiRelaxAdj& e, cudaStream_t s);
+// Adjoint contraction storing Qbar = A . B^T + g b_lin only; with
+// e.seed_sign set the A operand is generated from the concretisation signs.
+void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
+                          const EpiStoreQbar& e, cudaStream_t s);
 
 }  // namespace lb200
