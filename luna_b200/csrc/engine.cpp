@@ -229,6 +229,10 @@ static ReluParams relu_view(DevCache& c, const std::string& sfx, int B, int n) {
 // the input, both sides stacked, ending in the concretisation
 // (computeConcreteLowerBound/UpperBound).  Row totals land in "val/s".
 void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s) {
+    if (tc_) {
+        forward_start_tc(sp, B, nspec, save, alpha, s);
+        return;
+    }
     const int st = sp.s;
     const int R = sp.rows.R;
     if (R == 0) return;
@@ -238,8 +242,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     float* Q[2] = {cache_.as<float>(key("Q", 0), (size_t)M * maxw), cache_.as<float>(key("Q", 1), (size_t)M * maxw)};
     float* bias = cache_.as<float>(key("bias", st), M);
     int slots_total = 0;
-    for (int m = st - 1; m >= 1; --m)
-        slots_total += std::max(gemm_tiles_n(width(m - 1)), tc_tiles_n(width(m - 1)));
+    for (int m = st - 1; m >= 1; --m) slots_total += gemm_tiles_n(width(m - 1));
     float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
 
     const LinearLayer& Ls = layers_[st - 1];
@@ -279,10 +282,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
             e.Q = Q[1 - cur];
             prof_begin(s);
-            if (use_tc(M, N, Kd))
-                launch_tc_relax_fwd(Q[cur], L.Wt_hi, L.Wt_lo, M, N, Kd, e, part + (size_t)slot * M, s);
-            else
-                launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
             cur = 1 - cur;
         } else {
@@ -292,15 +292,125 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.xu = xu_;
             if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * N);
             prof_begin(s);
-            if (use_tc(M, N, Kd))
-                launch_tc_concretize(Q[cur], L.Wt_hi, L.Wt_lo, M, N, Kd, e, part + (size_t)slot * M, s);
-            else
-                launch_gemm_concretize(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
+            launch_gemm_concretize(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
         }
-        slot += use_tc(M, N, Kd) ? tc_tiles_n(N) : gemm_tiles_n(N);
+        slot += gemm_tiles_n(N);
     }
     launch_sum_partials(bias, part, slot, M, cache_.as<float>(key("val", st), M), s);
+    rows_ += M;
+}
+
+// Tensor-core schedule of the same pass.  A contraction whose N fits one
+// column tile forms its A operand in its prologue (the relaxation of the P
+// below it, or of the one-hot rows of W for an intermediate start) and the
+// step before it stores only the raw P; a contraction with several column
+// tiles reads a materialised Q by TMA instead (forming it in the prologue
+// would redo the relaxation once per column tile), and the step before it
+// relaxes in its epilogue.  Per-row bias sums come from prologues (one slot
+// each), relaxing epilogues and the concretisation (one slot per column tile).
+void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s) {
+    const int st = sp.s;
+    const int R = sp.rows.R;
+    if (R == 0) return;
+    const int M = 2 * R;
+    const int mb = st - 1;
+    int maxw = 0;
+    for (int m = 0; m < st; ++m) maxw = std::max(maxw, width(m));
+    auto in_prologue = [&](int m) { return tc_tiles_n(width(m - 1)) == 1; };
+    int slots_total = 0;
+    for (int m = 1; m <= mb; ++m) slots_total += 1 + tc_tiles_n(width(m - 1));
+    float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
+    float* Qbuf[2] = {cache_.as<float>(key("Q", 0), (size_t)M * maxw), cache_.as<float>(key("Q", 1), (size_t)M * maxw)};
+    float* Pscr[2] = {nullptr, nullptr};
+    if (!save)
+        for (int i = 0; i < 2; ++i) Pscr[i] = cache_.as<float>(key("Pfwd", i), (size_t)M * maxw);
+    int qcur = 0, pcur = 0, slot = 0;
+    float* base = nullptr;
+    const float* P_in = nullptr;  // raw P below the next contraction (prologue modes)
+    const float* Q_in = nullptr;  // materialised A of the next contraction (TMA mode)
+    const LinearLayer& Ls = layers_[st - 1];
+    if (st == K_ || !in_prologue(mb)) {
+        // Start step: P = C . W_K (output start) or the one-hot rows of W_s,
+        // relaxed here when the first contraction reads a materialised Q.
+        StartStep ss;
+        ss.rows = sp.rows;
+        ss.M = M;
+        ss.W = Ls.W;
+        ss.bW = Ls.b;
+        ss.spec_dim = Ls.n_out;
+        ss.n = Ls.n_in;
+        if (st == K_) {
+            ss.C = C_;
+            ss.c_per_box = c_per_box_;
+            ss.nspec = nspec;
+            ss.P_save = cache_.as<float>(key("Psave", st, mb), (size_t)M * width(mb));
+            flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
+        }
+        if (!in_prologue(mb)) {
+            ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+            if (alpha) ss.alpha = cache_.as<float>(key("alpha", mb, st), (size_t)M * width(mb));
+            ss.b_next = layers_[mb - 1].b;
+            ss.Q = Qbuf[qcur];
+            Q_in = Qbuf[qcur];
+            qcur ^= 1;
+        } else {
+            P_in = ss.P_save;
+        }
+        base = cache_.as<float>(key("bias", st), M);
+        ss.bias_acc = base;
+        launch_start_step(ss, s);
+    }
+    for (int m = mb; m >= 1; --m) {
+        const LinearLayer& L = layers_[m - 1];
+        const int N = L.n_in, Kd = L.n_out;
+        TcPrologue pro;
+        if (in_prologue(m)) {
+            pro.rows = sp.rows;
+            pro.rp = relu_view(cache_, std::to_string(m), B, Kd);
+            if (alpha) pro.alpha = cache_.as<float>(key("alpha", m, st), (size_t)M * Kd);
+            pro.b_lin = L.b;
+            if (m == mb && st != K_) {
+                pro.gather_W = Ls.W;
+                pro.gather_b = Ls.b;
+            } else {
+                pro.P = P_in;
+            }
+            pro.bias_part = part + (size_t)slot * M;
+            ++slot;
+        }
+        const float* A = in_prologue(m) ? nullptr : Q_in;
+        flops_ += 2.0 * M * (double)N * Kd;
+        prof_begin(s);
+        if (m == 1) {
+            EpiConcretize e;
+            e.rows = sp.rows;
+            e.xl = xl_;
+            e.xu = xu_;
+            if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * N);
+            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, nullptr, nullptr, &e, part + (size_t)slot * M, s);
+            slot += tc_tiles_n(N);
+        } else if (in_prologue(m - 1)) {
+            float* P_out = save ? cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N) : Pscr[pcur];
+            pcur ^= 1;
+            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, P_out, nullptr, nullptr, nullptr, s);
+            P_in = P_out;
+        } else {
+            EpiRelaxFwd e;
+            e.rows = sp.rows;
+            e.rp = relu_view(cache_, std::to_string(m - 1), B, N);
+            if (alpha) e.alpha = cache_.as<float>(key("alpha", m - 1, st), (size_t)M * N);
+            e.b_next = layers_[m - 2].b;
+            if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
+            e.Q = Qbuf[qcur];
+            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, nullptr, &e, nullptr, part + (size_t)slot * M, s);
+            slot += tc_tiles_n(N);
+            Q_in = Qbuf[qcur];
+            qcur ^= 1;
+        }
+        prof_end(s, 2.0 * M * (double)N * Kd);
+    }
+    launch_sum_partials(base, part, slot, M, cache_.as<float>(key("val", st), M), s);
     rows_ += M;
 }
 
@@ -320,7 +430,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     const uint8_t* sign = cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * n0);
     // On the tensor-core path the first contraction generates d loss / d A at
     // the input from the signs itself; the SIMT path materialises it.
-    const bool seed_in_kernel = use_tc(M, width(1), n0);
+    const bool seed_in_kernel = tc_;
     if (!seed_in_kernel) launch_adj_input_seed(sp.rows, M, sign, g, xl_, xu_, n0, Pb[0], s);
     int cur = 0;
     for (int m = 1; m <= st - 1; ++m) {
@@ -332,7 +442,10 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         e.rp = relu_view(cache_, std::to_string(m), B, N);
         e.gseed = g;
         e.b_lin = L.b;
-        e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * N);
+        if (tc_ && m == st - 1 && st != K_)
+            e.gather_W = layers_[st - 1].W;  // P of the ReLU below a one-hot start
+        else
+            e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * N);
         e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * N);
         e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
         // Projected Adam fused into the epilogue (torch::optim::Adam + clip).
@@ -341,7 +454,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         e.active = adam_active_;
         e.adam_step = adam_step_;
         e.adam_bc2_sqrt = adam_bc2_sqrt_;
-        const bool tc = use_tc(M, N, Kd);
+        const bool tc = tc_;
         e.B = B;
         e.kbar = cache_.as<float>(key("kbar", m), (size_t)B * N);
         e.bbar = cache_.as<float>(key("bbar", m), (size_t)B * N);
@@ -428,6 +541,7 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     xl_ = xl;
     xu_ = xu;
     C_ = C;
+    tc_ = tc_eligible();
     c_per_box_ = c_per_box;
     const int nout = width(K_);
     // IBP (CROWNAnalysis::computeIBPBounds): pure interval bounds of every Linear.
@@ -562,7 +676,15 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     (void)nout;
 }
 
-bool Model::use_tc(int M, int N, int K) const { return !force_simt_ && tc_supported(M, N, K); }
+// The tensor-core schedule needs every contraction shape on the tensor-core
+// path: all widths that appear as N or K of a contraction (n_0 .. n_{K-1})
+// multiples of 16.
+bool Model::tc_eligible() const {
+    if (force_simt_) return false;
+    for (int m = 0; m < K_; ++m)
+        if (!tc_supported(1, width(m), width(m)) || width(m) % 16 != 0) return false;
+    return true;
+}
 
 // ------------------------------------------------------------ profiling
 void Model::prof_begin(cudaStream_t s) {

@@ -116,7 +116,9 @@ private:
     bool last_alpha_ = false;
 
     bool force_simt_ = false;
-    bool use_tc(int M, int N, int K) const;
+    bool tc_ = false;  // tensor-core schedule for the current chunk
+    bool tc_eligible() const;
+    void forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s);
 
     // Adam step of the current alpha iteration (fused into the adjoint).
     const int* adam_active_ = nullptr;

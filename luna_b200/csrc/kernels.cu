@@ -307,7 +307,7 @@ __global__ void start_step_kernel(StartStep st) {
             const float s = lower_slope(st.rp, st.alpha, r, bx, c, st.n);
             Q = relax_fwd(P, p, s, st.rp.k_up[bj], st.rp.b_up[bj], part);
         }
-        st.Q[(size_t)r * st.n + c] = Q;
+        if (st.Q) st.Q[(size_t)r * st.n + c] = Q;
         if (st.b_next) part = fmaf(Q, st.b_next[c], part);
     }
     part = warp_sum(part);
@@ -593,7 +593,8 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
             for (int r = first + ty; r < last; r += 8) {
                 const size_t at = (size_t)r * n + c;
                 const float Qb = Qbar[at];
-                const float P = e.P_saved[at];
+                const float P = e.gather_W ? e.gather_W[(size_t)e.rows.row_id[r - p * e.rows.R] * n + c]
+                                           : e.P_saved[at];
                 const float g = e.gseed[r];
                 const float a = e.alpha ? e.alpha[at] : 0.f;
                 const float s = (e.alpha && use_alpha) ? a : sl;

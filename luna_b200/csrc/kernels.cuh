@@ -129,6 +129,10 @@ struct EpiRelaxAdj {
     // Direct accumulators [B, N] (launch_relax_adjoint).
     float* kbar = nullptr;
     float* bbar = nullptr;
+    // launch_relax_adjoint: when set, the pre-relaxation A of row r is the
+    // weight row gather_W[row_id[r]] (ReLU directly below a one-hot start)
+    // and P_saved is not read.
+    const float* gather_W = nullptr;
     // First adjoint step on the tensor-core path: the A operand (d loss / d A
     // at the input) is generated in the kernel from the concretisation signs
     // instead of being read from memory (see launch_adj_input_seed).

@@ -33,10 +33,13 @@ constexpr int WARP_TMA = 0, WARP_MMA = 1, EPI_WARP0 = 4, XF_WARP0 = 8;
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 constexpr int A_TILE_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 
-enum { KIND_FWD = 0, KIND_CONC = 1, KIND_ADJ = 2, KIND_QBAR = 3 };
-// A operand source: raw fp32 tile by TMA, or generated in the kernel from
-// the concretisation signs (first adjoint contraction).
-enum { AMODE_TMA = 0, AMODE_SEED = 1 };
+// Epilogues: relaxation of the next ReLU (stores P and Q), input
+// concretisation, Qbar store (adjoint), raw P store (forward).
+enum { KIND_FWD = 0, KIND_CONC = 1, KIND_QBAR = 3, KIND_STOREP = 4 };
+// A operand source: raw fp32 tile by TMA; generated in the kernel from the
+// concretisation signs (first adjoint contraction); the ReLU relaxation of a
+// TMA-loaded P (RELAX) or of gathered weight rows (GATHER, one-hot start).
+enum { AMODE_TMA = 0, AMODE_SEED = 1, AMODE_RELAX = 2, AMODE_GATHER = 3 };
 
 __device__ int g_tc_error;
 
@@ -45,6 +48,7 @@ struct TcEpi {
     EpiConcretize c;
     EpiRelaxAdj a;
     EpiStoreQbar q;
+    float* P_out = nullptr;  // KIND_STOREP
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -175,6 +179,9 @@ __device__ __forceinline__ void st16f(float* p, const float (&v)[16]) {
 // accumulator values for columns [c, c + 16).  N is a multiple of 16, so a
 // 16-column chunk is either fully inside [0, N) or fully outside.
 
+// Relaxation of the next ReLU down in the epilogue (used when the next
+// contraction takes its A operand by TMA): stores P (saved for the adjoint)
+// and Q = relax(P), and sums the relaxation intercepts + Q . b_next per row.
 __device__ __forceinline__ void epi_fwd(const EpiRelaxFwd& e, int r, int c, int N, const float (&v)[16],
                                         float& part) {
     int p, rr;
@@ -230,60 +237,6 @@ __device__ __forceinline__ void epi_conc(const EpiConcretize& e, int r, int c, i
     if (e.sign) *reinterpret_cast<uint4*>(e.sign + (size_t)r * N + c) = *reinterpret_cast<const uint4*>(sg);
 }
 
-// Relaxation adjoint; kv / bv receive this row's contributions to
-// d loss / d k_up and d loss / d b_up for the 16 columns.
-__device__ __forceinline__ void epi_adj(const EpiRelaxAdj& e, int r, int c, int N, const float (&v)[16], float g,
-                                        float (&kv)[16], float (&bv)[16]) {
-    int p, rr;
-    split_row2(r, e.rows.R, p, rr);
-    const int bx = e.rows.row_box[rr];
-    const size_t rb = (size_t)r * N + c;
-    const size_t bj = (size_t)bx * e.rp.n + c;
-    float P[16], bl[16], sl[16], ku[16], bu[16], al[16];
-    ld16f(e.P_saved + rb, P);
-    ld16f(e.b_lin + c, bl);
-    ld16f(e.rp.slope_lo + bj, sl);
-    ld16f(e.rp.k_up + bj, ku);
-    ld16f(e.rp.b_up + bj, bu);
-    if (e.alpha) ld16f(e.alpha + rb, al);
-    const uint4 fl4 = *reinterpret_cast<const uint4*>(e.rp.flags + bj);
-    const uint8_t* fl = reinterpret_cast<const uint8_t*>(&fl4);
-    float pb[16], ag[16];
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const float Qbar = v[i] + g * bl[i];
-        const float s = (e.alpha && (fl[i] & RF_USE_ALPHA)) ? al[i] : sl[i];
-        const float k = ku[i], b = bu[i];
-        const bool pos = P[i] >= 0.f, neg = P[i] <= 0.f;
-        const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
-        const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
-        const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
-        const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
-        pb[i] = Qbar * dq + g * db;
-        const float Pp = fmaxf(P[i], 0.f), Pn = fminf(P[i], 0.f);
-        ag[i] = (fl[i] & RF_USE_ALPHA) ? Qbar * (p == 0 ? Pp : Pn) : 0.f;
-        const bool un = (fl[i] & RF_UNSTABLE) != 0;
-        kv[i] = un ? Qbar * (p == 0 ? Pn : Pp) : 0.f;
-        bv[i] = un ? g * (p == 0 ? Pn : Pp) : 0.f;
-    }
-    if (e.Pbar) st16f(e.Pbar + rb, pb);
-    if (e.adam_m) {
-        if (e.active[bx]) {
-            float mm[16], vv[16];
-            ld16f(e.adam_m + rb, mm);
-            ld16f(e.adam_v + rb, vv);
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-                al[i] = adam_clip_update(al[i], ag[i], mm[i], vv[i], e.adam_step, e.adam_bc2_sqrt);
-            st16f(e.alpha + rb, al);
-            st16f(e.adam_m + rb, mm);
-            st16f(e.adam_v + rb, vv);
-        }
-    } else if (e.alpha_grad) {
-        st16f(e.alpha_grad + rb, ag);
-    }
-}
-
 // d loss / d A at the input for one row and 32 columns [k0, k0 + 32) of the
 // first adjoint contraction, from the concretisation signs (the value
 // launch_adj_input_seed writes): g x_a where A >= 0, g x_b where A <= 0.
@@ -326,7 +279,8 @@ __device__ __forceinline__ void seed_row(const EpiStoreQbar& e, int r, int M, in
 template <int BN, int S, int KIND, int AMODE>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tbh,
-                   const __grid_constant__ CUtensorMap tbl, int M, int N, int K, TcEpi ep, float* partial) {
+                   const __grid_constant__ CUtensorMap tbl, const __grid_constant__ CUtensorMap talpha, int M,
+                   int N, int K, TcEpi ep, TcPrologue pro, float* partial) {
     constexpr int B_TILE_BYTES = BN * TC_BK * 4;
     constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
     constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
@@ -387,8 +341,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const int s = g % S;
                     const uint32_t ph = (g / S) & 1;
                     if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
-                    mbar_arrive_tx(&full[s], (AMODE == AMODE_TMA ? A_TILE_BYTES : 0) + 2 * B_TILE_BYTES);
-                    if (AMODE == AMODE_TMA) tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
+                    // A raw (TMA / RELAX: P) lands in the hi slot, alpha (RELAX /
+                    // GATHER) in the lo slot; the split warps overwrite both.
+                    const bool load_a = AMODE == AMODE_TMA || AMODE == AMODE_RELAX;
+                    const bool load_alpha = (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) && pro.alpha;
+                    mbar_arrive_tx(&full[s], (load_a ? A_TILE_BYTES : 0) + (load_alpha ? A_TILE_BYTES : 0) +
+                                                 2 * B_TILE_BYTES);
+                    if (load_a) tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
+                    if (load_alpha) tma_load_2d(&talpha, &full[s], a_lo(s), kb * TC_BK, mb * TC_BM);
                     tma_load_2d(&tbh, &full[s], b_hi(s), kb * TC_BK, nb * BN);
                     tma_load_2d(&tbl, &full[s], b_lo(s), kb * TC_BK, nb * BN);
                 }
@@ -441,15 +401,82 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     } else if (warp >= XF_WARP0) {
         const int xt = threadIdx.x - XF_WARP0 * 32;
         uint32_t g = 0;
+        // RELAX / GATHER: this thread owns tile row xt (all 8 float4 chunks
+        // of it in every K block), so its bias row sum needs no reduction.
+        int rbox = 0, rid = 0, rside = 0;
+        float bsum = 0.f;
+        bool rok = false;
         for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
             bool ok = true;
+            const int mb_t = t / tiles_n, nb_t = t % tiles_n;
+            if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
+                const int r = mb_t * TC_BM + xt;
+                rok = r < M;
+                bsum = 0.f;
+                rbox = rid = rside = 0;
+                if (rok) {
+                    int p, rr;
+                    split_row2(r, pro.rows.R, p, rr);
+                    rside = p;
+                    rbox = pro.rows.row_box[rr];
+                    rid = pro.rows.row_id[rr];
+                }
+            }
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % S;
                 const uint32_t ph = (g / S) & 1;
                 if (!mbar_wait(&full[s], ph, abort)) { ok = false; break; }
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
-                if constexpr (AMODE == AMODE_TMA) {
+                if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
+                    // Logical chunk j of row xt sits at swizzled slot j ^ (xt % 8).
+#pragma unroll 2
+                    for (int j = 0; j < 8; ++j) {
+                        const int i = xt * 8 + (j ^ (xt & 7));
+                        const int col0 = kb * TC_BK + 4 * j;
+                        float4 h = make_float4(0.f, 0.f, 0.f, 0.f), l = h;
+                        if (rok && col0 < K) {
+                            float P[4], A[4] = {0.f, 0.f, 0.f, 0.f}, sl[4], ku[4], bu[4], bl[4];
+                            if (AMODE == AMODE_RELAX) {
+                                const float4 p4 = hi[i];
+                                P[0] = p4.x; P[1] = p4.y; P[2] = p4.z; P[3] = p4.w;
+                            } else {
+                                ld16f<4>(pro.gather_W + (size_t)rid * K + col0, P);
+                            }
+                            if (pro.alpha) {
+                                const float4 a4 = lo[i];
+                                A[0] = a4.x; A[1] = a4.y; A[2] = a4.z; A[3] = a4.w;
+                            }
+                            const size_t bj = (size_t)rbox * pro.rp.n + col0;
+                            ld16f<4>(pro.rp.slope_lo + bj, sl);
+                            ld16f<4>(pro.rp.k_up + bj, ku);
+                            ld16f<4>(pro.rp.b_up + bj, bu);
+                            ld16f<4>(pro.b_lin + col0, bl);
+                            const uchar4 f4 = *reinterpret_cast<const uchar4*>(pro.rp.flags + bj);
+                            const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
+                            float Q[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const float sv = (pro.alpha && (fl[q] & RF_USE_ALPHA)) ? A[q] : sl[q];
+                                const float pos = fmaxf(P[q], 0.f), neg = fminf(P[q], 0.f);
+                                if (rside == 0) {
+                                    bsum += neg * bu[q];
+                                    Q[q] = pos * sv + neg * ku[q];
+                                } else {
+                                    bsum += pos * bu[q];
+                                    Q[q] = pos * ku[q] + neg * sv;
+                                }
+                                bsum = fmaf(Q[q], bl[q], bsum);
+                            }
+                            h.x = rna_tf32(Q[0]); l.x = rna_tf32(Q[0] - h.x);
+                            h.y = rna_tf32(Q[1]); l.y = rna_tf32(Q[1] - h.y);
+                            h.z = rna_tf32(Q[2]); l.z = rna_tf32(Q[2] - h.z);
+                            h.w = rna_tf32(Q[3]); l.w = rna_tf32(Q[3] - h.w);
+                        }
+                        hi[i] = h;
+                        lo[i] = l;
+                    }
+                } else if constexpr (AMODE == AMODE_TMA) {
 #pragma unroll 4
                     for (int i = xt; i < A_TILE_BYTES / 16; i += 128) {
                         const float4 x = hi[i];
@@ -484,6 +511,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 mbar_arrive(&split[s]);
             }
             if (!ok) break;
+            if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
+                // One write per row: only the first column tile of each row block.
+                if (rok && nb_t == 0 && pro.bias_part)
+                    pro.bias_part[mb_t * TC_BM + xt] =
+                        bsum + ((AMODE == AMODE_GATHER && pro.gather_b) ? pro.gather_b[rid] : 0.f);
+            }
         }
     } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
         const int q = warp - EPI_WARP0;
@@ -498,55 +531,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const bool row_ok = r < M;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
             float part = 0.f;
-            if constexpr (KIND == KIND_ADJ) {
-                const EpiRelaxAdj& e = ep.a;
-                int vb = -1 - lane;  // rows past M never join a segment
-                float g = 0.f;
-                if (row_ok) {
-                    int p, rr;
-                    split_row2(r, e.rows.R, p, rr);
-                    vb = e.rows.row_box[rr] + p * e.B;
-                    g = e.gseed[r];
-                }
-                bool same[5];
-#pragma unroll
-                for (int o = 0; o < 5; ++o) {
-                    const int off = 1 << o;
-                    const int ovb = __shfl_down_sync(0xffffffffu, vb, off);
-                    same[o] = (lane + off < 32) && (ovb == vb);
-                }
-                const int up = __shfl_up_sync(0xffffffffu, vb, 1);
-                const bool head = row_ok && (lane == 0 || up != vb);
-                const size_t slot = (size_t)((r >> 5) + vb) * N;
+            if constexpr (KIND == KIND_STOREP) {
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float v[16];
                     tmem_ld16(taddr + (uint32_t)c0, v);
                     const int c = nb * BN + c0;
-                    if (c >= N) continue;
-                    float kv[16], bv[16];
-                    if (row_ok) {
-                        epi_adj(e, r, c, N, v, g, kv, bv);
-                    } else {
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) kv[i] = bv[i] = 0.f;
-                    }
-#pragma unroll
-                    for (int o = 0; o < 5; ++o) {
-                        const int off = 1 << o;
-#pragma unroll
-                        for (int i = 0; i < 16; ++i) {
-                            const float uk = __shfl_down_sync(0xffffffffu, kv[i], off);
-                            const float ub = __shfl_down_sync(0xffffffffu, bv[i], off);
-                            if (same[o]) {
-                                kv[i] += uk;
-                                bv[i] += ub;
-                            }
-                        }
-                    }
-                    if (head) {
-                        st16f(e.kslot + slot + c, kv);
-                        st16f(e.bslot + slot + c, bv);
-                    }
+                    if (c >= N || !row_ok) continue;
+                    st16f(ep.P_out + (size_t)r * N + c, v);
                 }
             } else if constexpr (KIND == KIND_QBAR) {
                 const float g = row_ok ? ep.q.gseed[r] : 0.f;
@@ -625,7 +616,7 @@ int num_sms() {
 
 template <int BN, int S, int KIND, int AMODE>
 void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
-            float* partial, cudaStream_t s) {
+            const TcPrologue& pro, float* partial, cudaStream_t s) {
     constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * BN * TC_BK * 4;
     constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
     static bool configured = false;
@@ -634,25 +625,28 @@ void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, in
                                      SMEM));
         configured = true;
     }
-    // In AMODE_SEED the A map is never read; it is encoded over B so that the
-    // descriptor stays valid.
-    const CUtensorMap ta = AMODE == AMODE_TMA ? make_map(A, M, K, TC_BM) : make_map(Bhi, N, K, TC_BM);
+    // Maps the mode does not read are encoded over B so that they stay valid.
+    const bool a_tma = AMODE == AMODE_TMA || AMODE == AMODE_RELAX;
+    const float* a_src = AMODE == AMODE_RELAX ? pro.P : A;
+    const CUtensorMap ta = a_tma ? make_map(a_src, M, K, TC_BM) : make_map(Bhi, N, K, TC_BM);
+    const CUtensorMap talpha = pro.alpha ? make_map(pro.alpha, M, K, TC_BM) : make_map(Bhi, N, K, TC_BM);
     const CUtensorMap tbh = make_map(Bhi, N, K, BN);
     const CUtensorMap tbl = make_map(Blo, N, K, BN);
     const int ntiles = ((N + BN - 1) / BN) * ((M + TC_BM - 1) / TC_BM);
     const int grid = std::min(ntiles, num_sms());
-    tc_gemm_kernel<BN, S, KIND, AMODE><<<grid, NUM_THREADS, SMEM, s>>>(ta, tbh, tbl, M, N, K, ep, partial);
+    tc_gemm_kernel<BN, S, KIND, AMODE><<<grid, NUM_THREADS, SMEM, s>>>(ta, tbh, tbl, talpha, M, N, K, ep, pro,
+                                                                       partial);
     LB_LAUNCH();
 }
 
-template <int KIND, int AMODE = AMODE_TMA>
+template <int KIND, int AMODE>
 void dispatch(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
-              float* partial, cudaStream_t s) {
+              const TcPrologue& pro, float* partial, cudaStream_t s) {
     switch (tc_block_n(N)) {
-    case 256: run_tc<256, 2, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
-    case 128: run_tc<128, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
-    case 112: run_tc<112, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
-    default: run_tc<64, 4, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, partial, s); break;
+    case 256: run_tc<256, 2, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 128: run_tc<128, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 112: run_tc<112, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    default: run_tc<64, 4, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
     }
 }
 
@@ -697,39 +691,44 @@ void launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, cudaSt
     LB_LAUNCH();
 }
 
-void launch_tc_relax_fwd(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                         const EpiRelaxFwd& e, float* partial, cudaStream_t s) {
-    if (M == 0) return;
-    TcEpi ep{};
-    ep.f = e;
-    dispatch<KIND_FWD>(A, Bhi, Blo, M, N, K, ep, partial, s);
-}
-
-void launch_tc_concretize(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                          const EpiConcretize& e, float* partial, cudaStream_t s) {
-    if (M == 0) return;
-    TcEpi ep{};
-    ep.c = e;
-    dispatch<KIND_CONC>(A, Bhi, Blo, M, N, K, ep, partial, s);
-}
-
-void launch_tc_relax_adj(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                         const EpiRelaxAdj& e, cudaStream_t s) {
-    if (M == 0) return;
-    TcEpi ep{};
-    ep.a = e;
-    dispatch<KIND_ADJ, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
-}
-
 void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
                           const EpiStoreQbar& e, cudaStream_t s) {
     if (M == 0) return;
     TcEpi ep{};
     ep.q = e;
+    const TcPrologue none{};
     if (e.seed_sign)
-        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
+        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, none, nullptr, s);
     else
-        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, nullptr, s);
+        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, none, nullptr, s);
+}
+
+template <int KIND>
+static void dispatch_amode(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M,
+                           int N, int K, const TcEpi& ep, float* partial, cudaStream_t s) {
+    if (pro.gather_W)
+        dispatch<KIND, AMODE_GATHER>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, s);
+    else if (pro.P)
+        dispatch<KIND, AMODE_RELAX>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, s);
+    else
+        dispatch<KIND, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, pro, partial, s);
+}
+
+void launch_tc_forward(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M, int N,
+                       int K, float* P_out, const EpiRelaxFwd* fwd, const EpiConcretize* conc, float* partial,
+                       cudaStream_t s) {
+    if (M == 0) return;
+    TcEpi ep{};
+    if (conc) {
+        ep.c = *conc;
+        dispatch_amode<KIND_CONC>(A, pro, Bhi, Blo, M, N, K, ep, partial, s);
+    } else if (fwd) {
+        ep.f = *fwd;
+        dispatch_amode<KIND_FWD>(A, pro, Bhi, Blo, M, N, K, ep, partial, s);
+    } else {
+        ep.P_out = P_out;
+        dispatch_amode<KIND_STOREP>(A, pro, Bhi, Blo, M, N, K, ep, nullptr, s);
+    }
 }
 
 }  // namespace lb200

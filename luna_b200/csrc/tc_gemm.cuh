@@ -27,16 +27,35 @@ void launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, cudaSt
 // out (0 = ok).  The engine checks it after each call.
 int* tc_error_flag();
 
-void launch_tc_relax_fwd(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                         const EpiRelaxFwd& e, float* partial, cudaStream_t s);
-void launch_tc_concretize(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                          const EpiConcretize& e, float* partial, cudaStream_t s);
-// Adjoint: the k_up / b_up slots are per (32-row group, virtual box).
-void launch_tc_relax_adj(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                         const EpiRelaxAdj& e, cudaStream_t s);
 // Adjoint contraction storing Qbar = A . B^T + g b_lin only; with
 // e.seed_sign set the A operand is generated from the concretisation signs.
 void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
                           const EpiStoreQbar& e, cudaStream_t s);
+
+// Forward contraction whose A operand is the ReLU relaxation of P, formed in
+// the kernel (BoundedReLUNode::boundBackward, dense A): Q = P+ s + P- k
+// (lower side) or P+ k + P- s (upper side), s = alpha or the static lower
+// slope.  P comes by TMA from `P` [M, K], or, when gather_W is set, is the
+// row gather_W[row_id] (the one-hot start A . W of an intermediate start).
+// The prologue also writes the row sums of the relaxation intercepts plus
+// Q . b_lin (plus gather_b[row_id] when gathering) into bias_part[M].
+struct TcPrologue {
+    RowMap rows;
+    ReluParams rp;                  // the ReLU below (rp.n == K)
+    const float* P = nullptr;       // [M, K] (TMA) unless gather_W
+    const float* alpha = nullptr;   // [M, K] or null (TMA)
+    const float* b_lin = nullptr;   // [K]
+    const float* gather_W = nullptr;
+    const float* gather_b = nullptr;
+    float* bias_part = nullptr;     // [M]
+};
+// One forward contraction.  A operand: the prologue's relaxation when
+// pro.gather_W or pro.P is set, else the raw (already relaxed) A [M, K] by
+// TMA.  Epilogue: the input concretisation when `conc` is set (partial sums
+// per column tile), the next ReLU's relaxation when `fwd` is set (stores P
+// and Q, partial sums per column tile), else a raw store of P into P_out.
+void launch_tc_forward(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M, int N,
+                       int K, float* P_out, const EpiRelaxFwd* fwd, const EpiConcretize* conc, float* partial,
+                       cudaStream_t s);
 
 }  // namespace lb200
