@@ -56,8 +56,10 @@ def config(n_gpus):
 
 def rank_boxes(rank, n_gpus):
     """This rank's slice of one seeded global box set (same weights on every rank)."""
+    from luna_b200.shard import shard_range
     g, bx = W.mlp_784_256x4_10(BOXES_PER_GPU * n_gpus)
-    return g, bx.slice(rank * BOXES_PER_GPU, (rank + 1) * BOXES_PER_GPU)
+    a, b = shard_range(rank, n_gpus, bx.n)
+    return g, bx.slice(a, b)
 
 
 # ---------------------------------------------------------------- clocks
@@ -165,7 +167,8 @@ def run_engine(args):
     B, nspec = bx.n, bx.C.shape[1]
     lb = torch.empty((B, nspec), device=dev)
     ub = torch.empty((B, nspec), device=dev)
-    gathered = torch.empty((world, 2, B, nspec), device=dev)
+    from luna_b200.shard import gather_bounds
+    counts = [BOXES_PER_GPU] * world
     flush = torch.empty(L2_FLUSH_BYTES // 4, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -173,7 +176,7 @@ def run_engine(args):
         model.compute_bounds_ptr(abi.METHOD_ALPHA_CROWN, xl.data_ptr(), xu.data_ptr(), B, Cm.data_ptr(),
                                  Cm.shape[0], nspec, lb.data_ptr(), ub.data_ptr(), stream.cuda_stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, torch.stack([lb, ub]).unsqueeze(0).contiguous())
+            gather_bounds(lb, ub, counts)  # NCCL all-gather of the final bounds
         return model.last_stats
 
     for _ in range(args.warmup):

@@ -635,10 +635,118 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
     }
 }
 
+// Vectorised variant (n % 4 == 0): one CTA per (box, 128 columns); 256
+// threads = 32 column lanes of 4 columns x 8 row lanes; float4 traffic.
+__global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, const float* __restrict__ Qbar,
+                                                               int M, int n) {
+    const int bx = blockIdx.x;
+    const int c = blockIdx.y * 128 + (threadIdx.x & 31) * 4;
+    const int ty = threadIdx.x >> 5;
+    __shared__ float4 sk[8][32], sb[8][32];
+    float ks[4] = {0.f, 0.f, 0.f, 0.f}, bs[4] = {0.f, 0.f, 0.f, 0.f};
+    const float* __restrict__ Ps = e.P_saved;
+    const float* __restrict__ Gw = e.gather_W;
+    const float* __restrict__ gs = e.gseed;
+    float* __restrict__ al = e.alpha;
+    float* __restrict__ am = e.adam_m;
+    float* __restrict__ av = e.adam_v;
+    float* __restrict__ pb = e.Pbar;
+    if (c < n) {
+        const size_t bj = (size_t)bx * e.rp.n + c;
+        float sl[4], ku[4], bu[4];
+        const float4 sl4 = *reinterpret_cast<const float4*>(e.rp.slope_lo + bj);
+        const float4 ku4 = *reinterpret_cast<const float4*>(e.rp.k_up + bj);
+        const float4 bu4 = *reinterpret_cast<const float4*>(e.rp.b_up + bj);
+        const uchar4 f4 = *reinterpret_cast<const uchar4*>(e.rp.flags + bj);
+        sl[0] = sl4.x; sl[1] = sl4.y; sl[2] = sl4.z; sl[3] = sl4.w;
+        ku[0] = ku4.x; ku[1] = ku4.y; ku[2] = ku4.z; ku[3] = ku4.w;
+        bu[0] = bu4.x; bu[1] = bu4.y; bu[2] = bu4.z; bu[3] = bu4.w;
+        const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
+        const bool act = e.active ? e.active[bx] != 0 : false;
+        const bool adam = am != nullptr && act;
+        for (int p = 0; p < 2; ++p) {
+            const int first = p * e.rows.R + e.rows.box_off[bx];
+            const int last = min(p * e.rows.R + e.rows.box_off[bx + 1], M);
+            for (int r = first + ty; r < last; r += 8) {
+                const size_t at = (size_t)r * n + c;
+                const float4 q4 = *reinterpret_cast<const float4*>(Qbar + at);
+                const float4 p4 = Gw ? *reinterpret_cast<const float4*>(Gw + (size_t)e.rows.row_id[r - p * e.rows.R] * n + c)
+                                     : *reinterpret_cast<const float4*>(Ps + at);
+                const float g = gs[r];
+                float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (al) a4 = *reinterpret_cast<const float4*>(al + at);
+                float4 m4, v4;
+                if (adam) {
+                    m4 = *reinterpret_cast<const float4*>(am + at);
+                    v4 = *reinterpret_cast<const float4*>(av + at);
+                }
+                const float Q[4] = {q4.x, q4.y, q4.z, q4.w};
+                const float P[4] = {p4.x, p4.y, p4.z, p4.w};
+                float A[4] = {a4.x, a4.y, a4.z, a4.w};
+                float Mm[4] = {0.f, 0.f, 0.f, 0.f}, Vv[4] = {0.f, 0.f, 0.f, 0.f};
+                if (adam) {
+                    Mm[0] = m4.x; Mm[1] = m4.y; Mm[2] = m4.z; Mm[3] = m4.w;
+                    Vv[0] = v4.x; Vv[1] = v4.y; Vv[2] = v4.z; Vv[3] = v4.w;
+                }
+                float out[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const bool use_alpha = (fl[i] & RF_USE_ALPHA) != 0, un = (fl[i] & RF_UNSTABLE) != 0;
+                    const float s = (al && use_alpha) ? A[i] : sl[i];
+                    const bool pos = P[i] >= 0.f, neg = P[i] <= 0.f;
+                    const float sP = p == 0 ? s : ku[i], sN = p == 0 ? ku[i] : s;
+                    const float bP = p == 0 ? 0.f : bu[i], bN = p == 0 ? bu[i] : 0.f;
+                    const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
+                    const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
+                    out[i] = Q[i] * dq + g * db;
+                    const float Pp = fmaxf(P[i], 0.f), Pn = fminf(P[i], 0.f);
+                    if (un) {
+                        ks[i] += Q[i] * (p == 0 ? Pn : Pp);
+                        bs[i] += g * (p == 0 ? Pn : Pp);
+                    }
+                    if (adam) {
+                        const float ag = use_alpha ? Q[i] * (p == 0 ? Pp : Pn) : 0.f;
+                        A[i] = adam_clip_update(A[i], ag, Mm[i], Vv[i], e.adam_step, e.adam_bc2_sqrt);
+                    }
+                }
+                if (pb) *reinterpret_cast<float4*>(pb + at) = make_float4(out[0], out[1], out[2], out[3]);
+                if (adam) {
+                    *reinterpret_cast<float4*>(al + at) = make_float4(A[0], A[1], A[2], A[3]);
+                    *reinterpret_cast<float4*>(am + at) = make_float4(Mm[0], Mm[1], Mm[2], Mm[3]);
+                    *reinterpret_cast<float4*>(av + at) = make_float4(Vv[0], Vv[1], Vv[2], Vv[3]);
+                }
+            }
+        }
+    }
+    sk[ty][threadIdx.x & 31] = make_float4(ks[0], ks[1], ks[2], ks[3]);
+    sb[ty][threadIdx.x & 31] = make_float4(bs[0], bs[1], bs[2], bs[3]);
+    __syncthreads();
+    if (ty == 0 && c < n) {
+        float4 kt = make_float4(0.f, 0.f, 0.f, 0.f), bt = kt;
+        for (int q = 0; q < 8; ++q) {
+            const float4 a = sk[q][threadIdx.x], b = sb[q][threadIdx.x];
+            kt.x += a.x; kt.y += a.y; kt.z += a.z; kt.w += a.w;
+            bt.x += b.x; bt.y += b.y; bt.z += b.z; bt.w += b.w;
+        }
+        float4* kp = reinterpret_cast<float4*>(e.kbar + (size_t)bx * n + c);
+        float4* bp = reinterpret_cast<float4*>(e.bbar + (size_t)bx * n + c);
+        float4 k0 = *kp, b0 = *bp;
+        k0.x += kt.x; k0.y += kt.y; k0.z += kt.z; k0.w += kt.w;
+        b0.x += bt.x; b0.y += bt.y; b0.z += bt.z; b0.w += bt.w;
+        *kp = k0;
+        *bp = b0;
+    }
+}
+
 void launch_relax_adjoint(const EpiRelaxAdj& e, const float* Qbar, int M, int n, cudaStream_t s) {
     if (M == 0 || e.B == 0) return;
-    dim3 grid(e.B, ceil_div(n, 32));
-    relax_adjoint_kernel<<<grid, 256, 0, s>>>(e, Qbar, M, n);
+    if (n % 4 == 0) {
+        dim3 grid(e.B, ceil_div(n, 128));
+        relax_adjoint_v4_kernel<<<grid, 256, 0, s>>>(e, Qbar, M, n);
+    } else {
+        dim3 grid(e.B, ceil_div(n, 32));
+        relax_adjoint_kernel<<<grid, 256, 0, s>>>(e, Qbar, M, n);
+    }
     LB_LAUNCH();
 }
 
