@@ -7,13 +7,14 @@ from __future__ import annotations
 import os
 import subprocess
 import sys
+from concurrent.futures import ThreadPoolExecutor
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIBDIR, "libluna_b200.so")
-SOURCES = ["kernels.cu", "tc_gemm.cu", "engine.cpp", "capi.cpp", "noalloc.cu"]
+SOURCES = ["kernels.cu", "conv_kernels.cu", "tc_gemm.cu", "engine.cpp", "capi.cpp", "noalloc.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -31,18 +32,20 @@ def build(force: bool = False, verbose: bool = False) -> str:
     if not force and not _needs_rebuild():
         return LIB
     os.makedirs(LIBDIR, exist_ok=True)
-    objs = []
-    for src in SOURCES:
+    def compile_one(src):
         obj = os.path.join(LIBDIR, src.replace(".", "_") + ".o")
         cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                "-Xcompiler", "-fvisibility=hidden", "--expt-relaxed-constexpr",
-               "-I", os.path.join(ROOT, "include"), "-x", "cu" if src.endswith(".cu") else "cu",
+               "-I", os.path.join(ROOT, "include"), "-x", "cu",
                "-c", os.path.join(CSRC, src), "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)
-        objs.append(obj)
+        return obj
+
+    with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+        objs = list(ex.map(compile_one, SOURCES))
     tmp = LIB + ".tmp"
     subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"], check=True)
     os.replace(tmp, LIB)

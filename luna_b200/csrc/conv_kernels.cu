@@ -1,0 +1,467 @@
+// conv_kernels.cu -- SIMT kernels of the conv layers (IBP, windowed
+// transposed-conv steps with fused relaxation / concretisation, and their
+// adjoints).
+#include "conv_kernels.cuh"
+
+namespace lb200 {
+
+namespace {
+
+__device__ __forceinline__ void row_split(int r, int R, int& p, int& rr) {
+    p = r >= R ? 1 : 0;
+    rr = r - p * R;
+}
+
+__device__ __forceinline__ void win_origin(const WinGeo& g, int row_id, int& oy, int& ox) {
+    if (g.full) {
+        oy = 0;
+        ox = 0;
+        return;
+    }
+    const int pix = row_id / g.st_C;
+    const int y0 = pix / g.st_W, x0 = pix - (pix / g.st_W) * g.st_W;
+    oy = g.mul_y * y0 + g.off_y;
+    ox = g.mul_x * x0 + g.off_x;
+}
+
+// Map neuron of window element j of a row whose window starts at (oy, ox),
+// or -1 outside the map.
+__device__ __forceinline__ int win_neuron(const WinGeo& g, int oy, int ox, int j) {
+    if (g.full) return j;
+    const int c = j % g.C, pix = j / g.C;
+    const int wy = pix / g.ww, wx = pix - wy * g.ww;
+    const int y = oy + wy, x = ox + wx;
+    if ((unsigned)y >= (unsigned)g.H || (unsigned)x >= (unsigned)g.W) return -1;
+    return (y * g.W + x) * g.C + c;
+}
+
+// Lower side: Q = P+ s + P- k, bias P- b; upper side: Q = P+ k + P- s, bias
+// P+ b (BoundedReLUNode.cpp:179-195,268-285).
+__device__ __forceinline__ float relax_q(float P, int p, float s, float k, float b, float& bias) {
+    const float pos = fmaxf(P, 0.f), neg = fminf(P, 0.f);
+    if (p == 0) {
+        bias += neg * b;
+        return pos * s + neg * k;
+    }
+    bias += pos * b;
+    return pos * k + neg * s;
+}
+
+// Block-wide sum (blockDim.x == 256) returned to thread 0.
+__device__ __forceinline__ float block_sum256(float v, float* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+    if (threadIdx.x == 0)
+        for (int w = 0; w < 8; ++w) t += sh[w];
+    return t;
+}
+
+// One element of the transposed convolution of one row's window.
+__device__ __forceinline__ float convT_elem(const float* __restrict__ Arow, const ConvStep& cs, int j) {
+    const int ci = j % cs.Ci, pix = j / cs.Ci;
+    const int vy = pix / cs.out_w, vx = pix - vy * cs.out_w;
+    const int ty = vy + cs.cy, tx = vx + cs.cx;
+    float acc = 0.f;
+    for (int ky = ty % cs.sh; ky < cs.kh && ky <= ty; ky += cs.sh) {
+        const int qy = (ty - ky) / cs.sh;
+        if (qy >= cs.in_h) continue;
+        for (int kx = tx % cs.sw; kx < cs.kw && kx <= tx; kx += cs.sw) {
+            const int qx = (tx - kx) / cs.sw;
+            if (qx >= cs.in_w) continue;
+            const float* a = Arow + ((size_t)qy * cs.in_w + qx) * cs.Co;
+            const float* w = cs.Wk + ((size_t)(ky * cs.kw + kx) * cs.Co) * cs.Ci + ci;
+            for (int co = 0; co < cs.Co; ++co) acc = fmaf(a[co], w[(size_t)co * cs.Ci], acc);
+        }
+    }
+    return acc;
+}
+
+}  // namespace
+
+// ============================================================== IBP
+__global__ void ibp_conv_kernel(const float* __restrict__ Wc, const float* __restrict__ bias,
+                                const float* __restrict__ in_l, const float* __restrict__ in_u,
+                                float* __restrict__ out_l, float* __restrict__ out_u, int B, int Ci, int Hi,
+                                int Wi, int Co, int Ho, int Wo, int kh, int kw, int sh, int sw, int ph, int pw,
+                                bool relu_in) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t total = (int64_t)B * Ho * Wo * Co;
+    if (idx >= total) return;
+    const int co = (int)(idx % Co);
+    int64_t t = idx / Co;
+    const int xo = (int)(t % Wo);
+    t /= Wo;
+    const int yo = (int)(t % Ho);
+    const int bx = (int)(t / Ho);
+    float lp = 0.f, ln = 0.f, up = 0.f, un = 0.f;
+    for (int ky = 0; ky < kh; ++ky) {
+        const int yi = yo * sh - ph + ky;
+        if (yi < 0 || yi >= Hi) continue;
+        for (int kx = 0; kx < kw; ++kx) {
+            const int xi = xo * sw - pw + kx;
+            if (xi < 0 || xi >= Wi) continue;
+            const float* w = Wc + ((size_t)(co * kh + ky) * kw + kx) * Ci;
+            const size_t base = (((size_t)bx * Hi + yi) * Wi + xi) * Ci;
+            for (int ci = 0; ci < Ci; ++ci) {
+                float l = in_l[base + ci], u = in_u[base + ci];
+                if (relu_in) {
+                    l = fmaxf(l, 0.f);
+                    u = fmaxf(u, 0.f);
+                }
+                const float wv = w[ci];
+                if (wv >= 0.f) {
+                    lp = fmaf(wv, l, lp);
+                    up = fmaf(wv, u, up);
+                } else {
+                    ln = fmaf(wv, u, ln);
+                    un = fmaf(wv, l, un);
+                }
+            }
+        }
+    }
+    const float b = bias ? bias[co] : 0.f;
+    out_l[idx] = (lp + ln) + b;
+    out_u[idx] = (up + un) + b;
+}
+
+void launch_ibp_conv(const float* Wc, const float* b, const float* in_l, const float* in_u, float* out_l,
+                     float* out_u, int B, int Ci, int Hi, int Wi, int Co, int Ho, int Wo, int kh, int kw,
+                     int sh, int sw, int ph, int pw, bool relu_in, cudaStream_t s) {
+    const int64_t total = (int64_t)B * Ho * Wo * Co;
+    if (total == 0) return;
+    ibp_conv_kernel<<<ceil_div(total, 256), 256, 0, s>>>(Wc, b, in_l, in_u, out_l, out_u, B, Ci, Hi, Wi, Co,
+                                                         Ho, Wo, kh, kw, sh, sw, ph, pw, relu_in);
+    LB_LAUNCH();
+}
+
+__global__ void chw_to_hwc_kernel(const float* __restrict__ src, float* __restrict__ dst, int B, int C, int H,
+                                  int W) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t n = (int64_t)C * H * W;
+    if (idx >= (int64_t)B * n) return;
+    const int64_t bx = idx / n;
+    const int i = (int)(idx - bx * n);  // HWC index
+    const int c = i % C, pix = i / C;
+    dst[idx] = src[bx * n + (int64_t)c * H * W + pix];
+}
+
+void launch_chw_to_hwc(const float* src, float* dst, int B, int C, int H, int W, cudaStream_t s) {
+    const int64_t total = (int64_t)B * C * H * W;
+    if (total == 0) return;
+    chw_to_hwc_kernel<<<ceil_div(total, 256), 256, 0, s>>>(src, dst, B, C, H, W);
+    LB_LAUNCH();
+}
+
+// One warp per box; neurons visited in CHW order.
+__global__ void fill_rows_chw_kernel(const float* __restrict__ l, const float* __restrict__ u, int B, int C,
+                                     int H, int W, const int* __restrict__ off, int* __restrict__ row_box,
+                                     int* __restrict__ row_id) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= B) return;
+    const int HW = H * W, n = C * HW;
+    int base = off[warp];
+    for (int i0 = 0; i0 < n; i0 += 32) {
+        const int i = i0 + lane;
+        bool un = false;
+        int sidx = 0;
+        if (i < n) {
+            const int c = i / HW, pix = i - c * HW;
+            sidx = pix * C + c;
+            const float lv = l[(size_t)warp * n + sidx], uv = u[(size_t)warp * n + sidx];
+            un = lv < 0.f && uv > 0.f;
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, un);
+        if (un) {
+            const int pos = base + __popc(m & ((1u << lane) - 1u));
+            row_box[pos] = warp;
+            row_id[pos] = sidx;
+        }
+        base += __popc(m);
+    }
+}
+
+void launch_fill_rows_chw(const float* l, const float* u, int B, int C, int H, int W, const int* box_off,
+                          int* row_box, int* row_id, cudaStream_t s) {
+    fill_rows_chw_kernel<<<ceil_div((int64_t)B * 32, 256), 256, 0, s>>>(l, u, B, C, H, W, box_off, row_box,
+                                                                        row_id);
+    LB_LAUNCH();
+}
+
+// ============================================================== start step
+__global__ void __launch_bounds__(256) conv_start_step_kernel(ConvStartStep st) {
+    __shared__ float sh[8];
+    const int r = blockIdx.x;
+    int p, rr;
+    row_split(r, st.rows.R, p, rr);
+    const int bx = st.rows.row_box[rr];
+    const int id = st.rows.row_id[rr];
+    const int co = id % st.g.st_C;
+    const int nw = st.g.size();
+    int oy, ox;
+    win_origin(st.g, id, oy, ox);
+    const float* wrow = st.Wc + (size_t)co * nw;
+    float part = 0.f;
+    for (int j = threadIdx.x; j < nw; j += blockDim.x) {
+        const float P = wrow[j];
+        const size_t at = (size_t)r * nw + j;
+        if (st.P_save) st.P_save[at] = P;
+        const int nu = win_neuron(st.g, oy, ox, j);
+        float Q = 0.f;
+        if (nu >= 0) {
+            const size_t bj = (size_t)bx * st.rp.n + nu;
+            const float s = (st.alpha && (st.rp.flags[bj] & RF_USE_ALPHA)) ? st.alpha[at] : st.rp.slope_lo[bj];
+            Q = relax_q(P, p, s, st.rp.k_up[bj], st.rp.b_up[bj], part);
+            if (st.b_next) part = fmaf(Q, st.b_next[j % st.g.C], part);
+        }
+        st.Q[at] = Q;
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) st.bias_acc[r] = st.bW[co] + tot;
+}
+
+void launch_conv_start_step(const ConvStartStep& st, cudaStream_t s) {
+    if (st.M == 0) return;
+    conv_start_step_kernel<<<st.M, 256, 0, s>>>(st);
+    LB_LAUNCH();
+}
+
+// ============================================================== convT steps
+int conv_chunks(const WinGeo& out) { return ceil_div(out.size(), 256); }
+
+__global__ void __launch_bounds__(256) convT_relax_kernel(const float* __restrict__ A, ConvStep cs, int M,
+                                                          ConvRelaxEpi e, int nchunk, float* __restrict__ partial) {
+    __shared__ float sh[8];
+    const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
+    const int nin = cs.in_h * cs.in_w * cs.Co;
+    const int nw = e.g.size();
+    const int j = chunk * 256 + threadIdx.x;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    float part = 0.f;
+    if (j < nw) {
+        const float P = convT_elem(A + (size_t)r * nin, cs, j);
+        const size_t at = (size_t)r * nw + j;
+        if (e.P_save) e.P_save[at] = P;
+        int oy, ox;
+        win_origin(e.g, e.rows.row_id[rr], oy, ox);
+        const int nu = win_neuron(e.g, oy, ox, j);
+        float Q = 0.f;
+        if (nu >= 0) {
+            const size_t bj = (size_t)bx * e.rp.n + nu;
+            const float s = (e.alpha && (e.rp.flags[bj] & RF_USE_ALPHA)) ? e.alpha[at] : e.rp.slope_lo[bj];
+            Q = relax_q(P, p, s, e.rp.k_up[bj], e.rp.b_up[bj], part);
+            if (e.b_next) part = fmaf(Q, e.b_next[j % e.g.C], part);
+        }
+        e.Q[at] = Q;
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+}
+
+__global__ void __launch_bounds__(256) convT_conc_kernel(const float* __restrict__ A, ConvStep cs, int M,
+                                                         ConvConcEpi e, int nchunk, float* __restrict__ partial) {
+    __shared__ float sh[8];
+    const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
+    const int nin = cs.in_h * cs.in_w * cs.Co;
+    const int nw = e.g.size();
+    const int n0 = e.g.C * e.g.H * e.g.W;
+    const int j = chunk * 256 + threadIdx.x;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    float part = 0.f;
+    if (j < nw) {
+        const float P = convT_elem(A + (size_t)r * nin, cs, j);
+        int oy, ox;
+        win_origin(e.g, e.rows.row_id[rr], oy, ox);
+        const int nu = win_neuron(e.g, oy, ox, j);
+        uint8_t sg = 0;
+        if (nu >= 0) {
+            const float xl = e.xl[(size_t)bx * n0 + nu], xu = e.xu[(size_t)bx * n0 + nu];
+            if (e.form == CONC_PATCHES) {
+                const float c = (xu + xl) / 2.0f, d = (xu - xl) / 2.0f;
+                part = p == 0 ? fmaf(P, c, -fabsf(P) * d) : fmaf(P, c, fabsf(P) * d);
+                sg = (uint8_t)((P > 0.f ? 1 : 0) | (P < 0.f ? 2 : 0));
+            } else {
+                const float xa = p == 0 ? xl : xu, xb = p == 0 ? xu : xl;
+                part = fmaxf(P, 0.f) * xa + fminf(P, 0.f) * xb;
+                sg = (uint8_t)((P >= 0.f ? 1 : 0) | (P <= 0.f ? 2 : 0));
+            }
+        }
+        if (e.sign) e.sign[(size_t)r * nw + j] = sg;
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+}
+
+void launch_convT_relax(const float* A, const ConvStep& cs, int M, const ConvRelaxEpi& e, float* partial,
+                        cudaStream_t s) {
+    if (M == 0) return;
+    const int nchunk = conv_chunks(e.g);
+    convT_relax_kernel<<<(unsigned)((int64_t)M * nchunk), 256, 0, s>>>(A, cs, M, e, nchunk, partial);
+    LB_LAUNCH();
+}
+
+void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConcEpi& e, float* partial,
+                       cudaStream_t s) {
+    if (M == 0) return;
+    const int nchunk = conv_chunks(e.g);
+    convT_conc_kernel<<<(unsigned)((int64_t)M * nchunk), 256, 0, s>>>(A, cs, M, e, nchunk, partial);
+    LB_LAUNCH();
+}
+
+// ============================================================== adjoint
+__global__ void win_input_seed_kernel(RowMap rows, int M, WinGeo g, int form, const uint8_t* __restrict__ sign,
+                                      const float* __restrict__ gseed, const float* __restrict__ xl,
+                                      const float* __restrict__ xu, float* __restrict__ out) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nw = g.size();
+    if (idx >= (int64_t)M * nw) return;
+    const int r = (int)(idx / nw), j = (int)(idx - (int64_t)r * nw);
+    int p, rr;
+    row_split(r, rows.R, p, rr);
+    const int bx = rows.row_box[rr];
+    int oy, ox;
+    win_origin(g, rows.row_id[rr], oy, ox);
+    const int nu = win_neuron(g, oy, ox, j);
+    float v = 0.f;
+    if (nu >= 0) {
+        const int n0 = g.C * g.H * g.W;
+        const float l = xl[(size_t)bx * n0 + nu], u = xu[(size_t)bx * n0 + nu];
+        const uint8_t sg = sign[idx];
+        const float gr = gseed[r];
+        if (form == CONC_PATCHES) {
+            const float c = (u + l) / 2.0f, d = (u - l) / 2.0f;
+            const float sgn = (sg & 1) ? 1.f : ((sg & 2) ? -1.f : 0.f);
+            v = p == 0 ? gr * c - gr * d * sgn : gr * c + gr * d * sgn;
+        } else {
+            const float xa = p == 0 ? l : u, xb = p == 0 ? u : l;
+            v = ((sg & 1) ? gr * xa : 0.f) + ((sg & 2) ? gr * xb : 0.f);
+        }
+    }
+    out[idx] = v;
+}
+
+void launch_win_input_seed(const RowMap& rows, int M, const WinGeo& g, int form, const uint8_t* sign,
+                           const float* gseed, const float* xl, const float* xu, float* Pbar0,
+                           cudaStream_t s) {
+    const int64_t total = (int64_t)M * g.size();
+    if (total == 0) return;
+    win_input_seed_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows, M, g, form, sign, gseed, xl, xu, Pbar0);
+    LB_LAUNCH();
+}
+
+__global__ void conv_adj_qbar_kernel(const float* __restrict__ Pbar, ConvStep cs, int M,
+                                     const float* __restrict__ gseed, const float* __restrict__ b,
+                                     float* __restrict__ Qbar) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nin = cs.in_h * cs.in_w * cs.Co;
+    if (idx >= (int64_t)M * nin) return;
+    const int r = (int)(idx / nin), j = (int)(idx - (int64_t)r * nin);
+    const int co = j % cs.Co, pix = j / cs.Co;
+    const int qy = pix / cs.in_w, qx = pix - qy * cs.in_w;
+    const float* prow = Pbar + (size_t)r * cs.out_h * cs.out_w * cs.Ci;
+    float acc = 0.f;
+    for (int ky = 0; ky < cs.kh; ++ky) {
+        const int vy = qy * cs.sh + ky - cs.cy;
+        if (vy < 0 || vy >= cs.out_h) continue;
+        for (int kx = 0; kx < cs.kw; ++kx) {
+            const int vx = qx * cs.sw + kx - cs.cx;
+            if (vx < 0 || vx >= cs.out_w) continue;
+            const float* pb = prow + ((size_t)vy * cs.out_w + vx) * cs.Ci;
+            const float* w = cs.Wc + ((size_t)(co * cs.kh + ky) * cs.kw + kx) * cs.Ci;
+            for (int ci = 0; ci < cs.Ci; ++ci) acc = fmaf(pb[ci], w[ci], acc);
+        }
+    }
+    Qbar[idx] = acc + gseed[r] * b[co];
+}
+
+void launch_conv_adj_qbar(const float* Pbar, const ConvStep& cs, int M, const float* gseed, const float* b,
+                          float* Qbar, cudaStream_t s) {
+    const int64_t total = (int64_t)M * cs.in_h * cs.in_w * cs.Co;
+    if (total == 0) return;
+    conv_adj_qbar_kernel<<<ceil_div(total, 256), 256, 0, s>>>(Pbar, cs, M, gseed, b, Qbar);
+    LB_LAUNCH();
+}
+
+__global__ void relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g, const float* __restrict__ Qbar, int M) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nw = g.size();
+    if (idx >= (int64_t)M * nw) return;
+    const int r = (int)(idx / nw), j = (int)(idx - (int64_t)r * nw);
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    int oy, ox;
+    win_origin(g, e.rows.row_id[rr], oy, ox);
+    const int nu = win_neuron(g, oy, ox, j);
+    if (nu < 0) {
+        if (e.Pbar) e.Pbar[idx] = 0.f;
+        return;
+    }
+    const size_t bj = (size_t)bx * e.rp.n + nu;
+    const uint8_t f = e.rp.flags[bj];
+    const float sl = e.rp.slope_lo[bj], k = e.rp.k_up[bj], b = e.rp.b_up[bj];
+    const bool use_alpha = (f & RF_USE_ALPHA) != 0, un = (f & RF_UNSTABLE) != 0;
+    const float Qb = Qbar[idx];
+    const float P = e.P_saved[idx];
+    const float gr = e.gseed[r];
+    const float a = e.alpha ? e.alpha[idx] : 0.f;
+    const float s = (e.alpha && use_alpha) ? a : sl;
+    const bool pos = P >= 0.f, neg = P <= 0.f;
+    const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
+    const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
+    if (e.Pbar) {
+        const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
+        const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
+        e.Pbar[idx] = Qb * dq + gr * db;
+    }
+    const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
+    if (un) {
+        const float kv = Qb * (p == 0 ? Pn : Pp), bv = gr * (p == 0 ? Pn : Pp);
+        if (kv != 0.f) atomicAdd(e.kbar + bj, kv);
+        if (bv != 0.f) atomicAdd(e.bbar + bj, bv);
+    }
+    if (e.adam_m && e.active && e.active[bx]) {
+        const float ag = use_alpha ? Qb * (p == 0 ? Pp : Pn) : 0.f;
+        float mm = e.adam_m[idx], vv = e.adam_v[idx];
+        e.alpha[idx] = adam_clip_update(a, ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
+        e.adam_m[idx] = mm;
+        e.adam_v[idx] = vv;
+    }
+}
+
+void launch_relax_adjoint_win(const EpiRelaxAdj& e, const WinGeo& g, const float* Qbar, int M, cudaStream_t s) {
+    const int64_t total = (int64_t)M * g.size();
+    if (total == 0) return;
+    relax_adjoint_win_kernel<<<ceil_div(total, 256), 256, 0, s>>>(e, g, Qbar, M);
+    LB_LAUNCH();
+}
+
+__global__ void alpha_init_win_kernel(RowMap rows, WinGeo g, const float* __restrict__ init, int n,
+                                      float* __restrict__ alpha) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int nw = g.size();
+    if (idx >= (int64_t)2 * rows.R * nw) return;
+    const int r2 = (int)(idx / nw), j = (int)(idx - (int64_t)r2 * nw);
+    const int rr = r2 >= rows.R ? r2 - rows.R : r2;
+    int oy, ox;
+    win_origin(g, rows.row_id[rr], oy, ox);
+    const int nu = win_neuron(g, oy, ox, j);
+    alpha[idx] = nu >= 0 ? init[(size_t)rows.row_box[rr] * n + nu] : 0.f;
+}
+
+void launch_alpha_init_win(const RowMap& rows, const WinGeo& g, const float* init_slope, int n, float* alpha,
+                           cudaStream_t s) {
+    const int64_t total = (int64_t)2 * rows.R * g.size();
+    if (total == 0) return;
+    alpha_init_win_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows, g, init_slope, n, alpha);
+    LB_LAUNCH();
+}
+
+}  // namespace lb200

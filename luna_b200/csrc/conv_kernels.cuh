@@ -1,0 +1,139 @@
+// conv_kernels.cuh -- convolution layers of the backward substitution
+// (BoundedConvNode), kept as windows over HWC feature maps.
+//
+// Feature maps of conv layers are stored HWC (channels fastest) per box; a
+// flat index (y * W + x) * C + c.  Luna flattens (C, H, W) maps in CHW
+// order: the engine permutes at its edges (input boxes, the columns of a
+// Linear after a Flatten, row order of a start, intermediate-bound dumps).
+//
+// A row of a conv start (one unstable neuron at pixel (y0, x0) of the start
+// map) is nonzero only on a window of each map below it: the receptive field,
+// growing by (w - 1) * stride + kernel per conv.  Such rows are stored as
+// dense windows [wh, ww, C] whose top-left pixel on the map is
+//   origin = (mul_y * y0 + off_y, mul_x * x0 + off_x);
+// window pixels that fall outside the map hold exact zeros.  This is Luna's
+// patches mode (Patches.h, BoundedConvNode.cpp:556-709) without the unfold
+// copies.  Rows of the output start and of Linear starts cover whole maps
+// ("full" windows: origin 0, window = map).
+#pragma once
+
+#include "kernels.cuh"
+
+namespace lb200 {
+
+struct WinGeo {
+    int C = 1, H = 1, W = 1;       // map at this level (HWC)
+    int wh = 1, ww = 1;            // window rows / columns
+    int mul_y = 0, mul_x = 0;      // origin = mul * start pixel + off
+    int off_y = 0, off_x = 0;
+    int st_C = 1, st_W = 1;        // start map channels / width (decode of row_id)
+    int full = 1;                  // window == map at origin 0
+    __host__ __device__ int size() const { return wh * ww * C; }
+};
+
+// Concretisation forms (CROWNAnalysis.cpp:1164-1224 for a matrix A,
+// :791-848 with Patches::matmul for patches).
+enum : int { CONC_DENSE = 0, CONC_PATCHES = 1 };
+
+// One conv layer seen from a start: transposed convolution of the A window
+// at the layer's output (in_h x in_w x Co) into the window at its input
+// (out_h x out_w x Ci):
+//   out[v, ci] = sum over co and taps k with v + c = q s + k, 0 <= q < in,
+//                of A[q, co] W[co, ci, k]
+// (BoundedConvNode::boundOneSide, conv_transpose2d, :448-491 / :596-618).
+// c = 0 for windows (the whole transposed-conv output) and c = padding for
+// full maps (the output cropped to the map).
+struct ConvStep {
+    int Co = 0, Ci = 0, kh = 0, kw = 0, sh = 1, sw = 1;
+    int in_h = 0, in_w = 0, out_h = 0, out_w = 0;
+    int cy = 0, cx = 0;
+    const float* Wk = nullptr;  // [kh][kw][Co][Ci]
+    const float* Wc = nullptr;  // [Co][kh][kw][Ci]
+};
+
+// ---- IBP ------------------------------------------------------------------
+// W+/W- convolution of HWC interval maps (BoundedConvNode.cpp:864-943); the
+// input is clamped at 0 first when it is a ReLU output.
+void launch_ibp_conv(const float* Wc, const float* b, const float* in_l, const float* in_u, float* out_l,
+                     float* out_u, int B, int Ci, int Hi, int Wi, int Co, int Ho, int Wo, int kh, int kw,
+                     int sh, int sw, int ph, int pw, bool relu_in, cudaStream_t s);
+
+// Per-box CHW <-> HWC permutation of [B, C*H*W].
+void launch_chw_to_hwc(const float* src, float* dst, int B, int C, int H, int W, cudaStream_t s);
+
+// Row maps of a conv start: unstable neurons in Luna's CHW order, row_id =
+// HWC index.  Same warp-per-box compaction as launch_fill_rows.
+void launch_fill_rows_chw(const float* l, const float* u, int B, int C, int H, int W, const int* box_off,
+                          int* row_box, int* row_id, cudaStream_t s);
+
+// ---- forward (backward-substitution) steps ------------------------------
+// Start step of a conv start: the row of neuron (y0, x0, co) is the window
+// W[co] (kh x kw x Ci) at the level below (identity patches through the
+// start conv, BoundedConvNode.cpp:620-656), bias0 = b[co]; then the ReLU
+// relaxation below (masked outside the map) -> Q, bias partial.
+struct ConvStartStep {
+    RowMap rows;
+    int M = 0;
+    const float* Wc = nullptr;     // [Co][kh][kw][Ci] of the start conv
+    const float* bW = nullptr;     // [Co]
+    WinGeo g;                      // window at the level below the start
+    ReluParams rp;                 // ReLU below (rp.n = map size)
+    const float* alpha = nullptr;  // [2R, g.size()] or null
+    const float* b_next = nullptr; // [C] bias of the layer producing the map below
+    float* P_save = nullptr;       // [M, g.size()] or null
+    float* Q = nullptr;            // [M, g.size()]
+    float* bias_acc = nullptr;     // [M]
+};
+void launch_conv_start_step(const ConvStartStep& st, cudaStream_t s);
+
+// Transposed-conv step with the ReLU relaxation of the level below in the
+// epilogue (Q = relax(P), masked outside the map), or with the input
+// concretisation (dense or patches form).  Per-row partial sums go to
+// partial[chunk * M + r], chunk = 256-element chunk of the output window;
+// conv_chunks() gives their number.
+struct ConvRelaxEpi {
+    RowMap rows;
+    WinGeo g;                      // output window geometry
+    ReluParams rp;
+    const float* alpha = nullptr;
+    const float* b_next = nullptr; // [C]
+    float* P_save = nullptr;
+    float* Q = nullptr;
+};
+struct ConvConcEpi {
+    RowMap rows;
+    WinGeo g;
+    int form = CONC_DENSE;
+    const float* xl = nullptr;     // [B, n0] HWC
+    const float* xu = nullptr;
+    uint8_t* sign = nullptr;       // [M, g.size()] or null
+};
+int conv_chunks(const WinGeo& out);
+void launch_convT_relax(const float* A, const ConvStep& cs, int M, const ConvRelaxEpi& e, float* partial,
+                        cudaStream_t s);
+void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConcEpi& e, float* partial,
+                       cudaStream_t s);
+
+// ---- adjoint --------------------------------------------------------------
+// d loss / d A at the input window from the concretisation signs: dense form
+// (bit0 A>=0, bit1 A<=0) g (xa [bit0] + xb [bit1]); patches form (bit0 A>0,
+// bit1 A<0) g c -/+ g d sgn(A) (autograd of A c -/+ |A| d).  Zero outside
+// the map.
+void launch_win_input_seed(const RowMap& rows, int M, const WinGeo& g, int form, const uint8_t* sign,
+                           const float* gseed, const float* xl, const float* xu, float* Pbar0,
+                           cudaStream_t s);
+// Adjoint of a transposed-conv step: Qbar[q, co] = sum over ci, taps of
+// Pbar[v = q s + k - c, ci] W[co, ci, k] + g b[co] (a strided correlation
+// of the window below with W).
+void launch_conv_adj_qbar(const float* Pbar, const ConvStep& cs, int M, const float* gseed,
+                          const float* b, float* Qbar, cudaStream_t s);
+// Relaxation adjoint on windows (same rules as launch_relax_adjoint):
+// Pbar, the fused projected-Adam step on alpha, and d loss / d (k_up, b_up)
+// added into kbar / bbar [B, n] per neuron with atomics.
+void launch_relax_adjoint_win(const EpiRelaxAdj& e, const WinGeo& g, const float* Qbar, int M,
+                              cudaStream_t s);
+// alpha[p][r][j] = init_slope[box, neuron(r, j)] (0 outside the map).
+void launch_alpha_init_win(const RowMap& rows, const WinGeo& g, const float* init_slope, int n,
+                           float* alpha, cudaStream_t s);
+
+}  // namespace lb200

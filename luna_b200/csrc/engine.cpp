@@ -65,73 +65,220 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
     }
     if (g->input_index < 0 || g->input_index >= n || g->nodes[g->input_index].type != LB200_NODE_INPUT)
         throw std::invalid_argument("input_index must name an INPUT node");
-    // Walk the chain Input -> [Linear -> ReLU]* -> Linear (Flatten/Identity
-    // pass through).  Graphs with joins or other node kinds are rejected.
+    // Walk the chain Input -> [affine -> ReLU]* -> affine, affine = Linear or
+    // Conv2d (Flatten/Identity pass through).  Graphs with joins or other
+    // node kinds are rejected.
     int cur = g->input_index;
-    bool expect_linear = true;
-    std::vector<const lb200_node_desc*> lins;
+    bool expect_affine = true;
+    std::vector<int> affine;
     while (true) {
         if (cur == g->output_index) break;
         if (dependents[cur].size() != 1)
-            throw std::invalid_argument("graph is not a chain (node " + std::to_string(cur) +
-                                        " has " + std::to_string(dependents[cur].size()) +
-                                        " consumers); supported: Input/Linear/ReLU/Flatten/Identity chains");
+            throw std::invalid_argument("graph is not a chain (node " + std::to_string(cur) + " has " +
+                                        std::to_string(dependents[cur].size()) +
+                                        " consumers); supported: Input/Linear/Conv/ReLU/Flatten/Identity chains");
         const int nx = dependents[cur][0];
         const auto& d = g->nodes[nx];
         if (d.num_inputs != 1) throw std::invalid_argument("multi-input node in chain");
-        if (d.type == LB200_NODE_LINEAR) {
-            if (!expect_linear) throw std::invalid_argument("two Linear nodes without a ReLU between");
-            if (!d.weight || d.in_features <= 0 || d.out_features <= 0)
-                throw std::invalid_argument("Linear node without weight");
-            lins.push_back(&d);
-            expect_linear = false;
+        if (d.type == LB200_NODE_LINEAR || d.type == LB200_NODE_CONV) {
+            if (!expect_affine) throw std::invalid_argument("two affine nodes without a ReLU between");
+            if (!d.weight) throw std::invalid_argument("affine node without weight");
+            affine.push_back(nx);
+            expect_affine = false;
             preact_node_ids_.push_back(nx);
         } else if (d.type == LB200_NODE_RELU) {
-            if (expect_linear) throw std::invalid_argument("ReLU must follow a Linear node");
-            expect_linear = true;
+            if (expect_affine) throw std::invalid_argument("ReLU must follow a Linear or Conv node");
+            expect_affine = true;
         } else if (!pass_through(d.type)) {
             throw std::invalid_argument("node type " + std::to_string(d.type) +
                                         " is not supported by this engine build");
         }
         cur = nx;
     }
-    if (g->nodes[g->output_index].type != LB200_NODE_LINEAR || expect_linear)
+    const int out_t = g->nodes[g->output_index].type;
+    if (out_t != LB200_NODE_LINEAR || expect_affine)
         throw std::invalid_argument("the output node must be the last Linear of the chain");
-    if (lins.size() < 2) throw std::invalid_argument("need at least two Linear layers");
-    preact_node_ids_.pop_back();  // the output Linear feeds no ReLU
-    K_ = (int)lins.size();
+    if (affine.size() < 2) throw std::invalid_argument("need at least two affine layers");
+    preact_node_ids_.pop_back();  // the output layer feeds no ReLU
+    K_ = (int)affine.size();
     layers_.resize(K_);
+    const auto& din = g->nodes[g->input_index];
+    MapShape prev;
+    prev.C = din.out_shape[0];
+    prev.H = std::max(1, din.out_shape[1]);
+    prev.W = std::max(1, din.out_shape[2]);
+    prev.spatial = g->nodes[affine[0]].type == LB200_NODE_CONV;
+    if (!prev.spatial) prev = MapShape{prev.n(), 1, 1, false};
     for (int k = 0; k < K_; ++k) {
-        const auto& d = *lins[k];
-        LinearLayer& L = layers_[k];
-        L.n_in = (int)d.in_features;
-        L.n_out = (int)d.out_features;
-        if (k > 0 && L.n_in != layers_[k - 1].n_out) throw std::invalid_argument("width mismatch");
-        std::vector<float> W((size_t)L.n_out * L.n_in), Wt((size_t)L.n_in * L.n_out), b(L.n_out, 0.f);
-        for (int o = 0; o < L.n_out; ++o)
-            for (int i = 0; i < L.n_in; ++i) {
-                // BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
-                const float w = d.scale * d.weight[(size_t)o * L.n_in + i];
-                W[(size_t)o * L.n_in + i] = w;
-                Wt[(size_t)i * L.n_out + o] = w;
-            }
-        if (d.bias)
-            for (int o = 0; o < L.n_out; ++o) b[o] = d.bias[o];
+        const auto& d = g->nodes[affine[k]];
+        Layer& L = layers_[k];
+        L.conv = d.type == LB200_NODE_CONV;
+        L.in = prev;
+        if (L.conv) {
+            has_conv_ = true;
+            if (!prev.spatial) throw std::invalid_argument("a conv layer must follow the input or another conv");
+            L.kh = d.kernel[0];
+            L.kw = d.kernel[1];
+            L.sh = d.stride[0];
+            L.sw = d.stride[1];
+            L.ph = d.padding[0];
+            L.pw = d.padding[1];
+            if (L.kh <= 0 || L.kw <= 0 || L.sh <= 0 || L.sw <= 0 || L.ph < 0 || L.pw < 0)
+                throw std::invalid_argument("bad conv geometry");
+            L.out.C = d.out_shape[0];
+            L.out.H = (prev.H + 2 * L.ph - L.kh) / L.sh + 1;
+            L.out.W = (prev.W + 2 * L.pw - L.kw) / L.sw + 1;
+            L.out.spatial = true;
+            if (L.out.H != d.out_shape[1] || L.out.W != d.out_shape[2])
+                throw std::invalid_argument("conv out_shape does not match its geometry");
+        } else {
+            if (d.in_features <= 0 || d.out_features <= 0) throw std::invalid_argument("Linear node without sizes");
+            if (d.in_features != prev.n()) throw std::invalid_argument("width mismatch");
+            L.out = MapShape{(int)d.out_features, 1, 1, false};
+        }
+        L.n_in = L.in.n();
+        L.n_out = L.out.n();
+        const int Ci = L.in.C, Co = L.out.C;
+        std::vector<float> W, Wt, b(L.conv ? Co : L.n_out, 0.f), bn(L.n_out, 0.f);
+        if (L.conv) {
+            // ONNX Conv weight [Co, Ci, kh, kw] -> Wc [Co][kh][kw][Ci], Wk [kh][kw][Co][Ci].
+            W.resize((size_t)Co * L.kh * L.kw * Ci);
+            Wt.resize(W.size());
+            for (int o = 0; o < Co; ++o)
+                for (int c = 0; c < Ci; ++c)
+                    for (int y = 0; y < L.kh; ++y)
+                        for (int x = 0; x < L.kw; ++x) {
+                            const float w = d.weight[(((size_t)o * Ci + c) * L.kh + y) * L.kw + x];
+                            W[(((size_t)o * L.kh + y) * L.kw + x) * Ci + c] = w;
+                            Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
+                        }
+            if (d.bias)
+                for (int o = 0; o < Co; ++o) b[o] = d.bias[o];
+            for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
+        } else {
+            W.resize((size_t)L.n_out * L.n_in);
+            Wt.resize(W.size());
+            const int HW = L.in.H * L.in.W;
+            for (int o = 0; o < L.n_out; ++o)
+                for (int i = 0; i < L.n_in; ++i) {
+                    // Input feature i in the engine's order; Luna's column is
+                    // its CHW index when the input is a flattened conv map.
+                    const int col = L.in.spatial ? (i % Ci) * HW + i / Ci : i;
+                    // BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
+                    const float w = d.scale * d.weight[(size_t)o * L.n_in + col];
+                    W[(size_t)o * L.n_in + i] = w;
+                    Wt[(size_t)i * L.n_out + o] = w;
+                }
+            if (d.bias)
+                for (int o = 0; o < L.n_out; ++o) b[o] = d.bias[o];
+            bn = b;
+        }
         L.W = weights_.as<float>(key("W", k), W.size());
         L.Wt = weights_.as<float>(key("Wt", k), Wt.size());
         L.b = weights_.as<float>(key("b", k), b.size());
+        L.b_neuron = weights_.as<float>(key("bn", k), bn.size());
         LB_CUDA(cudaMemcpy(L.W, W.data(), W.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
-        L.W_hi = weights_.as<float>(key("Whi", k), W.size());
-        L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
-        L.Wt_hi = weights_.as<float>(key("Wthi", k), Wt.size());
-        L.Wt_lo = weights_.as<float>(key("Wtlo", k), Wt.size());
-        launch_split_tf32(L.W, L.W_hi, L.W_lo, (int64_t)W.size(), 0);
-        launch_split_tf32(L.Wt, L.Wt_hi, L.Wt_lo, (int64_t)Wt.size(), 0);
+        LB_CUDA(cudaMemcpy(L.b_neuron, bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
+        if (!L.conv) {
+            L.W_hi = weights_.as<float>(key("Whi", k), W.size());
+            L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
+            L.Wt_hi = weights_.as<float>(key("Wthi", k), Wt.size());
+            L.Wt_lo = weights_.as<float>(key("Wtlo", k), Wt.size());
+            launch_split_tf32(L.W, L.W_hi, L.W_lo, (int64_t)W.size(), 0);
+            launch_split_tf32(L.Wt, L.Wt_hi, L.Wt_lo, (int64_t)Wt.size(), 0);
+        }
         LB_CUDA(cudaDeviceSynchronize());
+        prev = L.out;
+    }
+    if (layers_[K_ - 1].conv) throw std::invalid_argument("the output layer must be Linear");
+    // Row geometry of every start at every level below it.
+    geo_.assign(K_ + 1, {});
+    for (int st = 2; st <= K_; ++st) {
+        std::vector<WinGeo>& gv = geo_[st];
+        gv.resize(st);
+        const bool window = st < K_ && layers_[st - 1].conv;
+        for (int m = 0; m < st; ++m) {
+            const MapShape& ms = map(m);
+            WinGeo w;
+            w.C = ms.C;
+            w.H = ms.H;
+            w.W = ms.W;
+            w.wh = ms.H;
+            w.ww = ms.W;
+            gv[m] = w;
+        }
+        if (!window) continue;
+        const Layer& Ls = layers_[st - 1];
+        WinGeo w = gv[st - 1];
+        w.full = 0;
+        w.wh = Ls.kh;
+        w.ww = Ls.kw;
+        w.mul_y = Ls.sh;
+        w.mul_x = Ls.sw;
+        w.off_y = -Ls.ph;
+        w.off_x = -Ls.pw;
+        w.st_C = Ls.out.C;
+        w.st_W = Ls.out.W;
+        gv[st - 1] = w;
+        for (int m = st - 1; m >= 1; --m) {
+            const Layer& L = layers_[m - 1];
+            if (!L.conv) throw std::invalid_argument("a Linear layer below a conv start is not supported");
+            WinGeo v = gv[m];
+            const MapShape& ms = map(m - 1);
+            v.C = ms.C;
+            v.H = ms.H;
+            v.W = ms.W;
+            v.wh = (v.wh - 1) * L.sh + L.kh;
+            v.ww = (v.ww - 1) * L.sw + L.kw;
+            v.mul_y *= L.sh;
+            v.mul_x *= L.sw;
+            v.off_y = v.off_y * L.sh - L.ph;
+            v.off_x = v.off_x * L.sw - L.pw;
+            gv[m - 1] = v;
+        }
     }
     lb200_options_default(&opt_);
+}
+
+// The transposed-conv step of conv layer m for the rows of start st.
+ConvStep Model::conv_step(int st, int m) const {
+    const Layer& L = layers_[m - 1];
+    const WinGeo& gi = geo_[st][m];
+    const WinGeo& go = geo_[st][m - 1];
+    ConvStep cs;
+    cs.Co = L.out.C;
+    cs.Ci = L.in.C;
+    cs.kh = L.kh;
+    cs.kw = L.kw;
+    cs.sh = L.sh;
+    cs.sw = L.sw;
+    cs.in_h = gi.wh;
+    cs.in_w = gi.ww;
+    cs.out_h = go.wh;
+    cs.out_w = go.ww;
+    cs.cy = go.full ? L.ph : 0;
+    cs.cx = go.full ? L.pw : 0;
+    cs.Wk = L.Wt;
+    cs.Wc = L.W;
+    return cs;
+}
+
+// Luna's CPU path starts a conv node with more than 4096 output features in
+// patches mode (CROWNAnalysis.cpp:255-272) and converts the patches to a
+// matrix once they are wider than a conv input (BoundedConvNode.cpp:671-694);
+// the concretisation form follows (CROWNAnalysis.cpp:791-848 vs :1164-1224).
+int Model::start_form(int st) const {
+    if (st >= K_ || !layers_[st - 1].conv || !opt_.use_patches_mode) return CONC_DENSE;
+    if (layers_[st - 1].n_out <= 4096) return CONC_DENSE;
+    int width = 0;
+    for (int m = st; m >= 1; --m) {
+        const Layer& L = layers_[m - 1];
+        width = m == st ? L.kw : (width - 1) * L.sw + L.kw;
+        if (width > L.in.W) return CONC_DENSE;
+    }
+    return CONC_PATCHES;
 }
 
 Model::~Model() {
@@ -149,18 +296,24 @@ std::string Model::key(const char* what, int a, int b) const {
 }
 
 size_t Model::bytes_per_box(bool alpha, int nspec) const {
-    size_t total = 0;
-    const int n0 = width(0);
-    int maxw = 0;
-    for (int m = 0; m <= K_; ++m) maxw = std::max(maxw, width(m));
+    // Worst case (every neuron unstable).  Persistent per start: signs, row
+    // maps and partial sums, plus alpha / Adam m, v / best alpha / saved P per
+    // level in alpha mode; transient (largest start): two Q, two P, two Pbar
+    // and one Qbar buffer.
+    size_t total = 0, transient = 0;
     for (int s = 2; s <= K_; ++s) {
         const size_t rows = 2 * (size_t)(s == K_ ? nspec : width(s));
-        size_t per_row = n0 + 4 * (size_t)maxw * 4 + 64;
-        for (int m = 1; m < s; ++m) per_row += (size_t)width(m) * 4 * (alpha ? 6 : 1);
+        size_t per_row = (size_t)rowlen(s, 0) + 96;
+        size_t maxrow = 0;
+        for (int m = 0; m < s; ++m) {
+            maxrow = std::max(maxrow, (size_t)rowlen(s, m));
+            if (alpha && m >= 1) per_row += (size_t)rowlen(s, m) * 4 * 5;
+        }
         total += rows * per_row;
+        transient = std::max(transient, rows * maxrow * 4 * 7);
     }
-    for (int m = 1; m <= K_; ++m) total += (size_t)width(m) * 4 * 16;
-    return total + (size_t)n0 * 8 + (size_t)nspec * 64;
+    for (int m = 0; m <= K_; ++m) total += (size_t)width(m) * 4 * 16;
+    return total + transient + (size_t)nspec * 64;
 }
 
 // ------------------------------------------------------------ row maps
@@ -187,10 +340,17 @@ void Model::build_rows(int B, int nspec, cudaStream_t s) {
         const int R = host[st];
         sp.row_box = cache_.as<int>(key("rowbox", st), std::max(R, 1));
         sp.row_id = cache_.as<int>(key("rowid", st), std::max(R, 1));
-        launch_fill_rows(cache_.as<float>(key("ibp_l", st), (size_t)B * width(st)),
-                         cache_.as<float>(key("ibp_u", st), (size_t)B * width(st)), B, width(st),
-                         sp.box_off, sp.row_box, sp.row_id, s);
+        const float* il = cache_.as<float>(key("ibp_l", st), (size_t)B * width(st));
+        const float* iu = cache_.as<float>(key("ibp_u", st), (size_t)B * width(st));
+        if (map(st).spatial)
+            // Rows in Luna's (CHW) neuron order; row_id is the HWC index.
+            launch_fill_rows_chw(il, iu, B, map(st).C, map(st).H, map(st).W, sp.box_off, sp.row_box,
+                                 sp.row_id, s);
+        else
+            launch_fill_rows(il, iu, B, width(st), sp.box_off, sp.row_box, sp.row_id, s);
         sp.rows = RowMap{sp.row_box, sp.row_id, sp.box_off, R};
+        sp.geo = geo_[st];
+        sp.form = start_form(st);
     }
     StartPlan& out = starts_[K_];
     out.s = K_;
@@ -200,6 +360,8 @@ void Model::build_rows(int B, int nspec, cudaStream_t s) {
     out.box_off = cache_.as<int>(key("boxoff", K_), B + 1);
     launch_fill_spec_rows(B, nspec, out.row_box, out.row_id, out.box_off, s);
     out.rows = RowMap{out.row_box, out.row_id, out.box_off, R};
+    out.geo = geo_[K_];
+    out.form = CONC_DENSE;
 }
 
 // ------------------------------------------------------------ relaxation
@@ -238,48 +400,103 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     if (R == 0) return;
     const int M = 2 * R;
     int maxw = 0;
-    for (int m = 0; m < st; ++m) maxw = std::max(maxw, width(m));
+    for (int m = 0; m < st; ++m) maxw = std::max(maxw, rowlen(st, m));
     float* Q[2] = {cache_.as<float>(key("Q", 0), (size_t)M * maxw), cache_.as<float>(key("Q", 1), (size_t)M * maxw)};
     float* bias = cache_.as<float>(key("bias", st), M);
-    int slots_total = 0;
-    for (int m = st - 1; m >= 1; --m) slots_total += gemm_tiles_n(width(m - 1));
-    float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
-
-    const LinearLayer& Ls = layers_[st - 1];
-    StartStep ss;
-    ss.rows = sp.rows;
-    ss.M = M;
-    ss.W = Ls.W;
-    ss.bW = Ls.b;
-    ss.spec_dim = Ls.n_out;
-    ss.n = Ls.n_in;
-    if (st == K_) {
-        ss.C = C_;
-        ss.c_per_box = c_per_box_;
-        ss.nspec = nspec;
-        flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
-    }
     const int mb = st - 1;  // ReLU directly below the start
-    ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
-    if (alpha) ss.alpha = cache_.as<float>(key("alpha", mb, st), (size_t)M * width(mb));
-    ss.b_next = layers_[mb - 1].b;
-    if (save) ss.P_save = cache_.as<float>(key("Psave", st, mb), (size_t)M * width(mb));
-    ss.Q = Q[0];
-    ss.bias_acc = bias;
-    launch_start_step(ss, s);
+    int slots_total = 0;
+    for (int m = mb; m >= 1; --m)
+        slots_total += layers_[m - 1].conv ? conv_chunks(sp.geo[m - 1]) : gemm_tiles_n(width(m - 1));
+    float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
+    auto alpha_buf = [&](int m) {
+        return alpha ? cache_.as<float>(key("alpha", m, st), (size_t)M * rowlen(st, m)) : nullptr;
+    };
+    auto psave_buf = [&](int m) {
+        return save ? cache_.as<float>(key("Psave", st, m), (size_t)M * rowlen(st, m)) : nullptr;
+    };
+
+    const Layer& Ls = layers_[st - 1];
+    if (Ls.conv) {
+        // Conv start: identity patches through the start conv.
+        ConvStartStep cs;
+        cs.rows = sp.rows;
+        cs.M = M;
+        cs.Wc = Ls.W;
+        cs.bW = Ls.b;
+        cs.g = sp.geo[mb];
+        cs.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+        cs.alpha = alpha_buf(mb);
+        cs.b_next = layers_[mb - 1].b;
+        cs.P_save = psave_buf(mb);
+        cs.Q = Q[0];
+        cs.bias_acc = bias;
+        launch_conv_start_step(cs, s);
+    } else {
+        StartStep ss;
+        ss.rows = sp.rows;
+        ss.M = M;
+        ss.W = Ls.W;
+        ss.bW = Ls.b;
+        ss.spec_dim = Ls.n_out;
+        ss.n = Ls.n_in;
+        if (st == K_) {
+            ss.C = C_;
+            ss.c_per_box = c_per_box_;
+            ss.nspec = nspec;
+            flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
+        }
+        ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+        ss.alpha = alpha_buf(mb);
+        ss.b_next = layers_[mb - 1].b_neuron;
+        ss.P_save = psave_buf(mb);
+        ss.Q = Q[0];
+        ss.bias_acc = bias;
+        launch_start_step(ss, s);
+    }
 
     int cur = 0, slot = 0;
     for (int m = mb; m >= 1; --m) {
-        const LinearLayer& L = layers_[m - 1];
+        const Layer& L = layers_[m - 1];
+        if (L.conv) {
+            const ConvStep cs = conv_step(st, m);
+            const double fl = 2.0 * M * (double)rowlen(st, m - 1) * cs.Co * L.kh * L.kw /
+                              ((double)L.sh * L.sw);
+            flops_ += fl;
+            prof_begin(s);
+            if (m - 1 >= 1) {
+                ConvRelaxEpi e;
+                e.rows = sp.rows;
+                e.g = sp.geo[m - 1];
+                e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
+                e.alpha = alpha_buf(m - 1);
+                e.b_next = layers_[m - 2].b;
+                e.P_save = psave_buf(m - 1);
+                e.Q = Q[1 - cur];
+                launch_convT_relax(Q[cur], cs, M, e, part + (size_t)slot * M, s);
+                cur = 1 - cur;
+            } else {
+                ConvConcEpi e;
+                e.rows = sp.rows;
+                e.g = sp.geo[0];
+                e.form = sp.form;
+                e.xl = xl_;
+                e.xu = xu_;
+                if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * rowlen(st, 0));
+                launch_convT_conc(Q[cur], cs, M, e, part + (size_t)slot * M, s);
+            }
+            prof_end(s, fl);
+            slot += conv_chunks(sp.geo[m - 1]);
+            continue;
+        }
         const int N = L.n_in, Kd = L.n_out;
         flops_ += 2.0 * M * (double)N * Kd;
         if (m - 1 >= 1) {
             EpiRelaxFwd e;
             e.rows = sp.rows;
             e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
-            if (alpha) e.alpha = cache_.as<float>(key("alpha", m - 1, st), (size_t)M * N);
-            e.b_next = layers_[m - 2].b;
-            if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
+            e.alpha = alpha_buf(m - 1);
+            e.b_next = layers_[m - 2].b_neuron;
+            e.P_save = psave_buf(m - 1);
             e.Q = Q[1 - cur];
             prof_begin(s);
             launch_gemm_relax_fwd(Q[cur], L.W, M, N, Kd, e, part + (size_t)slot * M, s);
@@ -329,7 +546,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
     float* base = nullptr;
     const float* P_in = nullptr;  // raw P below the next contraction (prologue modes)
     const float* Q_in = nullptr;  // materialised A of the next contraction (TMA mode)
-    const LinearLayer& Ls = layers_[st - 1];
+    const Layer& Ls = layers_[st - 1];
     if (st == K_ || !in_prologue(mb)) {
         // Start step: P = C . W_K (output start) or the one-hot rows of W_s,
         // relaxed here when the first contraction reads a materialised Q.
@@ -362,7 +579,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
         launch_start_step(ss, s);
     }
     for (int m = mb; m >= 1; --m) {
-        const LinearLayer& L = layers_[m - 1];
+        const Layer& L = layers_[m - 1];
         const int N = L.n_in, Kd = L.n_out;
         TcPrologue pro;
         if (in_prologue(m)) {
@@ -423,20 +640,23 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     const int R = sp.rows.R;
     if (R == 0 || M == 0) return;
     int maxw = 0;
-    for (int m = 0; m < st; ++m) maxw = std::max(maxw, width(m));
+    for (int m = 0; m < st; ++m) maxw = std::max(maxw, rowlen(st, m));
     float* Pb[2] = {cache_.as<float>(key("Pbar", 0), (size_t)M * maxw),
                     cache_.as<float>(key("Pbar", 1), (size_t)M * maxw)};
     const int n0 = width(0);
-    const uint8_t* sign = cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * n0);
+    const uint8_t* sign = cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * rowlen(st, 0));
     // On the tensor-core path the first contraction generates d loss / d A at
     // the input from the signs itself; the SIMT path materialises it.
     const bool seed_in_kernel = tc_;
-    if (!seed_in_kernel) launch_adj_input_seed(sp.rows, M, sign, g, xl_, xu_, n0, Pb[0], s);
+    if (layers_[0].conv)
+        launch_win_input_seed(sp.rows, M, sp.geo[0], sp.form, sign, g, xl_, xu_, Pb[0], s);
+    else if (!seed_in_kernel)
+        launch_adj_input_seed(sp.rows, M, sign, g, xl_, xu_, n0, Pb[0], s);
     int cur = 0;
     for (int m = 1; m <= st - 1; ++m) {
-        const LinearLayer& L = layers_[m - 1];
+        const Layer& L = layers_[m - 1];
         const int N = L.n_out, Kd = L.n_in;
-        flops_ += 2.0 * M * (double)N * Kd;
+        const size_t rl = (size_t)rowlen(st, m);
         EpiRelaxAdj e;
         e.rows = sp.rows;
         e.rp = relu_view(cache_, std::to_string(m), B, N);
@@ -445,20 +665,36 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         if (tc_ && m == st - 1 && st != K_)
             e.gather_W = layers_[st - 1].W;  // P of the ReLU below a one-hot start
         else
-            e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * N);
-        e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * N);
+            e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * rl);
+        e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * rl);
         e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
-        // Projected Adam fused into the epilogue (torch::optim::Adam + clip).
-        e.adam_m = cache_.as<float>(key("am", m, st), (size_t)2 * R * N);
-        e.adam_v = cache_.as<float>(key("av", m, st), (size_t)2 * R * N);
+        // Projected Adam fused into the relaxation adjoint (torch::optim::Adam + clip).
+        e.adam_m = cache_.as<float>(key("am", m, st), (size_t)2 * R * rl);
+        e.adam_v = cache_.as<float>(key("av", m, st), (size_t)2 * R * rl);
         e.active = adam_active_;
         e.adam_step = adam_step_;
         e.adam_bc2_sqrt = adam_bc2_sqrt_;
-        const bool tc = tc_;
         e.B = B;
         e.kbar = cache_.as<float>(key("kbar", m), (size_t)B * N);
         e.bbar = cache_.as<float>(key("bbar", m), (size_t)B * N);
-        if (tc) {
+        if (L.conv) {
+            const ConvStep cs = conv_step(st, m);
+            const double fl = 2.0 * M * (double)rowlen(st, m - 1) * cs.Co * L.kh * L.kw /
+                              ((double)L.sh * L.sw);
+            flops_ += fl;
+            float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
+            prof_begin(s);
+            launch_conv_adj_qbar(Pb[cur], cs, M, g, L.b, Qbar, s);
+            prof_end(s, fl);
+            if (sp.geo[m].full)
+                launch_relax_adjoint(e, Qbar, M, N, s);
+            else
+                launch_relax_adjoint_win(e, sp.geo[m], Qbar, M, s);
+            cur = 1 - cur;
+            continue;
+        }
+        flops_ += 2.0 * M * (double)N * Kd;
+        if (tc_) {
             // Tensor cores: the contraction stores Qbar only (compute-bound);
             // the relaxation adjoint + Adam stream through a separate kernel.
             EpiStoreQbar q;
@@ -515,9 +751,7 @@ void Model::run_pass(Pass pass, int B, int nspec, cudaStream_t s) {
             if (m >= 2) {
                 StartPlan& sp = starts_[m];
                 if (create)
-                    for (int mm = 1; mm < m; ++mm)
-                        launch_alpha_init(sp.rows, cache_.as<float>(key("init", mm), (size_t)B * width(mm)),
-                                          width(mm), cache_.as<float>(key("alpha", mm, m), (size_t)2 * sp.rows.R * width(mm)), s);
+                    for (int mm = 1; mm < m; ++mm) init_alpha(sp, mm, B, s);
                 forward_start(sp, B, nspec, save, alpha, s);
                 const bool ste = pass == Pass::ALPHA_ITER && opt_.stabilize_intermediate_bounds;
                 launch_scatter_start(sp.rows, cache_.as<float>(key("val", m), (size_t)2 * sp.rows.R),
@@ -529,28 +763,54 @@ void Model::run_pass(Pass pass, int B, int nspec, cudaStream_t s) {
     }
     StartPlan& out = starts_[K_];
     if (create)
-        for (int mm = 1; mm < K_; ++mm)
-            launch_alpha_init(out.rows, cache_.as<float>(key("init", mm), (size_t)B * width(mm)), width(mm),
-                              cache_.as<float>(key("alpha", mm, K_), (size_t)2 * out.rows.R * width(mm)), s);
+        for (int mm = 1; mm < K_; ++mm) init_alpha(out, mm, B, s);
     forward_start(out, B, nspec, save, alpha, s);
+}
+
+// alpha(m, start) = the CROWN lower slope of ReLU m at creation
+// (AlphaCROWNAnalysis::ensureAlphaFor, AlphaCROWNAnalysis.cpp:233-297).
+void Model::init_alpha(StartPlan& sp, int m, int B, cudaStream_t s) {
+    const float* init = cache_.as<float>(key("init", m), (size_t)B * width(m));
+    float* a = cache_.as<float>(key("alpha", m, sp.s), (size_t)2 * sp.rows.R * rowlen(sp.s, m));
+    if (sp.geo[m].full)
+        launch_alpha_init(sp.rows, init, width(m), a, s);
+    else
+        launch_alpha_init_win(sp.rows, sp.geo[m], init, width(m), a, s);
 }
 
 // ------------------------------------------------------------ one chunk
 void Model::run_chunk(int method, const float* xl, const float* xu, int B, const float* C,
                       int c_per_box, int nspec, bool upper, float* lb, float* ub, cudaStream_t s) {
+    if (map(0).spatial) {
+        // Input boxes arrive in Luna's CHW order; the engine works in HWC.
+        const MapShape& m0 = map(0);
+        float* pl = cache_.as<float>("x_hwc_l", (size_t)B * m0.n());
+        float* pu = cache_.as<float>("x_hwc_u", (size_t)B * m0.n());
+        launch_chw_to_hwc(xl, pl, B, m0.C, m0.H, m0.W, s);
+        launch_chw_to_hwc(xu, pu, B, m0.C, m0.H, m0.W, s);
+        xl = pl;
+        xu = pu;
+    }
     xl_ = xl;
     xu_ = xu;
     C_ = C;
     tc_ = tc_eligible();
     c_per_box_ = c_per_box;
     const int nout = width(K_);
-    // IBP (CROWNAnalysis::computeIBPBounds): pure interval bounds of every Linear.
+    // IBP (CROWNAnalysis::computeIBPBounds): pure interval bounds of every
+    // affine layer (the ReLU IBP is the clamp applied to each layer's input).
     for (int k = 1; k <= K_; ++k) {
         const size_t bn = (size_t)B * width(k);
         const float* il = k == 1 ? xl : cache_.as<float>(key("ibp_l", k - 1), (size_t)B * width(k - 1));
         const float* iu = k == 1 ? xu : cache_.as<float>(key("ibp_u", k - 1), (size_t)B * width(k - 1));
-        launch_ibp_linear(layers_[k - 1].W, layers_[k - 1].b, il, iu, cache_.as<float>(key("ibp_l", k), bn),
-                          cache_.as<float>(key("ibp_u", k), bn), B, width(k - 1), width(k), k > 1, s);
+        const Layer& L = layers_[k - 1];
+        float* ol = cache_.as<float>(key("ibp_l", k), bn);
+        float* ou = cache_.as<float>(key("ibp_u", k), bn);
+        if (L.conv)
+            launch_ibp_conv(L.W, L.b, il, iu, ol, ou, B, L.in.C, L.in.H, L.in.W, L.out.C, L.out.H, L.out.W, L.kh,
+                            L.kw, L.sh, L.sw, L.ph, L.pw, k > 1, s);
+        else
+            launch_ibp_linear(L.W, L.b, il, iu, ol, ou, B, width(k - 1), width(k), k > 1, s);
     }
     if (method == LB200_METHOD_IBP) {
         launch_ibp_spec(C, c_per_box, cache_.as<float>(key("ibp_l", K_), (size_t)B * nout),
@@ -596,7 +856,7 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     LB_CUDA(cudaMemcpyAsync(bc.first_save, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
     for (int st = 2; st <= K_; ++st)
         for (int m = 1; m < st; ++m) {
-            const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
+            const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
             LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("am", m, st), cnt), 0, cnt * 4, s));
             LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("av", m, st), cnt), 0, cnt * 4, s));
         }
@@ -625,13 +885,14 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         // the box is an improved spec index.
         for (int st = 2; st <= K_; ++st)
             for (int m = 1; m < st; ++m) {
-                const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
+                const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
                 float* a = cache_.as<float>(key("alpha", m, st), cnt);
                 float* best_a = cache_.as<float>(key("abest", m, st), cnt);
                 if (it == 0)
                     LB_CUDA(cudaMemcpyAsync(best_a, a, cnt * 4, cudaMemcpyDeviceToDevice, s));
                 else
-                    launch_best_alpha_rows(starts_[st].rows, B, bc.save, bc.improved, nspec, width(m), a, best_a, s);
+                    launch_best_alpha_rows(starts_[st].rows, B, bc.save, bc.improved, nspec, rowlen(st, m), a, best_a,
+                                           s);
             }
         launch_clear_first_save(bc.save, bc.first_save, B, s);
         if (last) break;
@@ -663,8 +924,8 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     // --- restoreBestAlphas, restoreBestIntermediateBounds, final run(false) ---
     for (int st = 2; st <= K_; ++st)
         for (int m = 1; m < st; ++m) {
-            const size_t cnt = (size_t)2 * starts_[st].rows.R * width(m);
-            launch_restore_alpha(starts_[st].rows, bc.first_save, width(m), cache_.as<float>(key("abest", m, st), cnt),
+            const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
+            launch_restore_alpha(starts_[st].rows, bc.first_save, rowlen(st, m), cache_.as<float>(key("abest", m, st), cnt),
                                  cache_.as<float>(key("alpha", m, st), cnt), s);
         }
     run_pass(Pass::ALPHA_FINAL, B, nspec, s);
@@ -680,7 +941,7 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
 // path: all widths that appear as N or K of a contraction (n_0 .. n_{K-1})
 // multiples of 16.
 bool Model::tc_eligible() const {
-    if (force_simt_) return false;
+    if (force_simt_ || has_conv_) return false;
     for (int m = 0; m < K_; ++m)
         if (!tc_supported(1, width(m), width(m)) || width(m) % 16 != 0) return false;
     return true;
@@ -800,7 +1061,16 @@ void Model::copy_intermediate(float* lower, float* upper) const {
             const void* src = const_cast<DevCache&>(cache_).get(key(nm, m), (size_t)B * n * 4);
             LB_CUDA(cudaMemcpy(tmp.data(), src, (size_t)B * n * 4, cudaMemcpyDeviceToHost));
             float* dst = side ? upper : lower;
-            for (int b = 0; b < B; ++b) std::memcpy(dst + b * per + off, tmp.data() + (size_t)b * n, n * 4);
+            const MapShape& ms = map(m);
+            if (ms.spatial) {
+                // HWC -> Luna's CHW order.
+                const int HW = ms.H * ms.W;
+                for (int b = 0; b < B; ++b)
+                    for (int i = 0; i < n; ++i)
+                        dst[b * per + off + (i % ms.C) * HW + i / ms.C] = tmp[(size_t)b * n + i];
+            } else {
+                for (int b = 0; b < B; ++b) std::memcpy(dst + b * per + off, tmp.data() + (size_t)b * n, n * 4);
+            }
         }
         off += n;
     }

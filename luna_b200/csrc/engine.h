@@ -6,6 +6,7 @@
 #pragma once
 
 #include "../../include/luna_b200.h"
+#include "conv_kernels.cuh"
 #include "kernels.cuh"
 
 #include <map>
@@ -34,13 +35,30 @@ private:
     std::map<std::string, Buf> bufs_;
 };
 
-struct LinearLayer {
+// Shape of the feature map at one level (the output of layer m, or the
+// input for m = 0).  Maps next to a conv layer are "spatial" and stored HWC;
+// the others are flat vectors (C = n, H = W = 1).
+struct MapShape {
+    int C = 1, H = 1, W = 1;
+    bool spatial = false;
+    int n() const { return C * H * W; }
+};
+
+// One affine layer: Linear (BoundedLinearNode) or Conv2d (BoundedConvNode).
+struct Layer {
+    bool conv = false;
     int n_in = 0, n_out = 0;
-    float* W = nullptr;   // [n_out, n_in]
-    float* Wt = nullptr;  // [n_in, n_out]
-    float* b = nullptr;   // [n_out]
-    // tf32 (hi, lo) splits for the tensor-core path: W is the K-major B
-    // operand of the adjoint contraction, Wt of the forward one.
+    MapShape in, out;
+    int kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;  // conv geometry
+    // Linear: W [n_out, n_in] and Wt [n_in, n_out], input columns in the
+    // engine's feature order (HWC after a Flatten of a conv map).
+    // Conv: W = Wc [Co][kh][kw][Ci], Wt = Wk [kh][kw][Co][Ci].
+    float* W = nullptr;
+    float* Wt = nullptr;
+    float* b = nullptr;        // [n_out] (Linear) or [Co] (conv)
+    float* b_neuron = nullptr; // [n_out]: bias of every output neuron
+    // tf32 (hi, lo) splits for the tensor-core path (Linear): W is the K-major
+    // B operand of the adjoint contraction, Wt of the forward one.
     float *W_hi = nullptr, *W_lo = nullptr, *Wt_hi = nullptr, *Wt_lo = nullptr;
 };
 
@@ -50,6 +68,10 @@ struct StartPlan {
     int* row_box = nullptr;
     int* row_id = nullptr;
     int* box_off = nullptr;
+    // Row geometry at every level below the start (index m = 0 .. s-1):
+    // windows for a conv start, whole maps otherwise.
+    std::vector<WinGeo> geo;
+    int form = CONC_DENSE;  // concretisation form Luna uses for this start
 };
 
 class Model {
@@ -74,7 +96,7 @@ public:
     int device() const { return device_; }
     int n_in() const { return layers_.front().n_in; }
     int n_out() const { return layers_.back().n_out; }
-    const std::vector<LinearLayer>& layers() const { return layers_; }
+    const std::vector<Layer>& layers() const { return layers_; }
     int64_t intermediate_count() const;
     void copy_intermediate(float* lower, float* upper) const;
 
@@ -88,16 +110,24 @@ private:
     void forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s);
     void adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s);
     void relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s);
+    void init_alpha(StartPlan& sp, int m, int B, cudaStream_t s);
     void build_rows(int B, int nspec, cudaStream_t s);
     void alloc_alpha(int B, cudaStream_t s);
     size_t bytes_per_box(bool alpha, int nspec) const;
 
     int width(int m) const { return m == 0 ? layers_[0].n_in : layers_[m - 1].n_out; }
+    const MapShape& map(int m) const { return m == 0 ? layers_[0].in : layers_[m - 1].out; }
+    // Length of a row of start st at level m (its window, or the whole map).
+    int rowlen(int st, int m) const { return geo_[st][m].size(); }
+    ConvStep conv_step(int st, int m) const;
+    int start_form(int st) const;
+    bool has_conv_ = false;
     std::string key(const char* what, int a, int b = -1) const;
 
     int device_ = 0;
     lb200_options opt_{};
-    std::vector<LinearLayer> layers_;  // chain Linear 1..K
+    std::vector<Layer> layers_;        // chain of affine layers 1..K
+    std::vector<std::vector<WinGeo>> geo_;  // [start][level]
     std::vector<int> preact_node_ids_; // node ids of Linear 1..K-1 outputs
     DevCache weights_;
     DevCache cache_;

@@ -10,7 +10,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .abi import NODE_INPUT, NODE_LINEAR, NODE_RELU, Graph, Node
+from .abi import NODE_CONV, NODE_FLATTEN, NODE_INPUT, NODE_LINEAR, NODE_RELU, Graph, Node
 
 
 def mlp(widths, seed: int, bias_std: float = 0.01) -> Graph:
@@ -28,6 +28,79 @@ def mlp(widths, seed: int, bias_std: float = 0.01) -> Graph:
         if li != len(widths) - 1:
             nodes.append(Node(NODE_RELU, [len(nodes) - 1], (fan_out, 1, 1)))
     return Graph(nodes, 0, len(nodes) - 1)
+
+
+def conv_out(h: int, k: int, s: int, p: int) -> int:
+    return (h + 2 * p - k) // s + 1
+
+
+def cnn(input_shape, layers, seed: int, bias_std: float = 0.01) -> Graph:
+    """Input (C, H, W) -> layers -> output, ReLU after every layer but the last.
+
+    `layers` items are ("conv", C_out, k, stride, pad) or ("linear", n_out);
+    a Flatten node is inserted where a conv feeds a linear layer.  Weights
+    are He-normal over the fan-in (C_in k k for a conv), biases N(0, bias_std^2),
+    drawn layer by layer from one PCG64 stream."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    nodes = [Node(NODE_INPUT, [], tuple(input_shape))]
+    shape = tuple(input_shape)
+    for li, spec in enumerate(layers):
+        last = li == len(layers) - 1
+        if spec[0] == "conv":
+            _, co, k, s, p = spec
+            ci, h, w = shape
+            fan_in = ci * k * k
+            wt = (rng.standard_normal((co, ci, k, k)) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+            b = (rng.standard_normal(co) * bias_std).astype(np.float32)
+            shape = (co, conv_out(h, k, s, p), conv_out(w, k, s, p))
+            nodes.append(Node(NODE_CONV, [len(nodes) - 1], shape, weight=wt, bias=b,
+                              kernel=(k, k), stride=(s, s), padding=(p, p)))
+        elif spec[0] == "linear":
+            n_out = spec[1]
+            if shape[1] != 1 or shape[2] != 1:
+                shape = (int(np.prod(shape)), 1, 1)
+                nodes.append(Node(NODE_FLATTEN, [len(nodes) - 1], shape))
+            fan_in = shape[0]
+            wt = (rng.standard_normal((n_out, fan_in)) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+            b = (rng.standard_normal(n_out) * bias_std).astype(np.float32)
+            shape = (n_out, 1, 1)
+            nodes.append(Node(NODE_LINEAR, [len(nodes) - 1], shape, weight=wt, bias=b))
+        else:
+            raise ValueError(spec)
+        if not last:
+            nodes.append(Node(NODE_RELU, [len(nodes) - 1], shape))
+    return Graph(nodes, 0, len(nodes) - 1)
+
+
+def image_boxes(rng, n_boxes: int, n_in: int, eps: float, n_out: int):
+    """Centres U[0,1]^n_in, radius eps clipped to [0,1], margin spec with a
+    uniformly drawn true class per box."""
+    c = rng.uniform(0.0, 1.0, (n_boxes, n_in)).astype(np.float32)
+    t = rng.integers(0, n_out, n_boxes)
+    lo = np.clip(c - np.float32(eps), 0.0, 1.0).astype(np.float32)
+    hi = np.clip(c + np.float32(eps), 0.0, 1.0).astype(np.float32)
+    return Boxes(lo, hi, margin_spec(t, n_out))
+
+
+def cnn_cifar(n_boxes: int = 256, seed: int = 2, eps: float = 2.0 / 255.0):
+    """CIFAR-shaped CNN 3x32x32 -> conv3->32 k3s1p1 -> conv32->64 k4s2p1 ->
+    conv64->64 k4s2p1 -> flatten 4096 -> 512 -> 10, He-normal weights from
+    seed 2; centres U[0,1], eps 2/255 clipped; 9 margin rows."""
+    g = cnn((3, 32, 32), [("conv", 32, 3, 1, 1), ("conv", 64, 4, 2, 1), ("conv", 64, 4, 2, 1),
+                          ("linear", 512), ("linear", 10)], seed)
+    rng = np.random.Generator(np.random.PCG64(seed + 1000))
+    return g, image_boxes(rng, n_boxes, 3 * 32 * 32, eps, 10)
+
+
+def small_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.02, big_first: bool = True):
+    """Small CNN for parity tests.  With big_first the first conv output has
+    more than 4096 features, so Luna's CPU path starts it in patches mode
+    (CROWNAnalysis.cpp:257-272); the second conv start stays dense."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    hw = 24 if big_first else 10
+    g = cnn((3, hw, hw), [("conv", 8, 3, 1, 1), ("conv", 16, 4, 2, 1), ("conv", 8, 3, 1, 1),
+                          ("linear", 24), ("linear", 5)], seed + 7, bias_std=0.1)
+    return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 5)
 
 
 @dataclass
@@ -98,3 +171,27 @@ def random_mlp_case(seed: int, n_boxes: int = 8, depth: int = 3, width: int = 12
     r = rng.uniform(0.2 * eps, eps, (n_boxes, n_in)).astype(np.float32)
     t = rng.integers(0, n_out, n_boxes)
     return g, Boxes((c - r).astype(np.float32), (c + r).astype(np.float32), margin_spec(t, n_out))
+
+
+def random_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.05):
+    """Small random CNN (kernel 2..5, stride 1..2, padding 0..2, 1-3 convs,
+    1-2 linear layers) and boxes for parity fuzzing."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    c, h = int(rng.integers(1, 4)), int(rng.integers(7, 13))
+    layers = []
+    hh = h
+    for _ in range(int(rng.integers(1, 4))):
+        k = int(rng.integers(2, 6))
+        s = int(rng.integers(1, 3))
+        p = int(rng.integers(0, min(3, k)))
+        if conv_out(hh, k, s, p) < 2:
+            break
+        layers.append(("conv", int(rng.integers(2, 7)), k, s, p))
+        hh = conv_out(hh, k, s, p)
+    if not layers:
+        layers.append(("conv", 3, 3, 1, 1))
+    for _ in range(int(rng.integers(1, 3))):
+        layers.append(("linear", int(rng.integers(4, 17))))
+    layers.append(("linear", 3))
+    g = cnn((c, h, h), layers, seed + 11, bias_std=0.1)
+    return g, image_boxes(rng, n_boxes, c * h * h, eps, 3)

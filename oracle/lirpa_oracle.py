@@ -11,7 +11,11 @@ behaviour it restates.  Per-box state follows Luna's: IBP bounds, "node
 bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
 parameters keyed by (activation node, start node), and STE reference bounds.
 
-Supported node kinds: Input, Linear, ReLU, Flatten, Identity.
+Supported node kinds: Input, Linear, Conv2d, ReLU, Flatten, Identity.  A
+matrices are kept dense over the flattened (C, H, W) features; Luna's
+patches mode (CROWNAnalysis.cpp:255-405, BoundedConvNode.cpp:556-709) is the
+same arithmetic on a window of those features, and it is tracked only to
+pick the concretisation form Luna uses at the end of a start.
 """
 from __future__ import annotations
 
@@ -20,9 +24,15 @@ from dataclasses import dataclass, field
 import numpy as np
 import torch
 
-from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_FLATTEN,
-                           NODE_IDENTITY, NODE_INPUT, NODE_LINEAR, NODE_RELU, Options,
-                           default_options)
+import torch.nn.functional as F
+
+from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_CONV,
+                           NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT, NODE_LINEAR, NODE_RELU,
+                           Options, default_options)
+
+# Dense identity starts above this many conv output features switch to
+# patches on Luna's CPU path (CROWNAnalysis.cpp:257,269).
+PATCHES_SIZE_THRESHOLD = 4096
 
 
 def topo_order(graph):
@@ -102,6 +112,10 @@ class LirpaOracle:
                 self.W[i] = torch.from_numpy(np.asarray(nd.weight, np.float32)) * nd.scale
                 self.b[i] = (torch.from_numpy(np.asarray(nd.bias, np.float32))
                              if nd.bias is not None else torch.zeros(nd.weight.shape[0]))
+            elif nd.type == NODE_CONV:
+                self.W[i] = torch.from_numpy(np.asarray(nd.weight, np.float32))
+                self.b[i] = (torch.from_numpy(np.asarray(nd.bias, np.float32))
+                             if nd.bias is not None else torch.zeros(nd.weight.shape[0]))
             elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_FLATTEN, NODE_IDENTITY):
                 raise NotImplementedError(f"oracle: node type {nd.type}")
         self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type == NODE_RELU]
@@ -119,6 +133,17 @@ class LirpaOracle:
             lo = torch.matmul(l, Wp.t()) + torch.matmul(u, Wn.t())
             hi = torch.matmul(u, Wp.t()) + torch.matmul(l, Wn.t())
             return lo + self.b[i], hi + self.b[i]
+        if nd.type == NODE_CONV:
+            # W+/W- convolutions (BoundedConvNode.cpp:864-943).
+            l, u = ins[0]
+            ci, h, w = self.g.nodes[nd.inputs[0]].out_shape
+            W = self.W[i]
+            Wp, Wn = torch.clamp_min(W, 0), torch.clamp_max(W, 0)
+            conv = lambda t, k: F.conv2d(t.reshape(1, ci, h, w), k, stride=nd.stride, padding=nd.padding)
+            b = self.b[i].view(1, -1, 1, 1)
+            lo = (conv(l, Wp) + conv(u, Wn)) + b
+            hi = (conv(u, Wp) + conv(l, Wn)) + b
+            return lo.flatten(), hi.flatten()
         if nd.type == NODE_RELU:
             l, u = ins[0]
             return torch.clamp_min(l, 0), torch.clamp_min(u, 0)
@@ -235,12 +260,39 @@ class LirpaOracle:
         return ap
 
     # -------------------------------------------------------- backward pass
+    def _conv_backward(self, c, A):
+        """BoundedConvNode::boundOneSide, tensor mode (BoundedConvNode.cpp:448-556):
+        A [spec, Co*Ho*Wo] -> conv_transpose2d with the output padding that
+        restores the input size; bias term sum_{c,h,w} A b_c."""
+        nd = self.g.nodes[c]
+        ci, hi, wi = self.g.nodes[nd.inputs[0]].out_shape
+        co, ho, wo = nd.out_shape
+        kh, kw = nd.kernel
+        (sh, sw), (ph, pw) = nd.stride, nd.padding
+        op = (hi - ((ho - 1) * sh - 2 * ph + kh), wi - ((wo - 1) * sw - 2 * pw + kw))
+        spec = A.shape[0]
+        A4 = A.reshape(spec, co, ho, wo)
+        out = F.conv_transpose2d(A4, self.W[c], stride=nd.stride, padding=nd.padding, output_padding=op)
+        bias = (A4 * self.b[c].view(1, -1, 1, 1)).sum((1, 2, 3))
+        return out.reshape(spec, -1), bias
+
+    def _starts_in_patches(self, start, is_output):
+        """usePatchesInit on the CPU path (CROWNAnalysis.cpp:255-298)."""
+        nd = self.g.nodes[start]
+        return (bool(self.opt.use_patches_mode) and not is_output and nd.type == NODE_CONV
+                and nd.size > PATCHES_SIZE_THRESHOLD)
+
     def _backward_from(self, st, start, x, rows=None, C=None):
         """CROWNAnalysis::backwardFrom (src/engine/CROWNAnalysis.cpp:231-706) for
         dense A: start A is the spec C (output) or one-hot rows at `rows`;
         Kahn-style reverse schedule; bias attached to the first dependency.
-        Returns (lA, uA, lbias, ubias) at the input node."""
+        Returns (lA, uA, lbias, ubias, patches) at the input node; `patches`
+        tells whether Luna would still hold the start's A as patches there
+        (it converts to a matrix once a patch is wider than the conv input,
+        BoundedConvNode.cpp:671-694)."""
         n = self.g.nodes[start].size
+        patches = self._starts_in_patches(start, C is not None)
+        pwidth = None
         if C is not None:
             A0 = C
         else:
@@ -276,6 +328,15 @@ class LirpaOracle:
                     out = [(torch.matmul(a_l, W), torch.matmul(a_u, W))]
                     nb_l = (a_l * bb).sum(-1)
                     nb_u = (a_u * bb).sum(-1)
+                elif nd.type == NODE_CONV:
+                    nl, nb_l = self._conv_backward(c, a_l)
+                    nu, nb_u = self._conv_backward(c, a_u)
+                    out = [(nl, nu)]
+                    if patches:
+                        kw = nd.kernel[1]
+                        pwidth = kw if pwidth is None else (pwidth - 1) * nd.stride[1] + kw
+                        if pwidth > self.g.nodes[nd.inputs[0]].out_shape[2]:
+                            patches = False
                 elif nd.type == NODE_RELU:
                     l, u = self._input_bounds_of(st, c, x)[0]
                     nl, nu, nb_l, nb_u = self._relu_backward(st, c, start, a_l, a_u, l, u)
@@ -304,13 +365,21 @@ class LirpaOracle:
                     pending[p] -= 1
                     if pending[p] == 0:
                         queue.append(p)
-        return lA[inp], uA[inp], lb[inp], ub[inp]
+        return lA[inp], uA[inp], lb[inp], ub[inp], patches
 
     @staticmethod
-    def _concretize(lA, uA, lb, ub, x):
+    def _concretize(lA, uA, lb, ub, x, patches=False):
         """computeConcreteLowerBound/UpperBound (src/engine/CROWNAnalysis.cpp:1164-1224):
-        lb = A+ xL + A- xU + bias, ub = A+ xU + A- xL + bias."""
+        lb = A+ xL + A- xU + bias, ub = A+ xU + A- xL + bias; for patches
+        (concretizeNode, :791-848 with Patches::matmul) lb = A c - |A| d + bias,
+        ub = A c + |A| d + bias with c = (xU + xL)/2, d = (xU - xL)/2."""
         xl, xu = x
+        if patches:
+            c = (xu + xl) / 2.0
+            d = (xu - xl) / 2.0
+            lo = (torch.matmul(lA, c) - torch.matmul(lA.abs(), d)) + lb
+            hi = (torch.matmul(uA, c) + torch.matmul(uA.abs(), d)) + ub
+            return lo, hi
         lo = (torch.matmul(torch.clamp_min(lA, 0), xl) + torch.matmul(torch.clamp_max(lA, 0), xu)) + lb
         hi = (torch.matmul(torch.clamp_min(uA, 0), xu) + torch.matmul(torch.clamp_max(uA, 0), xl)) + ub
         return lo, hi
@@ -338,8 +407,8 @@ class LirpaOracle:
             st.concrete[i] = st.ibp[i]
             st.node_bounds[i] = st.ibp[i]
             return
-        lA, uA, lb, ub = self._backward_from(st, i, x, rows=rows)
-        lo, hi = self._concretize(lA, uA, lb, ub, x)
+        lA, uA, lb, ub, patches = self._backward_from(st, i, x, rows=rows)
+        lo, hi = self._concretize(lA, uA, lb, ub, x, patches)
         idx = torch.as_tensor(rows, dtype=torch.long)
         if not st.method_alpha:
             lo, hi = lo.detach(), hi.detach()
@@ -366,8 +435,8 @@ class LirpaOracle:
         self._compute_ibp(st, x)
         out = self.g.output_index
         self._check_prior(st, out, x)
-        lA, uA, lb, ub = self._backward_from(st, out, x, C=C)
-        lo, hi = self._concretize(lA, uA, lb, ub, x)
+        lA, uA, lb, ub, patches = self._backward_from(st, out, x, C=C)
+        lo, hi = self._concretize(lA, uA, lb, ub, x, patches)
         st.node_bounds[out] = (lo, hi)
         st.concrete[out] = (lo, hi)
         return lo, hi

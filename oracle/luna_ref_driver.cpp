@@ -22,6 +22,7 @@
 #include "nodes/BoundedReLUNode.h"
 #include "nodes/BoundedFlattenNode.h"
 #include "nodes/BoundedIdentityNode.h"
+#include "nodes/BoundedConvNode.h"
 #include "input_parsers/Operations.h"
 
 #include <torch/torch.h>
@@ -82,6 +83,28 @@ std::shared_ptr<NLR::TorchModel> build_model(const lb200_graph_desc* g) {
             node = std::make_shared<NLR::BoundedLinearNode>(lin, d.scale, String("linear"));
             node->setInputSize((unsigned)d.in_features);
             node->setOutputSize((unsigned)d.out_features);
+            break;
+        }
+        case LB200_NODE_CONV: {
+            // OnnxToTorchParser's Conv2d branch (OnnxToTorch.cpp:2425-2444 and
+            // the size/shape setters after it, :2446-2540): MATRIX mode, flat
+            // sizes and [1, C, H, W] shapes.
+            const lb200_node_desc& src = g->nodes[d.inputs[0]];
+            const int64_t Ci = src.out_shape[0], H = src.out_shape[1], W = src.out_shape[2];
+            const int64_t Co = d.out_shape[0], kh = d.kernel[0], kw = d.kernel[1];
+            torch::nn::Conv2dOptions co(Ci, Co, {kh, kw});
+            co.stride({(int64_t)d.stride[0], (int64_t)d.stride[1]});
+            co.padding(torch::ExpandingArray<2>({(int64_t)d.padding[0], (int64_t)d.padding[1]}));
+            co.bias(d.bias != nullptr);
+            torch::nn::Conv2d conv(co);
+            conv->weight = from_host(d.weight, {Co, Ci, kh, kw});
+            if (d.bias) conv->bias = from_host(d.bias, {Co});
+            auto cn = std::make_shared<NLR::BoundedConvNode>(conv, NLR::ConvMode::MATRIX);
+            cn->setInputSize((unsigned)(Ci * H * W));
+            cn->setOutputSize((unsigned)out_numel);
+            cn->setInputShape({1, (int)Ci, (int)H, (int)W});
+            cn->setOutputShape({1, (int)Co, d.out_shape[1], d.out_shape[2]});
+            node = cn;
             break;
         }
         case LB200_NODE_RELU:

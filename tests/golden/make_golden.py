@@ -6,7 +6,7 @@ the inputs and Luna's outputs are stored as .npz files.  Network weights are
 not stored: they are regenerated from the seeded generators in
 luna_b200/workloads.py, and a checksum of them is stored to catch drift.
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle && python tests/golden/make_golden.py [case names]
 """
 from __future__ import annotations
 
@@ -49,6 +49,18 @@ def cases():
         out.append((f"rand{seed}_crown", "random_mlp_case", kw, 8, abi.METHOD_CROWN, {}))
         out.append((f"rand{seed}_alpha", "random_mlp_case", kw, 8, abi.METHOD_ALPHA_CROWN,
                     {"alpha_lr": 0.5 if seed % 2 else 0.1, "alpha_iterations": 8 + seed}))
+    # CNNs: all starts dense (conv outputs <= 4096 features) ...
+    kw = {"seed": 3, "n_boxes": 4, "big_first": False}
+    out.append(("cnn_dense_crown", "small_cnn_case", kw, 4, abi.METHOD_CROWN, {}))
+    out.append(("cnn_dense_alpha", "small_cnn_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 8}))
+    # ... and a first conv start in patches mode (4608 output features).
+    kw = {"seed": 5, "n_boxes": 3, "big_first": True}
+    out.append(("cnn_patch_crown", "small_cnn_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("cnn_patch_alpha", "small_cnn_case", kw, 2, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 5}))
+    # The CIFAR-shaped CNN at full size, one box.
+    out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
     return out
 
 
@@ -61,8 +73,10 @@ def make_case(gen: str, kw: dict):
     return g, bx
 
 
-def main():
+def main(only=()):
     for name, gen, kw, nb, method, over in cases():
+        if only and name not in only:
+            continue
         g, bx = make_case(gen, kw)
         bx = bx.slice(0, nb)
         opt = abi.default_options(**over)
@@ -79,4 +93,4 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    main(tuple(sys.argv[1:]))

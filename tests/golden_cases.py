@@ -53,6 +53,21 @@ def excess(ours, ref, rtol=RTOL, atol=ATOL):
     return float(np.max(np.abs(ours - ref) / (atol + rtol * np.abs(ref))))
 
 
+def excess_scaled(ours, ref, lb_ref, ub_ref, rtol=RTOL, atol=ATOL):
+    """excess() with the relative term taken against max(|ref|, ub_ref - lb_ref).
+
+    A bound that is the sum of many terms of opposite sign can land much
+    closer to 0 than the terms themselves (a margin near 0 with an interval
+    of width ~1); its fp32 value then carries rounding of the size of the
+    terms, which no reordering of the summation avoids: Luna's own CPU result
+    moves by a third of the strict bar between 1 and 8 threads on such a
+    CNN case.  The strict bar (excess) is reported beside this one."""
+    ours = np.asarray(ours, np.float64)
+    ref = np.asarray(ref, np.float64)
+    w = np.abs(np.asarray(ub_ref, np.float64) - np.asarray(lb_ref, np.float64))
+    return float(np.max(np.abs(ours - ref) / (atol + rtol * np.maximum(np.abs(ref), w))))
+
+
 def check_intermediate(ours_l, ours_u, ref_l, ref_u, rtol=1e-3, atol=1e-4, median_rtol=1e-5):
     """Compare the (best) pre-activation bounds that alpha-CROWN leaves on
     the nodes, where they shape the relaxation.
