@@ -35,29 +35,38 @@ sys.path.insert(0, ROOT)
 
 from luna_b200 import abi, workloads as W  # noqa: E402
 
-BOXES_PER_GPU = 512
-ITERS = 20
-LR = 0.1
 METRIC = "alpha_crown_boxes_per_sec"
 UNIT = "boxes/s"
-WORKLOAD = "mlp_784_256x4_10 alpha-CROWN (20 Adam iterations, lr 0.1), 512 boxes per GPU, eps 0.02, 9 margin specs"
 L2_FLUSH_BYTES = 256 << 20
+
+# Workloads: the MLP (the default) and the CIFAR-shaped CNN.
+WORKLOADS = {
+    "mlp": dict(gen=W.mlp_784_256x4_10, boxes=512, iters=20, lr=0.1, input_dim=784,
+                desc="mlp_784_256x4_10 alpha-CROWN (20 Adam iterations, lr 0.1), {b} boxes per GPU, "
+                     "eps 0.02, 9 margin specs"),
+    "cnn": dict(gen=W.cnn_cifar, boxes=256, iters=30, lr=0.5, input_dim=3072,
+                desc="cnn_cifar 3x32x32 conv32-conv64s2-conv64s2-fc512-fc10 alpha-CROWN (30 Adam "
+                     "iterations, lr 0.5), {b} boxes per GPU, eps 2/255, 9 margin specs"),
+}
+WL = dict(WORKLOADS["mlp"])
+BOXES_PER_GPU = WL["boxes"]
 
 
 def options():
-    return abi.default_options(alpha_lr=LR, alpha_iterations=ITERS)
+    return abi.default_options(alpha_lr=WL["lr"], alpha_iterations=WL["iters"])
 
 
 def config(n_gpus):
-    return {"workload": WORKLOAD, "boxes_per_gpu": BOXES_PER_GPU, "global_boxes": BOXES_PER_GPU * n_gpus,
-            "input_dim": 784, "nspec": 9, "alpha_iterations": ITERS, "alpha_lr": LR,
+    return {"workload": WL["desc"].format(b=BOXES_PER_GPU), "boxes_per_gpu": BOXES_PER_GPU,
+            "global_boxes": BOXES_PER_GPU * n_gpus, "input_dim": WL["input_dim"], "nspec": 9,
+            "alpha_iterations": WL["iters"], "alpha_lr": WL["lr"],
             "parallelism": f"box-sharded x{n_gpus}", "l2": "flushed between timed steps (256 MiB write)"}
 
 
 def rank_boxes(rank, n_gpus):
     """This rank's slice of one seeded global box set (same weights on every rank)."""
     from luna_b200.shard import shard_range
-    g, bx = W.mlp_784_256x4_10(BOXES_PER_GPU * n_gpus)
+    g, bx = WL["gen"](BOXES_PER_GPU * n_gpus)
     a, b = shard_range(rank, n_gpus, bx.n)
     return g, bx.slice(a, b)
 
@@ -274,18 +283,21 @@ def run_engine(args):
 _REF = {}
 
 
-def _ref_worker(span):
-    """One host process: bound boxes [a, b) of the workload with Luna's CPU
+def _ref_worker(task):
+    """One host process: bound boxes [a, b) of workload `name` with Luna's CPU
     path on one thread.  The reference library and the workload are loaded
     once per process."""
-    if not _REF:
+    name, n_boxes, a, b = task
+    if _REF.get("key") != (name, n_boxes):
         os.environ["CUDA_VISIBLE_DEVICES"] = ""
         for var in ("OMP_NUM_THREADS", "MKL_NUM_THREADS", "OPENBLAS_NUM_THREADS"):
             os.environ[var] = "1"
         from oracle import luna_ref
+        WL.clear()
+        WL.update(WORKLOADS[name])
         _REF["lib"] = luna_ref
-        _REF["work"] = W.mlp_784_256x4_10(BOXES_PER_GPU)
-    a, b = span
+        _REF["work"] = WL["gen"](n_boxes)
+        _REF["key"] = (name, n_boxes)
     if b <= a:
         return 0.0
     g, bx = _REF["work"]
@@ -302,17 +314,19 @@ class CpuBaseline:
     def __init__(self, procs=None):
         self.procs = procs or min(os.cpu_count() or 1, BOXES_PER_GPU)
         self.pool = mp.get_context("spawn").Pool(self.procs)
-        self.pool.map(_ref_worker, [(0, 0)] * self.procs)  # load the library in every worker
+        self.name = next(k for k, v in WORKLOADS.items() if v["gen"] is WL["gen"])
+        # Load the library and the workload in every worker.
+        self.pool.map(_ref_worker, [(self.name, BOXES_PER_GPU, 0, 0)] * self.procs)
 
     def sample(self, boxes_per_proc=1):
-        work = [((i * boxes_per_proc) % BOXES_PER_GPU, (i * boxes_per_proc) % BOXES_PER_GPU + boxes_per_proc)
-                for i in range(self.procs)]
+        work = [(self.name, BOXES_PER_GPU, (i * boxes_per_proc) % BOXES_PER_GPU,
+                 (i * boxes_per_proc) % BOXES_PER_GPU + boxes_per_proc) for i in range(self.procs)]
         t0 = time.perf_counter()
         self.pool.map(_ref_worker, work, chunksize=1)
         wall = time.perf_counter() - t0
         n = self.procs * boxes_per_proc
         return {"value": n / wall, "unit": UNIT, "cores": self.procs, "kind": "reference",
-                "sample": f"{n} of the 512 boxes ({boxes_per_proc} per process, {self.procs} processes x 1 "
+                "sample": f"{n} of the {BOXES_PER_GPU} boxes ({boxes_per_proc} per process, {self.procs} processes x 1 "
                           f"thread), wall {wall:.2f} s", "wall_s": wall, "boxes": n}
 
     def close(self):
@@ -367,12 +381,13 @@ def main():
     ap.add_argument("--impl", default="engine", choices=["engine", "reference"])
     ap.add_argument("--cpu-boxes", type=int, default=1, help="boxes per host process in the CPU baseline")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--boxes", type=int, default=BOXES_PER_GPU,
-                    help="boxes per GPU (smaller cases are for profiling only)")
+    ap.add_argument("--boxes", type=int, default=0,
+                    help="boxes per GPU (default: the workload's; smaller cases are for profiling only)")
+    ap.add_argument("--workload", default="mlp", choices=sorted(WORKLOADS))
     args = ap.parse_args()
-    if args.boxes != BOXES_PER_GPU:
-        globals()["BOXES_PER_GPU"] = args.boxes
-        globals()["WORKLOAD"] = WORKLOAD.replace("512 boxes", f"{args.boxes} boxes")
+    WL.clear()
+    WL.update(WORKLOADS[args.workload])
+    globals()["BOXES_PER_GPU"] = args.boxes if args.boxes else WL["boxes"]
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -400,8 +400,9 @@ __global__ void relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g, const float* _
     int oy, ox;
     win_origin(g, e.rows.row_id[rr], oy, ox);
     const int nu = win_neuron(g, oy, ox, j);
+    const int64_t pdst = e.ps.s ? phase_dst(e.ps, r, j) : idx;
     if (nu < 0) {
-        if (e.Pbar) e.Pbar[idx] = 0.f;
+        if (e.Pbar) e.Pbar[pdst] = 0.f;
         return;
     }
     const size_t bj = (size_t)bx * e.rp.n + nu;
@@ -419,7 +420,7 @@ __global__ void relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g, const float* _
     if (e.Pbar) {
         const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
         const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
-        e.Pbar[idx] = Qb * dq + gr * db;
+        e.Pbar[pdst] = Qb * dq + gr * db;
     }
     const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
     if (un) {

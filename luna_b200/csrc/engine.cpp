@@ -181,6 +181,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.b_neuron, bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
+        if (L.conv) build_tc_conv(L, d.weight, k);
         if (!L.conv) {
             L.W_hi = weights_.as<float>(key("Whi", k), W.size());
             L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
@@ -240,6 +241,160 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         }
     }
     lb200_options_default(&opt_);
+}
+
+// Weight matrices of the tensor-core conv steps of one conv layer.
+void Model::build_tc_conv(Layer& L, const float* w, int k) {
+    const int Co = L.out.C, Ci = L.in.C, kh = L.kh, kw = L.kw, s = L.sh;
+    if (L.sh != L.sw) return;
+    auto wv = [&](int co, int ci, int ky, int kx) { return w[(((size_t)co * Ci + ci) * kh + ky) * kw + kx]; };
+    L.Uy = (kh + s - 1) / s;
+    L.Ux = (kw + s - 1) / s;
+    if (Co % 32 == 0 && s * s * Ci >= 64 && L.Uy * L.Ux * (Co / 32) <= TC_CONV_MAX_KB) {
+        const int mt = s * s * Ci, kt = L.Uy * L.Ux * Co;
+        std::vector<float> Wf((size_t)mt * kt, 0.f);
+        for (int py = 0; py < s; ++py)
+            for (int px = 0; px < s; ++px)
+                for (int ci = 0; ci < Ci; ++ci)
+                    for (int uy = 0; uy < L.Uy; ++uy)
+                        for (int ux = 0; ux < L.Ux; ++ux) {
+                            const int ky = py + s * uy, kx = px + s * ux;
+                            if (ky >= kh || kx >= kw) continue;
+                            for (int co = 0; co < Co; ++co)
+                                Wf[(size_t)((py * s + px) * Ci + ci) * kt + (uy * L.Ux + ux) * Co + co] =
+                                    wv(co, ci, ky, kx);
+                        }
+        float* tmp = weights_.as<float>(key("Wf", k), Wf.size());
+        LB_CUDA(cudaMemcpy(tmp, Wf.data(), Wf.size() * 4, cudaMemcpyHostToDevice));
+        L.Wf_hi = weights_.as<float>(key("Wfhi", k), Wf.size());
+        L.Wf_lo = weights_.as<float>(key("Wflo", k), Wf.size());
+        launch_split_tf32(tmp, L.Wf_hi, L.Wf_lo, (int64_t)Wf.size(), 0);
+        L.tcf = true;
+    }
+    if (Ci % 32 == 0) {
+        for (int py = 0; py < s; ++py)
+            for (int px = 0; px < s; ++px)
+                for (int uy = 0; uy < L.Uy; ++uy)
+                    for (int ux = 0; ux < L.Ux; ++ux) {
+                        if (py + s * uy >= kh || px + s * ux >= kw) continue;
+                        for (int cb = 0; cb < Ci / 32; ++cb) {
+                            TcConvTap t;
+                            t.plane = py * s + px;
+                            t.dy = uy;
+                            t.dx = ux;
+                            t.c0 = cb * 32;
+                            L.adj_kb.push_back(t);
+                        }
+                    }
+        const int nka = (int)L.adj_kb.size();
+        if (nka <= TC_CONV_MAX_KB) {
+            std::vector<float> Wa((size_t)Co * nka * 32, 0.f);
+            for (int a = 0; a < nka; ++a) {
+                const TcConvTap& t = L.adj_kb[a];
+                const int ky = t.plane / s + s * t.dy, kx = t.plane % s + s * t.dx;
+                for (int co = 0; co < Co; ++co)
+                    for (int cc = 0; cc < 32; ++cc)
+                        Wa[(size_t)co * nka * 32 + a * 32 + cc] = wv(co, t.c0 + cc, ky, kx);
+            }
+            float* tmp = weights_.as<float>(key("Wa", k), Wa.size());
+            LB_CUDA(cudaMemcpy(tmp, Wa.data(), Wa.size() * 4, cudaMemcpyHostToDevice));
+            L.Wa_hi = weights_.as<float>(key("Wahi", k), Wa.size());
+            L.Wa_lo = weights_.as<float>(key("Walo", k), Wa.size());
+            launch_split_tf32(tmp, L.Wa_hi, L.Wa_lo, (int64_t)Wa.size(), 0);
+            L.tca = true;
+        } else {
+            L.adj_kb.clear();
+        }
+    }
+}
+
+// Phase grid of conv layer m for start st: output window pixel v of the
+// level below sits at t = (v + c) div s - tlo in phase (v + c) mod s.
+void Model::conv_phase(int st, int m, int& cy, int& cx, int& tlo_y, int& tlo_x, int& nty, int& ntx) const {
+    const Layer& L = layers_[m - 1];
+    const WinGeo& go = geo_[st][m - 1];
+    cy = go.full ? L.ph : 0;
+    cx = go.full ? L.pw : 0;
+    tlo_y = cy / L.sh;
+    tlo_x = cx / L.sw;
+    nty = (go.wh - 1 + cy) / L.sh - tlo_y + 1;
+    ntx = (go.ww - 1 + cx) / L.sw - tlo_x + 1;
+}
+
+TcConvPlan Model::tc_fwd_plan(int st, int m, int rows, const float* data) const {
+    const Layer& L = layers_[m - 1];
+    const WinGeo& gi = geo_[st][m];
+    int cy, cx, tly, tlx, nty, ntx;
+    conv_phase(st, m, cy, cx, tly, tlx, nty, ntx);
+    TcConvPlan p;
+    p.data = data;
+    p.C = L.out.C;
+    p.X = gi.ww;
+    p.Y = gi.wh;
+    p.P = 1;
+    p.R = rows;
+    p.ny = nty;
+    p.nx = ntx;
+    for (int uy = 0; uy < L.Uy; ++uy)
+        for (int ux = 0; ux < L.Ux; ++ux)
+            for (int cb = 0; cb < L.out.C / 32; ++cb) {
+                TcConvTap& t = p.kb[p.nkb++];
+                t.plane = 0;
+                t.dy = tly - uy;
+                t.dx = tlx - ux;
+                t.c0 = cb * 32;
+            }
+    p.w_hi = L.Wf_hi;
+    p.w_lo = L.Wf_lo;
+    p.m_total = L.sh * L.sw * L.in.C;
+    tc_conv_tile(p, rows);
+    return p;
+}
+
+TcConvPlan Model::tc_adj_plan(int st, int m, int rows, const float* pbar) const {
+    const Layer& L = layers_[m - 1];
+    const WinGeo& gi = geo_[st][m];
+    int cy, cx, tly, tlx, nty, ntx;
+    conv_phase(st, m, cy, cx, tly, tlx, nty, ntx);
+    TcConvPlan p;
+    p.data = pbar;
+    p.C = L.in.C;
+    p.X = ntx;
+    p.Y = nty;
+    p.P = L.sh * L.sw;
+    p.R = rows;
+    p.ny = gi.wh;
+    p.nx = gi.ww;
+    for (const TcConvTap& a : L.adj_kb) {
+        TcConvTap& t = p.kb[p.nkb++];
+        t.plane = a.plane;
+        t.dy = a.dy - tly;
+        t.dx = a.dx - tlx;
+        t.c0 = a.c0;
+    }
+    p.w_hi = L.Wa_hi;
+    p.w_lo = L.Wa_lo;
+    p.m_total = L.out.C;
+    tc_conv_tile(p, rows);
+    return p;
+}
+
+PhaseSplit Model::phase_split(int st, int m) const {
+    const Layer& L = layers_[m - 1];
+    PhaseSplit ps;
+    int cy, cx, tly, tlx, nty, ntx;
+    conv_phase(st, m, cy, cx, tly, tlx, nty, ntx);
+    ps.s = L.sh;
+    ps.C = L.in.C;
+    ps.out_w = geo_[st][m - 1].ww;
+    ps.cy = cy;
+    ps.cx = cx;
+    ps.tlo_y = tly;
+    ps.tlo_x = tlx;
+    ps.nty = nty;
+    ps.ntx = ntx;
+    ps.row_stride = (int64_t)L.sh * L.sw * nty * ntx * L.in.C;
+    return ps;
 }
 
 // The transposed-conv step of conv layer m for the rows of start st.
@@ -404,9 +559,17 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     float* Q[2] = {cache_.as<float>(key("Q", 0), (size_t)M * maxw), cache_.as<float>(key("Q", 1), (size_t)M * maxw)};
     float* bias = cache_.as<float>(key("bias", st), M);
     const int mb = st - 1;  // ReLU directly below the start
+    // Conv layers above the first run on tensor cores when their shapes allow.
+    auto tc_fwd = [&](int m) { return tcconv_ && m >= 2 && layers_[m - 1].tcf; };
     int slots_total = 0;
-    for (int m = mb; m >= 1; --m)
-        slots_total += layers_[m - 1].conv ? conv_chunks(sp.geo[m - 1]) : gemm_tiles_n(width(m - 1));
+    for (int m = mb; m >= 1; --m) {
+        if (!layers_[m - 1].conv)
+            slots_total += gemm_tiles_n(width(m - 1));
+        else if (tc_fwd(m))
+            slots_total += tc_conv_fwd_slots(tc_fwd_plan(st, m, M, nullptr));
+        else
+            slots_total += conv_chunks(sp.geo[m - 1]);
+    }
     float* part = cache_.as<float>(key("part", st), (size_t)slots_total * M);
     auto alpha_buf = [&](int m) {
         return alpha ? cache_.as<float>(key("alpha", m, st), (size_t)M * rowlen(st, m)) : nullptr;
@@ -472,6 +635,22 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 e.b_next = layers_[m - 2].b;
                 e.P_save = psave_buf(m - 1);
                 e.Q = Q[1 - cur];
+                if (tc_fwd(m)) {
+                    const TcConvPlan plan = tc_fwd_plan(st, m, M, Q[cur]);
+                    TcConvFwd f;
+                    f.s = L.sh;
+                    f.Ci = L.in.C;
+                    int nty, ntx;
+                    conv_phase(st, m, f.cy, f.cx, f.tlo_y, f.tlo_x, nty, ntx);
+                    f.out_h = sp.geo[m - 1].wh;
+                    f.out_w = sp.geo[m - 1].ww;
+                    f.f = e;
+                    launch_tc_conv_fwd(plan, M, f, part + (size_t)slot * M, s);
+                    prof_end(s, fl);
+                    slot += tc_conv_fwd_slots(plan);
+                    cur = 1 - cur;
+                    continue;
+                }
                 launch_convT_relax(Q[cur], cs, M, e, part + (size_t)slot * M, s);
                 cur = 1 - cur;
             } else {
@@ -639,8 +818,14 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     const int st = sp.s;
     const int R = sp.rows.R;
     if (R == 0 || M == 0) return;
-    int maxw = 0;
-    for (int m = 0; m < st; ++m) maxw = std::max(maxw, rowlen(st, m));
+    // Conv layers above the first take their adjoint on tensor cores when
+    // their shapes allow; the Pbar below such a layer is stored phase-split.
+    auto tc_adj = [&](int m) { return tcconv_ && m >= 2 && m <= st - 1 && layers_[m - 1].tca; };
+    int64_t maxw = 0;
+    for (int m = 0; m < st; ++m) {
+        maxw = std::max<int64_t>(maxw, rowlen(st, m));
+        if (m >= 1 && tc_adj(m + 1)) maxw = std::max<int64_t>(maxw, phase_split(st, m + 1).row_stride);
+    }
     float* Pb[2] = {cache_.as<float>(key("Pbar", 0), (size_t)M * maxw),
                     cache_.as<float>(key("Pbar", 1), (size_t)M * maxw)};
     const int n0 = width(0);
@@ -668,6 +853,10 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * rl);
         e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * rl);
         e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
+        if (e.Pbar && tc_adj(m + 1)) {
+            e.ps = phase_split(st, m + 1);
+            LB_CUDA(cudaMemsetAsync(e.Pbar, 0, (size_t)M * e.ps.row_stride * 4, s));
+        }
         // Projected Adam fused into the relaxation adjoint (torch::optim::Adam + clip).
         e.adam_m = cache_.as<float>(key("am", m, st), (size_t)2 * R * rl);
         e.adam_v = cache_.as<float>(key("av", m, st), (size_t)2 * R * rl);
@@ -684,7 +873,17 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             flops_ += fl;
             float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
             prof_begin(s);
-            launch_conv_adj_qbar(Pb[cur], cs, M, g, L.b, Qbar, s);
+            if (tc_adj(m)) {
+                TcConvQbar q;
+                q.Co = L.out.C;
+                q.in_w = sp.geo[m].ww;
+                q.gseed = g;
+                q.b = L.b;
+                q.Qbar = Qbar;
+                launch_tc_conv_qbar(tc_adj_plan(st, m, M, Pb[cur]), M, q, s);
+            } else {
+                launch_conv_adj_qbar(Pb[cur], cs, M, g, L.b, Qbar, s);
+            }
             prof_end(s, fl);
             if (sp.geo[m].full)
                 launch_relax_adjoint(e, Qbar, M, N, s);

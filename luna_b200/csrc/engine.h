@@ -8,6 +8,7 @@
 #include "../../include/luna_b200.h"
 #include "conv_kernels.cuh"
 #include "kernels.cuh"
+#include "tc_conv.cuh"
 
 #include <map>
 #include <string>
@@ -60,6 +61,14 @@ struct Layer {
     // tf32 (hi, lo) splits for the tensor-core path (Linear): W is the K-major
     // B operand of the adjoint contraction, Wt of the forward one.
     float *W_hi = nullptr, *W_lo = nullptr, *Wt_hi = nullptr, *Wt_lo = nullptr;
+    // Tensor-core conv weights (weights-stationary implicit GEMM, tf32 hi/lo):
+    // forward (transposed conv) Wf [s*s*Ci, Uy*Ux*Co], rows (phase, ci), K
+    // blocks (u_y, u_x, co block); adjoint (correlation) Wa [Co, |adj_kb|*32],
+    // K blocks (phase, u_y, u_x, ci block) for the taps that exist.
+    bool tcf = false, tca = false;
+    int Uy = 0, Ux = 0;
+    float *Wf_hi = nullptr, *Wf_lo = nullptr, *Wa_hi = nullptr, *Wa_lo = nullptr;
+    std::vector<TcConvTap> adj_kb;  // plane, u_y (dy), u_x (dx), c0
 };
 
 struct StartPlan {
@@ -83,7 +92,10 @@ public:
     void set_profiling(bool on) { profile_ = on; }
     // Contraction path: tensor cores (3xTF32) where the shape allows, else
     // the SIMT fp32 kernel.  Forcing SIMT is for cross-checking only.
-    void set_force_simt(bool on) { force_simt_ = on; }
+    void set_force_simt(bool on) {
+        force_simt_ = on;
+        tcconv_ = !on;
+    }
     const lb200_options& options() const { return opt_; }
 
     void compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes,
@@ -111,6 +123,7 @@ private:
     void adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s);
     void relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s);
     void init_alpha(StartPlan& sp, int m, int B, cudaStream_t s);
+    void build_tc_conv(Layer& L, const float* w, int k);
     void build_rows(int B, int nspec, cudaStream_t s);
     void alloc_alpha(int B, cudaStream_t s);
     size_t bytes_per_box(bool alpha, int nspec) const;
@@ -120,6 +133,12 @@ private:
     // Length of a row of start st at level m (its window, or the whole map).
     int rowlen(int st, int m) const { return geo_[st][m].size(); }
     ConvStep conv_step(int st, int m) const;
+    // Tensor-core plans of conv layer m for the rows of start st.
+    void conv_phase(int st, int m, int& cy, int& cx, int& tlo_y, int& tlo_x, int& nty, int& ntx) const;
+    TcConvPlan tc_fwd_plan(int st, int m, int rows, const float* data) const;
+    TcConvPlan tc_adj_plan(int st, int m, int rows, const float* pbar) const;
+    PhaseSplit phase_split(int st, int m) const;
+    bool tcconv_ = true;
     int start_form(int st) const;
     bool has_conv_ = false;
     std::string key(const char* what, int a, int b = -1) const;

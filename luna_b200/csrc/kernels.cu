@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
                 if (e.Pbar) {
                     const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
                     const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
-                    e.Pbar[at] = Qb * dq + g * db;
+                    e.Pbar[e.ps.s ? phase_dst(e.ps, r, c) : (int64_t)at] = Qb * dq + g * db;
                 }
                 const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
                 if (un) {
@@ -709,7 +709,9 @@ __global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, co
                         A[i] = adam_clip_update(A[i], ag, Mm[i], Vv[i], e.adam_step, e.adam_bc2_sqrt);
                     }
                 }
-                if (pb) *reinterpret_cast<float4*>(pb + at) = make_float4(out[0], out[1], out[2], out[3]);
+                if (pb)
+                    *reinterpret_cast<float4*>(pb + (e.ps.s ? phase_dst(e.ps, r, c) : (int64_t)at)) =
+                        make_float4(out[0], out[1], out[2], out[3]);
                 if (adam) {
                     *reinterpret_cast<float4*>(al + at) = make_float4(A[0], A[1], A[2], A[3]);
                     *reinterpret_cast<float4*>(am + at) = make_float4(Mm[0], Mm[1], Mm[2], Mm[3]);

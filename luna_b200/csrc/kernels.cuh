@@ -101,7 +101,28 @@ struct EpiConcretize {
     const float* xu = nullptr;
     uint8_t* sign = nullptr;        // [M, N] or null: bit0 P>=0, bit1 P<=0
 };
+// Layout of Pbar when the layer above it takes its adjoint on tensor cores
+// as a strided correlation: the window (out_h x out_w x C, row-major HWC)
+// split into s*s phase planes of nty x ntx pixels, window pixel v sitting in
+// plane ((v + c) mod s) at t = (v + c) div s - tlo.  Slots that no window
+// pixel maps to stay zero (the caller clears the rows first).
+struct PhaseSplit {
+    int s = 0;  // 0: Pbar keeps the window layout
+    int C = 0, out_w = 0, cy = 0, cx = 0, tlo_y = 0, tlo_x = 0, nty = 0, ntx = 0;
+    int64_t row_stride = 0;  // s * s * nty * ntx * C
+};
+#ifdef __CUDACC__
+__device__ __forceinline__ int64_t phase_dst(const PhaseSplit& ps, int64_t r, int j) {
+    const int c = j % ps.C, pix = j / ps.C;
+    const int vy = pix / ps.out_w + ps.cy, vx = pix - (pix / ps.out_w) * ps.out_w + ps.cx;
+    const int plane = (vy % ps.s) * ps.s + vx % ps.s;
+    const int ty = vy / ps.s - ps.tlo_y, tx = vx / ps.s - ps.tlo_x;
+    return r * ps.row_stride + (((int64_t)plane * ps.nty + ty) * ps.ntx + tx) * ps.C + c;
+}
+#endif
+
 struct EpiRelaxAdj {
+    PhaseSplit ps;  // launch_relax_adjoint / launch_relax_adjoint_win only
     RowMap rows;
     ReluParams rp;
     const float* gseed = nullptr;   // [M] bias adjoint of each row

@@ -14,6 +14,7 @@
 // tile j+1.  Every wait is bounded (about 2 s); on expiry the CTA raises an
 // error flag, drains what it issued and returns.
 #include "tc_gemm.cuh"
+#include "tc_ptx.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -26,11 +27,12 @@ namespace lb200 {
 
 namespace {
 
+using namespace tcx;
+
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 32;  // fp32 columns per 128-byte swizzle row
 constexpr int NUM_THREADS = 384;
 constexpr int WARP_TMA = 0, WARP_MMA = 1, EPI_WARP0 = 4, XF_WARP0 = 8;
-constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
 constexpr int A_TILE_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 
 // Epilogues: relaxation of the next ReLU (stores P and Q), input
@@ -50,107 +52,6 @@ struct TcEpi {
     EpiStoreQbar q;
     float* P_out = nullptr;  // KIND_STOREP
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t cnt) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(cnt) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(smem_u32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Wait for the phase of parity `parity` to complete.  Gives up when another
-// role raised `abort` (unless ignore_abort) or after WAIT_CYCLES.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort,
-                                          bool ignore_abort = false) {
-    if (mbar_try(b, parity)) return true;
-    const long long t0 = clock64();
-    while (true) {
-        if (mbar_try(b, parity)) return true;
-        if (!ignore_abort && *abort) return false;
-        if (clock64() - t0 > WAIT_CYCLES) {
-            *abort = 1;
-            atomicExch(&g_tc_error, 1);
-            return false;
-        }
-    }
-}
-
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-            smem_u32(dst)),
-        "l"((uint64_t)map), "r"(smem_u32(bar)), "r"(x), "r"(y)
-        : "memory");
-}
-
-// K-major operand in shared memory, 128-byte swizzle: rows of 128 bytes,
-// 8-row atoms 1024 bytes apart (stride byte offset), descriptor version 1.
-__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-    d |= (uint64_t)1 << 16;
-    d |= (uint64_t)(1024 >> 4) << 32;
-    d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
-    return d;
-}
-
-// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    const uint32_t z = 0;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(z), "r"(z), "r"(z), "r"(z));
-}
-
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-    uint32_t r[16];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
-        "%15}, [%16];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-__device__ __forceinline__ float rna_tf32(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return __uint_as_float(r);
-}
 
 __device__ __forceinline__ void split_row2(int r, int R, int& p, int& rr) {
     p = r >= R ? 1 : 0;
@@ -340,7 +241,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int s = g % S;
                     const uint32_t ph = (g / S) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1, abort)) break;
+                    if (!mbar_wait(&empty[s], ph ^ 1, abort, &g_tc_error)) break;
                     // A raw (TMA / RELAX: P) lands in the hi slot, alpha (RELAX /
                     // GATHER) in the lo slot; the split warps overwrite both.
                     const bool load_a = AMODE == AMODE_TMA || AMODE == AMODE_RELAX;
@@ -356,7 +257,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if (*abort) {
                 // Drain: wait (bounded) for the last loads issued to land.
                 for (uint32_t q = (g > (uint32_t)S ? g - S : 0); q < g; ++q)
-                    mbar_wait(&full[q % S], (q / S) & 1, abort, true);
+                    mbar_wait(&full[q % S], (q / S) & 1, abort, &g_tc_error, true);
             }
         }
     } else if (warp == WARP_MMA) {
@@ -368,14 +269,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++j) {
                 const int acc = j & 1;
                 const uint32_t aph = (j >> 1) & 1;
-                if (!mbar_wait(&tempty[acc], aph ^ 1, abort)) break;
+                if (!mbar_wait(&tempty[acc], aph ^ 1, abort, &g_tc_error)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int s = g % S;
                     const uint32_t ph = (g / S) & 1;
-                    if (!mbar_wait(&split[s], ph, abort)) { ok = false; break; }
+                    if (!mbar_wait(&split[s], ph, abort, &g_tc_error)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t dah = desc_sw128(smem_u32(a_hi(s)));
                     const uint64_t dal = desc_sw128(smem_u32(a_lo(s)));
@@ -396,7 +297,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 if (!ok) break;
                 umma_commit(&tfull[acc]);
             }
-            if (*abort && issued) mbar_wait(last_commit, last_phase, abort, true);
+            if (*abort && issued) mbar_wait(last_commit, last_phase, abort, &g_tc_error, true);
         }
     } else if (warp >= XF_WARP0) {
         const int xt = threadIdx.x - XF_WARP0 * 32;
@@ -425,7 +326,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % S;
                 const uint32_t ph = (g / S) & 1;
-                if (!mbar_wait(&full[s], ph, abort)) { ok = false; break; }
+                if (!mbar_wait(&full[s], ph, abort, &g_tc_error)) { ok = false; break; }
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
                 if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
@@ -525,7 +426,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             const int mb = t / tiles_n, nb = t % tiles_n;
             const int acc = j & 1;
             const uint32_t aph = (j >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], aph, abort)) break;
+            if (!mbar_wait(&tfull[acc], aph, abort, &g_tc_error)) break;
             tc_fence_after();
             const int r = mb * TC_BM + q * 32 + lane;
             const bool row_ok = r < M;

@@ -195,3 +195,13 @@ def random_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.05):
     layers.append(("linear", 3))
     g = cnn((c, h, h), layers, seed + 11, bias_std=0.1)
     return g, image_boxes(rng, n_boxes, c * h * h, eps, 3)
+
+
+def cnn_wide_case(seed: int, n_boxes: int = 3, eps: float = 0.01, hw: int = 12):
+    """Small CNN whose strided convs have 32 / 64 channels (the shapes the
+    tensor-core conv path takes), for parity tests: 3 x hw x hw -> conv32 k3
+    -> conv32 k4s2p1 -> conv64 k4s2p1 -> 16 -> 4."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    g = cnn((3, hw, hw), [("conv", 32, 3, 1, 1), ("conv", 32, 4, 2, 1), ("conv", 64, 4, 2, 1),
+                          ("linear", 16), ("linear", 4)], seed + 5, bias_std=0.05)
+    return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)

@@ -65,6 +65,23 @@ def test_cnn_matches_oracle_random(seed, method):
     _assert_parity(f"cnn{seed}/{method}", lb, ub, olb, oub)
 
 
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_tc_conv_matches_simt_and_oracle(method):
+    """Strided 32/64-channel convs (tcgen05 implicit-GEMM steps, windows and
+    whole maps) agree with the SIMT conv kernels and with the oracle."""
+    from oracle.lirpa_oracle import LirpaOracle
+    g, bx = W.cnn_wide_case(21)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=6)
+    m = Model(g, options=opt)
+    tlb, tub = m.compute_bounds(bx, method)
+    m.set_contraction_path(1)
+    slb, sub = m.compute_bounds(bx, method)
+    olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
+    print(f"simt vs oracle: {G.excess_scaled(slb, olb, olb, oub):.3f} {G.excess_scaled(sub, oub, olb, oub):.3f}")
+    _assert_parity(f"tc vs simt/{method}", tlb, tub, slb, sub)
+    _assert_parity(f"tc vs oracle/{method}", tlb, tub, olb, oub)
+
+
 def _forward(graph, x):
     """Chain forward of a graph on a batch of flat inputs (CHW order)."""
     import torch.nn.functional as F
