@@ -3,6 +3,8 @@
 // adjoints).
 #include "conv_kernels.cuh"
 
+#include <stdexcept>
+
 namespace lb200 {
 
 namespace {
@@ -441,6 +443,169 @@ void launch_relax_adjoint_win(const EpiRelaxAdj& e, const WinGeo& g, const float
     const int64_t total = (int64_t)M * g.size();
     if (total == 0) return;
     relax_adjoint_win_kernel<<<ceil_div(total, 256), 256, 0, s>>>(e, g, Qbar, M);
+    LB_LAUNCH();
+}
+
+// ============================================================== first conv layer
+namespace {
+constexpr int FK = 3, FC = 3;  // kernel 3x3 over 3 input channels, stride 1
+
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+}  // namespace
+
+bool first_conv_fast(const ConvStep& cs) {
+    return cs.kh == FK && cs.kw == FK && cs.Ci == FC && cs.Co <= 32 && cs.sh == 1 && cs.sw == 1 && cs.cy <= FK &&
+           cs.cx <= FK && (cs.out_h + 2 * FK + 1) * (cs.out_w + 2 * FK + 1) * FC * 4 <= 48 * 1024;
+}
+
+__global__ void __launch_bounds__(256) first_convT_conc_kernel(const float* __restrict__ A, ConvStep cs, int M,
+                                                               ConvConcEpi e, float* __restrict__ partial) {
+    __shared__ float sh[8];
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    int oy, ox;
+    win_origin(e.g, e.rows.row_id[rr], oy, ox);
+    const int n0 = e.g.C * e.g.H * e.g.W;
+    const int nin = cs.in_h * cs.in_w * cs.Co;
+    const int nw = e.g.size();
+    const float* Arow = A + (size_t)r * nin;
+    float part = 0.f;
+    {
+        const int co = lane;  // Co <= 32
+        const bool cok = co < cs.Co;
+        float w[FK * FK * FC];
+#pragma unroll
+        for (int t = 0; t < FK * FK; ++t)
+#pragma unroll
+            for (int ci = 0; ci < FC; ++ci)
+                w[t * FC + ci] = cok ? cs.Wk[((size_t)t * cs.Co + co) * FC + ci] : 0.f;
+        for (int pix = warp; pix < cs.out_h * cs.out_w; pix += 8) {
+            const int vy = pix / cs.out_w, vx = pix - (pix / cs.out_w) * cs.out_w;
+            float acc[FC] = {0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ky = 0; ky < FK; ++ky) {
+                const int qy = vy + cs.cy - ky;
+                if (qy < 0 || qy >= cs.in_h) continue;
+#pragma unroll
+                for (int kx = 0; kx < FK; ++kx) {
+                    const int qx = vx + cs.cx - kx;
+                    if (qx < 0 || qx >= cs.in_w) continue;
+                    const float a = cok ? Arow[((size_t)qy * cs.in_w + qx) * cs.Co + co] : 0.f;
+#pragma unroll
+                    for (int ci = 0; ci < FC; ++ci) acc[ci] = fmaf(a, w[(ky * FK + kx) * FC + ci], acc[ci]);
+                }
+            }
+#pragma unroll
+            for (int ci = 0; ci < FC; ++ci) acc[ci] = warp_allsum(acc[ci]);
+            if (lane < FC) {
+                const float P = lane == 0 ? acc[0] : (lane == 1 ? acc[1] : acc[2]);
+                const int j = pix * FC + lane;
+                const int nu = win_neuron(e.g, oy, ox, j);
+                uint8_t sg = 0;
+                if (nu >= 0) {
+                    const float xl = e.xl[(size_t)bx * n0 + nu], xu = e.xu[(size_t)bx * n0 + nu];
+                    if (e.form == CONC_PATCHES) {
+                        const float c = (xu + xl) / 2.0f, d = (xu - xl) / 2.0f;
+                        part += p == 0 ? fmaf(P, c, -fabsf(P) * d) : fmaf(P, c, fabsf(P) * d);
+                        sg = (uint8_t)((P > 0.f ? 1 : 0) | (P < 0.f ? 2 : 0));
+                    } else {
+                        const float xa = p == 0 ? xl : xu, xb = p == 0 ? xu : xl;
+                        part += fmaxf(P, 0.f) * xa + fminf(P, 0.f) * xb;
+                        sg = (uint8_t)((P >= 0.f ? 1 : 0) | (P <= 0.f ? 2 : 0));
+                    }
+                }
+                if (e.sign) e.sign[(size_t)r * nw + j] = sg;
+            }
+        }
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) partial[r] = tot;
+}
+
+void launch_first_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConcEpi& e, float* partial,
+                             cudaStream_t s) {
+    if (M == 0) return;
+    if (cs.Co > 32) throw std::invalid_argument("first_convT_conc: Co > 32");
+    first_convT_conc_kernel<<<M, 256, 0, s>>>(A, cs, M, e, partial);
+    LB_LAUNCH();
+}
+
+__global__ void __launch_bounds__(256) first_conv_adj_kernel(RowMap rows, int M, WinGeo g0, int form,
+                                                             const uint8_t* __restrict__ sign,
+                                                             const float* __restrict__ gseed,
+                                                             const float* __restrict__ xl,
+                                                             const float* __restrict__ xu, ConvStep cs,
+                                                             const float* __restrict__ b,
+                                                             float* __restrict__ Qbar) {
+    extern __shared__ float sP[];  // seed window with a zero halo of FK on each side
+    const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int PW = cs.out_w + 2 * FK + 1, PH = cs.out_h + 2 * FK + 1;
+    for (int i = threadIdx.x; i < PH * PW * FC; i += blockDim.x) sP[i] = 0.f;
+    __syncthreads();
+    int p, rr;
+    row_split(r, rows.R, p, rr);
+    const int bx = rows.row_box[rr];
+    int oy, ox;
+    win_origin(g0, rows.row_id[rr], oy, ox);
+    const int n0 = g0.C * g0.H * g0.W;
+    const int nw = g0.size();
+    const float gr = gseed[r];
+    for (int j = threadIdx.x; j < nw; j += blockDim.x) {
+        const int nu = win_neuron(g0, oy, ox, j);
+        float v = 0.f;
+        if (nu >= 0) {
+            const float l = xl[(size_t)bx * n0 + nu], u = xu[(size_t)bx * n0 + nu];
+            const uint8_t sg = sign[(size_t)r * nw + j];
+            if (form == CONC_PATCHES) {
+                const float c = (u + l) / 2.0f, d = (u - l) / 2.0f;
+                const float sgn = (sg & 1) ? 1.f : ((sg & 2) ? -1.f : 0.f);
+                v = p == 0 ? gr * c - gr * d * sgn : gr * c + gr * d * sgn;
+            } else {
+                const float xa = p == 0 ? l : u, xbv = p == 0 ? u : l;
+                v = ((sg & 1) ? gr * xa : 0.f) + ((sg & 2) ? gr * xbv : 0.f);
+            }
+        }
+        const int ci = j % FC, pix = j / FC;
+        const int vy = pix / cs.out_w, vx = pix - (pix / cs.out_w) * cs.out_w;
+        sP[((vy + FK) * PW + vx + FK) * FC + ci] = v;
+    }
+    __syncthreads();
+    const int nq = cs.in_h * cs.in_w;
+    for (int cb = 0; cb < cs.Co; cb += 32) {
+        const int co = cb + lane;
+        const bool cok = co < cs.Co;
+        float w[FK * FK * FC];
+#pragma unroll
+        for (int t = 0; t < FK * FK * FC; ++t) w[t] = cok ? cs.Wc[(size_t)co * FK * FK * FC + t] : 0.f;
+        const float gb = cok ? gr * b[co] : 0.f;
+        for (int q = warp; q < nq; q += 8) {
+            const int qy = q / cs.in_w, qx = q - (q / cs.in_w) * cs.in_w;
+            const float* base = sP + ((qy - cs.cy + FK) * PW + qx - cs.cx + FK) * FC;
+            float acc = 0.f;
+#pragma unroll
+            for (int ky = 0; ky < FK; ++ky)
+#pragma unroll
+                for (int kx = 0; kx < FK; ++kx)
+#pragma unroll
+                    for (int ci = 0; ci < FC; ++ci)
+                        acc = fmaf(base[(ky * PW + kx) * FC + ci], w[(ky * FK + kx) * FC + ci], acc);
+            if (cok) Qbar[((size_t)r * nq + q) * cs.Co + co] = acc + gb;
+        }
+    }
+}
+
+void launch_first_conv_adj(const RowMap& rows, int M, const WinGeo& g0, int form, const uint8_t* sign,
+                           const float* gseed, const float* xl, const float* xu, const ConvStep& cs,
+                           const float* b, float* Qbar, cudaStream_t s) {
+    if (M == 0) return;
+    const size_t smem = (size_t)(cs.out_h + 2 * FK + 1) * (cs.out_w + 2 * FK + 1) * FC * 4;
+    first_conv_adj_kernel<<<M, 256, smem, s>>>(rows, M, g0, form, sign, gseed, xl, xu, cs, b, Qbar);
     LB_LAUNCH();
 }
 

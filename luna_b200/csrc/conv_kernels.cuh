@@ -132,6 +132,18 @@ void launch_conv_adj_qbar(const float* Pbar, const ConvStep& cs, int M, const fl
 // added into kbar / bbar [B, n] per neuron with atomics.
 void launch_relax_adjoint_win(const EpiRelaxAdj& e, const WinGeo& g, const float* Qbar, int M,
                               cudaStream_t s);
+// First conv layer with few channels (kh = kw = 3, Ci = 3, Co <= 32, stride
+// 1): its transposed-conv step fused with the input concretisation, and its
+// adjoint fused with the input seed.  One CTA per row, one output pixel per
+// warp iteration, lane = output channel of the conv (its 27 weights in
+// registers).  The concretisation writes one partial per row (slot 0).
+bool first_conv_fast(const ConvStep& cs);
+void launch_first_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConcEpi& e, float* partial,
+                             cudaStream_t s);
+void launch_first_conv_adj(const RowMap& rows, int M, const WinGeo& g0, int form, const uint8_t* sign,
+                           const float* gseed, const float* xl, const float* xu, const ConvStep& cs,
+                           const float* b, float* Qbar, cudaStream_t s);
+
 // alpha[p][r][j] = init_slope[box, neuron(r, j)] (0 outside the map).
 void launch_alpha_init_win(const RowMap& rows, const WinGeo& g, const float* init_slope, int n,
                            float* alpha, cudaStream_t s);

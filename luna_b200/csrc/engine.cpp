@@ -565,6 +565,8 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     for (int m = mb; m >= 1; --m) {
         if (!layers_[m - 1].conv)
             slots_total += gemm_tiles_n(width(m - 1));
+        else if (m == 1 && first_conv_fast(conv_step(st, 1)))
+            slots_total += 1;
         else if (tc_fwd(m))
             slots_total += tc_conv_fwd_slots(tc_fwd_plan(st, m, M, nullptr));
         else
@@ -661,6 +663,12 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 e.xl = xl_;
                 e.xu = xu_;
                 if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * rowlen(st, 0));
+                if (first_conv_fast(cs)) {
+                    launch_first_convT_conc(Q[cur], cs, M, e, part + (size_t)slot * M, s);
+                    prof_end(s, fl);
+                    slot += 1;
+                    continue;
+                }
                 launch_convT_conc(Q[cur], cs, M, e, part + (size_t)slot * M, s);
             }
             prof_end(s, fl);
@@ -833,10 +841,13 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     // On the tensor-core path the first contraction generates d loss / d A at
     // the input from the signs itself; the SIMT path materialises it.
     const bool seed_in_kernel = tc_;
-    if (layers_[0].conv)
-        launch_win_input_seed(sp.rows, M, sp.geo[0], sp.form, sign, g, xl_, xu_, Pb[0], s);
-    else if (!seed_in_kernel)
+    // A small first conv generates the input seed inside its adjoint kernel.
+    const bool first_fast = layers_[0].conv && first_conv_fast(conv_step(st, 1));
+    if (layers_[0].conv) {
+        if (!first_fast) launch_win_input_seed(sp.rows, M, sp.geo[0], sp.form, sign, g, xl_, xu_, Pb[0], s);
+    } else if (!seed_in_kernel) {
         launch_adj_input_seed(sp.rows, M, sign, g, xl_, xu_, n0, Pb[0], s);
+    }
     int cur = 0;
     for (int m = 1; m <= st - 1; ++m) {
         const Layer& L = layers_[m - 1];
@@ -873,7 +884,9 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             flops_ += fl;
             float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
             prof_begin(s);
-            if (tc_adj(m)) {
+            if (m == 1 && first_fast) {
+                launch_first_conv_adj(sp.rows, M, sp.geo[0], sp.form, sign, g, xl_, xu_, cs, L.b, Qbar, s);
+            } else if (tc_adj(m)) {
                 TcConvQbar q;
                 q.Co = L.out.C;
                 q.in_w = sp.geo[m].ww;
