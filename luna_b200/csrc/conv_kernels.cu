@@ -317,6 +317,61 @@ void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConc
     LB_LAUNCH();
 }
 
+int relax_window_chunks(const WinGeo& g) { return ceil_div(g.size(), 1024); }
+
+// 256 threads x 4 consecutive elements (one pixel's channels when C % 4 == 0).
+__global__ void __launch_bounds__(256) relax_window_kernel(const float* __restrict__ P, ConvRelaxEpi e, int M,
+                                                           int nchunk, float* __restrict__ partial) {
+    __shared__ float sh[8];
+    const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
+    const int nw = e.g.size();
+    const int j0 = chunk * 1024 + threadIdx.x * 4;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    int oy, ox;
+    win_origin(e.g, e.rows.row_id[rr], oy, ox);
+    float part = 0.f;
+    if (j0 < nw) {
+        const size_t at = (size_t)r * nw + j0;
+        const float4 p4 = *reinterpret_cast<const float4*>(P + at);
+        const float Pv[4] = {p4.x, p4.y, p4.z, p4.w};
+        float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (e.alpha) a4 = *reinterpret_cast<const float4*>(e.alpha + at);
+        const float Av[4] = {a4.x, a4.y, a4.z, a4.w};
+        const int nu0 = win_neuron(e.g, oy, ox, j0);  // the 4 elements share a pixel
+        float Qv[4] = {0.f, 0.f, 0.f, 0.f};
+        if (nu0 >= 0) {
+            const size_t bj = (size_t)bx * e.rp.n + nu0;
+            const float4 s4 = *reinterpret_cast<const float4*>(e.rp.slope_lo + bj);
+            const float4 k4 = *reinterpret_cast<const float4*>(e.rp.k_up + bj);
+            const float4 b4 = *reinterpret_cast<const float4*>(e.rp.b_up + bj);
+            const uchar4 f4 = *reinterpret_cast<const uchar4*>(e.rp.flags + bj);
+            const float sl[4] = {s4.x, s4.y, s4.z, s4.w}, ku[4] = {k4.x, k4.y, k4.z, k4.w},
+                        bu[4] = {b4.x, b4.y, b4.z, b4.w};
+            const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
+            const int c0 = j0 % e.g.C;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float sv = (e.alpha && (fl[i] & RF_USE_ALPHA)) ? Av[i] : sl[i];
+                Qv[i] = relax_q(Pv[i], p, sv, ku[i], bu[i], part);
+                if (e.b_next) part = fmaf(Qv[i], e.b_next[c0 + i], part);
+            }
+        }
+        *reinterpret_cast<float4*>(e.Q + at) = make_float4(Qv[0], Qv[1], Qv[2], Qv[3]);
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+}
+
+void launch_relax_window(const float* P, const ConvRelaxEpi& e, int M, float* partial, cudaStream_t s) {
+    if (M == 0) return;
+    if (e.g.C % 4 != 0) throw std::invalid_argument("relax_window: channels must be a multiple of 4");
+    const int nchunk = relax_window_chunks(e.g);
+    relax_window_kernel<<<(unsigned)((int64_t)M * nchunk), 256, 0, s>>>(P, e, M, nchunk, partial);
+    LB_LAUNCH();
+}
+
 // ============================================================== adjoint
 __global__ void win_input_seed_kernel(RowMap rows, int M, WinGeo g, int form, const uint8_t* __restrict__ sign,
                                       const float* __restrict__ gseed, const float* __restrict__ xl,

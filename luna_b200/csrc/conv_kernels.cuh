@@ -114,6 +114,13 @@ void launch_convT_relax(const float* A, const ConvStep& cs, int M, const ConvRel
 void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConcEpi& e, float* partial,
                        cudaStream_t s);
 
+// ReLU relaxation of a level from its raw A window P (stored by a tensor-core
+// step): Q = relax(P) masked outside the map, bias partials (intercepts +
+// Q . b_next per row) into partial[chunk * M + r], one chunk per 1024
+// elements of a row (relax_window_chunks).  e.P_save is not used.
+int relax_window_chunks(const WinGeo& g);
+void launch_relax_window(const float* P, const ConvRelaxEpi& e, int M, float* partial, cudaStream_t s);
+
 // ---- adjoint --------------------------------------------------------------
 // d loss / d A at the input window from the concretisation signs: dense form
 // (bit0 A>=0, bit1 A<=0) g (xa [bit0] + xb [bit1]); patches form (bit0 A>0,

@@ -568,7 +568,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
         else if (m == 1 && first_conv_fast(conv_step(st, 1)))
             slots_total += 1;
         else if (tc_fwd(m))
-            slots_total += tc_conv_fwd_slots(tc_fwd_plan(st, m, M, nullptr));
+            slots_total += relax_window_chunks(sp.geo[m - 1]);
         else
             slots_total += conv_chunks(sp.geo[m - 1]);
     }
@@ -638,7 +638,8 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 e.P_save = psave_buf(m - 1);
                 e.Q = Q[1 - cur];
                 if (tc_fwd(m)) {
-                    const TcConvPlan plan = tc_fwd_plan(st, m, M, Q[cur]);
+                    // Raw P from the tensor cores (into the saved P when the
+                    // adjoint needs it), then the relaxation streams over it.
                     TcConvFwd f;
                     f.s = L.sh;
                     f.Ci = L.in.C;
@@ -646,10 +647,11 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                     conv_phase(st, m, f.cy, f.cx, f.tlo_y, f.tlo_x, nty, ntx);
                     f.out_h = sp.geo[m - 1].wh;
                     f.out_w = sp.geo[m - 1].ww;
-                    f.f = e;
-                    launch_tc_conv_fwd(plan, M, f, part + (size_t)slot * M, s);
+                    f.P = e.P_save ? e.P_save : cache_.as<float>("Pconv", (size_t)M * rowlen(st, m - 1));
+                    launch_tc_conv_fwd(tc_fwd_plan(st, m, M, Q[cur]), M, f, s);
                     prof_end(s, fl);
-                    slot += tc_conv_fwd_slots(plan);
+                    launch_relax_window(f.P, e, M, part + (size_t)slot * M, s);
+                    slot += relax_window_chunks(sp.geo[m - 1]);
                     cur = 1 - cur;
                     continue;
                 }

@@ -33,30 +33,11 @@ constexpr int WARP_TMA = 0, WARP_MMA = 1, EPI_WARP0 = 4, XF_WARP0 = 8;
 constexpr int W_TILE_BYTES = 128 * 32 * 4;  // 16 KB
 enum { KIND_FWD = 0, KIND_QBAR = 1 };
 
-__device__ __forceinline__ float warp_sum32(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-
-__device__ __forceinline__ void conv_win_origin(const WinGeo& g, int row_id, int& oy, int& ox) {
-    if (g.full) {
-        oy = 0;
-        ox = 0;
-        return;
-    }
-    const int pix = row_id / g.st_C;
-    const int y0 = pix / g.st_W, x0 = pix - (pix / g.st_W) * g.st_W;
-    oy = g.mul_y * y0 + g.off_y;
-    ox = g.mul_x * x0 + g.off_x;
-}
-
 template <int BNMAX, int S, int KIND>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     tc_conv_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap twh,
                    const __grid_constant__ CUtensorMap twl, const __grid_constant__ TcConvPlan plan, int rows,
-                   const __grid_constant__ TcConvFwd ef, const __grid_constant__ TcConvQbar eq, float* partial,
-                   int* err) {
+                   const __grid_constant__ TcConvFwd ef, const __grid_constant__ TcConvQbar eq, int* err) {
     constexpr int X_TILE_BYTES = BNMAX * 128;
     constexpr int STAGE_BYTES = 2 * W_TILE_BYTES + 2 * X_TILE_BYTES;
     constexpr uint32_t TMEM_COLS = (2 * BNMAX <= 32) ? 32 : (2 * BNMAX <= 64) ? 64 : (2 * BNMAX <= 128) ? 128
@@ -223,68 +204,31 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             if constexpr (KIND == KIND_FWD) {
                 const int phase = m / ef.Ci, ci = m - (m / ef.Ci) * ef.Ci;
                 const int py = phase / ef.s, px = phase - (phase / ef.s) * ef.s;
-                const int nw = ef.f.g.size();
-                const int slot = (mt * 4 + q) * nyb + yb;
-                int cur_r = -1, box = 0, side = 0, oy = 0, ox = 0;
-                float part = 0.f;
+                const int nw = ef.out_h * ef.out_w * ef.Ci;
+                // Output pixel of the first column of each 16-column chunk,
+                // advanced column by column (warp-uniform).
                 for (int c0 = 0; c0 < N; c0 += 16) {
                     float v[16];
                     tmem_ld16(taddr + (uint32_t)c0, v);
-#pragma unroll 1
+                    int rl = c0 / pix_per_row, rem = c0 - rl * pix_per_row;
+                    int yy = rem / plan.BX, xx = rem - yy * plan.BX;
+#pragma unroll
                     for (int i = 0; i < 16; ++i) {
-                        const int n = c0 + i;
-                        const int rl = n / pix_per_row, rem = n - rl * pix_per_row;
                         const int r = rb * plan.BR + rl;
-                        if (n >= plan.BR * pix_per_row || r >= rows) break;
-                        if (r != cur_r) {
-                            if (cur_r >= 0) {
-                                const float tot = warp_sum32(part);
-                                if (lane == 0 && partial) partial[(size_t)slot * rows + cur_r] = tot;
-                            }
-                            part = 0.f;
-                            cur_r = r;
-                            side = r >= ef.f.rows.R ? 1 : 0;
-                            const int rr = r - side * ef.f.rows.R;
-                            box = ef.f.rows.row_box[rr];
-                            conv_win_origin(ef.f.g, ef.f.rows.row_id[rr], oy, ox);
-                        }
-                        const int ty = yb * plan.BY + rem / plan.BX, tx = rem - (rem / plan.BX) * plan.BX;
+                        const int ty = yb * plan.BY + yy;
                         const int vy = ef.s * (ty + ef.tlo_y) + py - ef.cy;
-                        const int vx = ef.s * (tx + ef.tlo_x) + px - ef.cx;
-                        if (!m_ok || ty >= plan.ny || vy < 0 || vy >= ef.out_h || vx < 0 || vx >= ef.out_w) continue;
-                        const int jw = (vy * ef.out_w + vx) * ef.Ci + ci;
-                        const size_t at = (size_t)r * nw + jw;
-                        const float P = v[i];
-                        if (ef.f.P_save) ef.f.P_save[at] = P;
-                        float Q = 0.f;
-                        int nu = jw;
-                        if (!ef.f.g.full) {
-                            const int y = oy + vy, x = ox + vx;
-                            nu = ((unsigned)y < (unsigned)ef.f.g.H && (unsigned)x < (unsigned)ef.f.g.W)
-                                     ? (y * ef.f.g.W + x) * ef.f.g.C + ci
-                                     : -1;
-                        }
-                        if (nu >= 0) {
-                            const size_t bj = (size_t)box * ef.f.rp.n + nu;
-                            const float sl = (ef.f.alpha && (ef.f.rp.flags[bj] & RF_USE_ALPHA)) ? ef.f.alpha[at]
-                                                                                                : ef.f.rp.slope_lo[bj];
-                            const float k = ef.f.rp.k_up[bj], b = ef.f.rp.b_up[bj];
-                            const float pos = fmaxf(P, 0.f), neg = fminf(P, 0.f);
-                            if (side == 0) {
-                                part += neg * b;
-                                Q = pos * sl + neg * k;
-                            } else {
-                                part += pos * b;
-                                Q = pos * k + neg * sl;
+                        const int vx = ef.s * (xx + ef.tlo_x) + px - ef.cx;
+                        if (m_ok && rl < plan.BR && r < rows && ty < plan.ny && (unsigned)vy < (unsigned)ef.out_h &&
+                            (unsigned)vx < (unsigned)ef.out_w)
+                            ef.P[(size_t)r * nw + (vy * ef.out_w + vx) * ef.Ci + ci] = v[i];
+                        if (++xx == plan.BX) {
+                            xx = 0;
+                            if (++yy == plan.BY) {
+                                yy = 0;
+                                ++rl;
                             }
-                            if (ef.f.b_next) part = fmaf(Q, ef.f.b_next[ci], part);
                         }
-                        ef.f.Q[at] = Q;
                     }
-                }
-                if (cur_r >= 0) {
-                    const float tot = warp_sum32(part);
-                    if (lane == 0 && partial) partial[(size_t)slot * rows + cur_r] = tot;
                 }
             } else {
                 const int co = m;
@@ -374,8 +318,7 @@ int sm_count() {
 }
 
 template <int BNMAX, int S, int KIND>
-void run_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcConvQbar& eq, float* partial,
-              cudaStream_t s) {
+void run_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcConvQbar& eq, cudaStream_t s) {
     constexpr int STAGE_BYTES = 2 * W_TILE_BYTES + 2 * BNMAX * 128;
     constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
     static bool configured = false;
@@ -391,18 +334,16 @@ void run_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcConvQb
     const int nyb = (p.ny + p.BY - 1) / p.BY;
     const int64_t ntiles = (int64_t)((rows + p.BR - 1) / p.BR) * nyb * ((p.m_total + 127) / 128);
     const int grid = (int)std::min<int64_t>(ntiles, sm_count());
-    tc_conv_kernel<BNMAX, S, KIND><<<grid, NUM_THREADS, SMEM, s>>>(tx, twh, twl, p, rows, ef, eq, partial,
-                                                                  tc_error_flag());
+    tc_conv_kernel<BNMAX, S, KIND><<<grid, NUM_THREADS, SMEM, s>>>(tx, twh, twl, p, rows, ef, eq, tc_error_flag());
     LB_LAUNCH();
 }
 
 template <int KIND>
-void dispatch_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcConvQbar& eq, float* partial,
-                   cudaStream_t s) {
+void dispatch_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcConvQbar& eq, cudaStream_t s) {
     if (p.N > 128)
-        run_conv<256, 2, KIND>(p, rows, ef, eq, partial, s);
+        run_conv<256, 2, KIND>(p, rows, ef, eq, s);
     else
-        run_conv<128, 3, KIND>(p, rows, ef, eq, partial, s);
+        run_conv<128, 3, KIND>(p, rows, ef, eq, s);
 }
 
 }  // namespace
@@ -420,19 +361,14 @@ void tc_conv_tile(TcConvPlan& p, int rows) {
     p.N = ((p.BR * p.BY * p.BX + 15) / 16) * 16;
 }
 
-int tc_conv_fwd_slots(const TcConvPlan& p) {
-    const int nyb = (p.ny + p.BY - 1) / p.BY;
-    return ((p.m_total + 127) / 128) * 4 * nyb;
-}
-
-void launch_tc_conv_fwd(const TcConvPlan& p, int rows, const TcConvFwd& e, float* partial, cudaStream_t s) {
+void launch_tc_conv_fwd(const TcConvPlan& p, int rows, const TcConvFwd& e, cudaStream_t s) {
     if (rows == 0) return;
-    dispatch_conv<KIND_FWD>(p, rows, e, TcConvQbar{}, partial, s);
+    dispatch_conv<KIND_FWD>(p, rows, e, TcConvQbar{}, s);
 }
 
 void launch_tc_conv_qbar(const TcConvPlan& p, int rows, const TcConvQbar& e, cudaStream_t s) {
     if (rows == 0) return;
-    dispatch_conv<KIND_QBAR>(p, rows, TcConvFwd{}, e, nullptr, s);
+    dispatch_conv<KIND_QBAR>(p, rows, TcConvFwd{}, e, s);
 }
 
 }  // namespace lb200

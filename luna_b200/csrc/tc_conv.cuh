@@ -44,11 +44,12 @@ struct TcConvPlan {
 };
 
 // Epilogue of a transposed-conv step: D[(phase, ci), t] is the A window of
-// the level below at v = s (t + tlo) - c + phase; relaxation of that level
-// (ConvRelaxEpi), per-row bias partials into partial[slot * rows + r].
+// the level below at v = s (t + tlo) - c + phase, stored raw into P [rows,
+// out_h * out_w * Ci] (the relaxation of that level streams through
+// launch_relax_window afterwards).
 struct TcConvFwd {
     int s = 1, Ci = 0, cy = 0, cx = 0, tlo_y = 0, tlo_x = 0, out_h = 0, out_w = 0;
-    ConvRelaxEpi f;
+    float* P = nullptr;
 };
 // Epilogue of a correlation step: Qbar[r, (qy * in_w + qx) * Co + co] =
 // D[co, q] + g[r] b[co].
@@ -64,10 +65,7 @@ struct TcConvQbar {
 bool tc_conv_supported(int data_C, int nx);
 // Tiling of a per-row pixel grid ny x nx over `rows` rows.
 void tc_conv_tile(TcConvPlan& p, int rows);
-// Slots of per-row partial sums a forward step writes: m_tiles * 4 * y_blocks.
-int tc_conv_fwd_slots(const TcConvPlan& p);
-
-void launch_tc_conv_fwd(const TcConvPlan& p, int rows, const TcConvFwd& e, float* partial, cudaStream_t s);
+void launch_tc_conv_fwd(const TcConvPlan& p, int rows, const TcConvFwd& e, cudaStream_t s);
 void launch_tc_conv_qbar(const TcConvPlan& p, int rows, const TcConvQbar& e, cudaStream_t s);
 
 }  // namespace lb200
