@@ -52,6 +52,8 @@ __device__ __forceinline__ float adam_clip_update(float a, float g, float& m, fl
 enum : uint8_t {
     RF_USE_ALPHA = 1,   // lower slope comes from the alpha tensor
     RF_UNSTABLE = 2,    // lb < 0 < ub now: k_up / b_up carry gradient to the bounds
+    RF_ASET = 4,        // in the alpha creation set: only these alphas ever take a
+                        // nonzero Adam step (the others keep m = v = 0)
 };
 
 }  // namespace lb200

@@ -336,9 +336,6 @@ __global__ void __launch_bounds__(256) relax_window_kernel(const float* __restri
         const size_t at = (size_t)r * nw + j0;
         const float4 p4 = *reinterpret_cast<const float4*>(P + at);
         const float Pv[4] = {p4.x, p4.y, p4.z, p4.w};
-        float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e.alpha) a4 = *reinterpret_cast<const float4*>(e.alpha + at);
-        const float Av[4] = {a4.x, a4.y, a4.z, a4.w};
         const int nu0 = win_neuron(e.g, oy, ox, j0);  // the 4 elements share a pixel
         float Qv[4] = {0.f, 0.f, 0.f, 0.f};
         if (nu0 >= 0) {
@@ -347,6 +344,10 @@ __global__ void __launch_bounds__(256) relax_window_kernel(const float* __restri
             const float4 k4 = *reinterpret_cast<const float4*>(e.rp.k_up + bj);
             const float4 b4 = *reinterpret_cast<const float4*>(e.rp.b_up + bj);
             const uchar4 f4 = *reinterpret_cast<const uchar4*>(e.rp.flags + bj);
+            float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e.alpha && ((f4.x | f4.y | f4.z | f4.w) & RF_USE_ALPHA))
+                a4 = *reinterpret_cast<const float4*>(e.alpha + at);
+            const float Av[4] = {a4.x, a4.y, a4.z, a4.w};
             const float sl[4] = {s4.x, s4.y, s4.z, s4.w}, ku[4] = {k4.x, k4.y, k4.z, k4.w},
                         bu[4] = {b4.x, b4.y, b4.z, b4.w};
             const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
@@ -469,7 +470,8 @@ __global__ void relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g, const float* _
     const float Qb = Qbar[idx];
     const float P = e.P_saved[idx];
     const float gr = e.gseed[r];
-    const float a = e.alpha ? e.alpha[idx] : 0.f;
+    const bool adam = e.adam_m && e.active && e.active[bx] && (f & RF_ASET);
+    const float a = (e.alpha && (use_alpha || adam)) ? e.alpha[idx] : 0.f;
     const float s = (e.alpha && use_alpha) ? a : sl;
     const bool pos = P >= 0.f, neg = P <= 0.f;
     const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
@@ -482,10 +484,10 @@ __global__ void relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g, const float* _
     const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
     if (un) {
         const float kv = Qb * (p == 0 ? Pn : Pp), bv = gr * (p == 0 ? Pn : Pp);
-        if (kv != 0.f) atomicAdd(e.kbar + bj, kv);
-        if (bv != 0.f) atomicAdd(e.bbar + bj, bv);
+        if (kv != 0.f) atomicAdd(e.kbar_d + bj, (double)kv);
+        if (bv != 0.f) atomicAdd(e.bbar_d + bj, (double)bv);
     }
-    if (e.adam_m && e.active && e.active[bx]) {
+    if (adam) {
         const float ag = use_alpha ? Qb * (p == 0 ? Pp : Pn) : 0.f;
         float mm = e.adam_m[idx], vv = e.adam_v[idx];
         e.alpha[idx] = adam_clip_update(a, ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
@@ -512,10 +514,24 @@ __device__ __forceinline__ float warp_allsum(float v) {
 }
 }  // namespace
 
+// Shared seed window of the first-conv adjoint: a zero halo of FK rows /
+// columns on each side, plus a segment of slack columns on the right so that
+// the last row segment's reads stay inside.
+constexpr int FSEG = 16;
+__host__ __device__ inline int first_seed_pw(int out_w) { return out_w + 2 * FK + FSEG; }
+__host__ __device__ inline int first_seed_ph(int out_h) { return out_h + 2 * FK + 1; }
+
 bool first_conv_fast(const ConvStep& cs) {
     return cs.kh == FK && cs.kw == FK && cs.Ci == FC && cs.Co <= 32 && cs.sh == 1 && cs.sw == 1 && cs.cy <= FK &&
-           cs.cx <= FK && (cs.out_h + 2 * FK + 1) * (cs.out_w + 2 * FK + 1) * FC * 4 <= 48 * 1024;
+           cs.cx <= FK && first_seed_ph(cs.out_h) * first_seed_pw(cs.out_w) * FC * 4 <= 48 * 1024;
 }
+
+// Warp task: one output row segment of FSEG pixels.  Lane = conv output
+// channel co (its 27 weights in registers); every loaded data column is used
+// by the three x-taps of its neighbouring pixels.  The per-lane partial sums
+// (FSEG pixels x 3 channels) are reduced across lanes by a transposed
+// butterfly: after the rounds over lane bits 16, 8, 4, 2 lane L holds the
+// three channels of pixel L >> 1, completed by a final exchange with L ^ 1.
 
 __global__ void __launch_bounds__(256) first_convT_conc_kernel(const float* __restrict__ A, ConvStep cs, int M,
                                                                ConvConcEpi e, float* __restrict__ partial) {
@@ -530,37 +546,83 @@ __global__ void __launch_bounds__(256) first_convT_conc_kernel(const float* __re
     const int nin = cs.in_h * cs.in_w * cs.Co;
     const int nw = e.g.size();
     const float* Arow = A + (size_t)r * nin;
+    const int co = lane;  // Co <= 32
+    const bool cok = co < cs.Co;
+    float w[FK * FK * FC];
+#pragma unroll
+    for (int t = 0; t < FK * FK; ++t)
+#pragma unroll
+        for (int ci = 0; ci < FC; ++ci) w[t * FC + ci] = cok ? cs.Wk[((size_t)t * cs.Co + co) * FC + ci] : 0.f;
     float part = 0.f;
-    {
-        const int co = lane;  // Co <= 32
-        const bool cok = co < cs.Co;
-        float w[FK * FK * FC];
+    const int nseg = (cs.out_w + FSEG - 1) / FSEG;
+    for (int task = warp; task < cs.out_h * nseg; task += 8) {
+        const int vy = task / nseg, x0 = (task - (task / nseg) * nseg) * FSEG;
+        float acc[FSEG * FC];
 #pragma unroll
-        for (int t = 0; t < FK * FK; ++t)
+        for (int i = 0; i < FSEG * FC; ++i) acc[i] = 0.f;
 #pragma unroll
-            for (int ci = 0; ci < FC; ++ci)
-                w[t * FC + ci] = cok ? cs.Wk[((size_t)t * cs.Co + co) * FC + ci] : 0.f;
-        for (int pix = warp; pix < cs.out_h * cs.out_w; pix += 8) {
-            const int vy = pix / cs.out_w, vx = pix - (pix / cs.out_w) * cs.out_w;
-            float acc[FC] = {0.f, 0.f, 0.f};
+        for (int c = 0; c < FSEG + FK - 1; ++c) {
+            const int qx = x0 + cs.cx - (FK - 1) + c;
+            const bool xok = cok && qx >= 0 && qx < cs.in_w;
+            float a[FK];
 #pragma unroll
             for (int ky = 0; ky < FK; ++ky) {
                 const int qy = vy + cs.cy - ky;
-                if (qy < 0 || qy >= cs.in_h) continue;
-#pragma unroll
-                for (int kx = 0; kx < FK; ++kx) {
-                    const int qx = vx + cs.cx - kx;
-                    if (qx < 0 || qx >= cs.in_w) continue;
-                    const float a = cok ? Arow[((size_t)qy * cs.in_w + qx) * cs.Co + co] : 0.f;
-#pragma unroll
-                    for (int ci = 0; ci < FC; ++ci) acc[ci] = fmaf(a, w[(ky * FK + kx) * FC + ci], acc[ci]);
-                }
+                a[ky] = (xok && qy >= 0 && qy < cs.in_h) ? Arow[((size_t)qy * cs.in_w + qx) * cs.Co + co] : 0.f;
             }
 #pragma unroll
-            for (int ci = 0; ci < FC; ++ci) acc[ci] = warp_allsum(acc[ci]);
-            if (lane < FC) {
-                const float P = lane == 0 ? acc[0] : (lane == 1 ? acc[1] : acc[2]);
-                const int j = pix * FC + lane;
+            for (int kx = 0; kx < FK; ++kx) {
+                const int pl = c - (FK - 1) + kx;
+                if (pl < 0 || pl >= FSEG) continue;
+#pragma unroll
+                for (int ky = 0; ky < FK; ++ky)
+#pragma unroll
+                    for (int ci = 0; ci < FC; ++ci)
+                        acc[pl * FC + ci] = fmaf(a[ky], w[(ky * FK + kx) * FC + ci], acc[pl * FC + ci]);
+            }
+        }
+        // Transposed butterfly over lane bits 16, 8, 4, 2.
+        float v24[24], v12[12], v6[6], v3[3];
+        {
+            const bool hi = lane & 16;
+#pragma unroll
+            for (int i = 0; i < 24; ++i) {
+                const float keep = hi ? acc[24 + i] : acc[i], send = hi ? acc[i] : acc[24 + i];
+                v24[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+        }
+        {
+            const bool hi = lane & 8;
+#pragma unroll
+            for (int i = 0; i < 12; ++i) {
+                const float keep = hi ? v24[12 + i] : v24[i], send = hi ? v24[i] : v24[12 + i];
+                v12[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+        }
+        {
+            const bool hi = lane & 4;
+#pragma unroll
+            for (int i = 0; i < 6; ++i) {
+                const float keep = hi ? v12[6 + i] : v12[i], send = hi ? v12[i] : v12[6 + i];
+                v6[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+        }
+        {
+            const bool hi = lane & 2;
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                const float keep = hi ? v6[3 + i] : v6[i], send = hi ? v6[i] : v6[3 + i];
+                v3[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 3; ++i) v3[i] += __shfl_xor_sync(0xffffffffu, v3[i], 1);
+        const int vx = x0 + (lane >> 1);
+        if ((lane & 1) == 0 && vx < cs.out_w) {
+#pragma unroll
+            for (int ci = 0; ci < FC; ++ci) {
+                const float P = v3[ci];
+                const int j = (vy * cs.out_w + vx) * FC + ci;
                 const int nu = win_neuron(e.g, oy, ox, j);
                 uint8_t sg = 0;
                 if (nu >= 0) {
@@ -598,9 +660,9 @@ __global__ void __launch_bounds__(256) first_conv_adj_kernel(RowMap rows, int M,
                                                              const float* __restrict__ xu, ConvStep cs,
                                                              const float* __restrict__ b,
                                                              float* __restrict__ Qbar) {
-    extern __shared__ float sP[];  // seed window with a zero halo of FK on each side
+    extern __shared__ float sP[];  // seed window (first_seed_ph x first_seed_pw x FC)
     const int r = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int PW = cs.out_w + 2 * FK + 1, PH = cs.out_h + 2 * FK + 1;
+    const int PW = first_seed_pw(cs.out_w), PH = first_seed_ph(cs.out_h);
     for (int i = threadIdx.x; i < PH * PW * FC; i += blockDim.x) sP[i] = 0.f;
     __syncthreads();
     int p, rr;
@@ -631,26 +693,43 @@ __global__ void __launch_bounds__(256) first_conv_adj_kernel(RowMap rows, int M,
         sP[((vy + FK) * PW + vx + FK) * FC + ci] = v;
     }
     __syncthreads();
-    const int nq = cs.in_h * cs.in_w;
-    for (int cb = 0; cb < cs.Co; cb += 32) {
-        const int co = cb + lane;
-        const bool cok = co < cs.Co;
-        float w[FK * FK * FC];
+    // Warp task: FSEG consecutive output pixels of one row; lane = co.  Each
+    // seed column is read once and used by the three x-taps that touch it.
+    const int co = lane;  // Co <= 32
+    const bool cok = co < cs.Co;
+    float w[FK * FK * FC];
 #pragma unroll
-        for (int t = 0; t < FK * FK * FC; ++t) w[t] = cok ? cs.Wc[(size_t)co * FK * FK * FC + t] : 0.f;
-        const float gb = cok ? gr * b[co] : 0.f;
-        for (int q = warp; q < nq; q += 8) {
-            const int qy = q / cs.in_w, qx = q - (q / cs.in_w) * cs.in_w;
-            const float* base = sP + ((qy - cs.cy + FK) * PW + qx - cs.cx + FK) * FC;
-            float acc = 0.f;
+    for (int t = 0; t < FK * FK * FC; ++t) w[t] = cok ? cs.Wc[(size_t)co * FK * FK * FC + t] : 0.f;
+    const float gb = cok ? gr * b[co] : 0.f;
+    const int nseg = (cs.in_w + FSEG - 1) / FSEG;
+    for (int task = warp; task < cs.in_h * nseg; task += 8) {
+        const int qy = task / nseg, x0 = (task - (task / nseg) * nseg) * FSEG;
+        const float* base = sP + ((qy - cs.cy + FK) * PW + x0 - cs.cx + FK) * FC;
+        float acc[FSEG];
+#pragma unroll
+        for (int i = 0; i < FSEG; ++i) acc[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < FSEG + FK - 1; ++c) {
+            float pv[FK * FC];
 #pragma unroll
             for (int ky = 0; ky < FK; ++ky)
 #pragma unroll
-                for (int kx = 0; kx < FK; ++kx)
+                for (int ci = 0; ci < FC; ++ci) pv[ky * FC + ci] = base[(ky * PW + c) * FC + ci];
+#pragma unroll
+            for (int kx = 0; kx < FK; ++kx) {
+                const int ql = c - kx;
+                if (ql < 0 || ql >= FSEG) continue;
+#pragma unroll
+                for (int ky = 0; ky < FK; ++ky)
 #pragma unroll
                     for (int ci = 0; ci < FC; ++ci)
-                        acc = fmaf(base[(ky * PW + kx) * FC + ci], w[(ky * FK + kx) * FC + ci], acc);
-            if (cok) Qbar[((size_t)r * nq + q) * cs.Co + co] = acc + gb;
+                        acc[ql] = fmaf(pv[ky * FC + ci], w[(ky * FK + kx) * FC + ci], acc[ql]);
+            }
+        }
+        if (cok) {
+#pragma unroll
+            for (int i = 0; i < FSEG; ++i)
+                if (x0 + i < cs.in_w) Qbar[((size_t)r * cs.in_h * cs.in_w + qy * cs.in_w + x0 + i) * cs.Co + co] = acc[i] + gb;
         }
     }
 }
@@ -659,8 +738,24 @@ void launch_first_conv_adj(const RowMap& rows, int M, const WinGeo& g0, int form
                            const float* gseed, const float* xl, const float* xu, const ConvStep& cs,
                            const float* b, float* Qbar, cudaStream_t s) {
     if (M == 0) return;
-    const size_t smem = (size_t)(cs.out_h + 2 * FK + 1) * (cs.out_w + 2 * FK + 1) * FC * 4;
+    const size_t smem = (size_t)first_seed_ph(cs.out_h) * first_seed_pw(cs.out_w) * FC * 4;
     first_conv_adj_kernel<<<M, 256, smem, s>>>(rows, M, g0, form, sign, gseed, xl, xu, cs, b, Qbar);
+    LB_LAUNCH();
+}
+
+__global__ void fold_double_kernel(double* __restrict__ sk, double* __restrict__ sb, float* __restrict__ dk,
+                                   float* __restrict__ db, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    dk[i] += (float)sk[i];
+    db[i] += (float)sb[i];
+    sk[i] = 0.0;
+    sb[i] = 0.0;
+}
+
+void launch_fold_double(double* src_k, double* src_b, float* dst_k, float* dst_b, int64_t n, cudaStream_t s) {
+    if (n == 0) return;
+    fold_double_kernel<<<ceil_div(n, 256), 256, 0, s>>>(src_k, src_b, dst_k, dst_b, n);
     LB_LAUNCH();
 }
 

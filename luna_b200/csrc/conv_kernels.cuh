@@ -151,6 +151,10 @@ void launch_first_conv_adj(const RowMap& rows, int M, const WinGeo& g0, int form
                            const float* gseed, const float* xl, const float* xu, const ConvStep& cs,
                            const float* b, float* Qbar, cudaStream_t s);
 
+// dst[i] += (float)src[i], src[i] = 0 for i < n (folds the double scratch of
+// launch_relax_adjoint_win into kbar / bbar).
+void launch_fold_double(double* src_k, double* src_b, float* dst_k, float* dst_b, int64_t n, cudaStream_t s);
+
 // alpha[p][r][j] = init_slope[box, neuron(r, j)] (0 outside the map).
 void launch_alpha_init_win(const RowMap& rows, const WinGeo& g, const float* init_slope, int n,
                            float* alpha, cudaStream_t s);

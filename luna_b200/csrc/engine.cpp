@@ -35,6 +35,11 @@ void* DevCache::get(const std::string& name, size_t bytes) {
     return b.p;
 }
 
+size_t DevCache::capacity(const std::string& name) const {
+    auto it = bufs_.find(name);
+    return it == bufs_.end() ? 0 : it->second.bytes;
+}
+
 size_t DevCache::total_bytes() const {
     size_t t = 0;
     for (auto& kv : bufs_) t += kv.second.bytes;
@@ -900,10 +905,20 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
                 launch_conv_adj_qbar(Pb[cur], cs, M, g, L.b, Qbar, s);
             }
             prof_end(s, fl);
-            if (sp.geo[m].full)
+            if (sp.geo[m].full) {
                 launch_relax_adjoint(e, Qbar, M, N, s);
-            else
+            } else {
+                const std::string kk = key("kbar_d", m), bk = key("bbar_d", m);
+                const bool fresh = cache_.capacity(kk) < (size_t)B * N * 8;
+                e.kbar_d = cache_.as<double>(kk, (size_t)B * N);
+                e.bbar_d = cache_.as<double>(bk, (size_t)B * N);
+                if (fresh) {
+                    LB_CUDA(cudaMemsetAsync(e.kbar_d, 0, (size_t)B * N * 8, s));
+                    LB_CUDA(cudaMemsetAsync(e.bbar_d, 0, (size_t)B * N * 8, s));
+                }
                 launch_relax_adjoint_win(e, sp.geo[m], Qbar, M, s);
+                launch_fold_double(e.kbar_d, e.bbar_d, e.kbar, e.bbar, (int64_t)B * N, s);
+            }
             cur = 1 - cur;
             continue;
         }

@@ -26,6 +26,7 @@ public:
         return static_cast<T*>(get(name, count * sizeof(T)));
     }
     size_t total_bytes() const;
+    size_t capacity(const std::string& name) const;
     void release();
 
 private:

@@ -198,6 +198,7 @@ __global__ void relu_params_kernel(const float* __restrict__ l, const float* __r
         slope_lo[idx] = active ? 1.f : 0.f;
         uint8_t f = 0;
         if (aset[idx] && !active) f |= RF_USE_ALPHA;
+        if (aset[idx]) f |= RF_ASET;
         if (!active && !inactive) f |= RF_UNSTABLE;
         flags[idx] = f;
     } else {
@@ -596,7 +597,8 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
                 const float P = e.gather_W ? e.gather_W[(size_t)e.rows.row_id[r - p * e.rows.R] * n + c]
                                            : e.P_saved[at];
                 const float g = e.gseed[r];
-                const float a = e.alpha ? e.alpha[at] : 0.f;
+                const bool adam = e.adam_m && act && (f & RF_ASET);
+                const float a = (e.alpha && (use_alpha || adam)) ? e.alpha[at] : 0.f;
                 const float s = (e.alpha && use_alpha) ? a : sl;
                 const bool pos = P >= 0.f, neg = P <= 0.f;
                 const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
@@ -611,7 +613,7 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
                     ks += Qb * (p == 0 ? Pn : Pp);
                     bs += g * (p == 0 ? Pn : Pp);
                 }
-                if (e.adam_m && act) {
+                if (adam) {
                     const float ag = use_alpha ? Qb * (p == 0 ? Pp : Pn) : 0.f;
                     float mm = e.adam_m[at], vv = e.adam_v[at];
                     e.alpha[at] = adam_clip_update(a, ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
@@ -663,10 +665,14 @@ __global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, co
         bu[0] = bu4.x; bu[1] = bu4.y; bu[2] = bu4.z; bu[3] = bu4.w;
         const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
         const bool act = e.active ? e.active[bx] != 0 : false;
-        const bool adam = am != nullptr && act;
+        // Alphas outside the creation set never move (zero gradient, zero
+        // moments): their 4-column group skips the Adam traffic.
+        const bool adam = am != nullptr && act && ((fl[0] | fl[1] | fl[2] | fl[3]) & RF_ASET);
+        const bool need_alpha = al != nullptr && (adam || ((fl[0] | fl[1] | fl[2] | fl[3]) & RF_USE_ALPHA));
         for (int p = 0; p < 2; ++p) {
             const int first = p * e.rows.R + e.rows.box_off[bx];
             const int last = min(p * e.rows.R + e.rows.box_off[bx + 1], M);
+#pragma unroll 2
             for (int r = first + ty; r < last; r += 8) {
                 const size_t at = (size_t)r * n + c;
                 const float4 q4 = *reinterpret_cast<const float4*>(Qbar + at);
@@ -674,7 +680,7 @@ __global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, co
                                      : *reinterpret_cast<const float4*>(Ps + at);
                 const float g = gs[r];
                 float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (al) a4 = *reinterpret_cast<const float4*>(al + at);
+                if (need_alpha) a4 = *reinterpret_cast<const float4*>(al + at);
                 float4 m4, v4;
                 if (adam) {
                     m4 = *reinterpret_cast<const float4*>(am + at);

@@ -150,6 +150,12 @@ struct EpiRelaxAdj {
     // Direct accumulators [B, N] (launch_relax_adjoint).
     float* kbar = nullptr;
     float* bbar = nullptr;
+    // Double-precision scratch [B, N] of launch_relax_adjoint_win: its
+    // atomics accumulate here (rounding error far below fp32 resolution, so
+    // the fp32 totals do not depend on the atomic order) and
+    // launch_fold_double adds the totals into kbar / bbar.
+    double* kbar_d = nullptr;
+    double* bbar_d = nullptr;
     // launch_relax_adjoint: when set, the pre-relaxation A of row r is the
     // weight row gather_W[row_id[r]] (ReLU directly below a one-hot start)
     // and P_saved is not read.
