@@ -3,6 +3,7 @@
 // adjoints).
 #include "conv_kernels.cuh"
 
+#include <algorithm>
 #include <stdexcept>
 
 namespace lb200 {
@@ -447,59 +448,155 @@ void launch_conv_adj_qbar(const float* Pbar, const ConvStep& cs, int M, const fl
     LB_LAUNCH();
 }
 
-__global__ void relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g, const float* __restrict__ Qbar, int M) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int nw = g.size();
-    if (idx >= (int64_t)M * nw) return;
-    const int r = (int)(idx / nw), j = (int)(idx - (int64_t)r * nw);
-    int p, rr;
-    row_split(r, e.rows.R, p, rr);
-    const int bx = e.rows.row_box[rr];
-    int oy, ox;
-    win_origin(g, e.rows.row_id[rr], oy, ox);
-    const int nu = win_neuron(g, oy, ox, j);
-    const int64_t pdst = e.ps.s ? phase_dst(e.ps, r, j) : idx;
-    if (nu < 0) {
-        if (e.Pbar) e.Pbar[pdst] = 0.f;
-        return;
+// Persistent blocks walk the rows; each block first tabulates, per window
+// pixel, its (wy, wx) and its pixel offset in the phase-split Pbar layout,
+// so the per-element work has no integer division.
+constexpr int WIN_MAX_PIX = 2048;
+
+__global__ void __launch_bounds__(256) relax_adjoint_win_kernel(EpiRelaxAdj e, WinGeo g,
+                                                                const float* __restrict__ Qbar, int M) {
+    __shared__ short2 pxy[WIN_MAX_PIX];
+    __shared__ int pdo[WIN_MAX_PIX];
+    const int npix = g.wh * g.ww, nw = g.size(), C = g.C;
+    for (int q = threadIdx.x; q < npix; q += blockDim.x) {
+        const int wy = q / g.ww, wx = q - (q / g.ww) * g.ww;
+        pxy[q] = make_short2((short)wy, (short)wx);
+        if (e.ps.s) {
+            const int vy = wy + e.ps.cy, vx = wx + e.ps.cx;
+            const int plane = (vy % e.ps.s) * e.ps.s + vx % e.ps.s;
+            pdo[q] = ((plane * e.ps.nty + vy / e.ps.s - e.ps.tlo_y) * e.ps.ntx + vx / e.ps.s - e.ps.tlo_x) * C;
+        } else {
+            pdo[q] = q * C;
+        }
     }
-    const size_t bj = (size_t)bx * e.rp.n + nu;
-    const uint8_t f = e.rp.flags[bj];
-    const float sl = e.rp.slope_lo[bj], k = e.rp.k_up[bj], b = e.rp.b_up[bj];
-    const bool use_alpha = (f & RF_USE_ALPHA) != 0, un = (f & RF_UNSTABLE) != 0;
-    const float Qb = Qbar[idx];
-    const float P = e.P_saved[idx];
-    const float gr = e.gseed[r];
-    const bool adam = e.adam_m && e.active && e.active[bx] && (f & RF_ASET);
-    const float a = (e.alpha && (use_alpha || adam)) ? e.alpha[idx] : 0.f;
-    const float s = (e.alpha && use_alpha) ? a : sl;
-    const bool pos = P >= 0.f, neg = P <= 0.f;
-    const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
-    const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
-    if (e.Pbar) {
-        const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
-        const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
-        e.Pbar[pdst] = Qb * dq + gr * db;
-    }
-    const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
-    if (un) {
-        const float kv = Qb * (p == 0 ? Pn : Pp), bv = gr * (p == 0 ? Pn : Pp);
-        if (kv != 0.f) atomicAdd(e.kbar_d + bj, (double)kv);
-        if (bv != 0.f) atomicAdd(e.bbar_d + bj, (double)bv);
-    }
-    if (adam) {
-        const float ag = use_alpha ? Qb * (p == 0 ? Pp : Pn) : 0.f;
-        float mm = e.adam_m[idx], vv = e.adam_v[idx];
-        e.alpha[idx] = adam_clip_update(a, ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
-        e.adam_m[idx] = mm;
-        e.adam_v[idx] = vv;
+    __syncthreads();
+    const bool cpow2 = (C & (C - 1)) == 0;
+    const int cshift = __ffs(C) - 1;
+    for (int r = blockIdx.x; r < M; r += gridDim.x) {
+        int p, rr;
+        row_split(r, e.rows.R, p, rr);
+        const int bx = e.rows.row_box[rr];
+        int oy, ox;
+        win_origin(g, e.rows.row_id[rr], oy, ox);
+        const float gr = e.gseed[r];
+        const bool act = e.active && e.active[bx];
+        const int64_t prow = e.ps.s ? (int64_t)r * e.ps.row_stride : (int64_t)r * nw;
+        if ((C & 3) == 0) {
+            // Four channels of one pixel per thread: float4 traffic.
+            for (int j = threadIdx.x * 4; j < nw; j += blockDim.x * 4) {
+                const int c = cpow2 ? (j & (C - 1)) : j % C, q = cpow2 ? (j >> cshift) : j / C;
+                const short2 w2 = pxy[q];
+                const int y = oy + w2.x, x = ox + w2.y;
+                const int64_t idx = (int64_t)r * nw + j;
+                float* pd = e.Pbar ? e.Pbar + prow + pdo[q] + c : nullptr;
+                if ((unsigned)y >= (unsigned)g.H || (unsigned)x >= (unsigned)g.W) {
+                    if (pd) *reinterpret_cast<float4*>(pd) = make_float4(0.f, 0.f, 0.f, 0.f);
+                    continue;
+                }
+                const size_t bj = (size_t)bx * e.rp.n + (y * g.W + x) * C + c;
+                const float4 q4 = *reinterpret_cast<const float4*>(Qbar + idx);
+                const float4 p4 = *reinterpret_cast<const float4*>(e.P_saved + idx);
+                const float4 s4 = *reinterpret_cast<const float4*>(e.rp.slope_lo + bj);
+                const float4 k4 = *reinterpret_cast<const float4*>(e.rp.k_up + bj);
+                const float4 b4 = *reinterpret_cast<const float4*>(e.rp.b_up + bj);
+                const uchar4 f4 = *reinterpret_cast<const uchar4*>(e.rp.flags + bj);
+                const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
+                const uint8_t fany = f4.x | f4.y | f4.z | f4.w;
+                const bool adam = e.adam_m && act && (fany & RF_ASET);
+                float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (e.alpha && (adam || (fany & RF_USE_ALPHA))) a4 = *reinterpret_cast<const float4*>(e.alpha + idx);
+                float4 m4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = m4;
+                if (adam) {
+                    m4 = *reinterpret_cast<const float4*>(e.adam_m + idx);
+                    v4 = *reinterpret_cast<const float4*>(e.adam_v + idx);
+                }
+                const float Qv[4] = {q4.x, q4.y, q4.z, q4.w}, Pv[4] = {p4.x, p4.y, p4.z, p4.w};
+                const float sl[4] = {s4.x, s4.y, s4.z, s4.w}, ku[4] = {k4.x, k4.y, k4.z, k4.w},
+                            bu[4] = {b4.x, b4.y, b4.z, b4.w};
+                float Av[4] = {a4.x, a4.y, a4.z, a4.w}, Mv[4] = {m4.x, m4.y, m4.z, m4.w},
+                      Vv[4] = {v4.x, v4.y, v4.z, v4.w}, out[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const bool use_alpha = (fl[i] & RF_USE_ALPHA) != 0, un = (fl[i] & RF_UNSTABLE) != 0;
+                    const float sv = (e.alpha && use_alpha) ? Av[i] : sl[i];
+                    const bool pos = Pv[i] >= 0.f, neg = Pv[i] <= 0.f;
+                    const float sP = p == 0 ? sv : ku[i], sN = p == 0 ? ku[i] : sv;
+                    const float bP = p == 0 ? 0.f : bu[i], bN = p == 0 ? bu[i] : 0.f;
+                    const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
+                    const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
+                    out[i] = Qv[i] * dq + gr * db;
+                    const float Pp = fmaxf(Pv[i], 0.f), Pn = fminf(Pv[i], 0.f);
+                    if (un) {
+                        const float kv = Qv[i] * (p == 0 ? Pn : Pp), bv = gr * (p == 0 ? Pn : Pp);
+                        if (kv != 0.f) atomicAdd(e.kbar_d + bj + i, (double)kv);
+                        if (bv != 0.f) atomicAdd(e.bbar_d + bj + i, (double)bv);
+                    }
+                    if (adam) {
+                        const float ag = use_alpha ? Qv[i] * (p == 0 ? Pp : Pn) : 0.f;
+                        Av[i] = adam_clip_update(Av[i], ag, Mv[i], Vv[i], e.adam_step, e.adam_bc2_sqrt);
+                    }
+                }
+                if (pd) *reinterpret_cast<float4*>(pd) = make_float4(out[0], out[1], out[2], out[3]);
+                if (adam) {
+                    *reinterpret_cast<float4*>(e.alpha + idx) = make_float4(Av[0], Av[1], Av[2], Av[3]);
+                    *reinterpret_cast<float4*>(e.adam_m + idx) = make_float4(Mv[0], Mv[1], Mv[2], Mv[3]);
+                    *reinterpret_cast<float4*>(e.adam_v + idx) = make_float4(Vv[0], Vv[1], Vv[2], Vv[3]);
+                }
+            }
+            continue;
+        }
+        for (int j = threadIdx.x; j < nw; j += blockDim.x) {
+            const int c = cpow2 ? (j & (C - 1)) : j % C, q = cpow2 ? (j >> cshift) : j / C;
+            const short2 w2 = pxy[q];
+            const int y = oy + w2.x, x = ox + w2.y;
+            const int64_t idx = (int64_t)r * nw + j;
+            const int64_t pdst = prow + pdo[q] + c;
+            if ((unsigned)y >= (unsigned)g.H || (unsigned)x >= (unsigned)g.W) {
+                if (e.Pbar) e.Pbar[pdst] = 0.f;
+                continue;
+            }
+            const size_t bj = (size_t)bx * e.rp.n + (y * g.W + x) * C + c;
+            const uint8_t f = e.rp.flags[bj];
+            const float sl = e.rp.slope_lo[bj], k = e.rp.k_up[bj], b = e.rp.b_up[bj];
+            const bool use_alpha = (f & RF_USE_ALPHA) != 0, un = (f & RF_UNSTABLE) != 0;
+            const float Qb = Qbar[idx];
+            const float P = e.P_saved[idx];
+            const bool adam = e.adam_m && act && (f & RF_ASET);
+            const float a = (e.alpha && (use_alpha || adam)) ? e.alpha[idx] : 0.f;
+            const float sv = (e.alpha && use_alpha) ? a : sl;
+            const bool pos = P >= 0.f, neg = P <= 0.f;
+            const float sP = p == 0 ? sv : k, sN = p == 0 ? k : sv;
+            const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
+            if (e.Pbar) {
+                const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
+                const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
+                e.Pbar[pdst] = Qb * dq + gr * db;
+            }
+            const float Pp = fmaxf(P, 0.f), Pn = fminf(P, 0.f);
+            if (un) {
+                const float kv = Qb * (p == 0 ? Pn : Pp), bv = gr * (p == 0 ? Pn : Pp);
+                if (kv != 0.f) atomicAdd(e.kbar_d + bj, (double)kv);
+                if (bv != 0.f) atomicAdd(e.bbar_d + bj, (double)bv);
+            }
+            if (adam) {
+                const float ag = use_alpha ? Qb * (p == 0 ? Pp : Pn) : 0.f;
+                float mm = e.adam_m[idx], vv = e.adam_v[idx];
+                e.alpha[idx] = adam_clip_update(a, ag, mm, vv, e.adam_step, e.adam_bc2_sqrt);
+                e.adam_m[idx] = mm;
+                e.adam_v[idx] = vv;
+            }
+        }
     }
 }
 
 void launch_relax_adjoint_win(const EpiRelaxAdj& e, const WinGeo& g, const float* Qbar, int M, cudaStream_t s) {
-    const int64_t total = (int64_t)M * g.size();
-    if (total == 0) return;
-    relax_adjoint_win_kernel<<<ceil_div(total, 256), 256, 0, s>>>(e, g, Qbar, M);
+    if ((int64_t)M * g.size() == 0) return;
+    if (g.wh * g.ww > WIN_MAX_PIX) throw std::invalid_argument("relax_adjoint_win: window too large");
+    int dev = 0, sms = 0;
+    LB_CUDA(cudaGetDevice(&dev));
+    LB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = std::min(M, sms * 8);
+    relax_adjoint_win_kernel<<<grid, 256, 0, s>>>(e, g, Qbar, M);
     LB_LAUNCH();
 }
 

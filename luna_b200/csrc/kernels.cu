@@ -639,7 +639,7 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
 
 // Vectorised variant (n % 4 == 0): one CTA per (box, 128 columns); 256
 // threads = 32 column lanes of 4 columns x 8 row lanes; float4 traffic.
-__global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, const float* __restrict__ Qbar,
+__global__ void __launch_bounds__(256, 3) relax_adjoint_v4_kernel(EpiRelaxAdj e, const float* __restrict__ Qbar,
                                                                int M, int n) {
     const int bx = blockIdx.x;
     const int c = blockIdx.y * 128 + (threadIdx.x & 31) * 4;
@@ -669,6 +669,9 @@ __global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, co
         // moments): their 4-column group skips the Adam traffic.
         const bool adam = am != nullptr && act && ((fl[0] | fl[1] | fl[2] | fl[3]) & RF_ASET);
         const bool need_alpha = al != nullptr && (adam || ((fl[0] | fl[1] | fl[2] | fl[3]) & RF_USE_ALPHA));
+        // Column part of the Pbar address (fixed for this thread).
+        const int64_t pcol = (pb && e.ps.s) ? phase_dst(e.ps, 0, c) : (int64_t)c;
+        const int64_t pstride = e.ps.s ? e.ps.row_stride : (int64_t)n;
         for (int p = 0; p < 2; ++p) {
             const int first = p * e.rows.R + e.rows.box_off[bx];
             const int last = min(p * e.rows.R + e.rows.box_off[bx + 1], M);
@@ -716,7 +719,7 @@ __global__ void __launch_bounds__(256) relax_adjoint_v4_kernel(EpiRelaxAdj e, co
                     }
                 }
                 if (pb)
-                    *reinterpret_cast<float4*>(pb + (e.ps.s ? phase_dst(e.ps, r, c) : (int64_t)at)) =
+                    *reinterpret_cast<float4*>(pb + (int64_t)r * pstride + pcol) =
                         make_float4(out[0], out[1], out[2], out[3]);
                 if (adam) {
                     *reinterpret_cast<float4*>(al + at) = make_float4(A[0], A[1], A[2], A[3]);
