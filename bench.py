@@ -10,10 +10,13 @@ A step bounds one batch of 512 boxes per GPU.  With N GPUs (torchrun) each
 rank bounds its own 512 boxes (weak scaling) and the final bounds are
 all-gathered over NCCL inside the step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload mlp|cnn]
 
 `--impl reference` times Luna's own CPU implementation (oracle/_ref) on the
-host cores for the same workload and metric.
+host cores for the same workload and metric.  `--workload cnn` measures the
+CIFAR-shaped CNN instead (3x32x32 -> conv32 k3 -> conv64 k4s2 -> conv64 k4s2
+-> 512 -> 10, He-normal weights, seed 2; 256 boxes per GPU, eps 2/255, 9
+margin rows; alpha-CROWN 30 iterations at Luna's default lr 0.5).
 """
 from __future__ import annotations
 
@@ -41,10 +44,10 @@ L2_FLUSH_BYTES = 256 << 20
 
 # Workloads: the MLP (the default) and the CIFAR-shaped CNN.
 WORKLOADS = {
-    "mlp": dict(gen=W.mlp_784_256x4_10, boxes=512, iters=20, lr=0.1, input_dim=784,
+    "mlp": dict(name="mlp", gen=W.mlp_784_256x4_10, boxes=512, iters=20, lr=0.1, input_dim=784,
                 desc="mlp_784_256x4_10 alpha-CROWN (20 Adam iterations, lr 0.1), {b} boxes per GPU, "
                      "eps 0.02, 9 margin specs"),
-    "cnn": dict(gen=W.cnn_cifar, boxes=256, iters=30, lr=0.5, input_dim=3072,
+    "cnn": dict(name="cnn", gen=W.cnn_cifar, boxes=256, iters=30, lr=0.5, input_dim=3072,
                 desc="cnn_cifar 3x32x32 conv32-conv64s2-conv64s2-fc512-fc10 alpha-CROWN (30 Adam "
                      "iterations, lr 0.5), {b} boxes per GPU, eps 2/255, 9 margin specs"),
 }
@@ -136,12 +139,12 @@ def peaks():
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def traffic_per_launch():
-    """DRAM bytes per launch of the contraction kernel from the committed ncu summary."""
+def traffic_per_launch(workload):
+    """DRAM bytes per contraction launch of `workload` from the committed ncu summary."""
     try:
         with open(os.path.join(ROOT, "profiles", "contraction_traffic.json")) as f:
-            return json.load(f)
-    except OSError:
+            return json.load(f).get(workload)
+    except (OSError, ValueError):
         return None
 
 
@@ -251,7 +254,7 @@ def run_engine(args):
         # the split issues three MMAs per product.
         peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
         achieved = (contr_flops / contr_launches) / (contr_ms / contr_launches) / 1e9 if contr_launches else 0.0
-        tr = traffic_per_launch()
+        tr = traffic_per_launch(WL["name"])
         line = {
             "metric": METRIC, "value": world * B / (ms_per_step / 1e3), "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -314,7 +317,7 @@ class CpuBaseline:
     def __init__(self, procs=None):
         self.procs = procs or min(os.cpu_count() or 1, BOXES_PER_GPU)
         self.pool = mp.get_context("spawn").Pool(self.procs)
-        self.name = next(k for k, v in WORKLOADS.items() if v["gen"] is WL["gen"])
+        self.name = WL["name"]
         # Load the library and the workload in every worker.
         self.pool.map(_ref_worker, [(self.name, BOXES_PER_GPU, 0, 0)] * self.procs)
 
