@@ -76,6 +76,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
     int cur = g->input_index;
     bool expect_affine = true;
     std::vector<int> affine;
+    std::vector<int> bn_after;  // BatchNorm node folded into affine[k], or -1
     while (true) {
         if (cur == g->output_index) break;
         if (dependents[cur].size() != 1)
@@ -89,8 +90,18 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
             if (!expect_affine) throw std::invalid_argument("two affine nodes without a ReLU between");
             if (!d.weight) throw std::invalid_argument("affine node without weight");
             affine.push_back(nx);
+            bn_after.push_back(-1);
             expect_affine = false;
             preact_node_ids_.push_back(nx);
+        } else if (d.type == LB200_NODE_BATCHNORM) {
+            // Folded into the affine layer before it (an affine map of an
+            // affine map; BoundedBatchNormNode.cpp:68-80,180-532).
+            if (expect_affine || bn_after.empty() || bn_after.back() >= 0)
+                throw std::invalid_argument("BatchNorm must directly follow a Linear or Conv node");
+            if (!d.weight || !d.bias || !d.running_mean || !d.running_var)
+                throw std::invalid_argument("BatchNorm node without parameters");
+            bn_after.back() = nx;
+            preact_node_ids_.back() = nx;
         } else if (d.type == LB200_NODE_RELU) {
             if (expect_affine) throw std::invalid_argument("ReLU must follow a Linear or Conv node");
             expect_affine = true;
@@ -101,7 +112,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         cur = nx;
     }
     const int out_t = g->nodes[g->output_index].type;
-    if (out_t != LB200_NODE_LINEAR || expect_affine)
+    if (out_t != LB200_NODE_LINEAR || expect_affine || bn_after.back() >= 0)
         throw std::invalid_argument("the output node must be the last Linear of the chain");
     if (affine.size() < 2) throw std::invalid_argument("need at least two affine layers");
     preact_node_ids_.pop_back();  // the output layer feeds no ReLU
@@ -144,7 +155,24 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         L.n_in = L.in.n();
         L.n_out = L.out.n();
         const int Ci = L.in.C, Co = L.out.C;
-        std::vector<float> W, Wt, b(L.conv ? Co : L.n_out, 0.f), bn(L.n_out, 0.f);
+        // The node's weight and bias with a following BatchNorm folded in:
+        // y = w (affine(x)) + (B - mean w), w = scale / sqrt(var + eps) per
+        // output channel (conv) or feature (Linear), computed in fp32 as
+        // BoundedBatchNormNode::ensureCachedParams does (:68-80).
+        const int nch = L.conv ? Co : L.n_out;
+        const size_t per_ch = L.conv ? (size_t)Ci * L.kh * L.kw : (size_t)L.n_in;
+        std::vector<float> wsrc(d.weight, d.weight + (size_t)nch * per_ch), bsrc(nch, 0.f);
+        if (d.bias)
+            for (int c = 0; c < nch; ++c) bsrc[c] = d.bias[c];
+        if (bn_after[k] >= 0) {
+            const auto& nb = g->nodes[bn_after[k]];
+            for (int c = 0; c < nch; ++c) {
+                const float w = nb.weight[c] / std::sqrt(nb.running_var[c] + nb.eps);
+                for (size_t q = 0; q < per_ch; ++q) wsrc[(size_t)c * per_ch + q] *= w;
+                bsrc[c] = bsrc[c] * w + (nb.bias[c] - nb.running_mean[c] * w);
+            }
+        }
+        std::vector<float> W, Wt, b(bsrc), bn(L.n_out, 0.f);
         if (L.conv) {
             // ONNX Conv weight [Co, Ci, kh, kw] -> Wc [Co][kh][kw][Ci], Wk [kh][kw][Co][Ci].
             W.resize((size_t)Co * L.kh * L.kw * Ci);
@@ -153,12 +181,10 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
                 for (int c = 0; c < Ci; ++c)
                     for (int y = 0; y < L.kh; ++y)
                         for (int x = 0; x < L.kw; ++x) {
-                            const float w = d.weight[(((size_t)o * Ci + c) * L.kh + y) * L.kw + x];
+                            const float w = wsrc[(((size_t)o * Ci + c) * L.kh + y) * L.kw + x];
                             W[(((size_t)o * L.kh + y) * L.kw + x) * Ci + c] = w;
                             Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
                         }
-            if (d.bias)
-                for (int o = 0; o < Co; ++o) b[o] = d.bias[o];
             for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
         } else {
             W.resize((size_t)L.n_out * L.n_in);
@@ -170,12 +196,10 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
                     // its CHW index when the input is a flattened conv map.
                     const int col = L.in.spatial ? (i % Ci) * HW + i / Ci : i;
                     // BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
-                    const float w = d.scale * d.weight[(size_t)o * L.n_in + col];
+                    const float w = d.scale * wsrc[(size_t)o * L.n_in + col];
                     W[(size_t)o * L.n_in + i] = w;
                     Wt[(size_t)i * L.n_out + o] = w;
                 }
-            if (d.bias)
-                for (int o = 0; o < L.n_out; ++o) b[o] = d.bias[o];
             bn = b;
         }
         L.W = weights_.as<float>(key("W", k), W.size());
@@ -186,7 +210,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
         LB_CUDA(cudaMemcpy(L.b_neuron, bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
-        if (L.conv) build_tc_conv(L, d.weight, k);
+        if (L.conv) build_tc_conv(L, wsrc.data(), k);
         if (!L.conv) {
             L.W_hi = weights_.as<float>(key("Whi", k), W.size());
             L.W_lo = weights_.as<float>(key("Wlo", k), W.size());

@@ -10,7 +10,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .abi import NODE_CONV, NODE_FLATTEN, NODE_INPUT, NODE_LINEAR, NODE_RELU, Graph, Node
+from .abi import NODE_BATCHNORM, NODE_CONV, NODE_FLATTEN, NODE_INPUT, NODE_LINEAR, NODE_RELU, Graph, Node
 
 
 def mlp(widths, seed: int, bias_std: float = 0.01) -> Graph:
@@ -37,16 +37,19 @@ def conv_out(h: int, k: int, s: int, p: int) -> int:
 def cnn(input_shape, layers, seed: int, bias_std: float = 0.01) -> Graph:
     """Input (C, H, W) -> layers -> output, ReLU after every layer but the last.
 
-    `layers` items are ("conv", C_out, k, stride, pad) or ("linear", n_out);
-    a Flatten node is inserted where a conv feeds a linear layer.  Weights
-    are He-normal over the fan-in (C_in k k for a conv), biases N(0, bias_std^2),
-    drawn layer by layer from one PCG64 stream."""
+    `layers` items are ("conv", C_out, k, stride, pad), ("convbn", C_out, k,
+    stride, pad) -- a conv followed by BatchNorm -- or ("linear", n_out); a
+    Flatten node is inserted where a conv feeds a linear layer.  Weights are
+    He-normal over the fan-in (C_in k k for a conv), biases N(0, bias_std^2);
+    BatchNorm gamma ~ U[0.5, 1.5], beta ~ N(0, 0.1^2), running mean ~ N(0,
+    0.1^2), running var ~ U[0.5, 2]; drawn layer by layer from one PCG64
+    stream."""
     rng = np.random.Generator(np.random.PCG64(seed))
     nodes = [Node(NODE_INPUT, [], tuple(input_shape))]
     shape = tuple(input_shape)
     for li, spec in enumerate(layers):
         last = li == len(layers) - 1
-        if spec[0] == "conv":
+        if spec[0] in ("conv", "convbn"):
             _, co, k, s, p = spec
             ci, h, w = shape
             fan_in = ci * k * k
@@ -55,6 +58,13 @@ def cnn(input_shape, layers, seed: int, bias_std: float = 0.01) -> Graph:
             shape = (co, conv_out(h, k, s, p), conv_out(w, k, s, p))
             nodes.append(Node(NODE_CONV, [len(nodes) - 1], shape, weight=wt, bias=b,
                               kernel=(k, k), stride=(s, s), padding=(p, p)))
+            if spec[0] == "convbn":
+                gamma = rng.uniform(0.5, 1.5, co).astype(np.float32)
+                beta = (rng.standard_normal(co) * 0.1).astype(np.float32)
+                mean = (rng.standard_normal(co) * 0.1).astype(np.float32)
+                var = rng.uniform(0.5, 2.0, co).astype(np.float32)
+                nodes.append(Node(NODE_BATCHNORM, [len(nodes) - 1], shape, weight=gamma, bias=beta,
+                                  running_mean=mean, running_var=var, eps=1e-5))
         elif spec[0] == "linear":
             n_out = spec[1]
             if shape[1] != 1 or shape[2] != 1:
@@ -173,9 +183,10 @@ def random_mlp_case(seed: int, n_boxes: int = 8, depth: int = 3, width: int = 12
     return g, Boxes((c - r).astype(np.float32), (c + r).astype(np.float32), margin_spec(t, n_out))
 
 
-def random_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.05):
+def random_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.05, bn: bool = False):
     """Small random CNN (kernel 2..5, stride 1..2, padding 0..2, 1-3 convs,
-    1-2 linear layers) and boxes for parity fuzzing."""
+    1-2 linear layers; with bn every conv is followed by BatchNorm) and boxes
+    for parity fuzzing."""
     rng = np.random.Generator(np.random.PCG64(seed))
     c, h = int(rng.integers(1, 4)), int(rng.integers(7, 13))
     layers = []
@@ -186,10 +197,10 @@ def random_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.05):
         p = int(rng.integers(0, min(3, k)))
         if conv_out(hh, k, s, p) < 2:
             break
-        layers.append(("conv", int(rng.integers(2, 7)), k, s, p))
+        layers.append(("convbn" if bn else "conv", int(rng.integers(2, 7)), k, s, p))
         hh = conv_out(hh, k, s, p)
     if not layers:
-        layers.append(("conv", 3, 3, 1, 1))
+        layers.append(("convbn" if bn else "conv", 3, 3, 1, 1))
     for _ in range(int(rng.integers(1, 3))):
         layers.append(("linear", int(rng.integers(4, 17))))
     layers.append(("linear", 3))
@@ -205,3 +216,14 @@ def cnn_wide_case(seed: int, n_boxes: int = 3, eps: float = 0.01, hw: int = 12):
     g = cnn((3, hw, hw), [("conv", 32, 3, 1, 1), ("conv", 32, 4, 2, 1), ("conv", 64, 4, 2, 1),
                           ("linear", 16), ("linear", 4)], seed + 5, bias_std=0.05)
     return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)
+
+
+def small_cnn_bn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, big_first: bool = True):
+    """Small CNN with BatchNorm after every conv; with big_first the first
+    BatchNorm output has more than 4096 features (a patches start on Luna's
+    CPU path)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    hw = 24 if big_first else 10
+    g = cnn((3, hw, hw), [("convbn", 8, 3, 1, 1), ("convbn", 16, 4, 2, 1), ("convbn", 8, 3, 1, 1),
+                          ("linear", 24), ("linear", 5)], seed + 7, bias_std=0.1)
+    return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 5)

@@ -11,7 +11,7 @@ behaviour it restates.  Per-box state follows Luna's: IBP bounds, "node
 bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
 parameters keyed by (activation node, start node), and STE reference bounds.
 
-Supported node kinds: Input, Linear, Conv2d, ReLU, Flatten, Identity.  A
+Supported node kinds: Input, Linear, Conv2d, BatchNorm, ReLU, Flatten, Identity.  A
 matrices are kept dense over the flattened (C, H, W) features; Luna's
 patches mode (CROWNAnalysis.cpp:255-405, BoundedConvNode.cpp:556-709) is the
 same arithmetic on a window of those features, and it is tracked only to
@@ -26,9 +26,9 @@ import torch
 
 import torch.nn.functional as F
 
-from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_CONV,
-                           NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT, NODE_LINEAR, NODE_RELU,
-                           Options, default_options)
+from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_BATCHNORM,
+                           NODE_CONV, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT, NODE_LINEAR,
+                           NODE_RELU, Options, default_options)
 
 # Dense identity starts above this many conv output features switch to
 # patches on Luna's CPU path (CROWNAnalysis.cpp:257,269).
@@ -116,6 +116,16 @@ class LirpaOracle:
                 self.W[i] = torch.from_numpy(np.asarray(nd.weight, np.float32))
                 self.b[i] = (torch.from_numpy(np.asarray(nd.bias, np.float32))
                              if nd.bias is not None else torch.zeros(nd.weight.shape[0]))
+            elif nd.type == NODE_BATCHNORM:
+                # BoundedBatchNormNode::ensureCachedParams (BoundedBatchNormNode.cpp:68-80):
+                # w = scale / sqrt(var + eps), b = B - mean * w, per channel,
+                # repeated over the spatial positions of a flat CHW input (:94-116).
+                f = lambda a: torch.from_numpy(np.asarray(a, np.float32))
+                w = f(nd.weight) / torch.sqrt(f(nd.running_var) + np.float32(nd.eps))
+                b = f(nd.bias) - f(nd.running_mean) * w
+                spatial = nd.size // w.numel()
+                self.W[i] = w.repeat_interleave(spatial)
+                self.b[i] = b.repeat_interleave(spatial)
             elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_FLATTEN, NODE_IDENTITY):
                 raise NotImplementedError(f"oracle: node type {nd.type}")
         self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type == NODE_RELU]
@@ -144,6 +154,12 @@ class LirpaOracle:
             lo = (conv(l, Wp) + conv(u, Wn)) + b
             hi = (conv(u, Wp) + conv(l, Wn)) + b
             return lo.flatten(), hi.flatten()
+        if nd.type == NODE_BATCHNORM:
+            # BoundedBatchNormNode::computeIntervalBoundPropagation (:151-178).
+            l, u = ins[0]
+            w, b = self.W[i], self.b[i]
+            wp, wn = torch.clamp_min(w, 0), torch.clamp_max(w, 0)
+            return wp * l + wn * u + b, wp * u + wn * l + b
         if nd.type == NODE_RELU:
             l, u = ins[0]
             return torch.clamp_min(l, 0), torch.clamp_min(u, 0)
@@ -277,10 +293,15 @@ class LirpaOracle:
         return out.reshape(spec, -1), bias
 
     def _starts_in_patches(self, start, is_output):
-        """usePatchesInit on the CPU path (CROWNAnalysis.cpp:255-298)."""
+        """usePatchesInit on the CPU path (CROWNAnalysis.cpp:255-298): a conv
+        start, or a BatchNorm start whose producer is a conv, with more than
+        4096 output features."""
         nd = self.g.nodes[start]
-        return (bool(self.opt.use_patches_mode) and not is_output and nd.type == NODE_CONV
-                and nd.size > PATCHES_SIZE_THRESHOLD)
+        if not self.opt.use_patches_mode or is_output or nd.size <= PATCHES_SIZE_THRESHOLD:
+            return False
+        if nd.type == NODE_CONV:
+            return True
+        return nd.type == NODE_BATCHNORM and self.g.nodes[nd.inputs[0]].type == NODE_CONV
 
     def _backward_from(self, st, start, x, rows=None, C=None):
         """CROWNAnalysis::backwardFrom (src/engine/CROWNAnalysis.cpp:231-706) for
@@ -328,6 +349,14 @@ class LirpaOracle:
                     out = [(torch.matmul(a_l, W), torch.matmul(a_u, W))]
                     nb_l = (a_l * bb).sum(-1)
                     nb_u = (a_u * bb).sum(-1)
+                elif nd.type == NODE_BATCHNORM:
+                    # BoundedBatchNormNode::boundOneSideTensor (:180-361): A w, bias A b.
+                    w, bb = self.W[c], self.b[c]
+                    out = [(a_l * w, a_u * w)]
+                    nb_l = (a_l * bb).sum(-1)
+                    nb_u = (a_u * bb).sum(-1)
+                    if patches and pwidth is None:
+                        pwidth = 1  # identity patches become 1x1 channel-diagonal patches (:389-420)
                 elif nd.type == NODE_CONV:
                     nl, nb_l = self._conv_backward(c, a_l)
                     nu, nb_u = self._conv_backward(c, a_u)

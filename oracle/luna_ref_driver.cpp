@@ -23,6 +23,7 @@
 #include "nodes/BoundedFlattenNode.h"
 #include "nodes/BoundedIdentityNode.h"
 #include "nodes/BoundedConvNode.h"
+#include "nodes/BoundedBatchNormNode.h"
 #include "input_parsers/Operations.h"
 
 #include <torch/torch.h>
@@ -105,6 +106,18 @@ std::shared_ptr<NLR::TorchModel> build_model(const lb200_graph_desc* g) {
             cn->setInputShape({1, (int)Ci, (int)H, (int)W});
             cn->setOutputShape({1, (int)Co, d.out_shape[1], d.out_shape[2]});
             node = cn;
+            break;
+        }
+        case LB200_NODE_BATCHNORM: {
+            // OnnxToTorchParser's BatchNormalization (OnnxToTorch.cpp:2173-2200):
+            // per-channel scale, B, mean, var; flat sizes.
+            const int64_t C = d.out_shape[0];
+            auto bn = std::make_shared<NLR::BoundedBatchNormNode>(
+                from_host(d.weight, {C}), from_host(d.bias, {C}), from_host(d.running_mean, {C}),
+                from_host(d.running_var, {C}), d.eps);
+            bn->setInputSize((unsigned)out_numel);
+            bn->setOutputSize((unsigned)out_numel);
+            node = bn;
             break;
         }
         case LB200_NODE_RELU:

@@ -59,6 +59,15 @@ def cases():
     out.append(("cnn_patch_crown", "small_cnn_case", kw, 3, abi.METHOD_CROWN, {}))
     out.append(("cnn_patch_alpha", "small_cnn_case", kw, 2, abi.METHOD_ALPHA_CROWN,
                 {"alpha_lr": 0.1, "alpha_iterations": 5}))
+    # BatchNorm after every conv: dense starts, and a patches start.
+    kw = {"seed": 4, "n_boxes": 3, "big_first": False}
+    out.append(("cnnbn_dense_crown", "small_cnn_bn_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("cnnbn_dense_alpha", "small_cnn_bn_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 6}))
+    kw = {"seed": 6, "n_boxes": 2, "big_first": True}
+    out.append(("cnnbn_patch_crown", "small_cnn_bn_case", kw, 2, abi.METHOD_CROWN, {}))
+    out.append(("cnnbn_patch_alpha", "small_cnn_bn_case", kw, 2, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 4}))
     # The CIFAR-shaped CNN at full size, one box.
     out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
     return out

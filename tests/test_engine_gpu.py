@@ -53,16 +53,18 @@ def test_engine_matches_oracle_random(seed, method):
     assert G.excess(ub, oub) <= 1.0
 
 
+@pytest.mark.parametrize("bn", [False, True])
 @pytest.mark.parametrize("seed", range(8))
 @pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
-def test_cnn_matches_oracle_random(seed, method):
-    """Random conv geometries (kernel 2-5, stride 1-2, padding 0-2) against the oracle."""
+def test_cnn_matches_oracle_random(seed, method, bn):
+    """Random conv geometries (kernel 2-5, stride 1-2, padding 0-2), with and
+    without BatchNorm after each conv, against the oracle."""
     from oracle.lirpa_oracle import LirpaOracle
-    g, bx = W.random_cnn_case(seed)
+    g, bx = W.random_cnn_case(seed, bn=bn)
     opt = abi.default_options(alpha_lr=0.3, alpha_iterations=6)
     lb, ub = Model(g, options=opt).compute_bounds(bx, method)
     olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
-    _assert_parity(f"cnn{seed}/{method}", lb, ub, olb, oub)
+    _assert_parity(f"cnn{seed}/{method}/bn{int(bn)}", lb, ub, olb, oub)
 
 
 @pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
@@ -94,6 +96,11 @@ def _forward(graph, x):
             x = F.conv2d(x.reshape(x.shape[0], *shape), torch.from_numpy(n.weight).cuda(),
                          torch.from_numpy(n.bias).cuda(), stride=n.stride, padding=n.padding)
             shape = n.out_shape
+        elif n.type == abi.NODE_BATCHNORM:
+            f = lambda a: torch.from_numpy(a).cuda()
+            w = f(n.weight) / torch.sqrt(f(n.running_var) + n.eps)
+            b = f(n.bias) - f(n.running_mean) * w
+            x = x.reshape(x.shape[0], *shape) * w.view(1, -1, 1, 1) + b.view(1, -1, 1, 1)
         elif n.type == abi.NODE_RELU:
             x = torch.relu(x)
     return x.reshape(x.shape[0], -1)
