@@ -202,14 +202,29 @@ __global__ void __launch_bounds__(256) conv_start_step_kernel(ConvStartStep st) 
     row_split(r, st.rows.R, p, rr);
     const int bx = st.rows.row_box[rr];
     const int id = st.rows.row_id[rr];
-    const int co = id % st.g.st_C;
+    const bool whole = st.g.full != 0;
+    const WinGeo& wgeo = whole ? st.wg : st.g;  // the weight window's geometry
+    const int co = id % wgeo.st_C;
+    const int nwin = wgeo.size();
     const int nw = st.g.size();
     int oy, ox;
     win_origin(st.g, id, oy, ox);
-    const float* wrow = st.Wc + (size_t)co * nw;
+    int wy0 = 0, wx0 = 0;
+    if (whole) win_origin(wgeo, id, wy0, wx0);
+    const float* wrow = st.Wc + (size_t)co * nwin;
     float part = 0.f;
     for (int j = threadIdx.x; j < nw; j += blockDim.x) {
-        const float P = wrow[j];
+        float P;
+        if (whole) {
+            // Map element j -> weight window element, or 0 outside it.
+            const int c = j % st.g.C, pix = j / st.g.C;
+            const int wy = pix / st.g.W - wy0, wx = pix - (pix / st.g.W) * st.g.W - wx0;
+            P = ((unsigned)wy < (unsigned)wgeo.wh && (unsigned)wx < (unsigned)wgeo.ww)
+                    ? wrow[(wy * wgeo.ww + wx) * wgeo.C + c]
+                    : 0.f;
+        } else {
+            P = wrow[j];
+        }
         const size_t at = (size_t)r * nw + j;
         if (st.P_save) st.P_save[at] = P;
         const int nu = win_neuron(st.g, oy, ox, j);
@@ -837,6 +852,175 @@ void launch_first_conv_adj(const RowMap& rows, int M, const WinGeo& g0, int form
     if (M == 0) return;
     const size_t smem = (size_t)first_seed_ph(cs.out_h) * first_seed_pw(cs.out_w) * FC * 4;
     first_conv_adj_kernel<<<M, 256, smem, s>>>(rows, M, g0, form, sign, gseed, xl, xu, cs, b, Qbar);
+    LB_LAUNCH();
+}
+
+// ============================================================== transposed-conv layers
+__global__ void ibp_convt_kernel(ConvTStep ct, const float* __restrict__ bias, const float* __restrict__ in_l,
+                                 const float* __restrict__ in_u, float* __restrict__ out_l,
+                                 float* __restrict__ out_u, int B, bool relu_in) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nout = (int64_t)ct.Ho * ct.Wo * ct.Co;
+    if (idx >= (int64_t)B * nout) return;
+    const int bx = (int)(idx / nout);
+    const int j = (int)(idx - (int64_t)bx * nout);
+    const int co = j % ct.Co, pix = j / ct.Co;
+    const int vy = pix / ct.Wo, vx = pix - (pix / ct.Wo) * ct.Wo;
+    float c = 0.f, d = 0.f;
+    for (int ky = 0; ky < ct.kh; ++ky) {
+        const int ty = vy + ct.ph - ky;
+        if (ty < 0 || ty % ct.sh) continue;
+        const int qy = ty / ct.sh;
+        if (qy >= ct.Hi) continue;
+        for (int kx = 0; kx < ct.kw; ++kx) {
+            const int tx = vx + ct.pw - kx;
+            if (tx < 0 || tx % ct.sw) continue;
+            const int qx = tx / ct.sw;
+            if (qx >= ct.Wi) continue;
+            const size_t base = (((size_t)bx * ct.Hi + qy) * ct.Wi + qx) * ct.Ci;
+            const float* w = ct.Wa + ((size_t)(ky * ct.kw + kx) * ct.Co + co) * ct.Ci;
+            for (int ci = 0; ci < ct.Ci; ++ci) {
+                float l = in_l[base + ci], u = in_u[base + ci];
+                if (relu_in) {
+                    l = fmaxf(l, 0.f);
+                    u = fmaxf(u, 0.f);
+                }
+                const float mid = (u + l) / 2.0f, diff = (u - l) / 2.0f;
+                c = fmaf(mid, w[ci], c);
+                d = fmaf(diff, fabsf(w[ci]), d);
+            }
+        }
+    }
+    c += bias ? bias[co] : 0.f;
+    out_l[idx] = c - d;
+    out_u[idx] = c + d;
+}
+
+void launch_ibp_convt(const ConvTStep& ct, const float* b, const float* in_l, const float* in_u, float* out_l,
+                      float* out_u, int B, bool relu_in, cudaStream_t s) {
+    const int64_t total = (int64_t)B * ct.Ho * ct.Wo * ct.Co;
+    if (total == 0) return;
+    ibp_convt_kernel<<<ceil_div(total, 256), 256, 0, s>>>(ct, b, in_l, in_u, out_l, out_u, B, relu_in);
+    LB_LAUNCH();
+}
+
+__global__ void __launch_bounds__(256) convt_back_relax_kernel(const float* __restrict__ A, ConvTStep ct, int M,
+                                                               ConvRelaxEpi e, int nchunk,
+                                                               float* __restrict__ partial) {
+    __shared__ float sh[8];
+    const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
+    const int nin = ct.Ho * ct.Wo * ct.Co;  // the rows' A at the layer's output
+    const int nw = ct.Hi * ct.Wi * ct.Ci;
+    const int j = chunk * 256 + threadIdx.x;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    float part = 0.f;
+    if (j < nw) {
+        const int ci = j % ct.Ci, pix = j / ct.Ci;
+        const int qy = pix / ct.Wi, qx = pix - (pix / ct.Wi) * ct.Wi;
+        const float* Arow = A + (size_t)r * nin;
+        float P = 0.f;
+        for (int ky = 0; ky < ct.kh; ++ky) {
+            const int vy = qy * ct.sh - ct.ph + ky;
+            if (vy < 0 || vy >= ct.Ho) continue;
+            for (int kx = 0; kx < ct.kw; ++kx) {
+                const int vx = qx * ct.sw - ct.pw + kx;
+                if (vx < 0 || vx >= ct.Wo) continue;
+                const float* a = Arow + ((size_t)vy * ct.Wo + vx) * ct.Co;
+                const float* w = ct.Wg + (((size_t)ci * ct.kh + ky) * ct.kw + kx) * ct.Co;
+                for (int co = 0; co < ct.Co; ++co) P = fmaf(a[co], w[co], P);
+            }
+        }
+        const size_t at = (size_t)r * nw + j;
+        if (e.P_save) e.P_save[at] = P;
+        const size_t bj = (size_t)bx * e.rp.n + j;
+        const float sl = (e.alpha && (e.rp.flags[bj] & RF_USE_ALPHA)) ? e.alpha[at] : e.rp.slope_lo[bj];
+        const float Q = relax_q(P, p, sl, e.rp.k_up[bj], e.rp.b_up[bj], part);
+        if (e.b_next) part = fmaf(Q, e.b_next[ci], part);
+        e.Q[at] = Q;
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+}
+
+void launch_convt_back_relax(const float* A, const ConvTStep& ct, int M, const ConvRelaxEpi& e, float* partial,
+                             cudaStream_t s) {
+    if (M == 0) return;
+    if (!e.g.full) throw std::invalid_argument("convt_back_relax: rows through a transposed conv are whole maps");
+    const int nchunk = conv_chunks(e.g);
+    convt_back_relax_kernel<<<(unsigned)((int64_t)M * nchunk), 256, 0, s>>>(A, ct, M, e, nchunk, partial);
+    LB_LAUNCH();
+}
+
+__global__ void __launch_bounds__(256) convt_start_step_kernel(ConvStartStep st, ConvTStep ct) {
+    __shared__ float sh[8];
+    const int r = blockIdx.x;
+    int p, rr;
+    row_split(r, st.rows.R, p, rr);
+    const int bx = st.rows.row_box[rr];
+    const int id = st.rows.row_id[rr];  // HWC index at the layer's output
+    const int co0 = id % ct.Co, pix0 = id / ct.Co;
+    const int vy0 = pix0 / ct.Wo, vx0 = pix0 - (pix0 / ct.Wo) * ct.Wo;
+    const int nw = ct.Hi * ct.Wi * ct.Ci;
+    float part = 0.f;
+    for (int j = threadIdx.x; j < nw; j += blockDim.x) {
+        const int ci = j % ct.Ci, pix = j / ct.Ci;
+        const int qy = pix / ct.Wi, qx = pix - (pix / ct.Wi) * ct.Wi;
+        const int ky = vy0 + ct.ph - qy * ct.sh, kx = vx0 + ct.pw - qx * ct.sw;
+        const float P = (ky >= 0 && ky < ct.kh && kx >= 0 && kx < ct.kw)
+                            ? ct.Wg[(((size_t)ci * ct.kh + ky) * ct.kw + kx) * ct.Co + co0]
+                            : 0.f;
+        const size_t at = (size_t)r * nw + j;
+        if (st.P_save) st.P_save[at] = P;
+        const size_t bj = (size_t)bx * st.rp.n + j;
+        const float sl = (st.alpha && (st.rp.flags[bj] & RF_USE_ALPHA)) ? st.alpha[at] : st.rp.slope_lo[bj];
+        const float Q = relax_q(P, p, sl, st.rp.k_up[bj], st.rp.b_up[bj], part);
+        if (st.b_next) part = fmaf(Q, st.b_next[ci], part);
+        st.Q[at] = Q;
+    }
+    const float tot = block_sum256(part, sh);
+    if (threadIdx.x == 0) st.bias_acc[r] = tot;
+}
+
+void launch_convt_start_step(const ConvStartStep& st, const ConvTStep& ct, cudaStream_t s) {
+    if (st.M == 0) return;
+    convt_start_step_kernel<<<st.M, 256, 0, s>>>(st, ct);
+    LB_LAUNCH();
+}
+
+__global__ void convt_adj_qbar_kernel(const float* __restrict__ Pbar, ConvTStep ct, int M, float* __restrict__ Qbar) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t nq = (int64_t)ct.Ho * ct.Wo * ct.Co;
+    if (idx >= (int64_t)M * nq) return;
+    const int r = (int)(idx / nq);
+    const int j = (int)(idx - (int64_t)r * nq);
+    const int co = j % ct.Co, pix = j / ct.Co;
+    const int vy = pix / ct.Wo, vx = pix - (pix / ct.Wo) * ct.Wo;
+    const float* prow = Pbar + (size_t)r * ct.Hi * ct.Wi * ct.Ci;
+    float acc = 0.f;
+    for (int ky = 0; ky < ct.kh; ++ky) {
+        const int ty = vy + ct.ph - ky;
+        if (ty < 0 || ty % ct.sh) continue;
+        const int qy = ty / ct.sh;
+        if (qy >= ct.Hi) continue;
+        for (int kx = 0; kx < ct.kw; ++kx) {
+            const int tx = vx + ct.pw - kx;
+            if (tx < 0 || tx % ct.sw) continue;
+            const int qx = tx / ct.sw;
+            if (qx >= ct.Wi) continue;
+            const float* pb = prow + ((size_t)qy * ct.Wi + qx) * ct.Ci;
+            const float* w = ct.Wa + ((size_t)(ky * ct.kw + kx) * ct.Co + co) * ct.Ci;
+            for (int ci = 0; ci < ct.Ci; ++ci) acc = fmaf(pb[ci], w[ci], acc);
+        }
+    }
+    Qbar[idx] = acc;
+}
+
+void launch_convt_adj_qbar(const float* Pbar, const ConvTStep& ct, int M, float* Qbar, cudaStream_t s) {
+    const int64_t total = (int64_t)M * ct.Ho * ct.Wo * ct.Co;
+    if (total == 0) return;
+    convt_adj_qbar_kernel<<<ceil_div(total, 256), 256, 0, s>>>(Pbar, ct, M, Qbar);
     LB_LAUNCH();
 }
 

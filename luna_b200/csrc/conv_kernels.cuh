@@ -77,6 +77,7 @@ struct ConvStartStep {
     const float* Wc = nullptr;     // [Co][kh][kw][Ci] of the start conv
     const float* bW = nullptr;     // [Co]
     WinGeo g;                      // window at the level below the start
+    WinGeo wg;                     // when g is a whole map: the weight window's placement
     ReluParams rp;                 // ReLU below (rp.n = map size)
     const float* alpha = nullptr;  // [2R, g.size()] or null
     const float* b_next = nullptr; // [C] bias of the layer producing the map below
@@ -150,6 +151,35 @@ void launch_first_convT_conc(const float* A, const ConvStep& cs, int M, const Co
 void launch_first_conv_adj(const RowMap& rows, int M, const WinGeo& g0, int form, const uint8_t* sign,
                            const float* gseed, const float* xl, const float* xu, const ConvStep& cs,
                            const float* b, float* Qbar, cudaStream_t s);
+
+// ---- transposed-conv layers (BoundedConvTransposeNode) -------------------
+// Geometry of a ConvTranspose2d layer: in (Ci, Hi, Wi) -> out (Co, Ho, Wo),
+// Ho = (Hi - 1) s - 2 p + kh; out[v] gets in[q] W[ci, co, k] for v = q s - p + k.
+// Rows through such a layer are whole maps.
+struct ConvTStep {
+    int Ci = 0, Co = 0, kh = 0, kw = 0, sh = 1, sw = 1, ph = 0, pw = 0;
+    int Hi = 0, Wi = 0, Ho = 0, Wo = 0;
+    const float* Wg = nullptr;  // [Ci][kh][kw][Co]
+    const float* Wa = nullptr;  // [kh][kw][Co][Ci]
+};
+// Centre / radius IBP (BoundedConvTransposeNode.cpp:466-488): c = convT(mid)
+// + b, d = convT(diff, |W|), [c - d, c + d]; inputs clamped at 0 first when
+// they are a ReLU output.
+void launch_ibp_convt(const ConvTStep& ct, const float* b, const float* in_l, const float* in_u, float* out_l,
+                      float* out_u, int B, bool relu_in, cudaStream_t s);
+// Back-substitution through the layer (a strided correlation,
+// BoundedConvTransposeNode.cpp:250-280): P_in[q, ci] = sum_{k, co}
+// A_out[q s - p + k, co] W[ci, co, k], with the ReLU relaxation of the level
+// below in the epilogue (whole maps; chunk partials as launch_convT_relax).
+void launch_convt_back_relax(const float* A, const ConvTStep& ct, int M, const ConvRelaxEpi& e, float* partial,
+                             cudaStream_t s);
+// Start step of a ConvTranspose start: the one-hot row at output neuron
+// (v0, co0) through the layer is W[:, co0, k] at the q with q s - p + k = v0;
+// the layer's bias does not enter (flat A, see launch_convt_back_relax).
+void launch_convt_start_step(const ConvStartStep& st, const ConvTStep& ct, cudaStream_t s);
+// Adjoint of the back-substitution step: Qbar[v, co] = sum P_in[q, ci]
+// W[ci, co, k] over v = q s - p + k (a transposed conv; no bias term).
+void launch_convt_adj_qbar(const float* Pbar, const ConvTStep& ct, int M, float* Qbar, cudaStream_t s);
 
 // dst[i] += (float)src[i], src[i] = 0 for i < n (folds the double scratch of
 // launch_relax_adjoint_win into kbar / bbar).

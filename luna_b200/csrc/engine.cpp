@@ -86,7 +86,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         const int nx = dependents[cur][0];
         const auto& d = g->nodes[nx];
         if (d.num_inputs != 1) throw std::invalid_argument("multi-input node in chain");
-        if (d.type == LB200_NODE_LINEAR || d.type == LB200_NODE_CONV) {
+        if (d.type == LB200_NODE_LINEAR || d.type == LB200_NODE_CONV || d.type == LB200_NODE_CONVTRANSPOSE) {
             if (!expect_affine) throw std::invalid_argument("two affine nodes without a ReLU between");
             if (!d.weight) throw std::invalid_argument("affine node without weight");
             affine.push_back(nx);
@@ -129,8 +129,30 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         const auto& d = g->nodes[affine[k]];
         Layer& L = layers_[k];
         L.conv = d.type == LB200_NODE_CONV;
+        L.convt = d.type == LB200_NODE_CONVTRANSPOSE;
         L.in = prev;
-        if (L.conv) {
+        if (L.convt) {
+            has_conv_ = true;
+            if (!prev.spatial) throw std::invalid_argument("a transposed conv must follow the input or a conv");
+            if (k == 0) throw std::invalid_argument("a transposed conv as the first layer is not supported");
+            if (bn_after[k] >= 0) throw std::invalid_argument("BatchNorm after a transposed conv is not supported");
+            L.kh = d.kernel[0];
+            L.kw = d.kernel[1];
+            L.sh = d.stride[0];
+            L.sw = d.stride[1];
+            L.ph = d.padding[0];
+            L.pw = d.padding[1];
+            if (d.output_padding[0] != 0 || d.output_padding[1] != 0)
+                throw std::invalid_argument("ConvTranspose output_padding must be 0 (BoundedConvTransposeNode.cpp:61-63)");
+            if (L.kh <= 0 || L.kw <= 0 || L.sh <= 0 || L.sw <= 0 || L.ph < 0 || L.pw < 0)
+                throw std::invalid_argument("bad transposed-conv geometry");
+            L.out.C = d.out_shape[0];
+            L.out.H = (prev.H - 1) * L.sh - 2 * L.ph + L.kh;
+            L.out.W = (prev.W - 1) * L.sw - 2 * L.pw + L.kw;
+            L.out.spatial = true;
+            if (L.out.H != d.out_shape[1] || L.out.W != d.out_shape[2] || L.out.H <= 0 || L.out.W <= 0)
+                throw std::invalid_argument("transposed-conv out_shape does not match its geometry");
+        } else if (L.conv) {
             has_conv_ = true;
             if (!prev.spatial) throw std::invalid_argument("a conv layer must follow the input or another conv");
             L.kh = d.kernel[0];
@@ -159,8 +181,8 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         // y = w (affine(x)) + (B - mean w), w = scale / sqrt(var + eps) per
         // output channel (conv) or feature (Linear), computed in fp32 as
         // BoundedBatchNormNode::ensureCachedParams does (:68-80).
-        const int nch = L.conv ? Co : L.n_out;
-        const size_t per_ch = L.conv ? (size_t)Ci * L.kh * L.kw : (size_t)L.n_in;
+        const int nch = (L.conv || L.convt) ? Co : L.n_out;
+        const size_t per_ch = (L.conv || L.convt) ? (size_t)Ci * L.kh * L.kw : (size_t)L.n_in;
         std::vector<float> wsrc(d.weight, d.weight + (size_t)nch * per_ch), bsrc(nch, 0.f);
         if (d.bias)
             for (int c = 0; c < nch; ++c) bsrc[c] = d.bias[c];
@@ -173,7 +195,20 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
             }
         }
         std::vector<float> W, Wt, b(bsrc), bn(L.n_out, 0.f);
-        if (L.conv) {
+        if (L.convt) {
+            // ONNX ConvTranspose weight [Ci, Co, kh, kw] -> Wg [Ci][kh][kw][Co], Wa [kh][kw][Co][Ci].
+            W.resize((size_t)Ci * L.kh * L.kw * Co);
+            Wt.resize(W.size());
+            for (int c = 0; c < Ci; ++c)
+                for (int o = 0; o < Co; ++o)
+                    for (int y = 0; y < L.kh; ++y)
+                        for (int x = 0; x < L.kw; ++x) {
+                            const float w = wsrc[(((size_t)c * Co + o) * L.kh + y) * L.kw + x];
+                            W[(((size_t)c * L.kh + y) * L.kw + x) * Co + o] = w;
+                            Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
+                        }
+            for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
+        } else if (L.conv) {
             // ONNX Conv weight [Co, Ci, kh, kw] -> Wc [Co][kh][kw][Ci], Wk [kh][kw][Co][Ci].
             W.resize((size_t)Co * L.kh * L.kw * Ci);
             Wt.resize(W.size());
@@ -228,7 +263,11 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
     for (int st = 2; st <= K_; ++st) {
         std::vector<WinGeo>& gv = geo_[st];
         gv.resize(st);
-        const bool window = st < K_ && layers_[st - 1].conv;
+        // Conv starts keep receptive-field windows when only convs lie below
+        // them; otherwise (a Linear or transposed conv below) their rows are
+        // whole maps.
+        bool window = st < K_ && layers_[st - 1].conv;
+        for (int m = st - 1; m >= 1 && window; --m) window = layers_[m - 1].conv;
         for (int m = 0; m < st; ++m) {
             const MapShape& ms = map(m);
             WinGeo w;
@@ -254,7 +293,6 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         gv[st - 1] = w;
         for (int m = st - 1; m >= 1; --m) {
             const Layer& L = layers_[m - 1];
-            if (!L.conv) throw std::invalid_argument("a Linear layer below a conv start is not supported");
             WinGeo v = gv[m];
             const MapShape& ms = map(m - 1);
             v.C = ms.C;
@@ -449,6 +487,26 @@ ConvStep Model::conv_step(int st, int m) const {
     return cs;
 }
 
+ConvTStep Model::convt_step(int m) const {
+    const Layer& L = layers_[m - 1];
+    ConvTStep ct;
+    ct.Ci = L.in.C;
+    ct.Co = L.out.C;
+    ct.kh = L.kh;
+    ct.kw = L.kw;
+    ct.sh = L.sh;
+    ct.sw = L.sw;
+    ct.ph = L.ph;
+    ct.pw = L.pw;
+    ct.Hi = L.in.H;
+    ct.Wi = L.in.W;
+    ct.Ho = L.out.H;
+    ct.Wo = L.out.W;
+    ct.Wg = L.W;
+    ct.Wa = L.Wt;
+    return ct;
+}
+
 // Luna's CPU path starts a conv node with more than 4096 output features in
 // patches mode (CROWNAnalysis.cpp:255-272) and converts the patches to a
 // matrix once they are wider than a conv input (BoundedConvNode.cpp:671-694);
@@ -456,6 +514,9 @@ ConvStep Model::conv_step(int st, int m) const {
 int Model::start_form(int st) const {
     if (st >= K_ || !layers_[st - 1].conv || !opt_.use_patches_mode) return CONC_DENSE;
     if (layers_[st - 1].n_out <= 4096) return CONC_DENSE;
+    if (geo_[st][st - 1].full)
+        throw std::invalid_argument("a conv start above a Linear or transposed conv with more than 4096 features "
+                                    "(Luna's patches mode there) is not supported");
     int width = 0;
     for (int m = st; m >= 1; --m) {
         const Layer& L = layers_[m - 1];
@@ -592,7 +653,9 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     auto tc_fwd = [&](int m) { return tcconv_ && m >= 2 && layers_[m - 1].tcf; };
     int slots_total = 0;
     for (int m = mb; m >= 1; --m) {
-        if (!layers_[m - 1].conv)
+        if (layers_[m - 1].convt)
+            slots_total += conv_chunks(sp.geo[m - 1]);
+        else if (!layers_[m - 1].conv)
             slots_total += gemm_tiles_n(width(m - 1));
         else if (m == 1 && first_conv_fast(conv_step(st, 1)))
             slots_total += 1;
@@ -610,21 +673,40 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     };
 
     const Layer& Ls = layers_[st - 1];
-    if (Ls.conv) {
-        // Conv start: identity patches through the start conv.
+    if (Ls.conv || Ls.convt) {
+        // Conv start: identity patches through the start conv; ConvTranspose
+        // start: the one-hot rows through the layer (whole maps).
         ConvStartStep cs;
         cs.rows = sp.rows;
         cs.M = M;
         cs.Wc = Ls.W;
         cs.bW = Ls.b;
         cs.g = sp.geo[mb];
+        if (Ls.conv && cs.g.full) {
+            // Whole-map rows of a conv start: the weight window sits at the
+            // start pixel's receptive field inside the map.
+            WinGeo w = cs.g;
+            w.full = 0;
+            w.wh = Ls.kh;
+            w.ww = Ls.kw;
+            w.mul_y = Ls.sh;
+            w.mul_x = Ls.sw;
+            w.off_y = -Ls.ph;
+            w.off_x = -Ls.pw;
+            w.st_C = Ls.out.C;
+            w.st_W = Ls.out.W;
+            cs.wg = w;
+        }
         cs.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
         cs.alpha = alpha_buf(mb);
-        cs.b_next = layers_[mb - 1].b;
+        cs.b_next = level_bias(mb);
         cs.P_save = psave_buf(mb);
         cs.Q = Q[0];
         cs.bias_acc = bias;
-        launch_conv_start_step(cs, s);
+        if (Ls.convt)
+            launch_convt_start_step(cs, convt_step(st), s);
+        else
+            launch_conv_start_step(cs, s);
     } else {
         StartStep ss;
         ss.rows = sp.rows;
@@ -641,7 +723,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
         }
         ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
         ss.alpha = alpha_buf(mb);
-        ss.b_next = layers_[mb - 1].b_neuron;
+        ss.b_next = level_bias_n(mb);
         ss.P_save = psave_buf(mb);
         ss.Q = Q[0];
         ss.bias_acc = bias;
@@ -651,6 +733,26 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     int cur = 0, slot = 0;
     for (int m = mb; m >= 1; --m) {
         const Layer& L = layers_[m - 1];
+        if (L.convt) {
+            // k > 1 for a transposed conv (checked at model creation).
+            const ConvTStep ct = convt_step(m);
+            const double fl = 2.0 * M * (double)rowlen(st, m) * ct.Ci * L.kh * L.kw / ((double)L.sh * L.sw);
+            flops_ += fl;
+            ConvRelaxEpi e;
+            e.rows = sp.rows;
+            e.g = sp.geo[m - 1];
+            e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
+            e.alpha = alpha_buf(m - 1);
+            e.b_next = level_bias(m - 1);
+            e.P_save = psave_buf(m - 1);
+            e.Q = Q[1 - cur];
+            prof_begin(s);
+            launch_convt_back_relax(Q[cur], ct, M, e, part + (size_t)slot * M, s);
+            prof_end(s, fl);
+            slot += conv_chunks(sp.geo[m - 1]);
+            cur = 1 - cur;
+            continue;
+        }
         if (L.conv) {
             const ConvStep cs = conv_step(st, m);
             const double fl = 2.0 * M * (double)rowlen(st, m - 1) * cs.Co * L.kh * L.kw /
@@ -663,7 +765,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 e.g = sp.geo[m - 1];
                 e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
                 e.alpha = alpha_buf(m - 1);
-                e.b_next = layers_[m - 2].b;
+                e.b_next = level_bias(m - 1);
                 e.P_save = psave_buf(m - 1);
                 e.Q = Q[1 - cur];
                 if (tc_fwd(m)) {
@@ -713,7 +815,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.rows = sp.rows;
             e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
             e.alpha = alpha_buf(m - 1);
-            e.b_next = layers_[m - 2].b_neuron;
+            e.b_next = level_bias_n(m - 1);
             e.P_save = psave_buf(m - 1);
             e.Q = Q[1 - cur];
             prof_begin(s);
@@ -908,6 +1010,18 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         e.B = B;
         e.kbar = cache_.as<float>(key("kbar", m), (size_t)B * N);
         e.bbar = cache_.as<float>(key("bbar", m), (size_t)B * N);
+        if (L.convt) {
+            const ConvTStep ct = convt_step(m);
+            const double fl = 2.0 * M * (double)rl * ct.Ci * L.kh * L.kw / ((double)L.sh * L.sw);
+            flops_ += fl;
+            float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
+            prof_begin(s);
+            launch_convt_adj_qbar(Pb[cur], ct, M, Qbar, s);
+            prof_end(s, fl);
+            launch_relax_adjoint(e, Qbar, M, N, s);
+            cur = 1 - cur;
+            continue;
+        }
         if (L.conv) {
             const ConvStep cs = conv_step(st, m);
             const double fl = 2.0 * M * (double)rowlen(st, m - 1) * cs.Co * L.kh * L.kw /
@@ -1059,7 +1173,9 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         const Layer& L = layers_[k - 1];
         float* ol = cache_.as<float>(key("ibp_l", k), bn);
         float* ou = cache_.as<float>(key("ibp_u", k), bn);
-        if (L.conv)
+        if (L.convt)
+            launch_ibp_convt(convt_step(k), L.b, il, iu, ol, ou, B, k > 1, s);
+        else if (L.conv)
             launch_ibp_conv(L.W, L.b, il, iu, ol, ou, B, L.in.C, L.in.H, L.in.W, L.out.C, L.out.H, L.out.W, L.kh,
                             L.kw, L.sh, L.sw, L.ph, L.pw, k > 1, s);
         else

@@ -49,6 +49,7 @@ struct MapShape {
 // One affine layer: Linear (BoundedLinearNode) or Conv2d (BoundedConvNode).
 struct Layer {
     bool conv = false;
+    bool convt = false;  // ConvTranspose2d (BoundedConvTransposeNode): W = Wg [Ci][kh][kw][Co], Wt = Wa [kh][kw][Co][Ci]
     int n_in = 0, n_out = 0;
     MapShape in, out;
     int kh = 1, kw = 1, sh = 1, sw = 1, ph = 0, pw = 0;  // conv geometry
@@ -134,6 +135,11 @@ private:
     // Length of a row of start st at level m (its window, or the whole map).
     int rowlen(int st, int m) const { return geo_[st][m].size(); }
     ConvStep conv_step(int st, int m) const;
+    ConvTStep convt_step(int m) const;
+    // Bias that back-substitution adds for the layer producing level m, per
+    // channel or per neuron (none for a ConvTranspose: Luna's A is flat there).
+    const float* level_bias(int m) const { return layers_[m - 1].convt ? nullptr : layers_[m - 1].b; }
+    const float* level_bias_n(int m) const { return layers_[m - 1].convt ? nullptr : layers_[m - 1].b_neuron; }
     // Tensor-core plans of conv layer m for the rows of start st.
     void conv_phase(int st, int m, int& cy, int& cx, int& tlo_y, int& tlo_x, int& nty, int& ntx) const;
     TcConvPlan tc_fwd_plan(int st, int m, int rows, const float* data) const;

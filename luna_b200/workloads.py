@@ -10,7 +10,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .abi import NODE_BATCHNORM, NODE_CONV, NODE_FLATTEN, NODE_INPUT, NODE_LINEAR, NODE_RELU, Graph, Node
+from .abi import (NODE_BATCHNORM, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_INPUT, NODE_LINEAR,
+                  NODE_RELU, Graph, Node)
 
 
 def mlp(widths, seed: int, bias_std: float = 0.01) -> Graph:
@@ -38,7 +39,8 @@ def cnn(input_shape, layers, seed: int, bias_std: float = 0.01) -> Graph:
     """Input (C, H, W) -> layers -> output, ReLU after every layer but the last.
 
     `layers` items are ("conv", C_out, k, stride, pad), ("convbn", C_out, k,
-    stride, pad) -- a conv followed by BatchNorm -- or ("linear", n_out); a
+    stride, pad) -- a conv followed by BatchNorm --, ("convT", C_out, k,
+    stride, pad) -- a transposed conv -- or ("linear", n_out); a
     Flatten node is inserted where a conv feeds a linear layer.  Weights are
     He-normal over the fan-in (C_in k k for a conv), biases N(0, bias_std^2);
     BatchNorm gamma ~ U[0.5, 1.5], beta ~ N(0, 0.1^2), running mean ~ N(0,
@@ -65,6 +67,16 @@ def cnn(input_shape, layers, seed: int, bias_std: float = 0.01) -> Graph:
                 var = rng.uniform(0.5, 2.0, co).astype(np.float32)
                 nodes.append(Node(NODE_BATCHNORM, [len(nodes) - 1], shape, weight=gamma, bias=beta,
                                   running_mean=mean, running_var=var, eps=1e-5))
+        elif spec[0] == "convT":
+            # Transposed conv, weight [C_in, C_out, k, k] (He-normal over C_in k k).
+            _, co, k, s, p = spec
+            ci, h, w = shape
+            fan_in = ci * k * k
+            wt = (rng.standard_normal((ci, co, k, k)) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+            b = (rng.standard_normal(co) * bias_std).astype(np.float32)
+            shape = (co, (h - 1) * s - 2 * p + k, (w - 1) * s - 2 * p + k)
+            nodes.append(Node(NODE_CONVTRANSPOSE, [len(nodes) - 1], shape, weight=wt, bias=b,
+                              kernel=(k, k), stride=(s, s), padding=(p, p)))
         elif spec[0] == "linear":
             n_out = spec[1]
             if shape[1] != 1 or shape[2] != 1:
@@ -227,3 +239,23 @@ def small_cnn_bn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, big_first:
     g = cnn((3, hw, hw), [("convbn", 8, 3, 1, 1), ("convbn", 16, 4, 2, 1), ("convbn", 8, 3, 1, 1),
                           ("linear", 24), ("linear", 5)], seed + 7, bias_std=0.1)
     return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 5)
+
+
+def convt_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 10, conv_after: bool = False):
+    """Small CNN with a strided transposed conv (conv -> conv s2 -> convT s2
+    [-> conv] -> linear head) for parity tests."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    layers = [("conv", 6, 3, 1, 1), ("conv", 8, 4, 2, 1), ("convT", 5, 4, 2, 1)]
+    if conv_after:
+        layers.append(("conv", 4, 3, 1, 1))
+    g = cnn((3, hw, hw), layers + [("linear", 12), ("linear", 4)], seed + 9, bias_std=0.1)
+    return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)
+
+
+def cnn_convt_cifar(n_boxes: int = 256, seed: int = 5, eps: float = 8.0 / 255.0):
+    """3x32x32 -> conv3->32 k3s1p1 -> conv32->64 k4s2p1 -> convT64->32 k4s2p1 ->
+    flatten 32768 -> 512 -> 10: the transposed-conv variant of the CIFAR CNN."""
+    g = cnn((3, 32, 32), [("conv", 32, 3, 1, 1), ("conv", 64, 4, 2, 1), ("convT", 32, 4, 2, 1),
+                          ("linear", 512), ("linear", 10)], seed)
+    rng = np.random.Generator(np.random.PCG64(seed + 1000))
+    return g, image_boxes(rng, n_boxes, 3 * 32 * 32, eps, 10)

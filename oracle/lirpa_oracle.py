@@ -11,7 +11,8 @@ behaviour it restates.  Per-box state follows Luna's: IBP bounds, "node
 bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
 parameters keyed by (activation node, start node), and STE reference bounds.
 
-Supported node kinds: Input, Linear, Conv2d, BatchNorm, ReLU, Flatten, Identity.  A
+Supported node kinds: Input, Linear, Conv2d, ConvTranspose2d, BatchNorm, ReLU, Flatten,
+Identity.  A
 matrices are kept dense over the flattened (C, H, W) features; Luna's
 patches mode (CROWNAnalysis.cpp:255-405, BoundedConvNode.cpp:556-709) is the
 same arithmetic on a window of those features, and it is tracked only to
@@ -27,8 +28,8 @@ import torch
 import torch.nn.functional as F
 
 from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_BATCHNORM,
-                           NODE_CONV, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT, NODE_LINEAR,
-                           NODE_RELU, Options, default_options)
+                           NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT,
+                           NODE_LINEAR, NODE_RELU, Options, default_options)
 
 # Dense identity starts above this many conv output features switch to
 # patches on Luna's CPU path (CROWNAnalysis.cpp:257,269).
@@ -112,7 +113,7 @@ class LirpaOracle:
                 self.W[i] = torch.from_numpy(np.asarray(nd.weight, np.float32)) * nd.scale
                 self.b[i] = (torch.from_numpy(np.asarray(nd.bias, np.float32))
                              if nd.bias is not None else torch.zeros(nd.weight.shape[0]))
-            elif nd.type == NODE_CONV:
+            elif nd.type in (NODE_CONV, NODE_CONVTRANSPOSE):
                 self.W[i] = torch.from_numpy(np.asarray(nd.weight, np.float32))
                 self.b[i] = (torch.from_numpy(np.asarray(nd.bias, np.float32))
                              if nd.bias is not None else torch.zeros(nd.weight.shape[0]))
@@ -154,6 +155,16 @@ class LirpaOracle:
             lo = (conv(l, Wp) + conv(u, Wn)) + b
             hi = (conv(u, Wp) + conv(l, Wn)) + b
             return lo.flatten(), hi.flatten()
+        if nd.type == NODE_CONVTRANSPOSE:
+            # Centre / radius (BoundedConvTransposeNode.cpp:466-488):
+            # c = convT(mid, W) + b, d = convT(diff, |W|), [c - d, c + d].
+            l, u = ins[0]
+            ci, h, w = self.g.nodes[nd.inputs[0]].out_shape
+            mid = ((u + l) / 2.0).reshape(1, ci, h, w)
+            diff = ((u - l) / 2.0).reshape(1, ci, h, w)
+            dev = F.conv_transpose2d(diff, self.W[i].abs(), stride=nd.stride, padding=nd.padding)
+            cen = F.conv_transpose2d(mid, self.W[i], self.b[i], stride=nd.stride, padding=nd.padding)
+            return (cen - dev).flatten(), (cen + dev).flatten()
         if nd.type == NODE_BATCHNORM:
             # BoundedBatchNormNode::computeIntervalBoundPropagation (:151-178).
             l, u = ins[0]
@@ -314,6 +325,11 @@ class LirpaOracle:
         n = self.g.nodes[start].size
         patches = self._starts_in_patches(start, C is not None)
         pwidth = None
+        # Luna keeps a tensor A flat ([spec, 1, n]) between nodes: a conv node
+        # reshapes its [spec, 1, C, H, W] result back when the input bounds
+        # are flat (BoundedConvNode.cpp:430-445).  ConvTranspose adds its
+        # bias term only for a 4-D / 5-D A or patches, so in tensor mode its
+        # bias never enters the back-substitution (BoundedConvTransposeNode.cpp:289-311).
         if C is not None:
             A0 = C
         else:
@@ -357,6 +373,21 @@ class LirpaOracle:
                     nb_u = (a_u * bb).sum(-1)
                     if patches and pwidth is None:
                         pwidth = 1  # identity patches become 1x1 channel-diagonal patches (:389-420)
+                elif nd.type == NODE_CONVTRANSPOSE:
+                    # BoundedConvTransposeNode::boundOneSide, tensor mode (:250-311):
+                    # conv2d(A, W, stride, padding); bias sum_{c,h,w} A b_c.
+                    ci, hi, wi = self.g.nodes[nd.inputs[0]].out_shape
+                    co, ho, wo = nd.out_shape
+                    outs = []
+                    for a in (a_l, a_u):
+                        a4 = a.reshape(a.shape[0], co, ho, wo)
+                        bias = ((a4.sum((2, 3)) * self.b[c].view(1, -1)).sum(-1) if patches
+                                else torch.zeros(a.shape[0]))
+                        outs.append((F.conv2d(a4, self.W[c], stride=nd.stride, padding=nd.padding)
+                                     .reshape(a.shape[0], -1), bias))
+                    out = [(outs[0][0], outs[1][0])]
+                    nb_l, nb_u = outs[0][1], outs[1][1]
+                    patches = False
                 elif nd.type == NODE_CONV:
                     nl, nb_l = self._conv_backward(c, a_l)
                     nu, nb_u = self._conv_backward(c, a_u)

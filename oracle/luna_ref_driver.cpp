@@ -24,6 +24,7 @@
 #include "nodes/BoundedIdentityNode.h"
 #include "nodes/BoundedConvNode.h"
 #include "nodes/BoundedBatchNormNode.h"
+#include "nodes/BoundedConvTransposeNode.h"
 #include "input_parsers/Operations.h"
 
 #include <torch/torch.h>
@@ -106,6 +107,28 @@ std::shared_ptr<NLR::TorchModel> build_model(const lb200_graph_desc* g) {
             cn->setInputShape({1, (int)Ci, (int)H, (int)W});
             cn->setOutputShape({1, (int)Co, d.out_shape[1], d.out_shape[2]});
             node = cn;
+            break;
+        }
+        case LB200_NODE_CONVTRANSPOSE: {
+            // OnnxToTorchParser's ConvTranspose (OnnxToTorch.cpp:2680-2717): weight
+            // [Ci, Co, kh, kw], MATRIX mode.
+            const lb200_node_desc& src = g->nodes[d.inputs[0]];
+            const int64_t Ci = src.out_shape[0];
+            const int64_t Co = d.out_shape[0], kh = d.kernel[0], kw = d.kernel[1];
+            torch::nn::ConvTranspose2dOptions co(Ci, Co, {kh, kw});
+            co.stride({(int64_t)d.stride[0], (int64_t)d.stride[1]});
+            co.padding(torch::ExpandingArray<2>({(int64_t)d.padding[0], (int64_t)d.padding[1]}));
+            co.output_padding(torch::ExpandingArray<2>({(int64_t)d.output_padding[0], (int64_t)d.output_padding[1]}));
+            co.bias(d.bias != nullptr);
+            torch::nn::ConvTranspose2d ct(co);
+            ct->weight = from_host(d.weight, {Ci, Co, kh, kw});
+            if (d.bias) ct->bias = from_host(d.bias, {Co});
+            auto tn = std::make_shared<NLR::BoundedConvTransposeNode>(ct, NLR::ConvMode::MATRIX);
+            // Sizes as a forward pass would leave them (a start at this node
+            // sizes its one-hot rows with getOutputSize()).
+            tn->setInputSize((unsigned)(Ci * src.out_shape[1] * src.out_shape[2]));
+            tn->setOutputSize((unsigned)out_numel);
+            node = tn;
             break;
         }
         case LB200_NODE_BATCHNORM: {

@@ -68,6 +68,15 @@ def cases():
     out.append(("cnnbn_patch_crown", "small_cnn_bn_case", kw, 2, abi.METHOD_CROWN, {}))
     out.append(("cnnbn_patch_alpha", "small_cnn_bn_case", kw, 2, abi.METHOD_ALPHA_CROWN,
                 {"alpha_lr": 0.1, "alpha_iterations": 4}))
+    # A strided transposed conv below a linear head, and below another conv.
+    kw = {"seed": 1, "n_boxes": 3}
+    out.append(("convt_crown", "convt_cnn_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("convt_alpha", "convt_cnn_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 6}))
+    kw = {"seed": 2, "n_boxes": 3, "conv_after": True}
+    out.append(("convt2_crown", "convt_cnn_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("convt2_alpha", "convt_cnn_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 6}))
     # The CIFAR-shaped CNN at full size, one box.
     out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
     return out
