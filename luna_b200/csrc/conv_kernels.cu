@@ -262,8 +262,9 @@ __global__ void __launch_bounds__(256) convT_relax_kernel(const float* __restric
     const int bx = e.rows.row_box[rr];
     float part = 0.f;
     if (j < nw) {
-        const float P = convT_elem(A + (size_t)r * nin, cs, j);
         const size_t at = (size_t)r * nw + j;
+        float P = convT_elem(A + (size_t)r * nin, cs, j);
+        if (e.addend) P += e.addend[at];
         if (e.P_save) e.P_save[at] = P;
         int oy, ox;
         win_origin(e.g, e.rows.row_id[rr], oy, ox);
@@ -336,7 +337,7 @@ void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConc
 int relax_window_chunks(const WinGeo& g) { return ceil_div(g.size(), 1024); }
 
 // 256 threads x 4 consecutive elements (one pixel's channels when C % 4 == 0).
-__global__ void __launch_bounds__(256) relax_window_kernel(const float* __restrict__ P, ConvRelaxEpi e, int M,
+__global__ void __launch_bounds__(256) relax_window_kernel(float* __restrict__ P, ConvRelaxEpi e, int M,
                                                            int nchunk, float* __restrict__ partial) {
     __shared__ float sh[8];
     const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
@@ -350,7 +351,12 @@ __global__ void __launch_bounds__(256) relax_window_kernel(const float* __restri
     float part = 0.f;
     if (j0 < nw) {
         const size_t at = (size_t)r * nw + j0;
-        const float4 p4 = *reinterpret_cast<const float4*>(P + at);
+        float4 p4 = *reinterpret_cast<const float4*>(P + at);
+        if (e.addend) {
+            const float4 a = *reinterpret_cast<const float4*>(e.addend + at);
+            p4 = make_float4(p4.x + a.x, p4.y + a.y, p4.z + a.z, p4.w + a.w);
+            *reinterpret_cast<float4*>(P + at) = p4;
+        }
         const float Pv[4] = {p4.x, p4.y, p4.z, p4.w};
         const int nu0 = win_neuron(e.g, oy, ox, j0);  // the 4 elements share a pixel
         float Qv[4] = {0.f, 0.f, 0.f, 0.f};
@@ -381,7 +387,7 @@ __global__ void __launch_bounds__(256) relax_window_kernel(const float* __restri
     if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
 }
 
-void launch_relax_window(const float* P, const ConvRelaxEpi& e, int M, float* partial, cudaStream_t s) {
+void launch_relax_window(float* P, const ConvRelaxEpi& e, int M, float* partial, cudaStream_t s) {
     if (M == 0) return;
     if (e.g.C % 4 != 0) throw std::invalid_argument("relax_window: channels must be a multiple of 4");
     const int nchunk = relax_window_chunks(e.g);
@@ -1021,6 +1027,98 @@ void launch_convt_adj_qbar(const float* Pbar, const ConvTStep& ct, int M, float*
     const int64_t total = (int64_t)M * ct.Ho * ct.Wo * ct.Co;
     if (total == 0) return;
     convt_adj_qbar_kernel<<<ceil_div(total, 256), 256, 0, s>>>(Pbar, ct, M, Qbar);
+    LB_LAUNCH();
+}
+
+// ============================================================== skip edges
+__global__ void skip_back_kernel(SkipStep k, RowMap rows, int M, const float* __restrict__ Q,
+                                 float* __restrict__ S) {
+    const int nw = k.go.size();
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)M * nw) return;
+    const int r = (int)(idx / nw), j = (int)(idx - (int64_t)r * nw);
+    const int ci = j % k.Ci, pix = j / k.Ci;
+    const int vy = pix / k.go.ww, vx = pix - (pix / k.go.ww) * k.go.ww;
+    const int ty = vy + k.cy, tx = vx + k.cx;
+    float acc = 0.f;
+    if (Q) {
+        const float* q = Q + (size_t)r * k.gi.size();
+        if (!k.Wk) {
+            if ((unsigned)ty < (unsigned)k.gi.wh && (unsigned)tx < (unsigned)k.gi.ww)
+                acc = q[((size_t)ty * k.gi.ww + tx) * k.Co + ci];
+        } else {
+            for (int ky = 0; ky < k.kh; ++ky) {
+                const int dy = ty - ky;
+                if (dy < 0 || dy % k.sh != 0 || dy / k.sh >= k.gi.wh) continue;
+                for (int kx = 0; kx < k.kw; ++kx) {
+                    const int dx = tx - kx;
+                    if (dx < 0 || dx % k.sw != 0 || dx / k.sw >= k.gi.ww) continue;
+                    const float* a = q + ((size_t)(dy / k.sh) * k.gi.ww + dx / k.sw) * k.Co;
+                    const float* w = k.Wk + ((size_t)(ky * k.kw + kx) * k.Co) * k.Ci + ci;
+                    for (int co = 0; co < k.Co; ++co) acc = fmaf(a[co], w[(size_t)co * k.Ci], acc);
+                }
+            }
+        }
+    } else {
+        // One-hot start row: its neuron sits at pixel q0, channel co0 of level i.
+        const int id = rows.row_id[r >= rows.R ? r - rows.R : r];
+        const int co0 = id % k.Co, q0 = k.gi.full ? id / k.Co : 0;
+        const int q0y = q0 / k.gi.ww, q0x = q0 - (q0 / k.gi.ww) * k.gi.ww;
+        if (!k.Wk) {
+            acc = (ty == q0y && tx == q0x && ci == co0) ? 1.f : 0.f;
+        } else {
+            const int ky = ty - q0y * k.sh, kx = tx - q0x * k.sw;
+            if ((unsigned)ky < (unsigned)k.kh && (unsigned)kx < (unsigned)k.kw)
+                acc = k.Wk[((size_t)(ky * k.kw + kx) * k.Co + co0) * k.Ci + ci];
+        }
+    }
+    S[idx] += acc;
+}
+
+void launch_skip_back(const SkipStep& k, const RowMap& rows, int M, const float* Q, float* S, cudaStream_t s) {
+    const int64_t total = (int64_t)M * k.go.size();
+    if (total == 0) return;
+    skip_back_kernel<<<ceil_div(total, 256), 256, 0, s>>>(k, rows, M, Q, S);
+    LB_LAUNCH();
+}
+
+__global__ void skip_adj_kernel(SkipStep k, int M, const float* __restrict__ Pbar, PhaseSplit ps,
+                                float* __restrict__ Qbar) {
+    const int ni = k.gi.size(), nw = k.go.size();
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)M * ni) return;
+    const int r = (int)(idx / ni), j = (int)(idx - (int64_t)r * ni);
+    const int co = j % k.Co, pix = j / k.Co;
+    const int qy = pix / k.gi.ww, qx = pix - (pix / k.gi.ww) * k.gi.ww;
+    auto pb = [&](int vy, int vx, int c) {
+        const int e = (vy * k.go.ww + vx) * k.Ci + c;
+        return ps.s ? Pbar[phase_dst(ps, r, e)] : Pbar[(size_t)r * nw + e];
+    };
+    float acc = 0.f;
+    if (!k.Wc) {
+        const int vy = qy - k.cy, vx = qx - k.cx;
+        if ((unsigned)vy < (unsigned)k.go.wh && (unsigned)vx < (unsigned)k.go.ww) acc = pb(vy, vx, co);
+    } else {
+        for (int ky = 0; ky < k.kh; ++ky) {
+            const int vy = qy * k.sh + ky - k.cy;
+            if ((unsigned)vy >= (unsigned)k.go.wh) continue;
+            for (int kx = 0; kx < k.kw; ++kx) {
+                const int vx = qx * k.sw + kx - k.cx;
+                if ((unsigned)vx >= (unsigned)k.go.ww) continue;
+                const float* w = k.Wc + ((size_t)(co * k.kh + ky) * k.kw + kx) * k.Ci;
+                for (int ci = 0; ci < k.Ci; ++ci) acc = fmaf(pb(vy, vx, ci), w[ci], acc);
+            }
+        }
+    }
+    Qbar[idx] += acc;
+}
+
+void launch_skip_adj(const SkipStep& k, const RowMap& rows, int M, const float* Pbar, const PhaseSplit& ps,
+                     float* Qbar, cudaStream_t s) {
+    (void)rows;
+    const int64_t total = (int64_t)M * k.gi.size();
+    if (total == 0) return;
+    skip_adj_kernel<<<ceil_div(total, 256), 256, 0, s>>>(k, M, Pbar, ps, Qbar);
     LB_LAUNCH();
 }
 

@@ -100,6 +100,7 @@ struct ConvRelaxEpi {
     const float* b_next = nullptr; // [C]
     float* P_save = nullptr;
     float* Q = nullptr;
+    const float* addend = nullptr; // [M, g.size()] or null: skip edges' A, added to P before the relaxation
 };
 struct ConvConcEpi {
     RowMap rows;
@@ -118,9 +119,10 @@ void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConc
 // ReLU relaxation of a level from its raw A window P (stored by a tensor-core
 // step): Q = relax(P) masked outside the map, bias partials (intercepts +
 // Q . b_next per row) into partial[chunk * M + r], one chunk per 1024
-// elements of a row (relax_window_chunks).  e.P_save is not used.
+// elements of a row (relax_window_chunks).  e.P_save is not used; with
+// e.addend, P + addend is written back to P first.
 int relax_window_chunks(const WinGeo& g);
-void launch_relax_window(const float* P, const ConvRelaxEpi& e, int M, float* partial, cudaStream_t s);
+void launch_relax_window(float* P, const ConvRelaxEpi& e, int M, float* partial, cudaStream_t s);
 
 // ---- adjoint --------------------------------------------------------------
 // d loss / d A at the input window from the concretisation signs: dense form
@@ -180,6 +182,28 @@ void launch_convt_start_step(const ConvStartStep& st, const ConvTStep& ct, cudaS
 // Adjoint of the back-substitution step: Qbar[v, co] = sum P_in[q, ci]
 // W[ci, co, k] over v = q s - p + k (a transposed conv; no bias term).
 void launch_convt_adj_qbar(const float* Pbar, const ConvTStep& ct, int M, float* Qbar, cudaStream_t s);
+
+// ---- residual joins (BoundedAddNode) ---------------------------------------
+// A skip edge carries the A at an Add (level i) to the ReLU output of level j
+// that feeds it, directly or through a conv; there it joins the A of the
+// main path before level j's relaxation (CROWNAnalysis::addA, :1248-1355;
+// BoundedAddNode::boundBackward, :167-279).  In window coordinates the skip
+// conv maps Q_i pixel q to S_j pixel v = q s + k - c (identity: v = q - c).
+struct SkipStep {
+    WinGeo gi, go;              // windows at level i (Q) and level j (S)
+    int Co = 0, Ci = 0;         // channels of level i / level j (equal for identity)
+    int kh = 1, kw = 1, sh = 1, sw = 1;
+    int cy = 0, cx = 0;
+    const float* Wk = nullptr;  // [kh][kw][Co][Ci]; null: identity
+    const float* Wc = nullptr;  // [Co][kh][kw][Ci]; null: identity
+};
+// S[r, v] += (skip^T Q)[r, v] over the window at level j; Q == null stands
+// for the one-hot rows of a start at level i (the start's own neuron).
+void launch_skip_back(const SkipStep& k, const RowMap& rows, int M, const float* Q, float* S, cudaStream_t s);
+// Adjoint: Qbar[r, q] += (skip Pbar)[r, q], Pbar in the window layout of
+// level j or phase-split as `ps` describes.
+void launch_skip_adj(const SkipStep& k, const RowMap& rows, int M, const float* Pbar, const PhaseSplit& ps,
+                     float* Qbar, cudaStream_t s);
 
 // dst[i] += (float)src[i], src[i] = 0 for i < n (folds the double scratch of
 // launch_relax_adjoint_win into kbar / bbar).

@@ -53,13 +53,37 @@ void DevCache::release() {
 }
 
 // ------------------------------------------------------------ Model
-static bool pass_through(int t) { return t == LB200_NODE_FLATTEN || t == LB200_NODE_IDENTITY; }
+namespace {
+// One input of a pre-activation: the output of level `src` (its ReLU, or the
+// input for level 0) through an affine node (with a BatchNorm folded in), or
+// directly (an Add operand that is an activation: an identity skip).
+struct EdgeDesc {
+    int src = -1;
+    int affine = -1;  // node id, -1: identity
+    int bn = -1;      // BatchNorm node folded into the affine node, or -1
+};
+// What a node's output is: an activation (level) or a sum of edges not yet
+// consumed by a ReLU.
+struct ValDesc {
+    int kind = 0;  // 0: unsupported, 1: activation of `level`, 2: pre-activation sum
+    int level = -1;
+    std::vector<EdgeDesc> edges;
+};
+}  // namespace
 
+// The graph must be Luna's feed-forward verification nets: an input, then
+// pre-activations each feeding one ReLU, each pre-activation the sum of an
+// affine map (Linear / Conv2d / ConvTranspose2d, optionally followed by
+// BatchNorm) of the level just below and, through an Add
+// (BoundedAddNode, two tensor operands), of skip edges from earlier levels
+// (the activation itself, or a conv of it); the output is a Linear of the
+// last level.  Flatten and Identity nodes pass through.
 Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
     if (!g || g->num_nodes <= 0 || !g->nodes) throw std::invalid_argument("empty graph");
     LB_CUDA(cudaSetDevice(device_));
     const int n = g->num_nodes;
     std::vector<std::vector<int>> dependents(n);
+    std::vector<int> indeg(n, 0);
     for (int i = 0; i < n; ++i) {
         const auto& d = g->nodes[i];
         if (d.num_inputs < 0 || d.num_inputs > 4) throw std::invalid_argument("bad num_inputs");
@@ -67,208 +91,362 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
             if (d.inputs[k] < 0 || d.inputs[k] >= n) throw std::invalid_argument("bad input index");
             dependents[d.inputs[k]].push_back(i);
         }
+        indeg[i] = d.num_inputs;
     }
     if (g->input_index < 0 || g->input_index >= n || g->nodes[g->input_index].type != LB200_NODE_INPUT)
         throw std::invalid_argument("input_index must name an INPUT node");
-    // Walk the chain Input -> [affine -> ReLU]* -> affine, affine = Linear or
-    // Conv2d (Flatten/Identity pass through).  Graphs with joins or other
-    // node kinds are rejected.
-    int cur = g->input_index;
-    bool expect_affine = true;
-    std::vector<int> affine;
-    std::vector<int> bn_after;  // BatchNorm node folded into affine[k], or -1
-    while (true) {
-        if (cur == g->output_index) break;
-        if (dependents[cur].size() != 1)
-            throw std::invalid_argument("graph is not a chain (node " + std::to_string(cur) + " has " +
-                                        std::to_string(dependents[cur].size()) +
-                                        " consumers); supported: Input/Linear/Conv/ReLU/Flatten/Identity chains");
-        const int nx = dependents[cur][0];
-        const auto& d = g->nodes[nx];
-        if (d.num_inputs != 1) throw std::invalid_argument("multi-input node in chain");
-        if (d.type == LB200_NODE_LINEAR || d.type == LB200_NODE_CONV || d.type == LB200_NODE_CONVTRANSPOSE) {
-            if (!expect_affine) throw std::invalid_argument("two affine nodes without a ReLU between");
-            if (!d.weight) throw std::invalid_argument("affine node without weight");
-            affine.push_back(nx);
-            bn_after.push_back(-1);
-            expect_affine = false;
-            preact_node_ids_.push_back(nx);
-        } else if (d.type == LB200_NODE_BATCHNORM) {
-            // Folded into the affine layer before it (an affine map of an
-            // affine map; BoundedBatchNormNode.cpp:68-80,180-532).
-            if (expect_affine || bn_after.empty() || bn_after.back() >= 0)
-                throw std::invalid_argument("BatchNorm must directly follow a Linear or Conv node");
-            if (!d.weight || !d.bias || !d.running_mean || !d.running_var)
-                throw std::invalid_argument("BatchNorm node without parameters");
-            bn_after.back() = nx;
-            preact_node_ids_.back() = nx;
-        } else if (d.type == LB200_NODE_RELU) {
-            if (expect_affine) throw std::invalid_argument("ReLU must follow a Linear or Conv node");
-            expect_affine = true;
-        } else if (!pass_through(d.type)) {
-            throw std::invalid_argument("node type " + std::to_string(d.type) +
-                                        " is not supported by this engine build");
+    if (g->output_index < 0 || g->output_index >= n) throw std::invalid_argument("bad output_index");
+    // Topological order (Kahn, ties by node id: TorchModel::topologicalSort).
+    std::vector<int> order;
+    {
+        std::vector<int> q;
+        for (int i = 0; i < n; ++i)
+            if (indeg[i] == 0) q.push_back(i);
+        for (size_t h = 0; h < q.size(); ++h) {
+            order.push_back(q[h]);
+            for (int d : dependents[q[h]])
+                if (--indeg[d] == 0) q.push_back(d);
         }
-        cur = nx;
+        if ((int)order.size() != n) throw std::invalid_argument("graph has a cycle");
     }
-    const int out_t = g->nodes[g->output_index].type;
-    if (out_t != LB200_NODE_LINEAR || expect_affine || bn_after.back() >= 0)
-        throw std::invalid_argument("the output node must be the last Linear of the chain");
-    if (affine.size() < 2) throw std::invalid_argument("need at least two affine layers");
-    preact_node_ids_.pop_back();  // the output layer feeds no ReLU
-    K_ = (int)affine.size();
-    layers_.resize(K_);
-    const auto& din = g->nodes[g->input_index];
-    MapShape prev;
-    prev.C = din.out_shape[0];
-    prev.H = std::max(1, din.out_shape[1]);
-    prev.W = std::max(1, din.out_shape[2]);
-    prev.spatial = g->nodes[affine[0]].type == LB200_NODE_CONV;
-    if (!prev.spatial) prev = MapShape{prev.n(), 1, 1, false};
-    for (int k = 0; k < K_; ++k) {
-        const auto& d = g->nodes[affine[k]];
-        Layer& L = layers_[k];
-        L.conv = d.type == LB200_NODE_CONV;
-        L.convt = d.type == LB200_NODE_CONVTRANSPOSE;
-        L.in = prev;
-        if (L.convt) {
-            has_conv_ = true;
-            if (!prev.spatial) throw std::invalid_argument("a transposed conv must follow the input or a conv");
-            if (k == 0) throw std::invalid_argument("a transposed conv as the first layer is not supported");
-            if (bn_after[k] >= 0) throw std::invalid_argument("BatchNorm after a transposed conv is not supported");
-            L.kh = d.kernel[0];
-            L.kw = d.kernel[1];
-            L.sh = d.stride[0];
-            L.sw = d.stride[1];
-            L.ph = d.padding[0];
-            L.pw = d.padding[1];
-            if (d.output_padding[0] != 0 || d.output_padding[1] != 0)
-                throw std::invalid_argument("ConvTranspose output_padding must be 0 (BoundedConvTransposeNode.cpp:61-63)");
-            if (L.kh <= 0 || L.kw <= 0 || L.sh <= 0 || L.sw <= 0 || L.ph < 0 || L.pw < 0)
-                throw std::invalid_argument("bad transposed-conv geometry");
-            L.out.C = d.out_shape[0];
-            L.out.H = (prev.H - 1) * L.sh - 2 * L.ph + L.kh;
-            L.out.W = (prev.W - 1) * L.sw - 2 * L.pw + L.kw;
-            L.out.spatial = true;
-            if (L.out.H != d.out_shape[1] || L.out.W != d.out_shape[2] || L.out.H <= 0 || L.out.W <= 0)
-                throw std::invalid_argument("transposed-conv out_shape does not match its geometry");
-        } else if (L.conv) {
-            has_conv_ = true;
-            if (!prev.spatial) throw std::invalid_argument("a conv layer must follow the input or another conv");
-            L.kh = d.kernel[0];
-            L.kw = d.kernel[1];
-            L.sh = d.stride[0];
-            L.sw = d.stride[1];
-            L.ph = d.padding[0];
-            L.pw = d.padding[1];
-            if (L.kh <= 0 || L.kw <= 0 || L.sh <= 0 || L.sw <= 0 || L.ph < 0 || L.pw < 0)
-                throw std::invalid_argument("bad conv geometry");
-            L.out.C = d.out_shape[0];
-            L.out.H = (prev.H + 2 * L.ph - L.kh) / L.sh + 1;
-            L.out.W = (prev.W + 2 * L.pw - L.kw) / L.sw + 1;
-            L.out.spatial = true;
-            if (L.out.H != d.out_shape[1] || L.out.W != d.out_shape[2])
-                throw std::invalid_argument("conv out_shape does not match its geometry");
-        } else {
-            if (d.in_features <= 0 || d.out_features <= 0) throw std::invalid_argument("Linear node without sizes");
-            if (d.in_features != prev.n()) throw std::invalid_argument("width mismatch");
-            L.out = MapShape{(int)d.out_features, 1, 1, false};
-        }
-        L.n_in = L.in.n();
-        L.n_out = L.out.n();
-        const int Ci = L.in.C, Co = L.out.C;
-        // The node's weight and bias with a following BatchNorm folded in:
-        // y = w (affine(x)) + (B - mean w), w = scale / sqrt(var + eps) per
-        // output channel (conv) or feature (Linear), computed in fp32 as
-        // BoundedBatchNormNode::ensureCachedParams does (:68-80).
-        const int nch = (L.conv || L.convt) ? Co : L.n_out;
-        const size_t per_ch = (L.conv || L.convt) ? (size_t)Ci * L.kh * L.kw : (size_t)L.n_in;
-        std::vector<float> wsrc(d.weight, d.weight + (size_t)nch * per_ch), bsrc(nch, 0.f);
-        if (d.bias)
-            for (int c = 0; c < nch; ++c) bsrc[c] = d.bias[c];
-        if (bn_after[k] >= 0) {
-            const auto& nb = g->nodes[bn_after[k]];
-            for (int c = 0; c < nch; ++c) {
-                const float w = nb.weight[c] / std::sqrt(nb.running_var[c] + nb.eps);
-                for (size_t q = 0; q < per_ch; ++q) wsrc[(size_t)c * per_ch + q] *= w;
-                bsrc[c] = bsrc[c] * w + (nb.bias[c] - nb.running_mean[c] * w);
+    auto bad = [&](int i, const std::string& why) {
+        throw std::invalid_argument("node " + std::to_string(i) + " (type " + std::to_string(g->nodes[i].type) +
+                                    "): " + why);
+    };
+    std::vector<ValDesc> val(n);
+    std::vector<std::vector<EdgeDesc>> lvl_edges(1);  // level 0 = input
+    std::vector<int> lvl_node(1, g->input_index);     // node whose output is the level's pre-activation
+    for (int i : order) {
+        const auto& d = g->nodes[i];
+        ValDesc& v = val[i];
+        auto operand = [&](int k) -> const ValDesc& { return val[d.inputs[k]]; };
+        switch (d.type) {
+        case LB200_NODE_INPUT:
+            if (i != g->input_index) bad(i, "a second input node");
+            v.kind = 1;
+            v.level = 0;
+            break;
+        case LB200_NODE_FLATTEN:
+        case LB200_NODE_IDENTITY:
+            if (d.num_inputs != 1) bad(i, "expects one input");
+            v = operand(0);
+            break;
+        case LB200_NODE_LINEAR:
+        case LB200_NODE_CONV:
+        case LB200_NODE_CONVTRANSPOSE:
+            if (d.num_inputs != 1 || operand(0).kind != 1)
+                bad(i, "an affine node must take the input or a ReLU output");
+            if (!d.weight) bad(i, "affine node without weight");
+            v.kind = 2;
+            v.edges = {EdgeDesc{operand(0).level, i, -1}};
+            break;
+        case LB200_NODE_BATCHNORM:
+            // Folded into the affine node before it (an affine map of an affine
+            // map; BoundedBatchNormNode.cpp:68-80,180-532).
+            if (d.num_inputs != 1 || operand(0).kind != 2 || operand(0).edges.size() != 1 ||
+                operand(0).edges[0].affine < 0 || operand(0).edges[0].bn >= 0)
+                bad(i, "BatchNorm must directly follow a Linear or Conv node");
+            if (!d.weight || !d.bias || !d.running_mean || !d.running_var) bad(i, "BatchNorm without parameters");
+            v = operand(0);
+            v.edges[0].bn = i;
+            break;
+        case LB200_NODE_ADD:
+            // BoundedAddNode of two tensors (:167-279): A reaches both operands.
+            if (d.num_inputs != 2) bad(i, "Add with a constant operand is not supported");
+            v.kind = 2;
+            for (int k = 0; k < 2; ++k) {
+                const ValDesc& o = operand(k);
+                if (o.kind == 1)
+                    v.edges.push_back(EdgeDesc{o.level, -1, -1});
+                else if (o.kind == 2)
+                    v.edges.insert(v.edges.end(), o.edges.begin(), o.edges.end());
+                else
+                    bad(i, "unsupported Add operand");
             }
+            break;
+        case LB200_NODE_RELU:
+            if (d.num_inputs != 1 || operand(0).kind != 2) bad(i, "a ReLU must follow an affine node or an Add");
+            lvl_edges.push_back(operand(0).edges);
+            lvl_node.push_back(d.inputs[0]);
+            v.kind = 1;
+            v.level = (int)lvl_edges.size() - 1;
+            break;
+        default:
+            bad(i, "node kind not supported by this engine build");
         }
-        std::vector<float> W, Wt, b(bsrc), bn(L.n_out, 0.f);
-        if (L.convt) {
-            // ONNX ConvTranspose weight [Ci, Co, kh, kw] -> Wg [Ci][kh][kw][Co], Wa [kh][kw][Co][Ci].
-            W.resize((size_t)Ci * L.kh * L.kw * Co);
-            Wt.resize(W.size());
-            for (int c = 0; c < Ci; ++c)
-                for (int o = 0; o < Co; ++o)
-                    for (int y = 0; y < L.kh; ++y)
-                        for (int x = 0; x < L.kw; ++x) {
-                            const float w = wsrc[(((size_t)c * Co + o) * L.kh + y) * L.kw + x];
-                            W[(((size_t)c * L.kh + y) * L.kw + x) * Co + o] = w;
-                            Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
-                        }
-            for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
-        } else if (L.conv) {
-            // ONNX Conv weight [Co, Ci, kh, kw] -> Wc [Co][kh][kw][Ci], Wk [kh][kw][Co][Ci].
-            W.resize((size_t)Co * L.kh * L.kw * Ci);
-            Wt.resize(W.size());
-            for (int o = 0; o < Co; ++o)
-                for (int c = 0; c < Ci; ++c)
-                    for (int y = 0; y < L.kh; ++y)
-                        for (int x = 0; x < L.kw; ++x) {
-                            const float w = wsrc[(((size_t)o * Ci + c) * L.kh + y) * L.kw + x];
-                            W[(((size_t)o * L.kh + y) * L.kw + x) * Ci + c] = w;
-                            Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
-                        }
-            for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
-        } else {
-            W.resize((size_t)L.n_out * L.n_in);
-            Wt.resize(W.size());
-            const int HW = L.in.H * L.in.W;
-            for (int o = 0; o < L.n_out; ++o)
-                for (int i = 0; i < L.n_in; ++i) {
-                    // Input feature i in the engine's order; Luna's column is
-                    // its CHW index when the input is a flattened conv map.
-                    const int col = L.in.spatial ? (i % Ci) * HW + i / Ci : i;
-                    // BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
-                    const float w = d.scale * wsrc[(size_t)o * L.n_in + col];
-                    W[(size_t)o * L.n_in + i] = w;
-                    Wt[(size_t)i * L.n_out + o] = w;
-                }
-            bn = b;
+        // A pre-activation sum is consumed exactly once (by its ReLU, an Add,
+        // a BatchNorm or as the output).
+        if (v.kind == 2 && i != g->output_index && dependents[i].size() != 1)
+            bad(i, "a pre-activation used by several nodes");
+    }
+    if (val[g->output_index].kind != 2) throw std::invalid_argument("the output node must be an affine node");
+    lvl_edges.push_back(val[g->output_index].edges);
+    lvl_node.push_back(g->output_index);
+    K_ = (int)lvl_edges.size() - 1;
+    if (K_ < 2) throw std::invalid_argument("need at least two affine layers");
+    // Main edge of every level: the affine edge from the level just below.
+    layers_.resize(K_);
+    skips_.assign(K_ + 1, {});
+    std::vector<EdgeDesc> main_edge(K_ + 1);
+    for (int m = 1; m <= K_; ++m) {
+        bool found = false;
+        for (const EdgeDesc& e : lvl_edges[m]) {
+            if (!found && e.src == m - 1 && e.affine >= 0) {
+                main_edge[m] = e;
+                found = true;
+                continue;
+            }
+            if (e.src < 1 || e.src > m - 2)
+                throw std::invalid_argument("level " + std::to_string(m) +
+                                            ": a skip edge must come from a ReLU output at least two levels below");
+            SkipEdge s;
+            s.src = e.src;
+            s.node = e.affine;
+            s.bn = e.bn;
+            skips_[m].push_back(s);
         }
-        L.W = weights_.as<float>(key("W", k), W.size());
-        L.Wt = weights_.as<float>(key("Wt", k), Wt.size());
-        L.b = weights_.as<float>(key("b", k), b.size());
-        L.b_neuron = weights_.as<float>(key("bn", k), bn.size());
-        LB_CUDA(cudaMemcpy(L.W, W.data(), W.size() * 4, cudaMemcpyHostToDevice));
-        LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
-        LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
-        LB_CUDA(cudaMemcpy(L.b_neuron, bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
-        if (L.conv) build_tc_conv(L, wsrc.data(), k);
-        if (!L.conv) {
-            L.W_hi = weights_.as<float>(key("Whi", k), W.size());
-            L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
-            L.Wt_hi = weights_.as<float>(key("Wthi", k), Wt.size());
-            L.Wt_lo = weights_.as<float>(key("Wtlo", k), Wt.size());
-            launch_split_tf32(L.W, L.W_hi, L.W_lo, (int64_t)W.size(), 0);
-            launch_split_tf32(L.Wt, L.Wt_hi, L.Wt_lo, (int64_t)Wt.size(), 0);
+        if (!found)
+            throw std::invalid_argument("level " + std::to_string(m) +
+                                        ": no affine input from the level below (unsupported graph shape)");
+    }
+    for (int m = 1; m < K_; ++m) preact_node_ids_.push_back(lvl_node[m]);
+    if (g->nodes[main_edge[K_].affine].type != LB200_NODE_LINEAR || main_edge[K_].bn >= 0 || !skips_[K_].empty())
+        throw std::invalid_argument("the output node must be a Linear of the last ReLU");
+
+    const auto& din = g->nodes[g->input_index];
+    MapShape in0;
+    in0.C = din.out_shape[0];
+    in0.H = std::max(1, din.out_shape[1]);
+    in0.W = std::max(1, din.out_shape[2]);
+    const int t1 = g->nodes[main_edge[1].affine].type;
+    in0.spatial = t1 == LB200_NODE_CONV || t1 == LB200_NODE_CONVTRANSPOSE;
+    if (!in0.spatial) in0 = MapShape{in0.n(), 1, 1, false};
+    for (int m = 1; m <= K_; ++m) {
+        const MapShape& prev = m == 1 ? in0 : layers_[m - 2].out;
+        build_layer(layers_[m - 1], g, main_edge[m].affine, main_edge[m].bn, prev, m - 1, m == 1);
+        for (size_t e = 0; e < skips_[m].size(); ++e) {
+            SkipEdge& s = skips_[m][e];
+            const MapShape& src = layers_[s.src - 1].out;
+            const MapShape& dst = layers_[m - 1].out;
+            if (s.node >= 0) {
+                if (g->nodes[s.node].type != LB200_NODE_CONV)
+                    throw std::invalid_argument("a skip edge through an affine node must be a Conv2d");
+                s.L = std::make_shared<Layer>();
+                build_layer(*s.L, g, s.node, s.bn, src, 1000 + 8 * m + (int)e, false);
+                if (s.L->out.C != dst.C || s.L->out.H != dst.H || s.L->out.W != dst.W)
+                    throw std::invalid_argument("level " + std::to_string(m) + ": Add operands differ in shape");
+            } else if (src.C != dst.C || src.H != dst.H || src.W != dst.W || src.spatial != dst.spatial) {
+                throw std::invalid_argument("level " + std::to_string(m) + ": Add operands differ in shape");
+            }
+            // The skip's source must be relaxed by a conv step (its addend
+            // joins that step's relaxation epilogue).
+            if (!layers_[s.src].conv)
+                throw std::invalid_argument("a skip source must feed a Conv2d on the main path");
+            if (layers_[m - 1].convt) throw std::invalid_argument("an Add after a transposed conv is not supported");
         }
-        LB_CUDA(cudaDeviceSynchronize());
-        prev = L.out;
     }
     if (layers_[K_ - 1].conv) throw std::invalid_argument("the output layer must be Linear");
-    // Row geometry of every start at every level below it.
+    // Bias that the back-substitution adds for level m: the main edge's (none
+    // for a ConvTranspose: Luna's A is flat there) plus every skip conv's.
+    lvl_b_.assign(K_ + 1, nullptr);
+    lvl_bn_.assign(K_ + 1, nullptr);
+    for (int m = 1; m <= K_; ++m) {
+        const Layer& L = layers_[m - 1];
+        if (L.convt) continue;
+        if (skips_[m].empty()) {
+            lvl_b_[m] = L.b;
+            lvl_bn_[m] = L.b_neuron;
+            continue;
+        }
+        const int nc = L.conv ? L.out.C : L.n_out;
+        std::vector<float> b(nc), bs(nc), bn((size_t)L.n_out);
+        LB_CUDA(cudaMemcpy(b.data(), L.b, nc * 4, cudaMemcpyDeviceToHost));
+        for (const SkipEdge& s : skips_[m]) {
+            if (!s.L) continue;
+            LB_CUDA(cudaMemcpy(bs.data(), s.L->b, nc * 4, cudaMemcpyDeviceToHost));
+            for (int c = 0; c < nc; ++c) b[c] += bs[c];
+        }
+        for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % nc];
+        lvl_b_[m] = weights_.as<float>(key("lvlb", m), b.size());
+        lvl_bn_[m] = weights_.as<float>(key("lvlbn", m), bn.size());
+        LB_CUDA(cudaMemcpy(lvl_b_[m], b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+        LB_CUDA(cudaMemcpy(lvl_bn_[m], bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
+    }
+    build_geometry();
+    lb200_options_default(&opt_);
+}
+
+// One affine edge: the node's weight and bias with a following BatchNorm
+// folded in, laid out for the engine's kernels.
+void Model::build_layer(Layer& L, const lb200_graph_desc* g, int node, int bn_node, const MapShape& prev, int k,
+                        bool first) {
+    const auto& d = g->nodes[node];
+    L.conv = d.type == LB200_NODE_CONV;
+    L.convt = d.type == LB200_NODE_CONVTRANSPOSE;
+    L.in = prev;
+    if (L.convt) {
+        has_conv_ = true;
+        if (!prev.spatial) throw std::invalid_argument("a transposed conv must follow the input or a conv");
+        if (first) throw std::invalid_argument("a transposed conv as the first layer is not supported");
+        if (bn_node >= 0) throw std::invalid_argument("BatchNorm after a transposed conv is not supported");
+        L.kh = d.kernel[0];
+        L.kw = d.kernel[1];
+        L.sh = d.stride[0];
+        L.sw = d.stride[1];
+        L.ph = d.padding[0];
+        L.pw = d.padding[1];
+        if (d.output_padding[0] != 0 || d.output_padding[1] != 0)
+            throw std::invalid_argument("ConvTranspose output_padding must be 0 (BoundedConvTransposeNode.cpp:61-63)");
+        if (L.kh <= 0 || L.kw <= 0 || L.sh <= 0 || L.sw <= 0 || L.ph < 0 || L.pw < 0)
+            throw std::invalid_argument("bad transposed-conv geometry");
+        L.out.C = d.out_shape[0];
+        L.out.H = (prev.H - 1) * L.sh - 2 * L.ph + L.kh;
+        L.out.W = (prev.W - 1) * L.sw - 2 * L.pw + L.kw;
+        L.out.spatial = true;
+        if (L.out.H != d.out_shape[1] || L.out.W != d.out_shape[2] || L.out.H <= 0 || L.out.W <= 0)
+            throw std::invalid_argument("transposed-conv out_shape does not match its geometry");
+    } else if (L.conv) {
+        has_conv_ = true;
+        if (!prev.spatial) throw std::invalid_argument("a conv layer must follow the input or another conv");
+        L.kh = d.kernel[0];
+        L.kw = d.kernel[1];
+        L.sh = d.stride[0];
+        L.sw = d.stride[1];
+        L.ph = d.padding[0];
+        L.pw = d.padding[1];
+        if (L.kh <= 0 || L.kw <= 0 || L.sh <= 0 || L.sw <= 0 || L.ph < 0 || L.pw < 0)
+            throw std::invalid_argument("bad conv geometry");
+        L.out.C = d.out_shape[0];
+        L.out.H = (prev.H + 2 * L.ph - L.kh) / L.sh + 1;
+        L.out.W = (prev.W + 2 * L.pw - L.kw) / L.sw + 1;
+        L.out.spatial = true;
+        if (L.out.H != d.out_shape[1] || L.out.W != d.out_shape[2])
+            throw std::invalid_argument("conv out_shape does not match its geometry");
+    } else {
+        if (d.in_features <= 0 || d.out_features <= 0) throw std::invalid_argument("Linear node without sizes");
+        if (d.in_features != prev.n()) throw std::invalid_argument("width mismatch");
+        L.out = MapShape{(int)d.out_features, 1, 1, false};
+    }
+    L.n_in = L.in.n();
+    L.n_out = L.out.n();
+    const int Ci = L.in.C, Co = L.out.C;
+    // The node's weight and bias with a following BatchNorm folded in:
+    // y = w (affine(x)) + (B - mean w), w = scale / sqrt(var + eps) per
+    // output channel (conv) or feature (Linear), computed in fp32 as
+    // BoundedBatchNormNode::ensureCachedParams does (:68-80).
+    const int nch = (L.conv || L.convt) ? Co : L.n_out;
+    const size_t per_ch = (L.conv || L.convt) ? (size_t)Ci * L.kh * L.kw : (size_t)L.n_in;
+    std::vector<float> wsrc(d.weight, d.weight + (size_t)nch * per_ch), bsrc(nch, 0.f);
+    if (d.bias)
+        for (int c = 0; c < nch; ++c) bsrc[c] = d.bias[c];
+    if (bn_node >= 0) {
+        const auto& nb = g->nodes[bn_node];
+        for (int c = 0; c < nch; ++c) {
+            const float w = nb.weight[c] / std::sqrt(nb.running_var[c] + nb.eps);
+            for (size_t q = 0; q < per_ch; ++q) wsrc[(size_t)c * per_ch + q] *= w;
+            bsrc[c] = bsrc[c] * w + (nb.bias[c] - nb.running_mean[c] * w);
+        }
+    }
+    std::vector<float> W, Wt, b(bsrc), bn(L.n_out, 0.f);
+    if (L.convt) {
+        // ONNX ConvTranspose weight [Ci, Co, kh, kw] -> Wg [Ci][kh][kw][Co], Wa [kh][kw][Co][Ci].
+        W.resize((size_t)Ci * L.kh * L.kw * Co);
+        Wt.resize(W.size());
+        for (int c = 0; c < Ci; ++c)
+            for (int o = 0; o < Co; ++o)
+                for (int y = 0; y < L.kh; ++y)
+                    for (int x = 0; x < L.kw; ++x) {
+                        const float w = wsrc[(((size_t)c * Co + o) * L.kh + y) * L.kw + x];
+                        W[(((size_t)c * L.kh + y) * L.kw + x) * Co + o] = w;
+                        Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
+                    }
+        for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
+    } else if (L.conv) {
+        // ONNX Conv weight [Co, Ci, kh, kw] -> Wc [Co][kh][kw][Ci], Wk [kh][kw][Co][Ci].
+        W.resize((size_t)Co * L.kh * L.kw * Ci);
+        Wt.resize(W.size());
+        for (int o = 0; o < Co; ++o)
+            for (int c = 0; c < Ci; ++c)
+                for (int y = 0; y < L.kh; ++y)
+                    for (int x = 0; x < L.kw; ++x) {
+                        const float w = wsrc[(((size_t)o * Ci + c) * L.kh + y) * L.kw + x];
+                        W[(((size_t)o * L.kh + y) * L.kw + x) * Ci + c] = w;
+                        Wt[(((size_t)y * L.kw + x) * Co + o) * Ci + c] = w;
+                    }
+        for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % Co];
+    } else {
+        W.resize((size_t)L.n_out * L.n_in);
+        Wt.resize(W.size());
+        const int HW = L.in.H * L.in.W;
+        for (int o = 0; o < L.n_out; ++o)
+            for (int i = 0; i < L.n_in; ++i) {
+                // Input feature i in the engine's order; Luna's column is
+                // its CHW index when the input is a flattened conv map.
+                const int col = L.in.spatial ? (i % Ci) * HW + i / Ci : i;
+                // BoundedLinearNode bakes alpha (Gemm scale) into the weight (:91-93).
+                const float w = d.scale * wsrc[(size_t)o * L.n_in + col];
+                W[(size_t)o * L.n_in + i] = w;
+                Wt[(size_t)i * L.n_out + o] = w;
+            }
+        bn = b;
+    }
+    L.W = weights_.as<float>(key("W", k), W.size());
+    L.Wt = weights_.as<float>(key("Wt", k), Wt.size());
+    L.b = weights_.as<float>(key("b", k), b.size());
+    L.b_neuron = weights_.as<float>(key("bn", k), bn.size());
+    LB_CUDA(cudaMemcpy(L.W, W.data(), W.size() * 4, cudaMemcpyHostToDevice));
+    LB_CUDA(cudaMemcpy(L.Wt, Wt.data(), Wt.size() * 4, cudaMemcpyHostToDevice));
+    LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
+    LB_CUDA(cudaMemcpy(L.b_neuron, bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
+    if (L.conv && k < 1000) build_tc_conv(L, wsrc.data(), k);
+    if (!L.conv && !L.convt) {
+        L.W_hi = weights_.as<float>(key("Whi", k), W.size());
+        L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
+        L.Wt_hi = weights_.as<float>(key("Wthi", k), Wt.size());
+        L.Wt_lo = weights_.as<float>(key("Wtlo", k), Wt.size());
+        launch_split_tf32(L.W, L.W_hi, L.W_lo, (int64_t)W.size(), 0);
+        launch_split_tf32(L.Wt, L.Wt_hi, L.Wt_lo, (int64_t)Wt.size(), 0);
+    }
+    LB_CUDA(cudaDeviceSynchronize());
+}
+
+// Window of a conv's input map that the transposed conv of window `w` (on
+// its output map) covers: the receptive field, (w - 1) s + k wide.
+static WinGeo conv_input_window(const WinGeo& w, const Layer& L) {
+    WinGeo v = w;
+    v.C = L.in.C;
+    v.H = L.in.H;
+    v.W = L.in.W;
+    if (w.full) {
+        v.wh = L.in.H;
+        v.ww = L.in.W;
+        return v;
+    }
+    v.wh = (w.wh - 1) * L.sh + L.kh;
+    v.ww = (w.ww - 1) * L.sw + L.kw;
+    v.mul_y *= L.sh;
+    v.mul_x *= L.sw;
+    v.off_y = w.off_y * L.sh - L.ph;
+    v.off_x = w.off_x * L.sw - L.pw;
+    return v;
+}
+
+// Row geometry of every start at every level up to it: receptive-field
+// windows for a conv start with only convs (and identity / conv skips)
+// below it, whole maps otherwise.  A skip's window must lie inside the main
+// path's window at its source level (true for "same"-padded blocks and 1x1
+// projections).
+void Model::build_geometry() {
     geo_.assign(K_ + 1, {});
     for (int st = 2; st <= K_; ++st) {
         std::vector<WinGeo>& gv = geo_[st];
-        gv.resize(st);
-        // Conv starts keep receptive-field windows when only convs lie below
-        // them; otherwise (a Linear or transposed conv below) their rows are
-        // whole maps.
+        gv.resize(st + 1);
         bool window = st < K_ && layers_[st - 1].conv;
-        for (int m = st - 1; m >= 1 && window; --m) window = layers_[m - 1].conv;
-        for (int m = 0; m < st; ++m) {
+        for (int m = st; m >= 1 && window; --m) {
+            window = layers_[m - 1].conv;
+            for (const SkipEdge& s : skips_[m]) window = window && (!s.L || s.L->conv);
+        }
+        for (int m = 0; m <= st; ++m) {
             const MapShape& ms = map(m);
             WinGeo w;
             w.C = ms.C;
@@ -279,35 +457,25 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
             gv[m] = w;
         }
         if (!window) continue;
-        const Layer& Ls = layers_[st - 1];
-        WinGeo w = gv[st - 1];
-        w.full = 0;
-        w.wh = Ls.kh;
-        w.ww = Ls.kw;
-        w.mul_y = Ls.sh;
-        w.mul_x = Ls.sw;
-        w.off_y = -Ls.ph;
-        w.off_x = -Ls.pw;
-        w.st_C = Ls.out.C;
-        w.st_W = Ls.out.W;
-        gv[st - 1] = w;
-        for (int m = st - 1; m >= 1; --m) {
-            const Layer& L = layers_[m - 1];
-            WinGeo v = gv[m];
-            const MapShape& ms = map(m - 1);
-            v.C = ms.C;
-            v.H = ms.H;
-            v.W = ms.W;
-            v.wh = (v.wh - 1) * L.sh + L.kh;
-            v.ww = (v.ww - 1) * L.sw + L.kw;
-            v.mul_y *= L.sh;
-            v.mul_x *= L.sw;
-            v.off_y = v.off_y * L.sh - L.ph;
-            v.off_x = v.off_x * L.sw - L.pw;
-            gv[m - 1] = v;
-        }
+        // The start row itself: one pixel of the start map.
+        WinGeo& ws = gv[st];
+        ws.full = 0;
+        ws.wh = ws.ww = 1;
+        ws.mul_y = ws.mul_x = 1;
+        ws.off_y = ws.off_x = 0;
+        ws.st_C = map(st).C;
+        ws.st_W = map(st).W;
+        for (int m = st; m >= 1; --m) gv[m - 1] = conv_input_window(gv[m], layers_[m - 1]);
+        for (int m = st; m >= 2; --m)
+            for (const SkipEdge& s : skips_[m]) {
+                const WinGeo w = s.L ? conv_input_window(gv[m], *s.L) : gv[m];
+                const WinGeo& o = gv[s.src];
+                if (w.mul_y != o.mul_y || w.mul_x != o.mul_x || w.off_y < o.off_y || w.off_x < o.off_x ||
+                    w.off_y + w.wh > o.off_y + o.wh || w.off_x + w.ww > o.off_x + o.ww)
+                    throw std::invalid_argument("level " + std::to_string(m) +
+                                                ": a skip edge reaches outside the main path's window");
+            }
     }
-    lb200_options_default(&opt_);
 }
 
 // Weight matrices of the tensor-core conv steps of one conv layer.
@@ -512,18 +680,82 @@ ConvTStep Model::convt_step(int m) const {
 // matrix once they are wider than a conv input (BoundedConvNode.cpp:671-694);
 // the concretisation form follows (CROWNAnalysis.cpp:791-848 vs :1164-1224).
 int Model::start_form(int st) const {
-    if (st >= K_ || !layers_[st - 1].conv || !opt_.use_patches_mode) return CONC_DENSE;
+    // The start node: a conv (or its BatchNorm) starts in patches mode; an
+    // Add start is a dense identity.
+    if (st >= K_ || !layers_[st - 1].conv || !skips_[st].empty() || !opt_.use_patches_mode) return CONC_DENSE;
     if (layers_[st - 1].n_out <= 4096) return CONC_DENSE;
     if (geo_[st][st - 1].full)
         throw std::invalid_argument("a conv start above a Linear or transposed conv with more than 4096 features "
                                     "(Luna's patches mode there) is not supported");
-    int width = 0;
+    // (patches?, patch width) of the A reaching each level: a conv widens
+    // the patch to (w - 1) s + k and turns it into a matrix once it is wider
+    // than its input; joins keep patches only when every operand is patches
+    // (CROWNAnalysis::addA, :1248-1355) and pad to the widest (Patches::add).
+    std::vector<int> patches(st + 1, -1), width(st + 1, 0);
+    patches[st] = 1;
+    width[st] = 1;  // identity patches act as 1 x 1 patches
+    auto join = [&](int j, bool p, int w) {
+        if (patches[j] < 0) {
+            patches[j] = p ? 1 : 0;
+            width[j] = w;
+        } else {
+            patches[j] = (patches[j] && p) ? 1 : 0;
+            width[j] = std::max(width[j], w);
+        }
+    };
+    auto through = [&](const Layer& L, bool p, int w, int& w_out) {
+        w_out = (w - 1) * L.sw + L.kw;
+        return p && L.conv && w_out <= L.in.W;
+    };
     for (int m = st; m >= 1; --m) {
-        const Layer& L = layers_[m - 1];
-        width = m == st ? L.kw : (width - 1) * L.sw + L.kw;
-        if (width > L.in.W) return CONC_DENSE;
+        const bool p = patches[m] == 1;
+        int w2;
+        const bool p2 = through(layers_[m - 1], p, width[m], w2);
+        join(m - 1, p2, w2);
+        for (const SkipEdge& sk : skips_[m]) {
+            if (sk.L) {
+                const bool p3 = through(*sk.L, p, width[m], w2);
+                join(sk.src, p3, w2);
+            } else {
+                join(sk.src, p, width[m]);
+            }
+        }
     }
-    return CONC_PATCHES;
+    return patches[0] == 1 ? CONC_PATCHES : CONC_DENSE;
+}
+
+SkipStep Model::skip_step(int st, int m, int e) const {
+    const SkipEdge& sk = skips_[m][e];
+    const WinGeo& gi = geo_[st][m];
+    const WinGeo& go = geo_[st][sk.src];
+    SkipStep k;
+    k.gi = gi;
+    k.go = go;
+    k.Co = map(m).C;
+    k.Ci = map(sk.src).C;
+    if (sk.L) {
+        const Layer& L = *sk.L;
+        k.kh = L.kh;
+        k.kw = L.kw;
+        k.sh = L.sh;
+        k.sw = L.sw;
+        k.Wk = L.Wt;
+        k.Wc = L.W;
+        // q s + k = v + c with c = off_j - off_i s + p (offsets 0 on whole maps).
+        k.cy = go.off_y - gi.off_y * L.sh + L.ph;
+        k.cx = go.off_x - gi.off_x * L.sw + L.pw;
+    } else {
+        k.cy = go.off_y - gi.off_y;
+        k.cx = go.off_x - gi.off_x;
+    }
+    return k;
+}
+
+bool Model::skip_source(int st, int j, bool with_start) const {
+    for (int m = j + 2; m <= (with_start ? st : st - 1); ++m)
+        for (const SkipEdge& sk : skips_[m])
+            if (sk.src == j) return true;
+    return false;
 }
 
 Model::~Model() {
@@ -544,18 +776,20 @@ size_t Model::bytes_per_box(bool alpha, int nspec) const {
     // Worst case (every neuron unstable).  Persistent per start: signs, row
     // maps and partial sums, plus alpha / Adam m, v / best alpha / saved P per
     // level in alpha mode; transient (largest start): two Q, two P, two Pbar
-    // and one Qbar buffer.
+    // and one Qbar buffer, plus the skip sums S_j and kept Pbar_j of the
+    // levels that feed skip edges.
     size_t total = 0, transient = 0;
     for (int s = 2; s <= K_; ++s) {
         const size_t rows = 2 * (size_t)(s == K_ ? nspec : width(s));
         size_t per_row = (size_t)rowlen(s, 0) + 96;
-        size_t maxrow = 0;
+        size_t maxrow = 0, skiprow = 0;
         for (int m = 0; m < s; ++m) {
             maxrow = std::max(maxrow, (size_t)rowlen(s, m));
             if (alpha && m >= 1) per_row += (size_t)rowlen(s, m) * 4 * 5;
+            if (m >= 1 && skip_source(s, m, true)) skiprow += (size_t)rowlen(s, m) * 4 * 2;
         }
         total += rows * per_row;
-        transient = std::max(transient, rows * maxrow * 4 * 7);
+        transient = std::max(transient, rows * (maxrow * 4 * 7 + skiprow));
     }
     for (int m = 0; m <= K_; ++m) total += (size_t)width(m) * 4 * 16;
     return total + transient + (size_t)nspec * 64;
@@ -671,6 +905,17 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     auto psave_buf = [&](int m) {
         return save ? cache_.as<float>(key("Psave", st, m), (size_t)M * rowlen(st, m)) : nullptr;
     };
+    // Residual joins: S_j collects the A that skip edges carry to level j; it
+    // joins the main path's A in the step that relaxes level j.
+    auto S_buf = [&](int j) { return cache_.as<float>(key("S", j), (size_t)M * rowlen(st, j)); };
+    auto addend = [&](int j) { return j >= 1 && skip_source(st, j, true) ? S_buf(j) : nullptr; };
+    auto run_skips = [&](int m, const float* Qm) {
+        for (size_t e = 0; e < skips_[m].size(); ++e)
+            launch_skip_back(skip_step(st, m, (int)e), sp.rows, M, Qm, S_buf(skips_[m][e].src), s);
+    };
+    for (int j = 1; j < st; ++j)
+        if (addend(j)) LB_CUDA(cudaMemsetAsync(S_buf(j), 0, (size_t)M * rowlen(st, j) * 4, s));
+    run_skips(st, nullptr);  // the start's own skip edges carry its one-hot rows
 
     const Layer& Ls = layers_[st - 1];
     if (Ls.conv || Ls.convt) {
@@ -680,7 +925,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
         cs.rows = sp.rows;
         cs.M = M;
         cs.Wc = Ls.W;
-        cs.bW = Ls.b;
+        cs.bW = Ls.convt ? Ls.b : level_bias(st);  // main and skip-conv biases of the start level
         cs.g = sp.geo[mb];
         if (Ls.conv && cs.g.full) {
             // Whole-map rows of a conv start: the weight window sits at the
@@ -733,6 +978,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     int cur = 0, slot = 0;
     for (int m = mb; m >= 1; --m) {
         const Layer& L = layers_[m - 1];
+        run_skips(m, Q[cur]);
         if (L.convt) {
             // k > 1 for a transposed conv (checked at model creation).
             const ConvTStep ct = convt_step(m);
@@ -768,6 +1014,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 e.b_next = level_bias(m - 1);
                 e.P_save = psave_buf(m - 1);
                 e.Q = Q[1 - cur];
+                e.addend = addend(m - 1);
                 if (tc_fwd(m)) {
                     // Raw P from the tensor cores (into the saved P when the
                     // adjoint needs it), then the relaxation streams over it.
@@ -981,11 +1228,26 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     } else if (!seed_in_kernel) {
         launch_adj_input_seed(sp.rows, M, sign, g, xl_, xu_, n0, Pb[0], s);
     }
-    int cur = 0;
+    // Pbar of a skip source stays in its own buffer until the skip's target
+    // level takes its adjoint.
+    auto ps_of = [&](int j) { return tc_adj(j + 1) ? phase_split(st, j + 1) : PhaseSplit{}; };
+    auto PbS_buf = [&](int j) {
+        const int64_t w = std::max<int64_t>(rowlen(st, j), tc_adj(j + 1) ? phase_split(st, j + 1).row_stride : 0);
+        return cache_.as<float>(key("PbS", j), (size_t)M * w);
+    };
+    float* pin = Pb[0];  // Pbar of the level below the current one
     for (int m = 1; m <= st - 1; ++m) {
         const Layer& L = layers_[m - 1];
         const int N = L.n_out, Kd = L.n_in;
         const size_t rl = (size_t)rowlen(st, m);
+        float* pout = nullptr;
+        if (m < st - 1) pout = skip_source(st, m, false) ? PbS_buf(m) : (pin == Pb[0] ? Pb[1] : Pb[0]);
+        auto add_skip_adjoints = [&](float* Qbar) {
+            for (size_t k = 0; k < skips_[m].size(); ++k) {
+                const int j = skips_[m][k].src;
+                launch_skip_adj(skip_step(st, m, (int)k), sp.rows, M, PbS_buf(j), ps_of(j), Qbar, s);
+            }
+        };
         EpiRelaxAdj e;
         e.rows = sp.rows;
         e.rp = relu_view(cache_, std::to_string(m), B, N);
@@ -996,7 +1258,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         else
             e.P_saved = cache_.as<float>(key("Psave", st, m), (size_t)2 * R * rl);
         e.alpha = cache_.as<float>(key("alpha", m, st), (size_t)2 * R * rl);
-        e.Pbar = (m < st - 1) ? Pb[1 - cur] : nullptr;
+        e.Pbar = pout;
         if (e.Pbar && tc_adj(m + 1)) {
             e.ps = phase_split(st, m + 1);
             LB_CUDA(cudaMemsetAsync(e.Pbar, 0, (size_t)M * e.ps.row_stride * 4, s));
@@ -1016,10 +1278,10 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             flops_ += fl;
             float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
             prof_begin(s);
-            launch_convt_adj_qbar(Pb[cur], ct, M, Qbar, s);
+            launch_convt_adj_qbar(pin, ct, M, Qbar, s);
             prof_end(s, fl);
             launch_relax_adjoint(e, Qbar, M, N, s);
-            cur = 1 - cur;
+            pin = pout;
             continue;
         }
         if (L.conv) {
@@ -1036,13 +1298,14 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
                 q.Co = L.out.C;
                 q.in_w = sp.geo[m].ww;
                 q.gseed = g;
-                q.b = L.b;
+                q.b = level_bias(m);
                 q.Qbar = Qbar;
-                launch_tc_conv_qbar(tc_adj_plan(st, m, M, Pb[cur]), M, q, s);
+                launch_tc_conv_qbar(tc_adj_plan(st, m, M, pin), M, q, s);
             } else {
-                launch_conv_adj_qbar(Pb[cur], cs, M, g, L.b, Qbar, s);
+                launch_conv_adj_qbar(pin, cs, M, g, level_bias(m), Qbar, s);
             }
             prof_end(s, fl);
+            add_skip_adjoints(Qbar);
             if (sp.geo[m].full) {
                 launch_relax_adjoint(e, Qbar, M, N, s);
             } else {
@@ -1057,7 +1320,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
                 launch_relax_adjoint_win(e, sp.geo[m], Qbar, M, s);
                 launch_fold_double(e.kbar_d, e.bbar_d, e.kbar, e.bbar, (int64_t)B * N, s);
             }
-            cur = 1 - cur;
+            pin = pout;
             continue;
         }
         flops_ += 2.0 * M * (double)N * Kd;
@@ -1075,7 +1338,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
                 q.seed_xu = xu_;
             }
             prof_begin(s);
-            launch_tc_store_qbar(Pb[cur], L.W_hi, L.W_lo, M, N, Kd, q, s);
+            launch_tc_store_qbar(pin, L.W_hi, L.W_lo, M, N, Kd, q, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
             launch_relax_adjoint(e, q.Qbar, M, N, s);
         } else {
@@ -1083,11 +1346,11 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             e.kslot = cache_.as<float>("kslot", nslot);
             e.bslot = cache_.as<float>("bslot", nslot);
             prof_begin(s);
-            launch_gemm_relax_adj(Pb[cur], L.Wt, M, N, Kd, e, nullptr, s);
+            launch_gemm_relax_adj(pin, L.Wt, M, N, Kd, e, nullptr, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
             launch_reduce_relax_grad(sp.rows, M, B, N, 8, e.kslot, e.bslot, e.kbar, e.bbar, s);
         }
-        cur = 1 - cur;
+        pin = pout;
     }
     rows_ += M;
 }
@@ -1180,6 +1443,21 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
                             L.kw, L.sh, L.sw, L.ph, L.pw, k > 1, s);
         else
             launch_ibp_linear(L.W, L.b, il, iu, ol, ou, B, width(k - 1), width(k), k > 1, s);
+        // Add: the interval sum with every skip edge's bounds.
+        for (const SkipEdge& sk : skips_[k]) {
+            const float* sl = cache_.as<float>(key("ibp_l", sk.src), (size_t)B * width(sk.src));
+            const float* su = cache_.as<float>(key("ibp_u", sk.src), (size_t)B * width(sk.src));
+            if (!sk.L) {
+                launch_add_bounds(ol, ou, sl, su, (int64_t)bn, true, s);
+                continue;
+            }
+            const Layer& P = *sk.L;
+            float* tl = cache_.as<float>("ibp_skip_l", bn);
+            float* tu = cache_.as<float>("ibp_skip_u", bn);
+            launch_ibp_conv(P.W, P.b, sl, su, tl, tu, B, P.in.C, P.in.H, P.in.W, P.out.C, P.out.H, P.out.W, P.kh, P.kw,
+                            P.sh, P.sw, P.ph, P.pw, true, s);
+            launch_add_bounds(ol, ou, tl, tu, (int64_t)bn, false, s);
+        }
     }
     if (method == LB200_METHOD_IBP) {
         launch_ibp_spec(C, c_per_box, cache_.as<float>(key("ibp_l", K_), (size_t)B * nout),
@@ -1416,13 +1694,17 @@ int64_t Model::intermediate_count() const {
 }
 
 void Model::copy_intermediate(float* lower, float* upper) const {
-    // Per box, pre-activations in node-id order (the chain order).
+    // Per box, pre-activations in the node-id order of the nodes that hold them.
     const int B = last_B_;
     int64_t per = 0;
     for (int m = 1; m < K_; ++m) per += width(m);
+    std::vector<int> lv;
+    for (int m = 1; m < K_; ++m) lv.push_back(m);
+    std::sort(lv.begin(), lv.end(),
+              [&](int a, int b) { return preact_node_ids_[a - 1] < preact_node_ids_[b - 1]; });
     std::vector<float> tmp;
     int64_t off = 0;
-    for (int m = 1; m < K_; ++m) {
+    for (int m : lv) {
         const int n = width(m);
         tmp.resize((size_t)B * n);
         for (int side = 0; side < 2; ++side) {

@@ -11,6 +11,7 @@
 #include "tc_conv.cuh"
 
 #include <map>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -73,13 +74,21 @@ struct Layer {
     std::vector<TcConvTap> adj_kb;  // plane, u_y (dy), u_x (dx), c0
 };
 
+// A skip edge into the Add at a level: from the ReLU output of level `src`,
+// directly (identity) or through a conv (L, BatchNorm folded).
+struct SkipEdge {
+    int src = 0;
+    int node = -1, bn = -1;  // graph node ids (-1: identity / no BatchNorm)
+    std::shared_ptr<Layer> L;
+};
+
 struct StartPlan {
     int s = 0;          // pre-activation index (1..K-1), or K for the output start
     RowMap rows;        // device row map (R rows per side)
     int* row_box = nullptr;
     int* row_id = nullptr;
     int* box_off = nullptr;
-    // Row geometry at every level below the start (index m = 0 .. s-1):
+    // Row geometry at every level up to the start (index m = 0 .. s):
     // windows for a conv start, whole maps otherwise.
     std::vector<WinGeo> geo;
     int form = CONC_DENSE;  // concretisation form Luna uses for this start
@@ -126,6 +135,14 @@ private:
     void relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s);
     void init_alpha(StartPlan& sp, int m, int B, cudaStream_t s);
     void build_tc_conv(Layer& L, const float* w, int k);
+    void build_layer(Layer& L, const lb200_graph_desc* g, int node, int bn_node, const MapShape& prev, int k,
+                     bool first);
+    void build_geometry();
+    // Skip-edge steps of level m's edge e for the rows of start st.
+    SkipStep skip_step(int st, int m, int e) const;
+    // Level j is the source of a skip edge into a level in (j, st] (or
+    // (j, st) without the start itself).
+    bool skip_source(int st, int j, bool with_start) const;
     void build_rows(int B, int nspec, cudaStream_t s);
     void alloc_alpha(int B, cudaStream_t s);
     size_t bytes_per_box(bool alpha, int nspec) const;
@@ -136,10 +153,11 @@ private:
     int rowlen(int st, int m) const { return geo_[st][m].size(); }
     ConvStep conv_step(int st, int m) const;
     ConvTStep convt_step(int m) const;
-    // Bias that back-substitution adds for the layer producing level m, per
-    // channel or per neuron (none for a ConvTranspose: Luna's A is flat there).
-    const float* level_bias(int m) const { return layers_[m - 1].convt ? nullptr : layers_[m - 1].b; }
-    const float* level_bias_n(int m) const { return layers_[m - 1].convt ? nullptr : layers_[m - 1].b_neuron; }
+    // Bias that back-substitution adds for level m, per channel or per
+    // neuron: the main edge's (none for a ConvTranspose: Luna's A is flat
+    // there) plus every skip conv's.
+    const float* level_bias(int m) const { return lvl_b_[m]; }
+    const float* level_bias_n(int m) const { return lvl_bn_[m]; }
     // Tensor-core plans of conv layer m for the rows of start st.
     void conv_phase(int st, int m, int& cy, int& cx, int& tlo_y, int& tlo_x, int& nty, int& ntx) const;
     TcConvPlan tc_fwd_plan(int st, int m, int rows, const float* data) const;
@@ -152,9 +170,11 @@ private:
 
     int device_ = 0;
     lb200_options opt_{};
-    std::vector<Layer> layers_;        // chain of affine layers 1..K
+    std::vector<Layer> layers_;        // main edge into level m = layers_[m - 1], m = 1..K
+    std::vector<std::vector<SkipEdge>> skips_;  // [level] skip edges into its Add
+    std::vector<float*> lvl_b_, lvl_bn_;        // [level] bias of level m (level_bias)
     std::vector<std::vector<WinGeo>> geo_;  // [start][level]
-    std::vector<int> preact_node_ids_; // node ids of Linear 1..K-1 outputs
+    std::vector<int> preact_node_ids_; // [m - 1] node whose output is pre-activation m (1..K-1)
     DevCache weights_;
     DevCache cache_;
 

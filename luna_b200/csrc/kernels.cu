@@ -1158,6 +1158,23 @@ void launch_ibp_spec(const float* C, int c_per_box, const float* l, const float*
     LB_LAUNCH();
 }
 
+__global__ void add_bounds_kernel(float* __restrict__ ol, float* __restrict__ ou, const float* __restrict__ il,
+                                  const float* __restrict__ iu, int64_t n, bool relu_in) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const float l = relu_in ? fmaxf(il[i], 0.f) : il[i];
+    const float u = relu_in ? fmaxf(iu[i], 0.f) : iu[i];
+    ol[i] += l;
+    ou[i] += u;
+}
+
+void launch_add_bounds(float* out_l, float* out_u, const float* in_l, const float* in_u, int64_t n, bool relu_in,
+                       cudaStream_t s) {
+    if (n == 0) return;
+    add_bounds_kernel<<<ceil_div(n, 256), 256, 0, s>>>(out_l, out_u, in_l, in_u, n, relu_in);
+    LB_LAUNCH();
+}
+
 // ============================================================== helpers
 __global__ void fill_f32_kernel(float* p, float v, int64_t n) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

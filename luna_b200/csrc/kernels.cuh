@@ -36,6 +36,11 @@ struct ReluParams {
 void launch_ibp_linear(const float* W, const float* b, const float* in_l, const float* in_u,
                        float* out_l, float* out_u, int B, int n_in, int n_out, bool relu_in,
                        cudaStream_t s);
+// Interval sum of an Add (BoundedAddNode::computeIntervalBoundPropagation,
+// :281-304): out += in over n entries; in clamped at 0 first when it is a
+// ReLU output.
+void launch_add_bounds(float* out_l, float* out_u, const float* in_l, const float* in_u, int64_t n, bool relu_in,
+                       cudaStream_t s);
 
 // ---- row maps ------------------------------------------------------------
 // counts[b] = #{i : l[b,i] < 0 < u[b,i]}

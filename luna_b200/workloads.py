@@ -10,8 +10,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .abi import (NODE_BATCHNORM, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_INPUT, NODE_LINEAR,
-                  NODE_RELU, Graph, Node)
+from .abi import (NODE_ADD, NODE_BATCHNORM, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_INPUT,
+                  NODE_LINEAR, NODE_RELU, NODE_SIGMOID, Graph, Node)
 
 
 def mlp(widths, seed: int, bias_std: float = 0.01) -> Graph:
@@ -259,3 +259,95 @@ def cnn_convt_cifar(n_boxes: int = 256, seed: int = 5, eps: float = 8.0 / 255.0)
                           ("linear", 512), ("linear", 10)], seed)
     rng = np.random.Generator(np.random.PCG64(seed + 1000))
     return g, image_boxes(rng, n_boxes, 3 * 32 * 32, eps, 10)
+
+
+def resnet(input_shape, stem: int, blocks, head, seed: int, bias_std: float = 0.01,
+           head_act: int = NODE_SIGMOID, bn_mean_std: float = 0.0) -> Graph:
+    """Small ResNet: Input (C, H, W) -> conv stem k3 s1 p1 -> ReLU -> residual
+    blocks -> Flatten -> Linear head.
+
+    Each block (C_out, stride) is conv k3 (stride) p1 -> BatchNorm -> ReLU ->
+    conv k3 s1 p1 -> BatchNorm -> Add(skip) -> ReLU; the skip is the block
+    input when the shape is unchanged, else a 1x1 projection conv with the
+    block's stride (node order as a torchvision BasicBlock exports: conv1,
+    bn1, relu, conv2, bn2, projection, add, relu).  `head` lists the Linear
+    widths; every head layer but the last is followed by `head_act` (ReLU or
+    Sigmoid).  Weights He-normal over the fan-in, biases N(0, bias_std^2);
+    BatchNorm gamma ~ U[0.5, 1.5], beta ~ N(0, 0.1^2), running mean ~
+    N(0, bn_mean_std^2) (0 by default), running var ~ U[0.5, 2]; one PCG64
+    stream, drawn node by node."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    nodes = [Node(NODE_INPUT, [], tuple(input_shape))]
+
+    def conv(src, shape, co, k, s, p):
+        ci, h, w = shape
+        wt = (rng.standard_normal((co, ci, k, k)) * np.sqrt(2.0 / (ci * k * k))).astype(np.float32)
+        b = (rng.standard_normal(co) * bias_std).astype(np.float32)
+        out = (co, conv_out(h, k, s, p), conv_out(w, k, s, p))
+        nodes.append(Node(NODE_CONV, [src], out, weight=wt, bias=b, kernel=(k, k), stride=(s, s), padding=(p, p)))
+        return len(nodes) - 1, out
+
+    def bn(src, shape):
+        co = shape[0]
+        gamma = rng.uniform(0.5, 1.5, co).astype(np.float32)
+        beta = (rng.standard_normal(co) * 0.1).astype(np.float32)
+        mean = (rng.standard_normal(co) * bn_mean_std).astype(np.float32)
+        var = rng.uniform(0.5, 2.0, co).astype(np.float32)
+        nodes.append(Node(NODE_BATCHNORM, [src], shape, weight=gamma, bias=beta, running_mean=mean,
+                          running_var=var, eps=1e-5))
+        return len(nodes) - 1
+
+    def act(src, shape, kind=NODE_RELU):
+        nodes.append(Node(kind, [src], shape))
+        return len(nodes) - 1
+
+    cur, shape = conv(0, tuple(input_shape), stem, 3, 1, 1)
+    cur = act(cur, shape)
+    for co, s in blocks:
+        x, xshape = cur, shape
+        h, shape = conv(x, xshape, co, 3, s, 1)
+        h = act(bn(h, shape), shape)
+        h, shape = conv(h, shape, co, 3, 1, 1)
+        h = bn(h, shape)
+        skip = x
+        if s != 1 or co != xshape[0]:
+            skip, _ = conv(x, xshape, co, 1, s, 0)
+        nodes.append(Node(NODE_ADD, [h, skip], shape))
+        cur = act(len(nodes) - 1, shape)
+    shape = (int(np.prod(shape)), 1, 1)
+    nodes.append(Node(NODE_FLATTEN, [cur], shape))
+    cur = len(nodes) - 1
+    for li, n_out in enumerate(head):
+        fan_in = shape[0]
+        wt = (rng.standard_normal((n_out, fan_in)) * np.sqrt(2.0 / fan_in)).astype(np.float32)
+        b = (rng.standard_normal(n_out) * bias_std).astype(np.float32)
+        shape = (n_out, 1, 1)
+        nodes.append(Node(NODE_LINEAR, [cur], shape, weight=wt, bias=b))
+        cur = len(nodes) - 1
+        if li != len(head) - 1:
+            cur = act(cur, shape, head_act)
+    return Graph(nodes, 0, len(nodes) - 1)
+
+
+def resnet_cifar(n_boxes: int = 128, seed: int = 3, eps: float = 1.0 / 255.0):
+    """Small CIFAR ResNet: stem conv3->16 k3, blocks (16, s1), (16, s1), (32, s2
+    with a 1x1 projection skip), (32, s1), BatchNorm with running mean 0,
+    flatten 8192 -> 100 -> Sigmoid -> 10; seed 3; centres U[0,1], eps 1/255
+    clipped; 9 margin rows."""
+    g = resnet((3, 32, 32), 16, [(16, 1), (16, 1), (32, 2), (32, 1)], [100, 10], seed)
+    rng = np.random.Generator(np.random.PCG64(seed + 1000))
+    return g, image_boxes(rng, n_boxes, 3 * 32 * 32, eps, 10)
+
+
+def small_resnet_case(seed: int, n_boxes: int = 3, eps: float = 0.01, hw: int = 8, head_act: int = NODE_RELU,
+                      big: bool = False):
+    """Small ResNet for parity tests: stem 4 channels, an identity block and a
+    strided block with a projection skip, head 12 -> 4.  With big the maps are
+    20 x 20 with 12 channels, so the block convs have more than 4096 output
+    features (patches starts on Luna's CPU path)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    c = 12 if big else 4
+    hw = 20 if big else hw
+    g = resnet((3, hw, hw), c, [(c, 1), (2 * c, 2)], [12, 4], seed + 13, bias_std=0.05, head_act=head_act,
+               bn_mean_std=0.1)
+    return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)

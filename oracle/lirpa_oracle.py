@@ -11,8 +11,8 @@ behaviour it restates.  Per-box state follows Luna's: IBP bounds, "node
 bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
 parameters keyed by (activation node, start node), and STE reference bounds.
 
-Supported node kinds: Input, Linear, Conv2d, ConvTranspose2d, BatchNorm, ReLU, Flatten,
-Identity.  A
+Supported node kinds: Input, Linear, Conv2d, ConvTranspose2d, BatchNorm, ReLU, Add (of
+two tensors), Flatten, Identity.  A
 matrices are kept dense over the flattened (C, H, W) features; Luna's
 patches mode (CROWNAnalysis.cpp:255-405, BoundedConvNode.cpp:556-709) is the
 same arithmetic on a window of those features, and it is tracked only to
@@ -27,7 +27,7 @@ import torch
 
 import torch.nn.functional as F
 
-from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_BATCHNORM,
+from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_ADD, NODE_BATCHNORM,
                            NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT,
                            NODE_LINEAR, NODE_RELU, Options, default_options)
 
@@ -127,6 +127,9 @@ class LirpaOracle:
                 spatial = nd.size // w.numel()
                 self.W[i] = w.repeat_interleave(spatial)
                 self.b[i] = b.repeat_interleave(spatial)
+            elif nd.type == NODE_ADD:
+                if len(nd.inputs) != 2:
+                    raise NotImplementedError("oracle: Add of a constant")
             elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_FLATTEN, NODE_IDENTITY):
                 raise NotImplementedError(f"oracle: node type {nd.type}")
         self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type == NODE_RELU]
@@ -174,6 +177,10 @@ class LirpaOracle:
         if nd.type == NODE_RELU:
             l, u = ins[0]
             return torch.clamp_min(l, 0), torch.clamp_min(u, 0)
+        if nd.type == NODE_ADD:
+            # BoundedAddNode::computeIntervalBoundPropagation (:281-304).
+            (l1, u1), (l2, u2) = ins
+            return l1 + l2, u1 + u2
         if nd.type in (NODE_FLATTEN, NODE_IDENTITY):
             return ins[0]
         raise NotImplementedError
@@ -321,10 +328,13 @@ class LirpaOracle:
         Returns (lA, uA, lbias, ubias, patches) at the input node; `patches`
         tells whether Luna would still hold the start's A as patches there
         (it converts to a matrix once a patch is wider than the conv input,
-        BoundedConvNode.cpp:671-694)."""
+        BoundedConvNode.cpp:671-694, and at a join of patches with a matrix,
+        CROWNAnalysis::addA :1307-1354; patches meeting patches are padded to
+        the wider one, Patches::add, Patches.cpp:86-129)."""
         n = self.g.nodes[start].size
-        patches = self._starts_in_patches(start, C is not None)
-        pwidth = None
+        # (patches?, patch width) of the A accumulated at each node; width
+        # None = the identity patches of the start.
+        form = {start: (self._starts_in_patches(start, C is not None), None)}
         # Luna keeps a tensor A flat ([spec, 1, n]) between nodes: a conv node
         # reshapes its [spec, 1, C, H, W] result back when the input bounds
         # are flat (BoundedConvNode.cpp:430-445).  ConvTranspose adds its
@@ -360,6 +370,7 @@ class LirpaOracle:
             nd = self.g.nodes[c]
             if c in lA:
                 a_l, a_u = lA[c], uA[c]
+                patches, pwidth = form[c]
                 if nd.type == NODE_LINEAR:
                     W, bb = self.W[c], self.b[c]
                     out = [(torch.matmul(a_l, W), torch.matmul(a_u, W))]
@@ -401,6 +412,11 @@ class LirpaOracle:
                     l, u = self._input_bounds_of(st, c, x)[0]
                     nl, nu, nb_l, nb_u = self._relu_backward(st, c, start, a_l, a_u, l, u)
                     out = [(nl, nu)]
+                elif nd.type == NODE_ADD:
+                    # BoundedAddNode::boundBackward (:167-279): the same A to both
+                    # operands (equal shapes), no bias of its own.
+                    out = [(a_l, a_u), (a_l, a_u)]
+                    nb_l = nb_u = None
                 elif nd.type in (NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT):
                     out = [(a_l, a_u)]
                     nb_l = nb_u = None
@@ -412,20 +428,31 @@ class LirpaOracle:
                     pl, pu = out[k]
                     lA[p] = lA[p] + pl if p in lA else pl
                     uA[p] = uA[p] + pu if p in uA else pu
+                    if p in form:
+                        fp, wp = form[p]
+                        form[p] = (fp and patches, max(wp or 1, pwidth or 1))
+                    else:
+                        form[p] = (patches, pwidth)
                     if k == 0:
                         # propagated = node bias + accumulated bias (:629-657)
-                        tl = lb[c] if nb_l is None else nb_l + lb[c]
-                        tu = ub[c] if nb_u is None else nb_u + ub[c]
+                        # A node reached only through a second operand has no
+                        # accumulated bias of its own.
+                        zero = torch.zeros(a_l.shape[0])
+                        acc_l, acc_u = lb.get(c, zero), ub.get(c, zero)
+                        tl = acc_l if nb_l is None else nb_l + acc_l
+                        tu = acc_u if nb_u is None else nb_u + acc_u
                         lb[p] = lb[p] + tl if p in lb else tl
                         ub[p] = ub[p] + tu if p in ub else tu
                 if c != inp:
-                    del lA[c], uA[c], lb[c], ub[c]
+                    del lA[c], uA[c]
+                    lb.pop(c, None)
+                    ub.pop(c, None)
             for p in nd.inputs:
                 if p in pending and pending[p] > 0:
                     pending[p] -= 1
                     if pending[p] == 0:
                         queue.append(p)
-        return lA[inp], uA[inp], lb[inp], ub[inp], patches
+        return lA[inp], uA[inp], lb[inp], ub[inp], form[inp][0]
 
     @staticmethod
     def _concretize(lA, uA, lb, ub, x, patches=False):

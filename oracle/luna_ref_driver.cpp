@@ -25,6 +25,8 @@
 #include "nodes/BoundedConvNode.h"
 #include "nodes/BoundedBatchNormNode.h"
 #include "nodes/BoundedConvTransposeNode.h"
+#include "nodes/BoundedAddNode.h"
+#include "nodes/BoundedSigmoidNode.h"
 #include "input_parsers/Operations.h"
 
 #include <torch/torch.h>
@@ -148,8 +150,21 @@ std::shared_ptr<NLR::TorchModel> build_model(const lb200_graph_desc* g) {
             node->setInputSize((unsigned)out_numel);
             node->setOutputSize((unsigned)out_numel);
             break;
+        case LB200_NODE_SIGMOID:
+            // BoundedOperationConverter::convertSigmoid (OnnxToTorch.cpp:2013-2035).
+            node = std::make_shared<NLR::BoundedSigmoidNode>(torch::nn::Sigmoid());
+            node->setInputSize((unsigned)out_numel);
+            node->setOutputSize((unsigned)out_numel);
+            break;
         case LB200_NODE_FLATTEN:
             node = std::make_shared<NLR::BoundedFlattenNode>(Operations::FlattenWrapper(1));
+            node->setInputSize((unsigned)out_numel);
+            node->setOutputSize((unsigned)out_numel);
+            break;
+        case LB200_NODE_ADD:
+            // BoundedOperationConverter::convertAdd for two tensors (OnnxToTorch.cpp:1769-1830):
+            // a BoundedAddNode with both producers as dependencies, flat sizes.
+            node = std::make_shared<NLR::BoundedAddNode>();
             node->setInputSize((unsigned)out_numel);
             node->setOutputSize((unsigned)out_numel);
             break;

@@ -77,6 +77,16 @@ def cases():
     out.append(("convt2_crown", "convt_cnn_case", kw, 3, abi.METHOD_CROWN, {}))
     out.append(("convt2_alpha", "convt_cnn_case", kw, 3, abi.METHOD_ALPHA_CROWN,
                 {"alpha_lr": 0.1, "alpha_iterations": 6}))
+    # Residual blocks (identity and projection skips): dense starts, and
+    # patches starts at the block convs.
+    kw = {"seed": 7, "n_boxes": 3}
+    out.append(("resnet_crown", "small_resnet_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("resnet_alpha", "small_resnet_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 6}))
+    kw = {"seed": 8, "n_boxes": 2, "big": True}
+    out.append(("resnetbig_crown", "small_resnet_case", kw, 2, abi.METHOD_CROWN, {}))
+    out.append(("resnetbig_alpha", "small_resnet_case", kw, 1, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 3}))
     # The CIFAR-shaped CNN at full size, one box.
     out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
     return out

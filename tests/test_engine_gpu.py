@@ -85,29 +85,39 @@ def test_tc_conv_matches_simt_and_oracle(method):
 
 
 def _forward(graph, x):
-    """Chain forward of a graph on a batch of flat inputs (CHW order)."""
+    """Forward of a graph (any DAG of the supported nodes) on a batch of flat
+    inputs in CHW order."""
     import torch.nn.functional as F
-    for n in graph.nodes:
+    from oracle.lirpa_oracle import topo_order
+    f = lambda a: torch.from_numpy(a).cuda()
+    val = {}
+    for i in topo_order(graph)[0]:
+        n = graph.nodes[i]
+        ins = [val[p] for p in n.inputs]
         if n.type == abi.NODE_INPUT:
-            shape = n.out_shape
+            y = x.reshape(x.shape[0], *n.out_shape)
         elif n.type == abi.NODE_LINEAR:
-            x = x.reshape(x.shape[0], -1) @ torch.from_numpy(n.weight).cuda().T + torch.from_numpy(n.bias).cuda()
+            y = ins[0].reshape(x.shape[0], -1) @ f(n.weight).T + f(n.bias)
         elif n.type == abi.NODE_CONV:
-            x = F.conv2d(x.reshape(x.shape[0], *shape), torch.from_numpy(n.weight).cuda(),
-                         torch.from_numpy(n.bias).cuda(), stride=n.stride, padding=n.padding)
-            shape = n.out_shape
+            y = F.conv2d(ins[0], f(n.weight), f(n.bias), stride=n.stride, padding=n.padding)
         elif n.type == abi.NODE_CONVTRANSPOSE:
-            x = F.conv_transpose2d(x.reshape(x.shape[0], *shape), torch.from_numpy(n.weight).cuda(),
-                                   torch.from_numpy(n.bias).cuda(), stride=n.stride, padding=n.padding)
-            shape = n.out_shape
+            y = F.conv_transpose2d(ins[0], f(n.weight), f(n.bias), stride=n.stride, padding=n.padding)
         elif n.type == abi.NODE_BATCHNORM:
-            f = lambda a: torch.from_numpy(a).cuda()
             w = f(n.weight) / torch.sqrt(f(n.running_var) + n.eps)
             b = f(n.bias) - f(n.running_mean) * w
-            x = x.reshape(x.shape[0], *shape) * w.view(1, -1, 1, 1) + b.view(1, -1, 1, 1)
+            y = ins[0] * w.view(1, -1, 1, 1) + b.view(1, -1, 1, 1)
         elif n.type == abi.NODE_RELU:
-            x = torch.relu(x)
-    return x.reshape(x.shape[0], -1)
+            y = torch.relu(ins[0])
+        elif n.type == abi.NODE_SIGMOID:
+            y = torch.sigmoid(ins[0])
+        elif n.type == abi.NODE_ADD:
+            y = ins[0] + ins[1]
+        elif n.type in (abi.NODE_FLATTEN, abi.NODE_IDENTITY):
+            y = ins[0].reshape(x.shape[0], -1) if n.type == abi.NODE_FLATTEN else ins[0]
+        else:
+            raise NotImplementedError(n.type)
+        val[i] = y
+    return val[graph.output_index].reshape(x.shape[0], -1)
 
 
 def _sample_outputs(graph, boxes, n_pts, seed=0, batch=20_000):
@@ -232,6 +242,34 @@ def test_cnn_convt_cifar_sound():
     """The transposed-conv variant of the CIFAR CNN: CROWN bounds are sound at
     10^5 sampled points per box and at least as tight as IBP."""
     g, bx = W.cnn_convt_cifar(2, eps=2.0 / 255.0)
+    m = Model(g, options=abi.default_options())
+    ilb, iub = m.compute_bounds(bx, abi.METHOD_IBP)
+    lb, ub = m.compute_bounds(bx, abi.METHOD_CROWN)
+    tol = 1e-4 * (1 + np.abs(lb))
+    assert np.isfinite(lb).all() and (lb >= ilb - tol).all() and (ub <= iub + tol).all()
+    for b, y in enumerate(_sample_outputs(g, bx, 100_000)):
+        assert (y.min(0).values.cpu().numpy() >= lb[b] - tol[b]).all()
+        assert (y.max(0).values.cpu().numpy() <= ub[b] + tol[b]).all()
+
+
+@pytest.mark.parametrize("seed,big", [(0, False), (1, False), (2, False), (3, True)])
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_resnet_matches_oracle(method, seed, big):
+    """Residual blocks (identity and 1x1 projection skips joined by Add), with
+    dense starts and, with big, patches starts at the block convs."""
+    from oracle.lirpa_oracle import LirpaOracle
+    g, bx = W.small_resnet_case(40 + seed, n_boxes=1 if big else 3, big=big)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=3 if big else 5)
+    lb, ub = Model(g, options=opt).compute_bounds(bx, method)
+    olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
+    _assert_parity(f"resnet{seed}/{method}/{int(big)}", lb, ub, olb, oub)
+
+
+def test_resnet_cifar_sound_and_ordered():
+    """The CIFAR ResNet (ReLU head variant): CROWN bounds are sound at 10^5
+    sampled points per box and at least as tight as IBP."""
+    g, bx = W.resnet_cifar(2)
+    g = W.resnet((3, 32, 32), 16, [(16, 1), (16, 1), (32, 2), (32, 1)], [100, 10], 3, head_act=abi.NODE_RELU)
     m = Model(g, options=abi.default_options())
     ilb, iub = m.compute_bounds(bx, abi.METHOD_IBP)
     lb, ub = m.compute_bounds(bx, abi.METHOD_CROWN)
