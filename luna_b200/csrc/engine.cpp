@@ -116,6 +116,7 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
     std::vector<ValDesc> val(n);
     std::vector<std::vector<EdgeDesc>> lvl_edges(1);  // level 0 = input
     std::vector<int> lvl_node(1, g->input_index);     // node whose output is the level's pre-activation
+    std::vector<int> lvl_act(1, 0);                   // activation of each level (0: none)
     for (int i : order) {
         const auto& d = g->nodes[i];
         ValDesc& v = val[i];
@@ -165,9 +166,12 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
             }
             break;
         case LB200_NODE_RELU:
-            if (d.num_inputs != 1 || operand(0).kind != 2) bad(i, "a ReLU must follow an affine node or an Add");
+        case LB200_NODE_SIGMOID:
+            if (d.num_inputs != 1 || operand(0).kind != 2)
+                bad(i, "an activation must follow an affine node or an Add");
             lvl_edges.push_back(operand(0).edges);
             lvl_node.push_back(d.inputs[0]);
+            lvl_act.push_back(d.type == LB200_NODE_SIGMOID ? ACT_SIGMOID : ACT_RELU);
             v.kind = 1;
             v.level = (int)lvl_edges.size() - 1;
             break;
@@ -182,6 +186,8 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
     if (val[g->output_index].kind != 2) throw std::invalid_argument("the output node must be an affine node");
     lvl_edges.push_back(val[g->output_index].edges);
     lvl_node.push_back(g->output_index);
+    lvl_act.push_back(0);
+    act_ = lvl_act;
     K_ = (int)lvl_edges.size() - 1;
     if (K_ < 2) throw std::invalid_argument("need at least two affine layers");
     // Main edge of every level: the affine edge from the level just below.
@@ -246,6 +252,16 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
         }
     }
     if (layers_[K_ - 1].conv) throw std::invalid_argument("the output layer must be Linear");
+    // Sigmoid levels: flat maps relaxed by the Linear above them.
+    for (int m = 1; m < K_; ++m) {
+        if (act_[m] != ACT_SIGMOID) continue;
+        has_sigmoid_ = true;
+        if (map(m).spatial || layers_[m].conv || layers_[m].convt)
+            throw std::invalid_argument("a Sigmoid is supported on flat (Linear) layers only");
+        for (int t = m + 2; t <= K_; ++t)
+            for (const SkipEdge& sk : skips_[t])
+                if (sk.src == m) throw std::invalid_argument("a Sigmoid output as a skip source is not supported");
+    }
     // Bias that the back-substitution adds for level m: the main edge's (none
     // for a ConvTranspose: Luna's A is flat there) plus every skip conv's.
     lvl_b_.assign(K_ + 1, nullptr);
@@ -847,6 +863,16 @@ void Model::build_rows(int B, int nspec, cudaStream_t s) {
 void Model::relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s) {
     const int n = width(m);
     const size_t bn = (size_t)B * n;
+    if (act_[m] == ACT_SIGMOID) {
+        // No alpha for a Sigmoid (Luna cannot create one: its 8-slot init
+        // throws, AlphaCROWNAnalysis.cpp:264-272); the CROWN relaxation stays.
+        if (create) LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("init", m), bn), 0, bn * 4, s));
+        launch_sigmoid_params(cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B, n,
+                              cache_.as<float>(key("rp_s", m), bn), cache_.as<float>(key("rp_bl", m), bn),
+                              cache_.as<float>(key("rp_k", m), bn), cache_.as<float>(key("rp_b", m), bn),
+                              cache_.as<uint8_t>(key("rp_f", m), bn), s);
+        return;
+    }
     launch_relu_params(cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B,
                        n, alpha_mode, create, cache_.as<uint8_t>(key("aset", m), bn),
                        cache_.as<float>(key("init", m), bn), cache_.as<int>(key("hasaset", m), B),
@@ -854,13 +880,14 @@ void Model::relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t
                        cache_.as<float>(key("rp_b", m), bn), cache_.as<uint8_t>(key("rp_f", m), bn), s);
 }
 
-static ReluParams relu_view(DevCache& c, const std::string& sfx, int B, int n) {
+ReluParams Model::rview(int m, int B, int n) {
     ReluParams rp;
     const size_t bn = (size_t)B * n;
-    rp.slope_lo = c.as<float>("rp_s/" + sfx, bn);
-    rp.k_up = c.as<float>("rp_k/" + sfx, bn);
-    rp.b_up = c.as<float>("rp_b/" + sfx, bn);
-    rp.flags = c.as<uint8_t>("rp_f/" + sfx, bn);
+    rp.slope_lo = cache_.as<float>(key("rp_s", m), bn);
+    rp.k_up = cache_.as<float>(key("rp_k", m), bn);
+    rp.b_up = cache_.as<float>(key("rp_b", m), bn);
+    rp.flags = cache_.as<uint8_t>(key("rp_f", m), bn);
+    if (act_[m] == ACT_SIGMOID) rp.b_lo = cache_.as<float>(key("rp_bl", m), bn);
     rp.n = n;
     return rp;
 }
@@ -942,7 +969,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             w.st_W = Ls.out.W;
             cs.wg = w;
         }
-        cs.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+        cs.rp = rview(mb, B, width(mb));
         cs.alpha = alpha_buf(mb);
         cs.b_next = level_bias(mb);
         cs.P_save = psave_buf(mb);
@@ -966,7 +993,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             ss.nspec = nspec;
             flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
         }
-        ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+        ss.rp = rview(mb, B, width(mb));
         ss.alpha = alpha_buf(mb);
         ss.b_next = level_bias_n(mb);
         ss.P_save = psave_buf(mb);
@@ -987,7 +1014,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             ConvRelaxEpi e;
             e.rows = sp.rows;
             e.g = sp.geo[m - 1];
-            e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
+            e.rp = rview(m - 1, B, width(m - 1));
             e.alpha = alpha_buf(m - 1);
             e.b_next = level_bias(m - 1);
             e.P_save = psave_buf(m - 1);
@@ -1009,7 +1036,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 ConvRelaxEpi e;
                 e.rows = sp.rows;
                 e.g = sp.geo[m - 1];
-                e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
+                e.rp = rview(m - 1, B, width(m - 1));
                 e.alpha = alpha_buf(m - 1);
                 e.b_next = level_bias(m - 1);
                 e.P_save = psave_buf(m - 1);
@@ -1060,7 +1087,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
         if (m - 1 >= 1) {
             EpiRelaxFwd e;
             e.rows = sp.rows;
-            e.rp = relu_view(cache_, std::to_string(m - 1), B, width(m - 1));
+            e.rp = rview(m - 1, B, width(m - 1));
             e.alpha = alpha_buf(m - 1);
             e.b_next = level_bias_n(m - 1);
             e.P_save = psave_buf(m - 1);
@@ -1132,7 +1159,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
             flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
         }
         if (!in_prologue(mb)) {
-            ss.rp = relu_view(cache_, std::to_string(mb), B, width(mb));
+            ss.rp = rview(mb, B, width(mb));
             if (alpha) ss.alpha = cache_.as<float>(key("alpha", mb, st), (size_t)M * width(mb));
             ss.b_next = layers_[mb - 1].b;
             ss.Q = Qbuf[qcur];
@@ -1151,7 +1178,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
         TcPrologue pro;
         if (in_prologue(m)) {
             pro.rows = sp.rows;
-            pro.rp = relu_view(cache_, std::to_string(m), B, Kd);
+            pro.rp = rview(m, B, Kd);
             if (alpha) pro.alpha = cache_.as<float>(key("alpha", m, st), (size_t)M * Kd);
             pro.b_lin = L.b;
             if (m == mb && st != K_) {
@@ -1182,7 +1209,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
         } else {
             EpiRelaxFwd e;
             e.rows = sp.rows;
-            e.rp = relu_view(cache_, std::to_string(m - 1), B, N);
+            e.rp = rview(m - 1, B, N);
             if (alpha) e.alpha = cache_.as<float>(key("alpha", m - 1, st), (size_t)M * N);
             e.b_next = layers_[m - 2].b;
             if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
@@ -1250,7 +1277,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         };
         EpiRelaxAdj e;
         e.rows = sp.rows;
-        e.rp = relu_view(cache_, std::to_string(m), B, N);
+        e.rp = rview(m, B, N);
         e.gseed = g;
         e.b_lin = L.b;
         if (tc_ && m == st - 1 && st != K_)
@@ -1345,10 +1372,18 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             const size_t nslot = (size_t)relax_grad_slots(M, B, 8) * N;
             e.kslot = cache_.as<float>("kslot", nslot);
             e.bslot = cache_.as<float>("bslot", nslot);
+            if (e.rp.b_lo) {
+                e.sslot = cache_.as<float>("sslot", nslot);
+                e.blslot = cache_.as<float>("blslot", nslot);
+            }
             prof_begin(s);
             launch_gemm_relax_adj(pin, L.Wt, M, N, Kd, e, nullptr, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
             launch_reduce_relax_grad(sp.rows, M, B, N, 8, e.kslot, e.bslot, e.kbar, e.bbar, s);
+            if (e.rp.b_lo)
+                launch_reduce_relax_grad(sp.rows, M, B, N, 8, e.sslot, e.blslot,
+                                         cache_.as<float>(key("sbar", m), (size_t)B * N),
+                                         cache_.as<float>(key("blbar", m), (size_t)B * N), s);
         }
         pin = pout;
     }
@@ -1433,16 +1468,27 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         const size_t bn = (size_t)B * width(k);
         const float* il = k == 1 ? xl : cache_.as<float>(key("ibp_l", k - 1), (size_t)B * width(k - 1));
         const float* iu = k == 1 ? xu : cache_.as<float>(key("ibp_u", k - 1), (size_t)B * width(k - 1));
+        bool relu_in = k > 1;
+        if (act_[k - 1] == ACT_SIGMOID) {
+            // The Sigmoid node's IBP: [sigmoid(l), sigmoid(u)].
+            const size_t bp = (size_t)B * width(k - 1);
+            float* sl = cache_.as<float>("ibp_sig_l", bp);
+            float* su = cache_.as<float>("ibp_sig_u", bp);
+            launch_sigmoid_bounds(il, iu, sl, su, (int64_t)bp, s);
+            il = sl;
+            iu = su;
+            relu_in = false;
+        }
         const Layer& L = layers_[k - 1];
         float* ol = cache_.as<float>(key("ibp_l", k), bn);
         float* ou = cache_.as<float>(key("ibp_u", k), bn);
         if (L.convt)
-            launch_ibp_convt(convt_step(k), L.b, il, iu, ol, ou, B, k > 1, s);
+            launch_ibp_convt(convt_step(k), L.b, il, iu, ol, ou, B, relu_in, s);
         else if (L.conv)
             launch_ibp_conv(L.W, L.b, il, iu, ol, ou, B, L.in.C, L.in.H, L.in.W, L.out.C, L.out.H, L.out.W, L.kh,
-                            L.kw, L.sh, L.sw, L.ph, L.pw, k > 1, s);
+                            L.kw, L.sh, L.sw, L.ph, L.pw, relu_in, s);
         else
-            launch_ibp_linear(L.W, L.b, il, iu, ol, ou, B, width(k - 1), width(k), k > 1, s);
+            launch_ibp_linear(L.W, L.b, il, iu, ol, ou, B, width(k - 1), width(k), relu_in, s);
         // Add: the interval sum with every skip edge's bounds.
         for (const SkipEdge& sk : skips_[k]) {
             const float* sl = cache_.as<float>(key("ibp_l", sk.src), (size_t)B * width(sk.src));
@@ -1549,6 +1595,10 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
             const size_t bn = (size_t)B * width(m);
             LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("kbar", m), bn), 0, bn * 4, s));
             LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("bbar", m), bn), 0, bn * 4, s));
+            if (act_[m] == ACT_SIGMOID) {
+                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("sbar", m), bn), 0, bn * 4, s));
+                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("blbar", m), bn), 0, bn * 4, s));
+            }
         }
         ++steps;
         adam_active_ = bc.active;
@@ -1561,9 +1611,16 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
             if (sp.rows.R == 0) continue;
             const size_t bn = (size_t)B * width(st);
             float* g = cache_.as<float>(key("g", st), (size_t)2 * sp.rows.R);
-            launch_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn), cache_.as<float>(key("cur_u", st), bn),
-                              cache_.as<uint8_t>(key("rp_f", st), bn), cache_.as<float>(key("kbar", st), bn),
-                              cache_.as<float>(key("bbar", st), bn), width(st), g, s);
+            if (act_[st] == ACT_SIGMOID)
+                launch_sigmoid_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn),
+                                          cache_.as<float>(key("cur_u", st), bn), cache_.as<float>(key("sbar", st), bn),
+                                          cache_.as<float>(key("blbar", st), bn), cache_.as<float>(key("kbar", st), bn),
+                                          cache_.as<float>(key("bbar", st), bn), width(st), g, s);
+            else
+                launch_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn),
+                                  cache_.as<float>(key("cur_u", st), bn), cache_.as<uint8_t>(key("rp_f", st), bn),
+                                  cache_.as<float>(key("kbar", st), bn), cache_.as<float>(key("bbar", st), bn),
+                                  width(st), g, s);
             adjoint_start(sp, B, g, 2 * sp.rows.R, s);
         }
         lr = lr * opt_.alpha_lr_decay;
@@ -1588,7 +1645,7 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
 // path: all widths that appear as N or K of a contraction (n_0 .. n_{K-1})
 // multiples of 16.
 bool Model::tc_eligible() const {
-    if (force_simt_ || has_conv_) return false;
+    if (force_simt_ || has_conv_ || has_sigmoid_) return false;
     for (int m = 0; m < K_; ++m)
         if (!tc_supported(1, width(m), width(m)) || width(m) % 16 != 0) return false;
     return true;

@@ -133,6 +133,8 @@ private:
     void forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s);
     void adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s);
     void relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s);
+    // Relaxation parameters of level m's activation for B boxes of n neurons.
+    ReluParams rview(int m, int B, int n);
     void init_alpha(StartPlan& sp, int m, int B, cudaStream_t s);
     void build_tc_conv(Layer& L, const float* w, int k);
     void build_layer(Layer& L, const lb200_graph_desc* g, int node, int bn_node, const MapShape& prev, int k,
@@ -173,6 +175,9 @@ private:
     std::vector<Layer> layers_;        // main edge into level m = layers_[m - 1], m = 1..K
     std::vector<std::vector<SkipEdge>> skips_;  // [level] skip edges into its Add
     std::vector<float*> lvl_b_, lvl_bn_;        // [level] bias of level m (level_bias)
+    enum { ACT_RELU = 1, ACT_SIGMOID = 2 };
+    std::vector<int> act_;                       // [level] activation (0 for the input and the output)
+    bool has_sigmoid_ = false;
     std::vector<std::vector<WinGeo>> geo_;  // [start][level]
     std::vector<int> preact_node_ids_; // [m - 1] node whose output is pre-activation m (1..K-1)
     DevCache weights_;

@@ -265,6 +265,23 @@ __device__ __forceinline__ float relax_fwd(float P, int p, float s, float k, flo
     return pos * k + neg * s;
 }
 
+// Same with a lower intercept bl (Sigmoid): lower bias P+ bl + P- b, upper
+// bias P+ b + P- bl (BoundedSigmoidNode.cpp:723-799).
+__device__ __forceinline__ float relax_fwd_bl(float P, int p, float s, float k, float b, float bl, float& bias) {
+    const float pos = fmaxf(P, 0.f), neg = fminf(P, 0.f);
+    if (p == 0) {
+        bias += pos * bl + neg * b;
+        return pos * s + neg * k;
+    }
+    bias += pos * b + neg * bl;
+    return pos * k + neg * s;
+}
+
+__device__ __forceinline__ float relax_any(const ReluParams& rp, size_t bj, float P, int p, float s, float& bias) {
+    if (rp.b_lo) return relax_fwd_bl(P, p, s, rp.k_up[bj], rp.b_up[bj], rp.b_lo[bj], bias);
+    return relax_fwd(P, p, s, rp.k_up[bj], rp.b_up[bj], bias);
+}
+
 __device__ __forceinline__ float lower_slope(const ReluParams& rp, const float* alpha, int r, int bx,
                                              int j, int ncols) {
     const size_t bj = (size_t)bx * rp.n + j;
@@ -306,7 +323,7 @@ __global__ void start_step_kernel(StartStep st) {
         if (st.rp.n > 0) {
             const size_t bj = (size_t)bx * st.rp.n + c;
             const float s = lower_slope(st.rp, st.alpha, r, bx, c, st.n);
-            Q = relax_fwd(P, p, s, st.rp.k_up[bj], st.rp.b_up[bj], part);
+            Q = relax_any(st.rp, bj, P, p, s, part);
         }
         if (st.Q) st.Q[(size_t)r * st.n + c] = Q;
         if (st.b_next) part = fmaf(Q, st.b_next[c], part);
@@ -348,7 +365,7 @@ struct EpiFwdOp {
                 if (e.P_save) e.P_save[(size_t)r * N + c] = P;
                 const size_t bj = (size_t)bx * e.rp.n + c;
                 const float s = lower_slope(e.rp, e.alpha, r, bx, c, N);
-                const float Q = relax_fwd(P, p, s, e.rp.k_up[bj], e.rp.b_up[bj], part[i]);
+                const float Q = relax_any(e.rp, bj, P, p, s, part[i]);
                 e.Q[(size_t)r * N + c] = Q;
                 if (e.b_next) part[i] = fmaf(Q, e.b_next[c], part[i]);
             }
@@ -383,11 +400,13 @@ struct EpiConcOp {
     }
 };
 
+template <bool SIG>
 struct EpiAdjOp {
     EpiRelaxAdj e;
     int M, N;
     // Flush the running sums of one (8-row group, virtual box) segment.
-    __device__ void flush(int rg, int vb, int c0, const float (&kacc)[8], const float (&bacc)[8]) const {
+    __device__ void flush(int rg, int vb, int c0, const float (&kacc)[8], const float (&bacc)[8],
+                          const float (&sacc)[8], const float (&blacc)[8]) const {
         const size_t slot = (size_t)(rg + vb) * N;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -395,15 +414,19 @@ struct EpiAdjOp {
             if (c < N) {
                 e.kslot[slot + c] = kacc[j];
                 e.bslot[slot + c] = bacc[j];
+                if (SIG) {
+                    e.sslot[slot + c] = sacc[j];
+                    e.blslot[slot + c] = blacc[j];
+                }
             }
         }
     }
     __device__ void operator()(int r0, int c0, float (&acc)[8][8], float (&part)[8]) const {
-        float kacc[8], bacc[8];
+        float kacc[8], bacc[8], sacc[8], blacc[8];
         int cur_vb = -1;
         const int rg = r0 >> 3;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) kacc[j] = bacc[j] = 0.f;
+        for (int j = 0; j < 8; ++j) kacc[j] = bacc[j] = sacc[j] = blacc[j] = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int r = r0 + i;
@@ -415,9 +438,9 @@ struct EpiAdjOp {
             const int vb = bx + p * e.B;
             if (vb != cur_vb) {
                 if (cur_vb >= 0) {
-                    flush(rg, cur_vb, c0, kacc, bacc);
+                    flush(rg, cur_vb, c0, kacc, bacc, sacc, blacc);
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) kacc[j] = bacc[j] = 0.f;
+                    for (int j = 0; j < 8; ++j) kacc[j] = bacc[j] = sacc[j] = blacc[j] = 0.f;
                 }
                 cur_vb = vb;
             }
@@ -432,9 +455,10 @@ struct EpiAdjOp {
                 const uint8_t f = e.rp.flags[bj];
                 const float s = lower_slope(e.rp, e.alpha, r, bx, c, N);
                 const float k = e.rp.k_up[bj], b = e.rp.b_up[bj];
+                const float bl = SIG ? e.rp.b_lo[bj] : 0.f;
                 const bool pos = P >= 0.f, neg = P <= 0.f;
                 const float sP = p == 0 ? s : k, sN = p == 0 ? k : s;
-                const float bP = p == 0 ? 0.f : b, bN = p == 0 ? b : 0.f;
+                const float bP = p == 0 ? bl : b, bN = p == 0 ? b : bl;
                 if (e.Pbar) {
                     const float dq = (pos ? sP : 0.f) + (neg ? sN : 0.f);
                     const float db = (pos ? bP : 0.f) + (neg ? bN : 0.f);
@@ -456,10 +480,14 @@ struct EpiAdjOp {
                 if (f & RF_UNSTABLE) {
                     kacc[j] += Qbar * (p == 0 ? Pn : Pp);
                     bacc[j] += g * (p == 0 ? Pn : Pp);
+                    if (SIG) {
+                        sacc[j] += Qbar * (p == 0 ? Pp : Pn);
+                        blacc[j] += g * (p == 0 ? Pp : Pn);
+                    }
                 }
             }
         }
-        if (cur_vb >= 0) flush(rg, cur_vb, c0, kacc, bacc);
+        if (cur_vb >= 0) flush(rg, cur_vb, c0, kacc, bacc, sacc, blacc);
     }
 };
 
@@ -569,7 +597,10 @@ void launch_gemm_concretize(const float* A, const float* Bm, int M, int N, int K
 }
 void launch_gemm_relax_adj(const float* A, const float* Bm, int M, int N, int K,
                            const EpiRelaxAdj& e, float* partial, cudaStream_t s) {
-    run_gemm(A, Bm, M, N, K, EpiAdjOp{e, M, N}, partial, s);
+    if (e.rp.b_lo)
+        run_gemm(A, Bm, M, N, K, EpiAdjOp<true>{e, M, N}, partial, s);
+    else
+        run_gemm(A, Bm, M, N, K, EpiAdjOp<false>{e, M, N}, partial, s);
 }
 
 // One CTA per (box, 32-column chunk); 256 threads = 32 columns x 8 row lanes.
@@ -1172,6 +1203,189 @@ void launch_add_bounds(float* out_l, float* out_u, const float* in_l, const floa
                        cudaStream_t s) {
     if (n == 0) return;
     add_bounds_kernel<<<ceil_div(n, 256), 256, 0, s>>>(out_l, out_u, in_l, in_u, n, relu_in);
+    LB_LAUNCH();
+}
+
+// ============================================================== Sigmoid
+namespace {
+__device__ __forceinline__ float sig_f(float x) { return 1.f / (1.f + expf(-x)); }
+__device__ __forceinline__ float dsig_f(float x) {
+    const float s = sig_f(x);
+    return s * (1.f - s);
+}
+__device__ __forceinline__ float d2sig_f(float x) {
+    const float s = sig_f(x);
+    return s * (1.f - s) * (1.f - 2.f * s);
+}
+constexpr float SIG_STEP = 0.01f;
+
+// Tangent point whose tangent passes through (b, sigmoid(b)) from below
+// (table d_lower at b = 0.01 i) or from above (table d_upper at b = -0.01 i).
+__device__ float sig_table_point(int i, bool lower_table) {
+    const float b = lower_table ? SIG_STEP * (float)i : -SIG_STEP * (float)i;
+    const float yb = sig_f(b);
+    auto ok = [&](float d) {
+        const float v = dsig_f(d) * (b - d) + sig_f(d);
+        return lower_table ? v <= yb : v >= yb;
+    };
+    if (lower_table) {
+        float l = -1.f, r = 0.f;
+        for (int t = 0; t < 64 && !ok(l); ++t) l *= 2.f;
+        for (int t = 0; t < 100; ++t) {
+            const float m = (l + r) / 2.f;
+            if (ok(m)) l = m;
+            else r = m;
+        }
+        return l;
+    }
+    float l = 0.f, r = 1.f;
+    for (int t = 0; t < 64 && !ok(r); ++t) r *= 2.f;
+    for (int t = 0; t < 100; ++t) {
+        const float m = (l + r) / 2.f;
+        if (ok(m)) r = m;
+        else l = m;
+    }
+    return r;
+}
+
+__device__ __forceinline__ int sig_index(float b) {
+    const float q = b / SIG_STEP;
+    return (q > 0.f ? (int)q : 0) + 1;  // max(0, trunc(q)) + 1
+}
+
+struct SigLines {
+    float kd;           // secant slope (or sigmoid'(l) for a tiny interval)
+    bool pos, neg, both, mdl, mdu, same;
+};
+
+__device__ __forceinline__ SigLines sig_cases(float l, float u) {
+    SigLines c;
+    c.pos = l >= 0.f;
+    c.neg = u <= 0.f;
+    c.both = !(c.pos || c.neg);
+    const float yl = sig_f(l), yu = sig_f(u);
+    c.same = fabsf(u - l) < 1e-4f;
+    c.kd = c.same ? dsig_f(l) : (yu - yl) / fmaxf(u - l, 1e-8f);
+    c.mdl = c.both && c.kd < dsig_f(l);
+    c.mdu = c.both && c.kd < dsig_f(u);
+    return c;
+}
+}  // namespace
+
+__global__ void sigmoid_params_kernel(const float* __restrict__ l, const float* __restrict__ u, int64_t total,
+                                      float* __restrict__ lw, float* __restrict__ lb, float* __restrict__ uw,
+                                      float* __restrict__ ub, uint8_t* __restrict__ flags) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const float lv = l[i], uv = u[i];
+    const SigLines c = sig_cases(lv, uv);
+    const float yl = sig_f(lv);
+    const float sec_b = yl - c.kd * lv;
+    const float m = (lv + uv) / 2.f;
+    const float km = dsig_f(m), bm = sig_f(m) - km * m;
+    float wl, bl, wu, bu;
+    if (c.pos) {
+        wl = c.kd, bl = sec_b, wu = km, bu = bm;
+    } else if (c.neg) {
+        wl = km, bl = bm, wu = c.kd, bu = sec_b;
+    } else {
+        if (c.mdl) {
+            wl = c.kd, bl = sec_b;
+        } else {
+            const float d = sig_table_point(sig_index(uv), true);
+            wl = dsig_f(d);
+            bl = sig_f(d) - wl * d;
+        }
+        if (c.mdu) {
+            wu = c.kd, bu = sec_b;
+        } else {
+            const float d = sig_table_point(sig_index(-lv), false);
+            wu = dsig_f(d);
+            bu = sig_f(d) - wu * d;
+        }
+    }
+    lw[i] = wl;
+    lb[i] = bl;
+    uw[i] = wu;
+    ub[i] = bu;
+    flags[i] = RF_UNSTABLE;
+}
+
+void launch_sigmoid_params(const float* l, const float* u, int B, int n, float* lw, float* lb, float* uw, float* ub,
+                           uint8_t* flags, cudaStream_t s) {
+    const int64_t total = (int64_t)B * n;
+    if (total == 0) return;
+    sigmoid_params_kernel<<<ceil_div(total, 128), 128, 0, s>>>(l, u, total, lw, lb, uw, ub, flags);
+    LB_LAUNCH();
+}
+
+__global__ void sigmoid_bound_grad_kernel(RowMap rows, const float* __restrict__ cur_l,
+                                          const float* __restrict__ cur_u, const float* __restrict__ sbar,
+                                          const float* __restrict__ blbar, const float* __restrict__ kbar,
+                                          const float* __restrict__ bbar, int n, float* __restrict__ g) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows.R) return;
+    const size_t at = (size_t)rows.row_box[r] * n + rows.row_id[r];
+    const float l = cur_l[at], u = cur_u[at];
+    const SigLines c = sig_cases(l, u);
+    // Secant line (k = kd, b = sigmoid(l) - kd l) and midpoint tangent
+    // (k = sigmoid'(m), b = sigmoid(m) - k m, m = (l + u) / 2).
+    float dkd_dl, dkd_du;
+    if (c.same) {
+        dkd_dl = d2sig_f(l);
+        dkd_du = 0.f;
+    } else {
+        const float D = fmaxf(u - l, 1e-8f), dy = sig_f(u) - sig_f(l);
+        dkd_du = dsig_f(u) / D - dy / (D * D);
+        dkd_dl = -dsig_f(l) / D + dy / (D * D);
+    }
+    float gl = 0.f, gu = 0.f;
+    auto secant = [&](float wb, float bb) {
+        const float t = wb - l * bb;
+        gl += t * dkd_dl + bb * (dsig_f(l) - c.kd);
+        gu += t * dkd_du;
+    };
+    auto midpoint = [&](float wb, float bb) {
+        const float m = (l + u) / 2.f;
+        const float gm = d2sig_f(m) * (wb - m * bb);
+        gl += 0.5f * gm;
+        gu += 0.5f * gm;
+    };
+    const float sb = sbar[at], lbb = blbar[at], kb = kbar[at], bb = bbar[at];
+    if (c.pos) {
+        secant(sb, lbb);
+        midpoint(kb, bb);
+    } else if (c.neg) {
+        midpoint(sb, lbb);
+        secant(kb, bb);
+    } else {
+        if (c.mdl) secant(sb, lbb);
+        if (c.mdu) secant(kb, bb);
+    }
+    g[r] = gl;
+    g[rows.R + r] = gu;
+}
+
+void launch_sigmoid_bound_grad(const RowMap& rows, const float* cur_l, const float* cur_u, const float* sbar,
+                               const float* blbar, const float* kbar, const float* bbar, int n, float* g,
+                               cudaStream_t s) {
+    if (rows.R == 0) return;
+    sigmoid_bound_grad_kernel<<<ceil_div(rows.R, 256), 256, 0, s>>>(rows, cur_l, cur_u, sbar, blbar, kbar, bbar, n,
+                                                                    g);
+    LB_LAUNCH();
+}
+
+__global__ void sigmoid_bounds_kernel(const float* __restrict__ l, const float* __restrict__ u, float* __restrict__ ol,
+                                      float* __restrict__ ou, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    ol[i] = sig_f(l[i]);
+    ou[i] = sig_f(u[i]);
+}
+
+void launch_sigmoid_bounds(const float* l, const float* u, float* ol, float* ou, int64_t n, cudaStream_t s) {
+    if (n == 0) return;
+    sigmoid_bounds_kernel<<<ceil_div(n, 256), 256, 0, s>>>(l, u, ol, ou, n);
     LB_LAUNCH();
 }
 

@@ -27,6 +27,7 @@ struct ReluParams {
     const float* k_up = nullptr;      // [B, n] upper slope
     const float* b_up = nullptr;      // [B, n] upper intercept
     const uint8_t* flags = nullptr;   // [B, n] RF_* bits
+    const float* b_lo = nullptr;      // [B, n] lower intercept (Sigmoid); null: 0 (ReLU)
     int n = 0;
 };
 
@@ -151,6 +152,10 @@ struct EpiRelaxAdj {
     // box is unique because rows are sorted by virtual box.
     float* kslot = nullptr;         // [(ceil(M/group) + 2B), N]
     float* bslot = nullptr;
+    // Sigmoid levels (rp.b_lo set): also d loss / d slope_lo and d loss /
+    // d b_lo, for every neuron.
+    float* sslot = nullptr;
+    float* blslot = nullptr;
     int B = 0;
     // Direct accumulators [B, N] (launch_relax_adjoint).
     float* kbar = nullptr;
@@ -205,6 +210,25 @@ void launch_relax_adjoint(const EpiRelaxAdj& e, const float* Qbar, int M, int n,
 // (8 for the SIMT kernel, 32 for the tensor-core kernel).
 void launch_reduce_relax_grad(const RowMap& rows, int M, int B, int N, int group, const float* kslot,
                               const float* bslot, float* kbar, float* bbar, cudaStream_t s);
+
+// ---- Sigmoid (BoundedSigmoidNode) -------------------------------------------
+// Relaxation lw x + lb <= sigmoid(x) <= uw x + ub on [l, u] per neuron
+// (boundRelaxImpl, BoundedSigmoidNode.cpp:282-338): secants where valid, the
+// midpoint tangent on the convex / concave side, and across 0 the tangent
+// points of Luna's tables (:75-151, entry max(0, int(b / 0.01)) + 1 of the
+// bound, :162-186), each entry found here by the same doubling and 100-step
+// fp32 bisection.  Writes slope_lo = lw, b_lo = lb, k_up = uw, b_up = ub and
+// flags RF_UNSTABLE (every neuron passes its parameter adjoints on).
+void launch_sigmoid_params(const float* l, const float* u, int B, int n, float* lw, float* lb, float* uw, float* ub,
+                           uint8_t* flags, cudaStream_t s);
+// d loss / d (l, u) of start row r's neuron from d loss / d (lw, lb, uw, ub)
+// (sbar, blbar, kbar, bbar), by the derivatives of the secant and midpoint
+// lines (the table tangents do not depend on l, u): g[r] and g[R + r].
+void launch_sigmoid_bound_grad(const RowMap& rows, const float* cur_l, const float* cur_u, const float* sbar,
+                               const float* blbar, const float* kbar, const float* bbar, int n, float* g,
+                               cudaStream_t s);
+// Sigmoid output bounds [sigmoid(l), sigmoid(u)] (monotone, :248-272).
+void launch_sigmoid_bounds(const float* l, const float* u, float* ol, float* ou, int64_t n, cudaStream_t s);
 int relax_grad_slots(int M, int B, int group);
 
 // out[r] = base[r] + sum_t partial[t * M + r] for t in [0, ntiles).

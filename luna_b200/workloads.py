@@ -195,6 +195,26 @@ def random_mlp_case(seed: int, n_boxes: int = 8, depth: int = 3, width: int = 12
     return g, Boxes((c - r).astype(np.float32), (c + r).astype(np.float32), margin_spec(t, n_out))
 
 
+def sigmoid_mlp_case(seed: int, n_boxes: int = 4, widths=(6, 14, 12, 4), acts=(NODE_SIGMOID, NODE_SIGMOID),
+                     eps: float = 0.5):
+    """Small MLP with Sigmoid (and ReLU) activations for parity tests:
+    weights 1.5x He-normal and biases N(0, 0.3^2) so that pre-activations
+    cover the convex, concave and crossing regions of the sigmoid."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    nodes = [Node(NODE_INPUT, [], (widths[0], 1, 1))]
+    for i in range(1, len(widths)):
+        w = (rng.standard_normal((widths[i], widths[i - 1])) * np.sqrt(2.0 / widths[i - 1]) * 1.5).astype(np.float32)
+        b = (rng.standard_normal(widths[i]) * 0.3).astype(np.float32)
+        nodes.append(Node(NODE_LINEAR, [len(nodes) - 1], (widths[i], 1, 1), weight=w, bias=b))
+        if i < len(widths) - 1:
+            nodes.append(Node(acts[i - 1], [len(nodes) - 1], (widths[i], 1, 1)))
+    g = Graph(nodes, 0, len(nodes) - 1)
+    c = rng.uniform(-1, 1, (n_boxes, widths[0])).astype(np.float32)
+    r = rng.uniform(0.2 * eps, eps, (n_boxes, widths[0])).astype(np.float32)
+    t = rng.integers(0, widths[-1], n_boxes)
+    return g, Boxes((c - r).astype(np.float32), (c + r).astype(np.float32), margin_spec(t, widths[-1]))
+
+
 def random_cnn_case(seed: int, n_boxes: int = 4, eps: float = 0.05, bn: bool = False):
     """Small random CNN (kernel 2..5, stride 1..2, padding 0..2, 1-3 convs,
     1-2 linear layers; with bn every conv is followed by BatchNorm) and boxes

@@ -11,8 +11,8 @@ behaviour it restates.  Per-box state follows Luna's: IBP bounds, "node
 bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
 parameters keyed by (activation node, start node), and STE reference bounds.
 
-Supported node kinds: Input, Linear, Conv2d, ConvTranspose2d, BatchNorm, ReLU, Add (of
-two tensors), Flatten, Identity.  A
+Supported node kinds: Input, Linear, Conv2d, ConvTranspose2d, BatchNorm, ReLU, Sigmoid,
+Add (of two tensors), Flatten, Identity.  A
 matrices are kept dense over the flattened (C, H, W) features; Luna's
 patches mode (CROWNAnalysis.cpp:255-405, BoundedConvNode.cpp:556-709) is the
 same arithmetic on a window of those features, and it is tracked only to
@@ -29,7 +29,7 @@ import torch.nn.functional as F
 
 from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_ADD, NODE_BATCHNORM,
                            NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT,
-                           NODE_LINEAR, NODE_RELU, Options, default_options)
+                           NODE_LINEAR, NODE_RELU, NODE_SIGMOID, Options, default_options)
 
 # Dense identity starts above this many conv output features switch to
 # patches on Luna's CPU path (CROWNAnalysis.cpp:257,269).
@@ -55,6 +55,130 @@ def topo_order(graph):
             if deg[d] == 0:
                 q.append(d)
     return out, dependents
+
+
+# ---------------------------------------------------------------- Sigmoid
+# BoundedSigmoidNode's tangent-point tables (BoundedSigmoidNode.cpp:75-151):
+# entry i of d_lower is the point whose tangent passes through
+# (0.01 i, sigmoid(0.01 i)) from below, found by doubling then 100 bisection
+# steps in fp32; d_upper mirrors it for (-0.01 i).  Every entry is computed
+# independently of the table length, so one cache grown on demand serves
+# every node (Luna grows its tables to the observed bound + 1, at least 20).
+SIG_STEP = 0.01
+SIG_CUTOFF = 20.0  # LunaConfiguration::SIGMOID_CUTOFF_CONSTANT
+
+
+def _sig(x):
+    return torch.sigmoid(x)
+
+
+def _dsig(x):
+    s = torch.sigmoid(x)
+    return s * (1 - s)
+
+
+class _SigmoidTables:
+    def __init__(self):
+        self.n = -1
+        self.d_lower = None
+        self.d_upper = None
+
+    def ensure(self, limit):
+        n = int(max(SIG_CUTOFF, limit) / SIG_STEP)
+        if n <= self.n:
+            return
+        def check_lower(upper, d):
+            return (_dsig(d) * (upper - d) + _sig(d)) <= _sig(upper)
+
+        def check_upper(lower, d):
+            return (_dsig(d) * (lower - d) + _sig(d)) >= _sig(lower)
+
+        upper = SIG_STEP * torch.arange(0, n + 5, dtype=torch.float32)
+        r = torch.zeros_like(upper)
+        l = -torch.ones_like(upper)
+        while True:
+            c = check_lower(upper, l).to(torch.int64)
+            l = c * l + (1 - c) * (l * 2)
+            if int(c.sum()) == l.numel():
+                break
+        for _ in range(100):
+            m = (l + r) / 2
+            c = check_lower(upper, m).to(torch.int64)
+            l = c * m + (1 - c) * l
+            r = c * r + (1 - c) * m
+        d_lower = l.clone()
+        lower = -SIG_STEP * torch.arange(0, n + 5, dtype=torch.float32)
+        l = torch.zeros_like(upper)
+        r = torch.ones_like(upper)
+        while True:
+            c = check_upper(lower, r).to(torch.int64)
+            r = c * r + (1 - c) * (r * 2)
+            if int(c.sum()) == l.numel():
+                break
+        for _ in range(100):
+            m = (l + r) / 2
+            c = check_upper(lower, m).to(torch.int64)
+            l = (1 - c) * m + c * l
+            r = (1 - c) * r + c * m
+        self.n, self.d_lower, self.d_upper = n, d_lower, r.clone()
+
+    @staticmethod
+    def retrieve(table, bound, default):
+        """retrieveFromPrecompute (:162-186): entry max(0, int(bound / 0.01)) + 1."""
+        idx = torch.clamp_min((bound.detach() / SIG_STEP).to(torch.int64).reshape(-1), 0) + 1
+        if int(idx.max()) >= table.numel():
+            ok = (idx < table.numel()).view(bound.shape)
+            sel = table.index_select(0, torch.clamp(idx, 0, table.numel() - 1)).view(bound.shape)
+            return torch.where(ok, sel, default)
+        return table.index_select(0, idx).view(bound.shape)
+
+
+_SIG_TABLES = _SigmoidTables()
+
+
+def sigmoid_relaxation(l, u):
+    """BoundedSigmoidNode::boundRelaxImpl (:282-338) with generateDLowerUpper
+    (:188-209): (lw, lb, uw, ub) with lw x + lb <= sigmoid(x) <= uw x + ub on
+    [l, u].  Secants where they are valid, the midpoint tangent on the
+    convex / concave side, table tangents across 0."""
+    needed = max(abs(float(l.detach().min())), abs(float(u.detach().max()))) + 1.0
+    _SIG_TABLES.ensure(needed)
+    mask_pos = l >= 0
+    mask_neg = u <= 0
+    mask_both = ~(mask_pos | mask_neg)
+    zero = torch.zeros_like(l)
+    lw, lb, uw, ub = zero, zero, zero, zero
+    y_l, y_u = _sig(l), _sig(u)
+    k_direct = (y_u - y_l) / (u - l).clamp_min(1e-8)
+    same = (u - l).abs() < 1e-4
+    k_direct = torch.where(same, _dsig(l), k_direct)
+    uw = torch.where(mask_neg, k_direct, uw)
+    ub = torch.where(mask_neg, y_l - k_direct * l, ub)
+    lw = torch.where(mask_pos, k_direct, lw)
+    lb = torch.where(mask_pos, y_l - k_direct * l, lb)
+    d_lo = _SigmoidTables.retrieve(_SIG_TABLES.d_lower, u, l.detach())
+    d_up = _SigmoidTables.retrieve(_SIG_TABLES.d_upper, -l, u.detach())
+    mdl = mask_both & (k_direct < _dsig(l))
+    mdu = mask_both & (k_direct < _dsig(u))
+    lw = torch.where(mdl, k_direct, lw)
+    lb = torch.where(mdl, y_l - k_direct * l, lb)
+    uw = torch.where(mdu, k_direct, uw)
+    ub = torch.where(mdu, y_l - k_direct * l, ub)
+    mbl = mask_both & ~mdl
+    mbu = mask_both & ~mdu
+    k_t, y_t = _dsig(d_lo), _sig(d_lo)
+    lw = torch.where(mbl, k_t, lw)
+    lb = torch.where(mbl, y_t - k_t * d_lo, lb)
+    k_t, y_t = _dsig(d_up), _sig(d_up)
+    uw = torch.where(mbu, k_t, uw)
+    ub = torch.where(mbu, y_t - k_t * d_up, ub)
+    m = (l + u) / 2
+    y_m, k_m = _sig(m), _dsig(m)
+    lw = torch.where(mask_neg, k_m, lw)
+    lb = torch.where(mask_neg, y_m - k_m * m, lb)
+    uw = torch.where(mask_pos, k_m, uw)
+    ub = torch.where(mask_pos, y_m - k_m * m, ub)
+    return lw, lb, uw, ub
 
 
 @dataclass
@@ -130,9 +254,9 @@ class LirpaOracle:
             elif nd.type == NODE_ADD:
                 if len(nd.inputs) != 2:
                     raise NotImplementedError("oracle: Add of a constant")
-            elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_FLATTEN, NODE_IDENTITY):
+            elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_SIGMOID, NODE_FLATTEN, NODE_IDENTITY):
                 raise NotImplementedError(f"oracle: node type {nd.type}")
-        self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type == NODE_RELU]
+        self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type in (NODE_RELU, NODE_SIGMOID)]
         self.preact_ids = sorted({graph.nodes[i].inputs[0] for i in self.act_ids})
 
     # ------------------------------------------------------------------ IBP
@@ -177,6 +301,10 @@ class LirpaOracle:
         if nd.type == NODE_RELU:
             l, u = ins[0]
             return torch.clamp_min(l, 0), torch.clamp_min(u, 0)
+        if nd.type == NODE_SIGMOID:
+            # Monotone (BoundedSigmoidNode.cpp:248-272).
+            l, u = ins[0]
+            return _sig(l), _sig(u)
         if nd.type == NODE_ADD:
             # BoundedAddNode::computeIntervalBoundPropagation (:281-304).
             (l1, u1), (l2, u2) = ins
@@ -412,6 +540,20 @@ class LirpaOracle:
                     l, u = self._input_bounds_of(st, c, x)[0]
                     nl, nu, nb_l, nb_u = self._relu_backward(st, c, start, a_l, a_u, l, u)
                     out = [(nl, nu)]
+                elif nd.type == NODE_SIGMOID:
+                    # BoundedSigmoidNode::boundBackward, tensor A (:639-832):
+                    # lower A+ lw + A- uw, bias A+ lb + A- ub; upper mirrored.
+                    # No alpha for Sigmoid: Luna's alpha-CROWN cannot create it
+                    # (ensureAlphaFor writes its 8 tangent slots along the
+                    # neuron axis and throws, AlphaCROWNAnalysis.cpp:264-272),
+                    # so the CROWN relaxation stays, differentiable in (l, u).
+                    l, u = self._input_bounds_of(st, c, x)[0]
+                    lw, lbs, uw, ubs = sigmoid_relaxation(l, u)
+                    Lp, Ln = torch.clamp_min(a_l, 0), torch.clamp_max(a_l, 0)
+                    Up, Un = torch.clamp_min(a_u, 0), torch.clamp_max(a_u, 0)
+                    out = [(Lp * lw + Ln * uw, Up * uw + Un * lw)]
+                    nb_l = (Lp * lbs + Ln * ubs).sum(-1)
+                    nb_u = (Up * ubs + Un * lbs).sum(-1)
                 elif nd.type == NODE_ADD:
                     # BoundedAddNode::boundBackward (:167-279): the same A to both
                     # operands (equal shapes), no bias of its own.
@@ -513,7 +655,7 @@ class LirpaOracle:
         nd = self.g.nodes[i]
         for p in nd.inputs:
             self._check_prior(st, p, x)
-        if nd.type == NODE_RELU:
+        if nd.type in (NODE_RELU, NODE_SIGMOID):
             self._lazy_intermediate(st, nd.inputs[0], x)
 
     def _run(self, st, x, C):

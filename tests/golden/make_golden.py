@@ -87,6 +87,14 @@ def cases():
     out.append(("resnetbig_crown", "small_resnet_case", kw, 2, abi.METHOD_CROWN, {}))
     out.append(("resnetbig_alpha", "small_resnet_case", kw, 1, abi.METHOD_ALPHA_CROWN,
                 {"alpha_lr": 0.1, "alpha_iterations": 3}))
+    # Sigmoid activations (CROWN only: Luna's alpha-CROWN throws on any
+    # Sigmoid node, AlphaCROWNAnalysis.cpp:264-272).
+    out.append(("sig_crown", "sigmoid_mlp_case", {"seed": 0}, 4, abi.METHOD_CROWN, {}))
+    out.append(("sigmix_crown", "sigmoid_mlp_case", {"seed": 1, "acts": (abi.NODE_RELU, abi.NODE_SIGMOID),
+                                                      "eps": 1.0}, 4, abi.METHOD_CROWN, {}))
+    out.append(("sigwide_crown", "sigmoid_mlp_case", {"seed": 3, "eps": 8.0}, 4, abi.METHOD_CROWN, {}))
+    out.append(("resnetsig_crown", "small_resnet_case", {"seed": 9, "n_boxes": 3, "head_act": abi.NODE_SIGMOID},
+                3, abi.METHOD_CROWN, {}))
     # The CIFAR-shaped CNN at full size, one box.
     out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
     return out

@@ -265,16 +265,38 @@ def test_resnet_matches_oracle(method, seed, big):
     _assert_parity(f"resnet{seed}/{method}/{int(big)}", lb, ub, olb, oub)
 
 
-def test_resnet_cifar_sound_and_ordered():
-    """The CIFAR ResNet (ReLU head variant): CROWN bounds are sound at 10^5
-    sampled points per box and at least as tight as IBP."""
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_resnet_cifar_sound_and_ordered(method):
+    """The CIFAR ResNet (Sigmoid head): bounds are sound at 10^5 sampled
+    points per box, CROWN at least as tight as IBP, alpha-CROWN's lower
+    bound at least CROWN's."""
     g, bx = W.resnet_cifar(2)
-    g = W.resnet((3, 32, 32), 16, [(16, 1), (16, 1), (32, 2), (32, 1)], [100, 10], 3, head_act=abi.NODE_RELU)
-    m = Model(g, options=abi.default_options())
+    m = Model(g, options=abi.default_options(alpha_lr=0.1, alpha_iterations=5))
     ilb, iub = m.compute_bounds(bx, abi.METHOD_IBP)
-    lb, ub = m.compute_bounds(bx, abi.METHOD_CROWN)
-    tol = 1e-4 * (1 + np.abs(lb))
-    assert np.isfinite(lb).all() and (lb >= ilb - tol).all() and (ub <= iub + tol).all()
+    clb, cub = m.compute_bounds(bx, abi.METHOD_CROWN)
+    lb, ub = m.compute_bounds(bx, method) if method != abi.METHOD_CROWN else (clb, cub)
+    tol = 1e-4 * (1 + np.abs(clb))
+    assert np.isfinite(lb).all() and (clb >= ilb - tol).all() and (cub <= iub + tol).all()
+    assert (lb >= clb - tol).all() and (lb <= ub).all()
     for b, y in enumerate(_sample_outputs(g, bx, 100_000)):
         assert (y.min(0).values.cpu().numpy() >= lb[b] - tol[b]).all()
         assert (y.max(0).values.cpu().numpy() <= ub[b] + tol[b]).all()
+
+
+@pytest.mark.parametrize("case", ["sig", "sigmix", "relusig", "resnetsig"])
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_sigmoid_matches_oracle(method, case):
+    """Sigmoid relaxations (secant, midpoint and table tangents), alone and
+    mixed with ReLU; under alpha-CROWN the gradient runs through the Sigmoid
+    relaxation's dependence on its input bounds."""
+    from oracle.lirpa_oracle import LirpaOracle
+    if case == "resnetsig":
+        g, bx = W.small_resnet_case(60, n_boxes=3, head_act=abi.NODE_SIGMOID)
+    else:
+        acts = {"sig": (abi.NODE_SIGMOID, abi.NODE_SIGMOID), "sigmix": (abi.NODE_SIGMOID, abi.NODE_RELU),
+                "relusig": (abi.NODE_RELU, abi.NODE_SIGMOID)}[case]
+        g, bx = W.sigmoid_mlp_case(70, n_boxes=6, widths=(8, 24, 20, 5), acts=acts, eps=1.0)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=6)
+    lb, ub = Model(g, options=opt).compute_bounds(bx, method)
+    olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
+    _assert_parity(f"{case}/{method}", lb, ub, olb, oub)
