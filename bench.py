@@ -10,13 +10,17 @@ A step bounds one batch of 512 boxes per GPU.  With N GPUs (torchrun) each
 rank bounds its own 512 boxes (weak scaling) and the final bounds are
 all-gathered over NCCL inside the step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload mlp|cnn]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload mlp|cnn|resnet]
 
 `--impl reference` times Luna's own CPU implementation (oracle/_ref) on the
 host cores for the same workload and metric.  `--workload cnn` measures the
 CIFAR-shaped CNN instead (3x32x32 -> conv32 k3 -> conv64 k4s2 -> conv64 k4s2
 -> 512 -> 10, He-normal weights, seed 2; 256 boxes per GPU, eps 2/255, 9
-margin rows; alpha-CROWN 30 iterations at Luna's default lr 0.5).
+margin rows; alpha-CROWN 30 iterations at Luna's default lr 0.5).  `--workload
+resnet` measures the small CIFAR ResNet (stem conv3->16 k3, residual blocks
+16, 16, 32 s2 with a 1x1 projection skip, 32, BatchNorm with running mean 0,
+flatten 8192 -> 100 -> Sigmoid -> 10, seed 3; 128 boxes per GPU, eps 1/255;
+alpha-CROWN 50 iterations at lr 0.5).
 """
 from __future__ import annotations
 
@@ -50,6 +54,10 @@ WORKLOADS = {
     "cnn": dict(name="cnn", gen=W.cnn_cifar, boxes=256, iters=30, lr=0.5, input_dim=3072,
                 desc="cnn_cifar 3x32x32 conv32-conv64s2-conv64s2-fc512-fc10 alpha-CROWN (30 Adam "
                      "iterations, lr 0.5), {b} boxes per GPU, eps 2/255, 9 margin specs"),
+    "resnet": dict(name="resnet", gen=W.resnet_cifar, boxes=128, iters=50, lr=0.5, input_dim=3072,
+                   desc="resnet_cifar 3x32x32 stem16 + 4 residual blocks (16,16,32s2+proj,32) with BatchNorm, "
+                        "fc100-Sigmoid-fc10 alpha-CROWN (50 Adam iterations, lr 0.5), {b} boxes per GPU, "
+                        "eps 1/255, 9 margin specs"),
 }
 WL = dict(WORKLOADS["mlp"])
 BOXES_PER_GPU = WL["boxes"]

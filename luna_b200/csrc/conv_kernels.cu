@@ -334,6 +334,204 @@ void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConc
     LB_LAUNCH();
 }
 
+// ============================================================== register-blocked steps
+constexpr int RB_MAX_W_FLOATS = 12 * 1024;  // 48 KB of weights in shared memory
+
+bool convT_rb_ok(const ConvStep& cs) {
+    return (cs.Ci == 8 || cs.Ci == 16 || cs.Ci == 32) && cs.Co % 4 == 0 && cs.cy >= 0 && cs.cx >= 0 &&
+           (int64_t)cs.kh * cs.kw * cs.Co * cs.Ci <= RB_MAX_W_FLOATS;
+}
+
+int convT_rb_chunks(const WinGeo& out) { return ceil_div(out.wh * out.ww, 256); }
+
+template <int CI>
+__global__ void __launch_bounds__(256) convT_relax_rb_kernel(const float* __restrict__ A, ConvStep cs, int M,
+                                                             ConvRelaxEpi e, int nchunk, float* __restrict__ partial) {
+    extern __shared__ float4 rb_w4[];
+    float* wsh = reinterpret_cast<float*>(rb_w4);
+    __shared__ float red[8];
+    const int nwt = cs.kh * cs.kw * cs.Co * CI;
+    for (int i = threadIdx.x; i < nwt; i += blockDim.x) wsh[i] = cs.Wk[i];
+    __syncthreads();
+    const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
+    const int npix = cs.out_h * cs.out_w;
+    const int pix = chunk * 256 + threadIdx.x;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    float part = 0.f;
+    if (pix < npix) {
+        float acc[CI];
+#pragma unroll
+        for (int c = 0; c < CI; ++c) acc[c] = 0.f;
+        const int vy = pix / cs.out_w, vx = pix - (pix / cs.out_w) * cs.out_w;
+        const int ty = vy + cs.cy, tx = vx + cs.cx;
+        const float* Arow = A + (size_t)r * cs.in_h * cs.in_w * cs.Co;
+        for (int ky = ty % cs.sh; ky < cs.kh && ky <= ty; ky += cs.sh) {
+            const int qy = (ty - ky) / cs.sh;
+            if (qy >= cs.in_h) continue;
+            for (int kx = tx % cs.sw; kx < cs.kw && kx <= tx; kx += cs.sw) {
+                const int qx = (tx - kx) / cs.sw;
+                if (qx >= cs.in_w) continue;
+                const float4* a4 = reinterpret_cast<const float4*>(Arow + ((size_t)qy * cs.in_w + qx) * cs.Co);
+                const float* w = wsh + (size_t)(ky * cs.kw + kx) * cs.Co * CI;
+                for (int c4 = 0; c4 < cs.Co / 4; ++c4) {
+                    const float4 a = __ldg(a4 + c4);
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(c4 * 4 + t) * CI);
+#pragma unroll
+                        for (int c = 0; c < CI / 4; ++c) {
+                            const float4 wv = wr[c];
+                            acc[4 * c + 0] = fmaf(av[t], wv.x, acc[4 * c + 0]);
+                            acc[4 * c + 1] = fmaf(av[t], wv.y, acc[4 * c + 1]);
+                            acc[4 * c + 2] = fmaf(av[t], wv.z, acc[4 * c + 2]);
+                            acc[4 * c + 3] = fmaf(av[t], wv.w, acc[4 * c + 3]);
+                        }
+                    }
+                }
+            }
+        }
+        const size_t at0 = (size_t)r * npix * CI + (size_t)pix * CI;
+        int oy, ox;
+        win_origin(e.g, e.rows.row_id[rr], oy, ox);
+        const int nu0 = win_neuron(e.g, oy, ox, pix * CI);  // the pixel's channel 0, or -1 outside the map
+#pragma unroll
+        for (int c = 0; c < CI; c += 4) {
+            float Pv[4] = {acc[c], acc[c + 1], acc[c + 2], acc[c + 3]};
+            if (e.addend) {
+                const float4 ad = *reinterpret_cast<const float4*>(e.addend + at0 + c);
+                Pv[0] += ad.x;
+                Pv[1] += ad.y;
+                Pv[2] += ad.z;
+                Pv[3] += ad.w;
+            }
+            if (e.P_save) *reinterpret_cast<float4*>(e.P_save + at0 + c) = make_float4(Pv[0], Pv[1], Pv[2], Pv[3]);
+            float Qv[4] = {0.f, 0.f, 0.f, 0.f};
+            if (nu0 >= 0) {
+                const size_t bj = (size_t)bx * e.rp.n + nu0 + c;
+                const float4 s4 = *reinterpret_cast<const float4*>(e.rp.slope_lo + bj);
+                const float4 k4 = *reinterpret_cast<const float4*>(e.rp.k_up + bj);
+                const float4 b4 = *reinterpret_cast<const float4*>(e.rp.b_up + bj);
+                const uchar4 f4 = *reinterpret_cast<const uchar4*>(e.rp.flags + bj);
+                float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (e.alpha && ((f4.x | f4.y | f4.z | f4.w) & RF_USE_ALPHA))
+                    a4 = *reinterpret_cast<const float4*>(e.alpha + at0 + c);
+                const float Av[4] = {a4.x, a4.y, a4.z, a4.w};
+                const float sl[4] = {s4.x, s4.y, s4.z, s4.w}, ku[4] = {k4.x, k4.y, k4.z, k4.w},
+                            bu[4] = {b4.x, b4.y, b4.z, b4.w};
+                const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float sv = (e.alpha && (fl[i] & RF_USE_ALPHA)) ? Av[i] : sl[i];
+                    Qv[i] = relax_q(Pv[i], p, sv, ku[i], bu[i], part);
+                    if (e.b_next) part = fmaf(Qv[i], e.b_next[c + i], part);
+                }
+            }
+            *reinterpret_cast<float4*>(e.Q + at0 + c) = make_float4(Qv[0], Qv[1], Qv[2], Qv[3]);
+        }
+    }
+    const float tot = block_sum256(part, red);
+    if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+}
+
+void launch_convT_relax_rb(const float* A, const ConvStep& cs, int M, const ConvRelaxEpi& e, float* partial,
+                           cudaStream_t s) {
+    if (M == 0) return;
+    if (!convT_rb_ok(cs) || e.g.C != cs.Ci || e.g.wh != cs.out_h || e.g.ww != cs.out_w)
+        throw std::invalid_argument("convT_relax_rb: unsupported step");
+    const int nchunk = convT_rb_chunks(e.g);
+    const size_t smem = (size_t)cs.kh * cs.kw * cs.Co * cs.Ci * 4;
+    const unsigned grid = (unsigned)((int64_t)M * nchunk);
+    if (cs.Ci == 8)
+        convT_relax_rb_kernel<8><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, partial);
+    else if (cs.Ci == 16)
+        convT_relax_rb_kernel<16><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, partial);
+    else
+        convT_relax_rb_kernel<32><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, partial);
+    LB_LAUNCH();
+}
+
+bool conv_adj_rb_ok(const ConvStep& cs) {
+    return (cs.Co == 8 || cs.Co == 16 || cs.Co == 32) && cs.Ci % 4 == 0 &&
+           (int64_t)cs.kh * cs.kw * cs.Co * cs.Ci <= RB_MAX_W_FLOATS;
+}
+
+template <int CO>
+__global__ void __launch_bounds__(256) conv_adj_qbar_rb_kernel(const float* __restrict__ Pbar, ConvStep cs, int M,
+                                                               const float* __restrict__ gseed,
+                                                               const float* __restrict__ b, float* __restrict__ Qbar) {
+    extern __shared__ float4 rb_w4[];
+    float* wsh = reinterpret_cast<float*>(rb_w4);
+    // wsh[((ky kw + kx) Ci + ci) CO + co] = W[co, ci, ky, kx]
+    const int taps = cs.kh * cs.kw;
+    const int nwt = taps * cs.Ci * CO;
+    for (int i = threadIdx.x; i < nwt; i += blockDim.x) {
+        const int co = i % CO, rest = i / CO;
+        const int ci = rest % cs.Ci, tap = rest / cs.Ci;
+        wsh[i] = cs.Wc[((size_t)co * taps + tap) * cs.Ci + ci];
+    }
+    __syncthreads();
+    const int nq = cs.in_h * cs.in_w;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)M * nq) return;
+    const int r = (int)(idx / nq), q = (int)(idx - (int64_t)r * nq);
+    const int qy = q / cs.in_w, qx = q - (q / cs.in_w) * cs.in_w;
+    const float* prow = Pbar + (size_t)r * cs.out_h * cs.out_w * cs.Ci;
+    float acc[CO];
+#pragma unroll
+    for (int c = 0; c < CO; ++c) acc[c] = 0.f;
+    for (int ky = 0; ky < cs.kh; ++ky) {
+        const int vy = qy * cs.sh + ky - cs.cy;
+        if (vy < 0 || vy >= cs.out_h) continue;
+        for (int kx = 0; kx < cs.kw; ++kx) {
+            const int vx = qx * cs.sw + kx - cs.cx;
+            if (vx < 0 || vx >= cs.out_w) continue;
+            const float4* p4 = reinterpret_cast<const float4*>(prow + ((size_t)vy * cs.out_w + vx) * cs.Ci);
+            const float* w = wsh + (size_t)(ky * cs.kw + kx) * cs.Ci * CO;
+            for (int c4 = 0; c4 < cs.Ci / 4; ++c4) {
+                const float4 pv = __ldg(p4 + c4);
+                const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(c4 * 4 + t) * CO);
+#pragma unroll
+                    for (int c = 0; c < CO / 4; ++c) {
+                        const float4 wv = wr[c];
+                        acc[4 * c + 0] = fmaf(pa[t], wv.x, acc[4 * c + 0]);
+                        acc[4 * c + 1] = fmaf(pa[t], wv.y, acc[4 * c + 1]);
+                        acc[4 * c + 2] = fmaf(pa[t], wv.z, acc[4 * c + 2]);
+                        acc[4 * c + 3] = fmaf(pa[t], wv.w, acc[4 * c + 3]);
+                    }
+                }
+            }
+        }
+    }
+    const float g = gseed[r];
+    float* out = Qbar + (size_t)idx * CO;
+#pragma unroll
+    for (int c = 0; c < CO; c += 4)
+        *reinterpret_cast<float4*>(out + c) = make_float4(acc[c] + g * b[c], acc[c + 1] + g * b[c + 1],
+                                                          acc[c + 2] + g * b[c + 2], acc[c + 3] + g * b[c + 3]);
+}
+
+void launch_conv_adj_qbar_rb(const float* Pbar, const ConvStep& cs, int M, const float* gseed, const float* b,
+                             float* Qbar, cudaStream_t s) {
+    const int64_t total = (int64_t)M * cs.in_h * cs.in_w;
+    if (total == 0) return;
+    if (!conv_adj_rb_ok(cs)) throw std::invalid_argument("conv_adj_qbar_rb: unsupported step");
+    const size_t smem = (size_t)cs.kh * cs.kw * cs.Co * cs.Ci * 4;
+    const unsigned grid = (unsigned)ceil_div(total, 256);
+    if (cs.Co == 8)
+        conv_adj_qbar_rb_kernel<8><<<grid, 256, smem, s>>>(Pbar, cs, M, gseed, b, Qbar);
+    else if (cs.Co == 16)
+        conv_adj_qbar_rb_kernel<16><<<grid, 256, smem, s>>>(Pbar, cs, M, gseed, b, Qbar);
+    else
+        conv_adj_qbar_rb_kernel<32><<<grid, 256, smem, s>>>(Pbar, cs, M, gseed, b, Qbar);
+    LB_LAUNCH();
+}
+
 int relax_window_chunks(const WinGeo& g) { return ceil_div(g.size(), 1024); }
 
 // 256 threads x 4 consecutive elements (one pixel's channels when C % 4 == 0).

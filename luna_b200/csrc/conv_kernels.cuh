@@ -116,6 +116,22 @@ void launch_convT_relax(const float* A, const ConvStep& cs, int M, const ConvRel
 void launch_convT_conc(const float* A, const ConvStep& cs, int M, const ConvConcEpi& e, float* partial,
                        cudaStream_t s);
 
+// Register-blocked forms of the two SIMT conv steps for layers with few
+// channels on the output side of the step (8, 16 or 32): one thread per
+// window pixel keeps all of that pixel's channels in registers, the layer's
+// weights sit in shared memory (at most 48 KB), and every element is summed
+// in the same order as launch_convT_relax / launch_conv_adj_qbar (identical
+// A and Qbar; the per-row bias partials are grouped differently).  The
+// forward step writes one partial per (row, 256-pixel chunk):
+// convT_rb_chunks() of them.
+bool convT_rb_ok(const ConvStep& cs);
+int convT_rb_chunks(const WinGeo& out);
+void launch_convT_relax_rb(const float* A, const ConvStep& cs, int M, const ConvRelaxEpi& e, float* partial,
+                           cudaStream_t s);
+bool conv_adj_rb_ok(const ConvStep& cs);
+void launch_conv_adj_qbar_rb(const float* Pbar, const ConvStep& cs, int M, const float* gseed, const float* b,
+                             float* Qbar, cudaStream_t s);
+
 // ReLU relaxation of a level from its raw A window P (stored by a tensor-core
 // step): Q = relax(P) masked outside the map, bias partials (intercepts +
 // Q . b_next per row) into partial[chunk * M + r], one chunk per 1024

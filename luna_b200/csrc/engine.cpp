@@ -922,6 +922,8 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             slots_total += 1;
         else if (tc_fwd(m))
             slots_total += relax_window_chunks(sp.geo[m - 1]);
+        else if (m >= 2 && convT_rb_ok(conv_step(st, m)))
+            slots_total += convT_rb_chunks(sp.geo[m - 1]);
         else
             slots_total += conv_chunks(sp.geo[m - 1]);
     }
@@ -1057,6 +1059,13 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                     prof_end(s, fl);
                     launch_relax_window(f.P, e, M, part + (size_t)slot * M, s);
                     slot += relax_window_chunks(sp.geo[m - 1]);
+                    cur = 1 - cur;
+                    continue;
+                }
+                if (convT_rb_ok(cs)) {
+                    launch_convT_relax_rb(Q[cur], cs, M, e, part + (size_t)slot * M, s);
+                    prof_end(s, fl);
+                    slot += convT_rb_chunks(sp.geo[m - 1]);
                     cur = 1 - cur;
                     continue;
                 }
@@ -1328,6 +1337,8 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
                 q.b = level_bias(m);
                 q.Qbar = Qbar;
                 launch_tc_conv_qbar(tc_adj_plan(st, m, M, pin), M, q, s);
+            } else if (conv_adj_rb_ok(cs)) {
+                launch_conv_adj_qbar_rb(pin, cs, M, g, level_bias(m), Qbar, s);
             } else {
                 launch_conv_adj_qbar(pin, cs, M, g, level_bias(m), Qbar, s);
             }
