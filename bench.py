@@ -57,7 +57,10 @@ WORKLOADS = {
     "resnet": dict(name="resnet", gen=W.resnet_cifar, boxes=128, iters=50, lr=0.5, input_dim=3072,
                    desc="resnet_cifar 3x32x32 stem16 + 4 residual blocks (16,16,32s2+proj,32) with BatchNorm, "
                         "fc100-Sigmoid-fc10 alpha-CROWN (50 Adam iterations, lr 0.5), {b} boxes per GPU, "
-                        "eps 1/255, 9 margin specs"),
+                        "eps 1/255, 9 margin specs",
+                   ref_unavailable="Luna's alpha-CROWN throws on any graph with a Sigmoid node "
+                                   "(AlphaCROWNAnalysis::ensureAlphaFor writes its 8 tangent slots along the "
+                                   "neuron axis: shape error), so its CPU path has no alpha-CROWN result here"),
 }
 WL = dict(WORKLOADS["mlp"])
 BOXES_PER_GPU = WL["boxes"]
@@ -283,7 +286,10 @@ def run_engine(args):
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(args.cpu_boxes)
+            if WL.get("ref_unavailable"):
+                line["cpu_baseline"] = {"unavailable": WL["ref_unavailable"]}
+            else:
+                line["cpu_baseline"] = cpu_baseline(args.cpu_boxes)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -360,6 +366,9 @@ def run_reference(args):
     from oracle import luna_ref
     if not luna_ref.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libluna_ref.so not built"}))
+        return
+    if WL.get("ref_unavailable"):
+        print(json.dumps({"impl": "reference", "unavailable": WL["ref_unavailable"]}))
         return
     cb = CpuBaseline()
     try:
