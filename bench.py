@@ -54,6 +54,10 @@ WORKLOADS = {
     "cnn": dict(name="cnn", gen=W.cnn_cifar, boxes=256, iters=30, lr=0.5, input_dim=3072,
                 desc="cnn_cifar 3x32x32 conv32-conv64s2-conv64s2-fc512-fc10 alpha-CROWN (30 Adam "
                      "iterations, lr 0.5), {b} boxes per GPU, eps 2/255, 9 margin specs"),
+    "sweep": dict(name="sweep", gen=W.convt_sweep_boxes, boxes=256, iters=50, lr=0.5, input_dim=3072,
+                  desc="cnn_convt_cifar sub-domain sweep (one eps 8/255 box split into 65,536 sub-domains along "
+                       "16 groups of 4 widest-gradient pixels), {b} sub-domains per GPU, alpha-CROWN (50 Adam "
+                       "iterations, lr 0.5), 9 margin specs"),
     "resnet": dict(name="resnet", gen=W.resnet_cifar, boxes=128, iters=50, lr=0.5, input_dim=3072,
                    desc="resnet_cifar 3x32x32 stem16 + 4 residual blocks (16,16,32s2+proj,32) with BatchNorm, "
                         "fc100-Sigmoid-fc10 alpha-CROWN (50 Adam iterations, lr 0.5), {b} boxes per GPU, "

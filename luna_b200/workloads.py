@@ -10,8 +10,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .abi import (NODE_ADD, NODE_BATCHNORM, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_INPUT,
-                  NODE_LINEAR, NODE_RELU, NODE_SIGMOID, Graph, Node)
+from .abi import (NODE_ADD, NODE_BATCHNORM, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY,
+                  NODE_INPUT, NODE_LINEAR, NODE_RELU, NODE_SIGMOID, Graph, Node)
 
 
 def mlp(widths, seed: int, bias_std: float = 0.01) -> Graph:
@@ -371,3 +371,129 @@ def small_resnet_case(seed: int, n_boxes: int = 3, eps: float = 0.01, hw: int = 
     g = resnet((3, hw, hw), c, [(c, 1), (2 * c, 2)], [12, 4], seed + 13, bias_std=0.05, head_act=head_act,
                bn_mean_std=0.1)
     return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)
+
+
+def graph_forward(graph, x):
+    """Plain forward of a graph on a batch of flat CHW inputs (torch, CPU);
+    used to rank input pixels when splitting a box, not on the bounding path."""
+    import torch
+    import torch.nn.functional as F
+    f = lambda a: torch.from_numpy(np.asarray(a, np.float32))
+    deg = [len(n.inputs) for n in graph.nodes]
+    users = [[] for _ in graph.nodes]
+    for i, n in enumerate(graph.nodes):
+        for p in n.inputs:
+            users[p].append(i)
+    order, q = [], [i for i, d in enumerate(deg) if d == 0]
+    while q:
+        c = q.pop(0)
+        order.append(c)
+        for u in users[c]:
+            deg[u] -= 1
+            if deg[u] == 0:
+                q.append(u)
+    val = {}
+    for i in order:
+        n = graph.nodes[i]
+        ins = [val[p] for p in n.inputs]
+        if n.type == NODE_INPUT:
+            y = x.reshape(x.shape[0], *n.out_shape)
+        elif n.type == NODE_LINEAR:
+            y = ins[0].reshape(x.shape[0], -1) @ (f(n.weight) * n.scale).T + (f(n.bias) if n.bias is not None else 0)
+        elif n.type == NODE_CONV:
+            y = F.conv2d(ins[0], f(n.weight), f(n.bias) if n.bias is not None else None, stride=n.stride,
+                         padding=n.padding)
+        elif n.type == NODE_CONVTRANSPOSE:
+            y = F.conv_transpose2d(ins[0], f(n.weight), f(n.bias) if n.bias is not None else None,
+                                   stride=n.stride, padding=n.padding)
+        elif n.type == NODE_BATCHNORM:
+            w = f(n.weight) / torch.sqrt(f(n.running_var) + n.eps)
+            b = f(n.bias) - f(n.running_mean) * w
+            y = ins[0] * w.view(1, -1, 1, 1) + b.view(1, -1, 1, 1)
+        elif n.type == NODE_RELU:
+            y = torch.relu(ins[0])
+        elif n.type == NODE_SIGMOID:
+            y = torch.sigmoid(ins[0])
+        elif n.type == NODE_ADD:
+            y = ins[0] + ins[1]
+        elif n.type in (NODE_FLATTEN, NODE_IDENTITY):
+            y = ins[0].reshape(x.shape[0], -1) if n.type == NODE_FLATTEN else ins[0]
+        else:
+            raise NotImplementedError(n.type)
+        val[i] = y
+    return val[graph.output_index].reshape(x.shape[0], -1)
+
+
+@dataclass
+class SubdomainSplit:
+    """A box split into 2^(groups) sub-domains: sub-domain `sid` takes, for
+    every group g, the lower half of the box on the group's pixels when bit g
+    of sid is 0 and the upper half when it is 1 (all other pixels keep the
+    whole box).  A group is bisected as a unit, so the sub-domains cover the
+    points whose pixels in each group lie on one side of the midpoint."""
+    lower: np.ndarray    # [n_in] the box
+    upper: np.ndarray
+    centre: np.ndarray   # [n_in] the point the pixels were ranked at
+    C: np.ndarray        # [1, nspec, n_out]
+    groups: np.ndarray   # [n_groups, group_size] input indices (CHW)
+
+    @property
+    def count(self) -> int:
+        return 1 << len(self.groups)
+
+    def boxes(self, first: int, n: int) -> Boxes:
+        """Sub-domains first .. first + n - 1 as a batch of boxes."""
+        ids = np.arange(first, first + n, dtype=np.int64)
+        if n and (ids[0] < 0 or ids[-1] >= self.count):
+            raise ValueError("sub-domain id out of range")
+        lo = np.repeat(self.lower[None], n, 0)
+        hi = np.repeat(self.upper[None], n, 0)
+        mid = ((self.lower + self.upper) / np.float32(2)).astype(np.float32)
+        for g, idx in enumerate(self.groups):
+            bit = ((ids >> g) & 1).astype(bool)
+            lo[np.ix_(bit, idx)] = mid[idx]
+            hi[np.ix_(~bit, idx)] = mid[idx]
+        return Boxes(lo, hi, self.C)
+
+
+def subdomain_split(graph, seed: int, eps: float, n_groups: int = 16, group_size: int = 4,
+                    n_in_shape=(3, 32, 32)) -> SubdomainSplit:
+    """Split one seeded eps-box (centre U[0,1], clipped to [0, 1], 9 margin rows
+    for a uniformly drawn true class) along its widest-gradient pixels: rank
+    the input coordinates by |d margin / d x| * width at the centre (margin =
+    the sum of the specification rows), take the top n_groups * group_size,
+    and group them in rank order into n_groups groups of group_size; each
+    bit of a sub-domain id bisects one group."""
+    import torch
+    rng = np.random.Generator(np.random.PCG64(seed))
+    n_in = int(np.prod(n_in_shape))
+    n_out = graph.nodes[graph.output_index].out_shape[0]
+    c = rng.uniform(0.0, 1.0, n_in).astype(np.float32)
+    t = int(rng.integers(0, n_out))
+    lo = np.clip(c - np.float32(eps), 0.0, 1.0).astype(np.float32)
+    hi = np.clip(c + np.float32(eps), 0.0, 1.0).astype(np.float32)
+    C = margin_spec(np.array([t]), n_out)
+    x = torch.from_numpy(c[None]).requires_grad_(True)
+    y = graph_forward(graph, x)
+    (y @ torch.from_numpy(C[0]).T).sum().backward()
+    score = np.abs(x.grad.numpy()[0]) * (hi - lo)
+    top = np.argsort(-score, kind="stable")[: n_groups * group_size]
+    return SubdomainSplit(lo, hi, c, C, top.reshape(n_groups, group_size).astype(np.int64))
+
+
+def convt_sweep(seed: int = 5, eps: float = 8.0 / 255.0):
+    """The transposed-conv CIFAR CNN and its eps = 8/255 box split into
+    65,536 sub-domains (16 groups of 4 widest-gradient pixels)."""
+    g, _ = cnn_convt_cifar(1, seed=seed)
+    return g, subdomain_split(g, seed + 2000, eps)
+
+
+_SWEEP = {}
+
+
+def convt_sweep_boxes(n_boxes: int, seed: int = 5):
+    """The first n_boxes sub-domains of convt_sweep (cached split)."""
+    if seed not in _SWEEP:
+        _SWEEP[seed] = convt_sweep(seed)
+    g, split = _SWEEP[seed]
+    return g, split.boxes(0, n_boxes)
