@@ -224,6 +224,34 @@ LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const float* d_x_lowe
  * per side; pass NULL buffers to query it. */
 LB200_API int lb200_get_intermediate_bounds(lb200_model* model, float* lower, float* upper, int64_t* count);
 
+/* ---- multi-GPU: box sharding over NCCL ------------------------------------
+ * Luna bounds one box per call and has no distributed path; boxes share only
+ * the read-only weights.  N ranks, one process per GPU, each bound a
+ * contiguous share of a batch and exchange only the final bounds (one NCCL
+ * all-gather).  NCCL is resolved at run time from the process's
+ * libnccl.so.2, so a caller may pass its own ncclComm_t as `comm`. */
+
+/* [begin, end) of n boxes for `rank` of `world` (shares differ by at most one). */
+LB200_API int lb200_shard_range(int rank, int world, int64_t n, int64_t* begin, int64_t* end);
+
+/* A 128-byte ncclUniqueId made on one rank and shared with the others by the
+ * caller; lb200_nccl_comm_create then joins the communicator on `device`
+ * (blocks until all `world` ranks have joined). */
+LB200_API int lb200_nccl_unique_id(uint8_t id[128]);
+LB200_API int lb200_nccl_comm_create(const uint8_t id[128], int rank, int world, int device, void** comm);
+LB200_API int lb200_nccl_comm_destroy(void* comm);
+
+/* Every rank passes the whole batch (host buffers, as lb200_compute_bounds);
+ * rank r bounds its share lb200_shard_range(r, world, n_boxes) and all
+ * ranks receive the bounds of every box in out_lb / out_ub [n_boxes, nspec].
+ * The wait for the gather is bounded by timeout_ms (60 s when <= 0): when it
+ * expires, or NCCL reports an asynchronous error, the communicator is
+ * aborted and an error returned.  stats covers this rank's share. */
+LB200_API int lb200_shard_run(lb200_model* model, void* comm, int rank, int world, int method,
+                              const float* x_lower, const float* x_upper, int64_t n_boxes,
+                              const float* C, int64_t c_boxes, int64_t nspec,
+                              float* out_lb, float* out_ub, int timeout_ms, lb200_stats* stats);
+
 /* Copy the last error message of this thread into buf (always terminated). */
 LB200_API int lb200_last_error(char* buf, size_t len);
 

@@ -14,7 +14,8 @@ ROOT = os.path.dirname(HERE)
 CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIBDIR, "libluna_b200.so")
-SOURCES = ["kernels.cu", "conv_kernels.cu", "tc_gemm.cu", "tc_conv.cu", "engine.cpp", "capi.cpp", "noalloc.cu"]
+SOURCES = ["kernels.cu", "conv_kernels.cu", "tc_gemm.cu", "tc_conv.cu", "engine.cpp", "capi.cpp", "noalloc.cu",
+           "shard.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -47,7 +48,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
         objs = list(ex.map(compile_one, SOURCES))
     tmp = LIB + ".tmp"
-    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"], check=True)
+    subprocess.run([NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart", "-ldl"], check=True)
     os.replace(tmp, LIB)
     for o in objs:
         os.remove(o)

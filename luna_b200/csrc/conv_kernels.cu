@@ -345,7 +345,7 @@ bool convT_rb_ok(const ConvStep& cs) {
 int convT_rb_chunks(const WinGeo& out) { return ceil_div(out.wh * out.ww, 256); }
 
 template <int CI>
-__global__ void __launch_bounds__(256) convT_relax_rb_kernel(const float* __restrict__ A, ConvStep cs, int M,
+__global__ void __launch_bounds__(256, CI <= 16 ? 3 : 2) convT_relax_rb_kernel(const float* __restrict__ A, ConvStep cs, int M,
                                                              ConvRelaxEpi e, int nchunk, float* __restrict__ partial) {
     extern __shared__ float4 rb_w4[];
     float* wsh = reinterpret_cast<float*>(rb_w4);
@@ -459,7 +459,7 @@ bool conv_adj_rb_ok(const ConvStep& cs) {
 }
 
 template <int CO>
-__global__ void __launch_bounds__(256) conv_adj_qbar_rb_kernel(const float* __restrict__ Pbar, ConvStep cs, int M,
+__global__ void __launch_bounds__(256, CO <= 16 ? 3 : 2) conv_adj_qbar_rb_kernel(const float* __restrict__ Pbar, ConvStep cs, int M,
                                                                const float* __restrict__ gseed,
                                                                const float* __restrict__ b, float* __restrict__ Qbar) {
     extern __shared__ float4 rb_w4[];

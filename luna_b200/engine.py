@@ -23,7 +23,9 @@ LIB_PATH = os.path.join(_HERE, "_lib", "libluna_b200.so")
 EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_compute_bounds", "lb200_compute_bounds_device",
            "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy",
-           "lb200_set_profiling", "lb200_set_contraction_path", "lb200_ibp_bounds_noalloc")
+           "lb200_set_profiling", "lb200_set_contraction_path", "lb200_ibp_bounds_noalloc",
+           "lb200_shard_range", "lb200_nccl_unique_id", "lb200_nccl_comm_create", "lb200_nccl_comm_destroy",
+           "lb200_shard_run")
 
 
 class EngineError(RuntimeError):
@@ -58,6 +60,13 @@ def load_library():
     lib.lb200_ibp_bounds_noalloc.argtypes = [vp, vp, vp, C.c_int64, vp, C.c_int64, C.c_int64, vp, vp, vp]
     lib.lb200_model_destroy.argtypes = [vp]
     lib.lb200_model_destroy.restype = None
+    u8p = C.POINTER(C.c_uint8)
+    lib.lb200_shard_range.argtypes = [C.c_int, C.c_int, C.c_int64, C.POINTER(C.c_int64), C.POINTER(C.c_int64)]
+    lib.lb200_nccl_unique_id.argtypes = [u8p]
+    lib.lb200_nccl_comm_create.argtypes = [u8p, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]
+    lib.lb200_nccl_comm_destroy.argtypes = [vp]
+    lib.lb200_shard_run.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, fp, fp, C.c_int64, fp, C.c_int64,
+                                    C.c_int64, fp, fp, C.c_int, C.POINTER(Stats)]
     _lib = lib
     return lib
 
@@ -67,6 +76,41 @@ def _check(rc: int, what: str):
         buf = C.create_string_buffer(4096)
         _lib.lb200_last_error(buf, len(buf))
         raise EngineError(f"{what}: {buf.value.decode(errors='replace')}")
+
+
+def shard_range(rank: int, world: int, n: int) -> tuple[int, int]:
+    """[begin, end) of n boxes for `rank` (lb200_shard_range)."""
+    load_library()
+    a, b = C.c_int64(), C.c_int64()
+    _check(_lib.lb200_shard_range(rank, world, n, C.byref(a), C.byref(b)), "lb200_shard_range")
+    return a.value, b.value
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh 128-byte NCCL unique id, to be shared with every rank."""
+    load_library()
+    buf = (C.c_uint8 * 128)()
+    _check(_lib.lb200_nccl_unique_id(buf), "lb200_nccl_unique_id")
+    return bytes(buf)
+
+
+class NcclComm:
+    """An NCCL communicator over `world` ranks made by the engine library
+    (lb200_nccl_comm_create); blocks until every rank has joined."""
+
+    def __init__(self, uid: bytes, rank: int, world: int, device: int):
+        load_library()
+        if len(uid) != 128:
+            raise ValueError("an NCCL unique id is 128 bytes")
+        buf = (C.c_uint8 * 128).from_buffer_copy(uid)
+        h = C.c_void_p()
+        _check(_lib.lb200_nccl_comm_create(buf, rank, world, device, C.byref(h)), "lb200_nccl_comm_create")
+        self.handle, self.rank, self.world = h, rank, world
+
+    def close(self):
+        if self.handle:
+            _check(_lib.lb200_nccl_comm_destroy(self.handle), "lb200_nccl_comm_destroy")
+            self.handle = None
 
 
 class Model:
@@ -108,6 +152,23 @@ class Model:
         _check(_lib.lb200_compute_bounds(self._h, method, fptr(xl), fptr(xu), B, fptr(Cm), Cm.shape[0],
                                          nspec, fptr(None), int(bound_lower), int(bound_upper),
                                          fptr(lb), fptr(ub), C.byref(st)), "lb200_compute_bounds")
+        self.last_stats = st
+        return lb, ub
+
+    def shard_run(self, comm: NcclComm, boxes, method: int, timeout_ms: int = 60000):
+        """Bound this rank's share of `boxes` and all-gather every rank's
+        bounds over `comm` (lb200_shard_run); returns (lb, ub) [B, nspec] for
+        the whole batch on every rank."""
+        xl = np.ascontiguousarray(boxes.lower, np.float32)
+        xu = np.ascontiguousarray(boxes.upper, np.float32)
+        Cm = np.ascontiguousarray(boxes.C, np.float32)
+        B, nspec = xl.shape[0], Cm.shape[1]
+        lb = np.empty((B, nspec), np.float32)
+        ub = np.empty((B, nspec), np.float32)
+        st = Stats()
+        _check(_lib.lb200_shard_run(self._h, comm.handle, comm.rank, comm.world, method, fptr(xl), fptr(xu), B,
+                                    fptr(Cm), Cm.shape[0], nspec, fptr(lb), fptr(ub), timeout_ms, C.byref(st)),
+               "lb200_shard_run")
         self.last_stats = st
         return lb, ub
 

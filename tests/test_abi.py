@@ -68,3 +68,18 @@ def test_struct_layout_matches_header(tmp_path):
         assert int(got[f"{st} size"]) == C.sizeof(cls), st
         for f, _ in cls._fields_:
             assert int(got[f"{st}.{f}"]) == getattr(cls, f).offset, (st, f)
+
+
+def test_shard_range_matches_the_host_sharding():
+    """lb200_shard_range (the native multi-GPU split) and luna_b200.shard agree,
+    cover every box once and differ in size by at most one."""
+    from luna_b200.engine import shard_range as native
+    from luna_b200.shard import shard_range as host
+    for n in (0, 1, 7, 512, 1000):
+        for world in (1, 2, 3, 8):
+            spans = [native(r, world, n) for r in range(world)]
+            assert spans == [host(r, world, n) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+            sizes = [b - a for a, b in spans]
+            assert max(sizes) - min(sizes) <= 1

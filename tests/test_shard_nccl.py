@@ -1,0 +1,70 @@
+"""Native multi-GPU sharding (lb200_shard_run over an NCCL communicator made
+by the engine library), on the GPU."""
+import multiprocessing as mp
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as G
+from luna_b200 import abi, workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def _case():
+    g, bx = W.small_cnn_case(2, n_boxes=7, big_first=False)
+    return g, bx, abi.default_options(alpha_lr=0.1, alpha_iterations=4)
+
+
+def test_single_rank_shard_run_matches_compute_bounds():
+    from luna_b200.build import build
+    from luna_b200.engine import Model, NcclComm, nccl_unique_id
+    build()
+    g, bx, opt = _case()
+    m = Model(g, device=0, options=opt)
+    ref = m.compute_bounds(bx, abi.METHOD_ALPHA_CROWN)
+    comm = NcclComm(nccl_unique_id(), 0, 1, 0)
+    try:
+        lb, ub = m.shard_run(comm, bx, abi.METHOD_ALPHA_CROWN, timeout_ms=30000)
+    finally:
+        comm.close()
+    assert np.array_equal(lb, ref[0]) and np.array_equal(ub, ref[1])
+
+
+def _rank(rank, world, uid, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from luna_b200.engine import Model, NcclComm
+    g, bx, opt = _case()
+    m = Model(g, device=rank, options=opt)
+    comm = NcclComm(uid, rank, world, rank)
+    try:
+        q.put((rank, m.shard_run(comm, bx, abi.METHOD_ALPHA_CROWN, timeout_ms=30000)))
+    finally:
+        comm.close()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_gather_every_box():
+    """Two processes, one GPU each: every rank ends with the bounds of every
+    box, equal to one GPU bounding the whole batch."""
+    from luna_b200.build import build
+    from luna_b200.engine import Model, nccl_unique_id
+    build()
+    g, bx, opt = _case()
+    ref = Model(g, device=0, options=opt).compute_bounds(bx, abi.METHOD_ALPHA_CROWN)
+    uid = nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, uid, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for r in range(2):
+        lb, ub = out[r]
+        assert G.excess_scaled(lb, ref[0], ref[0], ref[1]) <= 1.0
+        assert G.excess_scaled(ub, ref[1], ref[0], ref[1]) <= 1.0
