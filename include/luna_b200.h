@@ -252,6 +252,15 @@ LB200_API int lb200_shard_run(lb200_model* model, void* comm, int rank, int worl
                               const float* C, int64_t c_boxes, int64_t nspec,
                               float* out_lb, float* out_ub, int timeout_ms, lb200_stats* stats);
 
+/* Host only (no GPU is touched): check the graph as lb200_model_create does
+ * and describe the engine's plan for it as JSON -- every level (node, map
+ * shape, activation, main edge, skip edges) and every backward start (the
+ * concretisation form Luna's CPU path uses for it and the row window at each
+ * level below it).  *needed receives the length including the terminator;
+ * buf may be NULL to query it.  No counterpart in the reference. */
+LB200_API int lb200_describe_plan(const lb200_graph_desc* graph, const lb200_options* opt, char* buf, size_t len,
+                                  size_t* needed);
+
 /* Copy the last error message of this thread into buf (always terminated). */
 LB200_API int lb200_last_error(char* buf, size_t len);
 

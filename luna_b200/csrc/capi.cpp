@@ -143,6 +143,20 @@ int lb200_get_intermediate_bounds(lb200_model* model, float* lower, float* upper
     });
 }
 
+int lb200_describe_plan(const lb200_graph_desc* graph, const lb200_options* opt, char* buf, size_t len,
+                        size_t* needed) {
+    return guarded([&] {
+        lb200::Model m(graph, 0, /*on_device=*/false);
+        if (opt) m.set_options(*opt);
+        const std::string j = m.describe();
+        if (needed) *needed = j.size() + 1;
+        if (buf && len) {
+            std::strncpy(buf, j.c_str(), len - 1);
+            buf[len - 1] = '\0';
+        }
+    });
+}
+
 int lb200_last_error(char* buf, size_t len) {
     if (!buf || len == 0) return 1;
     std::strncpy(buf, g_last_error.c_str(), len - 1);

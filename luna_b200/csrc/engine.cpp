@@ -78,9 +78,9 @@ struct ValDesc {
 // (BoundedAddNode, two tensor operands), of skip edges from earlier levels
 // (the activation itself, or a conv of it); the output is a Linear of the
 // last level.  Flatten and Identity nodes pass through.
-Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
+Model::Model(const lb200_graph_desc* g, int device, bool on_device) : device_(device), on_device_(on_device) {
     if (!g || g->num_nodes <= 0 || !g->nodes) throw std::invalid_argument("empty graph");
-    LB_CUDA(cudaSetDevice(device_));
+    if (on_device_) LB_CUDA(cudaSetDevice(device_));
     const int n = g->num_nodes;
     std::vector<std::vector<int>> dependents(n);
     std::vector<int> indeg(n, 0);
@@ -275,14 +275,13 @@ Model::Model(const lb200_graph_desc* g, int device) : device_(device) {
             continue;
         }
         const int nc = L.conv ? L.out.C : L.n_out;
-        std::vector<float> b(nc), bs(nc), bn((size_t)L.n_out);
-        LB_CUDA(cudaMemcpy(b.data(), L.b, nc * 4, cudaMemcpyDeviceToHost));
+        std::vector<float> b(L.b_host), bn((size_t)L.n_out);
         for (const SkipEdge& s : skips_[m]) {
             if (!s.L) continue;
-            LB_CUDA(cudaMemcpy(bs.data(), s.L->b, nc * 4, cudaMemcpyDeviceToHost));
-            for (int c = 0; c < nc; ++c) b[c] += bs[c];
+            for (int c = 0; c < nc; ++c) b[c] += s.L->b_host[c];
         }
         for (int j = 0; j < L.n_out; ++j) bn[j] = b[j % nc];
+        if (!on_device_) continue;
         lvl_b_[m] = weights_.as<float>(key("lvlb", m), b.size());
         lvl_bn_[m] = weights_.as<float>(key("lvlbn", m), bn.size());
         LB_CUDA(cudaMemcpy(lvl_b_[m], b.data(), b.size() * 4, cudaMemcpyHostToDevice));
@@ -406,6 +405,8 @@ void Model::build_layer(Layer& L, const lb200_graph_desc* g, int node, int bn_no
             }
         bn = b;
     }
+    L.b_host = b;
+    if (!on_device_) return;
     L.W = weights_.as<float>(key("W", k), W.size());
     L.Wt = weights_.as<float>(key("Wt", k), Wt.size());
     L.b = weights_.as<float>(key("b", k), b.size());
@@ -740,6 +741,44 @@ int Model::start_form(int st) const {
     return patches[0] == 1 ? CONC_PATCHES : CONC_DENSE;
 }
 
+std::string Model::describe() const {
+    std::string j = "{\"levels\": [";
+    for (int m = 0; m <= K_; ++m) {
+        const MapShape& ms = map(m);
+        if (m) j += ", ";
+        j += "{\"level\": " + std::to_string(m);
+        j += ", \"node\": " + std::to_string(m == 0 ? -1 : (m < K_ ? preact_node_ids_[m - 1] : -2));
+        j += ", \"map\": [" + std::to_string(ms.C) + ", " + std::to_string(ms.H) + ", " + std::to_string(ms.W) + "]";
+        j += std::string(", \"act\": \"") + (act_[m] == ACT_RELU ? "relu" : act_[m] == ACT_SIGMOID ? "sigmoid" : "") + "\"";
+        if (m) {
+            const Layer& L = layers_[m - 1];
+            j += std::string(", \"edge\": \"") + (L.convt ? "convt" : L.conv ? "conv" : "linear") + "\"";
+            j += ", \"skips\": [";
+            for (size_t e = 0; e < skips_[m].size(); ++e) {
+                if (e) j += ", ";
+                j += "{\"src\": " + std::to_string(skips_[m][e].src) + ", \"conv\": " +
+                     (skips_[m][e].L ? "true" : "false") + "}";
+            }
+            j += "]";
+        }
+        j += "}";
+    }
+    j += "], \"starts\": [";
+    for (int st = 2; st <= K_; ++st) {
+        if (st > 2) j += ", ";
+        j += "{\"level\": " + std::to_string(st) + ", \"form\": \"" +
+             (start_form(st) == CONC_PATCHES ? "patches" : "dense") + "\", \"windows\": [";
+        for (int m = 0; m <= st; ++m) {
+            const WinGeo& g = geo_[st][m];
+            if (m) j += ", ";
+            j += "[" + std::to_string(g.wh) + ", " + std::to_string(g.ww) + ", " + std::to_string(g.mul_y) + ", " +
+                 std::to_string(g.off_y) + ", " + std::to_string(g.full) + "]";
+        }
+        j += "]}";
+    }
+    return j + "]}";
+}
+
 SkipStep Model::skip_step(int st, int m, int e) const {
     const SkipEdge& sk = skips_[m][e];
     const WinGeo& gi = geo_[st][m];
@@ -775,6 +814,7 @@ bool Model::skip_source(int st, int j, bool with_start) const {
 }
 
 Model::~Model() {
+    if (!on_device_) return;
     cudaSetDevice(device_);
     for (auto e : ev_pool_) cudaEventDestroy(e);
     cache_.release();

@@ -60,6 +60,7 @@ struct Layer {
     float* W = nullptr;
     float* Wt = nullptr;
     float* b = nullptr;        // [n_out] (Linear) or [Co] (conv)
+    std::vector<float> b_host; // the same bias on the host
     float* b_neuron = nullptr; // [n_out]: bias of every output neuron
     // tf32 (hi, lo) splits for the tensor-core path (Linear): W is the K-major
     // B operand of the adjoint contraction, Wt of the forward one.
@@ -96,7 +97,9 @@ struct StartPlan {
 
 class Model {
 public:
-    Model(const lb200_graph_desc* g, int device);
+    // on_device = false builds only the host-side plan (levels, row
+    // geometry, concretisation forms) for describe(); no GPU is touched.
+    Model(const lb200_graph_desc* g, int device, bool on_device = true);
     ~Model();
 
     void set_options(const lb200_options& o) { opt_ = o; }
@@ -108,6 +111,10 @@ public:
         tcconv_ = !on;
     }
     const lb200_options& options() const { return opt_; }
+    // The plan as JSON: every level (node, map, activation, main edge, skip
+    // edges) and every backward start (concretisation form and the row
+    // window at each level below it).
+    std::string describe() const;
 
     void compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes,
                  const float* d_C, int64_t c_boxes, int64_t nspec, const float* d_thr,
@@ -171,6 +178,7 @@ private:
     std::string key(const char* what, int a, int b = -1) const;
 
     int device_ = 0;
+    bool on_device_ = true;
     lb200_options opt_{};
     std::vector<Layer> layers_;        // main edge into level m = layers_[m - 1], m = 1..K
     std::vector<std::vector<SkipEdge>> skips_;  // [level] skip edges into its Add

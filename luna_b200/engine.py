@@ -25,7 +25,7 @@ EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy",
            "lb200_set_profiling", "lb200_set_contraction_path", "lb200_ibp_bounds_noalloc",
            "lb200_shard_range", "lb200_nccl_unique_id", "lb200_nccl_comm_create", "lb200_nccl_comm_destroy",
-           "lb200_shard_run")
+           "lb200_shard_run", "lb200_describe_plan")
 
 
 class EngineError(RuntimeError):
@@ -67,6 +67,8 @@ def load_library():
     lib.lb200_nccl_comm_destroy.argtypes = [vp]
     lib.lb200_shard_run.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, fp, fp, C.c_int64, fp, C.c_int64,
                                     C.c_int64, fp, fp, C.c_int, C.POINTER(Stats)]
+    lib.lb200_describe_plan.argtypes = [C.POINTER(GraphDesc), C.POINTER(Options), C.c_char_p, C.c_size_t,
+                                        C.POINTER(C.c_size_t)]
     _lib = lib
     return lib
 
@@ -76,6 +78,21 @@ def _check(rc: int, what: str):
         buf = C.create_string_buffer(4096)
         _lib.lb200_last_error(buf, len(buf))
         raise EngineError(f"{what}: {buf.value.decode(errors='replace')}")
+
+
+def describe_plan(graph, options: Options | None = None) -> dict:
+    """The engine's plan for `graph` (lb200_describe_plan, host only): levels
+    and, per backward start, its concretisation form and row windows."""
+    import json
+    load_library()
+    desc = graph.desc()
+    opt = options if options is not None else default_options()
+    need = C.c_size_t()
+    _check(_lib.lb200_describe_plan(C.byref(desc), C.byref(opt), None, 0, C.byref(need)), "lb200_describe_plan")
+    buf = C.create_string_buffer(need.value)
+    _check(_lib.lb200_describe_plan(C.byref(desc), C.byref(opt), buf, need.value, C.byref(need)),
+           "lb200_describe_plan")
+    return json.loads(buf.value.decode())
 
 
 def shard_range(rank: int, world: int, n: int) -> tuple[int, int]:
@@ -168,7 +185,7 @@ class Model:
         st = Stats()
         _check(_lib.lb200_shard_run(self._h, comm.handle, comm.rank, comm.world, method, fptr(xl), fptr(xu), B,
                                     fptr(Cm), Cm.shape[0], nspec, fptr(lb), fptr(ub), timeout_ms, C.byref(st)),
-               "lb200_shard_run")
+               "lb200_shard_run", "lb200_describe_plan")
         self.last_stats = st
         return lb, ub
 
