@@ -200,7 +200,8 @@ LB200_API int lb200_set_profiling(lb200_model* model, int on);
  * (for cross-checking).  Luna has no counterpart. */
 LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 
-/* IBP bounds of n_boxes boxes without allocating any device memory: the
+/* IBP bounds of n_boxes boxes without allocating any device memory, for
+ * Linear/ReLU networks (models with convs, Sigmoid or Add are rejected): the
  * same result as lb200_compute_bounds_device(..., LB200_METHOD_IBP, ...),
  * for callers that cannot call cudaMalloc where they need bounds (inside a
  * stream capture, or under a memory manager that owns every allocation).

@@ -127,6 +127,14 @@ public:
     int n_in() const { return layers_.front().n_in; }
     int n_out() const { return layers_.back().n_out; }
     const std::vector<Layer>& layers() const { return layers_; }
+    // Linear layers with ReLU between them and no joins (the networks the
+    // allocation-free IBP entry point takes).
+    bool is_relu_mlp() const {
+        if (has_conv_ || has_sigmoid_) return false;
+        for (const auto& sk : skips_)
+            if (!sk.empty()) return false;
+        return true;
+    }
     int64_t intermediate_count() const;
     void copy_intermediate(float* lower, float* upper) const;
 

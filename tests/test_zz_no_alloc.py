@@ -56,3 +56,15 @@ def test_no_alloc_rejects_batches_above_its_scratch():
     with pytest.raises(EngineError, match="scratch"):
         m.ibp_bounds_noalloc_ptr(xl.data_ptr(), xu.data_ptr(), too_many, Cm.data_ptr(), 1, 9,
                                  out.data_ptr(), out.data_ptr())
+
+
+def test_no_alloc_rejects_networks_other_than_linear_relu():
+    """A conv network is refused with an error (nothing is launched)."""
+    g, bx = W.small_cnn_case(1, n_boxes=2, big_first=False)
+    m = Model(g)
+    xl, xu, Cm = _device(bx)
+    n, nspec = bx.n, bx.C.shape[1]
+    out = torch.empty((n, nspec), device="cuda")
+    with pytest.raises(EngineError, match="Linear/ReLU"):
+        m.ibp_bounds_noalloc_ptr(xl.data_ptr(), xu.data_ptr(), n, Cm.data_ptr(), Cm.shape[0], nspec,
+                                 out.data_ptr(), out.data_ptr(), torch.cuda.current_stream().cuda_stream)
