@@ -1228,6 +1228,188 @@ void launch_convt_adj_qbar(const float* Pbar, const ConvTStep& ct, int M, float*
     LB_LAUNCH();
 }
 
+// ---- register-blocked transposed-conv layer steps ---------------------------
+constexpr int CT_BACK_CB = 16, CT_ADJ_CB = 8;
+
+bool convt_rb_ok(const ConvTStep& ct) {
+    return ct.Ci % CT_BACK_CB == 0 && ct.Co % 4 == 0 &&
+           (int64_t)ct.kh * ct.kw * ct.Co * CT_BACK_CB <= RB_MAX_W_FLOATS;
+}
+
+int convt_rb_chunks(const ConvTStep& ct) { return ceil_div(ct.Hi * ct.Wi, 256) * (ct.Ci / CT_BACK_CB); }
+
+__global__ void __launch_bounds__(256, 3) convt_back_relax_rb_kernel(const float* __restrict__ A, ConvTStep ct, int M,
+                                                                     ConvRelaxEpi e, int npc,
+                                                                     float* __restrict__ partial) {
+    extern __shared__ float4 rb_w4[];
+    float* wsh = reinterpret_cast<float*>(rb_w4);
+    __shared__ float red[8];
+    const int cg = blockIdx.y, c0 = cg * CT_BACK_CB;
+    const int taps = ct.kh * ct.kw;
+    // wsh[(tap Co + co) CB + cc] = W[c0 + cc, co, tap]
+    const int nwt = taps * ct.Co * CT_BACK_CB;
+    for (int i = threadIdx.x; i < nwt; i += blockDim.x) {
+        const int cc = i % CT_BACK_CB, rest = i / CT_BACK_CB;
+        const int co = rest % ct.Co, tap = rest / ct.Co;
+        wsh[i] = ct.Wg[((size_t)(c0 + cc) * taps + tap) * ct.Co + co];
+    }
+    __syncthreads();
+    const int r = (int)(blockIdx.x / npc), pc = (int)(blockIdx.x % npc);
+    const int npix = ct.Hi * ct.Wi;
+    const int pix = pc * 256 + threadIdx.x;
+    const int nw = npix * ct.Ci, nin = ct.Ho * ct.Wo * ct.Co;
+    int p, rr;
+    row_split(r, e.rows.R, p, rr);
+    const int bx = e.rows.row_box[rr];
+    float part = 0.f;
+    if (pix < npix) {
+        float acc[CT_BACK_CB];
+#pragma unroll
+        for (int c = 0; c < CT_BACK_CB; ++c) acc[c] = 0.f;
+        const int qy = pix / ct.Wi, qx = pix - (pix / ct.Wi) * ct.Wi;
+        const float* Arow = A + (size_t)r * nin;
+        for (int ky = 0; ky < ct.kh; ++ky) {
+            const int vy = qy * ct.sh - ct.ph + ky;
+            if (vy < 0 || vy >= ct.Ho) continue;
+            for (int kx = 0; kx < ct.kw; ++kx) {
+                const int vx = qx * ct.sw - ct.pw + kx;
+                if (vx < 0 || vx >= ct.Wo) continue;
+                const float4* a4 = reinterpret_cast<const float4*>(Arow + ((size_t)vy * ct.Wo + vx) * ct.Co);
+                const float* w = wsh + (size_t)(ky * ct.kw + kx) * ct.Co * CT_BACK_CB;
+                for (int c4 = 0; c4 < ct.Co / 4; ++c4) {
+                    const float4 a = __ldg(a4 + c4);
+                    const float av[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                    for (int t = 0; t < 4; ++t) {
+                        const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(c4 * 4 + t) * CT_BACK_CB);
+#pragma unroll
+                        for (int c = 0; c < CT_BACK_CB / 4; ++c) {
+                            const float4 wv = wr[c];
+                            acc[4 * c + 0] = fmaf(av[t], wv.x, acc[4 * c + 0]);
+                            acc[4 * c + 1] = fmaf(av[t], wv.y, acc[4 * c + 1]);
+                            acc[4 * c + 2] = fmaf(av[t], wv.z, acc[4 * c + 2]);
+                            acc[4 * c + 3] = fmaf(av[t], wv.w, acc[4 * c + 3]);
+                        }
+                    }
+                }
+            }
+        }
+        const size_t at0 = (size_t)r * nw + (size_t)pix * ct.Ci + c0;
+        const size_t bj0 = (size_t)bx * e.rp.n + (size_t)pix * ct.Ci + c0;
+#pragma unroll
+        for (int c = 0; c < CT_BACK_CB; c += 4) {
+            const float Pv[4] = {acc[c], acc[c + 1], acc[c + 2], acc[c + 3]};
+            if (e.P_save) *reinterpret_cast<float4*>(e.P_save + at0 + c) = make_float4(Pv[0], Pv[1], Pv[2], Pv[3]);
+            const float4 s4 = *reinterpret_cast<const float4*>(e.rp.slope_lo + bj0 + c);
+            const float4 k4 = *reinterpret_cast<const float4*>(e.rp.k_up + bj0 + c);
+            const float4 b4 = *reinterpret_cast<const float4*>(e.rp.b_up + bj0 + c);
+            const uchar4 f4 = *reinterpret_cast<const uchar4*>(e.rp.flags + bj0 + c);
+            float4 a4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (e.alpha && ((f4.x | f4.y | f4.z | f4.w) & RF_USE_ALPHA))
+                a4 = *reinterpret_cast<const float4*>(e.alpha + at0 + c);
+            const float Av[4] = {a4.x, a4.y, a4.z, a4.w};
+            const float sl[4] = {s4.x, s4.y, s4.z, s4.w}, ku[4] = {k4.x, k4.y, k4.z, k4.w},
+                        bu[4] = {b4.x, b4.y, b4.z, b4.w};
+            const uint8_t fl[4] = {f4.x, f4.y, f4.z, f4.w};
+            float Qv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float sv = (e.alpha && (fl[i] & RF_USE_ALPHA)) ? Av[i] : sl[i];
+                Qv[i] = relax_q(Pv[i], p, sv, ku[i], bu[i], part);
+                if (e.b_next) part = fmaf(Qv[i], e.b_next[c0 + c + i], part);
+            }
+            *reinterpret_cast<float4*>(e.Q + at0 + c) = make_float4(Qv[0], Qv[1], Qv[2], Qv[3]);
+        }
+    }
+    const float tot = block_sum256(part, red);
+    if (threadIdx.x == 0) partial[(size_t)(cg * npc + pc) * M + r] = tot;
+}
+
+void launch_convt_back_relax_rb(const float* A, const ConvTStep& ct, int M, const ConvRelaxEpi& e, float* partial,
+                                cudaStream_t s) {
+    if (M == 0) return;
+    if (!e.g.full || !convt_rb_ok(ct)) throw std::invalid_argument("convt_back_relax_rb: unsupported step");
+    const int npc = ceil_div(ct.Hi * ct.Wi, 256);
+    const size_t smem = (size_t)ct.kh * ct.kw * ct.Co * CT_BACK_CB * 4;
+    const dim3 grid((unsigned)((int64_t)M * npc), (unsigned)(ct.Ci / CT_BACK_CB));
+    convt_back_relax_rb_kernel<<<grid, 256, smem, s>>>(A, ct, M, e, npc, partial);
+    LB_LAUNCH();
+}
+
+bool convt_adj_rb_ok(const ConvTStep& ct) {
+    return ct.Co % CT_ADJ_CB == 0 && ct.Ci % 4 == 0 &&
+           (int64_t)ct.kh * ct.kw * ct.Ci * CT_ADJ_CB <= RB_MAX_W_FLOATS;
+}
+
+__global__ void __launch_bounds__(256, 3) convt_adj_qbar_rb_kernel(const float* __restrict__ Pbar, ConvTStep ct, int M,
+                                                                   float* __restrict__ Qbar) {
+    extern __shared__ float4 rb_w4[];
+    float* wsh = reinterpret_cast<float*>(rb_w4);
+    const int c0 = blockIdx.y * CT_ADJ_CB;
+    const int taps = ct.kh * ct.kw;
+    // wsh[(tap Ci + ci) CB + cc] = Wa[tap][c0 + cc][ci]
+    const int nwt = taps * ct.Ci * CT_ADJ_CB;
+    for (int i = threadIdx.x; i < nwt; i += blockDim.x) {
+        const int cc = i % CT_ADJ_CB, rest = i / CT_ADJ_CB;
+        const int ci = rest % ct.Ci, tap = rest / ct.Ci;
+        wsh[i] = ct.Wa[((size_t)tap * ct.Co + c0 + cc) * ct.Ci + ci];
+    }
+    __syncthreads();
+    const int npix = ct.Ho * ct.Wo;
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)M * npix) return;
+    const int r = (int)(idx / npix), pix = (int)(idx - (int64_t)r * npix);
+    const int vy = pix / ct.Wo, vx = pix - (pix / ct.Wo) * ct.Wo;
+    const float* prow = Pbar + (size_t)r * ct.Hi * ct.Wi * ct.Ci;
+    float acc[CT_ADJ_CB];
+#pragma unroll
+    for (int c = 0; c < CT_ADJ_CB; ++c) acc[c] = 0.f;
+    for (int ky = 0; ky < ct.kh; ++ky) {
+        const int ty = vy + ct.ph - ky;
+        if (ty < 0 || ty % ct.sh) continue;
+        const int qy = ty / ct.sh;
+        if (qy >= ct.Hi) continue;
+        for (int kx = 0; kx < ct.kw; ++kx) {
+            const int tx = vx + ct.pw - kx;
+            if (tx < 0 || tx % ct.sw) continue;
+            const int qx = tx / ct.sw;
+            if (qx >= ct.Wi) continue;
+            const float4* p4 = reinterpret_cast<const float4*>(prow + ((size_t)qy * ct.Wi + qx) * ct.Ci);
+            const float* w = wsh + (size_t)(ky * ct.kw + kx) * ct.Ci * CT_ADJ_CB;
+            for (int c4 = 0; c4 < ct.Ci / 4; ++c4) {
+                const float4 pv = __ldg(p4 + c4);
+                const float pa[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                    const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(c4 * 4 + t) * CT_ADJ_CB);
+#pragma unroll
+                    for (int c = 0; c < CT_ADJ_CB / 4; ++c) {
+                        const float4 wv = wr[c];
+                        acc[4 * c + 0] = fmaf(pa[t], wv.x, acc[4 * c + 0]);
+                        acc[4 * c + 1] = fmaf(pa[t], wv.y, acc[4 * c + 1]);
+                        acc[4 * c + 2] = fmaf(pa[t], wv.z, acc[4 * c + 2]);
+                        acc[4 * c + 3] = fmaf(pa[t], wv.w, acc[4 * c + 3]);
+                    }
+                }
+            }
+        }
+    }
+    float* out = Qbar + ((size_t)r * npix + pix) * ct.Co + c0;
+#pragma unroll
+    for (int c = 0; c < CT_ADJ_CB; c += 4)
+        *reinterpret_cast<float4*>(out + c) = make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+}
+
+void launch_convt_adj_qbar_rb(const float* Pbar, const ConvTStep& ct, int M, float* Qbar, cudaStream_t s) {
+    const int64_t total = (int64_t)M * ct.Ho * ct.Wo;
+    if (total == 0) return;
+    if (!convt_adj_rb_ok(ct)) throw std::invalid_argument("convt_adj_qbar_rb: unsupported step");
+    const size_t smem = (size_t)ct.kh * ct.kw * ct.Ci * CT_ADJ_CB * 4;
+    const dim3 grid((unsigned)ceil_div(total, 256), (unsigned)(ct.Co / CT_ADJ_CB));
+    convt_adj_qbar_rb_kernel<<<grid, 256, smem, s>>>(Pbar, ct, M, Qbar);
+    LB_LAUNCH();
+}
+
 // ============================================================== skip edges
 __global__ void skip_back_kernel(SkipStep k, RowMap rows, int M, const float* __restrict__ Q,
                                  float* __restrict__ S) {

@@ -191,6 +191,16 @@ void launch_ibp_convt(const ConvTStep& ct, const float* b, const float* in_l, co
 // below in the epilogue (whole maps; chunk partials as launch_convT_relax).
 void launch_convt_back_relax(const float* A, const ConvTStep& ct, int M, const ConvRelaxEpi& e, float* partial,
                              cudaStream_t s);
+// Register-blocked forms of the two steps (whole maps; the same per-element
+// summation order): one thread per pixel and 16 (back-substitution) or 8
+// (adjoint) channels, the weights of that channel group in shared memory.
+// The back-substitution writes convt_rb_chunks() partials per row.
+bool convt_rb_ok(const ConvTStep& ct);
+int convt_rb_chunks(const ConvTStep& ct);
+void launch_convt_back_relax_rb(const float* A, const ConvTStep& ct, int M, const ConvRelaxEpi& e, float* partial,
+                                cudaStream_t s);
+bool convt_adj_rb_ok(const ConvTStep& ct);
+void launch_convt_adj_qbar_rb(const float* Pbar, const ConvTStep& ct, int M, float* Qbar, cudaStream_t s);
 // Start step of a ConvTranspose start: the one-hot row at output neuron
 // (v0, co0) through the layer is W[:, co0, k] at the q with q s - p + k = v0;
 // the layer's bias does not enter (flat A, see launch_convt_back_relax).

@@ -955,7 +955,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     int slots_total = 0;
     for (int m = mb; m >= 1; --m) {
         if (layers_[m - 1].convt)
-            slots_total += conv_chunks(sp.geo[m - 1]);
+            slots_total += convt_rb_ok(convt_step(m)) ? convt_rb_chunks(convt_step(m)) : conv_chunks(sp.geo[m - 1]);
         else if (!layers_[m - 1].conv)
             slots_total += gemm_tiles_n(width(m - 1));
         else if (m == 1 && first_conv_fast(conv_step(st, 1)))
@@ -1062,9 +1062,14 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.P_save = psave_buf(m - 1);
             e.Q = Q[1 - cur];
             prof_begin(s);
-            launch_convt_back_relax(Q[cur], ct, M, e, part + (size_t)slot * M, s);
+            if (convt_rb_ok(ct)) {
+                launch_convt_back_relax_rb(Q[cur], ct, M, e, part + (size_t)slot * M, s);
+                slot += convt_rb_chunks(ct);
+            } else {
+                launch_convt_back_relax(Q[cur], ct, M, e, part + (size_t)slot * M, s);
+                slot += conv_chunks(sp.geo[m - 1]);
+            }
             prof_end(s, fl);
-            slot += conv_chunks(sp.geo[m - 1]);
             cur = 1 - cur;
             continue;
         }
@@ -1354,7 +1359,10 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             flops_ += fl;
             float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
             prof_begin(s);
-            launch_convt_adj_qbar(pin, ct, M, Qbar, s);
+            if (convt_adj_rb_ok(ct))
+                launch_convt_adj_qbar_rb(pin, ct, M, Qbar, s);
+            else
+                launch_convt_adj_qbar(pin, ct, M, Qbar, s);
             prof_end(s, fl);
             launch_relax_adjoint(e, Qbar, M, N, s);
             pin = pout;

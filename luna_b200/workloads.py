@@ -261,11 +261,16 @@ def small_cnn_bn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, big_first:
     return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 5)
 
 
-def convt_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 10, conv_after: bool = False):
+def convt_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 10, conv_after: bool = False,
+                   wide: bool = False):
     """Small CNN with a strided transposed conv (conv -> conv s2 -> convT s2
-    [-> conv] -> linear head) for parity tests."""
+    [-> conv] -> linear head) for parity tests; with wide the transposed conv
+    maps 16 to 8 channels (the register-blocked kernels' shapes)."""
     rng = np.random.Generator(np.random.PCG64(seed))
-    layers = [("conv", 6, 3, 1, 1), ("conv", 8, 4, 2, 1), ("convT", 5, 4, 2, 1)]
+    if wide:
+        layers = [("conv", 8, 3, 1, 1), ("conv", 16, 4, 2, 1), ("convT", 8, 4, 2, 1)]
+    else:
+        layers = [("conv", 6, 3, 1, 1), ("conv", 8, 4, 2, 1), ("convT", 5, 4, 2, 1)]
     if conv_after:
         layers.append(("conv", 4, 3, 1, 1))
     g = cnn((3, hw, hw), layers + [("linear", 12), ("linear", 4)], seed + 9, bias_std=0.1)

@@ -226,16 +226,17 @@ def test_cnn_cifar_sound_and_ordered(method):
         assert (y.max(0).values.cpu().numpy() <= ub[b] + tol[b]).all()
 
 
-@pytest.mark.parametrize("conv_after", [False, True])
+@pytest.mark.parametrize("conv_after,wide", [(False, False), (True, False), (False, True), (True, True)])
 @pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
-def test_convt_matches_oracle(method, conv_after):
-    """Strided transposed conv below a linear head / below another conv."""
+def test_convt_matches_oracle(method, conv_after, wide):
+    """Strided transposed conv below a linear head / below another conv; wide
+    takes the register-blocked transposed-conv kernels."""
     from oracle.lirpa_oracle import LirpaOracle
-    g, bx = W.convt_cnn_case(31, n_boxes=3, conv_after=conv_after)
+    g, bx = W.convt_cnn_case(31, n_boxes=3, conv_after=conv_after, wide=wide)
     opt = abi.default_options(alpha_lr=0.1, alpha_iterations=6)
     lb, ub = Model(g, options=opt).compute_bounds(bx, method)
     olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
-    _assert_parity(f"convT/{method}/{int(conv_after)}", lb, ub, olb, oub)
+    _assert_parity(f"convT/{method}/{int(conv_after)}/{int(wide)}", lb, ub, olb, oub)
 
 
 def test_cnn_convt_cifar_sound():
