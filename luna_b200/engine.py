@@ -185,7 +185,7 @@ class Model:
         st = Stats()
         _check(_lib.lb200_shard_run(self._h, comm.handle, comm.rank, comm.world, method, fptr(xl), fptr(xu), B,
                                     fptr(Cm), Cm.shape[0], nspec, fptr(lb), fptr(ub), timeout_ms, C.byref(st)),
-               "lb200_shard_run", "lb200_describe_plan")
+               "lb200_shard_run")
         self.last_stats = st
         return lb, ub
 
