@@ -670,12 +670,15 @@ __global__ void __launch_bounds__(256) relax_adjoint_kernel(EpiRelaxAdj e, const
 
 // Vectorised variant (n % 4 == 0): one CTA per (box, 128 columns); 256
 // threads = 32 column lanes of 4 columns x 8 row lanes; float4 traffic.
+// CT column threads x (256 / CT) row lanes per block, 4 columns per thread.
+template <int CT>
 __global__ void __launch_bounds__(256, 3) relax_adjoint_v4_kernel(EpiRelaxAdj e, const float* __restrict__ Qbar,
                                                                int M, int n) {
+    constexpr int RL = 256 / CT;
     const int bx = blockIdx.x;
-    const int c = blockIdx.y * 128 + (threadIdx.x & 31) * 4;
-    const int ty = threadIdx.x >> 5;
-    __shared__ float4 sk[8][32], sb[8][32];
+    const int c = blockIdx.y * (4 * CT) + (threadIdx.x % CT) * 4;
+    const int ty = threadIdx.x / CT;
+    __shared__ float4 sk[RL][CT], sb[RL][CT];
     float ks[4] = {0.f, 0.f, 0.f, 0.f}, bs[4] = {0.f, 0.f, 0.f, 0.f};
     const float* __restrict__ Ps = e.P_saved;
     const float* __restrict__ Gw = e.gather_W;
@@ -707,7 +710,7 @@ __global__ void __launch_bounds__(256, 3) relax_adjoint_v4_kernel(EpiRelaxAdj e,
             const int first = p * e.rows.R + e.rows.box_off[bx];
             const int last = min(p * e.rows.R + e.rows.box_off[bx + 1], M);
 #pragma unroll 2
-            for (int r = first + ty; r < last; r += 8) {
+            for (int r = first + ty; r < last; r += RL) {
                 const size_t at = (size_t)r * n + c;
                 const float4 q4 = *reinterpret_cast<const float4*>(Qbar + at);
                 const float4 p4 = Gw ? *reinterpret_cast<const float4*>(Gw + (size_t)e.rows.row_id[r - p * e.rows.R] * n + c)
@@ -760,12 +763,12 @@ __global__ void __launch_bounds__(256, 3) relax_adjoint_v4_kernel(EpiRelaxAdj e,
             }
         }
     }
-    sk[ty][threadIdx.x & 31] = make_float4(ks[0], ks[1], ks[2], ks[3]);
-    sb[ty][threadIdx.x & 31] = make_float4(bs[0], bs[1], bs[2], bs[3]);
+    sk[ty][threadIdx.x % CT] = make_float4(ks[0], ks[1], ks[2], ks[3]);
+    sb[ty][threadIdx.x % CT] = make_float4(bs[0], bs[1], bs[2], bs[3]);
     __syncthreads();
     if (ty == 0 && c < n) {
         float4 kt = make_float4(0.f, 0.f, 0.f, 0.f), bt = kt;
-        for (int q = 0; q < 8; ++q) {
+        for (int q = 0; q < RL; ++q) {
             const float4 a = sk[q][threadIdx.x], b = sb[q][threadIdx.x];
             kt.x += a.x; kt.y += a.y; kt.z += a.z; kt.w += a.w;
             bt.x += b.x; bt.y += b.y; bt.z += b.z; bt.w += b.w;
@@ -783,8 +786,10 @@ __global__ void __launch_bounds__(256, 3) relax_adjoint_v4_kernel(EpiRelaxAdj e,
 void launch_relax_adjoint(const EpiRelaxAdj& e, const float* Qbar, int M, int n, cudaStream_t s) {
     if (M == 0 || e.B == 0) return;
     if (n % 4 == 0) {
-        dim3 grid(e.B, ceil_div(n, 128));
-        relax_adjoint_v4_kernel<<<grid, 256, 0, s>>>(e, Qbar, M, n);
+        // 64 columns per block: twice the blocks of 128-column ones, so the
+        // boxes' uneven row counts leave a shorter tail.
+        dim3 grid(e.B, ceil_div(n, 64));
+        relax_adjoint_v4_kernel<16><<<grid, 256, 0, s>>>(e, Qbar, M, n);
     } else {
         dim3 grid(e.B, ceil_div(n, 32));
         relax_adjoint_kernel<<<grid, 256, 0, s>>>(e, Qbar, M, n);
