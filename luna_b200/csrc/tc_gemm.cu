@@ -141,17 +141,36 @@ __device__ __forceinline__ void epi_conc(const EpiConcretize& e, int r, int c, i
 // d loss / d A at the input for one row and 32 columns [k0, k0 + 32) of the
 // first adjoint contraction, from the concretisation signs (the value
 // launch_adj_input_seed writes): g x_a where A >= 0, g x_b where A <= 0.
-__device__ __forceinline__ void seed_row(const EpiStoreQbar& e, int r, int M, int K, int k0, float (&v)[32]) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = 0.f;
-    if (r >= M) return;
+// Per-row inputs of the seed: the row's sign bytes and its box's input
+// bounds in the order the row's side uses them, and its bias adjoint g.
+struct SeedRow {
+    const uint8_t* sg = nullptr;
+    const float* xa = nullptr;
+    const float* xb = nullptr;
+    float g = 0.f;
+};
+
+__device__ __forceinline__ SeedRow seed_row_info(const EpiStoreQbar& e, int r, int M, int K) {
+    SeedRow s;
+    if (r >= M) return s;
     int p, rr;
     split_row2(r, e.rows.R, p, rr);
     const int bx = e.rows.row_box[rr];
-    const float g = e.gseed[r];
-    const float* xa = (p == 0 ? e.seed_xl : e.seed_xu) + (size_t)bx * K;
-    const float* xb = (p == 0 ? e.seed_xu : e.seed_xl) + (size_t)bx * K;
-    const uint8_t* sg = e.seed_sign + (size_t)r * K;
+    s.g = e.gseed[r];
+    s.xa = (p == 0 ? e.seed_xl : e.seed_xu) + (size_t)bx * K;
+    s.xb = (p == 0 ? e.seed_xu : e.seed_xl) + (size_t)bx * K;
+    s.sg = e.seed_sign + (size_t)r * K;
+    return s;
+}
+
+__device__ __forceinline__ void seed_row(const SeedRow& sr, int K, int k0, float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    if (!sr.sg) return;
+    const float g = sr.g;
+    const float* xa = sr.xa;
+    const float* xb = sr.xb;
+    const uint8_t* sg = sr.sg;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int c = k0 + 4 * j;
@@ -310,6 +329,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
             bool ok = true;
             const int mb_t = t / tiles_n, nb_t = t % tiles_n;
+            SeedRow seed;
+            if constexpr (AMODE == AMODE_SEED) seed = seed_row_info(ep.q, mb_t * TC_BM + xt, M, K);
             if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
                 const int r = mb_t * TC_BM + xt;
                 rok = r < M;
@@ -326,6 +347,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % S;
                 const uint32_t ph = (g / S) & 1;
+                // The seed reads only global memory: issue its loads before
+                // waiting for the stage, so their latency overlaps the wait.
+                float v[32];
+                if constexpr (AMODE == AMODE_SEED) seed_row(seed, K, kb * TC_BK, v);
                 if (!mbar_wait(&full[s], ph, abort, &g_tc_error)) { ok = false; break; }
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
@@ -393,9 +418,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     // Generate row xt of the tile and store it in the
                     // 128-byte swizzled layout TMA would have produced:
                     // 16-byte chunk j of row r sits at chunk j ^ (r % 8).
-                    float v[32];
-                    const int mb = t / tiles_n;
-                    seed_row(ep.q, mb * TC_BM + xt, M, K, kb * TC_BK, v);
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
                         float4 h, l;
