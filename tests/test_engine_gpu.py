@@ -10,6 +10,11 @@ from luna_b200.engine import Model
 
 pytestmark = pytest.mark.gpu
 
+# The sampled network outputs the bounds are checked against are computed
+# with torch on the GPU: in full fp32, not with TF32 convolutions / matmuls.
+torch.backends.cudnn.allow_tf32 = False
+torch.backends.cuda.matmul.allow_tf32 = False
+
 
 @pytest.fixture(scope="module", autouse=True)
 def _built():
@@ -301,3 +306,33 @@ def test_sigmoid_matches_oracle(method, case):
     lb, ub = Model(g, options=opt).compute_bounds(bx, method)
     olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
     _assert_parity(f"{case}/{method}", lb, ub, olb, oub)
+
+
+@pytest.mark.parametrize("method", [abi.METHOD_IBP, abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_batch_edge_cases(method):
+    """Empty batch; a batch of one; zero-width boxes (points) and boxes with
+    some zero-width pixels in a CNN; one shared specification matrix against
+    one per box; splitting a batch does not change a box's bounds beyond the
+    parity bar."""
+    from oracle.lirpa_oracle import LirpaOracle
+    g, bx = W.small_cnn_case(11, n_boxes=5, big_first=False)
+    bx.upper[0] = bx.lower[0]                  # a point
+    bx.upper[1, ::3] = bx.lower[1, ::3]        # some pixels fixed
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=4)
+    m = Model(g, options=opt)
+    lb0, ub0 = m.compute_bounds(bx.slice(0, 0), method)
+    assert lb0.shape == (0, bx.C.shape[1]) and ub0.shape == (0, bx.C.shape[1])
+    lb, ub = m.compute_bounds(bx, method)
+    olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
+    _assert_parity(f"edge/{method}", lb, ub, olb, oub)
+    # A point box: lower and upper bounds meet at the network's value.
+    y = W.graph_forward(g, torch.from_numpy(bx.lower[:1])).detach().numpy()[0] @ bx.C[0].T
+    assert np.allclose(lb[0], y, atol=1e-4, rtol=1e-4) and np.allclose(ub[0], y, atol=1e-4, rtol=1e-4)
+    # Batch of one, and the same boxes with a per-box copy of C.
+    l1, u1 = m.compute_bounds(bx.slice(2, 3), method)
+    _assert_parity(f"edge1/{method}", l1, u1, lb[2:3], ub[2:3])
+    shared = W.Boxes(bx.lower, bx.upper, np.ascontiguousarray(bx.C[:1]))
+    per_box = W.Boxes(bx.lower, bx.upper, np.repeat(bx.C[:1], bx.n, 0))
+    ls, us = m.compute_bounds(shared, method)
+    lp, up = m.compute_bounds(per_box, method)
+    _assert_parity(f"edgeC/{method}", ls, us, lp, up)
