@@ -822,12 +822,6 @@ void launch_relax_adjoint_win(const EpiRelaxAdj& e, const WinGeo& g, const float
 // ============================================================== first conv layer
 namespace {
 constexpr int FK = 3, FC = 3;  // kernel 3x3 over 3 input channels, stride 1
-
-__device__ __forceinline__ float warp_allsum(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
 }  // namespace
 
 // Shared seed window of the first-conv adjoint: a zero halo of FK rows /
