@@ -163,32 +163,52 @@ __device__ __forceinline__ SeedRow seed_row_info(const EpiStoreQbar& e, int r, i
     return s;
 }
 
-__device__ __forceinline__ void seed_row(const SeedRow& sr, int K, int k0, float (&v)[32]) {
+// The 32 sign bytes of one row and K block [k0, k0 + 32): two 16-byte loads
+// (zero past K) when rows are 16-byte aligned (K % 16 == 0), else bytewise.
+__device__ __forceinline__ void seed_signs(const SeedRow& sr, int K, int k0, uint4 (&sg)[2]) {
+    sg[0] = sg[1] = make_uint4(0u, 0u, 0u, 0u);
+    if (!sr.sg) return;
+    if ((K & 15) == 0) {
+        if (k0 < K) sg[0] = *reinterpret_cast<const uint4*>(sr.sg + k0);
+        if (k0 + 16 < K) sg[1] = *reinterpret_cast<const uint4*>(sr.sg + k0 + 16);
+        return;
+    }
+    uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
+    for (int i = 0; i < 32 && k0 + i < K; ++i) w[i >> 2] |= (uint32_t)sr.sg[k0 + i] << (8 * (i & 3));
+    sg[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    sg[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__device__ __forceinline__ uint32_t sign_word(const uint4 (&sg)[2], int w) {
+    const uint4 q = sg[w >> 2];
+    return (w & 3) == 0 ? q.x : (w & 3) == 1 ? q.y : (w & 3) == 2 ? q.z : q.w;
+}
+
+// d loss / d A of one row for K block [k0, k0 + 32) from its sign bytes.
+__device__ __forceinline__ void seed_row(const SeedRow& sr, int K, int k0, const uint4 (&sg)[2], float (&v)[32]) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = 0.f;
     if (!sr.sg) return;
     const float g = sr.g;
-    const float* xa = sr.xa;
-    const float* xb = sr.xb;
-    const uint8_t* sg = sr.sg;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const int c = k0 + 4 * j;
+        const uint32_t sw = sign_word(sg, j);
         if (c + 3 < K) {
-            const uchar4 s4 = *reinterpret_cast<const uchar4*>(sg + c);
-            const float4 a4 = *reinterpret_cast<const float4*>(xa + c);
-            const float4 b4 = *reinterpret_cast<const float4*>(xb + c);
-            const uint8_t s[4] = {s4.x, s4.y, s4.z, s4.w};
+            const float4 a4 = *reinterpret_cast<const float4*>(sr.xa + c);
+            const float4 b4 = *reinterpret_cast<const float4*>(sr.xb + c);
             const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                v[4 * j + q] = ((s[q] & 1) ? g * a[q] : 0.f) + ((s[q] & 2) ? g * b[q] : 0.f);
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t s = sw >> (8 * q);
+                v[4 * j + q] = ((s & 1) ? g * a[q] : 0.f) + ((s & 2) ? g * b[q] : 0.f);
+            }
         } else {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 if (c + q < K) {
-                    const uint8_t s = sg[c + q];
-                    v[4 * j + q] = ((s & 1) ? g * xa[c + q] : 0.f) + ((s & 2) ? g * xb[c + q] : 0.f);
+                    const uint32_t s = sw >> (8 * q);
+                    v[4 * j + q] = ((s & 1) ? g * sr.xa[c + q] : 0.f) + ((s & 2) ? g * sr.xb[c + q] : 0.f);
                 }
             }
         }
@@ -330,7 +350,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             bool ok = true;
             const int mb_t = t / tiles_n, nb_t = t % tiles_n;
             SeedRow seed;
-            if constexpr (AMODE == AMODE_SEED) seed = seed_row_info(ep.q, mb_t * TC_BM + xt, M, K);
+            uint4 sg_next[2];  // sign bytes of the next K block, loaded one block ahead
+            if constexpr (AMODE == AMODE_SEED) {
+                seed = seed_row_info(ep.q, mb_t * TC_BM + xt, M, K);
+                seed_signs(seed, K, 0, sg_next);
+            }
             if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
                 const int r = mb_t * TC_BM + xt;
                 rok = r < M;
@@ -350,7 +374,19 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 // The seed reads only global memory: issue its loads before
                 // waiting for the stage, so their latency overlaps the wait.
                 float v[32];
-                if constexpr (AMODE == AMODE_SEED) seed_row(seed, K, kb * TC_BK, v);
+                if constexpr (AMODE == AMODE_SEED) {
+                    const uint4 sg_cur[2] = {sg_next[0], sg_next[1]};
+                    if (kb + 1 < nk) {
+                        seed_signs(seed, K, (kb + 1) * TC_BK, sg_next);
+                        // The next block's input bounds (one 128-byte line each) into L1.
+                        const int kn = (kb + 1) * TC_BK;
+                        if (seed.sg && kn < K) {
+                            asm volatile("prefetch.global.L1 [%0];" ::"l"(seed.xa + kn));
+                            asm volatile("prefetch.global.L1 [%0];" ::"l"(seed.xb + kn));
+                        }
+                    }
+                    seed_row(seed, K, kb * TC_BK, sg_cur, v);
+                }
                 if (!mbar_wait(&full[s], ph, abort, &g_tc_error)) { ok = false; break; }
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
