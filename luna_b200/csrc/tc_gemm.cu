@@ -391,6 +391,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
                 if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
+                    // The next block's relaxation parameters (and gathered
+                    // weight row) into L1 while this one is formed.
+                    const int kn = (kb + 1) * TC_BK;
+                    if (rok && kn < K) {
+                        const size_t bn = (size_t)rbox * pro.rp.n + kn;
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(pro.rp.slope_lo + bn));
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(pro.rp.k_up + bn));
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(pro.rp.b_up + bn));
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(pro.rp.flags + bn));
+                        if (AMODE == AMODE_GATHER)
+                            asm volatile("prefetch.global.L1 [%0];" ::"l"(pro.gather_W + (size_t)rid * K + kn));
+                    }
                     // Logical chunk j of row xt sits at swizzled slot j ^ (xt % 8).
 #pragma unroll 2
                     for (int j = 0; j < 8; ++j) {
