@@ -165,11 +165,13 @@ LB200_API int lb200_set_options(lb200_model* model, const lb200_options* opt);
  *   x_lower, x_upper : [n_boxes, n_in] host, the flat input box per box
  *   C                : [c_boxes, nspec, n_out] host; c_boxes is 1 (shared)
  *                      or n_boxes (one specification per box)
- *   thresholds       : [nspec] host or NULL.  With thresholds, a box whose
- *                      lower bounds exceed any threshold counts as verified
- *                      (TorchModel::isSpecVerified, TorchModel.cpp:616-651)
- *                      and the STOP_*_ON_VERIFIED options apply; without
- *                      them nothing is ever verified, as in Luna after
+ *   thresholds       : [nspec] host or NULL.  With thresholds, a box one of
+ *                      whose lower bounds exceeds its row's threshold
+ *                      counts as verified (TorchModel::isSpecVerified,
+ *                      TorchModel.cpp:616-651, for a conjunction; see
+ *                      lb200_compute_property for disjunctions) and the
+ *                      STOP_*_ON_VERIFIED options apply; without them
+ *                      nothing is ever verified, as in Luna after
  *                      setSpecificationMatrix.
  *   out_lb, out_ub   : [n_boxes, nspec] host
  *   stats            : may be NULL. */
@@ -261,6 +263,77 @@ LB200_API int lb200_shard_run(lb200_model* model, void* comm, int rank, int worl
  * buf may be NULL to query it.  No counterpart in the reference. */
 LB200_API int lb200_describe_plan(const lb200_graph_desc* graph, const lb200_options* opt, char* buf, size_t len,
                                   size_t* needed);
+
+/* ---- VNN-LIB properties ---------------------------------------------------
+ * A property is an input box over the variables X_i and output constraints
+ * over Y_j that describe the counterexample region: "C.y <= thresholds"
+ * for a conjunction of rows, or a disjunction (OR) of such conjunctions
+ * (branches).  The property is UNSAT (verified) when the bounds show that
+ * region unreachable.  Replaces VnnLibInputParser::parseInputBounds /
+ * parseOutputConstraints (src/input_parsers/VnnLibInputParser.cpp:335-372,
+ * 917-928), OutputConstraintSet::toCMatrix (OutputConstraint.cpp:71-173) and
+ * the CLI's evaluatePropertyStatus (src/engine/LunaMain.cpp:60-135). */
+typedef struct lb200_property lb200_property;
+
+typedef enum {
+    LB200_STATUS_UNKNOWN = 0, /* the bounds decide nothing */
+    LB200_STATUS_UNSAT = 1,   /* verified: the counterexample region is unreachable */
+    LB200_STATUS_SAT = 2      /* every point of the box is a counterexample */
+} lb200_status;
+
+typedef struct lb200_property_info {
+    int64_t n_in, n_out; /* the sizes the property was parsed for */
+    int64_t nspec;       /* rows of C; 0 when the text has no usable output constraints */
+    int32_t n_branches;  /* OR branches; 0 for a plain conjunction */
+    int32_t spec_dropped; /* 1 when output constraints were present but failed to convert */
+    char spec_error[256]; /* why, when spec_dropped */
+} lb200_property_info;
+
+/* Parse VNN-LIB text (the bytes of a .vnnlib file) for a network with n_in
+ * inputs and n_out outputs, as TorchModel(onnxPath, vnnlibPath) does
+ * (src/engine/TorchModelOnnxFactory.cpp:89-192): lines are trimmed, blank and
+ * ';' comment lines dropped, the rest joined; X_i bounds missing from the
+ * text are -inf / +inf; X_i with i >= n_in are ignored.  A malformed input
+ * bound fails the call.  Output constraints that fail to convert (a Y_j with
+ * j >= n_out, a bad number) leave the property without a specification, as
+ * Luna continues without them; info.spec_dropped says so. */
+LB200_API int lb200_property_parse(const char* text, int64_t len, int64_t n_in, int64_t n_out,
+                                   lb200_property** out);
+LB200_API int lb200_property_get_info(const lb200_property* prop, lb200_property_info* info);
+/* lower, upper: [n_in] each. */
+LB200_API int lb200_property_input_box(const lb200_property* prop, float* lower, float* upper);
+/* C: [nspec, n_out]; thresholds: [nspec]; branch_of_row: [nspec] (all 0 for
+ * a conjunction).  Any of them may be NULL. */
+LB200_API int lb200_property_spec(const lb200_property* prop, float* C, float* thresholds, int32_t* branch_of_row);
+LB200_API void lb200_property_free(lb200_property* prop);
+
+/* The verdict of each of n_boxes boxes from the bounds of its nspec rows
+ * (host arrays; lb, ub [n_boxes, nspec]); n_branches == 0 for a
+ * conjunction, else branch_of_row [nspec] gives each row's branch in
+ * [0, n_branches).  status: [n_boxes] lb200_status values. */
+LB200_API int lb200_property_status(const float* lb, const float* ub, int64_t n_boxes, int64_t nspec,
+                                    const float* thresholds, const int32_t* branch_of_row, int32_t n_branches,
+                                    int32_t* status);
+/* As lb200_property_status with every array in device memory of the current
+ * CUDA device, one thread per box, ordered on `stream`; returns without
+ * waiting. */
+LB200_API int lb200_property_status_device(const float* d_lb, const float* d_ub, int64_t n_boxes, int64_t nspec,
+                                           const float* d_thresholds, const int32_t* d_branch_of_row,
+                                           int32_t n_branches, int32_t* d_status, void* stream);
+
+/* Bound n_boxes boxes against a property, as the Luna CLI does for one
+ * (TorchModel(onnx, vnnlib) then compute_bounds(inputBounds, nullptr,
+ * method) then evaluatePropertyStatus, LunaMain.cpp:240-330): C, thresholds
+ * and branches come from the property and are shared by every box, so the
+ * STOP_CROWN_ON_VERIFIED / STOP_ALPHA_ON_VERIFIED options apply per box.
+ * x_lower / x_upper [n_boxes, n_in] host (sub-boxes of a split, say), or
+ * both NULL with n_boxes == 1 for the property's own input box.  out_lb,
+ * out_ub: [n_boxes, rows] host with rows = nspec, or n_out (raw output
+ * bounds, status UNKNOWN) when the property has no specification.
+ * status: [n_boxes] or NULL. */
+LB200_API int lb200_compute_property(lb200_model* model, int method, const lb200_property* prop,
+                                     const float* x_lower, const float* x_upper, int64_t n_boxes,
+                                     float* out_lb, float* out_ub, int32_t* status, lb200_stats* stats);
 
 /* Copy the last error message of this thread into buf (always terminated). */
 LB200_API int lb200_last_error(char* buf, size_t len);

@@ -31,6 +31,12 @@ METHOD_IBP = 0
 METHOD_CROWN = 1
 METHOD_ALPHA_CROWN = 2
 
+# lb200_status: the verdict on a VNN-LIB property for one box.
+STATUS_UNKNOWN = 0
+STATUS_UNSAT = 1  # verified: the counterexample region is unreachable
+STATUS_SAT = 2    # every point of the box is a counterexample
+STATUS_NAMES = {STATUS_UNKNOWN: "unknown", STATUS_UNSAT: "unsat", STATUS_SAT: "sat"}
+
 _fp = C.POINTER(C.c_float)
 
 
@@ -93,6 +99,17 @@ class Stats(C.Structure):
         ("ms_contractions", C.c_double),
         ("contraction_launches", C.c_int64),
         ("contraction_flops", C.c_double),
+    ]
+
+
+class PropertyInfo(C.Structure):
+    _fields_ = [
+        ("n_in", C.c_int64),
+        ("n_out", C.c_int64),
+        ("nspec", C.c_int64),
+        ("n_branches", C.c_int32),
+        ("spec_dropped", C.c_int32),
+        ("spec_error", C.c_char * 256),
     ]
 
 

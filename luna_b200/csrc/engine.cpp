@@ -1580,6 +1580,46 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         return;
     }
     if (opt_.optimize_upper) throw std::invalid_argument("optimize_upper is not supported by this engine build");
+    BoxControl bc;
+    bc.active = cache_.as<int>("ctl_active", B);
+    int* done = nullptr;
+    float* crown_lb = nullptr;
+    float* crown_ub = nullptr;
+    if (thr_ && opt_.stop_crown_on_verified) {
+        // --- TorchModel::runAlphaCROWN early stop (TorchModel.cpp:816-834):
+        // the CROWN initialisation pass (AlphaCROWNAnalysis.cpp:118-129, a
+        // plain CROWN pass) bounds every box; a box it verifies returns those
+        // bounds and takes no part in the optimisation.
+        alpha_ = false;
+        run_pass(Pass::CROWN, B, nspec, s);
+        crown_lb = cache_.as<float>("crown_lb", (size_t)B * nspec);
+        crown_ub = cache_.as<float>("crown_ub", (size_t)B * nspec);
+        launch_scatter_output(out.rows, cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R), nspec, true,
+                              crown_lb, crown_ub, s);
+        done = cache_.as<int>("ctl_done", B);
+        int* n_done = cache_.as<int>("ctl_ndone", 1);
+        LB_CUDA(cudaMemsetAsync(n_done, 0, sizeof(int), s));
+        launch_crown_verified(crown_lb, thr_, branch_, n_branches_, B, nspec, done, bc.active, n_done, s);
+        int h_done = 0;
+        LB_CUDA(cudaMemcpyAsync(&h_done, n_done, sizeof(int), cudaMemcpyDeviceToHost, s));
+        LB_CUDA(cudaStreamSynchronize(s));
+        if (h_done == B) {
+            // Every box verified: the intermediate bounds are the CROWN pass's.
+            for (int m = 1; m < K_; ++m) {
+                const size_t bn = (size_t)B * width(m) * 4;
+                LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_l", m), bn / 4),
+                                        cache_.as<float>(key("cur_l", m), bn / 4), bn, cudaMemcpyDeviceToDevice, s));
+                LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_u", m), bn / 4),
+                                        cache_.as<float>(key("cur_u", m), bn / 4), bn, cudaMemcpyDeviceToDevice, s));
+            }
+            LB_CUDA(cudaMemcpyAsync(lb, crown_lb, (size_t)B * nspec * 4, cudaMemcpyDeviceToDevice, s));
+            LB_CUDA(cudaMemcpyAsync(ub, crown_ub, (size_t)B * nspec * 4, cudaMemcpyDeviceToDevice, s));
+            return;
+        }
+    } else {
+        const std::vector<int> ones(B, 1);
+        LB_CUDA(cudaMemcpyAsync(bc.active, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
+    }
     alpha_ = true;
     // --- AlphaCROWNAnalysis::computeOptimizedBounds(Lower) ------------------
     run_pass(Pass::ALPHA_FIRST, B, nspec, s);
@@ -1590,11 +1630,9 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_u", m), bn / 4), cache_.as<float>(key("cur_u", m), bn / 4), bn,
                                 cudaMemcpyDeviceToDevice, s));
     }
-    BoxControl bc;
     bc.best = cache_.as<float>("ctl_best", (size_t)B * nspec);
     bc.best_loss = cache_.as<float>("ctl_bestloss", B);
     bc.patience = cache_.as<int>("ctl_pat", B);
-    bc.active = cache_.as<int>("ctl_active", B);
     bc.has_best = cache_.as<int>("ctl_hasbest", B);
     bc.save = cache_.as<int>("ctl_save", B);
     bc.improved = cache_.as<uint8_t>("ctl_improved", (size_t)B * nspec);
@@ -1603,9 +1641,16 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     LB_CUDA(cudaMemsetAsync(bc.patience, 0, B * 4, s));
     LB_CUDA(cudaMemsetAsync(bc.has_best, 0, B * 4, s));
     LB_CUDA(cudaMemsetAsync(bc.save, 0, B * 4, s));
-    std::vector<int> ones(B, 1);
-    LB_CUDA(cudaMemcpyAsync(bc.active, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
+    const std::vector<int> ones(B, 1);
     LB_CUDA(cudaMemcpyAsync(bc.first_save, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
+    if (thr_ && opt_.stop_alpha_on_verified) {
+        bc.thr = thr_;
+        bc.branch = branch_;
+        bc.n_branches = n_branches_;
+    }
+    // With thresholds, boxes stop early; the loop ends once none is left.
+    int* n_active = thr_ ? cache_.as<int>("ctl_nactive", 1) : nullptr;
+    bc.n_active = n_active;
     for (int st = 2; st <= K_; ++st)
         for (int m = 1; m < st; ++m) {
             const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
@@ -1620,11 +1665,13 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     float* cur_ub = cache_.as<float>("cur_ub", (size_t)B * nspec);
     float* gout = cache_.as<float>(key("g", K_), std::max(out.rows.R, 1));
     int steps = 0;
-    for (int it = 0; it < iters; ++it) {
+    int it = 0;
+    for (; it < iters; ++it) {
         const bool last = it == iters - 1;
         run_pass(Pass::ALPHA_ITER, B, nspec, s);
         val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
         launch_scatter_output(out.rows, val_out, nspec, false, cur_lb, cur_ub, s);
+        if (n_active) LB_CUDA(cudaMemsetAsync(n_active, 0, sizeof(int), s));
         launch_alpha_control(bc, cur_lb, B, nspec, it, save_after, (int)opt_.early_stop_patience, !last, s);
         for (int m = 1; m < K_; ++m) {
             const size_t bn = (size_t)B * width(m);
@@ -1648,6 +1695,14 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
             }
         launch_clear_first_save(bc.save, bc.first_save, B, s);
         if (last) break;
+        if (n_active) {
+            // Later iterations change nothing for a box that has stopped, so
+            // once every box has stopped the loop can end.
+            int h_active = 0;
+            LB_CUDA(cudaMemcpyAsync(&h_active, n_active, sizeof(int), cudaMemcpyDeviceToHost, s));
+            LB_CUDA(cudaStreamSynchronize(s));
+            if (h_active == 0) break;
+        }
         // --- hand-written adjoint of the whole pass (replaces loss.backward())
         // with the torch::optim::Adam step + [0, 1] clip fused into it ---------
         for (int m = 1; m < K_; ++m) {
@@ -1697,6 +1752,8 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     // upper side of this pass (same best intermediate bounds and alphas).
     launch_scatter_output(out.rows, val_out, nspec, upper, lb, ub, s);
     launch_max_best(bc.best, bc.has_best, B * nspec, nspec, lb, s);
+    if (done) launch_take_verified(done, crown_lb, crown_ub, B, nspec, lb, ub, s);
+    iters_run_ = std::max(iters_run_, std::min(it + 1, iters));
     (void)nout;
 }
 
@@ -1744,12 +1801,18 @@ double Model::prof_collect() {
 // ------------------------------------------------------------ entry
 void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes, const float* d_C,
                     int64_t c_boxes, int64_t nspec, const float* d_thr, bool lower, bool upper,
-                    float* d_lb, float* d_ub, cudaStream_t stream, lb200_stats* stats) {
+                    float* d_lb, float* d_ub, cudaStream_t stream, lb200_stats* stats, const int32_t* d_branch,
+                    int n_branches) {
     (void)lower;
     if (method < LB200_METHOD_IBP || method > LB200_METHOD_ALPHA_CROWN) throw std::invalid_argument("unknown method");
     if (n_boxes < 0 || nspec <= 0) throw std::invalid_argument("bad sizes");
     if (c_boxes != 1 && c_boxes != n_boxes) throw std::invalid_argument("c_boxes must be 1 or n_boxes");
-    if (d_thr) throw std::invalid_argument("thresholds are not supported by this engine build");
+    if (n_branches < 0 || (n_branches > 0 && (!d_branch || !d_thr)))
+        throw std::invalid_argument("OR branches need thresholds and a branch index per row");
+    thr_ = d_thr;
+    branch_ = d_branch;
+    n_branches_ = n_branches;
+    iters_run_ = 0;
     LB_CUDA(cudaSetDevice(device_));
     const auto t0 = std::chrono::steady_clock::now();
     launch_counter() = 0;
@@ -1796,7 +1859,7 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
         stats->kernel_launches = launch_counter();
         stats->backward_rows = rows_;
         stats->algorithmic_flops = flops_;
-        stats->alpha_iterations_run = alpha ? (int)opt_.alpha_iterations : 0;
+        stats->alpha_iterations_run = alpha ? iters_run_ : 0;
         stats->ms_contractions = prof_collect();
         stats->contraction_launches = contraction_launches_;
         stats->contraction_flops = contraction_flops_;

@@ -119,7 +119,7 @@ public:
     void compute(int method, const float* d_xl, const float* d_xu, int64_t n_boxes,
                  const float* d_C, int64_t c_boxes, int64_t nspec, const float* d_thr,
                  bool lower, bool upper, float* d_lb, float* d_ub, cudaStream_t stream,
-                 lb200_stats* stats);
+                 lb200_stats* stats, const int32_t* d_branch = nullptr, int n_branches = 0);
 
     // Host-side upload helpers for the host-buffer entry point.
     float* staging(const std::string& name, size_t count) { return cache_.as<float>(name, count); }
@@ -211,6 +211,12 @@ private:
     int64_t rows_ = 0;
     int last_B_ = 0;
     bool last_alpha_ = false;
+    // Specification thresholds of the current call (device, or null) and the
+    // OR branch of each row (n_branches_ == 0: a conjunction).
+    const float* thr_ = nullptr;
+    const int32_t* branch_ = nullptr;
+    int n_branches_ = 0;
+    int iters_run_ = 0;  // alpha iterations run, max over the chunks of a call
 
     bool force_simt_ = false;
     bool tc_ = false;  // tensor-core schedule for the current chunk

@@ -2,6 +2,7 @@
 // relaxation parameters, start steps, fp32 GEMM with fused epilogues,
 // alpha-CROWN control and the hand-written adjoint).
 #include "kernels.cuh"
+#include "property.cuh"
 
 #include <cmath>
 
@@ -898,6 +899,15 @@ __global__ void alpha_control_kernel(BoxControl c, const float* __restrict__ cur
     const float* cv = cur + (size_t)bx * nspec;
     float* best = c.best + (size_t)bx * nspec;
     uint8_t* imp = c.improved + (size_t)bx * nspec;
+    if (c.thr && lb200::box_verified(cv, c.thr, c.branch, nspec, c.n_branches)) {
+        // Verified during the optimisation (AlphaCROWNAnalysis.cpp:396-407):
+        // the best bound takes this iteration's, nothing is saved, the box
+        // stops.
+        for (int j = 0; j < nspec; ++j) best[j] = c.has_best[bx] ? fmaxf(best[j], cv[j]) : cv[j];
+        c.has_best[bx] = 1;
+        c.active[bx] = 0;
+        return;
+    }
     bool any = false;
     if (!c.has_best[bx]) {
         for (int j = 0; j < nspec; ++j) {
@@ -935,6 +945,42 @@ __global__ void alpha_control_kernel(BoxControl c, const float* __restrict__ cur
         }
     }
     if (c.patience[bx] >= patience_limit) c.active[bx] = 0;
+    else if (c.n_active) atomicAdd(c.n_active, 1);
+}
+
+__global__ void crown_verified_kernel(const float* __restrict__ lb, const float* __restrict__ thr,
+                                      const int32_t* __restrict__ branch, int n_branches, int B, int nspec,
+                                      int* __restrict__ done, int* __restrict__ active, int* n_done) {
+    const int bx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (bx >= B) return;
+    const bool v = lb200::box_verified(lb + (size_t)bx * nspec, thr, branch, nspec, n_branches);
+    done[bx] = v ? 1 : 0;
+    active[bx] = v ? 0 : 1;
+    if (v) atomicAdd(n_done, 1);
+}
+
+void launch_crown_verified(const float* lb, const float* thr, const int32_t* branch, int n_branches, int B,
+                           int nspec, int* done, int* active, int* n_done, cudaStream_t s) {
+    crown_verified_kernel<<<ceil_div(B, 128), 128, 0, s>>>(lb, thr, branch, n_branches, B, nspec, done, active,
+                                                           n_done);
+    LB_LAUNCH();
+}
+
+__global__ void take_verified_kernel(const int* __restrict__ done, const float* __restrict__ crown_lb,
+                                     const float* __restrict__ crown_ub, int B, int nspec, float* __restrict__ lb,
+                                     float* __restrict__ ub) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (int64_t)B * nspec) return;
+    if (!done[idx / nspec]) return;
+    lb[idx] = crown_lb[idx];
+    ub[idx] = crown_ub[idx];
+}
+
+void launch_take_verified(const int* done, const float* crown_lb, const float* crown_ub, int B, int nspec,
+                          float* lb, float* ub, cudaStream_t s) {
+    take_verified_kernel<<<ceil_div((int64_t)B * nspec, 256), 256, 0, s>>>(done, crown_lb, crown_ub, B, nspec, lb,
+                                                                           ub);
+    LB_LAUNCH();
 }
 
 void launch_alpha_control(const BoxControl& c, const float* cur, int B, int nspec, int iter,

@@ -256,11 +256,25 @@ struct BoxControl {
     int* save = nullptr;            // [B] set when this iteration saves alpha/bounds
     uint8_t* improved = nullptr;    // [B, nspec]
     int* first_save = nullptr;      // [B] 1 until the first alpha save
+    // STOP_ALPHA_ON_VERIFIED with thresholds (thr != null): a box whose
+    // current lower bounds verify the specification stops at once.
+    const float* thr = nullptr;     // [nspec]
+    const int32_t* branch = nullptr; // [nspec] OR branch of each row (n_branches > 0)
+    int n_branches = 0;
+    int* n_active = nullptr;        // [1] boxes still optimising after this iteration
 };
-// One iteration's bookkeeping (AlphaCROWNAnalysis.cpp:415-472) for every
+// One iteration's bookkeeping (AlphaCROWNAnalysis.cpp:394-472) for every
 // active box.  `cur` is the current lower bound [B, nspec].
 void launch_alpha_control(const BoxControl& c, const float* cur, int B, int nspec, int iter,
                           int save_after, int patience_limit, bool has_loss, cudaStream_t s);
+// STOP_CROWN_ON_VERIFIED (TorchModel.cpp:816-834): done[b] = the box's CROWN
+// lower bounds lb [B, nspec] verify the specification; active[b] = !done[b];
+// *n_done counts the done boxes (set to zero first by the caller).
+void launch_crown_verified(const float* lb, const float* thr, const int32_t* branch, int n_branches, int B,
+                           int nspec, int* done, int* active, int* n_done, cudaStream_t s);
+// lb, ub [B, nspec] = crown_lb, crown_ub for the boxes with done.
+void launch_take_verified(const int* done, const float* crown_lb, const float* crown_ub, int B, int nspec,
+                          float* lb, float* ub, cudaStream_t s);
 // best_l = max(best_l, cur_l), best_u = min(best_u, cur_u) for boxes with save.
 void launch_snapshot(const int* save, const float* cur_l, const float* cur_u, int B, int n,
                      float* best_l, float* best_u, cudaStream_t s);

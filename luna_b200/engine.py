@@ -15,7 +15,7 @@ import os
 
 import numpy as np
 
-from .abi import GraphDesc, Options, Stats, default_options, fptr
+from .abi import GraphDesc, Options, PropertyInfo, Stats, default_options, fptr
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "_lib", "libluna_b200.so")
@@ -25,7 +25,9 @@ EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_get_intermediate_bounds", "lb200_last_error", "lb200_model_destroy",
            "lb200_set_profiling", "lb200_set_contraction_path", "lb200_ibp_bounds_noalloc",
            "lb200_shard_range", "lb200_nccl_unique_id", "lb200_nccl_comm_create", "lb200_nccl_comm_destroy",
-           "lb200_shard_run", "lb200_describe_plan")
+           "lb200_shard_run", "lb200_describe_plan", "lb200_property_parse", "lb200_property_get_info",
+           "lb200_property_input_box", "lb200_property_spec", "lb200_property_free", "lb200_property_status",
+           "lb200_property_status_device", "lb200_compute_property")
 
 
 class EngineError(RuntimeError):
@@ -69,6 +71,16 @@ def load_library():
                                     C.c_int64, fp, fp, C.c_int, C.POINTER(Stats)]
     lib.lb200_describe_plan.argtypes = [C.POINTER(GraphDesc), C.POINTER(Options), C.c_char_p, C.c_size_t,
                                         C.POINTER(C.c_size_t)]
+    ip = C.POINTER(C.c_int32)
+    lib.lb200_property_parse.argtypes = [C.c_char_p, C.c_int64, C.c_int64, C.c_int64, C.POINTER(vp)]
+    lib.lb200_property_get_info.argtypes = [vp, C.POINTER(PropertyInfo)]
+    lib.lb200_property_input_box.argtypes = [vp, fp, fp]
+    lib.lb200_property_spec.argtypes = [vp, fp, fp, ip]
+    lib.lb200_property_free.argtypes = [vp]
+    lib.lb200_property_free.restype = None
+    lib.lb200_property_status.argtypes = [fp, fp, C.c_int64, C.c_int64, fp, ip, C.c_int32, ip]
+    lib.lb200_property_status_device.argtypes = [vp, vp, C.c_int64, C.c_int64, vp, vp, C.c_int32, vp, vp]
+    lib.lb200_compute_property.argtypes = [vp, C.c_int, vp, fp, fp, C.c_int64, fp, fp, ip, C.POINTER(Stats)]
     _lib = lib
     return lib
 
@@ -157,20 +169,49 @@ class Model:
         _check(_lib.lb200_set_contraction_path(self._h, int(path)), "lb200_set_contraction_path")
 
     def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,
-                       out_lb: np.ndarray | None = None, out_ub: np.ndarray | None = None):
-        """Bound every box from host arrays; returns (lb, ub) as [B, nspec] fp32."""
+                       out_lb: np.ndarray | None = None, out_ub: np.ndarray | None = None,
+                       thresholds: np.ndarray | None = None):
+        """Bound every box from host arrays; returns (lb, ub) as [B, nspec] fp32.
+        With `thresholds` [nspec] a box is verified once some row's lower bound
+        exceeds its threshold, and the STOP_*_ON_VERIFIED options apply."""
         xl = np.ascontiguousarray(boxes.lower, np.float32)
         xu = np.ascontiguousarray(boxes.upper, np.float32)
         Cm = np.ascontiguousarray(boxes.C, np.float32)
         B, nspec = xl.shape[0], Cm.shape[1]
+        thr = None if thresholds is None else np.ascontiguousarray(thresholds, np.float32).reshape(nspec)
         lb = out_lb if out_lb is not None else np.empty((B, nspec), np.float32)
         ub = out_ub if out_ub is not None else np.empty((B, nspec), np.float32)
         st = Stats()
         _check(_lib.lb200_compute_bounds(self._h, method, fptr(xl), fptr(xu), B, fptr(Cm), Cm.shape[0],
-                                         nspec, fptr(None), int(bound_lower), int(bound_upper),
+                                         nspec, fptr(thr), int(bound_lower), int(bound_upper),
                                          fptr(lb), fptr(ub), C.byref(st)), "lb200_compute_bounds")
         self.last_stats = st
         return lb, ub
+
+    def compute_property(self, prop, method: int, lower: np.ndarray | None = None,
+                         upper: np.ndarray | None = None):
+        """Bound boxes against a `vnnlib.Property` (lb200_compute_property):
+        the property's own input box when `lower`/`upper` are None, else the
+        boxes [B, n_in].  Returns (lb, ub, status) with lb, ub [B, rows] and
+        status [B] (abi.STATUS_*)."""
+        if (lower is None) != (upper is None):
+            raise ValueError("give both lower and upper, or neither")
+        if lower is None:
+            B, xl, xu = 1, None, None
+        else:
+            xl = np.ascontiguousarray(lower, np.float32).reshape(-1, prop.n_in)
+            xu = np.ascontiguousarray(upper, np.float32).reshape(-1, prop.n_in)
+            B = xl.shape[0]
+        rows = prop.nspec if prop.nspec > 0 else prop.n_out
+        lb = np.empty((B, rows), np.float32)
+        ub = np.empty((B, rows), np.float32)
+        status = np.empty(B, np.int32)
+        st = Stats()
+        _check(_lib.lb200_compute_property(self._h, method, prop.handle, fptr(xl), fptr(xu), B, fptr(lb), fptr(ub),
+                                           status.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(st)),
+               "lb200_compute_property")
+        self.last_stats = st
+        return lb, ub, status
 
     def shard_run(self, comm: NcclComm, boxes, method: int, timeout_ms: int = 60000):
         """Bound this rank's share of `boxes` and all-gather every rank's

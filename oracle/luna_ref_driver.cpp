@@ -28,10 +28,13 @@
 #include "nodes/BoundedAddNode.h"
 #include "nodes/BoundedSigmoidNode.h"
 #include "input_parsers/Operations.h"
+#include "input_parsers/OutputConstraint.h"
+#include "input_parsers/VnnLibInputParser.h"
 
 #include <torch/torch.h>
 
 #include <cstring>
+#include <iostream>
 #include <memory>
 #include <string>
 #include <vector>
@@ -275,6 +278,186 @@ int luna_ref_compute_bounds(const lb200_graph_desc* g, const lb200_options* opt,
                     off += sz;
                 }
             }
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 1;
+    } catch (...) {
+        set_error(err, errlen, "luna_ref_driver: unknown exception");
+        return 1;
+    }
+}
+
+// ---- VNN-LIB properties through Luna's own parser ------------------------
+//
+// As TorchModel(onnxPath, vnnlibPath) reads a property
+// (src/engine/TorchModelOnnxFactory.cpp:89-192): parseInputBounds (a failure
+// fails the call, return 2), then parseOutputConstraints + toCMatrix when
+// there are constraints (a failure drops the specification:
+// *spec_dropped = 1).  C [cap_rows, n_out], thresholds and branch [cap_rows]
+// receive up to cap_rows rows; *nspec is the true count (return 3 when it
+// exceeds cap_rows).  *n_branches is 0 without OR branches.
+int luna_ref_vnnlib_parse(const char* path, int64_t n_in, int64_t n_out, float* lower, float* upper,
+                          int64_t cap_rows, float* C, float* thresholds, int32_t* branch, int64_t* nspec,
+                          int32_t* n_branches, int32_t* spec_dropped, char* err, size_t errlen) {
+    *nspec = 0;
+    *n_branches = 0;
+    *spec_dropped = 0;
+    try {
+        auto ib = VnnLibInputParser::parseInputBounds(String(path), (unsigned)n_in);
+        auto lo = ib.lower().contiguous(), hi = ib.upper().contiguous();
+        std::memcpy(lower, lo.data_ptr<float>(), n_in * sizeof(float));
+        std::memcpy(upper, hi.data_ptr<float>(), n_in * sizeof(float));
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 2;
+    }
+    try {
+        auto oc = VnnLibInputParser::parseOutputConstraints(String(path), (unsigned)n_out);
+        if (!oc.hasConstraints()) return 0;
+        auto r = oc.toCMatrix();
+        const int64_t rows = r.C.size(0);
+        *nspec = rows;
+        *n_branches = r.hasORBranches ? (int32_t)r.branchSizes.size() : 0;
+        if (rows > cap_rows) return 3;
+        auto c = r.C.reshape({rows, n_out}).contiguous();
+        auto t = r.thresholds.contiguous();
+        std::memcpy(C, c.data_ptr<float>(), rows * n_out * sizeof(float));
+        std::memcpy(thresholds, t.data_ptr<float>(), rows * sizeof(float));
+        for (int64_t k = 0; k < rows; ++k) branch[k] = r.hasORBranches ? (int32_t)r.branchMapping[(unsigned)k] : 0;
+        return 0;
+    } catch (const std::exception& e) {
+        *nspec = 0;
+        *n_branches = 0;
+        *spec_dropped = 1;
+        set_error(err, errlen, e.what());
+        return 0;
+    }
+}
+
+}  // extern "C"
+
+namespace {
+
+// The CLI's verdict (src/engine/LunaMain.cpp:60-135, a static function of
+// the CLI, restated here): OR branches through Luna's own
+// OutputConstraintSet::evaluateORBranches, a conjunction by its two tests.
+int ref_status(const torch::Tensor& lb, const torch::Tensor& ub, const torch::Tensor& thr,
+               const Vector<unsigned>& mapping, const Vector<unsigned>& sizes, bool has_or) {
+    if (lb.numel() == 0 || ub.numel() == 0) return LB200_STATUS_UNKNOWN;
+    if (lb.numel() != thr.numel() || ub.numel() != thr.numel()) return LB200_STATUS_UNKNOWN;
+    if (has_or) {
+        auto res = NLR::OutputConstraintSet::evaluateORBranches(lb, ub, thr, mapping, sizes);
+        bool all_disproved = true, any_sat = false;
+        for (const auto& b : res) {
+            if (!b.verified) all_disproved = false;
+            if (b.refuted) any_sat = true;
+        }
+        if (all_disproved) return LB200_STATUS_UNSAT;
+        return any_sat ? LB200_STATUS_SAT : LB200_STATUS_UNKNOWN;
+    }
+    if ((lb - thr > 0).any().item<bool>()) return LB200_STATUS_UNSAT;
+    if ((ub - thr <= 0).all().item<bool>()) return LB200_STATUS_SAT;
+    return LB200_STATUS_UNKNOWN;
+}
+
+torch::Tensor rows_tensor(const float* p, int64_t n) { return from_host(p, {n}); }
+
+}  // namespace
+
+extern "C" {
+
+// Luna's verdict for n_boxes boxes of bounds [n_boxes, nspec]
+// (n_branches == 0: a conjunction).
+int luna_ref_property_status(const float* lb, const float* ub, int64_t n_boxes, int64_t nspec,
+                             const float* thresholds, const int32_t* branch, int32_t n_branches, int32_t* status,
+                             char* err, size_t errlen) {
+    try {
+        Vector<unsigned> mapping, sizes;
+        for (int64_t k = 0; k < nspec && n_branches > 0; ++k) mapping.append((unsigned)branch[k]);
+        for (int32_t b = 0; b < n_branches; ++b) {
+            unsigned cnt = 0;
+            for (int64_t k = 0; k < nspec; ++k) cnt += branch[k] == b;
+            sizes.append(cnt);
+        }
+        torch::Tensor thr = rows_tensor(thresholds, nspec);
+        for (int64_t b = 0; b < n_boxes; ++b)
+            status[b] = ref_status(rows_tensor(lb + b * nspec, nspec), rows_tensor(ub + b * nspec, nspec), thr,
+                                   mapping, sizes, n_branches > 0);
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 1;
+    }
+}
+
+// The CLI's flow for each box (src/engine/LunaMain.cpp:240-330): a fresh
+// model, the property's constraints set with setSpecificationFromConstraints
+// (thresholds and branches kept, so STOP_*_ON_VERIFIED apply), then
+// compute_bounds(box, nullptr, method, true, true) and the verdict.  The
+// constraints arrive as the rows Luna's toCMatrix made of them (C
+// [nspec, n_out], thresholds, branch of each row, n_branches == 0 for a
+// conjunction) and are rebuilt into an OutputConstraintSet: Luna's
+// tokenizer (std::regex) cannot run inside a Python process that has
+// imported torch, so the text is parsed out of process.  nspec == 0: no
+// specification, out_lb / out_ub are [n_boxes, n_out] and status UNKNOWN.
+int luna_ref_compute_property(const lb200_graph_desc* g, const lb200_options* opt, int method, const float* C,
+                              const float* thresholds, const int32_t* branch, int64_t nspec, int32_t n_branches,
+                              const float* x_lower, const float* x_upper, int64_t n_boxes, int64_t n_in,
+                              int64_t n_out, float* out_lb, float* out_ub, int32_t* status, int num_threads,
+                              char* err, size_t errlen) {
+    try {
+        at::set_num_threads(num_threads > 0 ? num_threads : 1);
+        apply_options(opt);
+        NLR::OutputConstraintSet oc;
+        oc.setOutputDimension((unsigned)n_out);
+        auto row = [&](int64_t r) {
+            NLR::OutputConstraint c;
+            for (int64_t j = 0; j < n_out; ++j)
+                if (C[r * n_out + j] != 0.f) c.terms.append(NLR::OutputTerm((unsigned)j, C[r * n_out + j]));
+            c.threshold = thresholds[r];
+            return c;
+        };
+        if (n_branches > 0) {
+            for (int32_t b = 0; b < n_branches; ++b) {
+                Vector<NLR::OutputConstraint> br;
+                for (int64_t r = 0; r < nspec; ++r)
+                    if (branch[r] == b) br.append(row(r));
+                oc.addORBranch(br);
+            }
+        } else {
+            for (int64_t r = 0; r < nspec; ++r) oc.addConstraint(row(r));
+        }
+        const bool spec = nspec > 0;
+        NLR::CMatrixResult cm;
+        if (spec) cm = oc.toCMatrix();
+        // The reference reports early stops on std::cout with numbers in
+        // them; number formatting through std::cout crashes when the library
+        // is loaded into a Python process, so the stream is muted (a stream
+        // in a failed state formats nothing) for the duration of the call.
+        struct Mute {
+            std::ios_base::iostate was = std::cout.rdstate();
+            Mute() { std::cout.setstate(std::ios_base::badbit); }
+            ~Mute() { std::cout.clear(was); }
+        } mute;
+        for (int64_t b = 0; b < n_boxes; ++b) {
+            auto model = build_model(g);
+            if (spec) model->setSpecificationFromConstraints(oc);
+            BoundedTensor<torch::Tensor> box(from_host(x_lower + b * n_in, {n_in}),
+                                             from_host(x_upper + b * n_in, {n_in}));
+            LunaConfiguration::ENABLE_FIRST_LINEAR_IBP = opt->enable_first_linear_ibp != 0;
+            auto m = method == LB200_METHOD_ALPHA_CROWN ? LunaConfiguration::AnalysisMethod::AlphaCROWN
+                                                         : LunaConfiguration::AnalysisMethod::CROWN;
+            auto res = model->compute_bounds(box, nullptr, m, true, true);
+            torch::Tensor rl = res.lower().flatten().contiguous(), ru = res.upper().flatten().contiguous();
+            const int64_t rows = spec ? nspec : n_out;
+            if (rl.numel() != rows || ru.numel() != rows)
+                throw std::runtime_error("luna_ref_driver: unexpected bound shape");
+            std::memcpy(out_lb + b * rows, rl.data_ptr<float>(), rows * sizeof(float));
+            std::memcpy(out_ub + b * rows, ru.data_ptr<float>(), rows * sizeof(float));
+            status[b] = spec ? ref_status(rl, ru, cm.thresholds, cm.branchMapping, cm.branchSizes, cm.hasORBranches)
+                             : LB200_STATUS_UNKNOWN;
         }
         return 0;
     } catch (const std::exception& e) {

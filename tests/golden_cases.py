@@ -19,7 +19,22 @@ ATOL = 1e-6
 
 
 def names():
-    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz")))
+    """Bound-computation cases (make_golden.py)."""
+    return sorted(n for n in (os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "*.npz")))
+                  if not n.startswith("prop_"))
+
+
+def prop_names():
+    """Property cases (make_property_golden.py)."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "prop_*.npz")))
+
+
+def load_prop(name):
+    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    g, _ = getattr(W, str(z["generator"]))(**ast.literal_eval(str(z["kwargs"])))
+    opt = abi.default_options(**ast.literal_eval(str(z["options"])))
+    return dict(graph=g, text=str(z["text"]), lower=z["lower"], upper=z["upper"], method=int(z["method"]),
+                options=opt, lb=z["lb"], ub=z["ub"], status=z["status"])
 
 
 def _digest(graph) -> str:

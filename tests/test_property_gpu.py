@@ -1,0 +1,101 @@
+"""Bounding boxes against VNN-LIB properties on the GPU, against Luna.
+
+Luna's CLI flow (the property read by Luna's parser, its thresholds kept on
+the model so STOP_CROWN_ON_VERIFIED / STOP_ALPHA_ON_VERIFIED apply, then the
+verdict) produced the golden fixtures tests/golden/prop_*.npz
+(make_property_golden.py).  Their thresholds put some boxes past the
+threshold after the initial CROWN pass, some part-way through the alpha
+optimisation and some never, so the bounds below check where each box
+stopped.  Every call goes through the C ABI (lb200_compute_property and
+lb200_property_status_device)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+import golden_cases as G
+from luna_b200 import abi
+from luna_b200.engine import Model, _check, load_library
+from luna_b200.vnnlib import Property
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _built():
+    from luna_b200.build import build
+    build()
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+
+
+@pytest.mark.parametrize("name", G.prop_names())
+def test_property_matches_luna(name):
+    c = G.load_prop(name)
+    g = c["graph"]
+    n_out = int(np.prod(g.nodes[g.output_index].out_shape))
+    prop = Property(c["text"], c["lower"].shape[1], n_out)
+    m = Model(g, options=c["options"])
+    lb, ub, status = m.compute_property(prop, c["method"], c["lower"], c["upper"])
+    assert m.last_stats.kernel_launches > 0
+    strict = max(G.excess(lb, c["lb"]), G.excess(ub, c["ub"]))
+    scaled = max(G.excess_scaled(lb, c["lb"], c["lb"], c["ub"]), G.excess_scaled(ub, c["ub"], c["lb"], c["ub"]))
+    print(f"{name}: strict excess {strict:.3f} interval-scaled excess {scaled:.3f}, "
+          f"alpha iterations run {m.last_stats.alpha_iterations_run}")
+    assert scaled <= 1.0, (strict, scaled)
+    assert status.tolist() == c["status"].tolist()
+    assert (prop.status(lb, ub) == status).all()
+
+
+def test_property_own_box():
+    """With no boxes given, the property's own input box is bounded."""
+    c = G.load_prop("prop_mlp5_or_crown")
+    g = c["graph"]
+    lo, hi = c["lower"][3], c["upper"][3]
+    text = c["text"] + "".join(f"(assert (>= X_{k} {float(v):.9g}))\n(assert (<= X_{k} {float(w):.9g}))\n"
+                               for k, (v, w) in enumerate(zip(lo, hi)))
+    prop = Property(text, len(lo), 5)
+    assert (prop.lower == lo).all() and (prop.upper == hi).all()
+    m = Model(g, options=c["options"])
+    lb, ub, status = m.compute_property(prop, c["method"])
+    assert G.excess(lb[0], c["lb"][3]) <= 1.0 and G.excess(ub[0], c["ub"][3]) <= 1.0
+    assert status[0] == c["status"][3]
+
+
+def test_thresholds_through_compute_bounds():
+    """lb200_compute_bounds with thresholds (a conjunction) stops boxes as
+    lb200_compute_property does for the same property."""
+    c = G.load_prop("prop_mlp5_conj_alpha")
+    prop = Property(c["text"], c["lower"].shape[1], 5)
+    from luna_b200.workloads import Boxes
+    m = Model(c["graph"], options=c["options"])
+    lb, ub = m.compute_bounds(Boxes(c["lower"], c["upper"], prop.C[None]), c["method"], thresholds=prop.thresholds)
+    scaled = max(G.excess_scaled(lb, c["lb"], c["lb"], c["ub"]), G.excess_scaled(ub, c["ub"], c["lb"], c["ub"]))
+    assert scaled <= 1.0
+
+
+def test_status_device_matches_host():
+    rng = np.random.default_rng(3)
+    lib = load_library()
+    for nspec, nb in ((4, 0), (6, 3), (1, 0), (9, 9)):
+        B = 5000
+        thr = rng.normal(size=nspec).astype(np.float32)
+        lb = (thr + rng.normal(size=(B, nspec)) - 1.0).astype(np.float32)
+        ub = (lb + 2 * np.abs(rng.normal(size=(B, nspec)))).astype(np.float32)
+        lb[rng.random(lb.shape) < 0.02] = np.nan
+        ub[rng.random(ub.shape) < 0.02] = np.nan
+        br = rng.integers(0, max(nb, 1), nspec).astype(np.int32)
+        host = np.zeros(B, np.int32)
+        ip = C.POINTER(C.c_int32)
+        fp = C.POINTER(C.c_float)
+        _check(lib.lb200_property_status(lb.ctypes.data_as(fp), ub.ctypes.data_as(fp), B, nspec,
+                                         thr.ctypes.data_as(fp), br.ctypes.data_as(ip), nb, host.ctypes.data_as(ip)),
+               "status")
+        t = {k: torch.from_numpy(v).cuda() for k, v in dict(lb=lb, ub=ub, thr=thr, br=br).items()}
+        dev = torch.zeros(B, dtype=torch.int32, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        _check(lib.lb200_property_status_device(t["lb"].data_ptr(), t["ub"].data_ptr(), B, nspec, t["thr"].data_ptr(),
+                                                t["br"].data_ptr(), nb, dev.data_ptr(), stream), "status_device")
+        torch.cuda.synchronize()
+        assert (dev.cpu().numpy() == host).all()
+        assert len(set(host.tolist())) == 3
