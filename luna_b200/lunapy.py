@@ -10,6 +10,14 @@ a `luna_b200.abi.Graph` (node list and weights) rather than an ONNX file,
 since this build has no ONNX front end; and besides Luna's single box
 (`[n_in]` bounds, `[nspec]` results) a batch of boxes (`[B, n_in]` bounds,
 `[B, nspec]` results) is accepted, bounded in one engine call.
+
+With `vnnlib_path` the input box and the specification (C, thresholds, OR
+branches) come from the property file, as in
+`TorchModel(onnx_path, vnnlib_path)`; `compute_bounds` then keeps the
+thresholds, so Luna's early stops on verified boxes apply, and
+`propertyStatus()` gives the CLI's verdict.  `setSpecificationMatrix`
+replaces the property's specification (and drops its thresholds), as in
+Luna.
 """
 from __future__ import annotations
 
@@ -47,7 +55,7 @@ class BoundedTensor:
 class TorchModel:
     """A network with bound propagation on one GPU (lunapy.TorchModel)."""
 
-    def __init__(self, graph, device: int = 0, options: abi.Options | None = None):
+    def __init__(self, graph, vnnlib_path=None, device: int = 0, options: abi.Options | None = None):
         if isinstance(graph, (str, bytes)):
             raise NotImplementedError("ONNX files are not read by this build; pass a luna_b200.abi.Graph")
         self._graph = graph
@@ -57,6 +65,12 @@ class TorchModel:
         self._lower = self._upper = None
         self._C = None
         self._final = None
+        self._property = None
+        self._status = None
+        if vnnlib_path is not None:
+            from .vnnlib import Property
+            self._property = Property.from_file(vnnlib_path, self.getInputSize(), self.getOutputSize())
+            self._lower, self._upper = self._property.lower.copy(), self._property.upper.copy()
 
     # ---------------------------------------------------------------- sizes
     def getInputSize(self) -> int:
@@ -103,9 +117,10 @@ class TorchModel:
         """C [nspec, n_out] (or [1, nspec, n_out]) for every box, or
         [B, nspec, n_out] with one specification per box."""
         self._C = self._spec(C)
+        self._property = None
 
     def hasSpecificationMatrix(self) -> bool:
-        return self._C is not None
+        return self._C is not None or (self._property is not None and self._property.has_spec)
 
     def _spec(self, C):
         C = np.asarray(C, np.float32)
@@ -126,19 +141,34 @@ class TorchModel:
         if self._lower is None:
             raise RuntimeError("input bounds are not set")
         spec = self._spec(C) if C is not None else self._C
+        if spec is None and self._property is not None and self._property.has_spec:
+            spec = self._property.C[None]
         if spec is None:
             spec = np.eye(self.getOutputSize(), dtype=np.float32)[None]
         single = self._lower.ndim == 1
         lo = self._lower.reshape(-1, self.getInputSize())
         hi = self._upper.reshape(-1, self.getInputSize())
-        if spec.shape[0] not in (1, lo.shape[0]):
-            raise ValueError("one specification for all boxes, or one per box")
-        from .workloads import Boxes
         if self._model is None:
             self._model = Model(self._graph, device=self._device, options=self._options)
-        lb, ub = self._model.compute_bounds(Boxes(lo, hi, spec), _METHODS[method], bound_lower, bound_upper)
+        self._status = None
+        if C is None and self._property is not None and _METHODS[method] != abi.METHOD_IBP:
+            # The property's specification with its thresholds (the CLI's path).
+            lb, ub, self._status = self._model.compute_property(self._property, _METHODS[method], lo, hi)
+        else:
+            if spec.shape[0] not in (1, lo.shape[0]):
+                raise ValueError("one specification for all boxes, or one per box")
+            from .workloads import Boxes
+            lb, ub = self._model.compute_bounds(Boxes(lo, hi, spec), _METHODS[method], bound_lower, bound_upper)
         self._final = BoundedTensor(lb[0] if single else lb, ub[0] if single else ub)
         return self._final
+
+    def propertyStatus(self):
+        """The CLI's verdict ('unsat' = verified, 'sat', 'unknown') of the last
+        bound computation against the property file, per box."""
+        if self._status is None:
+            raise RuntimeError("no property analysis has run")
+        names = [abi.STATUS_NAMES[int(v)] for v in self._status]
+        return names[0] if self._lower.ndim == 1 else names
 
     def runCROWN(self) -> BoundedTensor:
         return self.compute_bounds("CROWN")

@@ -84,10 +84,14 @@ def main(only=()):
         rows = margin_rows(n_out, label)
         Cm = np.stack([c for _, c in rows])[None]
         opt = abi.default_options(**over)
-        # Thresholds between the boxes' CROWN and alpha-CROWN margins.
+        # Each threshold halfway between two neighbouring alpha-CROWN margins
+        # of the boxes, so no box's bound sits at a threshold (a verdict
+        # there would turn on the last bits of the arithmetic).
         base = abi.default_options(**{k: v for k, v in over.items() if not k.startswith("stop_")})
         lA, _ = luna_ref.compute_bounds(g, Boxes(bx.lower, bx.upper, Cm), abi.METHOD_ALPHA_CROWN, base)
-        thr = np.quantile(lA, q, axis=0).astype(np.float32)
+        srt = np.sort(lA, axis=0)
+        k = min(max(int(q * (nb - 1)), 0), nb - 2)
+        thr = (0.5 * (srt[k] + srt[k + 1])).astype(np.float32)
         text = property_text(n_in, n_out, label, thr, kind)
         spec = luna_ref.vnnlib_parse(text, n_in, n_out)
         lb, ub, st = luna_ref.compute_property(g, spec, bx.lower, bx.upper, method, opt)

@@ -74,3 +74,38 @@ def test_identity_specification_and_batches():
         assert G.excess_scaled(one.upper(), res.upper()[b], res.lower()[b], res.upper()[b]) <= 1.0
         y = m.forward(0.5 * (bx.lower[b] + bx.upper[b]))
         assert (one.lower() <= y + 1e-5).all() and (y <= one.upper() + 1e-5).all()
+
+
+def test_vnnlib_constructor_reads_box_and_spec(tmp_path):
+    """TorchModel(graph, vnnlib_path): the box and the specification come
+    from the property file (CPU: nothing is bounded)."""
+    from luna_b200 import workloads as W
+    g, _ = W.mlp_5_50x6_5(n_boxes=1)
+    f = tmp_path / "p.vnnlib"
+    f.write_text("(assert (<= X_0 0.5))\n(assert (>= X_0 -0.5))\n"
+                 "(assert (or (and (>= Y_1 Y_0)) (and (>= Y_2 Y_0))))\n")
+    m = TorchModel(g, str(f))
+    b = m.getInputBounds()
+    assert b.lower()[0] == -0.5 and b.upper()[0] == 0.5 and np.isinf(b.lower()[1])
+    assert m.hasSpecificationMatrix()
+    m.setSpecificationMatrix(np.eye(5, dtype=np.float32))
+    assert m._property is None
+
+
+@pytest.mark.gpu
+def test_vnnlib_property_through_lunapy(tmp_path):
+    import golden_cases as G
+    c = G.load_prop("prop_mlp5_or_alpha")
+    lo, hi = c["lower"][6], c["upper"][6]
+    text = c["text"] + "".join(f"(assert (>= X_{k} {float(v):.9g}))\n(assert (<= X_{k} {float(w):.9g}))\n"
+                               for k, (v, w) in enumerate(zip(lo, hi)))
+    f = tmp_path / "p.vnnlib"
+    f.write_text(text)
+    m = TorchModel(c["graph"], str(f), options=c["options"])
+    r = m.compute_bounds("alpha-CROWN")
+    assert G.excess(r.lower(), c["lb"][6]) <= 1.0
+    assert m.propertyStatus() == abi.STATUS_NAMES[int(c["status"][6])]
+    # A batch of sub-boxes: one verdict per box.
+    m.setInputBounds(c["lower"][:4], c["upper"][:4])
+    m.compute_bounds("alpha-CROWN")
+    assert m.propertyStatus() == [abi.STATUS_NAMES[int(v)] for v in c["status"][:4]]

@@ -42,6 +42,10 @@ def test_property_matches_luna(name):
     scaled = max(G.excess_scaled(lb, c["lb"], c["lb"], c["ub"]), G.excess_scaled(ub, c["ub"], c["lb"], c["ub"]))
     print(f"{name}: strict excess {strict:.3f} interval-scaled excess {scaled:.3f}, "
           f"alpha iterations run {m.last_stats.alpha_iterations_run}")
+    if scaled > 1.0:
+        for b in range(lb.shape[0]):
+            print(f"  box {b}: status {status[b]} / {c['status'][b]}  lb excess {G.excess(lb[b], c['lb'][b]):.3f}"
+                  f"  ub excess {G.excess(ub[b], c['ub'][b]):.3f}  lb {lb[b]} luna {c['lb'][b]}")
     assert scaled <= 1.0, (strict, scaled)
     assert status.tolist() == c["status"].tolist()
     assert (prop.status(lb, ub) == status).all()
