@@ -10,7 +10,7 @@ A step bounds one batch of 512 boxes per GPU.  With N GPUs (torchrun) each
 rank bounds its own 512 boxes (weak scaling) and the final bounds are
 all-gathered over NCCL inside the step.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload mlp|cnn|resnet]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload mlp|cnn|resnet|sweep|property]
 
 `--impl reference` times Luna's own CPU implementation (oracle/_ref) on the
 host cores for the same workload and metric.  `--workload cnn` measures the
@@ -20,7 +20,10 @@ margin rows; alpha-CROWN 30 iterations at Luna's default lr 0.5).  `--workload
 resnet` measures the small CIFAR ResNet (stem conv3->16 k3, residual blocks
 16, 16, 32 s2 with a 1x1 projection skip, 32, BatchNorm with running mean 0,
 flatten 8192 -> 100 -> Sigmoid -> 10, seed 3; 128 boxes per GPU, eps 1/255;
-alpha-CROWN 50 iterations at lr 0.5).
+alpha-CROWN 50 iterations at lr 0.5).  `--workload property` bounds 512
+sub-domains of one VNN-LIB robustness property on the MLP through
+lb200_compute_property, with the property's thresholds stopping verified
+boxes early (one GPU; see the workload's description).
 """
 from __future__ import annotations
 
@@ -58,6 +61,13 @@ WORKLOADS = {
                   desc="cnn_convt_cifar sub-domain sweep (one eps 8/255 box split into 65,536 sub-domains along "
                        "16 groups of 4 widest-gradient pixels), {b} sub-domains per GPU, alpha-CROWN (50 Adam "
                        "iterations, lr 0.5), 9 margin specs"),
+    "property": dict(name="property", gen=W.mlp_property_boxes, boxes=512, iters=20, lr=0.1, input_dim=784,
+                     property=True,
+                     desc="VNN-LIB robustness property on mlp_784_256x4_10 (one eps 0.00317 box around a seeded "
+                          "point, OR over the 9 margins of the predicted label), split into {b} sub-domains along "
+                          "9 groups of 8 widest-gradient pixels; alpha-CROWN (20 Adam iterations, lr 0.1) with "
+                          "the property's thresholds, so boxes stop when verified (STOP_CROWN/ALPHA_ON_VERIFIED); "
+                          "bounds and verdicts through lb200_compute_property with host buffers"),
     "resnet": dict(name="resnet", gen=W.resnet_cifar, boxes=128, iters=50, lr=0.5, input_dim=3072,
                    desc="resnet_cifar 3x32x32 stem16 + 4 residual blocks (16,16,32s2+proj,32) with BatchNorm, "
                         "fc100-Sigmoid-fc10 alpha-CROWN (50 Adam iterations, lr 0.5), {b} boxes per GPU, "
@@ -300,6 +310,78 @@ def run_engine(args):
         dist.destroy_process_group()
 
 
+def run_property(args):
+    """The property workload: one GPU, every step one lb200_compute_property
+    call on the sub-domains (host buffers in and out, so the step is end to
+    end; the call returns once its stream is idle)."""
+    import torch
+
+    from luna_b200.build import build
+    from luna_b200.engine import Model
+    from luna_b200.vnnlib import Property
+
+    if int(os.environ.get("WORLD_SIZE", "1")) != 1 or args.gpus != 1:
+        raise SystemExit("--workload property runs on one GPU")
+    torch.cuda.set_device(0)
+    build()
+    g, bx = WL["gen"](BOXES_PER_GPU)
+    _, _, text = W.mlp_property_split()
+    prop = Property(text, WL["input_dim"], 10)
+    model = Model(g, device=0, options=options())
+    xl = np.ascontiguousarray(bx.lower)
+    xu = np.ascontiguousarray(bx.upper)
+    B = bx.n
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+    for _ in range(args.warmup):
+        model.compute_property(prop, abi.METHOD_ALPHA_CROWN, xl, xu)
+    torch.cuda.synchronize()
+    model.set_profiling(True)
+    sampler = ClockSampler(0)
+    sampler.start()
+    total_s, launches, contr_ms, contr_flops, contr_launches, iters = 0.0, 0, 0.0, 0.0, 0, 0
+    for _ in range(args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        lb, ub, status = model.compute_property(prop, abi.METHOD_ALPHA_CROWN, xl, xu)
+        total_s += time.perf_counter() - t0
+        st = model.last_stats
+        launches += st.kernel_launches
+        contr_ms += st.ms_contractions
+        contr_flops += st.contraction_flops
+        contr_launches += st.contraction_launches
+        iters = max(iters, st.alpha_iterations_run)
+    clocks = sampler.stop()
+    model.set_profiling(False)
+    s_per_step = total_s / args.steps
+    pk, pk_src = peaks()
+    peak = pk["bf16_tflops_sustained"] / 2.0 / 3.0
+    achieved = (contr_flops / contr_launches) / (contr_ms / contr_launches) / 1e9 if contr_launches else 0.0
+    counts = {abi.STATUS_NAMES[k]: int((status == k).sum()) for k in abi.STATUS_NAMES}
+    cfg = config(1)
+    cfg.update(nspec=prop.nspec, or_branches=prop.n_branches, verdicts=counts, alpha_iterations_run=iters,
+               timing="wall clock around each synchronous host-buffer call (no device-resident entry point "
+                      "takes OR branches), so value and e2e are the same measurement")
+    line = {
+        "metric": METRIC, "value": B / s_per_step, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * s_per_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded He-normal weights, seeded box centre)",
+        "config": cfg,
+        "e2e": {"value": B / s_per_step, "unit": UNIT, "h2d_bytes_per_step": int(xl.nbytes + xu.nbytes),
+                "d2h_bytes_per_step": int(lb.nbytes + ub.nbytes + status.nbytes)},
+        "gpu_launches": int(launches),
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak if peak else None, "traffic": None,
+                     "kernel": "A.W contraction (GEMM + fused relaxation / concretisation / adjoint epilogue)",
+                     "peak_source": f"{pk_src}: bf16_tflops_sustained / 2 (TF32) / 3 (3-pass split)",
+                     "contraction_share_of_step": contr_ms / (1e3 * total_s) if total_s else None},
+        "clocks": clocks,
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_boxes)
+    print(json.dumps(line), flush=True)
+
+
 # ---------------------------------------------------------------- reference arm
 _REF = {}
 
@@ -322,6 +404,17 @@ def _ref_worker(task):
     if b <= a:
         return 0.0
     g, bx = _REF["work"]
+    if WL.get("property"):
+        # Luna's CLI flow: the property's constraints set on the model, so
+        # its thresholds stop verified boxes early.
+        if "spec" not in _REF:
+            _, _, text = W.mlp_property_split()
+            _REF["spec"] = _REF["lib"].vnnlib_parse(text, WL["input_dim"], 10)
+        sub = bx.slice(a, b)
+        t0 = time.perf_counter()
+        _REF["lib"].compute_property(g, _REF["spec"], sub.lower, sub.upper, abi.METHOD_ALPHA_CROWN, options(),
+                                     num_threads=1)
+        return time.perf_counter() - t0
     t0 = time.perf_counter()
     _REF["lib"].compute_bounds(g, bx.slice(a, b), abi.METHOD_ALPHA_CROWN, options(), num_threads=1)
     return time.perf_counter() - t0
@@ -414,6 +507,8 @@ def main():
     globals()["BOXES_PER_GPU"] = args.boxes if args.boxes else WL["boxes"]
     if args.impl == "reference":
         run_reference(args)
+    elif WL.get("property"):
+        run_property(args)
     else:
         run_engine(args)
 

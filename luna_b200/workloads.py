@@ -502,3 +502,45 @@ def convt_sweep_boxes(n_boxes: int, seed: int = 5):
         _SWEEP[seed] = convt_sweep(seed)
     g, split = _SWEEP[seed]
     return g, split.boxes(0, n_boxes)
+
+
+def robustness_property(lower, upper, label: int, n_out: int) -> str:
+    """VNN-LIB text of a local robustness property: the box [lower, upper] and
+    the counterexample "some output j != label scores at least as high as
+    the label" (an OR over j of Y_label - Y_j <= 0)."""
+    lines = [f"; robustness of output {label} on a box of {len(lower)} inputs"]
+    lines += [f"(declare-const X_{k} Real)" for k in range(len(lower))]
+    lines += [f"(declare-const Y_{k} Real)" for k in range(n_out)]
+    for k, (a, b) in enumerate(zip(lower, upper)):
+        lines.append(f"(assert (>= X_{k} {float(a):.9g}))")
+        lines.append(f"(assert (<= X_{k} {float(b):.9g}))")
+    branches = " ".join(f"(and (<= (- Y_{label} Y_{j}) 0))" for j in range(n_out) if j != label)
+    lines.append(f"(assert (or {branches}))")
+    return "\n".join(lines) + "\n"
+
+
+_PROPERTY = {}
+
+
+def mlp_property_split(seed: int = 21, eps: float = 0.00317, n_groups: int = 9, group_size: int = 8):
+    """The MLP 784->256x4->10 (seed 1) and a robustness property around one
+    seeded point: the box centre U[0,1]^784, eps clipped to [0, 1], the label
+    the network's own prediction at the centre; the box is split into
+    2^n_groups sub-domains along its widest-gradient pixels
+    (subdomain_split).  Returns (graph, split, property text)."""
+    key = (seed, eps, n_groups, group_size)
+    if key not in _PROPERTY:
+        import torch
+        g = mlp([784, 256, 256, 256, 256, 10], 1)
+        split = subdomain_split(g, seed, eps, n_groups, group_size, n_in_shape=(784,))
+        y = graph_forward(g, torch.from_numpy(split.centre[None]))
+        t = int(y.argmax())
+        split.C = margin_spec(np.array([t]), 10)
+        _PROPERTY[key] = (g, split, robustness_property(split.lower, split.upper, t, 10))
+    return _PROPERTY[key]
+
+
+def mlp_property_boxes(n_boxes: int = 512, seed: int = 21):
+    """The first n_boxes sub-domains of mlp_property_split (C: the label's margins)."""
+    g, split, _ = mlp_property_split(seed)
+    return g, split.boxes(0, n_boxes)

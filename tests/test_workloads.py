@@ -37,3 +37,23 @@ def test_widest_gradient_pixels_rank_first():
     chosen = score[sp.groups.ravel()]
     rest = np.delete(score, sp.groups.ravel())
     assert chosen.min() >= rest.max() - 1e-6
+
+
+def test_property_workload_split():
+    """The property workload: 512 sub-domains inside the property's box, the
+    property's label the network's prediction at the centre, and the text
+    reads back as that box with 9 OR branches."""
+    import torch
+
+    from luna_b200.vnnlib import Property
+    g, split, text = W.mlp_property_split()
+    bx = split.boxes(0, 512)
+    assert bx.n == 512
+    assert (bx.lower >= split.lower).all() and (bx.upper <= split.upper).all()
+    assert (bx.lower <= bx.upper).all()
+    t = int(W.graph_forward(g, torch.from_numpy(split.centre[None])).argmax())
+    assert (split.C[0][:, t] == 1).all()
+    p = Property(text, 784, 10)
+    assert p.n_branches == 9 and p.nspec == 9
+    assert (p.lower == split.lower).all() and (p.upper == split.upper).all()
+    assert (p.C == split.C[0]).all() and (p.thresholds == 0).all()
