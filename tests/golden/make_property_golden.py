@@ -69,6 +69,13 @@ def cases():
         ("prop_mlp784_conj_alpha", "mlp_784_256x4_10", {"n_boxes": 4}, 4, abi.METHOD_ALPHA_CROWN,
          {"alpha_lr": 0.1}, "conj", 0.5),
         ("prop_mlp5_none_crown", "mlp_5_50x6_5", {"n_boxes": 4}, 4, abi.METHOD_CROWN, {}, "none", 0.0),
+        # Conv paths: dense starts, a patches start, residual joins.
+        ("prop_cnn_or_alpha", "small_cnn_case", {"seed": 3, "n_boxes": 6, "big_first": False}, 6,
+         abi.METHOD_ALPHA_CROWN, {"alpha_lr": 0.1, "alpha_iterations": 8}, "or", 0.4),
+        ("prop_cnnpatch_conj_alpha", "small_cnn_case", {"seed": 5, "n_boxes": 4, "big_first": True}, 4,
+         abi.METHOD_ALPHA_CROWN, {"alpha_lr": 0.1, "alpha_iterations": 5}, "conj", 0.5),
+        ("prop_resnet_or_alpha", "small_resnet_case", {"seed": 7, "n_boxes": 4}, 4, abi.METHOD_ALPHA_CROWN,
+         {"alpha_lr": 0.1, "alpha_iterations": 6}, "or", 0.5),
     ]
 
 
