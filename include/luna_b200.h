@@ -335,6 +335,17 @@ LB200_API int lb200_compute_property(lb200_model* model, int method, const lb200
                                      const float* x_lower, const float* x_upper, int64_t n_boxes,
                                      float* out_lb, float* out_ub, int32_t* status, lb200_stats* stats);
 
+/* As lb200_compute_property with the boxes and the results in device memory
+ * of the model's GPU (d_x_lower, d_x_upper [n_boxes, n_in]; d_out_lb,
+ * d_out_ub [n_boxes, rows]; d_status [n_boxes] or NULL); the property's
+ * specification is copied to the device on each call.  The work is ordered
+ * on `stream` (a cudaStream_t, or NULL for the legacy default stream) and
+ * the call returns once it has completed. */
+LB200_API int lb200_compute_property_device(lb200_model* model, int method, const lb200_property* prop,
+                                            const float* d_x_lower, const float* d_x_upper, int64_t n_boxes,
+                                            float* d_out_lb, float* d_out_ub, int32_t* d_status, void* stream,
+                                            lb200_stats* stats);
+
 /* Copy the last error message of this thread into buf (always terminated). */
 LB200_API int lb200_last_error(char* buf, size_t len);
 

@@ -571,6 +571,45 @@ void check_branches(const int32_t* branch, int64_t nspec, int32_t n_branches) {
                                         std::to_string(n_branches) + ")");
 }
 
+// The property's specification on the model's device, ordered on s: C
+// [rows, n_out] (the identity when the property has none, as Luna's
+// OutputConstraintSet::identityC), and with a specification its thresholds
+// and the branch of each row.
+struct DeviceSpec {
+    float* C = nullptr;
+    float* thr = nullptr;
+    int32_t* branch = nullptr;
+    int64_t rows = 0;
+};
+
+DeviceSpec stage_spec(lb200::Model& m, const lb200_property* prop, cudaStream_t s) {
+    if (prop->n_in != m.n_in() || prop->n_out != m.n_out())
+        throw std::invalid_argument("the property was parsed for " + std::to_string(prop->n_in) + " inputs / " +
+                                    std::to_string(prop->n_out) + " outputs, the model has " +
+                                    std::to_string(m.n_in()) + " / " + std::to_string(m.n_out()));
+    const bool spec = prop->nspec > 0;
+    const int64_t nout = m.n_out();
+    DeviceSpec d;
+    d.rows = spec ? prop->nspec : nout;
+    d.C = m.staging("io_C", (size_t)d.rows * nout);
+    std::vector<float> eye;
+    const float* C = prop->C.data();
+    if (!spec) {
+        eye.assign((size_t)nout * nout, 0.f);
+        for (int64_t k = 0; k < nout; ++k) eye[(size_t)(k * nout + k)] = 1.f;
+        C = eye.data();
+    }
+    // Pageable sources: each copy has left the host buffer when it returns.
+    LB_CUDA(cudaMemcpyAsync(d.C, C, (size_t)d.rows * nout * 4, cudaMemcpyHostToDevice, s));
+    if (spec) {
+        d.thr = m.staging("io_thr", (size_t)d.rows);
+        d.branch = reinterpret_cast<int32_t*>(m.staging("io_branch", (size_t)d.rows));
+        LB_CUDA(cudaMemcpyAsync(d.thr, prop->thr.data(), d.rows * 4, cudaMemcpyHostToDevice, s));
+        LB_CUDA(cudaMemcpyAsync(d.branch, prop->branch.data(), d.rows * 4, cudaMemcpyHostToDevice, s));
+    }
+    return d;
+}
+
 template <class F>
 int guard(F&& f) {
     try {
@@ -700,61 +739,60 @@ int lb200_compute_property(lb200_model* model, int method, const lb200_property*
     if (n_boxes > 0 && (!out_lb || !out_ub)) return lb200::set_last_error("lb200_compute_property: null buffer");
     return guard([&] {
         lb200::Model& m = *model->m;
-        if (prop->n_in != m.n_in() || prop->n_out != m.n_out())
-            throw std::invalid_argument("lb200_compute_property: the property was parsed for " +
-                                        std::to_string(prop->n_in) + " inputs / " + std::to_string(prop->n_out) +
-                                        " outputs, the model has " + std::to_string(m.n_in()) + " / " +
-                                        std::to_string(m.n_out()));
+        LB_CUDA(cudaSetDevice(m.device()));
+        cudaStream_t s = model->stream;
+        const DeviceSpec d = stage_spec(m, prop, s);
         if (n_boxes == 0) return;
         const float* xl = x_lower ? x_lower : prop->lower.data();
         const float* xu = x_upper ? x_upper : prop->upper.data();
         const bool spec = prop->nspec > 0;
-        const int64_t nout = m.n_out();
-        const int64_t rows = spec ? prop->nspec : nout;
-        LB_CUDA(cudaSetDevice(m.device()));
-        cudaStream_t s = model->stream;
         const size_t nx = (size_t)n_boxes * m.n_in();
-        const size_t no = (size_t)n_boxes * rows;
+        const size_t no = (size_t)n_boxes * d.rows;
         float* dxl = m.staging("io_xl", nx);
         float* dxu = m.staging("io_xu", nx);
-        float* dC = m.staging("io_C", (size_t)rows * nout);
         float* dlb = m.staging("io_lb", no);
         float* dub = m.staging("io_ub", no);
         LB_CUDA(cudaMemcpyAsync(dxl, xl, nx * 4, cudaMemcpyHostToDevice, s));
         LB_CUDA(cudaMemcpyAsync(dxu, xu, nx * 4, cudaMemcpyHostToDevice, s));
-        std::vector<float> eye;
-        const float* C = prop->C.data();
-        if (!spec) {
-            // No specification: bounds of every output (the identity C,
-            // OutputConstraintSet::identityC).
-            eye.assign((size_t)nout * nout, 0.f);
-            for (int64_t k = 0; k < nout; ++k) eye[(size_t)(k * nout + k)] = 1.f;
-            C = eye.data();
-        }
-        LB_CUDA(cudaMemcpyAsync(dC, C, (size_t)rows * nout * 4, cudaMemcpyHostToDevice, s));
-        float* dthr = nullptr;
-        int32_t* dbr = nullptr;
-        int32_t* dst = nullptr;
-        if (spec) {
-            dthr = m.staging("io_thr", (size_t)rows);
-            dbr = reinterpret_cast<int32_t*>(m.staging("io_branch", (size_t)rows));
-            LB_CUDA(cudaMemcpyAsync(dthr, prop->thr.data(), rows * 4, cudaMemcpyHostToDevice, s));
-            LB_CUDA(cudaMemcpyAsync(dbr, prop->branch.data(), rows * 4, cudaMemcpyHostToDevice, s));
-            if (status) dst = reinterpret_cast<int32_t*>(m.staging("io_status", (size_t)n_boxes));
-        }
+        int32_t* dst = (spec && status) ? reinterpret_cast<int32_t*>(m.staging("io_status", (size_t)n_boxes)) : nullptr;
         // Luna's CLI calls compute_bounds(..., COMPUTE_LOWER, COMPUTE_UPPER),
         // both on by default.
-        m.compute(method, dxl, dxu, n_boxes, dC, 1, rows, dthr, true, true, dlb, dub, s, stats, dbr,
+        m.compute(method, dxl, dxu, n_boxes, d.C, 1, d.rows, d.thr, true, true, dlb, dub, s, stats, d.branch,
                   prop->n_branches);
         LB_CUDA(cudaMemcpyAsync(out_lb, dlb, no * 4, cudaMemcpyDeviceToHost, s));
         LB_CUDA(cudaMemcpyAsync(out_ub, dub, no * 4, cudaMemcpyDeviceToHost, s));
         if (dst) {
-            launch_status(dlb, dub, n_boxes, rows, dthr, dbr, prop->n_branches, dst, s);
+            launch_status(dlb, dub, n_boxes, d.rows, d.thr, d.branch, prop->n_branches, dst, s);
             LB_CUDA(cudaMemcpyAsync(status, dst, (size_t)n_boxes * 4, cudaMemcpyDeviceToHost, s));
         }
         LB_CUDA(cudaStreamSynchronize(s));
         if (status && !spec)
             for (int64_t b = 0; b < n_boxes; ++b) status[b] = LB200_STATUS_UNKNOWN;
+    });
+}
+
+int lb200_compute_property_device(lb200_model* model, int method, const lb200_property* prop,
+                                  const float* d_x_lower, const float* d_x_upper, int64_t n_boxes, float* d_out_lb,
+                                  float* d_out_ub, int32_t* d_status, void* stream, lb200_stats* stats) {
+    if (!model || !prop) return lb200::set_last_error("lb200_compute_property_device: null model or property");
+    if (n_boxes < 0) return lb200::set_last_error("lb200_compute_property_device: bad sizes");
+    if (n_boxes > 0 && (!d_x_lower || !d_x_upper || !d_out_lb || !d_out_ub))
+        return lb200::set_last_error("lb200_compute_property_device: null buffer");
+    return guard([&] {
+        lb200::Model& m = *model->m;
+        LB_CUDA(cudaSetDevice(m.device()));
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        const DeviceSpec d = stage_spec(m, prop, s);
+        if (n_boxes == 0) return;
+        m.compute(method, d_x_lower, d_x_upper, n_boxes, d.C, 1, d.rows, d.thr, true, true, d_out_lb, d_out_ub, s,
+                  stats, d.branch, prop->n_branches);
+        if (d_status) {
+            if (prop->nspec > 0)
+                launch_status(d_out_lb, d_out_ub, n_boxes, d.rows, d.thr, d.branch, prop->n_branches, d_status, s);
+            else
+                LB_CUDA(cudaMemsetAsync(d_status, 0, (size_t)n_boxes * 4, s));  // LB200_STATUS_UNKNOWN
+        }
+        LB_CUDA(cudaStreamSynchronize(s));
     });
 }
 

@@ -27,7 +27,7 @@ EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_shard_range", "lb200_nccl_unique_id", "lb200_nccl_comm_create", "lb200_nccl_comm_destroy",
            "lb200_shard_run", "lb200_describe_plan", "lb200_property_parse", "lb200_property_get_info",
            "lb200_property_input_box", "lb200_property_spec", "lb200_property_free", "lb200_property_status",
-           "lb200_property_status_device", "lb200_compute_property")
+           "lb200_property_status_device", "lb200_compute_property", "lb200_compute_property_device")
 
 
 class EngineError(RuntimeError):
@@ -81,6 +81,8 @@ def load_library():
     lib.lb200_property_status.argtypes = [fp, fp, C.c_int64, C.c_int64, fp, ip, C.c_int32, ip]
     lib.lb200_property_status_device.argtypes = [vp, vp, C.c_int64, C.c_int64, vp, vp, C.c_int32, vp, vp]
     lib.lb200_compute_property.argtypes = [vp, C.c_int, vp, fp, fp, C.c_int64, fp, fp, ip, C.POINTER(Stats)]
+    lib.lb200_compute_property_device.argtypes = [vp, C.c_int, vp, vp, vp, C.c_int64, vp, vp, vp, vp,
+                                                  C.POINTER(Stats)]
     _lib = lib
     return lib
 
@@ -212,6 +214,17 @@ class Model:
                "lb200_compute_property")
         self.last_stats = st
         return lb, ub, status
+
+    def compute_property_ptr(self, prop, method: int, xl: int, xu: int, n_boxes: int, lb: int, ub: int,
+                             status: int = 0, stream: int = 0):
+        """Device-pointer variant of compute_property (pointers as ints, e.g.
+        torch data_ptr()); status may be 0 (no verdicts)."""
+        st = Stats()
+        _check(_lib.lb200_compute_property_device(self._h, method, prop.handle, xl, xu, n_boxes, lb, ub,
+                                                  status or None, stream or None, C.byref(st)),
+               "lb200_compute_property_device")
+        self.last_stats = st
+        return st
 
     def shard_run(self, comm: NcclComm, boxes, method: int, timeout_ms: int = 60000):
         """Bound this rank's share of `boxes` and all-gather every rank's

@@ -105,3 +105,56 @@ def test_status_device_matches_host():
         assert (dev.cpu().numpy() == host).all()
         seen |= set(host.tolist())
     assert seen == {abi.STATUS_UNKNOWN, abi.STATUS_UNSAT, abi.STATUS_SAT}
+
+
+def test_verdicts_sound_by_sampling():
+    """Verdicts hold on sampled points: in a box called UNSAT no point is a
+    counterexample, in a box called SAT every point is one, and every sampled
+    margin lies within the box's bounds."""
+    from luna_b200 import workloads as W
+    g, split, text = W.mlp_property_split()
+    bx = split.boxes(0, 64)
+    t = int(np.argmax(split.C[0].sum(0)))  # the label: its column is +1 in every row
+    # The same box with the label's worst rival as the label: SAT.
+    y0 = W.graph_forward(g, torch.from_numpy(split.centre[None])).detach().numpy()[0]
+    worst = int(np.argmin(y0))
+    text_sat = W.robustness_property(split.lower, split.upper, worst, 10)
+    m = Model(g, options=abi.default_options(alpha_lr=0.1, alpha_iterations=20))
+    rng = np.random.default_rng(0)
+    seen = set()
+    for txt, label in ((text, t), (text_sat, worst)):
+        prop = Property(txt, 784, 10)
+        lb, ub, status = m.compute_property(prop, abi.METHOD_ALPHA_CROWN, bx.lower, bx.upper)
+        for b in range(0, 64, 4):
+            u = rng.random((4000, 784), dtype=np.float32)
+            x = bx.lower[b] + u * (bx.upper[b] - bx.lower[b])
+            y = W.graph_forward(g, torch.from_numpy(x)).detach().numpy()
+            margins = (y @ prop.C.T).astype(np.float64)   # rows Y_label - Y_j
+            assert (margins >= lb[b] - 1e-4).all() and (margins <= ub[b] + 1e-4).all()
+            counterexample = (margins <= prop.thresholds).any(axis=1)   # OR of single-row branches
+            if status[b] == abi.STATUS_UNSAT:
+                assert not counterexample.any()
+            elif status[b] == abi.STATUS_SAT:
+                assert counterexample.all()
+            seen.add(int(status[b]))
+    assert {abi.STATUS_UNSAT, abi.STATUS_SAT} <= seen
+
+
+def test_property_device_entry_matches_host_entry():
+    """lb200_compute_property_device on device buffers gives the host entry's
+    bounds and verdicts bit for bit."""
+    c = G.load_prop("prop_mlp5_or_alpha")
+    prop = Property(c["text"], c["lower"].shape[1], 5)
+    m = Model(c["graph"], options=c["options"])
+    lb, ub, status = m.compute_property(prop, c["method"], c["lower"], c["upper"])
+    B = lb.shape[0]
+    xl = torch.from_numpy(c["lower"]).cuda()
+    xu = torch.from_numpy(c["upper"]).cuda()
+    dlb = torch.empty((B, prop.nspec), device="cuda")
+    dub = torch.empty_like(dlb)
+    dst = torch.empty(B, dtype=torch.int32, device="cuda")
+    m.compute_property_ptr(prop, c["method"], xl.data_ptr(), xu.data_ptr(), B, dlb.data_ptr(), dub.data_ptr(),
+                           dst.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert np.array_equal(dlb.cpu().numpy(), lb) and np.array_equal(dub.cpu().numpy(), ub)
+    assert np.array_equal(dst.cpu().numpy(), status)
