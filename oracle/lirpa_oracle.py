@@ -687,13 +687,39 @@ class LirpaOracle:
             lo, hi = self._run(st, x, C)
         return lo, hi, st
 
-    def alpha_crown(self, xl, xu, C, trace=None):
+    @staticmethod
+    def verified(lb, spec) -> bool:
+        """TorchModel::isSpecVerified (src/engine/TorchModel.cpp:616-651) from
+        the lower bounds: spec = (thresholds, branch of each row, n_branches);
+        a conjunction (n_branches 0) is broken by one row with lb - thr > 0,
+        a disjunction needs such a row in every branch
+        (OutputConstraintSet::evaluateORBranches, OutputConstraint.cpp:187-278)."""
+        thr, branch, nb = spec
+        d = (lb.reshape(-1) - thr.reshape(-1)) > 0
+        if nb <= 0:
+            return bool(d.any())
+        return all(bool(d[torch.as_tensor(branch) == b].any()) for b in range(nb))
+
+    def alpha_crown(self, xl, xu, C, trace=None, spec=None):
         """TorchModel::runAlphaCROWN (src/engine/TorchModel.cpp:798-893) with
         AlphaCROWNAnalysis::computeOptimizedBounds(Lower)
         (src/engine/AlphaCROWNAnalysis.cpp:306-511) for the lower side and
-        runCROWN on the same nodes for the upper side."""
+        runCROWN on the same nodes for the upper side.  With `spec`
+        (thresholds, branches, n_branches; see verified()) the early stops
+        apply: STOP_CROWN_ON_VERIFIED returns the CROWN initialisation pass's
+        bounds when they verify (TorchModel.cpp:816-834), and
+        STOP_ALPHA_ON_VERIFIED ends the optimisation at the first iteration
+        whose bounds verify, after taking them into the best bound
+        (AlphaCROWNAnalysis.cpp:394-407)."""
         o = self.opt
         x = (torch.as_tensor(xl), torch.as_tensor(xu))
+        if spec is not None and o.stop_crown_on_verified:
+            # performCROWNInitializationPass (AlphaCROWNAnalysis.cpp:118-129):
+            # plain CROWN with the first-linear-IBP shortcut off.
+            lo0, hi0, st0 = self.crown(xl, xu, C, _BoxState(first_linear_ibp=False))
+            if self.verified(lo0, spec):
+                inter = {i: st0.node_bounds[i] for i in self.preact_ids if i in st0.node_bounds}
+                return lo0.detach(), hi0.detach(), inter
         st = _BoxState(method_alpha=True, first_linear_ibp=False)
         out = self.g.output_index
         # The CROWN initialisation pass (AlphaCROWNAnalysis.cpp:118-129) only
@@ -732,6 +758,9 @@ class LirpaOracle:
             cur = cur_l.detach()
             if trace is not None:
                 trace.append(cur.clone())
+            if spec is not None and o.stop_alpha_on_verified and self.verified(cur, spec):
+                best = cur.clone() if best is None else torch.max(best, cur)
+                break
             loss = None if last else -cur_l.sum()
             if best is None:
                 best = cur.clone()
@@ -814,6 +843,42 @@ class LirpaOracle:
                 idx = torch.as_tensor([i for i in improved_idx if i < cur.shape[1]], dtype=torch.long)
                 if idx.numel():
                     best_alpha[key][:, idx] = cur[:, idx]
+
+    def compute_property(self, lower, upper, C, thresholds, branches, n_branches, method):
+        """Luna's CLI flow for each box [B, n_in] against one specification
+        (C [nspec, n_out] with thresholds and OR branches): bounds with the
+        early stops, and the CLI's verdict (LunaMain.cpp:60-135).  Returns
+        lb, ub [B, nspec] and status [B] (0 unknown, 1 unsat, 2 sat)."""
+        has_spec = np.size(thresholds) > 0  # without one: raw output bounds, verdict unknown
+        spec = (torch.as_tensor(np.asarray(thresholds, np.float32)), np.asarray(branches), int(n_branches)) \
+            if has_spec else None
+        Ct = torch.from_numpy(np.ascontiguousarray(C, np.float32))
+        B = lower.shape[0]
+        lb = np.zeros((B, Ct.shape[0]), np.float32)
+        ub = np.zeros((B, Ct.shape[0]), np.float32)
+        status = np.zeros(B, np.int32)
+        thr = np.asarray(thresholds, np.float32)
+        for b in range(B):
+            xl = torch.from_numpy(np.ascontiguousarray(lower[b]))
+            xu = torch.from_numpy(np.ascontiguousarray(upper[b]))
+            if method == METHOD_ALPHA_CROWN:
+                lo, hi, _ = self.alpha_crown(xl, xu, Ct, spec=spec)
+            else:
+                lo, hi, _ = self.crown(xl, xu, Ct)
+            lb[b], ub[b] = lo.numpy(), hi.numpy()
+            if not has_spec:
+                continue
+            dl, du = lb[b] - thr > 0, ub[b] - thr <= 0
+            if n_branches <= 0:
+                status[b] = 1 if dl.any() else (2 if du.all() else 0)
+            else:
+                br = np.asarray(branches)
+                rows = [br == k for k in range(n_branches)]
+                if all(dl[r].any() for r in rows):
+                    status[b] = 1
+                elif any(r.any() and not (ub[b][r] - thr[r] > 0).any() for r in rows):
+                    status[b] = 2
+        return lb, ub, status
 
     def compute_bounds(self, boxes, method, intermediate=False):
         """Bound every box with a fresh state.  Returns lb, ub [B, nspec] (and

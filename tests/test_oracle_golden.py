@@ -52,3 +52,22 @@ def test_planted_error_is_caught():
     finally:
         LirpaOracle._upper = staticmethod(orig)
     assert G.excess(lb, c["lb"]) > 1.0 or G.excess(ub, c["ub"]) > 1.0
+
+
+@pytest.mark.parametrize("name", [n for n in G.prop_names() if "mlp5" in n or "rand" in n])
+def test_oracle_property_matches_luna(name):
+    """The oracle's early stops on verified boxes (thresholds from a VNN-LIB
+    property) against Luna's CLI flow on the same boxes."""
+    from luna_b200.vnnlib import Property
+    from oracle.lirpa_oracle import LirpaOracle
+    c = G.load_prop(name)
+    g = c["graph"]
+    n_out = int(np.prod(g.nodes[g.output_index].out_shape))
+    p = Property(c["text"], c["lower"].shape[1], n_out)
+    C = p.C if p.has_spec else np.eye(n_out, dtype=np.float32)
+    lb, ub, st = LirpaOracle(g, c["options"]).compute_property(c["lower"], c["upper"], C, p.thresholds, p.branches,
+                                                                p.n_branches, c["method"])
+    assert G.excess_scaled(lb, c["lb"], c["lb"], c["ub"]) <= 1.0
+    assert G.excess_scaled(ub, c["ub"], c["lb"], c["ub"]) <= 1.0
+    if p.has_spec:
+        assert st.tolist() == c["status"].tolist()
