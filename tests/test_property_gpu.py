@@ -158,3 +158,35 @@ def test_property_device_entry_matches_host_entry():
     torch.cuda.synchronize()
     assert np.array_equal(dlb.cpu().numpy(), lb) and np.array_equal(dub.cpu().numpy(), ub)
     assert np.array_equal(dst.cpu().numpy(), status)
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_property_matches_oracle_random(seed):
+    """Random MLPs and boxes, a margin property per seed (a conjunction for
+    even seeds, an OR for odd ones) with thresholds halfway between
+    neighbouring boxes' alpha-CROWN margins: the engine's early-stopped
+    bounds and verdicts against the CPU oracle's."""
+    from luna_b200 import workloads as W
+    from luna_b200.workloads import Boxes
+    from oracle.lirpa_oracle import LirpaOracle
+    g, bx = W.random_mlp_case(700 + seed, n_boxes=8, depth=2 + seed % 3, width=16)
+    n_in, n_out = bx.lower.shape[1], 4
+    rows = [j for j in range(1, n_out)]
+    C = np.zeros((len(rows), n_out), np.float32)
+    for r, j in enumerate(rows):
+        C[r, 0], C[r, j] = 1, -1
+    opt = abi.default_options(alpha_lr=0.3, alpha_iterations=10)
+    ora = LirpaOracle(g, opt)
+    lA, _ = ora.compute_bounds(Boxes(bx.lower, bx.upper, C[None]), abi.METHOD_ALPHA_CROWN)
+    srt = np.sort(lA, axis=0)
+    thr = (0.5 * (srt[3] + srt[4])).astype(np.float32)
+    cmps = [f"(<= (- Y_0 Y_{j}) {float(t):.9g})" for j, t in zip(rows, thr)]
+    text = "\n".join(f"(assert {c})" for c in cmps) if seed % 2 == 0 else \
+        "(assert (or " + " ".join(f"(and {c})" for c in cmps) + "))"
+    prop = Property(text, n_in, n_out)
+    assert prop.nspec == len(rows) and (prop.n_branches > 0) == (seed % 2 == 1)
+    olb, oub, ost = ora.compute_property(bx.lower, bx.upper, prop.C, prop.thresholds, prop.branches,
+                                         prop.n_branches, abi.METHOD_ALPHA_CROWN)
+    lb, ub, st = Model(g, options=opt).compute_property(prop, abi.METHOD_ALPHA_CROWN, bx.lower, bx.upper)
+    assert G.excess_scaled(lb, olb, olb, oub) <= 1.0 and G.excess_scaled(ub, oub, olb, oub) <= 1.0
+    assert st.tolist() == ost.tolist()
