@@ -205,16 +205,19 @@ LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 /* IBP bounds of n_boxes boxes without allocating any device memory, for
  * Linear/ReLU networks (models with convs, Sigmoid or Add are rejected): the
  * same result as lb200_compute_bounds_device(..., LB200_METHOD_IBP, ...),
- * for callers that cannot call cudaMalloc where they need bounds (inside a
- * stream capture, or under a memory manager that owns every allocation).
+ * for callers that cannot call cudaMalloc where they need bounds (a service
+ * that reserves its GPU memory up front and forbids allocation on the
+ * request path, or a host whose own memory manager owns every allocation).
  * The per-layer interval bounds live in a fixed 16 MiB __device__ array
  * held by every GPU that loads this library until the process exits;
  * batches needing more (n_boxes * 2 * sum of Linear output widths floats
- * above 4 Mi) are rejected with an error.  Work is enqueued on `stream` and
- * the call returns without waiting.  The first call on a device resolves the
- * array's address on that device: make it before any stream capture.  All
- * calls share the array, so calls that overlap on the GPU race and must be
- * serialised by the caller.  No counterpart in the reference. */
+ * above 4 Mi) are rejected with an error, as are n_boxes * nspec above
+ * 2^31 - 1.  Work is enqueued on `stream` (a stream of the model's device)
+ * and the call returns without waiting; the caller's current device is left
+ * as it was.  The first call on a device resolves the array's address on
+ * that device: make it before any stream capture.  All calls share the
+ * array, so calls that overlap on the GPU race and must be serialised by
+ * the caller.  No counterpart in the reference. */
 LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const float* d_x_lower,
                                        const float* d_x_upper, int64_t n_boxes, const float* d_C,
                                        int64_t c_boxes, int64_t nspec, float* d_out_lb,

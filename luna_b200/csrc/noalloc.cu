@@ -1,14 +1,15 @@
 // noalloc.cu -- interval (IBP) bounds with no device allocation.
 //
 // Some callers cannot allocate device memory at the point where they need
-// bounds: code that runs inside a stream capture (a graph being recorded
-// rejects cudaMalloc), services that reserve all of their GPU memory up
-// front and forbid allocation on the request path, or hosts whose memory
-// manager owns every allocation.  lb200_ibp_bounds_noalloc serves them: it
-// computes the same IBP bounds as lb200_compute_bounds_device(...,
-// LB200_METHOD_IBP, ...) but keeps the per-layer interval bounds in the
-// fixed array below instead of engine-allocated buffers.  The caller still
-// passes the input boxes, the specification and the output buffers.
+// bounds: services that reserve all of their GPU memory up front and forbid
+// allocation on the request path, hosts whose own memory manager owns every
+// allocation on the device (another framework's caching allocator), and
+// latency-critical loops that cannot afford cudaMalloc's implicit device
+// synchronisation.  lb200_ibp_bounds_noalloc serves them: it computes the
+// same IBP bounds as lb200_compute_bounds_device(..., LB200_METHOD_IBP, ...)
+// but keeps the per-layer interval bounds in the fixed array below instead
+// of engine-allocated buffers.  The caller still passes the input boxes, the
+// specification and the output buffers.
 //
 // The array is a file-scope __device__ variable: every GPU that loads this
 // library holds its 16 MiB until the process exits.  In host code its name
@@ -23,6 +24,7 @@
 #include "handle.h"
 #include "kernels.cuh"
 
+#include <climits>
 #include <mutex>
 #include <string>
 
@@ -63,6 +65,18 @@ extern "C" LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const floa
         return lb200::set_last_error("lb200_ibp_bounds_noalloc: c_boxes must be 1 or n_boxes");
     if (!d_x_lower || !d_x_upper || !d_C || !d_out_lb || !d_out_ub)
         return lb200::set_last_error("lb200_ibp_bounds_noalloc: null buffer");
+    // Sizes go to the kernels as int: keep n_boxes, nspec and their product in range.
+    if (n_boxes > INT_MAX || nspec > INT_MAX || nspec > INT_MAX / n_boxes)
+        return lb200::set_last_error("lb200_ibp_bounds_noalloc: n_boxes x nspec above 2^31 - 1");
+    int prev_dev = -1;
+    if (cudaGetDevice(&prev_dev) != cudaSuccess) prev_dev = -1;
+    // The caller's current device is put back on every return path.
+    struct Restore {
+        int dev;
+        ~Restore() {
+            if (dev >= 0) cudaSetDevice(dev);
+        }
+    } restore{prev_dev};
     try {
         const lb200::Model& m = *model->m;
         if (!m.is_relu_mlp())
@@ -71,10 +85,12 @@ extern "C" LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const floa
         const auto& L = m.layers();
         int64_t per_box = 0;
         for (const auto& layer : L) per_box += 2 * (int64_t)layer.n_out;
-        if (per_box * n_boxes > kScratchFloats)
+        // Compared by division: per_box * n_boxes may not fit in 64 bits.
+        if (n_boxes > kScratchFloats / per_box)
             return lb200::set_last_error(
                 "lb200_ibp_bounds_noalloc: " + std::to_string(n_boxes) + " boxes need " +
-                std::to_string(per_box * n_boxes) + " floats of scratch, above the fixed " +
+                (n_boxes <= INT64_MAX / per_box ? std::to_string(per_box * n_boxes) : std::string("> 2^63")) +
+                " floats of scratch, above the fixed " +
                 std::to_string(kScratchFloats) + " (at most " + std::to_string(kScratchFloats / per_box) +
                 " boxes for this network)");
         LB_CUDA(cudaSetDevice(m.device()));

@@ -3,7 +3,8 @@
 This module is the oracle: a plain PyTorch (fp32, CPU, autograd) restatement
 of the algorithm Luna runs for one input box, written from the reference's
 behaviour and checked against Luna itself (oracle/_ref, built by
-oracle/Makefile) in tests/test_oracle_vs_ref.py.  Only tests, smoke() and the
+oracle/Makefile) in tests/test_oracle_golden.py, over the fixtures that
+tests/golden/make_golden.py writes from Luna's outputs.  Only tests, smoke() and the
 bench's CPU-baseline leg import it; the product never does.
 
 Each function cites the Luna source (path within the Luna project) whose

@@ -6,7 +6,16 @@ the inputs and Luna's outputs are stored as .npz files.  Network weights are
 not stored: they are regenerated from the seeded generators in
 luna_b200/workloads.py, and a checksum of them is stored to catch drift.
 
-    make -C oracle && python tests/golden/make_golden.py [case names]
+    make -C oracle && python tests/golden/make_golden.py [--procs P] [case names]
+    python tests/golden/make_golden.py --part K N case   # boxes of part K of N only
+    python tests/golden/make_golden.py --merge N case    # assemble the N parts
+
+Large cases run Luna on several host processes (one box range and one ATen
+thread per process, as the CPU baseline does); their boxes are regenerated
+from the seeded generator too and only a checksum is stored.  A case whose
+Luna processes need too much host memory to run side by side is made in
+parts (separate invocations, one box range each, results kept under
+oracle/_ref/parts/) and then merged.
 """
 from __future__ import annotations
 
@@ -32,6 +41,18 @@ def weights_digest(graph) -> str:
             if a is not None:
                 h.update(np.ascontiguousarray(a, np.float32).tobytes())
     return h.hexdigest()
+
+
+def boxes_digest(bx) -> str:
+    h = hashlib.sha256()
+    for a in (bx.lower, bx.upper, bx.C):
+        h.update(np.ascontiguousarray(a, np.float32).tobytes())
+    return h.hexdigest()
+
+
+# Cases whose boxes are regenerated rather than stored, and that carry no
+# intermediate bounds (their size would dominate the fixture directory).
+LARGE = {"cfg2_alpha512", "cfg3_alpha"}
 
 
 def cases():
@@ -97,6 +118,14 @@ def cases():
                 3, abi.METHOD_CROWN, {}))
     # The CIFAR-shaped CNN at full size, one box.
     out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
+    # The MLP alpha-CROWN workload at its own size: all 512 boxes, 20 Adam
+    # iterations at lr 0.1.
+    out.append(("cfg2_alpha512", "mlp_784_256x4_10", {"n_boxes": 512}, 512, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 20}))
+    # The CIFAR CNN alpha-CROWN workload (30 Adam iterations at Luna's default
+    # lr 0.5), the first 4 of its 256 boxes.
+    out.append(("cfg3_alpha", "cnn_cifar", {"n_boxes": 256}, 4, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.5, "alpha_iterations": 30}))
     return out
 
 
@@ -109,24 +138,88 @@ def make_case(gen: str, kw: dict):
     return g, bx
 
 
-def main(only=()):
+_WORK = {}
+
+
+def _luna_range(task):
+    """One host process: Luna on boxes [a, b) of a case, one ATen thread."""
+    gen, kw, a, b, method, over = task
+    key = (gen, repr(kw))
+    if _WORK.get("key") != key:
+        _WORK["case"] = make_case(gen, kw)
+        _WORK["key"] = key
+    g, bx = _WORK["case"]
+    return luna_ref.compute_bounds(g, bx.slice(a, b), method, abi.default_options(**over), num_threads=1)
+
+
+def run_luna(g, bx, gen, kw, nb, method, over, procs, intermediate):
+    if procs <= 1 or nb <= 1:
+        return luna_ref.compute_bounds(g, bx, method, abi.default_options(**over), intermediate=intermediate)
+    import multiprocessing as mp
+    p = min(procs, nb)
+    cuts = [nb * i // p for i in range(p + 1)]
+    tasks = [(gen, kw, cuts[i], cuts[i + 1], method, over) for i in range(p)]
+    with mp.get_context("spawn").Pool(p) as pool:
+        parts = pool.map(_luna_range, tasks, chunksize=1)
+    return np.concatenate([x[0] for x in parts]), np.concatenate([x[1] for x in parts])
+
+
+PARTS = os.path.join(ROOT, "oracle", "_ref", "parts")
+
+
+def part_path(name, k, n):
+    return os.path.join(PARTS, f"{name}.part{k}of{n}.npz")
+
+
+def main(only=(), procs=1, part=None, merge=0):
     for name, gen, kw, nb, method, over in cases():
         if only and name not in only:
             continue
         g, bx = make_case(gen, kw)
         bx = bx.slice(0, nb)
-        opt = abi.default_options(**over)
-        res = luna_ref.compute_bounds(g, bx, method, opt, intermediate=method != abi.METHOD_IBP)
-        payload = dict(lower=bx.lower, upper=bx.upper, C=bx.C, lb=res[0], ub=res[1],
-                       method=np.int32(method), generator=np.str_(gen),
+        large = name in LARGE
+        inter = method != abi.METHOD_IBP and not large
+        if part is not None:
+            k, n = part
+            a, b = nb * k // n, nb * (k + 1) // n
+            res = run_luna(g, bx.slice(a, b), gen, kw, b - a, method, over, procs, False)
+            os.makedirs(PARTS, exist_ok=True)
+            np.savez(part_path(name, k, n), lb=res[0], ub=res[1], box_range=np.array([a, b]))
+            print(name, f"part {k} of {n}: boxes [{a}, {b})", flush=True)
+            continue
+        if merge:
+            zs = [np.load(part_path(name, k, merge)) for k in range(merge)]
+            assert [int(z["box_range"][0]) for z in zs] == [nb * k // merge for k in range(merge)]
+            res = (np.concatenate([z["lb"] for z in zs]), np.concatenate([z["ub"] for z in zs]))
+        else:
+            res = run_luna(g, bx, gen, kw, nb, method, over, procs, inter)
+        payload = dict(lb=res[0], ub=res[1], method=np.int32(method), generator=np.str_(gen),
                        kwargs=np.str_(repr(kw)), options=np.str_(repr(over)),
                        weights_sha256=np.str_(weights_digest(g)))
-        if method != abi.METHOD_IBP:
+        if large:
+            payload.update(box_range=np.array([0, nb], np.int64), boxes_sha256=np.str_(boxes_digest(bx)))
+        else:
+            payload.update(lower=bx.lower, upper=bx.upper, C=bx.C)
+        if inter:
             payload["inter_lb"] = res[2]
             payload["inter_ub"] = res[3]
         np.savez_compressed(os.path.join(OUT, name + ".npz"), **payload)
-        print(name, res[0].shape, float(res[0].min()), float(res[1].max()))
+        print(name, res[0].shape, float(res[0].min()), float(res[1].max()), flush=True)
 
 
 if __name__ == "__main__":
-    main(tuple(sys.argv[1:]))
+    argv = list(sys.argv[1:])
+    procs, part, merge = 1, None, 0
+    if "--procs" in argv:
+        k = argv.index("--procs")
+        procs = int(argv[k + 1])
+        del argv[k:k + 2]
+    if "--part" in argv:
+        k = argv.index("--part")
+        part = (int(argv[k + 1]), int(argv[k + 2]))
+        del argv[k:k + 3]
+    if "--merge" in argv:
+        k = argv.index("--merge")
+        merge = int(argv[k + 1])
+        del argv[k:k + 2]
+    main(tuple(argv), procs, part, merge)

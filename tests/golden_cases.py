@@ -46,13 +46,28 @@ def _digest(graph) -> str:
     return h.hexdigest()
 
 
+def oracle_names():
+    """Oracle fixtures on full-size networks (make_oracle_golden.py)."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "oracle", "*.npz")))
+
+
 def load(name):
-    z = np.load(os.path.join(GOLDEN, name + ".npz"))
+    sub = "oracle" if name.startswith("oracle_") else ""
+    z = np.load(os.path.join(GOLDEN, sub, name + ".npz"))
     gen = str(z["generator"])
     kw = ast.literal_eval(str(z["kwargs"]))
-    g, _ = getattr(W, gen)(**kw)
+    g, gbx = getattr(W, gen)(**kw)
     assert _digest(g) == str(z["weights_sha256"]), f"{name}: regenerated weights differ"
-    boxes = Boxes(z["lower"], z["upper"], z["C"])
+    if "box_range" in z:
+        # Large cases store no boxes: they are regenerated and checked.
+        a, b = (int(v) for v in z["box_range"])
+        boxes = gbx.slice(a, b)
+        h = hashlib.sha256()
+        for arr in (boxes.lower, boxes.upper, boxes.C):
+            h.update(np.ascontiguousarray(arr, np.float32).tobytes())
+        assert h.hexdigest() == str(z["boxes_sha256"]), f"{name}: regenerated boxes differ"
+    else:
+        boxes = Boxes(z["lower"], z["upper"], z["C"])
     opt = abi.default_options(**ast.literal_eval(str(z["options"])))
     case = dict(graph=g, boxes=boxes, method=int(z["method"]), options=opt, lb=z["lb"], ub=z["ub"])
     if "inter_lb" in z:
@@ -68,6 +83,31 @@ def excess(ours, ref, rtol=RTOL, atol=ATOL):
     return float(np.max(np.abs(ours - ref) / (atol + rtol * np.abs(ref))))
 
 
+# Cases held to the interval-scaled bar (excess_scaled) instead of the strict
+# one, each with its measured strict excess and the reason.  Every other case
+# must meet the strict bar.
+LOOSE = {
+    # The CPU oracle keeps dense A matrices where Luna keeps patches; on this
+    # 12-channel 20x20 ResNet with patches starts its fp32 summation order
+    # differs enough to reach 1.161 of the strict bar (interval-scaled
+    # 0.063).  The engine itself meets the strict bar on the same case.
+    "oracle/resnetbig_crown": (1.161, "oracle dense-A summation order vs Luna's patches"),
+}
+
+
+def parity(name, lb, ub, ref_lb, ref_ub):
+    """Assert the parity bar on output bounds: strict (excess <= 1) unless
+    `name` is listed in LOOSE.  Prints both figures as a PARITY line."""
+    strict = max(excess(lb, ref_lb), excess(ub, ref_ub))
+    scaled = max(excess_scaled(lb, ref_lb, ref_lb, ref_ub), excess_scaled(ub, ref_ub, ref_lb, ref_ub))
+    print(f"PARITY {name} strict={strict:.4f} scaled={scaled:.4f}")
+    if name in LOOSE:
+        assert scaled <= 1.0, (name, strict, scaled)
+    else:
+        assert strict <= 1.0, (name, strict, scaled)
+    return strict
+
+
 def excess_scaled(ours, ref, lb_ref, ub_ref, rtol=RTOL, atol=ATOL):
     """excess() with the relative term taken against max(|ref|, ub_ref - lb_ref).
 
@@ -76,7 +116,7 @@ def excess_scaled(ours, ref, lb_ref, ub_ref, rtol=RTOL, atol=ATOL):
     of width ~1); its fp32 value then carries rounding of the size of the
     terms, which no reordering of the summation avoids: Luna's own CPU result
     moves by a third of the strict bar between 1 and 8 threads on such a
-    CNN case.  The strict bar (excess) is reported beside this one."""
+    CNN case.  Only the cases named in LOOSE are held to this bar."""
     ours = np.asarray(ours, np.float64)
     ref = np.asarray(ref, np.float64)
     w = np.abs(np.asarray(ub_ref, np.float64) - np.asarray(lb_ref, np.float64))

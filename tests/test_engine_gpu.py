@@ -37,13 +37,19 @@ def test_engine_matches_luna(name):
         assert e <= 1.0 and states, e
 
 
+@pytest.mark.parametrize("name", G.oracle_names())
+def test_engine_matches_oracle_full_size(name):
+    """Full-size networks of the ResNet and sweep workloads against the CPU
+    oracle's committed results (tests/golden/make_oracle_golden.py)."""
+    c = G.load(name)
+    lb, ub = Model(c["graph"], options=c["options"]).compute_bounds(c["boxes"], c["method"])
+    _assert_parity(name, lb, ub, c["lb"], c["ub"])
+
+
 def _assert_parity(name, lb, ub, ref_lb, ref_ub):
-    """Strict bar (1e-5 rel / 1e-6 abs) reported; the interval-scaled bar
-    (golden_cases.excess_scaled) asserted."""
-    strict = max(G.excess(lb, ref_lb), G.excess(ub, ref_ub))
-    scaled = max(G.excess_scaled(lb, ref_lb, ref_lb, ref_ub), G.excess_scaled(ub, ref_ub, ref_lb, ref_ub))
-    print(f"{name}: strict excess {strict:.3f} interval-scaled excess {scaled:.3f}")
-    assert scaled <= 1.0, (strict, scaled)
+    """The strict bar (1e-5 rel / 1e-6 abs), except for the cases that
+    golden_cases.LOOSE names with their reason."""
+    G.parity(name, lb, ub, ref_lb, ref_ub)
 
 
 @pytest.mark.parametrize("seed", range(4))
@@ -54,8 +60,7 @@ def test_engine_matches_oracle_random(seed, method):
     opt = abi.default_options(alpha_lr=0.3, alpha_iterations=6)
     lb, ub = Model(g, options=opt).compute_bounds(bx, method)
     olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
-    assert G.excess(lb, olb) <= 1.0
-    assert G.excess(ub, oub) <= 1.0
+    _assert_parity(f"mlp{seed}/{method}", lb, ub, olb, oub)
 
 
 @pytest.mark.parametrize("bn", [False, True])
@@ -84,9 +89,13 @@ def test_tc_conv_matches_simt_and_oracle(method):
     m.set_contraction_path(1)
     slb, sub = m.compute_bounds(bx, method)
     olb, oub = LirpaOracle(g, opt).compute_bounds(bx, method)
-    print(f"simt vs oracle: {G.excess_scaled(slb, olb, olb, oub):.3f} {G.excess_scaled(sub, oub, olb, oub):.3f}")
-    _assert_parity(f"tc vs simt/{method}", tlb, tub, slb, sub)
+    _assert_parity(f"simt vs oracle/{method}", slb, sub, olb, oub)
     _assert_parity(f"tc vs oracle/{method}", tlb, tub, olb, oub)
+    # The two engine paths, each within the bar of the oracle, differ by at
+    # most the sum of their allowances: twice the bar.
+    e = max(G.excess(tlb, slb, 2 * G.RTOL, 2 * G.ATOL), G.excess(tub, sub, 2 * G.RTOL, 2 * G.ATOL))
+    print(f"PARITY tc vs simt/{method} (2x bar) {e:.4f}")
+    assert e <= 1.0, e
 
 
 def _forward(graph, x):

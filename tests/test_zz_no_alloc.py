@@ -1,7 +1,8 @@
 """lb200_ibp_bounds_noalloc, the entry point for callers that cannot
-allocate device memory (inside a stream capture, or under a memory manager
-that owns all allocations): it must give the same IBP bounds as the
-allocating entry point, call after call, from its fixed scratch array.
+allocate device memory where they need bounds (a service that reserves its
+GPU memory up front, or a host whose memory manager owns all allocations):
+it must give the same IBP bounds as the allocating entry point, call after
+call, from its fixed scratch array.
 
 This file is collected last on purpose, so that a run stopping at the first
 failure has already run every other test; it also passes on its own."""
@@ -55,6 +56,14 @@ def test_no_alloc_rejects_batches_above_its_scratch():
     too_many = 3000  # 3000 boxes x 2 x 1034 floats > 4 Mi floats
     with pytest.raises(EngineError, match="scratch"):
         m.ibp_bounds_noalloc_ptr(xl.data_ptr(), xu.data_ptr(), too_many, Cm.data_ptr(), 1, 9,
+                                 out.data_ptr(), out.data_ptr())
+    # Sizes whose products overflow 32 or 64 bits are refused before any launch.
+    for n in (2 ** 31, (2 ** 63 - 1) // 2068 + 1, 2 ** 62):
+        with pytest.raises(EngineError, match="2\\^31|scratch"):
+            m.ibp_bounds_noalloc_ptr(xl.data_ptr(), xu.data_ptr(), n, Cm.data_ptr(), 1, 9,
+                                     out.data_ptr(), out.data_ptr())
+    with pytest.raises(EngineError, match="2\\^31"):
+        m.ibp_bounds_noalloc_ptr(xl.data_ptr(), xu.data_ptr(), 4, Cm.data_ptr(), 1, 2 ** 30,
                                  out.data_ptr(), out.data_ptr())
 
 
