@@ -77,8 +77,14 @@ enum {
  * and only read during lb200_model_create().  Kinds taken by this build:
  * INPUT, LINEAR, CONV, CONVTRANSPOSE, BATCHNORM (after a LINEAR / CONV),
  * RELU, SIGMOID (on flat layers), ADD (two tensor producers: residual joins
- * of a ReLU output, directly or through a CONV), FLATTEN, IDENTITY; other
- * graphs are rejected by lb200_model_create with a message. */
+ * of a ReLU output, directly or through a CONV), FLATTEN, IDENTITY,
+ * RESHAPE (to a flat vector, as Luna's Reshape flattens), SUB with a
+ * constant (on the input, or on a LINEAR / CONV output; a CONV's constant
+ * uniform per channel), SLICE of a flat vector (of a LINEAR output, or
+ * feeding LINEAR nodes), CONCAT along axis 1 of LINEAR outputs or of CONV
+ * outputs that read the same producer with the same geometry; each of the
+ * last four is rewritten into the same affine map over the kinds before it.
+ * Other graphs are rejected by lb200_model_create with a message. */
 typedef struct {
     int32_t type;          /* lb200_node_type */
     int32_t num_inputs;    /* number of producers (TorchModel dependencies) */
@@ -103,6 +109,20 @@ typedef struct {
     const float* running_mean;
     const float* running_var;
     float eps;
+    /* SUB with one producer (BoundedSubNode::setConstantValue,
+     * BoundedSubNode.h:54-57): constant [producer size] in Luna's flat (CHW)
+     * order; constant_second = 1 for x - constant, 0 for constant - x. */
+    const float* constant;
+    int32_t constant_second;
+    /* SLICE: BoundedSliceNode(start, end, axes, steps) (BoundedSliceNode.h:22)
+     * with ONNX's conventions (negative start / end count from the end,
+     * steps 1 or -1); CONCAT: BoundedConcatNode(axis, numInputs)
+     * (BoundedConcatNode.h:22).  Axis 1 is the feature axis of a flat vector
+     * or the channel axis of a (C, H, W) map. */
+    int32_t axis;
+    int64_t start;
+    int64_t end;
+    int64_t step;
 } lb200_node_desc;
 
 typedef struct {

@@ -58,6 +58,12 @@ class NodeDesc(C.Structure):
         ("running_mean", _fp),
         ("running_var", _fp),
         ("eps", C.c_float),
+        ("constant", _fp),
+        ("constant_second", C.c_int32),
+        ("axis", C.c_int32),
+        ("start", C.c_int64),
+        ("end", C.c_int64),
+        ("step", C.c_int64),
     ]
 
 
@@ -158,6 +164,14 @@ class Node:
     running_mean: np.ndarray | None = None
     running_var: np.ndarray | None = None
     eps: float = 1e-5
+    # SUB with a constant: x - constant (constant_second) or constant - x.
+    constant: np.ndarray | None = None
+    constant_second: int = 1
+    # SLICE (axis, start, end, step) and CONCAT (axis).
+    axis: int = 1
+    start: int = 0
+    end: int = 0
+    step: int = 1
 
     @property
     def size(self) -> int:
@@ -207,13 +221,18 @@ class Graph:
                 d.stride[k] = n.stride[k]
                 d.padding[k] = n.padding[k]
                 d.output_padding[k] = n.output_padding[k]
-            for name in ("running_mean", "running_var"):
+            for name in ("running_mean", "running_var", "constant"):
                 v = getattr(n, name)
                 if v is not None:
                     v = np.ascontiguousarray(v, dtype=np.float32)
                     keep.append(v)
                     setattr(d, name, fptr(v))
             d.eps = n.eps
+            d.constant_second = n.constant_second
+            d.axis = n.axis
+            d.start = n.start
+            d.end = n.end
+            d.step = n.step
         self._keep = [arr, keep]
         return GraphDesc(len(self.nodes), C.cast(arr, C.POINTER(NodeDesc)),
                          self.input_index, self.output_index)

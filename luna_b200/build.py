@@ -15,7 +15,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIBDIR = os.path.join(HERE, "_lib")
 LIB = os.path.join(LIBDIR, "libluna_b200.so")
 SOURCES = ["kernels.cu", "conv_kernels.cu", "tc_gemm.cu", "tc_conv.cu", "engine.cpp", "capi.cpp", "noalloc.cu",
-           "shard.cpp", "property.cu"]
+           "shard.cpp", "property.cu", "graph_canon.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -9,6 +9,7 @@
 // so each Linear step is a single GEMM whose epilogue applies the ReLU
 // relaxation of the box that owns the row.
 #include "engine.h"
+#include "graph_canon.h"
 #include "tc_gemm.cuh"
 
 #include <algorithm>
@@ -78,13 +79,18 @@ struct ValDesc {
 // (BoundedAddNode, two tensor operands), of skip edges from earlier levels
 // (the activation itself, or a conv of it); the output is a Linear of the
 // last level.  Flatten and Identity nodes pass through.
-Model::Model(const lb200_graph_desc* g, int device, bool on_device) : device_(device), on_device_(on_device) {
-    if (!g || g->num_nodes <= 0 || !g->nodes) throw std::invalid_argument("empty graph");
+Model::Model(const lb200_graph_desc* g_in, int device, bool on_device) : device_(device), on_device_(on_device) {
+    if (!g_in || g_in->num_nodes <= 0 || !g_in->nodes) throw std::invalid_argument("empty graph");
     if (on_device_) LB_CUDA(cudaSetDevice(device_));
+    // Reshape / Sub / Slice / Concat restated as the affine kinds below
+    // (graph_canon.h); nodes left without a path to the output are skipped.
+    const CanonGraph cg = canonicalize(g_in);
+    const lb200_graph_desc* g = &cg.desc;
     const int n = g->num_nodes;
     std::vector<std::vector<int>> dependents(n);
     std::vector<int> indeg(n, 0);
     for (int i = 0; i < n; ++i) {
+        if (cg.dead[i]) continue;
         const auto& d = g->nodes[i];
         if (d.num_inputs < 0 || d.num_inputs > 4) throw std::invalid_argument("bad num_inputs");
         for (int k = 0; k < d.num_inputs; ++k) {
@@ -100,14 +106,18 @@ Model::Model(const lb200_graph_desc* g, int device, bool on_device) : device_(de
     std::vector<int> order;
     {
         std::vector<int> q;
-        for (int i = 0; i < n; ++i)
+        int live = 0;
+        for (int i = 0; i < n; ++i) {
+            if (cg.dead[i]) continue;
+            ++live;
             if (indeg[i] == 0) q.push_back(i);
+        }
         for (size_t h = 0; h < q.size(); ++h) {
             order.push_back(q[h]);
             for (int d : dependents[q[h]])
                 if (--indeg[d] == 0) q.push_back(d);
         }
-        if ((int)order.size() != n) throw std::invalid_argument("graph has a cycle");
+        if ((int)order.size() != live) throw std::invalid_argument("graph has a cycle");
     }
     auto bad = [&](int i, const std::string& why) {
         throw std::invalid_argument("node " + std::to_string(i) + " (type " + std::to_string(g->nodes[i].type) +
@@ -289,6 +299,15 @@ Model::Model(const lb200_graph_desc* g, int device, bool on_device) : device_(de
     }
     build_geometry();
     lb200_options_default(&opt_);
+    if (cg.in_tf) {
+        in_tf_ = true;
+        in_neg_ = cg.in_neg;
+        if ((int)cg.in_const.size() != width(0)) throw std::invalid_argument("input Sub constant size");
+        if (on_device_) {
+            in_const_ = weights_.as<float>("in_const", cg.in_const.size());
+            LB_CUDA(cudaMemcpy(in_const_, cg.in_const.data(), cg.in_const.size() * 4, cudaMemcpyHostToDevice));
+        }
+    }
 }
 
 // One affine edge: the node's weight and bias with a following BatchNorm
@@ -1505,6 +1524,15 @@ void Model::init_alpha(StartPlan& sp, int m, int B, cudaStream_t s) {
 // ------------------------------------------------------------ one chunk
 void Model::run_chunk(int method, const float* xl, const float* xu, int B, const float* C,
                       int c_per_box, int nspec, bool upper, float* lb, float* ub, cudaStream_t s) {
+    if (in_tf_) {
+        // A Sub on the input: the box of x - c (or c - x), in Luna's order,
+        // as BoundedSubNode's interval forward computes it.
+        float* tl = cache_.as<float>("x_sub_l", (size_t)B * width(0));
+        float* tu = cache_.as<float>("x_sub_u", (size_t)B * width(0));
+        launch_input_sub(in_const_, in_neg_, xl, xu, tl, tu, B, width(0), s);
+        xl = tl;
+        xu = tu;
+    }
     if (map(0).spatial) {
         // Input boxes arrive in Luna's CHW order; the engine works in HWC.
         const MapShape& m0 = map(0);

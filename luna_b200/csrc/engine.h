@@ -130,7 +130,7 @@ public:
     // Linear layers with ReLU between them and no joins (the networks the
     // allocation-free IBP entry point takes).
     bool is_relu_mlp() const {
-        if (has_conv_ || has_sigmoid_) return false;
+        if (has_conv_ || has_sigmoid_ || in_tf_) return false;
         for (const auto& sk : skips_)
             if (!sk.empty()) return false;
         return true;
@@ -217,6 +217,11 @@ private:
     const int32_t* branch_ = nullptr;
     int n_branches_ = 0;
     int iters_run_ = 0;  // alpha iterations run, max over the chunks of a call
+
+    // Sub on the input node (graph_canon.h): boxes become x - c (or c - x).
+    bool in_tf_ = false;
+    bool in_neg_ = false;
+    float* in_const_ = nullptr;
 
     bool force_simt_ = false;
     bool tc_ = false;  // tensor-core schedule for the current chunk

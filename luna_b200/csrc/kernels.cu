@@ -1240,6 +1240,29 @@ void launch_ibp_spec(const float* C, int c_per_box, const float* l, const float*
     LB_LAUNCH();
 }
 
+__global__ void input_sub_kernel(const float* __restrict__ c, bool neg, const float* __restrict__ xl,
+                                 const float* __restrict__ xu, float* __restrict__ ol, float* __restrict__ ou,
+                                 int64_t total, int n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const float k = c[i % n];
+    if (neg) {
+        ol[i] = k - xu[i];
+        ou[i] = k - xl[i];
+    } else {
+        ol[i] = xl[i] - k;
+        ou[i] = xu[i] - k;
+    }
+}
+
+void launch_input_sub(const float* c, bool neg, const float* xl, const float* xu, float* ol, float* ou, int B, int n,
+                      cudaStream_t s) {
+    const int64_t total = (int64_t)B * n;
+    if (total == 0) return;
+    input_sub_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(c, neg, xl, xu, ol, ou, total, n);
+    LB_LAUNCH();
+}
+
 __global__ void add_bounds_kernel(float* __restrict__ ol, float* __restrict__ ou, const float* __restrict__ il,
                                   const float* __restrict__ iu, int64_t n, bool relu_in) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;

@@ -316,6 +316,11 @@ void launch_restore_alpha(const RowMap& rows, const int* first_save, int n, cons
 void launch_ibp_spec(const float* C, int c_per_box, const float* l, const float* u, int B, int nspec,
                      int nout, float* lb, float* ub, cudaStream_t s);
 
+// Sub on the input node (BoundedSubNode's interval forward): per box,
+// [xl - c, xu - c], or [c - xu, c - xl] when neg (constant first).
+void launch_input_sub(const float* c, bool neg, const float* xl, const float* xu, float* ol, float* ou, int B, int n,
+                      cudaStream_t s);
+
 // Fill / copy helpers.
 void launch_fill_f32(float* p, float v, int64_t n, cudaStream_t s);
 void launch_expand_spec(const float* C, int c_per_box, int B, int nspec, int nout, float* out,

@@ -81,7 +81,7 @@ extern "C" LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const floa
         const lb200::Model& m = *model->m;
         if (!m.is_relu_mlp())
             return lb200::set_last_error(
-                "lb200_ibp_bounds_noalloc: only Linear/ReLU networks (no conv, Sigmoid or Add) are supported");
+                "lb200_ibp_bounds_noalloc: only Linear/ReLU networks (no conv, Sigmoid, Add or Sub on the input) are supported");
         const auto& L = m.layers();
         int64_t per_box = 0;
         for (const auto& layer : L) per_box += 2 * (int64_t)layer.n_out;

@@ -10,7 +10,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .abi import (NODE_ADD, NODE_BATCHNORM, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY,
+from .abi import (NODE_ADD, NODE_BATCHNORM, NODE_CONCAT, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN,
+                  NODE_IDENTITY, NODE_RESHAPE, NODE_SLICE, NODE_SUB,
                   NODE_INPUT, NODE_LINEAR, NODE_RELU, NODE_SIGMOID, Graph, Node)
 
 
@@ -275,6 +276,133 @@ def convt_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 10,
         layers.append(("conv", 4, 3, 1, 1))
     g = cnn((3, hw, hw), layers + [("linear", 12), ("linear", 4)], seed + 9, bias_std=0.1)
     return g, image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)
+
+
+def _lin(rng, nodes, src, n_in, n_out, bias_std=0.1):
+    w = (rng.standard_normal((n_out, n_in)) * np.sqrt(2.0 / n_in)).astype(np.float32)
+    b = (rng.standard_normal(n_out) * bias_std).astype(np.float32)
+    nodes.append(Node(NODE_LINEAR, [src], (n_out, 1, 1), weight=w, bias=b))
+    return len(nodes) - 1
+
+
+def _conv(rng, nodes, src, shape, co, k, s, p, bias_std=0.1):
+    ci, h, w = shape
+    wt = (rng.standard_normal((co, ci, k, k)) * np.sqrt(2.0 / (ci * k * k))).astype(np.float32)
+    b = (rng.standard_normal(co) * bias_std).astype(np.float32)
+    out = (co, conv_out(h, k, s, p), conv_out(w, k, s, p))
+    nodes.append(Node(NODE_CONV, [src], out, weight=wt, bias=b, kernel=(k, k), stride=(s, s), padding=(p, p)))
+    return len(nodes) - 1, out
+
+
+def _act(nodes, src, shape):
+    nodes.append(Node(NODE_RELU, [src], shape))
+    return len(nodes) - 1
+
+
+def flat_boxes(rng, n_boxes: int, n_in: int, eps: float, n_out: int):
+    """Centres U[-1, 1]^n_in, radius U[0.2 eps, eps] per feature, margin spec."""
+    c = rng.uniform(-1.0, 1.0, (n_boxes, n_in)).astype(np.float32)
+    r = rng.uniform(0.2 * eps, eps, (n_boxes, n_in)).astype(np.float32)
+    t = rng.integers(0, n_out, n_boxes)
+    return Boxes((c - r).astype(np.float32), (c + r).astype(np.float32), margin_spec(t, n_out))
+
+
+def sub_mlp_case(seed: int, n_boxes: int = 6, where: str = "input", constant_second: int = 1, eps: float = 0.3):
+    """MLP 6 -> 12 -> 10 -> 4 with a Sub of a constant (BoundedSubNode):
+    on the input (an input normalisation), or on the first Linear's output
+    (where="linear"); constant_second = 0 gives constant - x."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    nodes = [Node(NODE_INPUT, [], (6, 1, 1))]
+    src, n = 0, 6
+    if where == "input":
+        c = rng.normal(0.3, 0.4, 6).astype(np.float32)
+        nodes.append(Node(NODE_SUB, [0], (6, 1, 1), constant=c, constant_second=constant_second))
+        src = 1
+    h = _lin(rng, nodes, src, n, 12)
+    if where == "linear":
+        c = rng.normal(0.1, 0.3, 12).astype(np.float32)
+        nodes.append(Node(NODE_SUB, [h], (12, 1, 1), constant=c, constant_second=constant_second))
+        h = len(nodes) - 1
+    h = _act(nodes, h, (12, 1, 1))
+    h = _act(nodes, _lin(rng, nodes, h, 12, 10), (10, 1, 1))
+    _lin(rng, nodes, h, 10, 4)
+    return Graph(nodes, 0, len(nodes) - 1), flat_boxes(rng, n_boxes, 6, eps, 4)
+
+
+def slice_mlp_case(seed: int, n_boxes: int = 6, eps: float = 0.3, reverse: bool = False):
+    """MLP with Slices of flat vectors (BoundedSliceNode): 6 -> Linear 16 ->
+    Slice [2:14] -> ReLU -> Linear 10 -> ReLU -> Slice [1:9] (or, reversed,
+    start 8, end 0, step -1: features 8 down to 0, as Luna's
+    BoundedSliceNode::_fixup_params reads it) -> Linear 4."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    nodes = [Node(NODE_INPUT, [], (6, 1, 1))]
+    h = _lin(rng, nodes, 0, 6, 16)
+    nodes.append(Node(NODE_SLICE, [h], (12, 1, 1), axis=1, start=2, end=14, step=1))
+    h = _act(nodes, len(nodes) - 1, (12, 1, 1))
+    h = _act(nodes, _lin(rng, nodes, h, 12, 10), (10, 1, 1))
+    k = 9 if reverse else 8
+    if reverse:
+        nodes.append(Node(NODE_SLICE, [h], (k, 1, 1), axis=1, start=8, end=0, step=-1))
+    else:
+        nodes.append(Node(NODE_SLICE, [h], (k, 1, 1), axis=1, start=1, end=-1, step=1))
+    _lin(rng, nodes, len(nodes) - 1, k, 4)
+    return Graph(nodes, 0, len(nodes) - 1), flat_boxes(rng, n_boxes, 6, eps, 4)
+
+
+def concat_mlp_case(seed: int, n_boxes: int = 6, eps: float = 0.3):
+    """Two Linear branches of the input concatenated (BoundedConcatNode,
+    axis 1): 6 -> [Linear 8, Linear 6] -> Concat 14 -> ReLU -> Linear 10 ->
+    ReLU -> Linear 4."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    nodes = [Node(NODE_INPUT, [], (6, 1, 1))]
+    a = _lin(rng, nodes, 0, 6, 8)
+    b = _lin(rng, nodes, 0, 6, 6)
+    nodes.append(Node(NODE_CONCAT, [a, b], (14, 1, 1), axis=1))
+    h = _act(nodes, len(nodes) - 1, (14, 1, 1))
+    h = _act(nodes, _lin(rng, nodes, h, 14, 10), (10, 1, 1))
+    _lin(rng, nodes, h, 10, 4)
+    return Graph(nodes, 0, len(nodes) - 1), flat_boxes(rng, n_boxes, 6, eps, 4)
+
+
+def concat_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 8):
+    """Two conv branches of the input concatenated along the channels: 3 x hw x
+    hw -> [conv 4 k3 p1, conv 3 k3 p1] -> Concat 7 -> ReLU -> conv 6 k4 s2 p1
+    -> ReLU -> Reshape (flatten) -> Linear 12 -> ReLU -> Linear 4."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    shape = (3, hw, hw)
+    nodes = [Node(NODE_INPUT, [], shape)]
+    a, sa = _conv(rng, nodes, 0, shape, 4, 3, 1, 1)
+    b, sb = _conv(rng, nodes, 0, shape, 3, 3, 1, 1)
+    cat = (sa[0] + sb[0], sa[1], sa[2])
+    nodes.append(Node(NODE_CONCAT, [a, b], cat, axis=1))
+    h = _act(nodes, len(nodes) - 1, cat)
+    c, sc = _conv(rng, nodes, h, cat, 6, 4, 2, 1)
+    h = _act(nodes, c, sc)
+    n = int(np.prod(sc))
+    nodes.append(Node(NODE_RESHAPE, [h], (n, 1, 1)))
+    h = _act(nodes, _lin(rng, nodes, len(nodes) - 1, n, 12), (12, 1, 1))
+    _lin(rng, nodes, h, 12, 4)
+    return Graph(nodes, 0, len(nodes) - 1), image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)
+
+
+def sub_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 8, constant_second: int = 1):
+    """Input normalisation on a CNN: 3 x hw x hw -> Sub (per-pixel constant)
+    -> conv 5 k3 p1 -> ReLU -> conv 6 k4 s2 p1 -> ReLU -> Reshape -> Linear 10
+    -> ReLU -> Linear 4 (starts small enough for dense A on Luna's path)."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    shape = (3, hw, hw)
+    nodes = [Node(NODE_INPUT, [], shape)]
+    c = rng.normal(0.45, 0.1, 3 * hw * hw).astype(np.float32)
+    nodes.append(Node(NODE_SUB, [0], shape, constant=c, constant_second=constant_second))
+    a, sa = _conv(rng, nodes, 1, shape, 5, 3, 1, 1)
+    h = _act(nodes, a, sa)
+    b, sb = _conv(rng, nodes, h, sa, 6, 4, 2, 1)
+    h = _act(nodes, b, sb)
+    n = int(np.prod(sb))
+    nodes.append(Node(NODE_RESHAPE, [h], (n, 1, 1)))
+    h = _act(nodes, _lin(rng, nodes, len(nodes) - 1, n, 10), (10, 1, 1))
+    _lin(rng, nodes, h, 10, 4)
+    return Graph(nodes, 0, len(nodes) - 1), image_boxes(rng, n_boxes, 3 * hw * hw, eps, 4)
 
 
 def cnn_convt_cifar(n_boxes: int = 256, seed: int = 5, eps: float = 8.0 / 255.0):

@@ -13,7 +13,9 @@ bounds" set by concretisation (BoundedTorchNode::setBounds), alpha
 parameters keyed by (activation node, start node), and STE reference bounds.
 
 Supported node kinds: Input, Linear, Conv2d, ConvTranspose2d, BatchNorm, ReLU, Sigmoid,
-Add (of two tensors), Flatten, Identity.  A
+Add (of two tensors), Flatten, Identity, Reshape (flattening), Sub with a
+constant, Slice of a flat vector (steps 1 / -1), Concat of flat vectors or
+of maps along the channels.  A
 matrices are kept dense over the flattened (C, H, W) features; Luna's
 patches mode (CROWNAnalysis.cpp:255-405, BoundedConvNode.cpp:556-709) is the
 same arithmetic on a window of those features, and it is tracked only to
@@ -29,12 +31,31 @@ import torch
 import torch.nn.functional as F
 
 from luna_b200.abi import (METHOD_ALPHA_CROWN, METHOD_CROWN, METHOD_IBP, NODE_ADD, NODE_BATCHNORM,
-                           NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT,
-                           NODE_LINEAR, NODE_RELU, NODE_SIGMOID, Options, default_options)
+                           NODE_CONCAT, NODE_CONV, NODE_CONVTRANSPOSE, NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT,
+                           NODE_LINEAR, NODE_RELU, NODE_RESHAPE, NODE_SIGMOID, NODE_SLICE, NODE_SUB, Options,
+                           default_options)
 
 # Dense identity starts above this many conv output features switch to
 # patches on Luna's CPU path (CROWNAnalysis.cpp:257,269).
 PATCHES_SIZE_THRESHOLD = 4096
+
+
+def slice_indices(nd, n_in: int):
+    """Input feature of each output feature of a flat Slice, after
+    BoundedSliceNode::_fixup_params (BoundedSliceNode.cpp:28-52): negative
+    start / end count from the end, step -1 swaps them and reverses."""
+    start, end = nd.start, nd.end
+    if start < 0:
+        start += n_in
+    if end < 0:
+        end = 0 if end == -9223372036854775807 else end + n_in
+    if nd.step == -1:
+        start, end = end, start
+        end += 1
+    end = min(end, n_in)
+    start = max(start, 0)
+    idx = list(range(start, end))
+    return idx[::-1] if nd.step == -1 else idx
 
 
 def topo_order(graph):
@@ -255,7 +276,14 @@ class LirpaOracle:
             elif nd.type == NODE_ADD:
                 if len(nd.inputs) != 2:
                     raise NotImplementedError("oracle: Add of a constant")
-            elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_SIGMOID, NODE_FLATTEN, NODE_IDENTITY):
+            elif nd.type == NODE_SUB:
+                if len(nd.inputs) != 1 or nd.constant is None:
+                    raise NotImplementedError("oracle: Sub of two tensors")
+                self.W[i] = torch.from_numpy(np.asarray(nd.constant, np.float32)).flatten()
+            elif nd.type == NODE_SLICE:
+                self.W[i] = torch.as_tensor(slice_indices(nd, graph.nodes[nd.inputs[0]].size), dtype=torch.long)
+            elif nd.type not in (NODE_INPUT, NODE_RELU, NODE_SIGMOID, NODE_FLATTEN, NODE_IDENTITY, NODE_RESHAPE,
+                                 NODE_CONCAT):
                 raise NotImplementedError(f"oracle: node type {nd.type}")
         self.act_ids = [i for i, nd in enumerate(graph.nodes) if nd.type in (NODE_RELU, NODE_SIGMOID)]
         self.preact_ids = sorted({graph.nodes[i].inputs[0] for i in self.act_ids})
@@ -310,8 +338,24 @@ class LirpaOracle:
             # BoundedAddNode::computeIntervalBoundPropagation (:281-304).
             (l1, u1), (l2, u2) = ins
             return l1 + l2, u1 + u2
-        if nd.type in (NODE_FLATTEN, NODE_IDENTITY):
+        if nd.type in (NODE_FLATTEN, NODE_IDENTITY, NODE_RESHAPE):
             return ins[0]
+        if nd.type == NODE_SUB:
+            # BoundedSubNode::computeIntervalBoundPropagation (:205-233):
+            # [l - c, u - c], or [c - u, c - l] for a constant first operand.
+            l, u = ins[0]
+            c = self.W[i]
+            if nd.constant_second:
+                return l - c, u - c
+            return c - u, c - l
+        if nd.type == NODE_SLICE:
+            # BoundedSliceNode::forward on both bounds (narrow, flipped for step -1).
+            l, u = ins[0]
+            return l[self.W[i]], u[self.W[i]]
+        if nd.type == NODE_CONCAT:
+            # BoundedConcatNode::computeIntervalBoundPropagation: cat of the
+            # flat bounds (channel order for maps).
+            return torch.cat([x[0] for x in ins]), torch.cat([x[1] for x in ins])
         raise NotImplementedError
 
     def _input_bounds_of(self, st, i, x):
@@ -560,8 +604,36 @@ class LirpaOracle:
                     # operands (equal shapes), no bias of its own.
                     out = [(a_l, a_u), (a_l, a_u)]
                     nb_l = nb_u = None
-                elif nd.type in (NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT):
+                elif nd.type in (NODE_FLATTEN, NODE_IDENTITY, NODE_INPUT, NODE_RESHAPE):
                     out = [(a_l, a_u)]
+                    nb_l = nb_u = None
+                elif nd.type == NODE_SUB:
+                    # BoundedSubNode::boundBackward with a constant (:61-165):
+                    # x - c passes A and adds -A c; c - x passes -A and adds A c.
+                    c_ = self.W[c]
+                    if nd.constant_second:
+                        out = [(a_l, a_u)]
+                        nb_l, nb_u = -torch.matmul(a_l, c_), -torch.matmul(a_u, c_)
+                    else:
+                        out = [(-a_l, -a_u)]
+                        nb_l, nb_u = torch.matmul(a_l, c_), torch.matmul(a_u, c_)
+                elif nd.type == NODE_SLICE:
+                    # BoundedSliceNode::boundBackward (:113-201): A scattered
+                    # into zeros of the input size at the sliced features.
+                    n_in = self.g.nodes[nd.inputs[0]].size
+                    idx = self.W[c]
+                    outs = []
+                    for a in (a_l, a_u):
+                        z = torch.zeros(a.shape[0], n_in)
+                        z[:, idx] = a
+                        outs.append(z)
+                    out = [tuple(outs)]
+                    nb_l = nb_u = None
+                elif nd.type == NODE_CONCAT:
+                    # BoundedConcatNode::boundBackward (:56-178): A split along
+                    # the features into the operands' sizes, no bias.
+                    sizes = [self.g.nodes[p].size for p in nd.inputs]
+                    out = list(zip(torch.split(a_l, sizes, dim=1), torch.split(a_u, sizes, dim=1)))
                     nb_l = nb_u = None
                 else:
                     raise NotImplementedError

@@ -111,6 +111,25 @@ BoundedSigmoidNode::BoundedSigmoidNode(const torch::nn::Sigmoid&, const std::str
 BoundedAddNode::BoundedAddNode() : BoundedNode(NLR::NodeType::ADD) {}
 BoundedFlattenNode::BoundedFlattenNode() : BoundedNode(NLR::NodeType::FLATTEN) {}
 BoundedIdentityNode::BoundedIdentityNode() : BoundedNode(NLR::NodeType::IDENTITY) {}
+BoundedReshapeNode::BoundedReshapeNode() : BoundedNode(NLR::NodeType::RESHAPE) {}
+BoundedSubNode::BoundedSubNode() : BoundedNode(NLR::NodeType::SUB) { d_.constant_second = 1; }
+
+void BoundedSubNode::setConstantValue(const torch::Tensor& constant, bool isSecondOperand) {
+    keep(constant, const_);
+    d_.constant_second = isSecondOperand ? 1 : 0;
+}
+
+BoundedSliceNode::BoundedSliceNode(int64_t start, int64_t end, int64_t axes, int64_t steps, const std::string&)
+    : BoundedNode(NLR::NodeType::SLICE) {
+    d_.start = start;
+    d_.end = end;
+    d_.axis = (int32_t)axes;
+    d_.step = steps;
+}
+
+BoundedConcatNode::BoundedConcatNode(int axis, unsigned, const std::string&) : BoundedNode(NLR::NodeType::CONCAT) {
+    d_.axis = axis;
+}
 
 // ------------------------------------------------------------ model
 TorchModel::TorchModel(const std::vector<std::shared_ptr<BoundedNode>>& nodes,
@@ -137,11 +156,12 @@ TorchModel::TorchModel(const std::vector<std::shared_ptr<BoundedNode>>& nodes,
         if (has || d.num_inputs == 0) continue;
         if (d.inputs[0] >= i) throw std::runtime_error("lb200_luna: nodes must be in topological order");
         const lb200_node_desc& p = descs_[d.inputs[0]];
-        if (d.type == LB200_NODE_FLATTEN) {
+        if (d.type == LB200_NODE_FLATTEN || d.type == LB200_NODE_RESHAPE) {
             d.out_shape[0] = p.out_shape[0] * p.out_shape[1] * p.out_shape[2];
             d.out_shape[1] = d.out_shape[2] = 1;
-        } else if (d.type == LB200_NODE_CONV || d.type == LB200_NODE_CONVTRANSPOSE) {
-            throw std::runtime_error("lb200_luna: conv node " + std::to_string(i) + " needs setOutputShape");
+        } else if (d.type == LB200_NODE_CONV || d.type == LB200_NODE_CONVTRANSPOSE || d.type == LB200_NODE_SLICE ||
+                   d.type == LB200_NODE_CONCAT) {
+            throw std::runtime_error("lb200_luna: node " + std::to_string(i) + " needs setOutputShape / setOutputSize");
         } else {
             for (int k = 0; k < 3; ++k) d.out_shape[k] = p.out_shape[k];
         }
@@ -154,6 +174,7 @@ TorchModel::TorchModel(const std::vector<std::shared_ptr<BoundedNode>>& nodes,
         d.bias = node.biases().empty() ? nullptr : node.biases().data();
         d.running_mean = node.means().empty() ? nullptr : node.means().data();
         d.running_var = node.vars().empty() ? nullptr : node.vars().data();
+        d.constant = node.constants().empty() ? nullptr : node.constants().data();
     }
     lb200_graph_desc g{};
     g.num_nodes = n;

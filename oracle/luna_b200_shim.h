@@ -62,12 +62,13 @@ public:
     const std::vector<float>& biases() const { return b_; }
     const std::vector<float>& means() const { return mean_; }
     const std::vector<float>& vars() const { return var_; }
+    const std::vector<float>& constants() const { return const_; }
 
 protected:
     explicit BoundedNode(NLR::NodeType t);
     void keep(const torch::Tensor& t, std::vector<float>& dst);
     lb200_node_desc d_{};
-    std::vector<float> w_, b_, mean_, var_;
+    std::vector<float> w_, b_, mean_, var_, const_;
 };
 
 class BoundedInputNode : public BoundedNode {
@@ -122,6 +123,29 @@ public:
 class BoundedIdentityNode : public BoundedNode {
 public:
     BoundedIdentityNode();
+};
+
+// Luna's Reshape flattens (OnnxToTorch.cpp:1959); the engine takes it as a Flatten.
+class BoundedReshapeNode : public BoundedNode {
+public:
+    BoundedReshapeNode();
+};
+
+class BoundedSubNode : public BoundedNode {
+public:
+    BoundedSubNode();
+    // BoundedSubNode::setConstantValue (BoundedSubNode.h:54-57).
+    void setConstantValue(const torch::Tensor& constant, bool isSecondOperand = true);
+};
+
+class BoundedSliceNode : public BoundedNode {
+public:
+    BoundedSliceNode(int64_t start, int64_t end, int64_t axes, int64_t steps = 1, const std::string& name = "");
+};
+
+class BoundedConcatNode : public BoundedNode {
+public:
+    BoundedConcatNode(int axis, unsigned numInputs, const std::string& name = "");
 };
 
 // The engine model behind NLR::TorchModel's interface.

@@ -27,6 +27,10 @@
 #include "nodes/BoundedConvTransposeNode.h"
 #include "nodes/BoundedAddNode.h"
 #include "nodes/BoundedSigmoidNode.h"
+#include "nodes/BoundedSubNode.h"
+#include "nodes/BoundedReshapeNode.h"
+#include "nodes/BoundedSliceNode.h"
+#include "nodes/BoundedConcatNode.h"
 #include "input_parsers/Operations.h"
 #include "input_parsers/OutputConstraint.h"
 #include "input_parsers/VnnLibInputParser.h"
@@ -176,6 +180,41 @@ std::shared_ptr<NLR::TorchModel> build_model(const lb200_graph_desc* g) {
             node->setInputSize((unsigned)out_numel);
             node->setOutputSize((unsigned)out_numel);
             break;
+        case LB200_NODE_SUB: {
+            // BoundedOperationConverter::convertSub with one constant operand
+            // (OnnxToTorch.cpp:2064-2100): setConstantValue(c, constant second?).
+            const lb200_node_desc& src = g->nodes[d.inputs[0]];
+            const int64_t n_src = (int64_t)src.out_shape[0] * src.out_shape[1] * src.out_shape[2];
+            auto sn = std::make_shared<NLR::BoundedSubNode>();
+            sn->setConstantValue(from_host(d.constant, {n_src}), d.constant_second != 0);
+            sn->setInputSize((unsigned)n_src);
+            sn->setOutputSize((unsigned)out_numel);
+            node = sn;
+            break;
+        }
+        case LB200_NODE_RESHAPE: {
+            // convertReshape (OnnxToTorch.cpp:1935-1972): shape -1, sizes set.
+            node = std::make_shared<NLR::BoundedReshapeNode>(Operations::ReshapeWrapper(torch::tensor({-1})));
+            node->setInputSize((unsigned)out_numel);
+            node->setOutputSize((unsigned)out_numel);
+            break;
+        }
+        case LB200_NODE_SLICE: {
+            // convertSlice (OnnxToTorch.cpp:2924): BoundedSliceNode(start, end, axes, steps).
+            const lb200_node_desc& src = g->nodes[d.inputs[0]];
+            node = std::make_shared<NLR::BoundedSliceNode>(d.start, d.end, (int64_t)d.axis, d.step, String("slice"));
+            node->setInputSize((unsigned)((int64_t)src.out_shape[0] * src.out_shape[1] * src.out_shape[2]));
+            node->setOutputSize((unsigned)out_numel);
+            break;
+        }
+        case LB200_NODE_CONCAT: {
+            // convertConcat (OnnxToTorch.cpp:2734): BoundedConcatNode(axis, numInputs).
+            auto cn = std::make_shared<NLR::BoundedConcatNode>((int)d.axis, (unsigned)d.num_inputs);
+            cn->setInputSize((unsigned)out_numel);
+            cn->setOutputSize((unsigned)out_numel);
+            node = cn;
+            break;
+        }
         default:
             throw std::runtime_error("luna_ref_driver: node type " + std::to_string(d.type) +
                                      " is not wired into the reference driver");

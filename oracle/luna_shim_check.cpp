@@ -22,6 +22,10 @@
 #include "nodes/BoundedLinearNode.h"
 #include "nodes/BoundedReLUNode.h"
 #include "nodes/BoundedSigmoidNode.h"
+#include "nodes/BoundedConcatNode.h"
+#include "nodes/BoundedReshapeNode.h"
+#include "nodes/BoundedSliceNode.h"
+#include "nodes/BoundedSubNode.h"
 
 #include <cstring>
 
@@ -128,11 +132,42 @@ Both make_node(const lb200_graph_desc* g, int i) {
         b.luna = std::make_shared<NLR::BoundedIdentityNode>(torch::nn::Identity());
         b.shim = std::make_shared<lb200_luna::BoundedIdentityNode>();
         break;
+    case LB200_NODE_SUB: {
+        const lb200_node_desc& src = g->nodes[d.inputs[0]];
+        const int64_t n_src = (int64_t)src.out_shape[0] * src.out_shape[1] * src.out_shape[2];
+        auto c = from_host(d.constant, {n_src});
+        auto ln = std::make_shared<NLR::BoundedSubNode>();
+        ln->setConstantValue(c, d.constant_second != 0);
+        b.luna = ln;
+        auto sn = std::make_shared<lb200_luna::BoundedSubNode>();
+        sn->setConstantValue(c, d.constant_second != 0);
+        b.shim = sn;
+        break;
+    }
+    case LB200_NODE_RESHAPE:
+        b.luna = std::make_shared<NLR::BoundedReshapeNode>(Operations::ReshapeWrapper(torch::tensor({-1})));
+        b.shim = std::make_shared<lb200_luna::BoundedReshapeNode>();
+        break;
+    case LB200_NODE_SLICE: {
+        b.luna = std::make_shared<NLR::BoundedSliceNode>(d.start, d.end, (int64_t)d.axis, d.step, String("slice"));
+        auto sn = std::make_shared<lb200_luna::BoundedSliceNode>(d.start, d.end, (int64_t)d.axis, d.step);
+        sn->setOutputShape({1, d.out_shape[0], d.out_shape[1], d.out_shape[2]});
+        b.shim = sn;
+        break;
+    }
+    case LB200_NODE_CONCAT: {
+        b.luna = std::make_shared<NLR::BoundedConcatNode>((int)d.axis, (unsigned)d.num_inputs);
+        auto sn = std::make_shared<lb200_luna::BoundedConcatNode>((int)d.axis, (unsigned)d.num_inputs);
+        sn->setOutputShape({1, d.out_shape[0], d.out_shape[1], d.out_shape[2]});
+        b.shim = sn;
+        break;
+    }
     default:
         throw std::runtime_error("luna_shim_check: node type " + std::to_string(d.type) + " not wired");
     }
     if (d.type == LB200_NODE_RELU || d.type == LB200_NODE_SIGMOID || d.type == LB200_NODE_FLATTEN ||
-        d.type == LB200_NODE_ADD || d.type == LB200_NODE_IDENTITY) {
+        d.type == LB200_NODE_ADD || d.type == LB200_NODE_IDENTITY || d.type == LB200_NODE_SUB ||
+        d.type == LB200_NODE_RESHAPE || d.type == LB200_NODE_SLICE || d.type == LB200_NODE_CONCAT) {
         b.luna->setInputSize((unsigned)numel);
         b.luna->setOutputSize((unsigned)numel);
     }

@@ -118,6 +118,26 @@ def cases():
                 3, abi.METHOD_CROWN, {}))
     # The CIFAR-shaped CNN at full size, one box.
     out.append(("cnn_cifar_crown", "cnn_cifar", {"n_boxes": 1}, 1, abi.METHOD_CROWN, {}))
+    # Sub (a constant on the input, or on a Linear output; x - c and c - x),
+    # Slice of flat vectors (after a Linear, and feeding one, step 1 and -1),
+    # Concat of Linear / Conv outputs, Reshape as a flatten.
+    a6 = {"alpha_lr": 0.1, "alpha_iterations": 6}
+    out.append(("sub_in_crown", "sub_mlp_case", {"seed": 1}, 6, abi.METHOD_CROWN, {}))
+    out.append(("sub_in_alpha", "sub_mlp_case", {"seed": 1}, 6, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("sub_in_neg_alpha", "sub_mlp_case", {"seed": 2, "constant_second": 0}, 6, abi.METHOD_ALPHA_CROWN,
+                a6))
+    out.append(("sub_lin_alpha", "sub_mlp_case", {"seed": 3, "where": "linear"}, 6, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("sub_lin_neg_crown", "sub_mlp_case", {"seed": 4, "where": "linear", "constant_second": 0}, 6,
+                abi.METHOD_CROWN, {}))
+    out.append(("slice_crown", "slice_mlp_case", {"seed": 5}, 6, abi.METHOD_CROWN, {}))
+    out.append(("slice_alpha", "slice_mlp_case", {"seed": 5}, 6, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("slice_rev_alpha", "slice_mlp_case", {"seed": 6, "reverse": True}, 6, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("concat_crown", "concat_mlp_case", {"seed": 7}, 6, abi.METHOD_CROWN, {}))
+    out.append(("concat_alpha", "concat_mlp_case", {"seed": 7}, 6, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("concat_cnn_crown", "concat_cnn_case", {"seed": 8}, 3, abi.METHOD_CROWN, {}))
+    out.append(("concat_cnn_alpha", "concat_cnn_case", {"seed": 8}, 3, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("sub_cnn_alpha", "sub_cnn_case", {"seed": 9}, 3, abi.METHOD_ALPHA_CROWN, a6))
+    out.append(("sub_cnn_neg_crown", "sub_cnn_case", {"seed": 10, "constant_second": 0}, 3, abi.METHOD_CROWN, {}))
     # The MLP alpha-CROWN workload at its own size: all 512 boxes, 20 Adam
     # iterations at lr 0.1.
     out.append(("cfg2_alpha512", "mlp_784_256x4_10", {"n_boxes": 512}, 512, abi.METHOD_ALPHA_CROWN,

@@ -59,6 +59,10 @@ CASES = [
     ("convt", lambda: W.convt_cnn_case(1, n_boxes=1), 0.1, 3),
     ("resnet", lambda: W.small_resnet_case(7, n_boxes=1), 0.1, 3),
     ("resnet_sigmoid", lambda: W.small_resnet_case(9, n_boxes=1, head_act=abi.NODE_SIGMOID), 0.1, 0),
+    ("sub_input", lambda: W.sub_mlp_case(1, n_boxes=2), 0.1, 4),
+    ("slice", lambda: W.slice_mlp_case(6, n_boxes=2, reverse=True), 0.1, 4),
+    ("concat_cnn", lambda: W.concat_cnn_case(8, n_boxes=1), 0.1, 3),
+    ("sub_cnn", lambda: W.sub_cnn_case(10, n_boxes=1, constant_second=0), 0.1, 3),
 ]
 
 

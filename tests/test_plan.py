@@ -117,8 +117,63 @@ def test_rejections():
     _expect_rejected(Graph(nodes, 0, 2), "output node")
     # A node kind the engine does not take.
     bad = copy.deepcopy(_mlp_graph())
-    bad.nodes[2].type = abi.NODE_SLICE
+    bad.nodes[2].type = abi.NODE_CONSTANT
     _expect_rejected(bad, "not supported")
+
+
+def test_rejections_of_sub_slice_concat_reshape():
+    """Placements of the rewritten node kinds with no exact rewrite are
+    refused with a message naming the node."""
+    g, _ = W.sub_mlp_case(1)
+    bad = copy.deepcopy(g)
+    bad.nodes[1].inputs = [0, 0]  # Sub of two tensors
+    _expect_rejected(bad, "two tensors")
+    bad = copy.deepcopy(g)
+    bad.nodes[1].constant = None
+    _expect_rejected(bad, "without a constant")
+    g, _ = W.sub_cnn_case(9)
+    bad = copy.deepcopy(g)
+    conv = 2
+    relu = 3
+    # A Sub after a conv whose constant varies inside a channel.
+    bad.nodes.append(Node(abi.NODE_SUB, [conv], bad.nodes[conv].out_shape,
+                          constant=np.arange(bad.nodes[conv].size, dtype=np.float32)))
+    bad.nodes[relu].inputs = [len(bad.nodes) - 1]
+    _expect_rejected(bad, "producers must precede|uniform")
+    g, _ = W.slice_mlp_case(5)
+    bad = copy.deepcopy(g)
+    bad.nodes[2].step = 2
+    _expect_rejected(bad, "steps")
+    bad = copy.deepcopy(g)
+    bad.nodes[2].axis = 2
+    _expect_rejected(bad, "features of a flat vector")
+    g, _ = W.concat_mlp_case(7)
+    bad = copy.deepcopy(g)
+    bad.nodes[2].inputs = [1]  # operands of different producers
+    _expect_rejected(bad, "one producer")
+    g, _ = W.concat_cnn_case(8)
+    bad = copy.deepcopy(g)
+    reshape = next(i for i, n in enumerate(bad.nodes) if n.type == abi.NODE_RESHAPE)
+    bad.nodes[reshape].out_shape = (6, 4, 4)
+    _expect_rejected(bad, "Reshape")
+
+
+@pytest.mark.parametrize("gen,kw,pre", [
+    ("sub_mlp_case", {"seed": 1}, [2, 4]),
+    ("sub_mlp_case", {"seed": 3, "where": "linear"}, [2, 4]),
+    ("slice_mlp_case", {"seed": 5}, [2, 4]),
+    ("concat_mlp_case", {"seed": 7}, [3, 5]),
+    ("concat_cnn_case", {"seed": 8}, [3, 5, 8]),
+    ("sub_cnn_case", {"seed": 9}, [2, 4, 7]),
+])
+def test_rewritten_kinds_keep_luna_node_ids(gen, kw, pre):
+    """Sub / Slice / Concat / Reshape graphs are taken, and the pre-activation
+    of every level keeps the id of the node that feeds its ReLU in Luna's
+    graph (the key of intermediate bounds)."""
+    g, _ = getattr(W, gen)(**kw)
+    plan = describe_plan(g)
+    nodes = [lv["node"] for lv in plan["levels"]][1:-1]
+    assert nodes == pre == g.activation_inputs()
 
 
 def test_plan_levels_of_the_cifar_resnet():
