@@ -243,6 +243,16 @@ LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const float* d_x_lowe
                                        int64_t c_boxes, int64_t nspec, float* d_out_lb,
                                        float* d_out_ub, void* stream);
 
+/* Failure-detection test hook for the tensor-core kernels' bounded waits,
+ * on CUDA device `device`.  starve = 1 makes the contraction producers
+ * announce their TMA loads but issue none, so every consumer's wait runs
+ * out: the kernels raise the device error flag and return, and the call that
+ * launched them returns non-zero ("a bounded wait expired") with the
+ * context still usable.  wait_cycles > 0 sets the waits' limit in SM clock
+ * cycles (0: the default, about 2 s).  (0, 0) restores normal operation.
+ * Luna has no counterpart (it runs no device waits). */
+LB200_API int lb200_test_set_contraction_fault(int device, int starve, int64_t wait_cycles);
+
 /* Copy the intermediate (pre-activation) bounds of the last call into host
  * buffers: for every node that feeds a ReLU, in node-id order, [n_boxes,
  * size] lower then upper.  Mirrors TorchModel::getState().allBounds

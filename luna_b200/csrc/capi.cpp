@@ -2,6 +2,7 @@
 // Every entry point catches all exceptions and reports them through
 // lb200_last_error(); nothing is thrown across the boundary.
 #include "handle.h"
+#include "tc_gemm.cuh"
 
 #include <cstring>
 #include <exception>
@@ -154,6 +155,14 @@ int lb200_describe_plan(const lb200_graph_desc* graph, const lb200_options* opt,
             std::strncpy(buf, j.c_str(), len - 1);
             buf[len - 1] = '\0';
         }
+    });
+}
+
+int lb200_test_set_contraction_fault(int device, int starve, int64_t wait_cycles) {
+    return guarded([&] {
+        if (wait_cycles < 0) throw std::invalid_argument("wait_cycles must be >= 0");
+        LB_CUDA(cudaSetDevice(device));
+        lb200::tc_set_test_fault(starve ? 1 : 0, (long long)wait_cycles);
     });
 }
 

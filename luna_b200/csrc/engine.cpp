@@ -1472,7 +1472,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
 void Model::run_pass(Pass pass, int B, int nspec, cudaStream_t s) {
     const bool alpha = pass != Pass::CROWN;
     const bool create = pass == Pass::ALPHA_FIRST;
-    const bool save = pass == Pass::ALPHA_FIRST || pass == Pass::ALPHA_ITER;
+    const bool save = pass == Pass::ALPHA_FIRST || pass == Pass::ALPHA_ITER || pass == Pass::ALPHA_RESTART;
     if (pass == Pass::ALPHA_FINAL) {
         // Intermediate bounds are the best ones (restoreBestIntermediateBounds)
         // and are not recomputed (computeIntermediateBoundsLazy sees node bounds).
@@ -1607,9 +1607,29 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         launch_scatter_output(out.rows, val_out, nspec, true, lb, ub, s);
         return;
     }
-    if (opt_.optimize_upper) throw std::invalid_argument("optimize_upper is not supported by this engine build");
+    // TorchModel::compute_bounds (TorchModel.cpp:683-684): a side is optimised
+    // when it is computed and its OPTIMIZE_* flag is set.
+    const bool opt_upper = upper && opt_.optimize_upper;
+    const bool opt_lower = opt_.optimize_lower != 0;
+    if (!opt_lower && !opt_upper) {
+        // runAlphaCROWN with no side to optimise delegates to runCROWN (:853-857);
+        // its pre-activation bounds are the ones reported.
+        alpha_ = false;
+        run_pass(Pass::CROWN, B, nspec, s);
+        for (int m = 1; m < K_; ++m) {
+            const size_t bn = (size_t)B * width(m) * 4;
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_l", m), bn / 4), cache_.as<float>(key("cur_l", m), bn / 4),
+                                    bn, cudaMemcpyDeviceToDevice, s));
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_u", m), bn / 4), cache_.as<float>(key("cur_u", m), bn / 4),
+                                    bn, cudaMemcpyDeviceToDevice, s));
+        }
+        launch_scatter_output(out.rows, cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R), nspec, upper, lb, ub,
+                              s);
+        return;
+    }
     BoxControl bc;
     bc.active = cache_.as<int>("ctl_active", B);
+    int* active0 = cache_.as<int>("ctl_active0", B);
     int* done = nullptr;
     float* crown_lb = nullptr;
     float* crown_ub = nullptr;
@@ -1648,16 +1668,8 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         const std::vector<int> ones(B, 1);
         LB_CUDA(cudaMemcpyAsync(bc.active, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
     }
+    LB_CUDA(cudaMemcpyAsync(active0, bc.active, B * 4, cudaMemcpyDeviceToDevice, s));
     alpha_ = true;
-    // --- AlphaCROWNAnalysis::computeOptimizedBounds(Lower) ------------------
-    run_pass(Pass::ALPHA_FIRST, B, nspec, s);
-    for (int m = 1; m < K_; ++m) {
-        const size_t bn = (size_t)B * width(m) * 4;
-        LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_l", m), bn / 4), cache_.as<float>(key("cur_l", m), bn / 4), bn,
-                                cudaMemcpyDeviceToDevice, s));
-        LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_u", m), bn / 4), cache_.as<float>(key("cur_u", m), bn / 4), bn,
-                                cudaMemcpyDeviceToDevice, s));
-    }
     bc.best = cache_.as<float>("ctl_best", (size_t)B * nspec);
     bc.best_loss = cache_.as<float>("ctl_bestloss", B);
     bc.patience = cache_.as<int>("ctl_pat", B);
@@ -1665,12 +1677,6 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     bc.save = cache_.as<int>("ctl_save", B);
     bc.improved = cache_.as<uint8_t>("ctl_improved", (size_t)B * nspec);
     bc.first_save = cache_.as<int>("ctl_first", B);
-    launch_fill_f32(bc.best_loss, INFINITY, B, s);
-    LB_CUDA(cudaMemsetAsync(bc.patience, 0, B * 4, s));
-    LB_CUDA(cudaMemsetAsync(bc.has_best, 0, B * 4, s));
-    LB_CUDA(cudaMemsetAsync(bc.save, 0, B * 4, s));
-    const std::vector<int> ones(B, 1);
-    LB_CUDA(cudaMemcpyAsync(bc.first_save, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
     if (thr_ && opt_.stop_alpha_on_verified) {
         bc.thr = thr_;
         bc.branch = branch_;
@@ -1679,109 +1685,169 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     // With thresholds, boxes stop early; the loop ends once none is left.
     int* n_active = thr_ ? cache_.as<int>("ctl_nactive", 1) : nullptr;
     bc.n_active = n_active;
-    for (int st = 2; st <= K_; ++st)
-        for (int m = 1; m < st; ++m) {
-            const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
-            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("am", m, st), cnt), 0, cnt * 4, s));
-            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("av", m, st), cnt), 0, cnt * 4, s));
-        }
-
     const int iters = (int)opt_.alpha_iterations;
     const int save_after = (int)((float)iters * opt_.start_save_best);
-    float lr = opt_.alpha_lr;
     float* cur_lb = cache_.as<float>("cur_lb", (size_t)B * nspec);
     float* cur_ub = cache_.as<float>("cur_ub", (size_t)B * nspec);
-    float* gout = cache_.as<float>(key("g", K_), std::max(out.rows.R, 1));
-    int steps = 0;
+    float* neg_ub = opt_upper ? cache_.as<float>("neg_ub", (size_t)B * nspec) : nullptr;
+    float* fin_lb = cache_.as<float>("fin_lb", (size_t)B * nspec);
+    float* fin_ub = cache_.as<float>("fin_ub", (size_t)B * nspec);
+    float* gout = cache_.as<float>(key("g", K_), std::max(2 * out.rows.R, 1));
+    // TorchModel::runAlphaCROWN (:838-850): the upper side is optimised first,
+    // then the lower side, in one AlphaCROWNAnalysis: the lower run starts from
+    // the alphas the upper run left (its best ones), with a new Adam state,
+    // learning rate and best-bound bookkeeping (computeOptimizedBounds,
+    // AlphaCROWNAnalysis.cpp:306-511, each call).
+    std::vector<bool> sides;
+    if (opt_upper) sides.push_back(true);
+    if (opt_lower) sides.push_back(false);
     int it = 0;
-    for (; it < iters; ++it) {
-        const bool last = it == iters - 1;
-        run_pass(Pass::ALPHA_ITER, B, nspec, s);
-        val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
-        launch_scatter_output(out.rows, val_out, nspec, false, cur_lb, cur_ub, s);
-        if (n_active) LB_CUDA(cudaMemsetAsync(n_active, 0, sizeof(int), s));
-        launch_alpha_control(bc, cur_lb, B, nspec, it, save_after, (int)opt_.early_stop_patience, !last, s);
+    for (size_t run = 0; run < sides.size(); ++run) {
+        const bool up = sides[run];
+        if (run > 0) LB_CUDA(cudaMemcpyAsync(bc.active, active0, B * 4, cudaMemcpyDeviceToDevice, s));
+        // First pass of the run: alphas created from the CROWN slopes in the
+        // first run, reused in the second; no STE reference bounds yet.
+        run_pass(run == 0 ? Pass::ALPHA_FIRST : Pass::ALPHA_RESTART, B, nspec, s);
         for (int m = 1; m < K_; ++m) {
-            const size_t bn = (size_t)B * width(m);
-            launch_snapshot(bc.save, cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B,
-                            width(m), cache_.as<float>(key("best_l", m), bn), cache_.as<float>(key("best_u", m), bn), s);
+            const size_t bn = (size_t)B * width(m) * 4;
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_l", m), bn / 4), cache_.as<float>(key("cur_l", m), bn / 4),
+                                    bn, cudaMemcpyDeviceToDevice, s));
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("best_u", m), bn / 4), cache_.as<float>(key("cur_u", m), bn / 4),
+                                    bn, cudaMemcpyDeviceToDevice, s));
         }
-        // updateBestAlphas: every active box saves at iteration 0 (nothing is
-        // best yet, so every spec improves), which is each box's first save
-        // and copies every row; later saves copy only rows whose index inside
-        // the box is an improved spec index.
+        launch_fill_f32(bc.best_loss, INFINITY, B, s);
+        LB_CUDA(cudaMemsetAsync(bc.patience, 0, B * 4, s));
+        LB_CUDA(cudaMemsetAsync(bc.has_best, 0, B * 4, s));
+        LB_CUDA(cudaMemsetAsync(bc.save, 0, B * 4, s));
+        const std::vector<int> ones(B, 1);
+        LB_CUDA(cudaMemcpyAsync(bc.first_save, ones.data(), B * 4, cudaMemcpyHostToDevice, s));
         for (int st = 2; st <= K_; ++st)
             for (int m = 1; m < st; ++m) {
                 const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
-                float* a = cache_.as<float>(key("alpha", m, st), cnt);
-                float* best_a = cache_.as<float>(key("abest", m, st), cnt);
-                if (it == 0)
-                    LB_CUDA(cudaMemcpyAsync(best_a, a, cnt * 4, cudaMemcpyDeviceToDevice, s));
+                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("am", m, st), cnt), 0, cnt * 4, s));
+                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("av", m, st), cnt), 0, cnt * 4, s));
+            }
+        float lr = opt_.alpha_lr;
+        int steps = 0;
+        for (it = 0; it < iters; ++it) {
+            const bool last = it == iters - 1;
+            run_pass(Pass::ALPHA_ITER, B, nspec, s);
+            val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
+            launch_scatter_output(out.rows, val_out, nspec, up, cur_lb, cur_ub, s);
+            if (n_active) LB_CUDA(cudaMemsetAsync(n_active, 0, sizeof(int), s));
+            if (up) {
+                // Minimising ub is maximising -ub (see launch_alpha_control).
+                launch_negate(cur_ub, neg_ub, (int64_t)B * nspec, s);
+                launch_alpha_control(bc, neg_ub, cur_lb, B, nspec, it, save_after, (int)opt_.early_stop_patience,
+                                     !last, s);
+            } else {
+                launch_alpha_control(bc, cur_lb, nullptr, B, nspec, it, save_after, (int)opt_.early_stop_patience,
+                                     !last, s);
+            }
+            for (int m = 1; m < K_; ++m) {
+                const size_t bn = (size_t)B * width(m);
+                launch_snapshot(bc.save, cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn),
+                                B, width(m), cache_.as<float>(key("best_l", m), bn),
+                                cache_.as<float>(key("best_u", m), bn), s);
+            }
+            // updateBestAlphas: every active box saves at iteration 0 (nothing is
+            // best yet, so every spec improves), which is each box's first save
+            // and copies every row; later saves copy only rows whose index inside
+            // the box is an improved spec index.
+            for (int st = 2; st <= K_; ++st)
+                for (int m = 1; m < st; ++m) {
+                    const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
+                    float* a = cache_.as<float>(key("alpha", m, st), cnt);
+                    float* best_a = cache_.as<float>(key("abest", m, st), cnt);
+                    if (it == 0)
+                        LB_CUDA(cudaMemcpyAsync(best_a, a, cnt * 4, cudaMemcpyDeviceToDevice, s));
+                    else
+                        launch_best_alpha_rows(starts_[st].rows, B, bc.save, bc.improved, nspec, rowlen(st, m), a,
+                                               best_a, s);
+                }
+            launch_clear_first_save(bc.save, bc.first_save, B, s);
+            if (last) break;
+            if (n_active) {
+                // Later iterations change nothing for a box that has stopped, so
+                // once every box has stopped the loop can end.
+                int h_active = 0;
+                LB_CUDA(cudaMemcpyAsync(&h_active, n_active, sizeof(int), cudaMemcpyDeviceToHost, s));
+                LB_CUDA(cudaStreamSynchronize(s));
+                if (h_active == 0) break;
+            }
+            // --- hand-written adjoint of the whole pass (replaces loss.backward())
+            // with the torch::optim::Adam step + [0, 1] clip fused into it ---------
+            for (int m = 1; m < K_; ++m) {
+                const size_t bn = (size_t)B * width(m);
+                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("kbar", m), bn), 0, bn * 4, s));
+                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("bbar", m), bn), 0, bn * 4, s));
+                if (act_[m] == ACT_SIGMOID) {
+                    LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("sbar", m), bn), 0, bn * 4, s));
+                    LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("blbar", m), bn), 0, bn * 4, s));
+                }
+            }
+            ++steps;
+            adam_active_ = bc.active;
+            adam_step_ = (float)((double)lr / (1.0 - std::pow(0.9, steps)));
+            adam_bc2_sqrt_ = (float)std::sqrt(1.0 - std::pow(0.999, steps));
+            if (up) {
+                // loss = sum ub: the upper rows of the output start, seed +1.
+                launch_output_seed_upper(out.rows, bc.active, gout, s);
+                adjoint_start(out, B, gout, 2 * out.rows.R, s);
+            } else {
+                launch_output_seed(out.rows, bc.active, gout, s);
+                adjoint_start(out, B, gout, out.rows.R, s);
+            }
+            for (int st = K_ - 1; st >= 2; --st) {
+                StartPlan& sp = starts_[st];
+                if (sp.rows.R == 0) continue;
+                const size_t bn = (size_t)B * width(st);
+                float* g = cache_.as<float>(key("g", st), (size_t)2 * sp.rows.R);
+                if (act_[st] == ACT_SIGMOID)
+                    launch_sigmoid_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn),
+                                              cache_.as<float>(key("cur_u", st), bn),
+                                              cache_.as<float>(key("sbar", st), bn),
+                                              cache_.as<float>(key("blbar", st), bn),
+                                              cache_.as<float>(key("kbar", st), bn),
+                                              cache_.as<float>(key("bbar", st), bn), width(st), g, s);
                 else
-                    launch_best_alpha_rows(starts_[st].rows, B, bc.save, bc.improved, nspec, rowlen(st, m), a, best_a,
-                                           s);
+                    launch_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn),
+                                      cache_.as<float>(key("cur_u", st), bn), cache_.as<uint8_t>(key("rp_f", st), bn),
+                                      cache_.as<float>(key("kbar", st), bn), cache_.as<float>(key("bbar", st), bn),
+                                      width(st), g, s);
+                adjoint_start(sp, B, g, 2 * sp.rows.R, s);
             }
-        launch_clear_first_save(bc.save, bc.first_save, B, s);
-        if (last) break;
-        if (n_active) {
-            // Later iterations change nothing for a box that has stopped, so
-            // once every box has stopped the loop can end.
-            int h_active = 0;
-            LB_CUDA(cudaMemcpyAsync(&h_active, n_active, sizeof(int), cudaMemcpyDeviceToHost, s));
-            LB_CUDA(cudaStreamSynchronize(s));
-            if (h_active == 0) break;
+            lr = lr * opt_.alpha_lr_decay;
         }
-        // --- hand-written adjoint of the whole pass (replaces loss.backward())
-        // with the torch::optim::Adam step + [0, 1] clip fused into it ---------
-        for (int m = 1; m < K_; ++m) {
-            const size_t bn = (size_t)B * width(m);
-            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("kbar", m), bn), 0, bn * 4, s));
-            LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("bbar", m), bn), 0, bn * 4, s));
-            if (act_[m] == ACT_SIGMOID) {
-                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("sbar", m), bn), 0, bn * 4, s));
-                LB_CUDA(cudaMemsetAsync(cache_.as<float>(key("blbar", m), bn), 0, bn * 4, s));
+        // --- restoreBestAlphas, restoreBestIntermediateBounds, final run(false) ---
+        for (int st = 2; st <= K_; ++st)
+            for (int m = 1; m < st; ++m) {
+                const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
+                launch_restore_alpha(starts_[st].rows, bc.first_save, rowlen(st, m),
+                                     cache_.as<float>(key("abest", m, st), cnt),
+                                     cache_.as<float>(key("alpha", m, st), cnt), s);
             }
+        run_pass(Pass::ALPHA_FINAL, B, nspec, s);
+        val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
+        if (up) {
+            // Upper: min(final, best).  A lower side that is not optimised is
+            // the runCROWN that follows (:858-862), over the same nodes: the
+            // lower side of this pass.
+            launch_scatter_output(out.rows, val_out, nspec, true, fin_lb, fin_ub, s);
+            launch_negate(fin_ub, neg_ub, (int64_t)B * nspec, s);
+            launch_max_best(bc.best, bc.has_best, B * nspec, nspec, neg_ub, s);
+            launch_negate(neg_ub, ub, (int64_t)B * nspec, s);
+            if (!opt_lower) LB_CUDA(cudaMemcpyAsync(lb, fin_lb, (size_t)B * nspec * 4, cudaMemcpyDeviceToDevice, s));
+        } else {
+            // Lower: max(final, best).  An upper side that is not optimised
+            // comes from the runCROWN that follows, over the same nodes (same
+            // best intermediate bounds and alphas): the upper side of this pass.
+            launch_scatter_output(out.rows, val_out, nspec, upper && !opt_upper, lb, ub, s);
+            launch_max_best(bc.best, bc.has_best, B * nspec, nspec, lb, s);
         }
-        ++steps;
-        adam_active_ = bc.active;
-        adam_step_ = (float)((double)lr / (1.0 - std::pow(0.9, steps)));
-        adam_bc2_sqrt_ = (float)std::sqrt(1.0 - std::pow(0.999, steps));
-        launch_output_seed(out.rows, bc.active, gout, s);
-        adjoint_start(out, B, gout, out.rows.R, s);
-        for (int st = K_ - 1; st >= 2; --st) {
-            StartPlan& sp = starts_[st];
-            if (sp.rows.R == 0) continue;
-            const size_t bn = (size_t)B * width(st);
-            float* g = cache_.as<float>(key("g", st), (size_t)2 * sp.rows.R);
-            if (act_[st] == ACT_SIGMOID)
-                launch_sigmoid_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn),
-                                          cache_.as<float>(key("cur_u", st), bn), cache_.as<float>(key("sbar", st), bn),
-                                          cache_.as<float>(key("blbar", st), bn), cache_.as<float>(key("kbar", st), bn),
-                                          cache_.as<float>(key("bbar", st), bn), width(st), g, s);
-            else
-                launch_bound_grad(sp.rows, cache_.as<float>(key("cur_l", st), bn),
-                                  cache_.as<float>(key("cur_u", st), bn), cache_.as<uint8_t>(key("rp_f", st), bn),
-                                  cache_.as<float>(key("kbar", st), bn), cache_.as<float>(key("bbar", st), bn),
-                                  width(st), g, s);
-            adjoint_start(sp, B, g, 2 * sp.rows.R, s);
-        }
-        lr = lr * opt_.alpha_lr_decay;
+        iters_run_ = std::max(iters_run_, std::min(it + 1, iters));
     }
-    // --- restoreBestAlphas, restoreBestIntermediateBounds, final run(false) ---
-    for (int st = 2; st <= K_; ++st)
-        for (int m = 1; m < st; ++m) {
-            const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
-            launch_restore_alpha(starts_[st].rows, bc.first_save, rowlen(st, m), cache_.as<float>(key("abest", m, st), cnt),
-                                 cache_.as<float>(key("alpha", m, st), cnt), s);
-        }
-    run_pass(Pass::ALPHA_FINAL, B, nspec, s);
-    val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
-    // Lower: max(final, best).  Upper: runCROWN over the same nodes, i.e. the
-    // upper side of this pass (same best intermediate bounds and alphas).
-    launch_scatter_output(out.rows, val_out, nspec, upper, lb, ub, s);
-    launch_max_best(bc.best, bc.has_best, B * nspec, nspec, lb, s);
     if (done) launch_take_verified(done, crown_lb, crown_ub, B, nspec, lb, ub, s);
-    iters_run_ = std::max(iters_run_, std::min(it + 1, iters));
     (void)nout;
 }
 

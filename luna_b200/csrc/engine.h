@@ -143,7 +143,9 @@ private:
     void run_chunk(int method, const float* xl, const float* xu, int B, const float* C, int c_per_box,
                    int nspec, bool upper, float* lb, float* ub, cudaStream_t s);
 
-    enum class Pass { CROWN, ALPHA_FIRST, ALPHA_ITER, ALPHA_FINAL };
+    // ALPHA_RESTART: the first pass of a second optimisation run (the lower
+    // side after the upper one): alphas kept, no STE reference bounds.
+    enum class Pass { CROWN, ALPHA_FIRST, ALPHA_ITER, ALPHA_FINAL, ALPHA_RESTART };
     void run_pass(Pass pass, int B, int nspec, cudaStream_t s);
     void forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s);
     void adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s);

@@ -890,8 +890,8 @@ void launch_scatter_output(const RowMap& rows, const float* val, int nspec, bool
 }
 
 // ============================================================== control
-__global__ void alpha_control_kernel(BoxControl c, const float* __restrict__ cur, int B, int nspec,
-                                     int iter, int save_after, int patience_limit, bool has_loss) {
+__global__ void alpha_control_kernel(BoxControl c, const float* __restrict__ cur, const float* __restrict__ verify,
+                                     int B, int nspec, int iter, int save_after, int patience_limit, bool has_loss) {
     const int bx = blockIdx.x * blockDim.x + threadIdx.x;
     if (bx >= B) return;
     c.save[bx] = 0;
@@ -899,7 +899,8 @@ __global__ void alpha_control_kernel(BoxControl c, const float* __restrict__ cur
     const float* cv = cur + (size_t)bx * nspec;
     float* best = c.best + (size_t)bx * nspec;
     uint8_t* imp = c.improved + (size_t)bx * nspec;
-    if (c.thr && lb200::box_verified(cv, c.thr, c.branch, nspec, c.n_branches)) {
+    const float* vv = verify ? verify + (size_t)bx * nspec : cv;
+    if (c.thr && lb200::box_verified(vv, c.thr, c.branch, nspec, c.n_branches)) {
         // Verified during the optimisation (AlphaCROWNAnalysis.cpp:396-407):
         // the best bound takes this iteration's, nothing is saved, the box
         // stops.
@@ -983,9 +984,9 @@ void launch_take_verified(const int* done, const float* crown_lb, const float* c
     LB_LAUNCH();
 }
 
-void launch_alpha_control(const BoxControl& c, const float* cur, int B, int nspec, int iter,
+void launch_alpha_control(const BoxControl& c, const float* cur, const float* verify, int B, int nspec, int iter,
                           int save_after, int patience_limit, bool has_loss, cudaStream_t s) {
-    alpha_control_kernel<<<ceil_div(B, 128), 128, 0, s>>>(c, cur, B, nspec, iter, save_after,
+    alpha_control_kernel<<<ceil_div(B, 128), 128, 0, s>>>(c, cur, verify, B, nspec, iter, save_after,
                                                           patience_limit, has_loss);
     LB_LAUNCH();
 }
@@ -1192,6 +1193,30 @@ __global__ void output_seed_kernel(RowMap rows, const int* __restrict__ active, 
 void launch_output_seed(const RowMap& rows, const int* active, float* g, cudaStream_t s) {
     if (rows.R == 0) return;
     output_seed_kernel<<<ceil_div(rows.R, 256), 256, 0, s>>>(rows, active, g);
+    LB_LAUNCH();
+}
+
+__global__ void output_seed_upper_kernel(RowMap rows, const int* __restrict__ active, float* __restrict__ g) {
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows.R) return;
+    g[r] = 0.f;
+    g[rows.R + r] = active[rows.row_box[r]] ? 1.f : 0.f;
+}
+
+void launch_output_seed_upper(const RowMap& rows, const int* active, float* g, cudaStream_t s) {
+    if (rows.R == 0) return;
+    output_seed_upper_kernel<<<ceil_div(rows.R, 256), 256, 0, s>>>(rows, active, g);
+    LB_LAUNCH();
+}
+
+__global__ void negate_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t n) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = -in[i];
+}
+
+void launch_negate(const float* in, float* out, int64_t n, cudaStream_t s) {
+    if (n == 0) return;
+    negate_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(in, out, n);
     LB_LAUNCH();
 }
 

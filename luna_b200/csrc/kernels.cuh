@@ -264,8 +264,13 @@ struct BoxControl {
     int* n_active = nullptr;        // [1] boxes still optimising after this iteration
 };
 // One iteration's bookkeeping (AlphaCROWNAnalysis.cpp:394-472) for every
-// active box.  `cur` is the current lower bound [B, nspec].
-void launch_alpha_control(const BoxControl& c, const float* cur, int B, int nspec, int iter,
+// active box.  `cur` is the bound being maximised [B, nspec]: the current
+// lower bound, or the negated upper bound when the upper side is optimised
+// (best = min, improvement = decrease and loss = sum of ub are then the same
+// arithmetic).  `verify` [B, nspec] (or null: `cur`) holds the lower bounds
+// that STOP_ALPHA_ON_VERIFIED checks (isSpecVerified reads lower bounds on
+// either side, AlphaCROWNAnalysis.cpp:396-407).
+void launch_alpha_control(const BoxControl& c, const float* cur, const float* verify, int B, int nspec, int iter,
                           int save_after, int patience_limit, bool has_loss, cudaStream_t s);
 // STOP_CROWN_ON_VERIFIED (TorchModel.cpp:816-834): done[b] = the box's CROWN
 // lower bounds lb [B, nspec] verify the specification; active[b] = !done[b];
@@ -307,6 +312,11 @@ void launch_bound_grad(const RowMap& rows, const float* cur_l, const float* cur_
                        float* g, cudaStream_t s);
 // Output-start seed: g[r] = -1 for rows of active boxes (loss = -sum lb), 0 else.
 void launch_output_seed(const RowMap& rows, const int* active, float* g, cudaStream_t s);
+// Output-start seed for the upper side [2R]: 0 on the lower rows, +1 on the
+// upper rows of active boxes (loss = sum ub, AlphaCROWNAnalysis::computeLoss).
+void launch_output_seed_upper(const RowMap& rows, const int* active, float* g, cudaStream_t s);
+// out[i] = -in[i].
+void launch_negate(const float* in, float* out, int64_t n, cudaStream_t s);
 
 // alpha = best_alpha on the rows of boxes that saved at least once
 // (AlphaCROWNAnalysis::restoreBestAlphas).

@@ -348,6 +348,10 @@ void dispatch_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcC
 
 }  // namespace
 
+void tc_conv_set_wait_limit(long long wait_cycles) {
+    LB_CUDA(cudaMemcpyToSymbol(tcx::g_wait_limit, &wait_cycles, sizeof(wait_cycles)));
+}
+
 bool tc_conv_supported(int data_C, int nx) { return data_C % 32 == 0 && data_C > 0 && nx >= 1 && nx <= 256; }
 
 void tc_conv_tile(TcConvPlan& p, int rows) {

@@ -44,6 +44,10 @@ enum { KIND_FWD = 0, KIND_CONC = 1, KIND_QBAR = 3, KIND_STOREP = 4 };
 enum { AMODE_TMA = 0, AMODE_SEED = 1, AMODE_RELAX = 2, AMODE_GATHER = 3 };
 
 __device__ int g_tc_error;
+// Failure-detection test hook (tc_set_test_fault): when set, the TMA
+// producers announce their loads but issue none, so every consumer's bounded
+// wait runs out and the kernels return with g_tc_error raised.
+__device__ int g_tc_starve;
 
 struct TcEpi {
     EpiRelaxFwd f;
@@ -275,6 +279,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (warp == WARP_TMA) {
         if (lane == 0) {
             uint32_t g = 0;
+            const bool starve = g_tc_starve != 0;
             for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
                 const int mb = t / tiles_n, nb = t % tiles_n;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
@@ -287,6 +292,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     const bool load_alpha = (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) && pro.alpha;
                     mbar_arrive_tx(&full[s], (load_a ? A_TILE_BYTES : 0) + (load_alpha ? A_TILE_BYTES : 0) +
                                                  2 * B_TILE_BYTES);
+                    if (starve) continue;
                     if (load_a) tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
                     if (load_alpha) tma_load_2d(&talpha, &full[s], a_lo(s), kb * TC_BK, mb * TC_BM);
                     tma_load_2d(&tbh, &full[s], b_hi(s), kb * TC_BK, nb * BN);
@@ -649,6 +655,13 @@ int tc_block_n(int N) {
 }
 
 int tc_tiles_n(int N) { return (N + tc_block_n(N) - 1) / tc_block_n(N); }
+
+void tc_set_test_fault(int starve, long long wait_cycles) {
+    const long long w = wait_cycles > 0 ? wait_cycles : WAIT_CYCLES;
+    LB_CUDA(cudaMemcpyToSymbol(g_tc_starve, &starve, sizeof(int)));
+    LB_CUDA(cudaMemcpyToSymbol(g_wait_limit, &w, sizeof(w)));
+    tc_conv_set_wait_limit(w);
+}
 
 int* tc_error_flag() {
     void* p = nullptr;

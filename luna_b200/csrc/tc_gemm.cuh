@@ -26,6 +26,11 @@ void launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, cudaSt
 // Device error flag written by a tensor-core kernel whose bounded waits ran
 // out (0 = ok).  The engine checks it after each call.
 int* tc_error_flag();
+// Failure-detection test hook, on the current device: starve = 1 makes the
+// tensor-core contraction producers issue no loads (their consumers' waits
+// run out); wait_cycles > 0 sets the waits' limit (0: the default ~2 s).
+void tc_set_test_fault(int starve, long long wait_cycles);
+void tc_conv_set_wait_limit(long long wait_cycles);
 
 // Adjoint contraction storing Qbar = A . B^T + g b_lin only; with
 // e.seed_sign set the A operand is generated from the concretisation signs.

@@ -10,6 +10,9 @@ namespace lb200 {
 namespace tcx {
 
 constexpr long long WAIT_CYCLES = 4000000000LL;  // ~2 s at 2 GHz
+// The wait limit the kernels of one translation unit use (WAIT_CYCLES unless
+// a failure-detection test shortens it).
+static __device__ long long g_wait_limit = WAIT_CYCLES;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -36,16 +39,17 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
     return ok != 0;
 }
 // Wait for the phase of parity `parity` to complete.  Gives up when another
-// role raised `abort` (unless ignore_abort) or after WAIT_CYCLES, in which
-// case it raises `abort` and the device error flag `err`.
+// role raised `abort` (unless ignore_abort) or after g_wait_limit cycles, in
+// which case it raises `abort` and the device error flag `err`.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort, int* err,
                                           bool ignore_abort = false) {
     if (mbar_try(b, parity)) return true;
     const long long t0 = clock64();
+    const long long limit = g_wait_limit;
     while (true) {
         if (mbar_try(b, parity)) return true;
         if (!ignore_abort && *abort) return false;
-        if (clock64() - t0 > WAIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             *abort = 1;
             atomicExch(err, 1);
             return false;

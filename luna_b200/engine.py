@@ -27,7 +27,8 @@ EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_shard_range", "lb200_nccl_unique_id", "lb200_nccl_comm_create", "lb200_nccl_comm_destroy",
            "lb200_shard_run", "lb200_describe_plan", "lb200_property_parse", "lb200_property_get_info",
            "lb200_property_input_box", "lb200_property_spec", "lb200_property_free", "lb200_property_status",
-           "lb200_property_status_device", "lb200_compute_property", "lb200_compute_property_device")
+           "lb200_property_status_device", "lb200_compute_property", "lb200_compute_property_device",
+           "lb200_test_set_contraction_fault")
 
 
 class EngineError(RuntimeError):
@@ -69,6 +70,7 @@ def load_library():
     lib.lb200_nccl_comm_destroy.argtypes = [vp]
     lib.lb200_shard_run.argtypes = [vp, vp, C.c_int, C.c_int, C.c_int, fp, fp, C.c_int64, fp, C.c_int64,
                                     C.c_int64, fp, fp, C.c_int, C.POINTER(Stats)]
+    lib.lb200_test_set_contraction_fault.argtypes = [C.c_int, C.c_int, C.c_int64]
     lib.lb200_describe_plan.argtypes = [C.POINTER(GraphDesc), C.POINTER(Options), C.c_char_p, C.c_size_t,
                                         C.POINTER(C.c_size_t)]
     ip = C.POINTER(C.c_int32)
@@ -85,6 +87,14 @@ def load_library():
                                                   C.POINTER(Stats)]
     _lib = lib
     return lib
+
+
+def set_contraction_fault(device: int, starve: bool, wait_cycles: int = 0) -> None:
+    """Failure-detection test hook (lb200_test_set_contraction_fault): with
+    starve the tensor-core kernels' bounded waits run out on `device`."""
+    load_library()
+    _check(_lib.lb200_test_set_contraction_fault(device, 1 if starve else 0, wait_cycles),
+           "lb200_test_set_contraction_fault")
 
 
 def _check(rc: int, what: str):

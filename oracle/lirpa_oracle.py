@@ -794,28 +794,51 @@ class LirpaOracle:
                 inter = {i: st0.node_bounds[i] for i in self.preact_ids if i in st0.node_bounds}
                 return lo0.detach(), hi0.detach(), inter
         st = _BoxState(method_alpha=True, first_linear_ibp=False)
-        out = self.g.output_index
-        # The CROWN initialisation pass (AlphaCROWNAnalysis.cpp:118-129) only
-        # matters with thresholds; its state is cleared before optimisation.
-        # --- computeOptimizedBounds(Lower)
         st.alpha_mode = True
-        st.node_bounds, st.concrete = {}, {}
-        lo, hi = self._run(st, x, C)
+        # TorchModel::runAlphaCROWN (:838-862): the upper side first when it is
+        # optimised, then the lower side, in one AlphaCROWNAnalysis (the alphas
+        # carry over); a side that is not optimised comes from the runCROWN
+        # that follows; with neither side optimised it is runCROWN alone.
+        sides = ([True] if o.optimize_upper else []) + ([False] if o.optimize_lower else [])
+        if not sides:
+            lo, hi, st0 = self.crown(xl, xu, C)
+            inter = {i: st0.node_bounds[i] for i in self.preact_ids if i in st0.node_bounds}
+            return lo.detach(), hi.detach(), inter
+        res = {}
+        for up in sides:
+            res[up] = self._optimize_side(st, x, C, up, trace, spec)
+        lb = res[False][0] if False in res else res[True][1]
+        ub = res[True][0] if True in res else res[False][1]
+        return lb, ub, res[sides[-1]][2]
+
+    def _optimize_side(self, st, x, C, upper, trace, spec):
+        """AlphaCROWNAnalysis::computeOptimizedBounds(side)
+        (src/engine/AlphaCROWNAnalysis.cpp:306-511) on the state `st` (alphas
+        kept across calls).  Upper: loss = sum ub, best = min, improvement =
+        decrease; STOP_ALPHA_ON_VERIFIED checks the lower bounds on either
+        side.  Returns (the optimised side's bound, the other side from the
+        runCROWN that follows over the same nodes, best intermediate bounds)."""
+        o = self.opt
+        st.node_bounds, st.concrete, st.reference = {}, {}, {}
+        self._run(st, x, C)
         best_int = {i: (st.node_bounds[i][0].detach().clone(), st.node_bounds[i][1].detach().clone())
                     for i in self.preact_ids if i in st.node_bounds}
         if o.stabilize_intermediate_bounds:
             st.reference = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
+
+        def other_side():
+            st2 = _BoxState(node_bounds={k: v for k, v in st.node_bounds.items() if k in best_int},
+                            alphas=st.alphas, alpha_mode=True, method_alpha=True, first_linear_ibp=False)
+            lo2, hi2 = self._run(st2, x, C)
+            return (lo2 if upper else hi2).detach()
+
         params = [ap.alpha for ap in st.alphas.values() if ap.alpha.requires_grad]
         if not params:
             # collectAlphaParameters() found nothing to optimise: one more
             # run(false) over the bounds still on the nodes (:360-364).
             with torch.no_grad():
-                lo, _ = self._run(st, x, C)
-                st2 = _BoxState(node_bounds={k: v for k, v in st.node_bounds.items() if k in best_int},
-                                alphas=st.alphas, alpha_mode=True, method_alpha=True,
-                                first_linear_ibp=False)
-                _, hi = self._run(st2, x, C)
-            return lo.detach(), hi.detach(), best_int
+                lo, hi = self._run(st, x, C)
+                return (hi if upper else lo).detach(), other_side(), best_int
         adam = _Adam(params)
         iters = int(o.alpha_iterations)
         best = None
@@ -828,20 +851,20 @@ class LirpaOracle:
             st.node_bounds, st.concrete = {}, {}
             with torch.set_grad_enabled(not last):
                 cur_l, cur_u = self._run(st, x, C)
-            cur = cur_l.detach()
+            cur = (cur_u if upper else cur_l).detach()
             if trace is not None:
                 trace.append(cur.clone())
-            if spec is not None and o.stop_alpha_on_verified and self.verified(cur, spec):
-                best = cur.clone() if best is None else torch.max(best, cur)
+            if spec is not None and o.stop_alpha_on_verified and self.verified(cur_l.detach(), spec):
+                best = cur.clone() if best is None else (torch.min(best, cur) if upper else torch.max(best, cur))
                 break
-            loss = None if last else -cur_l.sum()
+            loss = None if last else (cur_u.sum() if upper else -cur_l.sum())
             if best is None:
                 best = cur.clone()
                 improved_idx = list(range(cur.numel()))
             else:
-                improved_idx = torch.nonzero(cur > best).flatten().tolist()
+                improved_idx = torch.nonzero(cur < best if upper else cur > best).flatten().tolist()
                 if improved_idx:
-                    best = torch.max(best, cur)
+                    best = torch.min(best, cur) if upper else torch.max(best, cur)
             improved = len(improved_idx) > 0
             save = it < 1 or it > int(iters * o.start_save_best) or patience >= o.early_stop_patience
             if improved and save:
@@ -886,18 +909,17 @@ class LirpaOracle:
             st.reference = {}
             st.concrete = {}
             st.node_bounds = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
-            fin_l, _ = self._run(st, x, C)
-            lb_final = torch.max(fin_l, best) if best is not None else fin_l
+            fin_l, fin_u = self._run(st, x, C)
+            if upper:
+                final = torch.min(fin_u, best) if best is not None else fin_u
+            else:
+                final = torch.max(fin_l, best) if best is not None else fin_l
             # runCROWN for the non-optimised side: a new analysis over the same
             # nodes, whose pre-activation bounds are still the best ones and
             # whose ReLUs still read the optimised alphas (stage "opt").
-            st2 = _BoxState(node_bounds={k: v for k, v in st.node_bounds.items()
-                                         if k in best_int},
-                            alphas=st.alphas, alpha_mode=True, method_alpha=True,
-                            first_linear_ibp=False)
-            _, ub_final = self._run(st2, x, C)
+            other = other_side()
         inter = {k: (v[0].clone(), v[1].clone()) for k, v in best_int.items()}
-        return lb_final.detach(), ub_final.detach(), inter
+        return final.detach(), other, inter
 
     @staticmethod
     def _update_best_alphas(st, best_alpha, improved_idx):

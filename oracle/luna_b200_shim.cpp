@@ -1,6 +1,7 @@
 // luna_b200_shim.cpp -- see luna_b200_shim.h.
 #include "luna_b200_shim.h"
 
+#include <cstring>
 #include <stdexcept>
 #include <variant>
 
@@ -176,7 +177,7 @@ TorchModel::TorchModel(const std::vector<std::shared_ptr<BoundedNode>>& nodes,
         d.running_var = node.vars().empty() ? nullptr : node.vars().data();
         d.constant = node.constants().empty() ? nullptr : node.constants().data();
     }
-    lb200_graph_desc g{};
+    lb200_graph_desc& g = graph_;
     g.num_nodes = n;
     g.nodes = descs_.data();
     g.input_index = (int32_t)inputIndices[0];
@@ -185,7 +186,16 @@ TorchModel::TorchModel(const std::vector<std::shared_ptr<BoundedNode>>& nodes,
     const lb200_node_desc& dout = descs_[g.output_index];
     n_in_ = (unsigned)din.out_shape[0] * din.out_shape[1] * din.out_shape[2];
     n_out_ = (unsigned)dout.out_shape[0] * dout.out_shape[1] * dout.out_shape[2];
-    check(lb200_model_create(&g, device, &model_), "lb200_model_create");
+    if (device >= 0) check(lb200_model_create(&g, device, &model_), "lb200_model_create");
+}
+
+std::string TorchModel::describe() const {
+    size_t need = 0;
+    check(lb200_describe_plan(&graph_, nullptr, nullptr, 0, &need), "lb200_describe_plan");
+    std::string buf(need, '\0');
+    check(lb200_describe_plan(&graph_, nullptr, buf.data(), need, &need), "lb200_describe_plan");
+    buf.resize(std::strlen(buf.c_str()));
+    return buf;
 }
 
 TorchModel::~TorchModel() {
@@ -252,6 +262,7 @@ BoundedTensor<torch::Tensor> TorchModel::run(const BoundedTensor<torch::Tensor>&
     o.stop_alpha_on_verified = LunaConfiguration::STOP_ALPHA_ON_VERIFIED;
     o.enable_first_linear_ibp = LunaConfiguration::ENABLE_FIRST_LINEAR_IBP;
     o.use_patches_mode = LunaConfiguration::USE_PATCHES_MODE;
+    if (!model_) throw std::runtime_error("lb200_luna: a host-only model (device < 0) cannot bound");
     check(lb200_set_options(model_, &o), "lb200_set_options");
     auto lb = torch::zeros({B, nspec}, torch::kFloat32);
     auto ub = torch::zeros({B, nspec}, torch::kFloat32);

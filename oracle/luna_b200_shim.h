@@ -170,12 +170,18 @@ public:
     BoundedTensor<torch::Tensor> getFinalAnalysisBounds() const { return final_; }
     unsigned getInputSize() const { return n_in_; }
     unsigned getOutputSize() const { return n_out_; }
+    // The engine's graph description and its host-only plan (levels, starts,
+    // concretisation forms as JSON, lb200_describe_plan).  A model made with
+    // device < 0 has only these: no GPU is touched.
+    const lb200_graph_desc& graph() const { return graph_; }
+    std::string describe() const;
 
 private:
     BoundedTensor<torch::Tensor> run(const BoundedTensor<torch::Tensor>& in, int method, bool lower, bool upper,
                                      bool opt_lower, bool opt_upper);
     std::vector<std::shared_ptr<BoundedNode>> nodes_;
     std::vector<lb200_node_desc> descs_;
+    lb200_graph_desc graph_{};
     lb200_model* model_ = nullptr;
     unsigned n_in_ = 0, n_out_ = 0;
     torch::Tensor C_;

@@ -1,13 +1,17 @@
 // luna_shim_check.cpp -- test infrastructure, not product code.
 //
 // Checks the Luna-side shim (luna_b200_shim.h) the way a Luna front end
-// would use it: for one graph description, torch modules are made once and
+// would use it: for one graph description, torch modules are made and
 // handed both to Luna's own node constructors (an NLR::TorchModel, Luna's
 // CPU path) and to the shim's (an lb200_luna::TorchModel, the B200 engine),
 // exactly as OnnxToTorchParser would build the two side by side
 // (OnnxToTorch.cpp:1672-1696,2173-2200,2425-2444,2680-2717).  Both models
 // bound the same box through TorchModel::compute_bounds; the caller compares
-// the results.  Built by oracle/Makefile into oracle/_ref/libluna_shim_check.so.
+// the results.  Luna's CPU path picks the patches form for every conv start
+// when CUDA is available to its process (CROWNAnalysis.cpp:261-271) and by a
+// 4096-feature threshold otherwise, so a caller on a GPU host runs Luna's
+// side (`which` = 1) in a process with CUDA hidden and the shim's (`which` =
+// 2) in its own.  Built by oracle/Makefile into oracle/_ref/libluna_shim_check.so.
 #include "luna_b200_shim.h"
 
 #include "TorchModel.h"
@@ -185,14 +189,17 @@ void set_error(char* err, size_t len, const std::string& msg) {
 
 extern "C" {
 
-// One box through both models.  method: LB200_METHOD_CROWN or
-// LB200_METHOD_ALPHA_CROWN; C [nspec, n_out]; results [nspec] each.
-// The LunaConfiguration flags are set from `opt` before either model runs.
+// One box through Luna's model (which & 1) and the shim's (which & 2, on
+// CUDA device `device`).  method: LB200_METHOD_CROWN or
+// LB200_METHOD_ALPHA_CROWN; C [nspec, n_out]; results [nspec] each.  The
+// LunaConfiguration flags are set from `opt` before each model runs.
 int luna_shim_check(const lb200_graph_desc* g, const lb200_options* opt, int method, const float* x_lower,
                     const float* x_upper, int64_t n_in, const float* C, int64_t nspec, int64_t n_out, int device,
-                    float* luna_lb, float* luna_ub, float* shim_lb, float* shim_ub, char* err, size_t errlen) {
+                    int which, float* luna_lb, float* luna_ub, float* shim_lb, float* shim_ub, char* err,
+                    size_t errlen) {
     try {
         at::set_num_threads(1);
+        auto configure = [&] {
         LunaConfiguration::ALPHA_ITERATIONS = opt->alpha_iterations;
         LunaConfiguration::ALPHA_LR = opt->alpha_lr;
         LunaConfiguration::ALPHA_LR_DECAY = opt->alpha_lr_decay;
@@ -209,6 +216,7 @@ int luna_shim_check(const lb200_graph_desc* g, const lb200_options* opt, int met
         LunaConfiguration::USE_PATCHES_MODE = opt->use_patches_mode != 0;
         LunaConfiguration::USE_CUDA = false;
         LunaConfiguration::DEVICE = torch::Device(torch::kCPU);
+        };
 
         Vector<std::shared_ptr<NLR::BoundedTorchNode>> luna_nodes;
         Map<unsigned, Vector<unsigned>> luna_deps;
@@ -229,25 +237,75 @@ int luna_shim_check(const lb200_graph_desc* g, const lb200_options* opt, int met
         }
         Vector<unsigned> luna_in;
         luna_in.append((unsigned)g->input_index);
-        NLR::TorchModel luna(luna_nodes, luna_in, (unsigned)g->output_index, luna_deps);
-        lb200_luna::TorchModel shim(shim_nodes, {(unsigned)g->input_index}, (unsigned)g->output_index, shim_deps,
-                                    device);
-
         const auto am = method == LB200_METHOD_ALPHA_CROWN ? LunaConfiguration::AnalysisMethod::AlphaCROWN
                                                           : LunaConfiguration::AnalysisMethod::CROWN;
         BoundedTensor<torch::Tensor> box(from_host(x_lower, {n_in}), from_host(x_upper, {n_in}));
         torch::Tensor spec = from_host(C, {nspec, 1, n_out});
-        auto rl = luna.compute_bounds(box, &spec, am, true, true);
-        auto rs = shim.compute_bounds(box, &spec, am, true, true);
         auto put = [&](const torch::Tensor& t, float* dst) {
             auto c = t.detach().to(torch::kFloat32).contiguous().reshape({-1});
             if (c.numel() != nspec) throw std::runtime_error("unexpected result size");
             std::memcpy(dst, c.data_ptr<float>(), (size_t)nspec * 4);
         };
-        put(rl.lower(), luna_lb);
-        put(rl.upper(), luna_ub);
-        put(rs.lower(), shim_lb);
-        put(rs.upper(), shim_ub);
+        if (which & 1) {
+            configure();
+            NLR::TorchModel luna(luna_nodes, luna_in, (unsigned)g->output_index, luna_deps);
+            auto rl = luna.compute_bounds(box, &spec, am, true, true);
+            put(rl.lower(), luna_lb);
+            put(rl.upper(), luna_ub);
+        }
+        if (which & 2) {
+            configure();
+            lb200_luna::TorchModel shim(shim_nodes, {(unsigned)g->input_index}, (unsigned)g->output_index, shim_deps,
+                                        device);
+            auto rs = shim.compute_bounds(box, &spec, am, true, true);
+            put(rs.lower(), shim_lb);
+            put(rs.upper(), shim_ub);
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 1;
+    }
+}
+
+// The shim's graph description of `g` (built as luna_shim_check builds it,
+// no GPU): node kinds, producers, shapes and, per node, the sum of its
+// weight and bias arrays, for comparison with the description the caller
+// made directly.  out: [num_nodes, 12] doubles; raw (may be null): the
+// descriptors themselves, [num_nodes] lb200_node_desc.
+int luna_shim_describe(const lb200_graph_desc* g, double* out, lb200_node_desc* raw, char* err, size_t errlen) {
+    try {
+        std::vector<std::shared_ptr<lb200_luna::BoundedNode>> shim_nodes;
+        std::map<unsigned, std::vector<unsigned>> shim_deps;
+        for (int i = 0; i < g->num_nodes; ++i) {
+            shim_nodes.push_back(make_node(g, i).shim);
+            std::vector<unsigned> sv;
+            for (int k = 0; k < g->nodes[i].num_inputs; ++k) sv.push_back((unsigned)g->nodes[i].inputs[k]);
+            shim_deps[(unsigned)i] = sv;
+        }
+        lb200_luna::TorchModel shim(shim_nodes, {(unsigned)g->input_index}, (unsigned)g->output_index, shim_deps, -1);
+        const lb200_graph_desc& d = shim.graph();
+        if (raw) std::memcpy(raw, d.nodes, sizeof(lb200_node_desc) * d.num_nodes);
+        for (int i = 0; i < d.num_nodes; ++i) {
+            const lb200_node_desc& n = d.nodes[i];
+            double* o = out + 12 * i;
+            o[0] = n.type;
+            o[1] = n.num_inputs;
+            o[2] = n.num_inputs > 0 ? n.inputs[0] : -1;
+            o[3] = n.num_inputs > 1 ? n.inputs[1] : -1;
+            o[4] = n.out_shape[0];
+            o[5] = n.out_shape[1];
+            o[6] = n.out_shape[2];
+            o[7] = n.kernel[0] * 100 + n.stride[0] * 10 + n.padding[0];
+            double ws = 0, bs = 0;
+            const size_t nw = shim_nodes[i]->weights().size(), nb = shim_nodes[i]->biases().size();
+            for (size_t q = 0; q < nw; ++q) ws += n.weight[q];
+            for (size_t q = 0; q < nb; ++q) bs += n.bias[q];
+            o[8] = ws;
+            o[9] = bs;
+            o[10] = (double)nw;
+            o[11] = n.scale;
+        }
         return 0;
     } catch (const std::exception& e) {
         set_error(err, errlen, e.what());

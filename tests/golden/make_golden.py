@@ -138,6 +138,28 @@ def cases():
     out.append(("concat_cnn_alpha", "concat_cnn_case", {"seed": 8}, 3, abi.METHOD_ALPHA_CROWN, a6))
     out.append(("sub_cnn_alpha", "sub_cnn_case", {"seed": 9}, 3, abi.METHOD_ALPHA_CROWN, a6))
     out.append(("sub_cnn_neg_crown", "sub_cnn_case", {"seed": 10, "constant_second": 0}, 3, abi.METHOD_CROWN, {}))
+    # Strided 32/64-channel convs: the tensor-core (tcgen05) conv steps.
+    kw = {"seed": 21, "n_boxes": 3}
+    out.append(("cnnwide_crown", "cnn_wide_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("cnnwide_alpha", "cnn_wide_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 6}))
+    # OPTIMIZE_UPPER: the upper side optimised first, then the lower side
+    # (both), the upper side alone, and neither (runCROWN).
+    up = {"alpha_lr": 0.1, "alpha_iterations": 6, "optimize_upper": 1}
+    out.append(("mlp5_alpha_upper", "mlp_5_50x6_5", {"n_boxes": 8}, 8, abi.METHOD_ALPHA_CROWN, up))
+    out.append(("mlp5_alpha_uponly", "mlp_5_50x6_5", {"n_boxes": 8}, 8, abi.METHOD_ALPHA_CROWN,
+                dict(up, optimize_lower=0)))
+    out.append(("mlp5_alpha_noopt", "mlp_5_50x6_5", {"n_boxes": 8}, 8, abi.METHOD_ALPHA_CROWN,
+                dict(up, optimize_lower=0, optimize_upper=0)))
+    out.append(("mlp784_alpha_upper", "mlp_784_256x4_10", {"n_boxes": 3}, 3, abi.METHOD_ALPHA_CROWN, up))
+    out.append(("cnn_dense_alpha_upper", "small_cnn_case", {"seed": 3, "n_boxes": 4, "big_first": False}, 2,
+                abi.METHOD_ALPHA_CROWN, up))
+    out.append(("cnn_patch_alpha_upper", "small_cnn_case", {"seed": 5, "n_boxes": 3, "big_first": True}, 2,
+                abi.METHOD_ALPHA_CROWN, dict(up, alpha_iterations=4)))
+    out.append(("resnet_alpha_upper", "small_resnet_case", {"seed": 7, "n_boxes": 3}, 2, abi.METHOD_ALPHA_CROWN,
+                dict(up, alpha_iterations=4)))
+    out.append(("convt_alpha_upper", "convt_cnn_case", {"seed": 1, "n_boxes": 3}, 2, abi.METHOD_ALPHA_CROWN,
+                dict(up, alpha_iterations=4)))
     # The MLP alpha-CROWN workload at its own size: all 512 boxes, 20 Adam
     # iterations at lr 0.1.
     out.append(("cfg2_alpha512", "mlp_784_256x4_10", {"n_boxes": 512}, 512, abi.METHOD_ALPHA_CROWN,

@@ -65,3 +65,19 @@ def test_oracle_property_matches_luna(name):
     G.parity("oracle/" + name, lb, ub, c["lb"], c["ub"])
     if p.has_spec:
         assert st.tolist() == c["status"].tolist()
+
+
+def test_concat_alpha_rounding_sensitivity():
+    """Summation order alone moves concat_alpha beyond the bar: the oracle on
+    the graph as Luna builds it meets the bar, the oracle on the same graph
+    with the Concat of Linear nodes merged into one Linear (the same products
+    summed in another order) does not; the engine is held to the second."""
+    c = G.load("concat_alpha")
+    as_luna = LirpaOracle(c["graph"], c["options"]).compute_bounds(c["boxes"], c["method"])
+    merged = LirpaOracle(G.merged_concat_graph(c["graph"]), c["options"]).compute_bounds(c["boxes"], c["method"])
+    assert max(G.excess(as_luna[0], c["lb"]), G.excess(as_luna[1], c["ub"])) <= 1.0
+    assert max(G.excess(merged[0], c["lb"]), G.excess(merged[1], c["ub"])) > 1.0
+    # The CROWN bounds of the same graph are insensitive.
+    cc = G.load("concat_crown")
+    m = LirpaOracle(G.merged_concat_graph(cc["graph"]), cc["options"]).compute_bounds(cc["boxes"], cc["method"])
+    assert max(G.excess(m[0], cc["lb"]), G.excess(m[1], cc["ub"])) <= 1.0
