@@ -282,7 +282,9 @@ LB200_API int lb200_nccl_comm_destroy(void* comm);
  * ranks receive the bounds of every box in out_lb / out_ub [n_boxes, nspec].
  * The wait for the gather is bounded by timeout_ms (60 s when <= 0): when it
  * expires, or NCCL reports an asynchronous error, the communicator is
- * aborted and an error returned.  stats covers this rank's share. */
+ * aborted (ncclCommAbort releases it: the caller must neither use nor
+ * destroy it afterwards) and an error naming the abort returned; the model
+ * stays usable.  stats covers this rank's share. */
 LB200_API int lb200_shard_run(lb200_model* model, void* comm, int rank, int world, int method,
                               const float* x_lower, const float* x_upper, int64_t n_boxes,
                               const float* C, int64_t c_boxes, int64_t nspec,

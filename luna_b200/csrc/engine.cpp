@@ -435,6 +435,7 @@ void Model::build_layer(Layer& L, const lb200_graph_desc* g, int node, int bn_no
     LB_CUDA(cudaMemcpy(L.b, b.data(), b.size() * 4, cudaMemcpyHostToDevice));
     LB_CUDA(cudaMemcpy(L.b_neuron, bn.data(), bn.size() * 4, cudaMemcpyHostToDevice));
     if (L.conv && k < 1000) build_tc_conv(L, wsrc.data(), k);
+    if (L.convt && k < 1000) build_tc_convt(L, wsrc.data(), k);
     if (!L.conv && !L.convt) {
         L.W_hi = weights_.as<float>(key("Whi", k), W.size());
         L.W_lo = weights_.as<float>(key("Wlo", k), W.size());
@@ -577,6 +578,116 @@ void Model::build_tc_conv(Layer& L, const float* w, int k) {
             L.adj_kb.clear();
         }
     }
+}
+
+// Weight matrices of the tensor-core steps of one ConvTranspose2d layer
+// (ONNX weight w [Ci][Co][kh][kw]).
+void Model::build_tc_convt(Layer& L, const float* w, int k) {
+    const int Ci = L.in.C, Co = L.out.C, kh = L.kh, kw = L.kw, s = L.sh;
+    if (L.sh != L.sw) return;
+    auto wv = [&](int ci, int co, int ky, int kx) { return w[(((size_t)ci * Co + co) * kh + ky) * kw + kx]; };
+    // Back-substitution: P[q, ci] = sum over taps and co of A[q s - p + k, co] W[ci, co, k].
+    if (Co % 32 == 0 && tc_conv_supported(Co, L.in.W, s) && kh * kw * (Co / 32) <= TC_CONV_MAX_KB) {
+        for (int ky = 0; ky < kh; ++ky)
+            for (int kx = 0; kx < kw; ++kx)
+                for (int cb = 0; cb < Co / 32; ++cb) {
+                    TcConvTap t;
+                    t.plane = 0;
+                    t.dy = ky - L.ph;
+                    t.dx = kx - L.pw;
+                    t.c0 = cb * 32;
+                    L.tcb_kb.push_back(t);
+                }
+        const int nkb = (int)L.tcb_kb.size();
+        std::vector<float> Wb((size_t)Ci * nkb * 32, 0.f);
+        for (int a = 0; a < nkb; ++a) {
+            const TcConvTap& t = L.tcb_kb[a];
+            const int ky = t.dy + L.ph, kx = t.dx + L.pw;
+            for (int ci = 0; ci < Ci; ++ci)
+                for (int cc = 0; cc < 32; ++cc) Wb[(size_t)ci * nkb * 32 + a * 32 + cc] = wv(ci, t.c0 + cc, ky, kx);
+        }
+        float* tmp = weights_.as<float>(key("Wtb", k), Wb.size());
+        LB_CUDA(cudaMemcpy(tmp, Wb.data(), Wb.size() * 4, cudaMemcpyHostToDevice));
+        L.Wtb_hi = weights_.as<float>(key("Wtbhi", k), Wb.size());
+        L.Wtb_lo = weights_.as<float>(key("Wtblo", k), Wb.size());
+        launch_split_tf32(tmp, L.Wtb_hi, L.Wtb_lo, (int64_t)Wb.size(), 0);
+        L.tct_b = true;
+    }
+    // Adjoint: Qbar[v, co] = sum of Pbar[q, ci] W[ci, co, k] over v + p = q s + k,
+    // phases (v + p) mod s stacked in M, tap k = phase + s u.
+    const int Uy = (kh + s - 1) / s, Ux = (kw + s - 1) / s;
+    if (Ci % 32 == 0 && s * s * Co >= 64 && Uy * Ux * (Ci / 32) <= TC_CONV_MAX_KB &&
+        tc_conv_supported(Ci, (L.out.W - 1 + L.pw) / s - L.pw / s + 1)) {
+        const int mt = s * s * Co, kt = Uy * Ux * Ci;
+        std::vector<float> Wj((size_t)mt * kt, 0.f);
+        for (int py = 0; py < s; ++py)
+            for (int px = 0; px < s; ++px)
+                for (int co = 0; co < Co; ++co)
+                    for (int uy = 0; uy < Uy; ++uy)
+                        for (int ux = 0; ux < Ux; ++ux) {
+                            const int ky = py + s * uy, kx = px + s * ux;
+                            if (ky >= kh || kx >= kw) continue;
+                            for (int ci = 0; ci < Ci; ++ci)
+                                Wj[(size_t)((py * s + px) * Co + co) * kt + (uy * Ux + ux) * Ci + ci] =
+                                    wv(ci, co, ky, kx);
+                        }
+        float* tmp = weights_.as<float>(key("Wtj", k), Wj.size());
+        LB_CUDA(cudaMemcpy(tmp, Wj.data(), Wj.size() * 4, cudaMemcpyHostToDevice));
+        L.Wtj_hi = weights_.as<float>(key("Wtjhi", k), Wj.size());
+        L.Wtj_lo = weights_.as<float>(key("Wtjlo", k), Wj.size());
+        launch_split_tf32(tmp, L.Wtj_hi, L.Wtj_lo, (int64_t)Wj.size(), 0);
+        L.Uy = Uy;
+        L.Ux = Ux;
+        L.tct_a = true;
+    }
+}
+
+TcConvPlan Model::tct_back_plan(int m, int rows, const float* data) const {
+    const Layer& L = layers_[m - 1];
+    TcConvPlan p;
+    p.data = data;
+    p.C = L.out.C;
+    p.X = L.out.W;
+    p.Y = L.out.H;
+    p.P = 1;
+    p.R = rows;
+    p.ds = L.sh;
+    p.ny = L.in.H;
+    p.nx = L.in.W;
+    for (const TcConvTap& t : L.tcb_kb) p.kb[p.nkb++] = t;
+    p.w_hi = L.Wtb_hi;
+    p.w_lo = L.Wtb_lo;
+    p.m_total = L.in.C;
+    tc_conv_tile(p, rows);
+    return p;
+}
+
+TcConvPlan Model::tct_adj_plan(int m, int rows, const float* pbar) const {
+    const Layer& L = layers_[m - 1];
+    const int s = L.sh, tly = L.ph / s, tlx = L.pw / s;
+    TcConvPlan p;
+    p.data = pbar;
+    p.C = L.in.C;
+    p.X = L.in.W;
+    p.Y = L.in.H;
+    p.P = 1;
+    p.R = rows;
+    p.ny = (L.out.H - 1 + L.ph) / s - tly + 1;
+    p.nx = (L.out.W - 1 + L.pw) / s - tlx + 1;
+    for (int uy = 0; uy < L.Uy; ++uy)
+        for (int ux = 0; ux < L.Ux; ++ux)
+            for (int cb = 0; cb < L.in.C / 32; ++cb) {
+                TcConvTap& t = p.kb[p.nkb++];
+                t.plane = 0;
+                t.dy = tly - uy;
+                t.dx = tlx - ux;
+                t.c0 = cb * 32;
+            }
+    p.w_hi = L.Wtj_hi;
+    p.w_lo = L.Wtj_lo;
+    p.m_total = s * s * L.out.C;
+    tc_conv_tile(p, rows);
+    return p;
 }
 
 // Phase grid of conv layer m for start st: output window pixel v of the
@@ -972,8 +1083,11 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
     // Conv layers above the first run on tensor cores when their shapes allow.
     auto tc_fwd = [&](int m) { return tcconv_ && m >= 2 && layers_[m - 1].tcf; };
     int slots_total = 0;
+    auto tct_back = [&](int m) { return tcconv_ && layers_[m - 1].convt && layers_[m - 1].tct_b; };
     for (int m = mb; m >= 1; --m) {
-        if (layers_[m - 1].convt)
+        if (tct_back(m))
+            slots_total += relax_window_chunks(sp.geo[m - 1]);
+        else if (layers_[m - 1].convt)
             slots_total += convt_rb_ok(convt_step(m)) ? convt_rb_chunks(convt_step(m)) : conv_chunks(sp.geo[m - 1]);
         else if (!layers_[m - 1].conv)
             slots_total += gemm_tiles_n(width(m - 1));
@@ -1081,6 +1195,21 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             e.P_save = psave_buf(m - 1);
             e.Q = Q[1 - cur];
             prof_begin(s);
+            if (tct_back(m)) {
+                // Tensor cores: the strided correlation stores raw P (into the
+                // saved P when the adjoint needs it), then the relaxation of
+                // the level below streams over it.
+                TcConvQbar q;
+                q.Co = L.in.C;
+                q.in_w = L.in.W;
+                q.Qbar = e.P_save ? e.P_save : cache_.as<float>("Pconv", (size_t)M * rowlen(st, m - 1));
+                launch_tc_conv_qbar(tct_back_plan(m, M, Q[cur]), M, q, s);
+                prof_end(s, fl);
+                launch_relax_window(q.Qbar, e, M, part + (size_t)slot * M, s);
+                slot += relax_window_chunks(sp.geo[m - 1]);
+                cur = 1 - cur;
+                continue;
+            }
             if (convt_rb_ok(ct)) {
                 launch_convt_back_relax_rb(Q[cur], ct, M, e, part + (size_t)slot * M, s);
                 slot += convt_rb_chunks(ct);
@@ -1378,10 +1507,24 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             flops_ += fl;
             float* Qbar = cache_.as<float>("Qbar", (size_t)M * rl);
             prof_begin(s);
-            if (convt_adj_rb_ok(ct))
+            if (tcconv_ && L.tct_a) {
+                // Tensor cores: the transposed conv of Pbar, phases stacked in M.
+                TcConvFwd f;
+                f.s = L.sh;
+                f.Ci = L.out.C;
+                f.cy = L.ph;
+                f.cx = L.pw;
+                f.tlo_y = L.ph / L.sh;
+                f.tlo_x = L.pw / L.sw;
+                f.out_h = L.out.H;
+                f.out_w = L.out.W;
+                f.P = Qbar;
+                launch_tc_conv_fwd(tct_adj_plan(m, M, pin), M, f, s);
+            } else if (convt_adj_rb_ok(ct)) {
                 launch_convt_adj_qbar_rb(pin, ct, M, Qbar, s);
-            else
+            } else {
                 launch_convt_adj_qbar(pin, ct, M, Qbar, s);
+            }
             prof_end(s, fl);
             launch_relax_adjoint(e, Qbar, M, N, s);
             pin = pout;

@@ -73,6 +73,14 @@ struct Layer {
     int Uy = 0, Ux = 0;
     float *Wf_hi = nullptr, *Wf_lo = nullptr, *Wa_hi = nullptr, *Wa_lo = nullptr;
     std::vector<TcConvTap> adj_kb;  // plane, u_y (dy), u_x (dx), c0
+    // Tensor-core steps of a ConvTranspose2d layer (same kernel kinds with
+    // the roles of the two sides swapped): back-substitution as a strided
+    // correlation, Wtb [Ci, |tcb_kb| * 32], K blocks (tap, co block) reading
+    // A at (q s - p + k); adjoint as a transposed conv with the s*s phases
+    // stacked in M, Wtj [s*s*Co, Uy*Ux*Ci], K blocks (u_y, u_x, ci block).
+    bool tct_b = false, tct_a = false;
+    float *Wtb_hi = nullptr, *Wtb_lo = nullptr, *Wtj_hi = nullptr, *Wtj_lo = nullptr;
+    std::vector<TcConvTap> tcb_kb;
 };
 
 // A skip edge into the Add at a level: from the ReLU output of level `src`,
@@ -154,6 +162,10 @@ private:
     ReluParams rview(int m, int B, int n);
     void init_alpha(StartPlan& sp, int m, int B, cudaStream_t s);
     void build_tc_conv(Layer& L, const float* w, int k);
+    void build_tc_convt(Layer& L, const float* w, int k);
+    // Tensor-core plans of transposed-conv layer m (whole-map rows).
+    TcConvPlan tct_back_plan(int m, int rows, const float* data) const;
+    TcConvPlan tct_adj_plan(int m, int rows, const float* pbar) const;
     void build_layer(Layer& L, const lb200_graph_desc* g, int node, int bn_node, const MapShape& prev, int k,
                      bool first);
     void build_geometry();

@@ -187,7 +187,8 @@ int lb200_shard_run(lb200_model* model, void* comm, int rank, int world, int met
             if (ar != ncclSuccess || ms > (timeout_ms > 0 ? timeout_ms : 60000)) {
                 api.comm_abort(c);
                 throw std::runtime_error(ar != ncclSuccess
-                                             ? std::string("bound gather failed: ") + api.error_string(ar)
+                                             ? std::string("bound gather failed (") + api.error_string(ar) +
+                                                   "); the communicator was aborted"
                                              : "bound gather timed out; the communicator was aborted");
             }
             std::this_thread::sleep_for(std::chrono::microseconds(200));

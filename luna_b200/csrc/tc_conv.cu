@@ -105,7 +105,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                     mbar_arrive_tx(&full[s], 2 * W_TILE_BYTES + box_bytes);
                     tma_load_2d(&twh, &full[s], w_hi(s), kb * 32, mt * 128);
                     tma_load_2d(&twl, &full[s], w_lo(s), kb * 32, mt * 128);
-                    tma_load_5d(&tx, &full[s], x_hi(s), tp.c0, tp.dx, yb * plan.BY + tp.dy, tp.plane, rb * plan.BR);
+                    tma_load_5d(&tx, &full[s], x_hi(s), tp.c0, tp.dx, yb * plan.BY * plan.ds + tp.dy, tp.plane,
+                                rb * plan.BR);
                 }
             }
             if (*abort) {
@@ -233,7 +234,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             } else {
                 const int co = m;
                 const int nq = plan.ny * plan.nx * eq.Co;
-                const float bco = m_ok ? eq.b[co] : 0.f;
+                const float bco = (m_ok && eq.b) ? eq.b[co] : 0.f;
                 for (int c0 = 0; c0 < N; c0 += 16) {
                     float v[16];
                     tmem_ld16(taddr + (uint32_t)c0, v);
@@ -246,7 +247,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         if (n >= plan.BR * pix_per_row || r >= rows) break;
                         const int ty = yb * plan.BY + rem / plan.BX, tx = rem - (rem / plan.BX) * plan.BX;
                         if (ty >= plan.ny) continue;
-                        eq.Qbar[(size_t)r * nq + (ty * eq.in_w + tx) * eq.Co + co] = v[i] + eq.gseed[r] * bco;
+                        eq.Qbar[(size_t)r * nq + (ty * eq.in_w + tx) * eq.Co + co] =
+                            eq.b ? v[i] + eq.gseed[r] * bco : v[i];
                     }
                 }
             }
@@ -298,8 +300,10 @@ CUtensorMap map_5d(const TcConvPlan& p) {
     strides[1] = strides[0] * p.X;
     strides[2] = strides[1] * p.Y;
     strides[3] = strides[2] * p.P;
-    cuuint32_t box[5] = {32, (cuuint32_t)p.BX, (cuuint32_t)p.BY, 1, (cuuint32_t)p.BR};
-    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    // With ds > 1 the box traverses ds * BX x ds * BY pixels with element
+    // stride ds, loading BX x BY of them (the same bytes as ds = 1).
+    cuuint32_t box[5] = {32, (cuuint32_t)(p.BX * p.ds), (cuuint32_t)(p.BY * p.ds), 1, (cuuint32_t)p.BR};
+    cuuint32_t estr[5] = {1, (cuuint32_t)p.ds, (cuuint32_t)p.ds, 1, 1};
     const CUresult r = conv_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float*>(p.data), dims,
                                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -326,7 +330,8 @@ void run_conv(const TcConvPlan& p, int rows, const TcConvFwd& ef, const TcConvQb
         LB_CUDA(cudaFuncSetAttribute(tc_conv_kernel<BNMAX, S, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
         configured = true;
     }
-    if (p.N > BNMAX || p.N % 16 != 0 || p.nkb <= 0 || p.nkb > TC_CONV_MAX_KB)
+    if (p.N > BNMAX || p.N % 16 != 0 || p.nkb <= 0 || p.nkb > TC_CONV_MAX_KB || p.ds < 1 || p.ds > 8 ||
+        p.BX * p.ds > 256 || p.BY * p.ds > 256)
         throw std::invalid_argument("tc conv: bad tiling");
     const CUtensorMap tx = map_5d(p);
     const CUtensorMap twh = map_2d(p.w_hi, p.m_total, p.nkb * 32, 128);
@@ -352,11 +357,14 @@ void tc_conv_set_wait_limit(long long wait_cycles) {
     LB_CUDA(cudaMemcpyToSymbol(tcx::g_wait_limit, &wait_cycles, sizeof(wait_cycles)));
 }
 
-bool tc_conv_supported(int data_C, int nx) { return data_C % 32 == 0 && data_C > 0 && nx >= 1 && nx <= 256; }
+bool tc_conv_supported(int data_C, int nx, int ds) {
+    return data_C % 32 == 0 && data_C > 0 && nx >= 1 && ds >= 1 && ds <= 8 && nx * ds <= 256;
+}
 
 void tc_conv_tile(TcConvPlan& p, int rows) {
     p.BX = p.nx;
-    p.BY = std::max(1, std::min(p.ny, 256 / p.nx));
+    // BY pixels rows of nx; the strided box spans BY * ds data rows (<= 256).
+    p.BY = std::max(1, std::min(std::min(p.ny, 256 / p.nx), 256 / std::max(p.ds, 1)));
     p.BR = 1;
     if (p.BY >= p.ny) {
         p.BY = p.ny;

@@ -29,9 +29,13 @@ struct TcConvTap {
 };
 
 struct TcConvPlan {
-    // Data tensor (C, X, Y, P, R), fp32, row-major with C fastest.
+    // Data tensor (C, X, Y, P, R), fp32, row-major with C fastest.  With
+    // ds > 1 output pixel (ty, tx) of a K block reads data pixel
+    // (ty ds + dy, tx ds + dx): the TMA box traverses X and Y with element
+    // stride ds (a strided correlation without a phase-split copy).
     const float* data = nullptr;
     int C = 0, X = 0, Y = 0, P = 1, R = 0;
+    int ds = 1;
     // Output pixel grid per row (ny x nx) and its tiling.
     int ny = 0, nx = 0;
     int BR = 1, BY = 1, BX = 1, N = 16;  // N = BR*BY*BX rounded up to 16 (<= 256)
@@ -52,7 +56,7 @@ struct TcConvFwd {
     float* P = nullptr;
 };
 // Epilogue of a correlation step: Qbar[r, (qy * in_w + qx) * Co + co] =
-// D[co, q] + g[r] b[co].
+// D[co, q] + g[r] b[co] (D alone when b is null).
 struct TcConvQbar {
     int Co = 0, in_w = 0;
     const float* gseed = nullptr;
@@ -61,8 +65,9 @@ struct TcConvQbar {
 };
 
 // True when the tensor-core conv path handles the step (channel counts
-// multiples of 32 on the data side, pixel grid rows <= 256 wide).
-bool tc_conv_supported(int data_C, int nx);
+// multiples of 32 on the data side, pixel grid rows <= 256 wide, and no
+// wider than 256 / ds data pixels).
+bool tc_conv_supported(int data_C, int nx, int ds = 1);
 // Tiling of a per-row pixel grid ny x nx over `rows` rows.
 void tc_conv_tile(TcConvPlan& p, int rows);
 void launch_tc_conv_fwd(const TcConvPlan& p, int rows, const TcConvFwd& e, cudaStream_t s);

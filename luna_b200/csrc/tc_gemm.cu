@@ -31,7 +31,6 @@ using namespace tcx;
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 32;  // fp32 columns per 128-byte swizzle row
-constexpr int NUM_THREADS = 384;
 constexpr int WARP_TMA = 0, WARP_MMA = 1, EPI_WARP0 = 4, XF_WARP0 = 8;
 constexpr int A_TILE_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 
@@ -42,6 +41,18 @@ enum { KIND_FWD = 0, KIND_CONC = 1, KIND_QBAR = 3, KIND_STOREP = 4 };
 // concretisation signs (first adjoint contraction); the ReLU relaxation of a
 // TMA-loaded P (RELAX) or of gathered weight rows (GATHER, one-hot start).
 enum { AMODE_TMA = 0, AMODE_SEED = 1, AMODE_RELAX = 2, AMODE_GATHER = 3 };
+// Operand-forming (XF) threads: one per tile row, or, when the A operand is
+// generated from the concretisation signs (its inputs come from global
+// memory), two per row (16 columns of each K block each) so that twice the
+// loads are in flight.
+template <int AMODE>
+constexpr int xf_threads() {
+    return AMODE == AMODE_SEED ? 256 : 128;
+}
+template <int AMODE>
+constexpr int kernel_threads() {
+    return XF_WARP0 * 32 + xf_threads<AMODE>();
+}
 
 __device__ int g_tc_error;
 // Failure-detection test hook (tc_set_test_fault): when set, the TMA
@@ -167,37 +178,26 @@ __device__ __forceinline__ SeedRow seed_row_info(const EpiStoreQbar& e, int r, i
     return s;
 }
 
-// The 32 sign bytes of one row and K block [k0, k0 + 32): two 16-byte loads
-// (zero past K) when rows are 16-byte aligned (K % 16 == 0), else bytewise.
-__device__ __forceinline__ void seed_signs(const SeedRow& sr, int K, int k0, uint4 (&sg)[2]) {
-    sg[0] = sg[1] = make_uint4(0u, 0u, 0u, 0u);
-    if (!sr.sg) return;
-    if ((K & 15) == 0) {
-        if (k0 < K) sg[0] = *reinterpret_cast<const uint4*>(sr.sg + k0);
-        if (k0 + 16 < K) sg[1] = *reinterpret_cast<const uint4*>(sr.sg + k0 + 16);
-        return;
-    }
-    uint32_t w[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};
-    for (int i = 0; i < 32 && k0 + i < K; ++i) w[i >> 2] |= (uint32_t)sr.sg[k0 + i] << (8 * (i & 3));
-    sg[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    sg[1] = make_uint4(w[4], w[5], w[6], w[7]);
+// The 16 sign bytes of one row at [k0, k0 + 16) (zero past K).
+__device__ __forceinline__ uint4 seed_signs16(const SeedRow& sr, int K, int k0) {
+    if (!sr.sg || k0 >= K) return make_uint4(0u, 0u, 0u, 0u);
+    if ((K & 15) == 0) return *reinterpret_cast<const uint4*>(sr.sg + k0);
+    uint32_t w[4] = {0u, 0u, 0u, 0u};
+    for (int i = 0; i < 16 && k0 + i < K; ++i) w[i >> 2] |= (uint32_t)sr.sg[k0 + i] << (8 * (i & 3));
+    return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__device__ __forceinline__ uint32_t sign_word(const uint4 (&sg)[2], int w) {
-    const uint4 q = sg[w >> 2];
-    return (w & 3) == 0 ? q.x : (w & 3) == 1 ? q.y : (w & 3) == 2 ? q.z : q.w;
-}
-
-// d loss / d A of one row for K block [k0, k0 + 32) from its sign bytes.
-__device__ __forceinline__ void seed_row(const SeedRow& sr, int K, int k0, const uint4 (&sg)[2], float (&v)[32]) {
+// d loss / d A of one row for the 16 columns [k0, k0 + 16) (half a K block).
+__device__ __forceinline__ void seed_row16(const SeedRow& sr, int K, int k0, const uint4 sg, float (&v)[16]) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    for (int i = 0; i < 16; ++i) v[i] = 0.f;
     if (!sr.sg) return;
     const float g = sr.g;
+    const uint32_t words[4] = {sg.x, sg.y, sg.z, sg.w};
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
         const int c = k0 + 4 * j;
-        const uint32_t sw = sign_word(sg, j);
+        const uint32_t sw = words[j];
         if (c + 3 < K) {
             const float4 a4 = *reinterpret_cast<const float4*>(sr.xa + c);
             const float4 b4 = *reinterpret_cast<const float4*>(sr.xb + c);
@@ -221,7 +221,7 @@ __device__ __forceinline__ void seed_row(const SeedRow& sr, int K, int k0, const
 
 // ------------------------------------------------------------- kernel
 template <int BN, int S, int KIND, int AMODE>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tbh,
                    const __grid_constant__ CUtensorMap tbl, const __grid_constant__ CUtensorMap talpha, int M,
                    int N, int K, TcEpi ep, TcPrologue pro, float* partial) {
@@ -246,7 +246,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&split[s], 128);
+            mbar_init(&split[s], xf_threads<AMODE>());
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
@@ -344,6 +344,58 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             }
             if (*abort && issued) mbar_wait(last_commit, last_phase, abort, &g_tc_error, true);
         }
+    } else if (warp >= XF_WARP0 && AMODE == AMODE_SEED) {
+        // Two threads per tile row: thread xt forms columns [16 h, 16 h + 16)
+        // of row xt % 128 in every K block (h = xt / 128).
+        const int xt = threadIdx.x - XF_WARP0 * 32;
+        const int xrow = xt & (TC_BM - 1), h = xt / TC_BM;
+        uint32_t g = 0;
+        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+            bool ok = true;
+            const int mb_t = t / tiles_n;
+            const SeedRow seed = seed_row_info(ep.q, mb_t * TC_BM + xrow, M, K);
+            uint4 sg_next = seed_signs16(seed, K, 16 * h);  // next K block's signs, one block ahead
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const int s = g % S;
+                const uint32_t ph = (g / S) & 1;
+                // The seed reads only global memory: issue its loads before
+                // waiting for the stage, so their latency overlaps the wait.
+                const uint4 sg_cur = sg_next;
+                const int k0 = kb * TC_BK + 16 * h;
+                if (kb + 1 < nk) {
+                    sg_next = seed_signs16(seed, K, k0 + TC_BK);
+                    if (seed.sg && k0 + TC_BK < K) {
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(seed.xa + k0 + TC_BK));
+                        asm volatile("prefetch.global.L1 [%0];" ::"l"(seed.xb + k0 + TC_BK));
+                    }
+                }
+                float v[16];
+                seed_row16(seed, K, k0, sg_cur, v);
+                if (!mbar_wait(&full[s], ph, abort, &g_tc_error)) {
+                    ok = false;
+                    break;
+                }
+                float4* hi = reinterpret_cast<float4*>(a_hi(s));
+                float4* lo = reinterpret_cast<float4*>(a_lo(s));
+                // Logical 16-byte chunk j of row xrow sits at chunk j ^ (xrow % 8)
+                // of the 128-byte swizzled layout TMA would have produced.
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int j = 4 * h + jj;
+                    float4 hv, lv;
+                    hv.x = rna_tf32(v[4 * jj]);     lv.x = rna_tf32(v[4 * jj] - hv.x);
+                    hv.y = rna_tf32(v[4 * jj + 1]); lv.y = rna_tf32(v[4 * jj + 1] - hv.y);
+                    hv.z = rna_tf32(v[4 * jj + 2]); lv.z = rna_tf32(v[4 * jj + 2] - hv.z);
+                    hv.w = rna_tf32(v[4 * jj + 3]); lv.w = rna_tf32(v[4 * jj + 3] - hv.w);
+                    const int at = xrow * 8 + (j ^ (xrow & 7));
+                    hi[at] = hv;
+                    lo[at] = lv;
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mbar_arrive(&split[s]);
+            }
+            if (!ok) break;
+        }
     } else if (warp >= XF_WARP0) {
         const int xt = threadIdx.x - XF_WARP0 * 32;
         uint32_t g = 0;
@@ -355,12 +407,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
             bool ok = true;
             const int mb_t = t / tiles_n, nb_t = t % tiles_n;
-            SeedRow seed;
-            uint4 sg_next[2];  // sign bytes of the next K block, loaded one block ahead
-            if constexpr (AMODE == AMODE_SEED) {
-                seed = seed_row_info(ep.q, mb_t * TC_BM + xt, M, K);
-                seed_signs(seed, K, 0, sg_next);
-            }
             if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
                 const int r = mb_t * TC_BM + xt;
                 rok = r < M;
@@ -377,22 +423,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % S;
                 const uint32_t ph = (g / S) & 1;
-                // The seed reads only global memory: issue its loads before
-                // waiting for the stage, so their latency overlaps the wait.
-                float v[32];
-                if constexpr (AMODE == AMODE_SEED) {
-                    const uint4 sg_cur[2] = {sg_next[0], sg_next[1]};
-                    if (kb + 1 < nk) {
-                        seed_signs(seed, K, (kb + 1) * TC_BK, sg_next);
-                        // The next block's input bounds (one 128-byte line each) into L1.
-                        const int kn = (kb + 1) * TC_BK;
-                        if (seed.sg && kn < K) {
-                            asm volatile("prefetch.global.L1 [%0];" ::"l"(seed.xa + kn));
-                            asm volatile("prefetch.global.L1 [%0];" ::"l"(seed.xb + kn));
-                        }
-                    }
-                    seed_row(seed, K, kb * TC_BK, sg_cur, v);
-                }
                 if (!mbar_wait(&full[s], ph, abort, &g_tc_error)) { ok = false; break; }
                 float4* hi = reinterpret_cast<float4*>(a_hi(s));
                 float4* lo = reinterpret_cast<float4*>(a_lo(s));
@@ -467,21 +497,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                         h.w = rna_tf32(x.w); l.w = rna_tf32(x.w - h.w);
                         hi[i] = h;
                         lo[i] = l;
-                    }
-                } else {
-                    // Generate row xt of the tile and store it in the
-                    // 128-byte swizzled layout TMA would have produced:
-                    // 16-byte chunk j of row r sits at chunk j ^ (r % 8).
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        float4 h, l;
-                        h.x = rna_tf32(v[4 * j]);     l.x = rna_tf32(v[4 * j] - h.x);
-                        h.y = rna_tf32(v[4 * j + 1]); l.y = rna_tf32(v[4 * j + 1] - h.y);
-                        h.z = rna_tf32(v[4 * j + 2]); l.z = rna_tf32(v[4 * j + 2] - h.z);
-                        h.w = rna_tf32(v[4 * j + 3]); l.w = rna_tf32(v[4 * j + 3] - h.w);
-                        const int at = xt * 8 + (j ^ (xt & 7));
-                        hi[at] = h;
-                        lo[at] = l;
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -611,7 +626,7 @@ void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, in
     const CUtensorMap tbl = make_map(Blo, N, K, BN);
     const int ntiles = ((N + BN - 1) / BN) * ((M + TC_BM - 1) / TC_BM);
     const int grid = std::min(ntiles, num_sms());
-    tc_gemm_kernel<BN, S, KIND, AMODE><<<grid, NUM_THREADS, SMEM, s>>>(ta, tbh, tbl, talpha, M, N, K, ep, pro,
+    tc_gemm_kernel<BN, S, KIND, AMODE><<<grid, kernel_threads<AMODE>(), SMEM, s>>>(ta, tbh, tbl, talpha, M, N, K, ep, pro,
                                                                        partial);
     LB_LAUNCH();
 }

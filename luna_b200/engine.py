@@ -97,6 +97,14 @@ def set_contraction_fault(device: int, starve: bool, wait_cycles: int = 0) -> No
            "lb200_test_set_contraction_fault")
 
 
+def last_error() -> str:
+    """The calling thread's lb200_last_error() text."""
+    load_library()
+    buf = C.create_string_buffer(4096)
+    _lib.lb200_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
 def _check(rc: int, what: str):
     if rc != 0:
         buf = C.create_string_buffer(4096)
@@ -247,9 +255,11 @@ class Model:
         lb = np.empty((B, nspec), np.float32)
         ub = np.empty((B, nspec), np.float32)
         st = Stats()
-        _check(_lib.lb200_shard_run(self._h, comm.handle, comm.rank, comm.world, method, fptr(xl), fptr(xu), B,
-                                    fptr(Cm), Cm.shape[0], nspec, fptr(lb), fptr(ub), timeout_ms, C.byref(st)),
-               "lb200_shard_run")
+        rc = _lib.lb200_shard_run(self._h, comm.handle, comm.rank, comm.world, method, fptr(xl), fptr(xu), B,
+                                  fptr(Cm), Cm.shape[0], nspec, fptr(lb), fptr(ub), timeout_ms, C.byref(st))
+        if rc != 0 and "aborted" in last_error():
+            comm.handle = None  # ncclCommAbort released it
+        _check(rc, "lb200_shard_run")
         self.last_stats = st
         return lb, ub
 

@@ -263,12 +263,15 @@ def small_cnn_bn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, big_first:
 
 
 def convt_cnn_case(seed: int, n_boxes: int = 3, eps: float = 0.02, hw: int = 10, conv_after: bool = False,
-                   wide: bool = False):
+                   wide: bool = False, tc: bool = False):
     """Small CNN with a strided transposed conv (conv -> conv s2 -> convT s2
     [-> conv] -> linear head) for parity tests; with wide the transposed conv
-    maps 16 to 8 channels (the register-blocked kernels' shapes)."""
+    maps 16 to 8 channels (the register-blocked kernels' shapes), with tc 32
+    to 32 channels (the tensor-core transposed-conv steps' shapes)."""
     rng = np.random.Generator(np.random.PCG64(seed))
-    if wide:
+    if tc:
+        layers = [("conv", 8, 3, 1, 1), ("conv", 32, 4, 2, 1), ("convT", 32, 4, 2, 1)]
+    elif wide:
         layers = [("conv", 8, 3, 1, 1), ("conv", 16, 4, 2, 1), ("convT", 8, 4, 2, 1)]
     else:
         layers = [("conv", 6, 3, 1, 1), ("conv", 8, 4, 2, 1), ("convT", 5, 4, 2, 1)]

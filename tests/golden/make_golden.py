@@ -143,6 +143,11 @@ def cases():
     out.append(("cnnwide_crown", "cnn_wide_case", kw, 3, abi.METHOD_CROWN, {}))
     out.append(("cnnwide_alpha", "cnn_wide_case", kw, 3, abi.METHOD_ALPHA_CROWN,
                 {"alpha_lr": 0.1, "alpha_iterations": 6}))
+    # A 32 -> 32-channel transposed conv: the tensor-core transposed-conv steps.
+    kw = {"seed": 11, "n_boxes": 3, "tc": True}
+    out.append(("convttc_crown", "convt_cnn_case", kw, 3, abi.METHOD_CROWN, {}))
+    out.append(("convttc_alpha", "convt_cnn_case", kw, 3, abi.METHOD_ALPHA_CROWN,
+                {"alpha_lr": 0.1, "alpha_iterations": 5}))
     # OPTIMIZE_UPPER: the upper side optimised first, then the lower side
     # (both), the upper side alone, and neither (runCROWN).
     up = {"alpha_lr": 0.1, "alpha_iterations": 6, "optimize_upper": 1}

@@ -2,13 +2,17 @@
 full workload size, where Luna itself cannot give a reference in bounded
 time or at all:
 
-* oracle_resnet_cifar_alpha: the CIFAR ResNet of the ResNet workload
+* oracle_resnet_cifar_crown: the CIFAR ResNet of the ResNet workload
   (3x32x32, stem 16, residual blocks 16/16/32s2/32 with BatchNorm, Sigmoid
   head); Luna's alpha-CROWN throws on its Sigmoid node
-  (AlphaCROWNAnalysis.cpp:264-272), so the oracle is the reference here;
-* oracle_convt_sweep_alpha: the transposed-conv CIFAR CNN of the sub-domain
-  sweep, on its first sub-domains (one Luna alpha-CROWN box of this size
-  takes over an hour on one core).
+  (AlphaCROWNAnalysis.cpp:264-272);
+* oracle_convt_sweep_crown: the transposed-conv CIFAR CNN of the sub-domain
+  sweep, on its first sub-domains.
+At these sizes almost every pre-activation is IBP-unstable (16384 rows per
+start on the ResNet, 32768 on the sweep network), and the oracle keeps dense
+A matrices: CROWN fits in host memory, while alpha-CROWN, which keeps every
+start's A for autograd, needs well over 60 GB; the alpha paths of both
+networks are pinned on their smaller relatives (resnet_*, convt_* fixtures).
 
 The oracle itself is pinned against Luna's outputs by
 tests/test_oracle_golden.py.  Boxes and weights are regenerated from the
@@ -37,10 +41,8 @@ OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "oracle")
 def cases():
     """(name, generator, kwargs, box count, method, option overrides)."""
     return [
-        ("oracle_resnet_cifar_alpha", "resnet_cifar", {"n_boxes": 128}, 2, abi.METHOD_ALPHA_CROWN,
-         {"alpha_lr": 0.1, "alpha_iterations": 4}),
-        ("oracle_convt_sweep_alpha", "convt_sweep_boxes", {"n_boxes": 256}, 2, abi.METHOD_ALPHA_CROWN,
-         {"alpha_lr": 0.1, "alpha_iterations": 4}),
+        ("oracle_resnet_cifar_crown", "resnet_cifar", {"n_boxes": 128}, 2, abi.METHOD_CROWN, {}),
+        ("oracle_convt_sweep_crown", "convt_sweep_boxes", {"n_boxes": 256}, 2, abi.METHOD_CROWN, {}),
     ]
 
 

@@ -106,6 +106,24 @@ def test_tc_conv_matches_simt_and_oracle(method):
         assert e <= 1.0, (what, e)
 
 
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_tc_convt_matches_simt(method):
+    """A 32 -> 32-channel transposed conv takes its back-substitution (a
+    strided correlation read by element-strided TMA boxes) and its adjoint (a
+    transposed conv, phases stacked in M) on tensor cores; against the SIMT
+    kernels at twice the bar (each is held to the bar against Luna by the
+    convttc_* goldens)."""
+    g, bx = W.convt_cnn_case(11, n_boxes=3, tc=True)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=5)
+    m = Model(g, options=opt)
+    tlb, tub = m.compute_bounds(bx, method)
+    m.set_contraction_path(1)
+    slb, sub = m.compute_bounds(bx, method)
+    e = max(G.excess(tlb, slb, 2 * G.RTOL, 2 * G.ATOL), G.excess(tub, sub, 2 * G.RTOL, 2 * G.ATOL))
+    print(f"PARITY tc convT vs simt/{method} (2x bar) {e:.4f}")
+    assert e <= 1.0, e
+
+
 def _forward(graph, x):
     """Forward of a graph (any DAG of the supported nodes) on a batch of flat
     inputs in CHW order."""

@@ -67,3 +67,53 @@ def test_two_ranks_gather_every_box():
     for r in range(2):
         lb, ub = out[r]
         G.parity(f"shard rank {r}", lb, ub, ref[0], ref[1])
+
+
+def _rank_absent(rank, world, uid, q, gone):
+    """Rank 1 joins the communicator and then never joins the gather: it
+    stays alive, with nothing in flight, until rank 0 has reported, and
+    leaves without touching the communicator again."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from luna_b200.engine import EngineError, Model, NcclComm
+    g, bx, opt = _case()
+    m = Model(g, device=rank, options=opt)
+    comm = NcclComm(uid, rank, world, rank)
+    if rank == 0:
+        try:
+            m.shard_run(comm, bx, abi.METHOD_ALPHA_CROWN, timeout_ms=3000)
+            q.put((0, "no error", None))
+        except EngineError as e:
+            # The model stays usable after the aborted gather.
+            q.put((0, str(e) + (" | handle released" if comm.handle is None else ""),
+                   m.compute_bounds(bx, abi.METHOD_ALPHA_CROWN)))
+        gone.set()
+    else:
+        gone.wait(timeout=120)
+        q.put((1, "left", None))
+    os._exit(0)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_absent_rank_times_out_the_gather():
+    """A rank that never reaches the gather: the other's bounded wait ends,
+    the communicator is aborted, the call fails with an error, and its model
+    still bounds correctly.  NVLS off (NCCL_NVLS_ENABLE=0)."""
+    from luna_b200.build import build
+    from luna_b200.engine import Model, nccl_unique_id
+    build()
+    g, bx, opt = _case()
+    ref = Model(g, device=0, options=opt).compute_bounds(bx, abi.METHOD_ALPHA_CROWN)
+    uid = nccl_unique_id()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    gone = ctx.Event()
+    procs = [ctx.Process(target=_rank_absent, args=(r, 2, uid, q, gone)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {r: (msg, res) for r, msg, res in (q.get(timeout=300) for _ in procs)}
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    msg, res = out[0]
+    assert "timed out" in msg and "aborted" in msg and "handle released" in msg, msg
+    G.parity("after the aborted gather", res[0], res[1], ref[0], ref[1])
