@@ -218,8 +218,10 @@ LB200_API int lb200_set_profiling(lb200_model* model, int on);
 
 /* Contraction path: 0 (default) uses the tcgen05 tensor cores with 3xTF32
  * split precision wherever the shape allows (N a multiple of 16, K of 4),
- * the SIMT fp32 kernel elsewhere; 1 uses the SIMT fp32 kernel everywhere
- * (for cross-checking).  Luna has no counterpart. */
+ * with 224-column tiles on CTA pairs (cta_group::2) for wide N, the SIMT fp32
+ * kernel elsewhere; 1 uses the SIMT fp32 kernel everywhere; 2 the tensor
+ * cores on single CTAs only (1 and 2 for cross-checking).  Luna has no
+ * counterpart. */
 LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 
 /* IBP bounds of n_boxes boxes without allocating any device memory, for
@@ -235,7 +237,7 @@ LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
  * 2^31 - 1.  Work is enqueued on `stream` (a stream of the model's device)
  * and the call returns without waiting; the caller's current device is left
  * as it was.  The first call on a device resolves the array's address on
- * that device: make it before any stream capture.  All calls share the
+ * that device (cudaGetSymbolAddress).  All calls share the
  * array, so calls that overlap on the GPU race and must be serialised by
  * the caller.  No counterpart in the reference. */
 LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const float* d_x_lower,
@@ -272,7 +274,11 @@ LB200_API int lb200_shard_range(int rank, int world, int64_t n, int64_t* begin, 
 
 /* A 128-byte ncclUniqueId made on one rank and shared with the others by the
  * caller; lb200_nccl_comm_create then joins the communicator on `device`
- * (blocks until all `world` ranks have joined). */
+ * (blocks until all `world` ranks have joined) and runs one all-gather so
+ * that NCCL's peer connections exist before the first lb200_shard_run: a
+ * communicator passed in by the caller should have run a collective of its
+ * own first, since NCCL sets up connections on first use and that setup
+ * waits on the host, outside lb200_shard_run's bounded wait. */
 LB200_API int lb200_nccl_unique_id(uint8_t id[128]);
 LB200_API int lb200_nccl_comm_create(const uint8_t id[128], int rank, int world, int device, void** comm);
 LB200_API int lb200_nccl_comm_destroy(void* comm);

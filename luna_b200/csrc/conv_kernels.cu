@@ -344,23 +344,40 @@ bool convT_rb_ok(const ConvStep& cs) {
 
 int convT_rb_chunks(const WinGeo& out) { return ceil_div(out.wh * out.ww, 256); }
 
+// Work items: with gs == 256, one 256-pixel chunk of one row (nchunk per
+// row, block-wide partial sum); with gs a power of two <= 32 (windows of at
+// most gs pixels), 256 / gs rows per item, one gs-lane group per row
+// (shuffle partial sum).  Blocks are persistent over the items, so the
+// layer's weights are staged in shared memory once per block.
 template <int CI>
 __global__ void __launch_bounds__(256, CI <= 16 ? 3 : 2) convT_relax_rb_kernel(const float* __restrict__ A, ConvStep cs, int M,
-                                                             ConvRelaxEpi e, int nchunk, float* __restrict__ partial) {
+                                                             ConvRelaxEpi e, int nchunk, int gs,
+                                                             float* __restrict__ partial) {
     extern __shared__ float4 rb_w4[];
     float* wsh = reinterpret_cast<float*>(rb_w4);
     __shared__ float red[8];
     const int nwt = cs.kh * cs.kw * cs.Co * CI;
     for (int i = threadIdx.x; i < nwt; i += blockDim.x) wsh[i] = cs.Wk[i];
     __syncthreads();
-    const int r = (int)(blockIdx.x / nchunk), chunk = (int)(blockIdx.x % nchunk);
     const int npix = cs.out_h * cs.out_w;
-    const int pix = chunk * 256 + threadIdx.x;
-    int p, rr;
-    row_split(r, e.rows.R, p, rr);
-    const int bx = e.rows.row_box[rr];
+    const int rpb = 256 / gs;
+    const int64_t items = gs == 256 ? (int64_t)M * nchunk : ((int64_t)M + rpb - 1) / rpb;
+    for (int64_t w = blockIdx.x; w < items; w += gridDim.x) {
+    int r, chunk, pix;
+    if (gs == 256) {
+        r = (int)(w / nchunk);
+        chunk = (int)(w - (int64_t)r * nchunk);
+        pix = chunk * 256 + threadIdx.x;
+    } else {
+        r = (int)(w * rpb) + (int)threadIdx.x / gs;
+        chunk = 0;
+        pix = (int)threadIdx.x % gs;
+    }
     float part = 0.f;
-    if (pix < npix) {
+    if (r < M && pix < npix) {
+        int p, rr;
+        row_split(r, e.rows.R, p, rr);
+        const int bx = e.rows.row_box[rr];
         float acc[CI];
 #pragma unroll
         for (int c = 0; c < CI; ++c) acc[c] = 0.f;
@@ -374,13 +391,13 @@ __global__ void __launch_bounds__(256, CI <= 16 ? 3 : 2) convT_relax_rb_kernel(c
                 const int qx = (tx - kx) / cs.sw;
                 if (qx >= cs.in_w) continue;
                 const float4* a4 = reinterpret_cast<const float4*>(Arow + ((size_t)qy * cs.in_w + qx) * cs.Co);
-                const float* w = wsh + (size_t)(ky * cs.kw + kx) * cs.Co * CI;
+                const float* wt = wsh + (size_t)(ky * cs.kw + kx) * cs.Co * CI;
                 for (int c4 = 0; c4 < cs.Co / 4; ++c4) {
                     const float4 a = __ldg(a4 + c4);
                     const float av[4] = {a.x, a.y, a.z, a.w};
 #pragma unroll
                     for (int t = 0; t < 4; ++t) {
-                        const float4* wr = reinterpret_cast<const float4*>(w + (size_t)(c4 * 4 + t) * CI);
+                        const float4* wr = reinterpret_cast<const float4*>(wt + (size_t)(c4 * 4 + t) * CI);
 #pragma unroll
                         for (int c = 0; c < CI / 4; ++c) {
                             const float4 wv = wr[c];
@@ -432,8 +449,26 @@ __global__ void __launch_bounds__(256, CI <= 16 ? 3 : 2) convT_relax_rb_kernel(c
             *reinterpret_cast<float4*>(e.Q + at0 + c) = make_float4(Qv[0], Qv[1], Qv[2], Qv[3]);
         }
     }
-    const float tot = block_sum256(part, red);
-    if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+    if (gs == 256) {
+        const float tot = block_sum256(part, red);
+        if (threadIdx.x == 0) partial[(size_t)chunk * M + r] = tot;
+        __syncthreads();  // red[] is reused by the next item
+    } else {
+        for (int o = gs >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+        if ((int)threadIdx.x % gs == 0 && r < M) partial[r] = part;
+    }
+    }
+}
+
+// Resident blocks of a kernel with `smem` dynamic shared memory, times 148-SM
+// waves: the grid of the persistent register-blocked conv kernels.
+template <class K>
+int rb_grid(K kernel, size_t smem, int64_t items) {
+    int per_sm = 1, dev = 0, sms = 148;
+    LB_CUDA(cudaGetDevice(&dev));
+    LB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    LB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, smem));
+    return (int)std::max<int64_t>(1, std::min<int64_t>(items, (int64_t)std::max(per_sm, 1) * sms * 4));
 }
 
 void launch_convT_relax_rb(const float* A, const ConvStep& cs, int M, const ConvRelaxEpi& e, float* partial,
@@ -443,13 +478,24 @@ void launch_convT_relax_rb(const float* A, const ConvStep& cs, int M, const Conv
         throw std::invalid_argument("convT_relax_rb: unsupported step");
     const int nchunk = convT_rb_chunks(e.g);
     const size_t smem = (size_t)cs.kh * cs.kw * cs.Co * cs.Ci * 4;
-    const unsigned grid = (unsigned)((int64_t)M * nchunk);
-    if (cs.Ci == 8)
-        convT_relax_rb_kernel<8><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, partial);
-    else if (cs.Ci == 16)
-        convT_relax_rb_kernel<16><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, partial);
-    else
-        convT_relax_rb_kernel<32><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, partial);
+    // Windows of at most 32 pixels: several rows per work item.
+    const int npix = cs.out_h * cs.out_w;
+    int gs = 256;
+    if (npix <= 32) {
+        gs = 1;
+        while (gs < npix) gs <<= 1;
+    }
+    const int64_t items = gs == 256 ? (int64_t)M * nchunk : ((int64_t)M + 256 / gs - 1) / (256 / gs);
+    if (cs.Ci == 8) {
+        const int grid = rb_grid(convT_relax_rb_kernel<8>, smem, items);
+        convT_relax_rb_kernel<8><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, gs, partial);
+    } else if (cs.Ci == 16) {
+        const int grid = rb_grid(convT_relax_rb_kernel<16>, smem, items);
+        convT_relax_rb_kernel<16><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, gs, partial);
+    } else {
+        const int grid = rb_grid(convT_relax_rb_kernel<32>, smem, items);
+        convT_relax_rb_kernel<32><<<grid, 256, smem, s>>>(A, cs, M, e, nchunk, gs, partial);
+    }
     LB_LAUNCH();
 }
 
@@ -474,8 +520,8 @@ __global__ void __launch_bounds__(256, CO <= 16 ? 3 : 2) conv_adj_qbar_rb_kernel
     }
     __syncthreads();
     const int nq = cs.in_h * cs.in_w;
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (int64_t)M * nq) return;
+    for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < (int64_t)M * nq;
+         idx += (int64_t)gridDim.x * blockDim.x) {
     const int r = (int)(idx / nq), q = (int)(idx - (int64_t)r * nq);
     const int qy = q / cs.in_w, qx = q - (q / cs.in_w) * cs.in_w;
     const float* prow = Pbar + (size_t)r * cs.out_h * cs.out_w * cs.Ci;
@@ -514,6 +560,7 @@ __global__ void __launch_bounds__(256, CO <= 16 ? 3 : 2) conv_adj_qbar_rb_kernel
     for (int c = 0; c < CO; c += 4)
         *reinterpret_cast<float4*>(out + c) = make_float4(acc[c] + g * b[c], acc[c + 1] + g * b[c + 1],
                                                           acc[c + 2] + g * b[c + 2], acc[c + 3] + g * b[c + 3]);
+    }
 }
 
 void launch_conv_adj_qbar_rb(const float* Pbar, const ConvStep& cs, int M, const float* gseed, const float* b,
@@ -522,13 +569,17 @@ void launch_conv_adj_qbar_rb(const float* Pbar, const ConvStep& cs, int M, const
     if (total == 0) return;
     if (!conv_adj_rb_ok(cs)) throw std::invalid_argument("conv_adj_qbar_rb: unsupported step");
     const size_t smem = (size_t)cs.kh * cs.kw * cs.Co * cs.Ci * 4;
-    const unsigned grid = (unsigned)ceil_div(total, 256);
+    // Persistent blocks: the weights are staged once per block.
+    const int64_t items = ceil_div(total, 256);
     if (cs.Co == 8)
-        conv_adj_qbar_rb_kernel<8><<<grid, 256, smem, s>>>(Pbar, cs, M, gseed, b, Qbar);
+        conv_adj_qbar_rb_kernel<8><<<rb_grid(conv_adj_qbar_rb_kernel<8>, smem, items), 256, smem, s>>>(
+            Pbar, cs, M, gseed, b, Qbar);
     else if (cs.Co == 16)
-        conv_adj_qbar_rb_kernel<16><<<grid, 256, smem, s>>>(Pbar, cs, M, gseed, b, Qbar);
+        conv_adj_qbar_rb_kernel<16><<<rb_grid(conv_adj_qbar_rb_kernel<16>, smem, items), 256, smem, s>>>(
+            Pbar, cs, M, gseed, b, Qbar);
     else
-        conv_adj_qbar_rb_kernel<32><<<grid, 256, smem, s>>>(Pbar, cs, M, gseed, b, Qbar);
+        conv_adj_qbar_rb_kernel<32><<<rb_grid(conv_adj_qbar_rb_kernel<32>, smem, items), 256, smem, s>>>(
+            Pbar, cs, M, gseed, b, Qbar);
     LB_LAUNCH();
 }
 
@@ -1514,22 +1565,23 @@ void launch_fold_double(double* src_k, double* src_b, float* dst_k, float* dst_b
 
 __global__ void alpha_init_win_kernel(RowMap rows, WinGeo g, const float* __restrict__ init, int n,
                                       float* __restrict__ alpha) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int nw = g.size();
-    if (idx >= (int64_t)2 * rows.R * nw) return;
-    const int r2 = (int)(idx / nw), j = (int)(idx - (int64_t)r2 * nw);
-    const int rr = r2 >= rows.R ? r2 - rows.R : r2;
-    int oy, ox;
-    win_origin(g, rows.row_id[rr], oy, ox);
-    const int nu = win_neuron(g, oy, ox, j);
-    alpha[idx] = nu >= 0 ? init[(size_t)rows.row_box[rr] * n + nu] : 0.f;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    for (int r2 = blockIdx.y; r2 < 2 * rows.R; r2 += gridDim.y) {
+        const int rr = r2 >= rows.R ? r2 - rows.R : r2;
+        if (j >= nw) continue;
+        int oy, ox;
+        win_origin(g, rows.row_id[rr], oy, ox);
+        const int nu = win_neuron(g, oy, ox, j);
+        alpha[(size_t)r2 * nw + j] = nu >= 0 ? init[(size_t)rows.row_box[rr] * n + nu] : 0.f;
+    }
 }
 
 void launch_alpha_init_win(const RowMap& rows, const WinGeo& g, const float* init_slope, int n, float* alpha,
                            cudaStream_t s) {
-    const int64_t total = (int64_t)2 * rows.R * g.size();
-    if (total == 0) return;
-    alpha_init_win_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows, g, init_slope, n, alpha);
+    if (rows.R == 0 || g.size() == 0) return;
+    const dim3 grid(ceil_div(g.size(), 256), std::min(2 * rows.R, 65535));
+    alpha_init_win_kernel<<<grid, 256, 0, s>>>(rows, g, init_slope, n, alpha);
     LB_LAUNCH();
 }
 

@@ -118,6 +118,9 @@ public:
         force_simt_ = on;
         tcconv_ = !on;
     }
+    // Tensor-core contractions on CTA pairs (default) or on single CTAs
+    // (for cross-checking).
+    void set_pairs(bool on) { pairs_ = on; }
     const lb200_options& options() const { return opt_; }
     // The plan as JSON: every level (node, map, activation, main edge, skip
     // edges) and every backward start (concretisation form and the row
@@ -195,6 +198,7 @@ private:
     TcConvPlan tc_adj_plan(int st, int m, int rows, const float* pbar) const;
     PhaseSplit phase_split(int st, int m) const;
     bool tcconv_ = true;
+    bool pairs_ = true;
     int start_form(int st) const;
     bool has_conv_ = false;
     std::string key(const char* what, int a, int b = -1) const;

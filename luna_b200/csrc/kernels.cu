@@ -4,6 +4,7 @@
 #include "kernels.cuh"
 #include "property.cuh"
 
+#include <algorithm>
 #include <cmath>
 
 namespace lb200 {
@@ -237,19 +238,29 @@ void launch_relu_params(const float* l, const float* u, int B, int n, bool alpha
     LB_LAUNCH();
 }
 
+// Row copies [2R, n] <- per-box rows: block (x, y) copies 1024 floats of row y
+// (rows beyond gridDim.y in steps of gridDim.y), by float4 when n % 4 == 0.
+__device__ __forceinline__ void copy_row(const float* __restrict__ src, float* __restrict__ dst, int n) {
+    const int c0 = blockIdx.x * 1024 + threadIdx.x * 4;
+    if ((n & 3) == 0) {
+        if (c0 < n) *reinterpret_cast<float4*>(dst + c0) = *reinterpret_cast<const float4*>(src + c0);
+    } else {
+        for (int c = c0; c < min(c0 + 4, n); ++c) dst[c] = src[c];
+    }
+}
+
 __global__ void alpha_init_kernel(const int* __restrict__ row_box, int R, const float* __restrict__ init,
                                   int n, float* __restrict__ alpha) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (int64_t)2 * R * n) return;
-    const int r2 = (int)(idx / n), j = (int)(idx % n);
-    const int rr = r2 >= R ? r2 - R : r2;
-    alpha[idx] = init[(size_t)row_box[rr] * n + j];
+    for (int r2 = blockIdx.y; r2 < 2 * R; r2 += gridDim.y) {
+        const int rr = r2 >= R ? r2 - R : r2;
+        copy_row(init + (size_t)row_box[rr] * n, alpha + (size_t)r2 * n, n);
+    }
 }
 
 void launch_alpha_init(const RowMap& rows, const float* init_slope, int n, float* alpha, cudaStream_t s) {
-    const int64_t total = (int64_t)2 * rows.R * n;
-    if (total == 0) return;
-    alpha_init_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows.row_box, rows.R, init_slope, n, alpha);
+    if (rows.R == 0 || n == 0) return;
+    const dim3 grid(ceil_div(n, 1024), std::min(2 * rows.R, 65535));
+    alpha_init_kernel<<<grid, 256, 0, s>>>(rows.row_box, rows.R, init_slope, n, alpha);
     LB_LAUNCH();
 }
 
@@ -1035,31 +1046,26 @@ void launch_best_alpha(const RowMap& rows, const int* save, const int* first_sav
     LB_LAUNCH();
 }
 
-// Thread per (side, box, local row < nspec, column).
+// Block row y = (side, box, local row < nspec); x = 1024 columns.
 __global__ void best_alpha_rows_kernel(RowMap rows, int B, const int* __restrict__ save,
                                        const uint8_t* __restrict__ improved, int nspec, int n,
                                        const float* __restrict__ alpha, float* __restrict__ best) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const int64_t per_side = (int64_t)B * nspec * n;
-    if (idx >= 2 * per_side) return;
-    const int p = (int)(idx / per_side);
-    const int64_t rem = idx % per_side;
-    const int bx = (int)(rem / ((int64_t)nspec * n));
-    const int local = (int)((rem / n) % nspec);
-    const int c = (int)(rem % n);
-    if (!save[bx] || !improved[(size_t)bx * nspec + local]) return;
-    const int first = rows.box_off[bx];
-    if (first + local >= rows.box_off[bx + 1]) return;
-    const size_t at = ((size_t)p * rows.R + first + local) * n + c;
-    best[at] = alpha[at];
+    for (int y = blockIdx.y; y < 2 * B * nspec; y += gridDim.y) {
+        const int p = y / (B * nspec), rem = y - p * (B * nspec);
+        const int bx = rem / nspec, local = rem - bx * nspec;
+        if (!save[bx] || !improved[(size_t)bx * nspec + local]) continue;
+        const int first = rows.box_off[bx];
+        if (first + local >= rows.box_off[bx + 1]) continue;
+        const size_t row = (size_t)p * rows.R + first + local;
+        copy_row(alpha + row * n, best + row * n, n);
+    }
 }
 
 void launch_best_alpha_rows(const RowMap& rows, int B, const int* save, const uint8_t* improved, int nspec,
                             int n, const float* alpha, float* best_alpha, cudaStream_t s) {
-    const int64_t total = (int64_t)2 * B * nspec * n;
-    if (total == 0 || rows.R == 0) return;
-    best_alpha_rows_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows, B, save, improved, nspec, n, alpha,
-                                                                best_alpha);
+    if (B == 0 || nspec == 0 || n == 0 || rows.R == 0) return;
+    const dim3 grid(ceil_div(n, 1024), std::min(2 * B * nspec, 65535));
+    best_alpha_rows_kernel<<<grid, 256, 0, s>>>(rows, B, save, improved, nspec, n, alpha, best_alpha);
     LB_LAUNCH();
 }
 
@@ -1222,18 +1228,17 @@ void launch_negate(const float* in, float* out, int64_t n, cudaStream_t s) {
 
 __global__ void restore_alpha_kernel(RowMap rows, const int* __restrict__ first_save, int n,
                                      const float* __restrict__ best, float* __restrict__ alpha) {
-    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= (int64_t)2 * rows.R * n) return;
-    const int r2 = (int)(idx / n);
-    const int rr = r2 >= rows.R ? r2 - rows.R : r2;
-    if (!first_save[rows.row_box[rr]]) alpha[idx] = best[idx];
+    for (int r2 = blockIdx.y; r2 < 2 * rows.R; r2 += gridDim.y) {
+        const int rr = r2 >= rows.R ? r2 - rows.R : r2;
+        if (!first_save[rows.row_box[rr]]) copy_row(best + (size_t)r2 * n, alpha + (size_t)r2 * n, n);
+    }
 }
 
 void launch_restore_alpha(const RowMap& rows, const int* first_save, int n, const float* best_alpha,
                           float* alpha, cudaStream_t s) {
-    const int64_t total = (int64_t)2 * rows.R * n;
-    if (total == 0) return;
-    restore_alpha_kernel<<<ceil_div(total, 256), 256, 0, s>>>(rows, first_save, n, best_alpha, alpha);
+    if (rows.R == 0 || n == 0) return;
+    const dim3 grid(ceil_div(n, 1024), std::min(2 * rows.R, 65535));
+    restore_alpha_kernel<<<grid, 256, 0, s>>>(rows, first_save, n, best_alpha, alpha);
     LB_LAUNCH();
 }
 

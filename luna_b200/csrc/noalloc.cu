@@ -15,10 +15,9 @@
 // library holds its 16 MiB until the process exits.  In host code its name
 // is only a host-side stand-in, never a device address; the address is
 // obtained per device with cudaGetSymbolAddress, with that device current,
-// on the first call made on that device (so make that first call before any
-// stream capture begins).  All calls share the array and it keeps the last
-// call's contents; nothing in it needs to start at zero (every layer is
-// fully written before it is read).  Calls whose work overlaps on the GPU
+// on the first call made on that device.  All calls share the array and it
+// keeps the last call's contents; nothing in it needs to start at zero
+// (every layer is fully written before it is read).  Calls whose work overlaps on the GPU
 // (different streams, or different host threads) race on the array and
 // must be serialised by the caller.
 #include "handle.h"

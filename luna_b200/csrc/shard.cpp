@@ -117,6 +117,27 @@ int lb200_nccl_comm_create(const uint8_t id[128], int rank, int world, int devic
         std::memcpy(&u, id, 128);
         ncclComm_t c = nullptr;
         nccl_check(nccl().comm_init_rank(&c, world, u, rank), "ncclCommInitRank");
+        // NCCL sets up a collective's peer connections on its first use, and
+        // that setup waits on the host for every peer.  One all-gather now,
+        // while every rank is known to be here, makes it happen at creation,
+        // so that a later gather whose peer never arrives only waits on the
+        // device, where lb200_shard_run's bounded wait can abort it.
+        cudaStream_t s = nullptr;
+        float* buf = nullptr;
+        try {
+            LB_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+            LB_CUDA(cudaMalloc(&buf, sizeof(float) * (size_t)(world + 1)));
+            LB_CUDA(cudaMemsetAsync(buf, 0, sizeof(float) * (size_t)(world + 1), s));
+            nccl_check(nccl().all_gather(buf + world, buf, 1, ncclFloat32, c, s), "ncclAllGather (connection setup)");
+            LB_CUDA(cudaStreamSynchronize(s));
+        } catch (...) {
+            if (buf) cudaFree(buf);
+            if (s) cudaStreamDestroy(s);
+            nccl().comm_abort(c);
+            throw;
+        }
+        LB_CUDA(cudaFree(buf));
+        LB_CUDA(cudaStreamDestroy(s));
         *comm = c;
     });
 }

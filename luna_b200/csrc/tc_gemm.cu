@@ -220,16 +220,22 @@ __device__ __forceinline__ void seed_row16(const SeedRow& sr, int K, int k0, con
 }
 
 // ------------------------------------------------------------- kernel
-template <int BN, int S, int KIND, int AMODE>
+template <int BN, int S, int KIND, int AMODE, int CG>
 __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tbh,
                    const __grid_constant__ CUtensorMap tbl, const __grid_constant__ CUtensorMap talpha, int M,
                    int N, int K, TcEpi ep, TcPrologue pro, float* partial) {
-    constexpr int B_TILE_BYTES = BN * TC_BK * 4;
+    // CG = 2: a CTA pair (cluster of 2) shares each 256-row tile; this CTA
+    // holds 128 rows of A and BN / 2 rows of B, and the even CTA issues the
+    // MMAs for both.
+    static_assert(CG == 1 || CG == 2, "CTA group of 1 or 2");
+    constexpr int BN_CTA = BN / CG;
+    constexpr int TILE_M = TC_BM * CG;
+    constexpr int B_TILE_BYTES = BN_CTA * TC_BK * 4;
     constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;
     constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                                      : (2 * BN <= 256) ? 256 : 512;
-    constexpr uint32_t IDESC = idesc_tf32(BN);
+    constexpr uint32_t IDESC = idesc_tf32(BN, TILE_M);
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -243,33 +249,65 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0;
     if (threadIdx.x == 0) {
         for (int s = 0; s < S; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&split[s], xf_threads<AMODE>());
+            // The leader's split barrier counts the operand-forming threads of
+            // both CTAs; its tempty barrier both CTAs' epilogue threads.
+            mbar_init(&split[s], xf_threads<AMODE>() * CG);
             mbar_init(&empty[s], 1);
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&tfull[a], 1);
-            mbar_init(&tempty[a], 128);
+            mbar_init(&tempty[a], 128 * CG);
         }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == WARP_TMA) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        if constexpr (CG == 2) {
+            // One warp of each CTA of the pair allocates, collectively.
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"(TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_u32(tmem_slot)),
+                         "r"(TMEM_COLS));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (CG == 2) cluster_sync();  // the peer's barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
     const int tiles_n = (N + BN - 1) / BN;
-    const int tiles_m = (M + TC_BM - 1) / TC_BM;
+    const int tiles_m = (M + TILE_M - 1) / TILE_M;
     const int ntiles = tiles_n * tiles_m;
     const int nk = (K + TC_BK - 1) / TC_BK;
+    // Tiles are walked per CTA group: group g takes tiles g, g + groups, ...
+    const int group = blockIdx.x / CG, groups = gridDim.x / CG;
+    // Barrier waits whose phase the peer CTA may complete use cluster-scope
+    // acquire.
+    auto wait_bar = [&](uint64_t* b, uint32_t ph, bool ignore_abort = false) {
+        if constexpr (CG == 2) return mbar_wait_cluster(b, ph, abort, &g_tc_error, ignore_abort);
+        else return mbar_wait(b, ph, abort, &g_tc_error, ignore_abort);
+    };
+    // Arrival on a barrier the leader waits on (the leader's copy).
+    auto arrive_leader = [&](uint64_t* b) {
+        if constexpr (CG == 2) {
+            if (!leader) {
+                mbar_arrive_remote(peer_addr(b, 0));
+                return;
+            }
+        }
+        mbar_arrive(b);
+    };
 
     auto a_hi = [&](int s) { return base + (size_t)s * STAGE_BYTES; };
     auto a_lo = [&](int s) { return base + (size_t)s * STAGE_BYTES + A_TILE_BYTES; };
@@ -280,12 +318,13 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
         if (lane == 0) {
             uint32_t g = 0;
             const bool starve = g_tc_starve != 0;
-            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+            for (int t = group; t < ntiles && !*abort; t += groups) {
                 const int mb = t / tiles_n, nb = t % tiles_n;
+                const int row0 = mb * TILE_M + (int)rank * TC_BM;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int s = g % S;
                     const uint32_t ph = (g / S) & 1;
-                    if (!mbar_wait(&empty[s], ph ^ 1, abort, &g_tc_error)) break;
+                    if (!wait_bar(&empty[s], ph ^ 1)) break;
                     // A raw (TMA / RELAX: P) lands in the hi slot, alpha (RELAX /
                     // GATHER) in the lo slot; the split warps overwrite both.
                     const bool load_a = AMODE == AMODE_TMA || AMODE == AMODE_RELAX;
@@ -293,10 +332,10 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
                     mbar_arrive_tx(&full[s], (load_a ? A_TILE_BYTES : 0) + (load_alpha ? A_TILE_BYTES : 0) +
                                                  2 * B_TILE_BYTES);
                     if (starve) continue;
-                    if (load_a) tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, mb * TC_BM);
-                    if (load_alpha) tma_load_2d(&talpha, &full[s], a_lo(s), kb * TC_BK, mb * TC_BM);
-                    tma_load_2d(&tbh, &full[s], b_hi(s), kb * TC_BK, nb * BN);
-                    tma_load_2d(&tbl, &full[s], b_lo(s), kb * TC_BK, nb * BN);
+                    if (load_a) tma_load_2d(&ta, &full[s], a_hi(s), kb * TC_BK, row0);
+                    if (load_alpha) tma_load_2d(&talpha, &full[s], a_lo(s), kb * TC_BK, row0);
+                    tma_load_2d(&tbh, &full[s], b_hi(s), kb * TC_BK, nb * BN + (int)rank * BN_CTA);
+                    tma_load_2d(&tbl, &full[s], b_lo(s), kb * TC_BK, nb * BN + (int)rank * BN_CTA);
                 }
             }
             if (*abort) {
@@ -306,22 +345,23 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
             }
         }
     } else if (warp == WARP_MMA) {
-        if (lane == 0) {
+        // One thread of the leader issues every MMA of the CTA group.
+        if (lane == 0 && leader) {
             uint32_t g = 0, j = 0;
             bool issued = false;
             uint64_t* last_commit = nullptr;
             uint32_t last_phase = 0;
-            for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++j) {
+            for (int t = group; t < ntiles && !*abort; t += groups, ++j) {
                 const int acc = j & 1;
                 const uint32_t aph = (j >> 1) & 1;
-                if (!mbar_wait(&tempty[acc], aph ^ 1, abort, &g_tc_error)) break;
+                if (!wait_bar(&tempty[acc], aph ^ 1)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int s = g % S;
                     const uint32_t ph = (g / S) & 1;
-                    if (!mbar_wait(&split[s], ph, abort, &g_tc_error)) { ok = false; break; }
+                    if (!wait_bar(&split[s], ph)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t dah = desc_sw128(smem_u32(a_hi(s)));
                     const uint64_t dal = desc_sw128(smem_u32(a_lo(s)));
@@ -330,19 +370,27 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
 #pragma unroll
                     for (int k8 = 0; k8 < TC_BK / 8; ++k8) {
                         const uint64_t off = (uint64_t)(k8 * 32) >> 4;  // 8 tf32 = 32 bytes along K
-                        umma_tf32(d, dal + off, dbh + off, IDESC, (kb | k8) != 0);
-                        umma_tf32(d, dah + off, dbl + off, IDESC, 1);
-                        umma_tf32(d, dah + off, dbh + off, IDESC, 1);
+                        if constexpr (CG == 2) {
+                            umma_tf32_pair(d, dal + off, dbh + off, IDESC, (kb | k8) != 0);
+                            umma_tf32_pair(d, dah + off, dbl + off, IDESC, 1);
+                            umma_tf32_pair(d, dah + off, dbh + off, IDESC, 1);
+                        } else {
+                            umma_tf32(d, dal + off, dbh + off, IDESC, (kb | k8) != 0);
+                            umma_tf32(d, dah + off, dbl + off, IDESC, 1);
+                            umma_tf32(d, dah + off, dbh + off, IDESC, 1);
+                        }
                     }
-                    umma_commit(&empty[s]);
+                    if constexpr (CG == 2) umma_commit_pair(&empty[s]);
+                    else umma_commit(&empty[s]);
                     issued = true;
                     last_commit = &empty[s];
                     last_phase = ph;
                 }
                 if (!ok) break;
-                umma_commit(&tfull[acc]);
+                if constexpr (CG == 2) umma_commit_pair(&tfull[acc]);
+                else umma_commit(&tfull[acc]);
             }
-            if (*abort && issued) mbar_wait(last_commit, last_phase, abort, &g_tc_error, true);
+            if (*abort && issued) wait_bar(last_commit, last_phase, true);
         }
     } else if (warp >= XF_WARP0 && AMODE == AMODE_SEED) {
         // Two threads per tile row: thread xt forms columns [16 h, 16 h + 16)
@@ -350,10 +398,10 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
         const int xt = threadIdx.x - XF_WARP0 * 32;
         const int xrow = xt & (TC_BM - 1), h = xt / TC_BM;
         uint32_t g = 0;
-        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        for (int t = group; t < ntiles && !*abort; t += groups) {
             bool ok = true;
             const int mb_t = t / tiles_n;
-            const SeedRow seed = seed_row_info(ep.q, mb_t * TC_BM + xrow, M, K);
+            const SeedRow seed = seed_row_info(ep.q, mb_t * TILE_M + (int)rank * TC_BM + xrow, M, K);
             uint4 sg_next = seed_signs16(seed, K, 16 * h);  // next K block's signs, one block ahead
             for (int kb = 0; kb < nk; ++kb, ++g) {
                 const int s = g % S;
@@ -392,7 +440,7 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
                     lo[at] = lv;
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&split[s]);
+                arrive_leader(&split[s]);
             }
             if (!ok) break;
         }
@@ -404,11 +452,12 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
         int rbox = 0, rid = 0, rside = 0;
         float bsum = 0.f;
         bool rok = false;
-        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        for (int t = group; t < ntiles && !*abort; t += groups) {
             bool ok = true;
             const int mb_t = t / tiles_n, nb_t = t % tiles_n;
+            const int row0 = mb_t * TILE_M + (int)rank * TC_BM;
             if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
-                const int r = mb_t * TC_BM + xt;
+                const int r = row0 + xt;
                 rok = r < M;
                 bsum = 0.f;
                 rbox = rid = rside = 0;
@@ -500,26 +549,26 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
                     }
                 }
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&split[s]);
+                arrive_leader(&split[s]);
             }
             if (!ok) break;
             if constexpr (AMODE == AMODE_RELAX || AMODE == AMODE_GATHER) {
                 // One write per row: only the first column tile of each row block.
                 if (rok && nb_t == 0 && pro.bias_part)
-                    pro.bias_part[mb_t * TC_BM + xt] =
+                    pro.bias_part[row0 + xt] =
                         bsum + ((AMODE == AMODE_GATHER && pro.gather_b) ? pro.gather_b[rid] : 0.f);
             }
         }
     } else if (warp >= EPI_WARP0 && warp < EPI_WARP0 + 4) {
         const int q = warp - EPI_WARP0;
         uint32_t j = 0;
-        for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x, ++j) {
+        for (int t = group; t < ntiles && !*abort; t += groups, ++j) {
             const int mb = t / tiles_n, nb = t % tiles_n;
             const int acc = j & 1;
             const uint32_t aph = (j >> 1) & 1;
-            if (!mbar_wait(&tfull[acc], aph, abort, &g_tc_error)) break;
+            if (!wait_bar(&tfull[acc], aph)) break;
             tc_fence_after();
-            const int r = mb * TC_BM + q * 32 + lane;
+            const int r = mb * TILE_M + (int)rank * TC_BM + q * 32 + lane;
             const bool row_ok = r < M;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
             float part = 0.f;
@@ -556,14 +605,20 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
                 if (row_ok && partial) partial[(size_t)nb * M + r] = part;
             }
             tc_fence_before();
-            mbar_arrive(&tempty[acc]);
+            arrive_leader(&tempty[acc]);
         }
     }
     tc_fence_before();
     __syncthreads();
+    // Neither CTA of a pair releases its TMEM or exits while the other may
+    // still use the pair's resources.
+    if constexpr (CG == 2) cluster_sync();
     if (warp == WARP_TMA) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+        if constexpr (CG == 2)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS));
     }
 }
 
@@ -606,39 +661,77 @@ int num_sms() {
     return n;
 }
 
-template <int BN, int S, int KIND, int AMODE>
+template <int BN, int S, int KIND, int AMODE, int CG>
 void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
             const TcPrologue& pro, float* partial, cudaStream_t s) {
-    constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * BN * TC_BK * 4;
+    constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * (BN / CG) * TC_BK * 4;
     constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
-    static bool configured = false;
-    if (!configured) {
-        LB_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<BN, S, KIND, AMODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     SMEM));
-        configured = true;
+    auto kernel = tc_gemm_kernel<BN, S, KIND, AMODE, CG>;
+    static int max_groups = 0;
+    if (!max_groups) {
+        LB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
+        if (CG == 2) {
+            // CTA pairs that can be resident at once (a pair sits in one GPC).
+            cudaLaunchConfig_t q = {};
+            q.gridDim = dim3(2 * num_sms());
+            q.blockDim = dim3(kernel_threads<AMODE>());
+            q.dynamicSmemBytes = SMEM;
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 2;
+            at[0].val.clusterDim.y = 1;
+            at[0].val.clusterDim.z = 1;
+            q.attrs = at;
+            q.numAttrs = 1;
+            int n = 0;
+            LB_CUDA(cudaOccupancyMaxActiveClusters(&n, kernel, &q));
+            if (n <= 0) throw std::runtime_error("tc contraction: no CTA pair fits on this GPU");
+            max_groups = n;
+        } else {
+            max_groups = num_sms();
+        }
     }
     // Maps the mode does not read are encoded over B so that they stay valid.
     const bool a_tma = AMODE == AMODE_TMA || AMODE == AMODE_RELAX;
     const float* a_src = AMODE == AMODE_RELAX ? pro.P : A;
     const CUtensorMap ta = a_tma ? make_map(a_src, M, K, TC_BM) : make_map(Bhi, N, K, TC_BM);
     const CUtensorMap talpha = pro.alpha ? make_map(pro.alpha, M, K, TC_BM) : make_map(Bhi, N, K, TC_BM);
-    const CUtensorMap tbh = make_map(Bhi, N, K, BN);
-    const CUtensorMap tbl = make_map(Blo, N, K, BN);
-    const int ntiles = ((N + BN - 1) / BN) * ((M + TC_BM - 1) / TC_BM);
-    const int grid = std::min(ntiles, num_sms());
-    tc_gemm_kernel<BN, S, KIND, AMODE><<<grid, kernel_threads<AMODE>(), SMEM, s>>>(ta, tbh, tbl, talpha, M, N, K, ep, pro,
-                                                                       partial);
+    const CUtensorMap tbh = make_map(Bhi, N, K, BN / CG);
+    const CUtensorMap tbl = make_map(Blo, N, K, BN / CG);
+    const int ntiles = ((N + BN - 1) / BN) * ((M + TC_BM * CG - 1) / (TC_BM * CG));
+    const int groups = std::min(ntiles, max_groups);
+    if (CG == 1) {
+        kernel<<<groups, kernel_threads<AMODE>(), SMEM, s>>>(ta, tbh, tbl, talpha, M, N, K, ep, pro, partial);
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * groups);
+        cfg.blockDim = dim3(kernel_threads<AMODE>());
+        cfg.dynamicSmemBytes = SMEM;
+        cfg.stream = s;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 2;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        LB_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tbh, tbl, talpha, M, N, K, ep, pro, partial));
+    }
     LB_LAUNCH();
 }
 
 template <int KIND, int AMODE>
 void dispatch(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
-              const TcPrologue& pro, float* partial, cudaStream_t s) {
-    switch (tc_block_n(N)) {
-    case 256: run_tc<256, 2, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
-    case 128: run_tc<128, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
-    case 112: run_tc<112, 3, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
-    default: run_tc<64, 4, KIND, AMODE>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+              const TcPrologue& pro, float* partial, bool pairs, cudaStream_t s) {
+    if (tc_block_n(N, pairs) == 224) {
+        run_tc<224, 3, KIND, AMODE, 2>(A, Bhi, Blo, M, N, K, ep, pro, partial, s);
+        return;
+    }
+    switch (tc_block_n(N, false)) {
+    case 256: run_tc<256, 2, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 128: run_tc<128, 3, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 112: run_tc<112, 3, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    default: run_tc<64, 4, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
     }
 }
 
@@ -656,7 +749,7 @@ __global__ void split_tf32_kernel(const float* __restrict__ src, float* __restri
 
 bool tc_supported(int M, int N, int K) { return M > 0 && N >= 16 && N % 16 == 0 && K % 4 == 0 && K >= 4; }
 
-int tc_block_n(int N) {
+static int block_n_single(int N) {
     const int cands[4] = {256, 128, 112, 64};
     int best = 64, best_pad = 1 << 30;
     for (int bn : cands) {
@@ -669,7 +762,20 @@ int tc_block_n(int N) {
     return best;
 }
 
-int tc_tiles_n(int N) { return (N + tc_block_n(N) - 1) / tc_block_n(N); }
+int tc_block_n(int N, bool pairs) {
+    const int single = block_n_single(N);
+    // CTA pairs take 224-column tiles (112 per CTA) where single CTAs would
+    // take several 112-column ones and the padding stays within 15%.  Only
+    // there did pairs measure faster (the 784-wide input concretisation of
+    // the MLP: tensor pipe 41% -> 52%, 187 -> 172 us per launch); the
+    // 256-column tiles whose A operand is formed in the kernel (seed,
+    // relaxation prologue) ran slower on pairs, since each stage then waits
+    // for the slower of two CTAs' operand-forming warps.
+    if (pairs && single == 112 && N > 224 && ((N + 223) / 224) * 224 * 20 <= N * 23) return 224;
+    return single;
+}
+
+int tc_tiles_n(int N, bool pairs) { return (N + tc_block_n(N, pairs) - 1) / tc_block_n(N, pairs); }
 
 void tc_set_test_fault(int starve, long long wait_cycles) {
     const long long w = wait_cycles > 0 ? wait_cycles : WAIT_CYCLES;
@@ -691,42 +797,42 @@ void launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, cudaSt
 }
 
 void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                          const EpiStoreQbar& e, cudaStream_t s) {
+                          const EpiStoreQbar& e, bool pairs, cudaStream_t s) {
     if (M == 0) return;
     TcEpi ep{};
     ep.q = e;
     const TcPrologue none{};
     if (e.seed_sign)
-        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, none, nullptr, s);
+        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, none, nullptr, pairs, s);
     else
-        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, none, nullptr, s);
+        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, none, nullptr, pairs, s);
 }
 
 template <int KIND>
 static void dispatch_amode(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M,
-                           int N, int K, const TcEpi& ep, float* partial, cudaStream_t s) {
+                           int N, int K, const TcEpi& ep, float* partial, bool pairs, cudaStream_t s) {
     if (pro.gather_W)
-        dispatch<KIND, AMODE_GATHER>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, s);
+        dispatch<KIND, AMODE_GATHER>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
     else if (pro.P)
-        dispatch<KIND, AMODE_RELAX>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, s);
+        dispatch<KIND, AMODE_RELAX>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
     else
-        dispatch<KIND, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, pro, partial, s);
+        dispatch<KIND, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
 }
 
 void launch_tc_forward(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M, int N,
                        int K, float* P_out, const EpiRelaxFwd* fwd, const EpiConcretize* conc, float* partial,
-                       cudaStream_t s) {
+                       bool pairs, cudaStream_t s) {
     if (M == 0) return;
     TcEpi ep{};
     if (conc) {
         ep.c = *conc;
-        dispatch_amode<KIND_CONC>(A, pro, Bhi, Blo, M, N, K, ep, partial, s);
+        dispatch_amode<KIND_CONC>(A, pro, Bhi, Blo, M, N, K, ep, partial, pairs, s);
     } else if (fwd) {
         ep.f = *fwd;
-        dispatch_amode<KIND_FWD>(A, pro, Bhi, Blo, M, N, K, ep, partial, s);
+        dispatch_amode<KIND_FWD>(A, pro, Bhi, Blo, M, N, K, ep, partial, pairs, s);
     } else {
         ep.P_out = P_out;
-        dispatch_amode<KIND_STOREP>(A, pro, Bhi, Blo, M, N, K, ep, nullptr, s);
+        dispatch_amode<KIND_STOREP>(A, pro, Bhi, Blo, M, N, K, ep, nullptr, pairs, s);
     }
 }
 

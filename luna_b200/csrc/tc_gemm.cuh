@@ -15,9 +15,12 @@ namespace lb200 {
 // strides; the MMA needs N a multiple of 16).
 bool tc_supported(int M, int N, int K);
 // Column tile of the tensor-core path for N (its partial-sum tile count is
-// ceil(N / tc_block_n(N))).
-int tc_block_n(int N);
-int tc_tiles_n(int N);
+// ceil(N / tc_block_n(N, pairs))).  With `pairs`, wide N that single CTAs
+// would cut into 112-column tiles takes 224-column tiles on CTA pairs
+// (tcgen05 cta_group::2, 256-row tiles): each SM of a pair stages half of the
+// B tile and 128 rows of A.
+int tc_block_n(int N, bool pairs);
+int tc_tiles_n(int N, bool pairs);
 
 // Split src into tf32 (hi, lo) with round-to-nearest: hi = rna(x),
 // lo = rna(x - hi); n elements.
@@ -35,7 +38,7 @@ void tc_conv_set_wait_limit(long long wait_cycles);
 // Adjoint contraction storing Qbar = A . B^T + g b_lin only; with
 // e.seed_sign set the A operand is generated from the concretisation signs.
 void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                          const EpiStoreQbar& e, cudaStream_t s);
+                          const EpiStoreQbar& e, bool pairs, cudaStream_t s);
 
 // Forward contraction whose A operand is the ReLU relaxation of P, formed in
 // the kernel (BoundedReLUNode::boundBackward, dense A): Q = P+ s + P- k
@@ -61,6 +64,6 @@ struct TcPrologue {
 // and Q, partial sums per column tile), else a raw store of P into P_out.
 void launch_tc_forward(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M, int N,
                        int K, float* P_out, const EpiRelaxFwd* fwd, const EpiConcretize* conc, float* partial,
-                       cudaStream_t s);
+                       bool pairs, cudaStream_t s);
 
 }  // namespace lb200

@@ -57,6 +57,54 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
     }
 }
 
+// ---- CTA pairs (cluster of 2, tcgen05 cta_group::2) ------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Shared-memory address of the same variable in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t peer_addr(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Arrive on an mbarrier of another CTA of the cluster (release at cluster
+// scope, so this thread's earlier writes are visible to the waiter).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// try_wait with acquire at cluster scope (the phase may have been completed
+// by arrivals from the peer CTA).
+__device__ __forceinline__ bool mbar_try_cluster(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* b, uint32_t parity, volatile int* abort, int* err,
+                                                  bool ignore_abort = false) {
+    if (mbar_try_cluster(b, parity)) return true;
+    const long long t0 = clock64();
+    const long long limit = g_wait_limit;
+    while (true) {
+        if (mbar_try_cluster(b, parity)) return true;
+        if (!ignore_abort && *abort) return false;
+        if (clock64() - t0 > limit) {
+            *abort = 1;
+            atomicExch(err, 1);
+            return false;
+        }
+    }
+}
+
 __device__ __forceinline__ void tma_load_2d(const void* map, uint64_t* bar, void* dst, int x, int y) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -86,9 +134,10 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
     return d;
 }
 
-// Instruction descriptor: D fp32, A/B tf32, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t idesc_tf32(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+// Instruction descriptor: D fp32, A/B tf32, both K-major, M = m (128, or 256
+// for a CTA pair), N = n.
+__host__ __device__ constexpr uint32_t idesc_tf32(int n, int m = 128) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
@@ -101,6 +150,28 @@ __device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t a, uint64_t 
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+// CTA pair: one MMA, issued by the even CTA, computes a 256-row tile; each
+// CTA supplies its 128 rows of A and half of B's rows from its own shared
+// memory at the same offsets, and receives its 128 rows of D in its own
+// TMEM.
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc,
+                                               uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+// Completion of the pair's MMAs issued so far, signalled on the mbarrier at
+// the same offset in both CTAs (one commit per CTA, the peer's barrier by its
+// cluster address).
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     peer_addr(bar, 1))
                  : "memory");
 }
 

@@ -185,7 +185,8 @@ class Model:
         _check(_lib.lb200_set_profiling(self._h, int(on)), "lb200_set_profiling")
 
     def set_contraction_path(self, path: int):
-        """0: tensor cores (3xTF32) where the shape allows; 1: SIMT fp32 only."""
+        """0: tensor cores (3xTF32) where the shape allows, 224-column tiles on
+        CTA pairs for wide N; 1: SIMT fp32 only; 2: tensor cores on single CTAs."""
         _check(_lib.lb200_set_contraction_path(self._h, int(path)), "lb200_set_contraction_path")
 
     def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,

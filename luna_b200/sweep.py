@@ -155,3 +155,29 @@ def run_sweep(model, split, method: int, path: str, chunk: int = 256, prop=None,
             sd.write(k, lb, ub)
     return sd
 
+
+
+def finish_ranks(sd: SweepDir, world: int, timeout_s: float | None = None) -> list[int]:
+    """End of a multi-rank sweep (torch.distributed initialised, one process
+    per rank): wait for every rank at a barrier, then return the chunks that
+    are still pending over all ranks (empty when the sweep is complete).
+
+    A rank that died before the barrier makes the wait fail on the others:
+    the peer's closed connection or the group's timeout (`timeout_s`, with
+    gloo's monitored barrier; otherwise the process group's own) raises.  This
+    function then raises RuntimeError naming the chunks left pending, which a
+    rerun of the same sweep, at any world size, bounds without redoing the
+    chunks already written."""
+    import datetime
+
+    import torch.distributed as dist
+    try:
+        if timeout_s is not None and dist.get_backend() == "gloo":
+            dist.monitored_barrier(timeout=datetime.timedelta(seconds=timeout_s))
+        else:
+            dist.barrier()
+    except RuntimeError as e:
+        missing = sd.pending(0, 1)
+        raise RuntimeError(f"a rank did not reach the end of the sweep ({e}); "
+                           f"{len(missing)} of {sd.n_chunks} chunks pending: rerun to resume") from e
+    return sd.pending(0, 1)

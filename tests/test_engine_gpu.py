@@ -43,13 +43,30 @@ def test_engine_matches_luna(name):
         assert e <= 1.0 and states, e
 
 
+def test_cfg2_simt_path_matches_luna_as_luna_matches_itself():
+    """The 512-box MLP alpha-CROWN golden through the SIMT fp32 contractions:
+    as many boxes beyond the strict bar as Luna's own result shows between
+    1 and 4 ATen threads (the tensor-core path's larger count comes from its
+    accumulation, not from the algorithm)."""
+    c = G.load("cfg2_alpha512")
+    m = Model(c["graph"], options=c["options"])
+    m.set_contraction_path(1)
+    lb, ub = m.compute_bounds(c["boxes"], c["method"])
+    G.parity("cfg2_alpha512/simt", lb, ub, c["lb"], c["ub"])
+
+
 @pytest.mark.parametrize("name", G.oracle_names())
 def test_engine_matches_oracle_full_size(name):
     """Full-size networks of the ResNet and sweep workloads against the CPU
     oracle's committed results (tests/golden/make_oracle_golden.py)."""
     c = G.load(name)
     lb, ub = Model(c["graph"], options=c["options"]).compute_bounds(c["boxes"], c["method"])
-    _assert_parity(name, lb, ub, c["lb"], c["ub"])
+    # The oracle, not Luna, is the reference here: both it and the engine are
+    # held to the bar against Luna on these networks' smaller relatives, so
+    # the two may differ by the sum of their allowances (twice the bar).
+    e = max(G.excess(lb, c["lb"], 2 * G.RTOL, 2 * G.ATOL), G.excess(ub, c["ub"], 2 * G.RTOL, 2 * G.ATOL))
+    print(f"PARITY {name} vs oracle (2x bar) {e:.4f}, strict {max(G.excess(lb, c['lb']), G.excess(ub, c['ub'])):.4f}")
+    assert e <= 1.0, e
 
 
 def _assert_parity(name, lb, ub, ref_lb, ref_ub):
@@ -229,6 +246,34 @@ def test_tensor_core_path_matches_simt_path(method):
     slb, sub = m.compute_bounds(bx, method)
     print(f"tc vs simt: lb {G.excess(tlb, slb):.3f} ub {G.excess(tub, sub):.3f}")
     assert G.excess(tlb, slb) <= 1.0 and G.excess(tub, sub) <= 1.0
+
+
+@pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
+def test_cta_pair_contractions_match_single_cta(method):
+    """Contractions on CTA pairs (tcgen05 cta_group::2, 256-row tiles) against
+    single-CTA tiles.  A network of 256-wide layers never takes pairs
+    (bit-identical by construction, a check of the path switch); the MLP's
+    784-wide input concretisation takes 224-column pair tiles instead of
+    112-column ones (its per-tile partial sums are added in another order),
+    so that MLP is held to the parity bar.  600 boxes: M = 2 R rows spans
+    several 256-row tiles with a ragged last one."""
+    rng = np.random.default_rng(7)
+    g = W.mlp([256, 256, 256, 256, 10], 11, bias_std=0.1)
+    c = rng.uniform(-1.0, 1.0, (40, 256)).astype(np.float32)
+    bx = W.Boxes((c - 0.05).astype(np.float32), (c + 0.05).astype(np.float32),
+                 W.margin_spec(rng.integers(0, 10, 40), 10))
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=4)
+    m = Model(g, options=opt)
+    plb, pub = m.compute_bounds(bx, method)
+    m.set_contraction_path(2)
+    slb, sub = m.compute_bounds(bx, method)
+    assert np.array_equal(plb, slb) and np.array_equal(pub, sub)
+    g, bx = W.mlp_784_256x4_10(600)
+    m = Model(g, options=opt)
+    plb, pub = m.compute_bounds(bx, method)
+    m.set_contraction_path(2)
+    slb, sub = m.compute_bounds(bx, method)
+    G.parity(f"cta pairs vs single ctas/{method}", plb, pub, slb, sub)
 
 
 def test_device_pointer_entry_point_matches_host_entry_point():

@@ -81,3 +81,24 @@ def test_concat_alpha_rounding_sensitivity():
     cc = G.load("concat_crown")
     m = LirpaOracle(G.merged_concat_graph(cc["graph"]), cc["options"]).compute_bounds(cc["boxes"], cc["method"])
     assert max(G.excess(m[0], cc["lb"]), G.excess(m[1], cc["ub"])) <= 1.0
+
+
+def test_luna_thread_count_spread_on_cfg2():
+    """Luna's own alpha-CROWN result on some of the 512 MLP boxes moves by
+    more than the strict bar between 1 and 4 ATen threads (the golden uses 1):
+    20 Adam steps amplify a last-bit difference in a gradient sum.  This is
+    the measured reason why cfg2_alpha512 cannot be held to the strict bar
+    box by box."""
+    from oracle import luna_ref
+    if not luna_ref.available():
+        pytest.skip("oracle/_ref is not built (make -C oracle)")
+    c = G.load("cfg2_alpha512")
+    spread = {}
+    for b in (429, 251):
+        sub = c["boxes"].slice(b, b + 1)
+        one = luna_ref.compute_bounds(c["graph"], sub, c["method"], c["options"], num_threads=1)
+        four = luna_ref.compute_bounds(c["graph"], sub, c["method"], c["options"], num_threads=4)
+        assert np.array_equal(one[0], c["lb"][b:b + 1]) and np.array_equal(one[1], c["ub"][b:b + 1])
+        spread[b] = max(G.excess(four[0], one[0]), G.excess(four[1], one[1]))
+    assert spread[429] > 5.0, spread   # 9.1 measured
+    assert spread[251] <= 1.0, spread  # most boxes do not move

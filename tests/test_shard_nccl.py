@@ -70,34 +70,38 @@ def test_two_ranks_gather_every_box():
 
 
 def _rank_absent(rank, world, uid, q, gone):
-    """Rank 1 joins the communicator and then never joins the gather: it
-    stays alive, with nothing in flight, until rank 0 has reported, and
-    leaves without touching the communicator again."""
+    """Both ranks bound and gather a first batch; then rank 1 leaves the job
+    between steps: it stays alive, with nothing in flight, until rank 0 has
+    reported, and never touches the communicator again.  Rank 0's second
+    gather must end at its bounded wait."""
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from luna_b200.engine import EngineError, Model, NcclComm
     g, bx, opt = _case()
     m = Model(g, device=rank, options=opt)
     comm = NcclComm(uid, rank, world, rank)
+    first = m.shard_run(comm, bx, abi.METHOD_ALPHA_CROWN, timeout_ms=30000)
     if rank == 0:
         try:
             m.shard_run(comm, bx, abi.METHOD_ALPHA_CROWN, timeout_ms=3000)
-            q.put((0, "no error", None))
+            q.put((0, "no error", first, None))
         except EngineError as e:
             # The model stays usable after the aborted gather.
-            q.put((0, str(e) + (" | handle released" if comm.handle is None else ""),
+            q.put((0, str(e) + (" | handle released" if comm.handle is None else ""), first,
                    m.compute_bounds(bx, abi.METHOD_ALPHA_CROWN)))
         gone.set()
     else:
+        q.put((1, "left", first, None))
         gone.wait(timeout=120)
-        q.put((1, "left", None))
     os._exit(0)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_absent_rank_times_out_the_gather():
-    """A rank that never reaches the gather: the other's bounded wait ends,
-    the communicator is aborted, the call fails with an error, and its model
-    still bounds correctly.  NVLS off (NCCL_NVLS_ENABLE=0)."""
+    """A rank that leaves between steps: the other's next gather ends at its
+    bounded wait, the communicator is aborted, the call fails with an error,
+    and its model still bounds correctly.  NVLS off (NCCL_NVLS_ENABLE=0)."""
+    import queue
+
     from luna_b200.build import build
     from luna_b200.engine import Model, nccl_unique_id
     build()
@@ -110,10 +114,26 @@ def test_absent_rank_times_out_the_gather():
     procs = [ctx.Process(target=_rank_absent, args=(r, 2, uid, q, gone)) for r in range(2)]
     for p in procs:
         p.start()
-    out = {r: (msg, res) for r, msg, res in (q.get(timeout=300) for _ in procs)}
-    for p in procs:
-        p.join(timeout=120)
-        assert p.exitcode == 0
-    msg, res = out[0]
+    out = {}
+    try:
+        for _ in procs:
+            r, msg, first, res = q.get(timeout=180)
+            out[r] = (msg, first, res)
+        for p in procs:
+            p.join(timeout=120)
+    except queue.Empty:
+        pass
+    finally:
+        # A rank still running here is stuck: end it so the test reports
+        # instead of waiting on its process at exit.
+        for p in procs:
+            if p.is_alive():
+                p.kill()
+                p.join(timeout=30)
+    assert sorted(out) == [0, 1], f"ranks that reported: {sorted(out)}"
+    assert all(p.exitcode == 0 for p in procs)
+    for r in range(2):
+        G.parity(f"first step rank {r}", out[r][1][0], out[r][1][1], ref[0], ref[1])
+    msg, _, res = out[0]
     assert "timed out" in msg and "aborted" in msg and "handle released" in msg, msg
     G.parity("after the aborted gather", res[0], res[1], ref[0], ref[1])

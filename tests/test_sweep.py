@@ -116,3 +116,93 @@ def test_two_ranks_share_one_directory(tmp_path):
     assert np.array_equal(lb, elb) and np.array_equal(ub, eub)
     # Each rank took its own chunks: rank 1 alone has nothing left to do.
     assert sd.pending(1, 2) == [] and sd.pending(0, 2) == []
+
+
+class InjectedFailure(Exception):
+    pass
+
+
+class FailingModel(FakeModel):
+    """FakeModel that raises on its call number `fail_at` (1-based)."""
+
+    def __init__(self, fail_at):
+        super().__init__()
+        self.fail_at = fail_at
+
+    def compute_bounds(self, boxes, method):
+        if self.calls + 1 == self.fail_at:
+            raise InjectedFailure("injected")
+        return super().compute_bounds(boxes, method)
+
+
+def _gloo_rank(rank, world, port, path, fail_rank, fail_at, out):
+    import datetime
+
+    import torch.distributed as dist
+
+    from luna_b200.sweep import finish_ranks
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    split = _split()
+    model = FailingModel(fail_at) if rank == fail_rank else FakeModel()
+    try:
+        sd = run_sweep(model, split, abi.METHOD_CROWN, path, chunk=3, rank=rank, world=world)
+    except InjectedFailure:
+        os._exit(3)  # the rank dies between chunks, before the end-of-sweep barrier
+    try:
+        missing = finish_ranks(sd, world, timeout_s=5)
+        msg = f"ok {len(missing)} {model.calls}"
+    except RuntimeError as e:
+        msg = f"failed {e}"
+    with open(f"{out}.{rank}", "w") as f:
+        f.write(msg)
+    os._exit(0)
+
+
+def _free_port():
+    import socket
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _launch(world, path, fail_rank, fail_at, out):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, world, port, path, fail_rank, fail_at, out))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    return [p.exitcode for p in procs]
+
+
+@pytest.mark.timeout(300)
+def test_failed_gloo_rank_is_resumed(tmp_path):
+    """Rank 1 of two gloo ranks raises after one chunk: it exits, rank 0
+    finishes its own chunks and learns of the failure at the end-of-sweep
+    barrier, with the lost chunks named.  A rerun of the sweep bounds only
+    those chunks (rank 0 has none left), and the collected result equals one
+    uninterrupted sweep."""
+    path = str(tmp_path / "sweep")
+    out = str(tmp_path / "msg")
+    codes = _launch(2, path, fail_rank=1, fail_at=2, out=out)
+    assert codes == [0, 3]
+    with open(out + ".0") as f:
+        msg = f.read()
+    assert msg.startswith("failed a rank did not reach the end of the sweep"), msg
+    split = _split()
+    sd = SweepDir(path, split.count, 3, 3, {"method": abi.METHOD_CROWN, "property": False})
+    lost = sd.pending(1, 2)
+    assert sd.pending(0, 2) == [] and len(lost) == len(range(1, sd.n_chunks, 2)) - 1
+    assert f"{len(lost)} of {sd.n_chunks} chunks pending" in msg
+    codes = _launch(2, path, fail_rank=-1, fail_at=0, out=out)
+    assert codes == [0, 0]
+    for r, calls in ((0, 0), (1, len(lost))):
+        with open(f"{out}.{r}") as f:
+            assert f.read() == f"ok 0 {calls}"
+    lb, ub, _ = sd.collect()
+    elb, eub = _expected(split)
+    assert np.array_equal(lb, elb) and np.array_equal(ub, eub)
