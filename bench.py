@@ -92,6 +92,11 @@ def config(n_gpus):
             "parallelism": f"box-sharded x{n_gpus}", "l2": "flushed between timed steps (256 MiB write)"}
 
 
+def global_boxes(n_gpus):
+    """The seeded global box set of an n_gpus job."""
+    return WL["gen"](BOXES_PER_GPU * n_gpus)[1]
+
+
 def rank_boxes(rank, n_gpus):
     """This rank's slice of one seeded global box set (same weights on every rank)."""
     from luna_b200.shard import shard_range
@@ -244,7 +249,11 @@ def run_engine(args):
         dist.barrier()
     clocks = sampler.stop()
     t = torch.tensor([total_ms], device=dev)
+    rank_ms = [total_ms / args.steps]
     if world > 1:
+        parts = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(parts, t)
+        rank_ms = [float(x.item()) / args.steps for x in parts]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_per_step = float(t.item()) / args.steps
 
@@ -262,22 +271,45 @@ def run_engine(args):
         prof_ms += st.ms_device
     model.set_profiling(False)
 
-    # ---- end to end through the host-buffer C ABI (pinned host memory)
-    hxl = torch.from_numpy(bx.lower).pin_memory()
-    hxu = torch.from_numpy(bx.upper).pin_memory()
-    hC = torch.from_numpy(bx.C).pin_memory()
-    hlb = torch.empty((B, nspec)).pin_memory()
-    hub = torch.empty((B, nspec)).pin_memory()
-    model.compute_bounds_host_ptr(abi.METHOD_ALPHA_CROWN, hxl.data_ptr(), hxu.data_ptr(), B, hC.data_ptr(),
-                                  hC.shape[0], nspec, hlb.data_ptr(), hub.data_ptr())
-    if world > 1:
+    # ---- end to end through the public C ABI with host buffers (pinned):
+    # one GPU: lb200_compute_bounds; N GPUs: lb200_shard_run over the
+    # library's own NCCL communicator (each rank copies its share in, bounds
+    # it, all-gathers every rank's bounds and copies them all out).
+    e2e_steps = max(1, args.steps)
+    if world == 1:
+        hxl = torch.from_numpy(bx.lower).pin_memory()
+        hxu = torch.from_numpy(bx.upper).pin_memory()
+        hC = torch.from_numpy(bx.C).pin_memory()
+        hlb = torch.empty((B, nspec)).pin_memory()
+        hub = torch.empty((B, nspec)).pin_memory()
+        model.compute_bounds_host_ptr(abi.METHOD_ALPHA_CROWN, hxl.data_ptr(), hxu.data_ptr(), B, hC.data_ptr(),
+                                      hC.shape[0], nspec, hlb.data_ptr(), hub.data_ptr())
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            model.compute_bounds_host_ptr(abi.METHOD_ALPHA_CROWN, hxl.data_ptr(), hxu.data_ptr(), B,
+                                          hC.data_ptr(), hC.shape[0], nspec, hlb.data_ptr(), hub.data_ptr())
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        h2d = int(hxl.numel() * 4 + hxu.numel() * 4 + hC.numel() * 4)
+        d2h = int(hlb.numel() * 4 + hub.numel() * 4)
+    else:
+        from luna_b200.engine import NcclComm, nccl_unique_id
+        uid = torch.zeros(128, dtype=torch.uint8, device=dev)
+        if rank == 0:
+            uid.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = NcclComm(bytes(uid.cpu().numpy().tobytes()), rank, world, local)
+        gbx = global_boxes(world)
+        pinned = [torch.from_numpy(a).pin_memory() for a in (gbx.lower, gbx.upper, gbx.C)]
+        hbx = W.Boxes(*(p.numpy() for p in pinned))
+        model.shard_run(comm, hbx, abi.METHOD_ALPHA_CROWN, timeout_ms=120000)
         dist.barrier()
-    e2e_steps = max(1, min(args.steps, 3))
-    t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        model.compute_bounds_host_ptr(abi.METHOD_ALPHA_CROWN, hxl.data_ptr(), hxu.data_ptr(), B,
-                                      hC.data_ptr(), hC.shape[0], nspec, hlb.data_ptr(), hub.data_ptr())
-    e2e_s = (time.perf_counter() - t0) / e2e_steps
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            model.shard_run(comm, hbx, abi.METHOD_ALPHA_CROWN, timeout_ms=120000)
+        e2e_s = (time.perf_counter() - t0) / e2e_steps
+        comm.close()
+        h2d = int((bx.lower.size + bx.upper.size + bx.C.size) * 4)  # this rank's share
+        d2h = int(2 * gbx.n * nspec * 4)  # every rank's bounds
     te = torch.tensor([e2e_s], device=dev)
     if world > 1:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
@@ -296,9 +328,10 @@ def run_engine(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded He-normal weights, uniform box centres)",
             "config": config(world),
-            "e2e": {"value": world * B / e2e_s, "unit": UNIT,
-                    "h2d_bytes_per_step": int(hxl.numel() * 4 + hxu.numel() * 4 + hC.numel() * 4),
-                    "d2h_bytes_per_step": int(hlb.numel() * 4 + hub.numel() * 4)},
+            "e2e": {"value": world * B / e2e_s, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h,
+                    "api": "lb200_compute_bounds" if world == 1 else "lb200_shard_run (NCCL all-gather inside)"},
+            "rank_ms_per_step": rank_ms,
             "gpu_launches": int(launches),
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": achieved / peak if peak else None,
