@@ -220,8 +220,9 @@ LB200_API int lb200_set_profiling(lb200_model* model, int on);
  * split precision wherever the shape allows (N a multiple of 16, K of 4),
  * with 224-column tiles on CTA pairs (cta_group::2) for wide N, the SIMT fp32
  * kernel elsewhere; 1 uses the SIMT fp32 kernel everywhere; 2 the tensor
- * cores on single CTAs only (1 and 2 for cross-checking).  Luna has no
- * counterpart. */
+ * cores on single CTAs only; 3 the tensor cores for the forward
+ * contractions and the SIMT kernel for the adjoint ones (1-3 for
+ * cross-checking).  Luna has no counterpart. */
 LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 
 /* IBP bounds of n_boxes boxes without allocating any device memory, for

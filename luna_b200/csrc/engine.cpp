@@ -1449,7 +1449,8 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
     const uint8_t* sign = cache_.as<uint8_t>(key("sign", st), (size_t)2 * R * rowlen(st, 0));
     // On the tensor-core path the first contraction generates d loss / d A at
     // the input from the signs itself; the SIMT path materialises it.
-    const bool seed_in_kernel = tc_;
+    const bool tc_adj_gemm = tc_ && !simt_adjoint_;  // tensor-core adjoint contractions
+    const bool seed_in_kernel = tc_adj_gemm;
     // A small first conv generates the input seed inside its adjoint kernel.
     const bool first_fast = layers_[0].conv && first_conv_fast(conv_step(st, 1));
     if (layers_[0].conv) {
@@ -1572,7 +1573,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
             continue;
         }
         flops_ += 2.0 * M * (double)N * Kd;
-        if (tc_) {
+        if (tc_adj_gemm) {
             // Tensor cores: the contraction stores Qbar only (compute-bound);
             // the relaxation adjoint + Adam stream through a separate kernel.
             EpiStoreQbar q;

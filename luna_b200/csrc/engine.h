@@ -121,6 +121,9 @@ public:
     // Tensor-core contractions on CTA pairs (default) or on single CTAs
     // (for cross-checking).
     void set_pairs(bool on) { pairs_ = on; }
+    // Adjoint contractions on the SIMT fp32 kernel while the forward ones use
+    // the tensor cores (for cross-checking where precision matters).
+    void set_simt_adjoint(bool on) { simt_adjoint_ = on; }
     const lb200_options& options() const { return opt_; }
     // The plan as JSON: every level (node, map, activation, main edge, skip
     // edges) and every backward start (concretisation form and the row
@@ -199,6 +202,7 @@ private:
     PhaseSplit phase_split(int st, int m) const;
     bool tcconv_ = true;
     bool pairs_ = true;
+    bool simt_adjoint_ = false;
     int start_form(int st) const;
     bool has_conv_ = false;
     std::string key(const char* what, int a, int b = -1) const;

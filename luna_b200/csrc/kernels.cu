@@ -462,7 +462,10 @@ struct EpiAdjOp {
                 const int c = c0 + j;
                 if (c >= N) continue;
                 const float Qbar = acc[i][j] + g * e.b_lin[c];
-                const float P = e.P_saved[(size_t)r * N + c];
+                // P of the ReLU below a one-hot start is its weight row when
+                // the forward pass gathered it instead of saving it.
+                const float P = e.gather_W ? e.gather_W[(size_t)e.rows.row_id[rr] * N + c]
+                                           : e.P_saved[(size_t)r * N + c];
                 const size_t bj = (size_t)bx * e.rp.n + c;
                 const uint8_t f = e.rp.flags[bj];
                 const float s = lower_slope(e.rp, e.alpha, r, bx, c, N);

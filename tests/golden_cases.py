@@ -162,6 +162,7 @@ def merged_concat_graph(graph):
 SPREAD = {
     "cfg2_alpha512": (11.5, 128, "3xTF32 accumulation amplified by Adam: 111/512 over, max 10.97"),
     "cfg2_alpha512/simt": (10.0, 24, "SIMT fp32: 17/512 over, max 5.65 (Luna's own thread spread 9/512, 9.1)"),
+    # (the CPU suite runs the oracle on the first 48 boxes: 8/512 over on all)
     "oracle/cfg2_alpha512": (10.0, 16, "Luna 1 vs 4 threads: 9/512 over, max 9.1 on box 429"),
     # The engine's two tensor-core tilings of the 784-wide input
     # concretisation (224-column tiles on CTA pairs, 112 on single CTAs) add

@@ -252,6 +252,10 @@ def test_tensor_core_path_matches_simt_path(method):
     slb, sub = m.compute_bounds(bx, method)
     print(f"tc vs simt: lb {G.excess(tlb, slb):.3f} ub {G.excess(tub, sub):.3f}")
     assert G.excess(tlb, slb) <= 1.0 and G.excess(tub, sub) <= 1.0
+    # Tensor-core forward contractions with SIMT adjoint ones (path 3).
+    m.set_contraction_path(3)
+    mlb, mub = m.compute_bounds(bx, method)
+    G.parity(f"tc forward + simt adjoint vs simt/{method}", mlb, mub, slb, sub)
 
 
 @pytest.mark.parametrize("method", [abi.METHOD_CROWN, abi.METHOD_ALPHA_CROWN])
