@@ -219,10 +219,13 @@ LB200_API int lb200_set_profiling(lb200_model* model, int on);
 /* Contraction path: 0 (default) uses the tcgen05 tensor cores with 3xTF32
  * split precision wherever the shape allows (N a multiple of 16, K of 4),
  * with 224-column tiles on CTA pairs (cta_group::2) for wide N, the SIMT fp32
- * kernel elsewhere; 1 uses the SIMT fp32 kernel everywhere; 2 the tensor
- * cores on single CTAs only; 3 the tensor cores for the forward
- * contractions and the SIMT kernel for the adjoint ones (1-3 for
- * cross-checking).  Luna has no counterpart. */
+ * kernel elsewhere, and the adjoint contractions accumulating the split's
+ * cross terms apart from its main term; 1 uses the SIMT fp32 kernel
+ * everywhere; 2 the tensor cores on single CTAs only; 3 the tensor cores
+ * for the forward contractions and the SIMT kernel for the adjoint ones;
+ * 4 as 0 without the separate cross-term accumulation; 5 as 0 with it in
+ * the forward contractions too (1-5 for cross-checking).  Luna has no
+ * counterpart. */
 LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 
 /* IBP bounds of n_boxes boxes without allocating any device memory, for

@@ -84,10 +84,11 @@ int lb200_set_profiling(lb200_model* model, int on) {
 
 int lb200_set_contraction_path(lb200_model* model, int path) {
     if (!model) return fail("lb200_set_contraction_path: null model");
-    if (path < 0 || path > 3) return fail("lb200_set_contraction_path: path must be 0, 1, 2 or 3");
+    if (path < 0 || path > 5) return fail("lb200_set_contraction_path: path must be 0 to 5");
     model->m->set_force_simt(path == 1);
-    model->m->set_pairs(path == 0 || path == 3);
+    model->m->set_pairs(path != 2);
     model->m->set_simt_adjoint(path == 3);
+    model->m->set_split_acc(path != 4, path == 5);
     return 0;
 }
 

@@ -1401,12 +1401,12 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
             e.xl = xl_;
             e.xu = xu_;
             if (save) e.sign = cache_.as<uint8_t>(key("sign", st), (size_t)M * N);
-            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, nullptr, nullptr, &e, part + (size_t)slot * M, pairs_, s);
+            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, nullptr, nullptr, &e, part + (size_t)slot * M, pairs_, split_fwd_, s);
             slot += tc_tiles_n(N, pairs_);
         } else if (in_prologue(m - 1)) {
             float* P_out = save ? cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N) : Pscr[pcur];
             pcur ^= 1;
-            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, P_out, nullptr, nullptr, nullptr, pairs_, s);
+            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, P_out, nullptr, nullptr, nullptr, pairs_, split_fwd_, s);
             P_in = P_out;
         } else {
             EpiRelaxFwd e;
@@ -1416,7 +1416,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
             e.b_next = layers_[m - 2].b;
             if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
             e.Q = Qbuf[qcur];
-            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, nullptr, &e, nullptr, part + (size_t)slot * M, pairs_, s);
+            launch_tc_forward(A, pro, L.Wt_hi, L.Wt_lo, M, N, Kd, nullptr, &e, nullptr, part + (size_t)slot * M, pairs_, split_fwd_, s);
             slot += tc_tiles_n(N, pairs_);
             Q_in = Qbuf[qcur];
             qcur ^= 1;
@@ -1587,7 +1587,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
                 q.seed_xu = xu_;
             }
             prof_begin(s);
-            launch_tc_store_qbar(pin, L.W_hi, L.W_lo, M, N, Kd, q, pairs_, s);
+            launch_tc_store_qbar(pin, L.W_hi, L.W_lo, M, N, Kd, q, pairs_, split_adj_, s);
             prof_end(s, 2.0 * M * (double)N * Kd);
             launch_relax_adjoint(e, q.Qbar, M, N, s);
         } else {

@@ -124,6 +124,12 @@ public:
     // Adjoint contractions on the SIMT fp32 kernel while the forward ones use
     // the tensor cores (for cross-checking where precision matters).
     void set_simt_adjoint(bool on) { simt_adjoint_ = on; }
+    // Tensor-core contractions with the 3xTF32 cross terms in their own TMEM
+    // accumulator: the adjoint ones (default) and the forward ones.
+    void set_split_acc(bool adjoint, bool forward) {
+        split_adj_ = adjoint;
+        split_fwd_ = forward;
+    }
     const lb200_options& options() const { return opt_; }
     // The plan as JSON: every level (node, map, activation, main edge, skip
     // edges) and every backward start (concretisation form and the row
@@ -203,6 +209,8 @@ private:
     bool tcconv_ = true;
     bool pairs_ = true;
     bool simt_adjoint_ = false;
+    bool split_adj_ = true;
+    bool split_fwd_ = false;
     int start_form(int st) const;
     bool has_conv_ = false;
     std::string key(const char* what, int a, int b = -1) const;

@@ -37,6 +37,13 @@ constexpr int A_TILE_BYTES = TC_BM * TC_BK * 4;  // 16 KB
 // Epilogues: relaxation of the next ReLU (stores P and Q), input
 // concretisation, Qbar store (adjoint), raw P store (forward).
 enum { KIND_FWD = 0, KIND_CONC = 1, KIND_QBAR = 3, KIND_STOREP = 4 };
+// XS (split accumulation): the two small cross terms of the 3xTF32 split
+// (lo.hi + hi.lo) accumulate in a second TMEM accumulator, so the large
+// hi.hi accumulator takes one addition per K = 8 step instead of three (the
+// tensor core's fp32 accumulation rounds at every addition); the epilogue
+// adds the two.  The accumulator is then single-buffered (TMEM holds 512
+// columns), so the epilogue of a tile no longer overlaps the next tile's
+// MMAs.
 // A operand source: raw fp32 tile by TMA; generated in the kernel from the
 // concretisation signs (first adjoint contraction); the ReLU relaxation of a
 // TMA-loaded P (RELAX) or of gathered weight rows (GATHER, one-hot start).
@@ -220,7 +227,7 @@ __device__ __forceinline__ void seed_row16(const SeedRow& sr, int K, int k0, con
 }
 
 // ------------------------------------------------------------- kernel
-template <int BN, int S, int KIND, int AMODE, int CG>
+template <int BN, int S, int KIND, int AMODE, int CG, bool XS>
 __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tbh,
                    const __grid_constant__ CUtensorMap tbl, const __grid_constant__ CUtensorMap talpha, int M,
@@ -236,6 +243,7 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
     constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128
                                                      : (2 * BN <= 256) ? 256 : 512;
     constexpr uint32_t IDESC = idesc_tf32(BN, TILE_M);
+    constexpr bool XACC = XS;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -352,11 +360,12 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
             uint64_t* last_commit = nullptr;
             uint32_t last_phase = 0;
             for (int t = group; t < ntiles && !*abort; t += groups, ++j) {
-                const int acc = j & 1;
-                const uint32_t aph = (j >> 1) & 1;
+                const int acc = XACC ? 0 : (int)(j & 1);
+                const uint32_t aph = XACC ? (j & 1) : ((j >> 1) & 1);
                 if (!wait_bar(&tempty[acc], aph ^ 1)) break;
                 tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(acc * BN);
+                const uint32_t dx = XACC ? tmem_base + (uint32_t)BN : d;  // cross-term accumulator
                 bool ok = true;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const int s = g % S;
@@ -367,17 +376,22 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
                     const uint64_t dal = desc_sw128(smem_u32(a_lo(s)));
                     const uint64_t dbh = desc_sw128(smem_u32(b_hi(s)));
                     const uint64_t dbl = desc_sw128(smem_u32(b_lo(s)));
+                    auto mma = [&](uint32_t dd, uint64_t a, uint64_t b, uint32_t en) {
+                        if constexpr (CG == 2) umma_tf32_pair(dd, a, b, IDESC, en);
+                        else umma_tf32(dd, a, b, IDESC, en);
+                    };
 #pragma unroll
                     for (int k8 = 0; k8 < TC_BK / 8; ++k8) {
                         const uint64_t off = (uint64_t)(k8 * 32) >> 4;  // 8 tf32 = 32 bytes along K
-                        if constexpr (CG == 2) {
-                            umma_tf32_pair(d, dal + off, dbh + off, IDESC, (kb | k8) != 0);
-                            umma_tf32_pair(d, dah + off, dbl + off, IDESC, 1);
-                            umma_tf32_pair(d, dah + off, dbh + off, IDESC, 1);
+                        const uint32_t first = (kb | k8) != 0;
+                        if constexpr (XACC) {
+                            mma(dx, dal + off, dbh + off, first);
+                            mma(dx, dah + off, dbl + off, 1);
+                            mma(d, dah + off, dbh + off, first);
                         } else {
-                            umma_tf32(d, dal + off, dbh + off, IDESC, (kb | k8) != 0);
-                            umma_tf32(d, dah + off, dbl + off, IDESC, 1);
-                            umma_tf32(d, dah + off, dbh + off, IDESC, 1);
+                            mma(d, dal + off, dbh + off, first);
+                            mma(d, dah + off, dbl + off, 1);
+                            mma(d, dah + off, dbh + off, 1);
                         }
                     }
                     if constexpr (CG == 2) umma_commit_pair(&empty[s]);
@@ -564,18 +578,28 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
         uint32_t j = 0;
         for (int t = group; t < ntiles && !*abort; t += groups, ++j) {
             const int mb = t / tiles_n, nb = t % tiles_n;
-            const int acc = j & 1;
-            const uint32_t aph = (j >> 1) & 1;
+            const int acc = XACC ? 0 : (int)(j & 1);
+            const uint32_t aph = XACC ? (j & 1) : ((j >> 1) & 1);
             if (!wait_bar(&tfull[acc], aph)) break;
             tc_fence_after();
             const int r = mb * TILE_M + (int)rank * TC_BM + q * 32 + lane;
             const bool row_ok = r < M;
             const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+            // 16 accumulator columns from c0 (main plus cross terms when split).
+            auto ld_acc = [&](int c0, float (&v)[16]) {
+                tmem_ld16(taddr + (uint32_t)c0, v);
+                if constexpr (XACC) {
+                    float x[16];
+                    tmem_ld16(taddr + (uint32_t)(BN + c0), x);
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) v[i] += x[i];
+                }
+            };
             float part = 0.f;
             if constexpr (KIND == KIND_STOREP) {
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float v[16];
-                    tmem_ld16(taddr + (uint32_t)c0, v);
+                    ld_acc(c0, v);
                     const int c = nb * BN + c0;
                     if (c >= N || !row_ok) continue;
                     st16f(ep.P_out + (size_t)r * N + c, v);
@@ -584,7 +608,7 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
                 const float g = row_ok ? ep.q.gseed[r] : 0.f;
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float v[16];
-                    tmem_ld16(taddr + (uint32_t)c0, v);
+                    ld_acc(c0, v);
                     const int c = nb * BN + c0;
                     if (c >= N || !row_ok) continue;
                     float bl[16];
@@ -596,7 +620,7 @@ __global__ void __launch_bounds__(kernel_threads<AMODE>(), 1)
             } else {
                 for (int c0 = 0; c0 < BN; c0 += 16) {
                     float v[16];
-                    tmem_ld16(taddr + (uint32_t)c0, v);
+                    ld_acc(c0, v);
                     const int c = nb * BN + c0;
                     if (c >= N || !row_ok) continue;
                     if constexpr (KIND == KIND_FWD) epi_fwd(ep.f, r, c, N, v, part);
@@ -661,12 +685,12 @@ int num_sms() {
     return n;
 }
 
-template <int BN, int S, int KIND, int AMODE, int CG>
+template <int BN, int S, int KIND, int AMODE, int CG, bool XS>
 void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
             const TcPrologue& pro, float* partial, cudaStream_t s) {
     constexpr int STAGE_BYTES = 2 * A_TILE_BYTES + 2 * (BN / CG) * TC_BK * 4;
     constexpr int SMEM = S * STAGE_BYTES + 1024 + 256;
-    auto kernel = tc_gemm_kernel<BN, S, KIND, AMODE, CG>;
+    auto kernel = tc_gemm_kernel<BN, S, KIND, AMODE, CG, XS>;
     static int max_groups = 0;
     if (!max_groups) {
         LB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
@@ -720,19 +744,28 @@ void run_tc(const float* A, const float* Bhi, const float* Blo, int M, int N, in
     LB_LAUNCH();
 }
 
-template <int KIND, int AMODE>
-void dispatch(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
-              const TcPrologue& pro, float* partial, bool pairs, cudaStream_t s) {
+template <int KIND, int AMODE, bool XS>
+void dispatch_xs(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
+                 const TcPrologue& pro, float* partial, bool pairs, cudaStream_t s) {
     if (tc_block_n(N, pairs) == 224) {
-        run_tc<224, 3, KIND, AMODE, 2>(A, Bhi, Blo, M, N, K, ep, pro, partial, s);
+        run_tc<224, 3, KIND, AMODE, 2, XS>(A, Bhi, Blo, M, N, K, ep, pro, partial, s);
         return;
     }
     switch (tc_block_n(N, false)) {
-    case 256: run_tc<256, 2, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
-    case 128: run_tc<128, 3, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
-    case 112: run_tc<112, 3, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
-    default: run_tc<64, 4, KIND, AMODE, 1>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 256: run_tc<256, 2, KIND, AMODE, 1, XS>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 128: run_tc<128, 3, KIND, AMODE, 1, XS>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    case 112: run_tc<112, 3, KIND, AMODE, 1, XS>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
+    default: run_tc<64, 4, KIND, AMODE, 1, XS>(A, Bhi, Blo, M, N, K, ep, pro, partial, s); break;
     }
+}
+
+template <int KIND, int AMODE>
+void dispatch(const float* A, const float* Bhi, const float* Blo, int M, int N, int K, const TcEpi& ep,
+              const TcPrologue& pro, float* partial, bool pairs, bool xs, cudaStream_t s) {
+    if (xs)
+        dispatch_xs<KIND, AMODE, true>(A, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
+    else
+        dispatch_xs<KIND, AMODE, false>(A, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
 }
 
 __global__ void split_tf32_kernel(const float* __restrict__ src, float* __restrict__ hi, float* __restrict__ lo,
@@ -797,42 +830,42 @@ void launch_split_tf32(const float* src, float* hi, float* lo, int64_t n, cudaSt
 }
 
 void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                          const EpiStoreQbar& e, bool pairs, cudaStream_t s) {
+                          const EpiStoreQbar& e, bool pairs, bool split_acc, cudaStream_t s) {
     if (M == 0) return;
     TcEpi ep{};
     ep.q = e;
     const TcPrologue none{};
     if (e.seed_sign)
-        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, none, nullptr, pairs, s);
+        dispatch<KIND_QBAR, AMODE_SEED>(A, Bhi, Blo, M, N, K, ep, none, nullptr, pairs, split_acc, s);
     else
-        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, none, nullptr, pairs, s);
+        dispatch<KIND_QBAR, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, none, nullptr, pairs, split_acc, s);
 }
 
 template <int KIND>
 static void dispatch_amode(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M,
-                           int N, int K, const TcEpi& ep, float* partial, bool pairs, cudaStream_t s) {
+                           int N, int K, const TcEpi& ep, float* partial, bool pairs, bool xs, cudaStream_t s) {
     if (pro.gather_W)
-        dispatch<KIND, AMODE_GATHER>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
+        dispatch<KIND, AMODE_GATHER>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, pairs, xs, s);
     else if (pro.P)
-        dispatch<KIND, AMODE_RELAX>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
+        dispatch<KIND, AMODE_RELAX>(nullptr, Bhi, Blo, M, N, K, ep, pro, partial, pairs, xs, s);
     else
-        dispatch<KIND, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, pro, partial, pairs, s);
+        dispatch<KIND, AMODE_TMA>(A, Bhi, Blo, M, N, K, ep, pro, partial, pairs, xs, s);
 }
 
 void launch_tc_forward(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M, int N,
                        int K, float* P_out, const EpiRelaxFwd* fwd, const EpiConcretize* conc, float* partial,
-                       bool pairs, cudaStream_t s) {
+                       bool pairs, bool split_acc, cudaStream_t s) {
     if (M == 0) return;
     TcEpi ep{};
     if (conc) {
         ep.c = *conc;
-        dispatch_amode<KIND_CONC>(A, pro, Bhi, Blo, M, N, K, ep, partial, pairs, s);
+        dispatch_amode<KIND_CONC>(A, pro, Bhi, Blo, M, N, K, ep, partial, pairs, split_acc, s);
     } else if (fwd) {
         ep.f = *fwd;
-        dispatch_amode<KIND_FWD>(A, pro, Bhi, Blo, M, N, K, ep, partial, pairs, s);
+        dispatch_amode<KIND_FWD>(A, pro, Bhi, Blo, M, N, K, ep, partial, pairs, split_acc, s);
     } else {
         ep.P_out = P_out;
-        dispatch_amode<KIND_STOREP>(A, pro, Bhi, Blo, M, N, K, ep, nullptr, pairs, s);
+        dispatch_amode<KIND_STOREP>(A, pro, Bhi, Blo, M, N, K, ep, nullptr, pairs, split_acc, s);
     }
 }
 

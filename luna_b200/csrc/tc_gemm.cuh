@@ -37,8 +37,10 @@ void tc_conv_set_wait_limit(long long wait_cycles);
 
 // Adjoint contraction storing Qbar = A . B^T + g b_lin only; with
 // e.seed_sign set the A operand is generated from the concretisation signs.
+// split_acc: the cross terms of the split in a second TMEM accumulator
+// (single-buffered accumulator, single CTAs).
 void launch_tc_store_qbar(const float* A, const float* Bhi, const float* Blo, int M, int N, int K,
-                          const EpiStoreQbar& e, bool pairs, cudaStream_t s);
+                          const EpiStoreQbar& e, bool pairs, bool split_acc, cudaStream_t s);
 
 // Forward contraction whose A operand is the ReLU relaxation of P, formed in
 // the kernel (BoundedReLUNode::boundBackward, dense A): Q = P+ s + P- k
@@ -64,6 +66,6 @@ struct TcPrologue {
 // and Q, partial sums per column tile), else a raw store of P into P_out.
 void launch_tc_forward(const float* A, const TcPrologue& pro, const float* Bhi, const float* Blo, int M, int N,
                        int K, float* P_out, const EpiRelaxFwd* fwd, const EpiConcretize* conc, float* partial,
-                       bool pairs, cudaStream_t s);
+                       bool pairs, bool split_acc, cudaStream_t s);
 
 }  // namespace lb200

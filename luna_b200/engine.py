@@ -186,8 +186,10 @@ class Model:
 
     def set_contraction_path(self, path: int):
         """0: tensor cores (3xTF32) where the shape allows, 224-column tiles on
-        CTA pairs for wide N; 1: SIMT fp32 only; 2: tensor cores on single CTAs;
-        3: tensor-core forward contractions, SIMT adjoint contractions."""
+        CTA pairs for wide N, split cross-term accumulation in the adjoint
+        contractions; 1: SIMT fp32 only; 2: tensor cores on single CTAs;
+        3: tensor-core forward, SIMT adjoint contractions; 4: as 0 without the
+        split accumulation; 5: as 0 with it in the forward contractions too."""
         _check(_lib.lb200_set_contraction_path(self._h, int(path)), "lb200_set_contraction_path")
 
     def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,
