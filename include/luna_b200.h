@@ -74,7 +74,7 @@ enum {
 
 /* One node of the computation graph (one Bounded*Node).  Fields a node kind
  * does not use are ignored.  All pointers are host memory, fp32, row-major,
- * and only read during lb200_model_create().  Kinds taken by this build:
+ * and only read during lb200_model_create().  Kinds the engine takes:
  * INPUT, LINEAR, CONV, CONVTRANSPOSE, BATCHNORM (after a LINEAR / CONV),
  * RELU, SIGMOID (on flat layers), ADD (two tensor producers: residual joins
  * of a ReLU output, directly or through a CONV), FLATTEN, IDENTITY,

@@ -7,7 +7,7 @@ specification matrix are set on the model, `compute_bounds` runs IBP,
 CROWN or alpha-CROWN and returns a `BoundedTensor`, and the last result is
 kept for `getFinalAnalysisBounds`.  Two differences: the model is built from
 a `luna_b200.abi.Graph` (node list and weights) rather than an ONNX file,
-since this build has no ONNX front end; and besides Luna's single box
+since the engine has no ONNX front end; and besides Luna's single box
 (`[n_in]` bounds, `[nspec]` results) a batch of boxes (`[B, n_in]` bounds,
 `[B, nspec]` results) is accepted, bounded in one engine call.
 
@@ -57,7 +57,7 @@ class TorchModel:
 
     def __init__(self, graph, vnnlib_path=None, device: int = 0, options: abi.Options | None = None):
         if isinstance(graph, (str, bytes)):
-            raise NotImplementedError("ONNX files are not read by this build; pass a luna_b200.abi.Graph")
+            raise NotImplementedError("ONNX files are not read by this library; pass a luna_b200.abi.Graph")
         self._graph = graph
         self._options = options if options is not None else abi.default_options()
         self._device = device
