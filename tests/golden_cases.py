@@ -106,6 +106,13 @@ LOOSE = {
     # doubled bar used for engine-vs-oracle comparisons), so this one case is
     # held to the interval-scaled doubled bar.
     "oracle_resnet_cifar_crown": (2.180, "oracle dense-A summation order on 32x32 ResNet maps"),
+    # The CIFAR CNN's alpha-CROWN at its workload's lr 0.5 over 30 Adam
+    # steps: per box 0.60 / 1.32 / 1.12 / 0.46 of the strict bar on the
+    # default path, 1.16 / 0.28 / 0.50 / 0.16 with SIMT fp32 contractions,
+    # interval-scaled 0.73 at most; Luna itself moves 0.26 / 0.13 (boxes 0 /
+    # 1) between 1 and 4 threads.  The engine's window (patches) sums differ
+    # in order from Luna's conv_transpose2d, and lr 0.5 amplifies it.
+    "cfg3_alpha": (1.320, "summation order amplified by 30 Adam steps at lr 0.5 (interval-scaled 0.73)"),
 }
 
 
