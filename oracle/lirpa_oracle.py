@@ -773,7 +773,7 @@ class LirpaOracle:
             return bool(d.any())
         return all(bool(d[torch.as_tensor(branch) == b].any()) for b in range(nb))
 
-    def alpha_crown(self, xl, xu, C, trace=None, spec=None):
+    def alpha_crown(self, xl, xu, C, trace=None, spec=None, seed=None):
         """TorchModel::runAlphaCROWN (src/engine/TorchModel.cpp:798-893) with
         AlphaCROWNAnalysis::computeOptimizedBounds(Lower)
         (src/engine/AlphaCROWNAnalysis.cpp:306-511) for the lower side and
@@ -783,10 +783,21 @@ class LirpaOracle:
         bounds when they verify (TorchModel.cpp:816-834), and
         STOP_ALPHA_ON_VERIFIED ends the optimisation at the first iteration
         whose bounds verify, after taking them into the best bound
-        (AlphaCROWNAnalysis.cpp:394-407)."""
+        (AlphaCROWNAnalysis.cpp:394-407).
+
+        `seed` ({(relu id, start id): _Alpha}, another box's last_alphas) is
+        TorchModel::loadState's warm start (TorchModel.cpp:975-983, :813-814;
+        AlphaCROWNAnalysis::seedAlphas, AlphaCROWNAnalysis.cpp:971-997): the
+        analysis starts from copies of those alphas, all requiring grad,
+        marked initialised (no CROWN initialisation pass), with the
+        best-alpha map aliasing the seeded tensors; ensureAlphaFor reuses a
+        seeded alpha only when its specification count matches and
+        recreates it otherwise (_relu_backward).  After the call,
+        last_alphas holds this box's alphas as TorchModel::getState returns
+        them."""
         o = self.opt
         x = (torch.as_tensor(xl), torch.as_tensor(xu))
-        if spec is not None and o.stop_crown_on_verified:
+        if seed is None and spec is not None and o.stop_crown_on_verified:
             # performCROWNInitializationPass (AlphaCROWNAnalysis.cpp:118-129):
             # plain CROWN with the first-linear-IBP shortcut off.
             lo0, hi0, st0 = self.crown(xl, xu, C, _BoxState(first_linear_ibp=False))
@@ -795,6 +806,11 @@ class LirpaOracle:
                 return lo0.detach(), hi0.detach(), inter
         st = _BoxState(method_alpha=True, first_linear_ibp=False)
         st.alpha_mode = True
+        st.seeded = {}
+        for k, ap in (seed or {}).items():
+            a = ap.alpha.detach().clone().requires_grad_(True)
+            st.alphas[k] = _Alpha(a, ap.idx.clone())
+            st.seeded[k] = a
         # TorchModel::runAlphaCROWN (:838-862): the upper side first when it is
         # optimised, then the lower side, in one AlphaCROWNAnalysis (the alphas
         # carry over); a side that is not optimised comes from the runCROWN
@@ -807,6 +823,7 @@ class LirpaOracle:
         res = {}
         for up in sides:
             res[up] = self._optimize_side(st, x, C, up, trace, spec)
+        self.last_alphas = {k: _Alpha(ap.alpha.detach().clone(), ap.idx.clone()) for k, ap in st.alphas.items()}
         lb = res[False][0] if False in res else res[True][1]
         ub = res[True][0] if True in res else res[False][1]
         return lb, ub, res[sides[-1]][2]
@@ -845,7 +862,9 @@ class LirpaOracle:
         lr = float(o.alpha_lr)
         patience = 0
         best_loss = None
-        best_alpha = {}
+        # Seeded alphas: the best-alpha map starts as the alpha map itself
+        # (the same tensors), so saving and restoring them are no-ops.
+        best_alpha = {k: a.detach() for k, a in getattr(st, "seeded", {}).items()}
         for it in range(iters):
             last = it == iters - 1
             st.node_bounds, st.concrete = {}, {}
@@ -892,7 +911,7 @@ class LirpaOracle:
                     patience += 1
             if patience >= o.early_stop_patience:
                 break
-            if not last and loss is not None:
+            if not last and loss is not None and loss.requires_grad:
                 for p in params:
                     p.grad = None
                 loss.backward()
@@ -974,6 +993,25 @@ class LirpaOracle:
                 elif any(r.any() and not (ub[b][r] - thr[r] > 0).any() for r in rows):
                     status[b] = 2
         return lb, ub, status
+
+    def compute_bounds_warm(self, parents, children):
+        """Branch-and-bound's warm start: for each i, alpha-CROWN on parent box
+        i, then alpha-CROWN on child box i seeded with the parent's alphas
+        (TorchModel::getState / loadState).  Intermediate bounds are not
+        seeded: RECOMPUTE_INTERMEDIATE_BOUNDS (default true) recomputes them.
+        C is taken from `children`.  Returns the children's lb, ub [B, nspec]."""
+        B = children.n
+        nspec = children.C.shape[1]
+        lb = np.zeros((B, nspec), np.float32)
+        ub = np.zeros((B, nspec), np.float32)
+        for b in range(B):
+            C = torch.from_numpy(children.C[0 if children.C.shape[0] == 1 else b].copy())
+            self.alpha_crown(torch.from_numpy(parents.lower[b].copy()), torch.from_numpy(parents.upper[b].copy()), C)
+            lo, hi, _ = self.alpha_crown(torch.from_numpy(children.lower[b].copy()),
+                                         torch.from_numpy(children.upper[b].copy()), C, seed=self.last_alphas)
+            lb[b] = lo.numpy()
+            ub[b] = hi.numpy()
+        return lb, ub
 
     def compute_bounds(self, boxes, method, intermediate=False):
         """Bound every box with a fresh state.  Returns lb, ub [B, nspec] (and

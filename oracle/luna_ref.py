@@ -41,6 +41,10 @@ def _load():
             C.POINTER(GraphDesc), C.POINTER(Options), C.c_int, fp, fp, C.c_int64, C.c_int64,
             fp, C.c_int64, C.c_int64, C.c_int64, fp, fp, fp, fp, C.c_int, C.c_char_p, C.c_size_t]
         lib.luna_ref_compute_bounds.restype = C.c_int
+        lib.luna_ref_compute_bounds_warm.argtypes = [
+            C.POINTER(GraphDesc), C.POINTER(Options), fp, fp, fp, fp, C.c_int64, C.c_int64, fp, C.c_int64,
+            C.c_int64, C.c_int64, fp, fp, C.c_int, C.c_char_p, C.c_size_t]
+        lib.luna_ref_compute_bounds_warm.restype = C.c_int
         ip = C.POINTER(C.c_int32)
         lib.luna_ref_property_status.argtypes = [fp, fp, C.c_int64, C.c_int64, fp, ip, C.c_int32, ip, C.c_char_p,
                                                  C.c_size_t]
@@ -76,6 +80,31 @@ def compute_bounds(graph, boxes, method: int, options: Options | None = None,
         raise RuntimeError("luna reference failed: " + err.value.decode(errors="replace"))
     if intermediate:
         return lb, ub, il[:, :n_int], iu[:, :n_int]
+    return lb, ub
+
+
+def compute_bounds_warm(graph, parents, children, options: Options | None = None, num_threads: int = 1):
+    """Luna's warm start: child i bounded with alpha-CROWN after loading the
+    state (TorchModel::getState / loadState) its parent box parents[i] left.
+    C is taken from `children`.  Returns the children's (lb, ub) [B, nspec]."""
+    lib = _load()
+    opt = options if options is not None else default_options()
+    desc = graph.desc()
+    B, n_in = children.lower.shape
+    if parents.lower.shape != (B, n_in):
+        raise ValueError("one parent box per child")
+    Cm = np.ascontiguousarray(children.C, np.float32)
+    nspec, n_out = Cm.shape[1], Cm.shape[2]
+    lb = np.zeros((B, nspec), np.float32)
+    ub = np.zeros((B, nspec), np.float32)
+    arrs = [np.ascontiguousarray(a, np.float32)
+            for a in (parents.lower, parents.upper, children.lower, children.upper)]
+    err = C.create_string_buffer(4096)
+    rc = lib.luna_ref_compute_bounds_warm(C.byref(desc), C.byref(opt), *(fptr(a) for a in arrs), B, n_in,
+                                          fptr(Cm), Cm.shape[0], nspec, n_out, fptr(lb), fptr(ub), num_threads,
+                                          err, len(err))
+    if rc != 0:
+        raise RuntimeError("luna reference failed: " + err.value.decode(errors="replace"))
     return lb, ub
 
 

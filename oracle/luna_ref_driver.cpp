@@ -328,6 +328,53 @@ int luna_ref_compute_bounds(const lb200_graph_desc* g, const lb200_options* opt,
     }
 }
 
+// ---- Warm start: a child box bounded from its parent's state -------------
+//
+// As branch-and-bound hands a sub-domain its parent's state: the parent box
+// is bounded with alpha-CROWN (TorchModel::compute_bounds), its state taken
+// (TorchModel::getState, src/engine/TorchModel.h:123-135) and loaded into the
+// same model with the child's input box (TorchModel::loadState), then the
+// child is bounded with alpha-CROWN.  parents / children are [n_children,
+// n_in] each (child i's parent is parent box i).
+int luna_ref_compute_bounds_warm(const lb200_graph_desc* g, const lb200_options* opt, const float* p_lower,
+                                 const float* p_upper, const float* c_lower, const float* c_upper,
+                                 int64_t n_children, int64_t n_in, const float* C, int64_t c_boxes,
+                                 int64_t nspec, int64_t n_out, float* out_lb, float* out_ub, int num_threads,
+                                 char* err, size_t errlen) {
+    try {
+        at::set_num_threads(num_threads > 0 ? num_threads : 1);
+        apply_options(opt);
+        const auto alpha = LunaConfiguration::AnalysisMethod::AlphaCROWN;
+        for (int64_t b = 0; b < n_children; ++b) {
+            auto model = build_model(g);
+            const float* cb = C + (c_boxes == 1 ? 0 : b) * nspec * n_out;
+            torch::Tensor Cm = from_host(cb, {1, nspec, n_out});
+            BoundedTensor<torch::Tensor> parent(from_host(p_lower + b * n_in, {n_in}),
+                                                from_host(p_upper + b * n_in, {n_in}));
+            LunaConfiguration::ENABLE_FIRST_LINEAR_IBP = opt->enable_first_linear_ibp != 0;
+            model->compute_bounds(parent, &Cm, alpha, true, true);
+            auto state = model->getState();
+            BoundedTensor<torch::Tensor> child(from_host(c_lower + b * n_in, {n_in}),
+                                               from_host(c_upper + b * n_in, {n_in}));
+            model->loadState(child, state.allBounds, state.alphas);
+            LunaConfiguration::ENABLE_FIRST_LINEAR_IBP = opt->enable_first_linear_ibp != 0;
+            auto res = model->compute_bounds(child, &Cm, alpha, true, true);
+            torch::Tensor rl = res.lower().flatten(), ru = res.upper().flatten();
+            if (rl.numel() != nspec || ru.numel() != nspec)
+                throw std::runtime_error("luna_ref_driver: unexpected bound shape");
+            std::memcpy(out_lb + b * nspec, rl.contiguous().data_ptr<float>(), nspec * sizeof(float));
+            std::memcpy(out_ub + b * nspec, ru.contiguous().data_ptr<float>(), nspec * sizeof(float));
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 1;
+    } catch (...) {
+        set_error(err, errlen, "luna_ref_driver: unknown exception");
+        return 1;
+    }
+}
+
 // ---- VNN-LIB properties through Luna's own parser ------------------------
 //
 // As TorchModel(onnxPath, vnnlibPath) reads a property

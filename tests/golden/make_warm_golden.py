@@ -1,0 +1,78 @@
+"""Generate the warm-start golden fixtures in tests/golden/warm/ by running Luna.
+
+Branch-and-bound bounds a sub-domain after loading its parent's state: the
+parent box is bounded with alpha-CROWN, TorchModel::getState() taken and
+handed to TorchModel::loadState() with the child's box, and the child
+bounded with alpha-CROWN (oracle/luna_ref_driver.cpp,
+luna_ref_compute_bounds_warm).  Each parent here is split in half along one
+input dimension (the lower half for even children, the upper half for odd
+ones), as an input split of branch-and-bound does.  Luna's fresh bounds of
+the same children are stored beside the warm ones, to show that the state
+changes the result.
+
+    make -C oracle && python tests/golden/make_warm_golden.py [case names]
+"""
+from __future__ import annotations
+
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+
+from luna_b200 import abi, workloads as W  # noqa: E402
+from luna_b200.workloads import Boxes  # noqa: E402
+from oracle import luna_ref  # noqa: E402
+from make_golden import weights_digest  # noqa: E402
+
+OUT = os.path.join(os.path.dirname(os.path.abspath(__file__)), "warm")
+
+
+def cases():
+    """(name, generator, generator kwargs, option overrides, input dimensions split over)."""
+    return [
+        ("mlp5_warm", "mlp_5_50x6_5", {"n_boxes": 12}, {"alpha_lr": 0.1, "alpha_iterations": 8}, 5),
+        ("rand_warm", "random_mlp_case", {"seed": 42, "n_boxes": 12, "depth": 3, "width": 16, "n_in": 6},
+         {"alpha_lr": 0.1, "alpha_iterations": 10}, 6),
+        ("mlp784_warm", "mlp_784_256x4_10", {"n_boxes": 6}, {"alpha_lr": 0.1, "alpha_iterations": 20}, 784),
+    ]
+
+
+def children_of(bx: Boxes, nd: int) -> Boxes:
+    """Child b: box b halved along input dimension (7 b) mod nd, the lower
+    half for even b and the upper half for odd b (midpoint in fp32)."""
+    lo = bx.lower.copy()
+    hi = bx.upper.copy()
+    for b in range(bx.n):
+        d = (7 * b) % nd
+        mid = np.float32((np.float32(bx.lower[b, d]) + np.float32(bx.upper[b, d])) / np.float32(2))
+        if b % 2 == 0:
+            hi[b, d] = mid
+        else:
+            lo[b, d] = mid
+    return Boxes(lo, hi, bx.C.copy())
+
+
+def main(only=()):
+    os.makedirs(OUT, exist_ok=True)
+    for name, gen, kw, over, nd in cases():
+        if only and name not in only:
+            continue
+        g, parents = getattr(W, gen)(**kw)
+        kids = children_of(parents, nd)
+        opt = abi.default_options(**over)
+        lb, ub = luna_ref.compute_bounds_warm(g, parents, kids, opt)
+        flb, fub = luna_ref.compute_bounds(g, kids, abi.METHOD_ALPHA_CROWN, opt)
+        moved = int(np.sum(np.any((lb != flb) | (ub != fub), axis=1)))
+        np.savez_compressed(os.path.join(OUT, name + ".npz"), lb=lb, ub=ub, fresh_lb=flb, fresh_ub=fub,
+                            parent_lower=parents.lower, parent_upper=parents.upper, lower=kids.lower,
+                            upper=kids.upper, C=kids.C, generator=np.str_(gen), kwargs=np.str_(repr(kw)),
+                            options=np.str_(repr(over)), weights_sha256=np.str_(weights_digest(g)))
+        print(name, lb.shape, f"warm differs from fresh on {moved}/{lb.shape[0]} boxes", flush=True)
+
+
+if __name__ == "__main__":
+    main(tuple(sys.argv[1:]))

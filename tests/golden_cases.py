@@ -37,6 +37,24 @@ def load_prop(name):
                 options=opt, lb=z["lb"], ub=z["ub"], status=z["status"])
 
 
+def warm_names():
+    """Warm-start cases (make_warm_golden.py)."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "warm", "*.npz")))
+
+
+def load_warm(name):
+    """A warm-start case: parent and child boxes (child i of parent i),
+    Luna's warm bounds of the children (lb, ub) and its fresh ones."""
+    z = np.load(os.path.join(GOLDEN, "warm", name + ".npz"))
+    g, _ = getattr(W, str(z["generator"]))(**ast.literal_eval(str(z["kwargs"])))
+    assert _digest(g) == str(z["weights_sha256"]), f"{name}: regenerated weights differ"
+    C = z["C"]
+    return dict(graph=g, parents=Boxes(z["parent_lower"], z["parent_upper"], C),
+                children=Boxes(z["lower"], z["upper"], C),
+                options=abi.default_options(**ast.literal_eval(str(z["options"]))), lb=z["lb"], ub=z["ub"],
+                fresh_lb=z["fresh_lb"], fresh_ub=z["fresh_ub"])
+
+
 def _digest(graph) -> str:
     h = hashlib.sha256()
     for n in graph.nodes:

@@ -138,3 +138,15 @@ def test_luna_thread_count_spread_on_cfg2():
         spread[b] = max(G.excess(four[0], one[0]), G.excess(four[1], one[1]))
     assert spread[429] > 5.0, spread   # 9.1 measured
     assert spread[251] <= 1.0, spread  # most boxes do not move
+
+
+@pytest.mark.parametrize("name", G.warm_names())
+def test_oracle_warm_start_matches_luna(name):
+    """The oracle's warm start (a child bounded from its parent's alphas,
+    TorchModel::getState / loadState) against Luna's own on the same parent
+    and child boxes.  Luna's warm bounds differ from its fresh ones on these
+    cases, so a warm start that ignored the state would fail here."""
+    c = G.load_warm(name)
+    lb, ub = LirpaOracle(c["graph"], c["options"]).compute_bounds_warm(c["parents"], c["children"])
+    G.parity("oracle/warm/" + name, lb, ub, c["lb"], c["ub"])
+    assert not (np.array_equal(c["lb"], c["fresh_lb"]) and np.array_equal(c["ub"], c["fresh_ub"]))
