@@ -228,6 +228,37 @@ LB200_API int lb200_set_profiling(lb200_model* model, int on);
  * counterpart. */
 LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
 
+/* Warm start, as branch-and-bound hands each sub-domain its parent's state
+ * (TorchModel::getState / TorchModel::loadState, src/engine/TorchModel.h:123-135,
+ * and AlphaCROWNAnalysis::seedAlphas, src/engine/AlphaCROWNAnalysis.cpp:971-997).
+ * With keep != 0, every later alpha-CROWN call retains its boxes' final
+ * alphas (the ones getState returns) and their creation sets; keep == 0
+ * drops them.  lb200_set_warm_parents(model, parent, n) then makes the NEXT
+ * call (alpha-CROWN, n boxes, one chunk) start box b from retained box
+ * parent[b]: per (ReLU, start) the parent's alphas are reused, row by row,
+ * when the start has as many rows for box b as it had for the parent, and
+ * created afresh otherwise; the reused alphas are their own best alphas, so
+ * restoring the best alphas leaves them as optimised; no CROWN
+ * initialisation pass.  parent[b] == -1 bounds box b afresh.  Intermediate
+ * bounds are recomputed (Luna's RECOMPUTE_INTERMEDIATE_BOUNDS default).
+ * Networks with convolutions or Sigmoid, OPTIMIZE_UPPER, specification
+ * thresholds and calls split into chunks are refused (an error, not a
+ * fresh run).  Both return 0, or nonzero with lb200_last_error set. */
+LB200_API int lb200_set_warm_start(lb200_model* model, int keep);
+LB200_API int lb200_set_warm_parents(lb200_model* model, const int64_t* parent, int64_t n);
+/* The alpha part of TorchModel::getState (src/engine/TorchModel.cpp:995-1014)
+ * for one retained box: the alphas of activation `level` (1-based, in
+ * topological order) for start `start` (the pre-activation of level `start`,
+ * 2 <= start < K, or the output, start == K, for a network of K affine
+ * layers), both sides, as [2][rows][cols] floats (side 0 lower, 1 upper;
+ * rows = that start's rows for the box; cols = the activation's width: every
+ * neuron, where Luna keeps only the creation set's); creation_set (may be
+ * NULL) receives [cols] bytes, 1 for the neurons the alpha was created for.
+ * *rows and *cols are always set; out is written only when
+ * cap >= 2 * rows * cols (out NULL: sizes only). */
+LB200_API int lb200_warm_alpha(lb200_model* model, int level, int start, int64_t box, float* out, int64_t cap,
+                               int64_t* rows, int64_t* cols, uint8_t* creation_set);
+
 /* IBP bounds of n_boxes boxes without allocating any device memory, for
  * Linear/ReLU networks (models with convs, Sigmoid or Add are rejected): the
  * same result as lb200_compute_bounds_device(..., LB200_METHOD_IBP, ...),

@@ -92,6 +92,23 @@ int lb200_set_contraction_path(lb200_model* model, int path) {
     return 0;
 }
 
+int lb200_set_warm_start(lb200_model* model, int keep) {
+    if (!model) return fail("lb200_set_warm_start: null model");
+    model->m->set_warm_keep(keep != 0);
+    return 0;
+}
+
+int lb200_set_warm_parents(lb200_model* model, const int64_t* parent, int64_t n) {
+    if (!model) return fail("lb200_set_warm_parents: null model");
+    return guarded([&] { model->m->set_warm_parents(parent, n); });
+}
+
+int lb200_warm_alpha(lb200_model* model, int level, int start, int64_t box, float* out, int64_t cap,
+                     int64_t* rows, int64_t* cols, uint8_t* creation_set) {
+    if (!model || !rows || !cols) return fail("lb200_warm_alpha: null argument");
+    return guarded([&] { model->m->warm_alpha(level, start, box, out, cap, rows, cols, creation_set); });
+}
+
 int lb200_compute_bounds_device(lb200_model* model, int method, const float* d_x_lower,
                                 const float* d_x_upper, int64_t n_boxes, const float* d_C,
                                 int64_t c_boxes, int64_t nspec, const float* d_thresholds,

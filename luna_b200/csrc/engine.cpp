@@ -971,13 +971,16 @@ size_t Model::bytes_per_box(bool alpha, int nspec) const {
         size_t maxrow = 0, skiprow = 0;
         for (int m = 0; m < s; ++m) {
             maxrow = std::max(maxrow, (size_t)rowlen(s, m));
-            if (alpha && m >= 1) per_row += (size_t)rowlen(s, m) * 4 * 5;
+            if (alpha && m >= 1) per_row += (size_t)rowlen(s, m) * 4 * ((warm_keep_ || warm_pending_) ? 6 : 5);
             if (m >= 1 && skip_source(s, m, true)) skiprow += (size_t)rowlen(s, m) * 4 * 2;
         }
         total += rows * per_row;
         transient = std::max(transient, rows * (maxrow * 4 * 7 + skiprow));
     }
     for (int m = 0; m <= K_; ++m) total += (size_t)width(m) * 4 * 16;
+    // Warm start: per-start relaxation parameters and creation sets.
+    if (alpha && (warm_keep_ || warm_pending_))
+        for (int m = 1; m < K_; ++m) total += (size_t)width(m) * 16 * (K_ - m);
     return total + transient + (size_t)nspec * 64;
 }
 
@@ -1050,9 +1053,17 @@ void Model::relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t
                        cache_.as<float>(key("rp_b", m), bn), cache_.as<uint8_t>(key("rp_f", m), bn), s);
 }
 
-ReluParams Model::rview(int m, int B, int n) {
+ReluParams Model::rview(int m, int B, int n, int st) {
     ReluParams rp;
     const size_t bn = (size_t)B * n;
+    if (warm_on_ && alpha_ && st > m) {
+        rp.slope_lo = cache_.as<float>(key("wrp_s", m, st), bn);
+        rp.k_up = cache_.as<float>(key("wrp_k", m, st), bn);
+        rp.b_up = cache_.as<float>(key("wrp_b", m, st), bn);
+        rp.flags = cache_.as<uint8_t>(key("wrp_f", m, st), bn);
+        rp.n = n;
+        return rp;
+    }
     rp.slope_lo = cache_.as<float>(key("rp_s", m), bn);
     rp.k_up = cache_.as<float>(key("rp_k", m), bn);
     rp.b_up = cache_.as<float>(key("rp_b", m), bn);
@@ -1060,6 +1071,94 @@ ReluParams Model::rview(int m, int B, int n) {
     if (act_[m] == ACT_SIGMOID) rp.b_lo = cache_.as<float>(key("rp_bl", m), bn);
     rp.n = n;
     return rp;
+}
+
+// ------------------------------------------------------------ warm start
+// A seeded alpha keeps the creation set (unstableIndices) its parent's run
+// made it with (AlphaCROWNAnalysis::seedAlphas, AlphaCROWNAnalysis.cpp:971-997),
+// so the ReLU relaxation of level m differs per start: each start above m
+// reads its own parameters, with every box's creation set (the parent's where
+// the box is seeded for that start, its own otherwise).  Only ReLU levels
+// reach here (a warm start is refused on networks with a Sigmoid).
+void Model::warm_relu_params(int m, int B, bool create, cudaStream_t s) {
+    const int n = width(m);
+    const size_t bn = (size_t)B * n;
+    for (int st = m + 1; st <= K_; ++st) {
+        uint8_t* wa = cache_.as<uint8_t>(key("waset", m, st), bn);
+        int* wh = cache_.as<int>(key("whas", m, st), B);
+        if (create)
+            launch_warm_aset(cache_.as<int>(key("wseed", st), B), cache_.as<int>("wparent", B), B, n,
+                             cache_.as<uint8_t>(key("w_aset", m, st), (size_t)warm_B_ * n),
+                             cache_.as<uint8_t>(key("aset", m), bn), wa, wh, s);
+        launch_relu_params(cache_.as<float>(key("cur_l", m), bn), cache_.as<float>(key("cur_u", m), bn), B, n,
+                           true, false, wa, cache_.as<float>(key("init", m), bn), wh,
+                           cache_.as<float>(key("wrp_s", m, st), bn), cache_.as<float>(key("wrp_k", m, st), bn),
+                           cache_.as<float>(key("wrp_b", m, st), bn), cache_.as<uint8_t>(key("wrp_f", m, st), bn), s);
+    }
+}
+
+// TorchModel::getState after the call (TorchModel.cpp:995-1014): the alphas
+// extractAlphas returns (the best ones, which restoreBestAlphas has just made
+// current), with the creation sets they were made with, and each start's
+// rows per box.
+void Model::warm_retain(int B, cudaStream_t s) {
+    warm_R_.assign(K_ + 1, 0);
+    for (int st = 2; st <= K_; ++st) {
+        const StartPlan& sp = starts_[st];
+        warm_R_[st] = sp.rows.R;
+        LB_CUDA(cudaMemcpyAsync(cache_.as<int>(key("w_boxoff", st), B + 1), sp.box_off, (size_t)(B + 1) * 4,
+                                cudaMemcpyDeviceToDevice, s));
+        for (int m = 1; m < st; ++m) {
+            const size_t cnt = (size_t)2 * sp.rows.R * rowlen(st, m);
+            LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("w_alpha", m, st), cnt),
+                                    cache_.as<float>(key("alpha", m, st), cnt), cnt * 4, cudaMemcpyDeviceToDevice, s));
+            const size_t bn = (size_t)B * width(m);
+            const uint8_t* src = warm_on_ ? cache_.as<uint8_t>(key("waset", m, st), bn)
+                                          : cache_.as<uint8_t>(key("aset", m), bn);
+            LB_CUDA(cudaMemcpyAsync(cache_.as<uint8_t>(key("w_aset", m, st), bn), src, bn, cudaMemcpyDeviceToDevice,
+                                    s));
+        }
+    }
+    warm_B_ = B;
+    warm_valid_ = true;
+}
+
+void Model::set_warm_parents(const int64_t* parent, int64_t n) {
+    if (n < 0 || (n > 0 && !parent)) throw std::invalid_argument("set_warm_parents: bad arguments");
+    if (!warm_valid_)
+        throw std::invalid_argument(
+            "set_warm_parents: no retained state (run an alpha-CROWN call with warm start on first)");
+    std::vector<int> p((size_t)n);
+    for (int64_t i = 0; i < n; ++i) {
+        if (parent[i] < -1 || parent[i] >= warm_B_)
+            throw std::invalid_argument("set_warm_parents: parent index out of range of the retained boxes");
+        p[(size_t)i] = (int)parent[i];
+    }
+    warm_parent_ = std::move(p);
+    warm_pending_ = true;
+}
+
+void Model::warm_alpha(int m, int st, int64_t box, float* out, int64_t cap, int64_t* rows, int64_t* cols,
+                       uint8_t* aset) {
+    if (!warm_valid_) throw std::invalid_argument("warm_alpha: no retained state");
+    if (st < 2 || st > K_ || m < 1 || m >= st) throw std::invalid_argument("warm_alpha: bad level or start");
+    if (box < 0 || box >= warm_B_) throw std::invalid_argument("warm_alpha: box out of range of the retained boxes");
+    const int n = rowlen(st, m), R = warm_R_[st];
+    int bo[2] = {0, 0};
+    LB_CUDA(cudaSetDevice(device_));
+    LB_CUDA(cudaMemcpy(bo, cache_.as<int>(key("w_boxoff", st), warm_B_ + 1) + box, 2 * sizeof(int),
+                       cudaMemcpyDeviceToHost));
+    const int64_t nr = bo[1] - bo[0];
+    *rows = nr;
+    *cols = n;
+    const float* a = cache_.as<float>(key("w_alpha", m, st), (size_t)2 * R * n);
+    if (out && cap >= 2 * nr * n && nr > 0) {
+        LB_CUDA(cudaMemcpy(out, a + (size_t)bo[0] * n, (size_t)nr * n * 4, cudaMemcpyDeviceToHost));
+        LB_CUDA(cudaMemcpy(out + nr * n, a + ((size_t)R + bo[0]) * n, (size_t)nr * n * 4, cudaMemcpyDeviceToHost));
+    }
+    if (aset)
+        LB_CUDA(cudaMemcpy(aset, cache_.as<uint8_t>(key("w_aset", m, st), (size_t)warm_B_ * width(m)) + box * width(m),
+                           (size_t)width(m), cudaMemcpyDeviceToHost));
 }
 
 // ------------------------------------------------------------ forward start
@@ -1144,7 +1243,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             w.st_W = Ls.out.W;
             cs.wg = w;
         }
-        cs.rp = rview(mb, B, width(mb));
+        cs.rp = rview(mb, B, width(mb), st);
         cs.alpha = alpha_buf(mb);
         cs.b_next = level_bias(mb);
         cs.P_save = psave_buf(mb);
@@ -1168,7 +1267,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             ss.nspec = nspec;
             flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
         }
-        ss.rp = rview(mb, B, width(mb));
+        ss.rp = rview(mb, B, width(mb), st);
         ss.alpha = alpha_buf(mb);
         ss.b_next = level_bias_n(mb);
         ss.P_save = psave_buf(mb);
@@ -1189,7 +1288,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
             ConvRelaxEpi e;
             e.rows = sp.rows;
             e.g = sp.geo[m - 1];
-            e.rp = rview(m - 1, B, width(m - 1));
+            e.rp = rview(m - 1, B, width(m - 1), st);
             e.alpha = alpha_buf(m - 1);
             e.b_next = level_bias(m - 1);
             e.P_save = psave_buf(m - 1);
@@ -1231,7 +1330,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
                 ConvRelaxEpi e;
                 e.rows = sp.rows;
                 e.g = sp.geo[m - 1];
-                e.rp = rview(m - 1, B, width(m - 1));
+                e.rp = rview(m - 1, B, width(m - 1), st);
                 e.alpha = alpha_buf(m - 1);
                 e.b_next = level_bias(m - 1);
                 e.P_save = psave_buf(m - 1);
@@ -1289,7 +1388,7 @@ void Model::forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha
         if (m - 1 >= 1) {
             EpiRelaxFwd e;
             e.rows = sp.rows;
-            e.rp = rview(m - 1, B, width(m - 1));
+            e.rp = rview(m - 1, B, width(m - 1), st);
             e.alpha = alpha_buf(m - 1);
             e.b_next = level_bias_n(m - 1);
             e.P_save = psave_buf(m - 1);
@@ -1361,7 +1460,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
             flops_ += 2.0 * M * (double)Ls.n_in * Ls.n_out;
         }
         if (!in_prologue(mb)) {
-            ss.rp = rview(mb, B, width(mb));
+            ss.rp = rview(mb, B, width(mb), st);
             if (alpha) ss.alpha = cache_.as<float>(key("alpha", mb, st), (size_t)M * width(mb));
             ss.b_next = layers_[mb - 1].b;
             ss.Q = Qbuf[qcur];
@@ -1380,7 +1479,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
         TcPrologue pro;
         if (in_prologue(m)) {
             pro.rows = sp.rows;
-            pro.rp = rview(m, B, Kd);
+            pro.rp = rview(m, B, Kd, st);
             if (alpha) pro.alpha = cache_.as<float>(key("alpha", m, st), (size_t)M * Kd);
             pro.b_lin = L.b;
             if (m == mb && st != K_) {
@@ -1411,7 +1510,7 @@ void Model::forward_start_tc(StartPlan& sp, int B, int nspec, bool save, bool al
         } else {
             EpiRelaxFwd e;
             e.rows = sp.rows;
-            e.rp = rview(m - 1, B, N);
+            e.rp = rview(m - 1, B, N, st);
             if (alpha) e.alpha = cache_.as<float>(key("alpha", m - 1, st), (size_t)M * N);
             e.b_next = layers_[m - 2].b;
             if (save) e.P_save = cache_.as<float>(key("Psave", st, m - 1), (size_t)M * N);
@@ -1480,7 +1579,7 @@ void Model::adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStrea
         };
         EpiRelaxAdj e;
         e.rows = sp.rows;
-        e.rp = rview(m, B, N);
+        e.rp = rview(m, B, N, st);
         e.gseed = g;
         e.b_lin = L.b;
         if (tc_ && m == st - 1 && st != K_)
@@ -1627,6 +1726,7 @@ void Model::run_pass(Pass pass, int B, int nspec, cudaStream_t s) {
             LB_CUDA(cudaMemcpyAsync(cache_.as<float>(key("cur_u", m), bn / 4), cache_.as<float>(key("best_u", m), bn / 4),
                                     bn, cudaMemcpyDeviceToDevice, s));
             relu_params(m, B, true, false, s);
+            if (warm_on_) warm_relu_params(m, B, false, s);
         }
     } else {
         for (int m = 1; m < K_; ++m) {
@@ -1646,6 +1746,7 @@ void Model::run_pass(Pass pass, int B, int nspec, cudaStream_t s) {
                                      ste ? cache_.as<float>(key("best_u", m), bn) : nullptr, width(m), cl, cu, s);
             }
             relu_params(m, B, alpha, create, s);
+            if (warm_on_ && alpha) warm_relu_params(m, B, create, s);
         }
     }
     StartPlan& out = starts_[K_];
@@ -1663,6 +1764,14 @@ void Model::init_alpha(StartPlan& sp, int m, int B, cudaStream_t s) {
         launch_alpha_init(sp.rows, init, width(m), a, s);
     else
         launch_alpha_init_win(sp.rows, sp.geo[m], init, width(m), a, s);
+    // Warm start: a seeded box takes its parent's alpha rows instead
+    // (ensureAlphaFor reuses a seeded alpha whose specification count matches,
+    // row by row in order).
+    if (warm_on_)
+        launch_warm_alpha(sp.rows, cache_.as<int>(key("wseed", sp.s), B), cache_.as<int>("wparent", B),
+                          cache_.as<int>(key("w_boxoff", sp.s), warm_B_ + 1), warm_R_[sp.s], rowlen(sp.s, m),
+                          cache_.as<float>(key("w_alpha", m, sp.s), (size_t)2 * warm_R_[sp.s] * rowlen(sp.s, m)), a,
+                          s);
 }
 
 // ------------------------------------------------------------ one chunk
@@ -1742,6 +1851,10 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         return;
     }
     build_rows(B, nspec, s);
+    if (warm_on_)
+        for (int st = 2; st <= K_; ++st)
+            launch_warm_seed(starts_[st].box_off, cache_.as<int>(key("w_boxoff", st), warm_B_ + 1),
+                             cache_.as<int>("wparent", B), B, cache_.as<int>(key("wseed", st), B), s);
     StartPlan& out = starts_[K_];
     float* val_out = nullptr;
     if (method == LB200_METHOD_CROWN) {
@@ -1967,9 +2080,13 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         for (int st = 2; st <= K_; ++st)
             for (int m = 1; m < st; ++m) {
                 const size_t cnt = (size_t)2 * starts_[st].rows.R * rowlen(st, m);
+                // A seeded box's best alphas are its alphas themselves
+                // (seedAlphas: _bestAlphaByNodeStart = _alphaByNodeStart), so
+                // restoring leaves them as they are.
                 launch_restore_alpha(starts_[st].rows, bc.first_save, rowlen(st, m),
                                      cache_.as<float>(key("abest", m, st), cnt),
-                                     cache_.as<float>(key("alpha", m, st), cnt), s);
+                                     cache_.as<float>(key("alpha", m, st), cnt), s,
+                                     warm_on_ ? cache_.as<int>(key("wseed", st), B) : nullptr);
             }
         run_pass(Pass::ALPHA_FINAL, B, nspec, s);
         val_out = cache_.as<float>(key("val", K_), (size_t)2 * out.rows.R);
@@ -1992,6 +2109,12 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
         iters_run_ = std::max(iters_run_, std::min(it + 1, iters));
     }
     if (done) launch_take_verified(done, crown_lb, crown_ub, B, nspec, lb, ub, s);
+    if (warm_keep_) {
+        if (!opt_upper && !has_conv_ && !has_sigmoid_ && !thr_)
+            warm_retain(B, s);
+        else
+            warm_valid_ = false;
+    }
     (void)nout;
 }
 
@@ -2047,6 +2170,31 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
     if (c_boxes != 1 && c_boxes != n_boxes) throw std::invalid_argument("c_boxes must be 1 or n_boxes");
     if (n_branches < 0 || (n_branches > 0 && (!d_branch || !d_thr)))
         throw std::invalid_argument("OR branches need thresholds and a branch index per row");
+    // Warm start: parents set by set_warm_parents apply to this call only.
+    const bool warm = warm_pending_;
+    warm_pending_ = false;
+    if (warm) {
+        if (method != LB200_METHOD_ALPHA_CROWN) throw std::invalid_argument("warm start: alpha-CROWN calls only");
+        if ((int64_t)warm_parent_.size() != n_boxes)
+            throw std::invalid_argument("warm start: one parent index per box is needed");
+        if (has_conv_ || has_sigmoid_)
+            throw std::invalid_argument("warm start: networks with convolutions or Sigmoid are not supported");
+        if (d_thr) throw std::invalid_argument("warm start: specification thresholds are not supported");
+        if (upper && opt_.optimize_upper) throw std::invalid_argument("warm start: OPTIMIZE_UPPER is not supported");
+    }
+    // A call that fails after this point leaves no retained state behind.
+    struct WarmReset {
+        Model* m;
+        bool ok = false;
+        ~WarmReset() {
+            m->warm_on_ = false;
+            if (!ok && m->warm_keep_) m->warm_valid_ = false;
+        }
+    } warm_reset{this};
+    // What warm start does not cover leaves no retained state.
+    if (warm_keep_ && method == LB200_METHOD_ALPHA_CROWN &&
+        (d_thr || has_conv_ || has_sigmoid_ || (upper && opt_.optimize_upper)))
+        warm_valid_ = false;
     thr_ = d_thr;
     branch_ = d_branch;
     n_branches_ = n_branches;
@@ -2070,6 +2218,13 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
     const int64_t per_box = std::max<int64_t>(1, (int64_t)bytes_per_box(alpha, (int)nspec));
     int64_t chunk = std::max<int64_t>(1, std::min<int64_t>(n_boxes, (int64_t)(budget / per_box)));
     chunk = std::min<int64_t>(chunk, 65536);
+    if (warm) {
+        if (chunk < n_boxes)
+            throw std::invalid_argument("warm start: the boxes do not fit one chunk on this device");
+        LB_CUDA(cudaMemcpyAsync(cache_.as<int>("wparent", std::max<int64_t>(n_boxes, 1)), warm_parent_.data(),
+                                (size_t)n_boxes * sizeof(int), cudaMemcpyHostToDevice, stream));
+        warm_on_ = n_boxes > 0;
+    }
     const int n0 = n_in(), nout = n_out();
     for (int64_t b0 = 0; b0 < n_boxes; b0 += chunk) {
         const int B = (int)std::min<int64_t>(chunk, n_boxes - b0);
@@ -2079,6 +2234,8 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
         last_B_ = B;
     }
     last_alpha_ = alpha;
+    // Retained state covers one chunk: a call split into several keeps none.
+    if (warm_keep_ && n_boxes > chunk) warm_valid_ = false;
     LB_CUDA(cudaEventRecord(e1, stream));
     LB_CUDA(cudaEventSynchronize(e1));
     int tc_err = 0;
@@ -2087,6 +2244,7 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
         LB_CUDA(cudaMemset(tc_error_flag(), 0, sizeof(int)));
         throw std::runtime_error("tensor-core contraction: a bounded wait expired; results are invalid");
     }
+    warm_reset.ok = true;
     float ms = 0.f;
     LB_CUDA(cudaEventElapsedTime(&ms, e0, e1));
     cudaEventDestroy(e0);

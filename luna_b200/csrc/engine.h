@@ -130,6 +130,22 @@ public:
         split_adj_ = adjoint;
         split_fwd_ = forward;
     }
+    // Warm start (TorchModel::getState / loadState, as branch-and-bound
+    // hands a sub-domain its parent's state): with keep on, every
+    // alpha-CROWN call retains its boxes' final alphas and creation sets;
+    // set_warm_parents then makes the next call seed its box b from
+    // retained box parent[b] (-1: bounded afresh).  Turning keep off drops
+    // the retained state.
+    void set_warm_keep(bool on) {
+        warm_keep_ = on;
+        if (!on) warm_valid_ = false;
+    }
+    void set_warm_parents(const int64_t* parent, int64_t n);
+    // The retained alphas of one box for (activation level m, start st), both
+    // sides [2, rows, cols] into out (when cap allows), and the creation set
+    // [cols] into aset (when non-null); rows / cols are always set.
+    void warm_alpha(int m, int st, int64_t box, float* out, int64_t cap, int64_t* rows, int64_t* cols,
+                    uint8_t* aset);
     const lb200_options& options() const { return opt_; }
     // The plan as JSON: every level (node, map, activation, main edge, skip
     // edges) and every backward start (concretisation form and the row
@@ -170,8 +186,15 @@ private:
     void forward_start(StartPlan& sp, int B, int nspec, bool save, bool alpha, cudaStream_t s);
     void adjoint_start(StartPlan& sp, int B, const float* g, int M, cudaStream_t s);
     void relu_params(int m, int B, bool alpha_mode, bool create, cudaStream_t s);
-    // Relaxation parameters of level m's activation for B boxes of n neurons.
-    ReluParams rview(int m, int B, int n);
+    // Relaxation parameters of level m's activation for B boxes of n neurons,
+    // as the rows of start st read them (the start's own copy in a warm-started
+    // call, where seeded boxes keep their parent's creation sets).
+    ReluParams rview(int m, int B, int n, int st = 0);
+    // Warm start: level m's relaxation per start above it, with each box's
+    // creation set (its parent's where seeded) formed when `create`.
+    void warm_relu_params(int m, int B, bool create, cudaStream_t s);
+    // Retain this call's final alphas, creation sets and row offsets.
+    void warm_retain(int B, cudaStream_t s);
     void init_alpha(StartPlan& sp, int m, int B, cudaStream_t s);
     void build_tc_conv(Layer& L, const float* w, int k);
     void build_tc_convt(Layer& L, const float* w, int k);
@@ -252,6 +275,17 @@ private:
     bool in_tf_ = false;
     bool in_neg_ = false;
     float* in_const_ = nullptr;
+
+    // Warm start: keep requested, retained state present, the current call
+    // seeds from it, parents set for the next call; the retained boxes' count
+    // and row totals per start; the parents of the next call's boxes.
+    bool warm_keep_ = false;
+    bool warm_valid_ = false;
+    bool warm_on_ = false;
+    bool warm_pending_ = false;
+    int warm_B_ = 0;
+    std::vector<int> warm_R_;
+    std::vector<int> warm_parent_;
 
     bool force_simt_ = false;
     bool tc_ = false;  // tensor-core schedule for the current chunk

@@ -1229,19 +1229,83 @@ void launch_negate(const float* in, float* out, int64_t n, cudaStream_t s) {
     LB_LAUNCH();
 }
 
-__global__ void restore_alpha_kernel(RowMap rows, const int* __restrict__ first_save, int n,
+__global__ void restore_alpha_kernel(RowMap rows, const int* __restrict__ first_save,
+                                     const int* __restrict__ keep_current, int n,
                                      const float* __restrict__ best, float* __restrict__ alpha) {
     for (int r2 = blockIdx.y; r2 < 2 * rows.R; r2 += gridDim.y) {
         const int rr = r2 >= rows.R ? r2 - rows.R : r2;
-        if (!first_save[rows.row_box[rr]]) copy_row(best + (size_t)r2 * n, alpha + (size_t)r2 * n, n);
+        const int bx = rows.row_box[rr];
+        if (!first_save[bx] && !(keep_current && keep_current[bx]))
+            copy_row(best + (size_t)r2 * n, alpha + (size_t)r2 * n, n);
     }
 }
 
 void launch_restore_alpha(const RowMap& rows, const int* first_save, int n, const float* best_alpha,
-                          float* alpha, cudaStream_t s) {
+                          float* alpha, cudaStream_t s, const int* keep_current) {
     if (rows.R == 0 || n == 0) return;
     const dim3 grid(ceil_div(n, 1024), std::min(2 * rows.R, 65535));
-    restore_alpha_kernel<<<grid, 256, 0, s>>>(rows, first_save, n, best_alpha, alpha);
+    restore_alpha_kernel<<<grid, 256, 0, s>>>(rows, first_save, keep_current, n, best_alpha, alpha);
+    LB_LAUNCH();
+}
+
+// ---- warm start ---------------------------------------------------------------
+__global__ void warm_seed_kernel(const int* __restrict__ box_off, const int* __restrict__ prev_box_off,
+                                 const int* __restrict__ parent, int B, int* __restrict__ seed) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int p = parent[b];
+    seed[b] = (p >= 0 && box_off[b + 1] - box_off[b] == prev_box_off[p + 1] - prev_box_off[p]) ? 1 : 0;
+}
+
+void launch_warm_seed(const int* box_off, const int* prev_box_off, const int* parent, int B, int* seed,
+                      cudaStream_t s) {
+    if (B == 0) return;
+    warm_seed_kernel<<<ceil_div(B, 256), 256, 0, s>>>(box_off, prev_box_off, parent, B, seed);
+    LB_LAUNCH();
+}
+
+__global__ void warm_alpha_kernel(RowMap rows, const int* __restrict__ seed, const int* __restrict__ parent,
+                                  const int* __restrict__ prev_box_off, int prev_R, int n,
+                                  const float* __restrict__ prev_alpha, float* __restrict__ alpha) {
+    for (int r2 = blockIdx.y; r2 < 2 * rows.R; r2 += gridDim.y) {
+        const int side = r2 >= rows.R ? 1 : 0;
+        const int rr = r2 - side * rows.R;
+        const int bx = rows.row_box[rr];
+        if (!seed[bx]) continue;
+        const int src = side * prev_R + prev_box_off[parent[bx]] + (rr - rows.box_off[bx]);
+        copy_row(prev_alpha + (size_t)src * n, alpha + (size_t)r2 * n, n);
+    }
+}
+
+void launch_warm_alpha(const RowMap& rows, const int* seed, const int* parent, const int* prev_box_off, int prev_R,
+                       int n, const float* prev_alpha, float* alpha, cudaStream_t s) {
+    if (rows.R == 0 || n == 0) return;
+    const dim3 grid(ceil_div(n, 1024), std::min(2 * rows.R, 65535));
+    warm_alpha_kernel<<<grid, 256, 0, s>>>(rows, seed, parent, prev_box_off, prev_R, n, prev_alpha, alpha);
+    LB_LAUNCH();
+}
+
+// One block per box: the creation set a start uses (the parent's for a
+// seeded box, the box's own otherwise) and whether it is non-empty.
+__global__ void warm_aset_kernel(const int* __restrict__ seed, const int* __restrict__ parent, int n,
+                                 const uint8_t* __restrict__ prev_aset, const uint8_t* __restrict__ aset,
+                                 uint8_t* __restrict__ out, int* __restrict__ has) {
+    const int b = blockIdx.x;
+    const uint8_t* src = seed[b] ? prev_aset + (size_t)parent[b] * n : aset + (size_t)b * n;
+    int any = 0;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+        const uint8_t v = src[j];
+        out[(size_t)b * n + j] = v;
+        any |= v;
+    }
+    any = __syncthreads_or(any);
+    if (threadIdx.x == 0) has[b] = any ? 1 : 0;
+}
+
+void launch_warm_aset(const int* seed, const int* parent, int B, int n, const uint8_t* prev_aset,
+                      const uint8_t* aset, uint8_t* out, int* has, cudaStream_t s) {
+    if (B == 0) return;
+    warm_aset_kernel<<<B, 256, 0, s>>>(seed, parent, n, prev_aset, aset, out, has);
     LB_LAUNCH();
 }
 

@@ -321,7 +321,21 @@ void launch_negate(const float* in, float* out, int64_t n, cudaStream_t s);
 // alpha = best_alpha on the rows of boxes that saved at least once
 // (AlphaCROWNAnalysis::restoreBestAlphas).
 void launch_restore_alpha(const RowMap& rows, const int* first_save, int n, const float* best_alpha,
-                          float* alpha, cudaStream_t s);
+                          float* alpha, cudaStream_t s, const int* keep_current = nullptr);
+// ---- warm start (TorchModel::loadState / seedAlphas) --------------------------
+// seed[b] = 1 when box b has a parent (parent[b] >= 0) whose start had as many
+// rows as box b's (AlphaCROWNAnalysis::ensureAlphaFor reuses a seeded alpha
+// only when its specification count matches).
+void launch_warm_seed(const int* box_off, const int* prev_box_off, const int* parent, int B, int* seed,
+                      cudaStream_t s);
+// Seeded boxes' alpha rows (both sides) copied from the parent's rows by
+// position within the box.
+void launch_warm_alpha(const RowMap& rows, const int* seed, const int* parent, const int* prev_box_off, int prev_R,
+                       int n, const float* prev_alpha, float* alpha, cudaStream_t s);
+// The creation set of one (ReLU, start) per box: the parent's for seeded
+// boxes, the box's own otherwise; has[b] = it is non-empty.
+void launch_warm_aset(const int* seed, const int* parent, int B, int n, const uint8_t* prev_aset,
+                      const uint8_t* aset, uint8_t* out, int* has, cudaStream_t s);
 // IBP of the specification: lb = C+ l + C- u, ub = C+ u + C- l per box.
 void launch_ibp_spec(const float* C, int c_per_box, const float* l, const float* u, int B, int nspec,
                      int nout, float* lb, float* ub, cudaStream_t s);

@@ -28,7 +28,8 @@ EXPORTS = ("lb200_options_default", "lb200_model_create", "lb200_set_options",
            "lb200_shard_run", "lb200_describe_plan", "lb200_property_parse", "lb200_property_get_info",
            "lb200_property_input_box", "lb200_property_spec", "lb200_property_free", "lb200_property_status",
            "lb200_property_status_device", "lb200_compute_property", "lb200_compute_property_device",
-           "lb200_test_set_contraction_fault")
+           "lb200_test_set_contraction_fault", "lb200_set_warm_start", "lb200_set_warm_parents",
+           "lb200_warm_alpha")
 
 
 class EngineError(RuntimeError):
@@ -60,6 +61,10 @@ def load_library():
     lib.lb200_last_error.argtypes = [C.c_char_p, C.c_size_t]
     lib.lb200_set_profiling.argtypes = [vp, C.c_int]
     lib.lb200_set_contraction_path.argtypes = [vp, C.c_int]
+    lib.lb200_set_warm_start.argtypes = [vp, C.c_int]
+    lib.lb200_set_warm_parents.argtypes = [vp, C.POINTER(C.c_int64), C.c_int64]
+    lib.lb200_warm_alpha.argtypes = [vp, C.c_int, C.c_int, C.c_int64, fp, C.c_int64, C.POINTER(C.c_int64),
+                                     C.POINTER(C.c_int64), C.POINTER(C.c_uint8)]
     lib.lb200_ibp_bounds_noalloc.argtypes = [vp, vp, vp, C.c_int64, vp, C.c_int64, C.c_int64, vp, vp, vp]
     lib.lb200_model_destroy.argtypes = [vp]
     lib.lb200_model_destroy.restype = None
@@ -94,7 +99,8 @@ def set_contraction_fault(device: int, starve: bool, wait_cycles: int = 0) -> No
     starve the tensor-core kernels' bounded waits run out on `device`."""
     load_library()
     _check(_lib.lb200_test_set_contraction_fault(device, 1 if starve else 0, wait_cycles),
-           "lb200_test_set_contraction_fault")
+           "lb200_test_set_contraction_fault", "lb200_set_warm_start", "lb200_set_warm_parents",
+           "lb200_warm_alpha")
 
 
 def last_error() -> str:
@@ -191,6 +197,32 @@ class Model:
         3: tensor-core forward, SIMT adjoint contractions; 4: as 0 without the
         split accumulation; 5: as 0 with it in the forward contractions too."""
         _check(_lib.lb200_set_contraction_path(self._h, int(path)), "lb200_set_contraction_path")
+
+    def set_warm_start(self, keep: bool):
+        """Retain every later alpha-CROWN call's final alphas (TorchModel::getState)
+        for warm-starting the boxes of a following call; False drops them."""
+        _check(_lib.lb200_set_warm_start(self._h, int(keep)), "lb200_set_warm_start")
+
+    def set_warm_parents(self, parent):
+        """The next call's box b starts from retained box parent[b]
+        (TorchModel::loadState); -1 bounds it afresh."""
+        p = np.ascontiguousarray(np.asarray(parent, np.int64).reshape(-1))
+        _check(_lib.lb200_set_warm_parents(self._h, p.ctypes.data_as(C.POINTER(C.c_int64)), p.size),
+               "lb200_set_warm_parents")
+
+    def warm_alpha(self, level: int, start: int, box: int):
+        """Retained alphas of one box (the alpha part of TorchModel::getState):
+        ([2, rows, cols] fp32, creation set [cols] bool) for activation
+        `level` and start `start` (lb200_warm_alpha)."""
+        rows, cols = C.c_int64(), C.c_int64()
+        _check(_lib.lb200_warm_alpha(self._h, int(level), int(start), int(box), None, 0, C.byref(rows),
+                                     C.byref(cols), None), "lb200_warm_alpha")
+        out = np.zeros((2, rows.value, cols.value), np.float32)
+        aset = np.zeros(cols.value, np.uint8)
+        _check(_lib.lb200_warm_alpha(self._h, int(level), int(start), int(box),
+                                     out.ctypes.data_as(C.POINTER(C.c_float)), out.size, C.byref(rows),
+                                     C.byref(cols), aset.ctypes.data_as(C.POINTER(C.c_uint8))), "lb200_warm_alpha")
+        return out, aset.astype(bool)
 
     def compute_bounds(self, boxes, method: int, bound_lower: bool = True, bound_upper: bool = True,
                        out_lb: np.ndarray | None = None, out_ub: np.ndarray | None = None,

@@ -194,6 +194,16 @@ SPREAD = {
     # concretisation (224-column tiles on CTA pairs, 112 on single CTAs) add
     # their per-tile partial sums in different orders: the same effect.
     "cta pairs vs single ctas/2": (10.0, 16, "partial-sum order of 224- vs 112-column tiles"),
+    # Warm start on the 784-wide MLP (20 Adam steps for the parent, 20 more
+    # for the child): the parent is a fresh run whose last iterations already
+    # drift by a few tenths of the bar, which leaves whole best-alpha rows
+    # 0.01-0.04 away from Luna's; the child starts from them and its 20 steps
+    # amplify that to 1.4-4.2 (tensor cores, 6/6 boxes) or up to 4.15
+    # (SIMT fp32, 2/6).  The oracle started from the engine's own retained
+    # alphas reproduces the engine's children to the strict bar
+    # (test_warm_gpu.py::test_warm_start_pinned_by_oracle_from_engine_state).
+    "warm/mlp784_warm": (10.0, 6, "parent rounding carried into the seeds: max 4.23, 6/6 over"),
+    "warm/mlp784_warm/simt": (10.0, 3, "parent rounding carried into the seeds: max 4.15, 2/6 over"),
 }
 
 
