@@ -204,6 +204,13 @@ SPREAD = {
     # (test_warm_gpu.py::test_warm_start_pinned_by_oracle_from_engine_state).
     "warm/mlp784_warm": (10.0, 6, "parent rounding carried into the seeds: max 4.23, 6/6 over"),
     "warm/mlp784_warm/simt": (10.0, 3, "parent rounding carried into the seeds: max 4.15, 2/6 over"),
+    # The same children against the oracle started from the engine's own
+    # retained alphas: the SIMT fp32 path meets the strict bar (0.36), so the
+    # warm start is exact; with tensor-core contractions the child's own 20
+    # steps carry 3xTF32 rounding from a start near the optimum, where Adam's
+    # normalised steps amplify it (2/6 boxes over, max 7.15).  Over 3 child
+    # steps the tensor-core path meets the strict bar (0.10).
+    "warm-pinned/mlp784_warm": (10.0, 3, "3xTF32 rounding over the child's 20 Adam steps: max 7.15, 2/6 over"),
 }
 
 

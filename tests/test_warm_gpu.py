@@ -63,12 +63,15 @@ def _oracle_seed(oracle, graph, model, box):
     return seed
 
 
-@pytest.mark.parametrize("path", [0, 1])
+@pytest.mark.parametrize("path,child_iters", [(0, None), (1, None), (0, 3)])
 @pytest.mark.parametrize("name", G.warm_names())
-def test_warm_start_pinned_by_oracle_from_engine_state(name, path):
+def test_warm_start_pinned_by_oracle_from_engine_state(name, path, child_iters):
     """The warm start itself, free of the parent's rounding: the oracle's
     child run started from the engine's own retained alphas (the state
-    lb200_warm_alpha reads back) must give the engine's child bounds."""
+    lb200_warm_alpha reads back) must give the engine's child bounds.  With
+    child_iters the children take that many Adam steps instead (the parents
+    keep the case's count), which bounds how far the tensor-core rounding of
+    the child's own steps can grow."""
     from oracle.lirpa_oracle import LirpaOracle
     c = G.load_warm(name)
     B = c["children"].n
@@ -78,6 +81,11 @@ def test_warm_start_pinned_by_oracle_from_engine_state(name, path):
     m.compute_bounds(c["parents"], abi.METHOD_ALPHA_CROWN)
     o = LirpaOracle(c["graph"], c["options"])
     seeds = [_oracle_seed(o, c["graph"], m, b) for b in range(B)]
+    child_opt = c["options"]
+    if child_iters is not None:
+        child_opt = abi.default_options(**{**{f: getattr(c["options"], f) for f, _ in c["options"]._fields_},
+                                           "alpha_iterations": child_iters})
+        m.set_options(child_opt)
     m.set_warm_parents(np.arange(B))
     lb, ub = m.compute_bounds(c["children"], abi.METHOD_ALPHA_CROWN)
     ch = c["children"]
@@ -88,12 +96,13 @@ def test_warm_start_pinned_by_oracle_from_engine_state(name, path):
     try:
         for b in range(B):
             C = torch.from_numpy(ch.C[0 if ch.C.shape[0] == 1 else b].copy())
-            lo, hi, _ = LirpaOracle(c["graph"], c["options"]).alpha_crown(
+            lo, hi, _ = LirpaOracle(c["graph"], child_opt).alpha_crown(
                 torch.from_numpy(ch.lower[b].copy()), torch.from_numpy(ch.upper[b].copy()), C, seed=seeds[b])
             olb[b], oub[b] = lo.numpy(), hi.numpy()
     finally:
         torch.set_num_threads(n)
-    G.parity("warm-pinned/" + name + ("/simt" if path == 1 else ""), lb, ub, olb, oub)
+    tag = "warm-pinned/" + name + ("/simt" if path == 1 else "") + (f"/{child_iters}it" if child_iters else "")
+    G.parity(tag, lb, ub, olb, oub)
 
 
 def test_unseeded_boxes_are_bounded_afresh():
