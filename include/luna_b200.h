@@ -272,7 +272,8 @@ LB200_API int lb200_warm_alpha(lb200_model* model, int level, int start, int64_t
  * 2^31 - 1.  Work is enqueued on `stream` (a stream of the model's device)
  * and the call returns without waiting; the caller's current device is left
  * as it was.  The first call on a device resolves the array's address on
- * that device (cudaGetSymbolAddress).  All calls share the
+ * that device (cudaGetSymbolAddress), so make that first call before any
+ * stream capture begins.  All calls share the
  * array, so calls that overlap on the GPU race and must be serialised by
  * the caller.  No counterpart in the reference. */
 LB200_API int lb200_ibp_bounds_noalloc(lb200_model* model, const float* d_x_lower,
