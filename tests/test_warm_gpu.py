@@ -143,3 +143,71 @@ def test_warm_start_rejections():
     m.set_warm_start(False)
     with pytest.raises(RuntimeError, match="no retained state"):
         m.set_warm_parents(np.arange(B))
+
+
+def _halves(bx, parents, dims, upper):
+    """Boxes parents[i] of bx halved along dims[i] (upper half where upper[i])."""
+    from luna_b200.workloads import Boxes
+    lo = bx.lower[parents].copy()
+    hi = bx.upper[parents].copy()
+    for i, (d, u) in enumerate(zip(dims, upper)):
+        mid = np.float32((lo[i, d] + hi[i, d]) / np.float32(2))
+        if u:
+            lo[i, d] = mid
+        else:
+            hi[i, d] = mid
+    C = bx.C if bx.C.shape[0] == 1 else bx.C[parents]
+    return Boxes(lo, hi, np.ascontiguousarray(C))
+
+
+def test_warm_start_chain_matches_oracle_and_is_sound():
+    """Three levels of a split tree (as Luna's own repeated loadState / run /
+    getState test does, tests/unit/analysis/test_bab_state.cpp): 6 boxes,
+    then both halves of each (12 children, shuffled, so parent indices are
+    not the identity and every parent has two children), then one half of
+    each child (parents in reverse order).  Each level is seeded from the
+    one before; its bounds match the oracle's chain of seeded runs and hold
+    at sampled points."""
+    from luna_b200 import workloads as W
+    from oracle.lirpa_oracle import LirpaOracle
+    g, L0 = W.random_mlp_case(seed=42, n_boxes=6, depth=3, width=16, n_in=6)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=10)
+    rng = np.random.default_rng(3)
+    p1 = rng.permutation(np.repeat(np.arange(6), 2))
+    L1 = _halves(L0, p1, rng.integers(0, 6, 12), np.arange(12) % 2 == 1)
+    p2 = np.arange(12)[::-1].copy()
+    L2 = _halves(L1, p2, rng.integers(0, 6, 12), rng.integers(0, 2, 12) == 1)
+    m = Model(g, options=opt)
+    m.set_contraction_path(1)
+    m.set_warm_start(True)
+    m.compute_bounds(L0, abi.METHOD_ALPHA_CROWN)
+    m.set_warm_parents(p1)
+    lb1, ub1 = m.compute_bounds(L1, abi.METHOD_ALPHA_CROWN)
+    m.set_warm_parents(p2)
+    lb2, ub2 = m.compute_bounds(L2, abi.METHOD_ALPHA_CROWN)
+
+    def run(o, bx, b, seed=None):
+        C = torch.from_numpy(bx.C[0 if bx.C.shape[0] == 1 else b].copy())
+        lo, hi, _ = o.alpha_crown(torch.from_numpy(bx.lower[b].copy()), torch.from_numpy(bx.upper[b].copy()), C,
+                                  seed=seed)
+        return lo.numpy(), hi.numpy(), o.last_alphas
+
+    n = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        o = LirpaOracle(g, opt)
+        s0 = [run(o, L0, b)[2] for b in range(6)]
+        r1 = [run(o, L1, j, s0[p1[j]]) for j in range(12)]
+        r2 = [run(o, L2, k, r1[p2[k]][2]) for k in range(12)]
+    finally:
+        torch.set_num_threads(n)
+    G.parity("warm chain/level 1", lb1, ub1, np.stack([r[0] for r in r1]), np.stack([r[1] for r in r1]))
+    G.parity("warm chain/level 2", lb2, ub2, np.stack([r[0] for r in r2]), np.stack([r[1] for r in r2]))
+    for bx, lb, ub in ((L1, lb1, ub1), (L2, lb2, ub2)):
+        t = np.random.default_rng(5).random((bx.n, 2000, bx.lower.shape[1]), dtype=np.float32)
+        x = bx.lower[:, None] + t * (bx.upper - bx.lower)[:, None]
+        y = W.graph_forward(g, torch.from_numpy(x.reshape(-1, x.shape[-1]))).numpy().reshape(bx.n, 2000, -1)
+        C = np.broadcast_to(bx.C, (bx.n,) + bx.C.shape[1:])
+        cy = np.einsum("bsn,bpn->bps", C, y)
+        tol = 1e-4 * (1 + np.abs(lb).max())
+        assert (cy >= lb[:, None] - tol).all() and (cy <= ub[:, None] + tol).all()
