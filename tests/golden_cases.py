@@ -218,9 +218,10 @@ SPREAD = {
     # in fp32 differ by 4.98x the bar on that box, the oracle and Luna by
     # 8.43x (every other box of both levels: at most 0.11).  The engine
     # (SIMT fp32) is 10.82x off the oracle there, 1/12 boxes over; at level 2
-    # 3.70x, 1/12, where the seeds carry that state one level down.
+    # one box is 3.70x, where the oracle's own fp64/fp32 spread is at most
+    # 0.11: the difference comes with the seeds from level 1.
     "warm chain/level 1": (20.0, 1, "one bound of 0.14 that rounding moves 5-11x the bar: 10.82, 1/12 over"),
-    "warm chain/level 2": (10.0, 1, "that box's state carried one level down: 3.70, 1/12 over"),
+    "warm chain/level 2": (10.0, 1, "level-1 state carried down: 3.70, 1/12 over"),
 }
 
 
