@@ -45,6 +45,10 @@ def _load():
             C.POINTER(GraphDesc), C.POINTER(Options), fp, fp, fp, fp, C.c_int64, C.c_int64, fp, C.c_int64,
             C.c_int64, C.c_int64, fp, fp, C.c_int, C.c_char_p, C.c_size_t]
         lib.luna_ref_compute_bounds_warm.restype = C.c_int
+        lib.luna_ref_compute_bounds_chain.argtypes = [
+            C.POINTER(GraphDesc), C.POINTER(Options), fp, fp, C.c_int64, C.c_int64, C.c_int64, fp, C.c_int64,
+            C.c_int64, C.c_int64, fp, fp, C.c_int, C.c_char_p, C.c_size_t]
+        lib.luna_ref_compute_bounds_chain.restype = C.c_int
         ip = C.POINTER(C.c_int32)
         lib.luna_ref_property_status.argtypes = [fp, fp, C.c_int64, C.c_int64, fp, ip, C.c_int32, ip, C.c_char_p,
                                                  C.c_size_t]
@@ -103,6 +107,29 @@ def compute_bounds_warm(graph, parents, children, options: Options | None = None
     rc = lib.luna_ref_compute_bounds_warm(C.byref(desc), C.byref(opt), *(fptr(a) for a in arrs), B, n_in,
                                           fptr(Cm), Cm.shape[0], nspec, n_out, fptr(lb), fptr(ub), num_threads,
                                           err, len(err))
+    if rc != 0:
+        raise RuntimeError("luna reference failed: " + err.value.decode(errors="replace"))
+    return lb, ub
+
+
+def compute_bounds_chain(graph, lower, upper, spec, options: Options | None = None, num_threads: int = 1):
+    """Luna down split-tree paths: lower / upper [n_paths, depth, n_in] (root
+    first), spec [1 or n_paths, nspec, n_out]; the root of each path is bounded
+    fresh with alpha-CROWN and every later box after getState / loadState of
+    the box above.  Returns (lb, ub) [n_paths, depth, nspec]."""
+    lib = _load()
+    opt = options if options is not None else default_options()
+    desc = graph.desc()
+    P, D, n_in = lower.shape
+    Cm = np.ascontiguousarray(spec, np.float32)
+    nspec, n_out = Cm.shape[1], Cm.shape[2]
+    lb = np.zeros((P, D, nspec), np.float32)
+    ub = np.zeros((P, D, nspec), np.float32)
+    lo = np.ascontiguousarray(lower, np.float32)
+    hi = np.ascontiguousarray(upper, np.float32)
+    err = C.create_string_buffer(4096)
+    rc = lib.luna_ref_compute_bounds_chain(C.byref(desc), C.byref(opt), fptr(lo), fptr(hi), P, D, n_in, fptr(Cm),
+                                           Cm.shape[0], nspec, n_out, fptr(lb), fptr(ub), num_threads, err, len(err))
     if rc != 0:
         raise RuntimeError("luna reference failed: " + err.value.decode(errors="replace"))
     return lb, ub

@@ -375,6 +375,51 @@ int luna_ref_compute_bounds_warm(const lb200_graph_desc* g, const lb200_options*
     }
 }
 
+// A chain of warm starts down one path of a split tree, as a
+// branch-and-bound driver repeats getState / loadState / compute_bounds
+// (Luna's own tests/unit/analysis/test_bab_state.cpp, repeatedLoadStateAndRun):
+// for each of n_paths paths, boxes [depth, n_in] from the root down; the
+// root is bounded fresh, every later box after loading the state the one
+// above it left.  out_lb / out_ub receive [n_paths, depth, nspec]; C is
+// [1 or n_paths, nspec, n_out] (one specification per path).
+int luna_ref_compute_bounds_chain(const lb200_graph_desc* g, const lb200_options* opt, const float* lower,
+                                  const float* upper, int64_t n_paths, int64_t depth, int64_t n_in, const float* C,
+                                  int64_t c_boxes, int64_t nspec, int64_t n_out, float* out_lb, float* out_ub,
+                                  int num_threads, char* err, size_t errlen) {
+    try {
+        at::set_num_threads(num_threads > 0 ? num_threads : 1);
+        apply_options(opt);
+        const auto alpha = LunaConfiguration::AnalysisMethod::AlphaCROWN;
+        for (int64_t p = 0; p < n_paths; ++p) {
+            auto model = build_model(g);
+            const float* cb = C + (c_boxes == 1 ? 0 : p) * nspec * n_out;
+            torch::Tensor Cm = from_host(cb, {1, nspec, n_out});
+            for (int64_t d = 0; d < depth; ++d) {
+                const int64_t at_box = (p * depth + d) * n_in;
+                BoundedTensor<torch::Tensor> box(from_host(lower + at_box, {n_in}), from_host(upper + at_box, {n_in}));
+                if (d > 0) {
+                    auto state = model->getState();
+                    model->loadState(box, state.allBounds, state.alphas);
+                }
+                LunaConfiguration::ENABLE_FIRST_LINEAR_IBP = opt->enable_first_linear_ibp != 0;
+                auto res = model->compute_bounds(box, &Cm, alpha, true, true);
+                torch::Tensor rl = res.lower().flatten(), ru = res.upper().flatten();
+                if (rl.numel() != nspec || ru.numel() != nspec)
+                    throw std::runtime_error("luna_ref_driver: unexpected bound shape");
+                std::memcpy(out_lb + (p * depth + d) * nspec, rl.contiguous().data_ptr<float>(), nspec * sizeof(float));
+                std::memcpy(out_ub + (p * depth + d) * nspec, ru.contiguous().data_ptr<float>(), nspec * sizeof(float));
+            }
+        }
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(err, errlen, e.what());
+        return 1;
+    } catch (...) {
+        set_error(err, errlen, "luna_ref_driver: unknown exception");
+        return 1;
+    }
+}
+
 // ---- VNN-LIB properties through Luna's own parser ------------------------
 //
 // As TorchModel(onnxPath, vnnlibPath) reads a property

@@ -10,7 +10,11 @@ ones), as an input split of branch-and-bound does.  Luna's fresh bounds of
 the same children are stored beside the warm ones, to show that the state
 changes the result.
 
-    make -C oracle && python tests/golden/make_warm_golden.py [case names]
+    make -C oracle && python tests/golden/make_warm_golden.py [case names | split3]
+
+It also writes tests/golden/warm_chain/split3.npz: Luna's bounds down a
+three-level split tree, each box bounded after the state of the one above
+it (getState / loadState repeated, luna_ref_compute_bounds_chain).
 """
 from __future__ import annotations
 
@@ -22,6 +26,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 from luna_b200 import abi, workloads as W  # noqa: E402
 from luna_b200.workloads import Boxes  # noqa: E402
@@ -56,6 +61,50 @@ def children_of(bx: Boxes, nd: int) -> Boxes:
     return Boxes(lo, hi, bx.C.copy())
 
 
+def start_rows(graph, bx):
+    """Rows of every intermediate start per box: the IBP-unstable count of
+    each pre-activation after the first (numpy interval arithmetic)."""
+    lin = [nd for nd in graph.nodes if nd.type == abi.NODE_LINEAR]
+    l, u = bx.lower.astype(np.float64), bx.upper.astype(np.float64)
+    rows = []
+    for k, nd in enumerate(lin[:-1]):
+        W = np.asarray(nd.weight, np.float64) * nd.scale
+        b = np.asarray(nd.bias, np.float64) if nd.bias is not None else 0.0
+        if k > 0:
+            l, u = np.maximum(l, 0), np.maximum(u, 0)
+        Wp, Wn = np.maximum(W, 0), np.minimum(W, 0)
+        l, u = l @ Wp.T + u @ Wn.T + b, u @ Wp.T + l @ Wn.T + b
+        if k > 0:
+            rows.append(((l < 0) & (u > 0)).sum(1))
+    return np.stack(rows, 1)
+
+
+def make_chain():
+    """Luna down the paths of golden_cases.split_chain()'s tree: for leaf k
+    the path is (root p1[p2[k]], level-1 box p2[k], level-2 box k).  Only
+    paths whose level-1 box reuses every seeded alpha (each start has as
+    many rows as at the root) are kept: where Luna recreates one, its best
+    map keeps the seeded alpha's unstableIndices beside the new alpha
+    (AlphaCROWNAnalysis.cpp:601 replaces only `alpha`), so the state it hands
+    to level 2 pairs new values with old indices (its next run then throws a
+    scatter-shape error when there are fewer values than indices)."""
+    import golden_cases as GC
+    g, opt, (L0, L1, L2), (p1, p2) = GC.split_chain()
+    r0 = start_rows(g, L0)[p1[p2]]
+    r1 = start_rows(g, L1)[p2]
+    keep = np.nonzero((r0 == r1).all(1))[0]
+    lo = np.stack([L0.lower[p1[p2]], L1.lower[p2], L2.lower], axis=1)[keep]
+    hi = np.stack([L0.upper[p1[p2]], L1.upper[p2], L2.upper], axis=1)[keep]
+    lb, ub = luna_ref.compute_bounds_chain(g, lo, hi, L2.C[keep], opt)
+    out = os.path.join(os.path.dirname(OUT), "warm_chain")
+    os.makedirs(out, exist_ok=True)
+    levels = {f"lower{k}": L.lower for k, L in enumerate((L0, L1, L2))}
+    levels.update({f"upper{k}": L.upper for k, L in enumerate((L0, L1, L2))})
+    np.savez_compressed(os.path.join(out, "split3.npz"), leaves=keep, lb1=lb[:, 1], ub1=ub[:, 1], lb2=lb[:, 2],
+                        ub2=ub[:, 2], weights_sha256=np.str_(weights_digest(g)), **levels)
+    print("split3: paths kept", keep.tolist(), "of", len(p2), flush=True)
+
+
 def main(only=()):
     os.makedirs(OUT, exist_ok=True)
     for name, gen, kw, over, nd in cases():
@@ -75,4 +124,9 @@ def main(only=()):
 
 
 if __name__ == "__main__":
-    main(tuple(sys.argv[1:]))
+    args = tuple(sys.argv[1:])
+    rest = tuple(a for a in args if a != "split3")
+    if not args or "split3" in args:
+        make_chain()
+    if not args or rest:
+        main(rest)

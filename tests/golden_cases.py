@@ -55,6 +55,48 @@ def load_warm(name):
                 fresh_lb=z["fresh_lb"], fresh_ub=z["fresh_ub"])
 
 
+def halves(bx, parents, dims, upper):
+    """Boxes parents[i] of bx halved along dims[i] (upper half where upper[i])."""
+    lo = bx.lower[parents].copy()
+    hi = bx.upper[parents].copy()
+    for i, (d, u) in enumerate(zip(dims, upper)):
+        mid = np.float32((lo[i, d] + hi[i, d]) / np.float32(2))
+        if u:
+            lo[i, d] = mid
+        else:
+            hi[i, d] = mid
+    C = bx.C if bx.C.shape[0] == 1 else bx.C[parents]
+    return Boxes(lo, hi, np.ascontiguousarray(C))
+
+
+def split_chain():
+    """Three levels of a split tree on a random 6-16-16-16-4 MLP: 6 root
+    boxes; both halves of each (12 boxes, shuffled: parents p1, two children
+    each); one half of each of those (12 boxes, parents p2 in reverse
+    order).  Returns graph, options, (L0, L1, L2), (p1, p2)."""
+    g, L0 = W.random_mlp_case(seed=42, n_boxes=6, depth=3, width=16, n_in=6)
+    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=10)
+    rng = np.random.default_rng(3)
+    p1 = rng.permutation(np.repeat(np.arange(6), 2))
+    L1 = halves(L0, p1, rng.integers(0, 6, 12), np.arange(12) % 2 == 1)
+    p2 = np.arange(12)[::-1].copy()
+    L2 = halves(L1, p2, rng.integers(0, 6, 12), rng.integers(0, 2, 12) == 1)
+    return g, opt, (L0, L1, L2), (p1, p2)
+
+
+def load_chain():
+    """split_chain() with Luna's bounds down the kept paths (make_warm_golden.py):
+    for leaf k in `leaves`, the level-1 box p2[k] bounded after its root
+    p1[p2[k]] (lb1, ub1) and the level-2 box k after that (lb2, ub2)."""
+    z = np.load(os.path.join(GOLDEN, "warm_chain", "split3.npz"))
+    g, opt, levels, parents = split_chain()
+    assert _digest(g) == str(z["weights_sha256"]), "split3: regenerated weights differ"
+    for k, L in enumerate(levels):
+        assert np.array_equal(L.lower, z[f"lower{k}"]) and np.array_equal(L.upper, z[f"upper{k}"])
+    return dict(graph=g, options=opt, levels=levels, parents=parents, leaves=z["leaves"], lb1=z["lb1"],
+                ub1=z["ub1"], lb2=z["lb2"], ub2=z["ub2"])
+
+
 def _digest(graph) -> str:
     h = hashlib.sha256()
     for n in graph.nodes:

@@ -150,3 +150,30 @@ def test_oracle_warm_start_matches_luna(name):
     lb, ub = LirpaOracle(c["graph"], c["options"]).compute_bounds_warm(c["parents"], c["children"])
     G.parity("oracle/warm/" + name, lb, ub, c["lb"], c["ub"])
     assert not (np.array_equal(c["lb"], c["fresh_lb"]) and np.array_equal(c["ub"], c["fresh_ub"]))
+
+
+def test_oracle_warm_chain_matches_luna():
+    """Two warm starts in a row (root, level-1 box, level-2 box), as Luna's
+    repeated getState / loadState / compute_bounds: the oracle's chain of
+    seeded runs against Luna's on the paths whose level-1 run reuses every
+    seeded alpha (tests/golden/warm_chain/split3.npz)."""
+    c = G.load_chain()
+    L0, L1, L2 = c["levels"]
+    p1, p2 = c["parents"]
+    o = LirpaOracle(c["graph"], c["options"])
+
+    def run(bx, b, seed=None):
+        C = torch.from_numpy(bx.C[0 if bx.C.shape[0] == 1 else b].copy())
+        lo, hi, _ = o.alpha_crown(torch.from_numpy(bx.lower[b].copy()), torch.from_numpy(bx.upper[b].copy()), C,
+                                  seed=seed)
+        return lo.numpy(), hi.numpy(), o.last_alphas
+
+    out = []
+    for k in c["leaves"]:
+        s0 = run(L0, p1[p2[k]])[2]
+        r1 = run(L1, p2[k], s0)
+        r2 = run(L2, k, r1[2])
+        out.append((r1[0], r1[1], r2[0], r2[1]))
+    lb1, ub1, lb2, ub2 = (np.stack([r[i] for r in out]) for i in range(4))
+    G.parity("oracle/warm chain/level 1", lb1, ub1, c["lb1"], c["ub1"])
+    G.parity("oracle/warm chain/level 2", lb2, ub2, c["lb2"], c["ub2"])

@@ -145,20 +145,6 @@ def test_warm_start_rejections():
         m.set_warm_parents(np.arange(B))
 
 
-def _halves(bx, parents, dims, upper):
-    """Boxes parents[i] of bx halved along dims[i] (upper half where upper[i])."""
-    from luna_b200.workloads import Boxes
-    lo = bx.lower[parents].copy()
-    hi = bx.upper[parents].copy()
-    for i, (d, u) in enumerate(zip(dims, upper)):
-        mid = np.float32((lo[i, d] + hi[i, d]) / np.float32(2))
-        if u:
-            lo[i, d] = mid
-        else:
-            hi[i, d] = mid
-    C = bx.C if bx.C.shape[0] == 1 else bx.C[parents]
-    return Boxes(lo, hi, np.ascontiguousarray(C))
-
 
 def test_warm_start_chain_matches_oracle_and_is_sound():
     """Three levels of a split tree (as Luna's own repeated loadState / run /
@@ -170,13 +156,7 @@ def test_warm_start_chain_matches_oracle_and_is_sound():
     at sampled points."""
     from luna_b200 import workloads as W
     from oracle.lirpa_oracle import LirpaOracle
-    g, L0 = W.random_mlp_case(seed=42, n_boxes=6, depth=3, width=16, n_in=6)
-    opt = abi.default_options(alpha_lr=0.1, alpha_iterations=10)
-    rng = np.random.default_rng(3)
-    p1 = rng.permutation(np.repeat(np.arange(6), 2))
-    L1 = _halves(L0, p1, rng.integers(0, 6, 12), np.arange(12) % 2 == 1)
-    p2 = np.arange(12)[::-1].copy()
-    L2 = _halves(L1, p2, rng.integers(0, 6, 12), rng.integers(0, 2, 12) == 1)
+    g, opt, (L0, L1, L2), (p1, p2) = G.split_chain()
     m = Model(g, options=opt)
     m.set_contraction_path(1)
     m.set_warm_start(True)
