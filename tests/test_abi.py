@@ -47,6 +47,24 @@ def test_errors_are_reported_not_thrown():
     assert buf.value
 
 
+def test_warm_start_entry_points_reject_missing_arguments():
+    """The warm-start calls fail with a message, not a crash, on a null model
+    or null outputs (no device is touched)."""
+    lib = engine.load_library()
+    buf = C.create_string_buffer(256)
+    assert lib.lb200_set_warm_start(None, 1) != 0
+    lib.lb200_last_error(buf, 256)
+    assert b"null model" in buf.value
+    parent = (C.c_int64 * 2)(0, 1)
+    assert lib.lb200_set_warm_parents(None, parent, 2) != 0
+    lib.lb200_last_error(buf, 256)
+    assert b"null model" in buf.value
+    rows, cols = C.c_int64(), C.c_int64()
+    assert lib.lb200_warm_alpha(None, 1, 2, 0, None, 0, C.byref(rows), C.byref(cols), None) != 0
+    lib.lb200_last_error(buf, 256)
+    assert b"null argument" in buf.value
+
+
 @pytest.mark.skipif(not os.path.exists("/usr/bin/gcc") and not os.path.exists("/opt/gcc/bin/gcc"),
                     reason="no C compiler")
 def test_struct_layout_matches_header(tmp_path):
