@@ -12,7 +12,8 @@ changes the result.
 
     make -C oracle && python tests/golden/make_warm_golden.py [case names | split3]
 
-It also writes tests/golden/warm_chain/split3.npz: Luna's bounds down a
+Cases on networks with convolutions go to tests/golden/warm_conv/.  It
+also writes tests/golden/warm_chain/split3.npz: Luna's bounds down a
 three-level split tree, each box bounded after the state of the one above
 it (getState / loadState repeated, luna_ref_compute_bounds_chain).
 """
@@ -43,6 +44,18 @@ def cases():
         ("rand_warm", "random_mlp_case", {"seed": 42, "n_boxes": 12, "depth": 3, "width": 16, "n_in": 6},
          {"alpha_lr": 0.1, "alpha_iterations": 10}, 6),
         ("mlp784_warm", "mlp_784_256x4_10", {"n_boxes": 6}, {"alpha_lr": 0.1, "alpha_iterations": 20}, 784),
+    ]
+
+
+def conv_cases():
+    """Warm-start cases on networks with convolutions (tests/golden/warm_conv/):
+    dense conv starts, a patches start (a first conv of 4608 features), and
+    a strided transposed conv."""
+    a5 = {"alpha_lr": 0.1, "alpha_iterations": 5}
+    return [
+        ("cnn_warm", "small_cnn_case", {"seed": 3, "n_boxes": 3, "big_first": False}, a5, None),
+        ("cnnpatch_warm", "small_cnn_case", {"seed": 5, "n_boxes": 2, "big_first": True}, a5, None),
+        ("convt_warm", "convt_cnn_case", {"seed": 1, "n_boxes": 2}, a5, None),
     ]
 
 
@@ -106,17 +119,18 @@ def make_chain():
 
 
 def main(only=()):
-    os.makedirs(OUT, exist_ok=True)
-    for name, gen, kw, over, nd in cases():
+    for name, gen, kw, over, nd in cases() + conv_cases():
         if only and name not in only:
             continue
+        out_dir = OUT if nd is not None else os.path.join(os.path.dirname(OUT), "warm_conv")
+        os.makedirs(out_dir, exist_ok=True)
         g, parents = getattr(W, gen)(**kw)
-        kids = children_of(parents, nd)
+        kids = children_of(parents, nd if nd is not None else parents.lower.shape[1])
         opt = abi.default_options(**over)
         lb, ub = luna_ref.compute_bounds_warm(g, parents, kids, opt)
         flb, fub = luna_ref.compute_bounds(g, kids, abi.METHOD_ALPHA_CROWN, opt)
         moved = int(np.sum(np.any((lb != flb) | (ub != fub), axis=1)))
-        np.savez_compressed(os.path.join(OUT, name + ".npz"), lb=lb, ub=ub, fresh_lb=flb, fresh_ub=fub,
+        np.savez_compressed(os.path.join(out_dir, name + ".npz"), lb=lb, ub=ub, fresh_lb=flb, fresh_ub=fub,
                             parent_lower=parents.lower, parent_upper=parents.upper, lower=kids.lower,
                             upper=kids.upper, C=kids.C, generator=np.str_(gen), kwargs=np.str_(repr(kw)),
                             options=np.str_(repr(over)), weights_sha256=np.str_(weights_digest(g)))

@@ -37,15 +37,16 @@ def load_prop(name):
                 options=opt, lb=z["lb"], ub=z["ub"], status=z["status"])
 
 
-def warm_names():
-    """Warm-start cases (make_warm_golden.py)."""
-    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "warm", "*.npz")))
+def warm_names(sub="warm"):
+    """Warm-start cases (make_warm_golden.py); sub="warm_conv" for the ones
+    on networks with convolutions."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, sub, "*.npz")))
 
 
-def load_warm(name):
+def load_warm(name, sub="warm"):
     """A warm-start case: parent and child boxes (child i of parent i),
     Luna's warm bounds of the children (lb, ub) and its fresh ones."""
-    z = np.load(os.path.join(GOLDEN, "warm", name + ".npz"))
+    z = np.load(os.path.join(GOLDEN, sub, name + ".npz"))
     g, _ = getattr(W, str(z["generator"]))(**ast.literal_eval(str(z["kwargs"])))
     assert _digest(g) == str(z["weights_sha256"]), f"{name}: regenerated weights differ"
     C = z["C"]

@@ -140,13 +140,16 @@ def test_luna_thread_count_spread_on_cfg2():
     assert spread[251] <= 1.0, spread  # most boxes do not move
 
 
-@pytest.mark.parametrize("name", G.warm_names())
-def test_oracle_warm_start_matches_luna(name):
+@pytest.mark.parametrize("sub,name", [("warm", n) for n in G.warm_names()] +
+                         [("warm_conv", n) for n in G.warm_names("warm_conv")])
+def test_oracle_warm_start_matches_luna(sub, name):
     """The oracle's warm start (a child bounded from its parent's alphas,
     TorchModel::getState / loadState) against Luna's own on the same parent
-    and child boxes.  Luna's warm bounds differ from its fresh ones on these
-    cases, so a warm start that ignored the state would fail here."""
-    c = G.load_warm(name)
+    and child boxes, on MLPs and on networks with convolutions (dense and
+    patches starts, a transposed conv).  Luna's warm bounds differ from its
+    fresh ones on these cases, so a warm start that ignored the state would
+    fail here."""
+    c = G.load_warm(name, sub)
     lb, ub = LirpaOracle(c["graph"], c["options"]).compute_bounds_warm(c["parents"], c["children"])
     G.parity("oracle/warm/" + name, lb, ub, c["lb"], c["ub"])
     assert not (np.array_equal(c["lb"], c["fresh_lb"]) and np.array_equal(c["ub"], c["fresh_ub"]))
