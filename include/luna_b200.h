@@ -241,9 +241,8 @@ LB200_API int lb200_set_contraction_path(lb200_model* model, int path);
  * restoring the best alphas leaves them as optimised; no CROWN
  * initialisation pass.  parent[b] == -1 bounds box b afresh.  Intermediate
  * bounds are recomputed (Luna's RECOMPUTE_INTERMEDIATE_BOUNDS default).
- * Networks with convolutions or Sigmoid, OPTIMIZE_UPPER, specification
- * thresholds and calls split into chunks are refused (an error, not a
- * fresh run).  Both return 0, or nonzero with lb200_last_error set. */
+ * Networks with Sigmoid, OPTIMIZE_UPPER, specification thresholds and calls
+ * split into chunks are refused (an error, not a fresh run).  Both return 0, or nonzero with lb200_last_error set. */
 LB200_API int lb200_set_warm_start(lb200_model* model, int keep);
 LB200_API int lb200_set_warm_parents(lb200_model* model, const int64_t* parent, int64_t n);
 /* The alpha part of TorchModel::getState (src/engine/TorchModel.cpp:995-1014)

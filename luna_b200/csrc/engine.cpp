@@ -2110,7 +2110,7 @@ void Model::run_chunk(int method, const float* xl, const float* xu, int B, const
     }
     if (done) launch_take_verified(done, crown_lb, crown_ub, B, nspec, lb, ub, s);
     if (warm_keep_) {
-        if (!opt_upper && !has_conv_ && !has_sigmoid_ && !thr_)
+        if (!opt_upper && !has_sigmoid_ && !thr_)
             warm_retain(B, s);
         else
             warm_valid_ = false;
@@ -2177,8 +2177,7 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
         if (method != LB200_METHOD_ALPHA_CROWN) throw std::invalid_argument("warm start: alpha-CROWN calls only");
         if ((int64_t)warm_parent_.size() != n_boxes)
             throw std::invalid_argument("warm start: one parent index per box is needed");
-        if (has_conv_ || has_sigmoid_)
-            throw std::invalid_argument("warm start: networks with convolutions or Sigmoid are not supported");
+        if (has_sigmoid_) throw std::invalid_argument("warm start: networks with Sigmoid are not supported");
         if (d_thr) throw std::invalid_argument("warm start: specification thresholds are not supported");
         if (upper && opt_.optimize_upper) throw std::invalid_argument("warm start: OPTIMIZE_UPPER is not supported");
     }
@@ -2193,7 +2192,7 @@ void Model::compute(int method, const float* d_xl, const float* d_xu, int64_t n_
     } warm_reset{this};
     // What warm start does not cover leaves no retained state.
     if (warm_keep_ && method == LB200_METHOD_ALPHA_CROWN &&
-        (d_thr || has_conv_ || has_sigmoid_ || (upper && opt_.optimize_upper)))
+        (d_thr || has_sigmoid_ || (upper && opt_.optimize_upper)))
         warm_valid_ = false;
     thr_ = d_thr;
     branch_ = d_branch;

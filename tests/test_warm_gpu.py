@@ -44,6 +44,16 @@ def test_warm_start_matches_luna(name, path):
     assert not (np.array_equal(c["lb"], c["fresh_lb"]) and np.array_equal(c["ub"], c["fresh_ub"]))
 
 
+@pytest.mark.parametrize("path", [0, 1])
+@pytest.mark.parametrize("name", G.warm_names("warm_conv"))
+def test_warm_start_with_convolutions_matches_luna(name, path):
+    """Warm start on networks with convolutions: dense conv starts, a patches
+    start (window rows), a strided transposed conv."""
+    c = G.load_warm(name, "warm_conv")
+    lb, ub, _ = _warm(c, np.arange(c["children"].n), path)
+    G.parity("warm/" + name + ("/simt" if path == 1 else ""), lb, ub, c["lb"], c["ub"])
+
+
 def _oracle_seed(oracle, graph, model, box):
     """The engine's retained alphas of one box (lb200_warm_alpha) as the
     oracle's seed: keyed by (ReLU node, start node), compacted to the
