@@ -207,7 +207,13 @@ __global__ void relu_params_kernel(const float* __restrict__ l, const float* __r
         k_up[idx] = d;
         b_up[idx] = -lb_r * d;
         slope_lo[idx] = dlo;
-        flags[idx] = 0;
+        // A box whose alpha for this activation was created empty keeps the
+        // CROWN relaxation (BoundedReLUNode::_maskAlpha with no unstable
+        // indices); its upper line still depends on the bounds, so in the
+        // alpha loop a neuron that has become unstable passes gradient to
+        // them.  (With the stabilised intermediate bounds no neuron of such
+        // a box can become unstable.)
+        flags[idx] = (alpha_mode && unstable) ? RF_UNSTABLE : 0;
     }
 }
 

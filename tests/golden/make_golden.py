@@ -176,6 +176,16 @@ def cases():
     return out
 
 
+# Cases with Luna's stabilised intermediate bounds switched off
+# (STABILIZE_INTERMEDIATE_BOUNDS = false), written to tests/golden/nostab/:
+# a random MLP on which one box's third layer, stable when its alphas are
+# created, has an unstable neuron at the first Adam iteration.
+def nostab_cases():
+    kw = {"seed": 39, "n_boxes": 4, "depth": 3, "width": 12, "eps": 0.2}
+    return [("rand39_alpha_nostab", "random_mlp_case", kw, 4, abi.METHOD_ALPHA_CROWN,
+             {"alpha_lr": 0.5, "alpha_iterations": 10, "stabilize_intermediate_bounds": 0})]
+
+
 def make_case(gen: str, kw: dict):
     g, bx = getattr(W, gen)(**kw)
     if gen == "random_mlp_case":
@@ -219,7 +229,8 @@ def part_path(name, k, n):
 
 
 def main(only=(), procs=1, part=None, merge=0):
-    for name, gen, kw, nb, method, over in cases():
+    nostab = {c[0] for c in nostab_cases()}
+    for name, gen, kw, nb, method, over in cases() + nostab_cases():
         if only and name not in only:
             continue
         g, bx = make_case(gen, kw)
@@ -250,7 +261,9 @@ def main(only=(), procs=1, part=None, merge=0):
         if inter:
             payload["inter_lb"] = res[2]
             payload["inter_ub"] = res[3]
-        np.savez_compressed(os.path.join(OUT, name + ".npz"), **payload)
+        out_dir = os.path.join(OUT, "nostab") if name in nostab else OUT
+        os.makedirs(out_dir, exist_ok=True)
+        np.savez_compressed(os.path.join(out_dir, name + ".npz"), **payload)
         print(name, res[0].shape, float(res[0].min()), float(res[1].max()), flush=True)
 
 

@@ -112,8 +112,14 @@ def oracle_names():
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "oracle", "*.npz")))
 
 
-def load(name):
-    sub = "oracle" if name.startswith("oracle_") else ""
+def nostab_names():
+    """Cases with the stabilised intermediate bounds off (make_golden.py)."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "nostab", "*.npz")))
+
+
+def load(name, sub=None):
+    if sub is None:
+        sub = "oracle" if name.startswith("oracle_") else ""
     z = np.load(os.path.join(GOLDEN, sub, name + ".npz"))
     gen = str(z["generator"])
     kw = ast.literal_eval(str(z["kwargs"]))

@@ -180,3 +180,14 @@ def test_oracle_warm_chain_matches_luna():
     lb1, ub1, lb2, ub2 = (np.stack([r[i] for r in out]) for i in range(4))
     G.parity("oracle/warm chain/level 1", lb1, ub1, c["lb1"], c["ub1"])
     G.parity("oracle/warm chain/level 2", lb2, ub2, c["lb2"], c["ub2"])
+
+
+@pytest.mark.parametrize("name", G.nostab_names())
+def test_oracle_matches_luna_without_stabilised_bounds(name):
+    """STABILIZE_INTERMEDIATE_BOUNDS off: no straight-through clamp of the
+    intermediate bounds, so a layer stable when its alphas were created can
+    turn unstable during the optimisation (box 2 here); the oracle follows
+    Luna through it."""
+    c = G.load(name, "nostab")
+    lb, ub = LirpaOracle(c["graph"], c["options"]).compute_bounds(c["boxes"], c["method"])
+    G.parity("oracle/nostab/" + name, lb, ub, c["lb"], c["ub"])
