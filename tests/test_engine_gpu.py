@@ -426,3 +426,15 @@ def test_batch_edge_cases(method):
     ls, us = m.compute_bounds(shared, method)
     lp, up = m.compute_bounds(per_box, method)
     _assert_parity(f"edgeC/{method}", ls, us, lp, up)
+
+
+@pytest.mark.parametrize("path", [0, 1])
+@pytest.mark.parametrize("name", G.nostab_names())
+def test_engine_matches_luna_without_stabilised_bounds(name, path):
+    """STABILIZE_INTERMEDIATE_BOUNDS off, on a case where a layer stable at
+    alpha creation turns unstable during the optimisation."""
+    c = G.load(name, "nostab")
+    m = Model(c["graph"], options=c["options"])
+    m.set_contraction_path(path)
+    lb, ub = m.compute_bounds(c["boxes"], c["method"])
+    G.parity("nostab/" + name + ("/simt" if path == 1 else ""), lb, ub, c["lb"], c["ub"])
