@@ -186,6 +186,31 @@ def nostab_cases():
              {"alpha_lr": 0.5, "alpha_iterations": 10, "stabilize_intermediate_bounds": 0})]
 
 
+# Result-affecting options at non-default values (the default runs above
+# keep Luna's defaults), written to tests/golden/options/: early-stop
+# patience short enough to end runs early, the best-alpha save window moved
+# both ways, a faster learning-rate decay, CROWN with the first Linear layer
+# back-substituted, and a large first conv concretised densely instead of in
+# patches.
+def option_cases():
+    a = {"alpha_lr": 0.5, "alpha_iterations": 12}
+    m5 = {"n_boxes": 8}
+    return [
+        # lr 1.0 over 30 steps: boxes 2, 3 and 6 stop early (at 16, 19, 21).
+        ("mlp5_alpha_patience2", "mlp_5_50x6_5", m5, 8, abi.METHOD_ALPHA_CROWN,
+         {"alpha_lr": 1.0, "alpha_iterations": 30, "early_stop_patience": 2}),
+        ("mlp5_alpha_save02", "mlp_5_50x6_5", m5, 8, abi.METHOD_ALPHA_CROWN, dict(a, start_save_best=0.2)),
+        ("mlp5_alpha_save09", "mlp_5_50x6_5", m5, 8, abi.METHOD_ALPHA_CROWN, dict(a, start_save_best=0.9)),
+        ("mlp5_alpha_decay09", "mlp_5_50x6_5", m5, 8, abi.METHOD_ALPHA_CROWN, dict(a, alpha_lr_decay=0.9)),
+        ("mlp5_crown_nofirstibp", "mlp_5_50x6_5", {"n_boxes": 16}, 16, abi.METHOD_CROWN,
+         {"enable_first_linear_ibp": 0}),
+        ("cnn_patch_crown_dense", "small_cnn_case", {"seed": 5, "n_boxes": 3, "big_first": True}, 3,
+         abi.METHOD_CROWN, {"use_patches_mode": 0}),
+        ("cnn_patch_alpha_dense", "small_cnn_case", {"seed": 5, "n_boxes": 3, "big_first": True}, 2,
+         abi.METHOD_ALPHA_CROWN, {"alpha_lr": 0.1, "alpha_iterations": 5, "use_patches_mode": 0}),
+    ]
+
+
 def make_case(gen: str, kw: dict):
     g, bx = getattr(W, gen)(**kw)
     if gen == "random_mlp_case":
@@ -230,7 +255,8 @@ def part_path(name, k, n):
 
 def main(only=(), procs=1, part=None, merge=0):
     nostab = {c[0] for c in nostab_cases()}
-    for name, gen, kw, nb, method, over in cases() + nostab_cases():
+    options = {c[0] for c in option_cases()}
+    for name, gen, kw, nb, method, over in cases() + nostab_cases() + option_cases():
         if only and name not in only:
             continue
         g, bx = make_case(gen, kw)
@@ -261,7 +287,8 @@ def main(only=(), procs=1, part=None, merge=0):
         if inter:
             payload["inter_lb"] = res[2]
             payload["inter_ub"] = res[3]
-        out_dir = os.path.join(OUT, "nostab") if name in nostab else OUT
+        out_dir = os.path.join(OUT, "nostab") if name in nostab else (
+            os.path.join(OUT, "options") if name in options else OUT)
         os.makedirs(out_dir, exist_ok=True)
         np.savez_compressed(os.path.join(out_dir, name + ".npz"), **payload)
         print(name, res[0].shape, float(res[0].min()), float(res[1].max()), flush=True)

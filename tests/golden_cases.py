@@ -112,6 +112,11 @@ def oracle_names():
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "oracle", "*.npz")))
 
 
+def option_names():
+    """Cases at non-default option values (make_golden.py, tests/golden/options/)."""
+    return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "options", "*.npz")))
+
+
 def nostab_names():
     """Cases with the stabilised intermediate bounds off (make_golden.py)."""
     return sorted(os.path.basename(p)[:-4] for p in glob.glob(os.path.join(GOLDEN, "nostab", "*.npz")))

@@ -191,3 +191,14 @@ def test_oracle_matches_luna_without_stabilised_bounds(name):
     c = G.load(name, "nostab")
     lb, ub = LirpaOracle(c["graph"], c["options"]).compute_bounds(c["boxes"], c["method"])
     G.parity("oracle/nostab/" + name, lb, ub, c["lb"], c["ub"])
+
+
+@pytest.mark.parametrize("name", G.option_names())
+def test_oracle_matches_luna_at_non_default_options(name):
+    """Early-stop patience that ends runs early, the best-alpha save window
+    moved both ways, a faster learning-rate decay, CROWN with the first
+    Linear layer back-substituted, and a large first conv concretised
+    densely (tests/golden/options/)."""
+    c = G.load(name, "options")
+    lb, ub = LirpaOracle(c["graph"], c["options"]).compute_bounds(c["boxes"], c["method"])
+    G.parity("oracle/options/" + name, lb, ub, c["lb"], c["ub"])
